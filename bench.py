@@ -1,0 +1,345 @@
+"""Benchmark of the B200 prediction hot path: tabicl-anywhere's in-context stage (src/predict.rs:381-586) on
+BASELINE config 2 - the full-size TabICL v2 classifier (12 in-context layers, d 512, 4 heads of 128), a
+10,000-row x 100-feature fitted member with an i16 key/value cache - predicting batches of test rows.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--rows R] [--impl ours|reference]
+
+A step is one pass of the in-context stage over one batch of R test rows (default 2048). `value` is rows/s
+over all ranks with inputs resident in HBM; `e2e` is the same through the host-buffer C ABI call
+(`tcu_stage`, pinned host memory, copies in the timed region). The cache (248 MB) is larger than L2, so no L2
+flush is needed between steps. Multi-GPU: one process per GPU, each a replica with its own batches (the path has
+no data exchange: weak scaling, replicas only). `--impl reference` times the CPU restatement of the reference
+path (oracle/, the reference's Rust crate cannot be built here) on the host cores.
+
+Synthetic inputs (no dataset is named and there is no network): random-init weights of the published
+architecture, seeded N(0,1) row representations, uniform labels; the cache is fitted on the device from them.
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+TRAIN_ROWS, FEATURES, CHUNK, KV = 10000, 100, 256, 1  # config 2: 10k x 100, i16 cache, default chunk
+KV_NAME = {0: "f32", 1: "i16", 2: "i8"}
+
+
+def args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--rows", type=int, default=2048)
+    p.add_argument("--train-rows", type=int, default=TRAIN_ROWS)
+    p.add_argument("--kv", type=int, default=KV)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--latency-reps", type=int, default=100)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def package():
+    from __graft_entry__ import _package
+    return _package()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def workload(a):
+    return {
+        "workload": f"BASELINE config 2: full-size TabICL v2 in-context stage (12 layers, d 512, 4 heads), "
+                    f"{a.train_rows:,}-row x {FEATURES}-feature fitted member, {KV_NAME[a.kv]} cache, "
+                    f"{a.rows} test rows per call",
+        "train_rows": a.train_rows, "features": FEATURES, "kv": KV_NAME[a.kv], "chunk": CHUNK,
+        "rows_per_step": a.rows, "global_batch": a.rows * a.gpus,
+        "l2": "no flush: the cache streamed every layer is larger than L2",
+    }
+
+
+# ---- clocks during the timed region (NVML reads only) ---------------------------------------------------------
+
+class Clocks:
+    def __init__(self, uuid):
+        self.samples, self.stop = [], threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.max = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # noqa: BLE001
+            self.err = str(e)
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((sm, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.05)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self.stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        nv = self.nv
+        names = {
+            "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+            "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+            "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+        }
+        seen = set()
+        for _, r in self.samples:
+            for n, bit in names.items():
+                if r & bit and n != "gpu_idle":
+                    seen.add(n)
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.max,
+                "reasons": sorted(seen), "samples": len(self.samples)}
+
+
+# ---- the CPU leg: the oracle (a restatement of the reference's CPU path) ----------------------------------------
+
+def oracle_rows_per_s(model, kv, layers, scales, rows, h, target_s):
+    """Time the oracle's in-context stage on a bounded sample sized to about target_s seconds of CPU work."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    threads = oracle.threads()
+    n = max(1, threads)
+    t0 = time.perf_counter()
+    oracle.in_context(model, kv, layers, scales, rows, CHUNK, h[:n], model.outs)
+    dt = time.perf_counter() - t0
+    n2 = int(min(h.shape[0], max(n, n * target_s / max(dt, 1e-3))))
+    t0 = time.perf_counter()
+    oracle.in_context(model, kv, layers, scales, rows, CHUNK, h[:n2], model.outs)
+    dt2 = time.perf_counter() - t0
+    return n2 / dt2, n2, dt2, threads
+
+
+def reference_arm(a):
+    """`--impl reference`: the CPU restatement of the reference's path timed on this host's cores. The cache is
+    packed from seeded Gaussian keys/values in the stored format (the attention's cost does not depend on them)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    pkg = package()
+    from tabicl_anywhere_b200 import synth
+    cfg = synth.config("full")
+    wt = synth.weights(cfg, seed=0)
+    m = oracle.Model({k: v for k, v in wt.items() if k.startswith("icl_predictor.")}, cfg["icl_nhead"],
+                     cfg["icl_num_blocks"], cfg["max_classes"])
+    rng = np.random.default_rng(3)
+    layers = []
+    for _ in range(m.layers):
+        k = rng.standard_normal((a.train_rows, m.d), dtype=np.float32)
+        v = rng.standard_normal((a.train_rows, m.d), dtype=np.float32)
+        layers.append(oracle.pack_layer(a.kv, m.d, k, v, CHUNK))
+    scales = np.stack([m.query_scale(l, a.train_rows) for l in range(m.layers)])
+    threads = oracle.threads()
+    # size one step so the whole run stays within about a minute and a half
+    probe = synth.row_reps(threads, m.d, 99)
+    t0 = time.perf_counter()
+    oracle.in_context(m, a.kv, layers, scales, a.train_rows, CHUNK, probe, m.outs)
+    per_row = (time.perf_counter() - t0) / threads
+    step_rows = int(max(threads, min(a.rows, 90.0 / (a.steps + a.warmup) / per_row)))
+    h = synth.row_reps(step_rows, m.d, 100)
+    for _ in range(a.warmup):
+        oracle.in_context(m, a.kv, layers, scales, a.train_rows, CHUNK, h, m.outs)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        oracle.in_context(m, a.kv, layers, scales, a.train_rows, CHUNK, h, m.outs)
+    dt = time.perf_counter() - t0
+    v = step_rows * a.steps / dt
+    sample = f"{step_rows} test rows per step, the oracle's in-context stage on {threads} threads"
+    print(json.dumps({
+        "impl": "reference", "metric": "predicted rows/sec (in-context stage, config 2)", "value": v,
+        "unit": "rows/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": dt / a.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "config": workload(a),
+        "cpu_baseline": {"value": v, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "C restatement of the reference CPU path (oracle/): the reference is Rust and cargo is absent",
+    }))
+    del pkg
+    return 0
+
+
+# ---- our arm ---------------------------------------------------------------------------------------------------
+
+def main():
+    a = args()
+    if a.impl == "reference":
+        return reference_arm(a)
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    a.gpus = world
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    pkg = package()
+    from tabicl_anywhere_b200 import synth
+    cfg = synth.config("full")
+    wt = synth.weights(cfg, seed=0)
+    shape = synth.icl_shape(cfg)
+    d = shape["d"]
+    gpu = pkg.Gpu(local)
+    w = pkg.GpuWeights.from_tensors(gpu, shape, {k: v for k, v in wt.items() if k.startswith("icl_")}, for_fit=True)
+    # the fitted member: training rows through fitting's in-context stage on the device
+    htr = torch.from_numpy(synth.row_reps(a.train_rows, d, 1)).cuda()
+    ytr = torch.from_numpy(synth.labels(a.train_rows, 10, 2)).cuda()
+    vm = pkg.fit_icl(w, htr.data_ptr(), ytr.data_ptr(), a.train_rows, CHUNK, a.kv)
+    del htr, ytr
+    classes = 10
+    R = a.rows
+    h = torch.from_numpy(synth.row_reps(R, d, 100 + rank)).cuda()
+    out = torch.empty((R, classes), device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        vm.stage_device(h.data_ptr(), R, classes, out.data_ptr(), sp)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    props = torch.cuda.get_device_properties(local)
+    clocks = Clocks("GPU-" + str(props.uuid))
+    launches0 = gpu.launches
+    gpu.profile(True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with clocks:
+        e0.record(stream)
+        for _ in range(a.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    attn_ms, attn_passes = gpu.profile(False)
+    launches = gpu.launches - launches0
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    value = R * a.steps * world / (ms / 1e3)
+
+    # end to end through the host-buffer C ABI (pinned host memory; copies in the timed region)
+    hh = torch.from_numpy(synth.row_reps(R, d, 100 + rank)).pin_memory()
+    ho = torch.empty((R, classes), dtype=torch.float32).pin_memory()
+    hn, on = hh.numpy(), ho.numpy()
+    for _ in range(2):
+        vm.stage(hn, classes, out=on)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        vm.stage(hn, classes, out=on)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = R * a.steps * world / e2e_s
+
+    # 1-row latency on one device: CUDA events around each call, plus the decode attention's HBM rate
+    h1 = h[:1].contiguous()
+    o1 = out[:1].contiguous()
+    lat = []
+    for _ in range(5):
+        vm.stage_device(h1.data_ptr(), 1, classes, o1.data_ptr(), sp)
+    gpu.profile(True)
+    for _ in range(a.latency_reps):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        vm.stage_device(h1.data_ptr(), 1, classes, o1.data_ptr(), sp)
+        s1.record(stream)
+        s1.synchronize()
+        lat.append(s0.elapsed_time(s1) * 1e3)
+    lat_attn_ms, lat_passes = gpu.profile(False)
+    lat.sort()
+    pct = lambda p: lat[min(len(lat) - 1, int(p * len(lat)))]
+
+    hbm, bf16, kind = peaks()
+    layer_bytes = pkg.record(a.kv, d, CHUNK) * (a.train_rows // CHUNK) + (pkg.record(a.kv, d, a.train_rows % CHUNK) if a.train_rows % CHUNK else 0)
+    flops_per_pass = 4.0 * a.train_rows * d * R  # QK^T and PV, 2 flops per multiply-add
+    per_pass_s = attn_ms / max(attn_passes, 1) / 1e3
+    achieved_tf = flops_per_pass / per_pass_s / 1e12
+    lat_pass_s = lat_attn_ms / max(lat_passes, 1) / 1e3
+    lat_gbs = layer_bytes / lat_pass_s / 1e9
+
+    line = {
+        "metric": "predicted rows/sec (in-context stage, config 2)", "value": value, "unit": "rows/s",
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(workload(a), parallelism=f"replicas{world}"),
+        "e2e": {"value": e2e, "unit": "rows/s", "h2d_bytes_per_step": R * d * 4, "d2h_bytes_per_step": R * classes * 4},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": bf16, "unit": "TFLOP/s",
+                     "frac": achieved_tf / bf16, "traffic": None, "peak_kind": kind,
+                     "kernel": "attention pass (one layer, all rows)", "per_launch_ms": per_pass_s * 1e3,
+                     "algorithmic_flops_per_launch": flops_per_pass},
+        "latency_1row": {"p50_us": pct(0.5), "p10_us": pct(0.1), "p90_us": pct(0.9), "reps": len(lat),
+                         "roofline": {"bound": "hbm", "achieved": lat_gbs, "peak": hbm, "unit": "GB/s",
+                                      "frac": lat_gbs / hbm, "peak_kind": kind,
+                                      "kernel": "decode attention pass (one layer, one row)",
+                                      "per_launch_us": lat_pass_s * 1e6, "algorithmic_bytes_per_launch": layer_bytes}},
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        m = oracle.Model({k: v for k, v in wt.items() if k.startswith("icl_predictor.")}, cfg["icl_nhead"],
+                         cfg["icl_num_blocks"], cfg["max_classes"])
+        layers = [vm.layer_bytes(l, layer_bytes) for l in range(m.layers)]
+        rps, n, dt, threads = oracle_rows_per_s(m, a.kv, layers, vm.scales(), a.train_rows,
+                                                synth.row_reps(512, d, 200), 12.0)
+        line["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": threads, "kind": "port",
+                                "sample": f"{n} test rows of the same workload through the oracle's in-context "
+                                          f"stage, {dt:.1f} s"}
+    if rank == 0:
+        print(json.dumps(line))
+    vm.free(), w.free(), gpu.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

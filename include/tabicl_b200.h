@@ -1,0 +1,149 @@
+/*
+ * tabicl_b200.h - C ABI of the B200 backend for tabicl-anywhere's prediction hot path.
+ *
+ * The entry points are what a Rust shim crate would bind to implement tabicl-anywhere's accelerator hook
+ * `predict::AttendCached` (src/predict.rs:63-79) and the card tier around it (src/gpu.rs:2495-2701), reading the
+ * same `.tirs` bundles byte for byte (src/store.rs:1-11). Plain pointers and sizes only. Every call returns a
+ * status: TCU_OK (0), TCU_DECLINED (1, the caller's CPU path answers, as `Ok(None)` in predict.rs:58-61), or a
+ * negative error; `tcu_last_error` then says why (gpu.rs:2525-2527).
+ *
+ * Threading: a context serialises the calls made on it (one in flight at a time); use one context per thread for
+ * concurrency. Handles must not be used after they are freed; a model must be freed before its weights, and
+ * weights before their context.
+ */
+#ifndef TABICL_B200_H
+#define TABICL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TCU_API __attribute__((visibility("default")))
+#else
+#define TCU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    TCU_OK = 0,
+    TCU_DECLINED = 1,
+    TCU_ERR_ARG = -1,    /* bad argument (shape, pointer, range) */
+    TCU_ERR_FORMAT = -2, /* bundle or tensor not as tabicl-anywhere writes it */
+    TCU_ERR_CUDA = -3,   /* a CUDA call failed */
+    TCU_ERR_MEMORY = -4, /* device or host memory exhausted */
+    TCU_ERR_STATE = -5,  /* handle not ready (weights or layers missing) */
+    TCU_ERR_IO = -6,     /* file could not be read */
+};
+
+/* Stored number format of the in-context keys and values: the codes of `fit::Kv` (src/fit.rs:103-122), which a
+ * fitted member stores in `m{i}/meta[4]`. */
+enum { TCU_KV_F32 = 0, TCU_KV_I16 = 1, TCU_KV_I8 = 2 };
+
+typedef struct tcu_ctx tcu_ctx;         /* one device and its stream: gpu::Gpu (src/gpu.rs:725-747) */
+typedef struct tcu_weights tcu_weights; /* in-context weights on the device: gpu::GpuWeights (src/gpu.rs:1838-2028) */
+typedef struct tcu_model tcu_model;     /* one fitted problem's cache on the device: gpu::VramModel (src/gpu.rs:2033-2116) */
+
+/* Sizes of the in-context stage (src/model.rs:110-143): width d, heads, layers, feed-forward width ff
+ * (linear1 rows), scalable-softmax hidden width hid (query_mlp.0 rows), decoder hidden dec_ff (decoder.0 rows),
+ * decoder outputs outs (decoder.2 rows), max_classes (0 for a regression model). */
+typedef struct {
+    int32_t d, heads, layers, ff, hid, dec_ff, outs, max_classes;
+} tcu_icl_shape;
+
+/* ---- context ---------------------------------------------------------------------------------------------- */
+
+/* Open device `device` (gpu::Gpu::new_async, src/gpu.rs:930-971). */
+TCU_API int tcu_open(int device, tcu_ctx **out);
+TCU_API void tcu_close(tcu_ctx *ctx);
+/* Why the last failing call on this context failed ("" if none): VramTier::last_error (src/gpu.rs:2525-2527). */
+TCU_API const char *tcu_last_error(const tcu_ctx *ctx);
+/* Kernels this context has launched so far (each of this library's own kernels counts once per launch). */
+TCU_API uint64_t tcu_launches(const tcu_ctx *ctx);
+
+/* ---- weights (GpuWeights::new, src/gpu.rs:1876; tensor names of src/model.rs:52-98, 236-270) --------------- */
+
+/* Empty weights of this shape; `for_fit` also keeps what fitting needs (key/value rows of in_proj, the
+ * scalable softmax's base MLP, the target embedding). */
+TCU_API int tcu_weights_new(tcu_ctx *ctx, const tcu_icl_shape *shape, int for_fit, tcu_weights **out);
+/* One tensor by its bundle name (e.g. "icl_predictor.tf_icl.blocks.3.linear1.weight"), `count` elements of
+ * dtype 0 = float32 or 1 = float16 (widened exactly, src/store.rs:363-375). Names the stage does not use are
+ * ignored; a layer norm bias never put is zero (src/model.rs:56-57, 261-266). */
+TCU_API int tcu_weights_put(tcu_weights *w, const char *name, int dtype, const void *data, size_t count);
+/* Upload to the device; every needed tensor must have been put. */
+TCU_API int tcu_weights_ready(tcu_weights *w);
+/* The whole of the above from a weight bundle file (Model::load, src/model.rs:202-272, in-context part). */
+TCU_API int tcu_weights_from_bundle(tcu_ctx *ctx, const char *path, int for_fit, tcu_weights **out);
+TCU_API int tcu_weights_shape(const tcu_weights *w, tcu_icl_shape *out);
+TCU_API void tcu_weights_free(tcu_weights *w);
+
+/* ---- resident caches (VramTier::preload / Gpu::load, src/gpu.rs:2546-2556, 2062-2116) ------------------------ */
+
+/* A problem of a fitted member: `meta` is the member's `m{i}/meta` ([rows, features, classes, chunk, kv, digits,
+ * nodes], src/fit.rs:291); node_rows / node_k the problem's rows and outputs from `m{i}/tree`
+ * (src/predict.rs:137-161). */
+TCU_API int tcu_model_new(tcu_weights *w, const int32_t meta[7], int32_t node_rows, int32_t node_k, tcu_model **out);
+/* `n{node}_scale`, [layers][d] floats (src/fit.rs:746). */
+TCU_API int tcu_model_put_scales(tcu_model *m, const float *scales, size_t count);
+/* Bytes [offset, offset + nbytes) of `n{node}_kv{layer}`, exactly as stored (no repacking; src/fit.rs:224-241). */
+TCU_API int tcu_model_put_layer(tcu_model *m, int layer, size_t offset, const void *bytes, size_t nbytes);
+/* The whole of the above from a fitted bundle file, member `prefix` ("m0/", or "" for a raw fit), problem node. */
+TCU_API int tcu_model_from_bundle(tcu_weights *w, const char *path, const char *prefix, int node, tcu_model **out);
+/* Device bytes the cache holds (Gpu::model_bytes, for tier budgets). */
+TCU_API size_t tcu_model_bytes(const tcu_model *m);
+/* Copy back a layer's stored bytes / the scales (for writing a bundle after a device fit). */
+TCU_API int tcu_model_get_layer(const tcu_model *m, int layer, void *bytes, size_t nbytes);
+TCU_API int tcu_model_get_scales(const tcu_model *m, float *scales, size_t count);
+TCU_API void tcu_model_free(tcu_model *m);
+
+/* ---- AttendCached (src/predict.rs:63-79) --------------------------------------------------------------------- */
+
+/* `attend`: attention outputs [rows][d] (before the output projection) for scaled queries q [rows][d] against
+ * in-context layer `layer`. Host buffers. */
+TCU_API int tcu_attend(tcu_model *m, int layer, const float *q, int rows, int d, int heads, float *out);
+/* `stage`: the whole in-context stage, row representations h [rows][d] to the first out_n decoder outputs per
+ * row [rows][out_n]. Host buffers; h is not modified. */
+TCU_API int tcu_stage(tcu_model *m, const float *h, int rows, int d, int out_n, float *out);
+/* The same two on device buffers, queued on `stream` (a cudaStream_t; NULL = the context's stream); inputs are
+ * not modified. */
+TCU_API int tcu_attend_device(tcu_model *m, int layer, const float *q, int rows, float *out, void *stream);
+TCU_API int tcu_stage_device(tcu_model *m, const float *h, int rows, int out_n, float *out, void *stream);
+
+/* ---- heads (src/table.rs) ------------------------------------------------------------------------------------ */
+
+/* Classifier::logit_sums_async (src/table.rs:265-269) for one member: sums[r][c] += logits[r][classes_of[c]]
+ * in f64; then finish_proba (src/table.rs:70-78) when `finish` is nonzero (members, temperature). Device
+ * buffers on the context stream. */
+TCU_API int tcu_class_head_device(tcu_ctx *ctx, const float *logits, int rows, int classes, int stride,
+                          const int32_t *member_classes, double *sums, int finish, int members, double temperature);
+/* Regressor::predict_async (src/table.rs:457-496) for one member: each row's nq quantile outputs read as a
+ * QuantileDist (src/table.rs:292-346); mean, variance, median and the quantiles at alphas, back-transformed,
+ * ADDED to the f64 outputs (divide by the member count at the end). Device buffers. */
+TCU_API int tcu_regression_head_device(tcu_ctx *ctx, const float *qout, int rows, int nq, int stride, const double *alphas,
+                               int na, double target_mean, double target_scale, double *mean, double *variance,
+                               double *median, double *quantiles);
+
+/* ---- fitting's in-context stage on the device (src/fit.rs:577-747) ----------------------------------------- */
+
+/* Training rows h [rows][d] (device; consumed) with targets y [rows] (device; class index or standardised
+ * value) to a resident cache: every layer's keys and values packed as `kv` in chunks of `chunk` rows
+ * (src/fit.rs:549-576) and the query scales. `w` must have been made with for_fit. */
+TCU_API int tcu_fit_icl_device(tcu_weights *w, float *h, const float *y, int rows, int chunk, int kv, tcu_model **out);
+
+/* Pack one chunk: c [2d][rc] floats (device) to its stored record (device, tcu_record bytes): src/fit.rs:549-576. */
+TCU_API int tcu_pack_device(tcu_ctx *ctx, int kv, int d, int rc, const float *c, void *rec);
+/* Bytes of a stored chunk of rc rows (src/fit.rs:124-126). */
+TCU_API size_t tcu_record(int kv, int d, int rc);
+
+/* Measurement hook (no counterpart in the reference, which times stages with wall clocks, src/predict.rs:20-56):
+ * while enabled, every attention pass (one layer's attention kernels) is bracketed by CUDA events on its stream.
+ * A call reads the total device time and count of the passes since the last call (when the pointers are set,
+ * after synchronising the device), then enables or disables timing and starts a new count. */
+TCU_API int tcu_profile(tcu_ctx *ctx, int enable, double *attend_ms, uint64_t *attend_launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

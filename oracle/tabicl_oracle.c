@@ -1,0 +1,823 @@
+/*
+ * TEST INFRASTRUCTURE ONLY - the parity oracle and timed CPU baseline.
+ *
+ * A plain-C restatement of tabicl-anywhere's CPU prediction path (the Rust crate cannot be built here: no Rust
+ * toolchain), used by tests/ as the checker and by bench.py as the CPU baseline. Nothing in the product links,
+ * loads or calls this file. Every function cites the reference file:line it restates (paths inside the
+ * tabicl-anywhere repository). Arithmetic is f32 as in the reference; compiled with -ffp-contract=off so that no
+ * multiply-add is fused unless written as fmaf (the reference's `mul_add_e` inner loops), as Rust never fuses on
+ * its own.
+ *
+ * Parity is pinned by tests/test_oracle_golden.py against the reference's committed golden vectors
+ * (tests/data/tiny-raw.tirs: PyTorch TabICL's row representations, in-context keys/values and logits).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <pthread.h>
+#include <stdatomic.h>
+#include <unistd.h>
+
+#define EXPORT __attribute__((visibility("default")))
+
+/* ---- a small parallel-for over host threads (the reference's rayon `each`, predict.rs:270-278) ---------- */
+
+static int g_threads = 0;
+
+EXPORT void or_set_threads(int n) { g_threads = n; }
+
+EXPORT int or_threads(void) {
+    if (g_threads > 0) return g_threads;
+    const char *e = getenv("ORACLE_THREADS");
+    if (e && atoi(e) > 0) return atoi(e);
+    long n = sysconf(_SC_NPROCESSORS_ONLN);
+    return n > 0 ? (int)n : 1;
+}
+
+typedef struct {
+    void (*fn)(void *, int);
+    void *ctx;
+    int n;
+    atomic_int next;
+} par_job;
+
+static void *par_worker(void *arg) {
+    par_job *j = (par_job *)arg;
+    for (;;) {
+        int i = atomic_fetch_add(&j->next, 1);
+        if (i >= j->n) break;
+        j->fn(j->ctx, i);
+    }
+    return NULL;
+}
+
+static void par_for(int n, void (*fn)(void *, int), void *ctx) {
+    int t = or_threads();
+    if (t > n) t = n;
+    if (t <= 1) {
+        for (int i = 0; i < n; i++) fn(ctx, i);
+        return;
+    }
+    par_job j;
+    j.fn = fn, j.ctx = ctx, j.n = n;
+    atomic_init(&j.next, 0);
+    pthread_t *th = (pthread_t *)malloc(sizeof(pthread_t) * t);
+    for (int k = 1; k < t; k++) pthread_create(&th[k], NULL, par_worker, &j);
+    par_worker(&j);
+    for (int k = 1; k < t; k++) pthread_join(th[k], NULL);
+    free(th);
+}
+
+/* ---- kern.rs: scalar restatements of the inner loops ---------------------------------------------------- */
+
+/* kern.rs:214-216 */
+static const float OR_LOG2E = 1.44269504088896340736f;
+static const float OR_LN2_HI = 0.6933594f;
+static const float OR_LN2_LO = -2.1219444e-4f;
+
+static inline float clampf(float x, float lo, float hi) {
+    /* Rust f32::clamp: NaN stays NaN */
+    if (x < lo) return lo;
+    if (x > hi) return hi;
+    return x;
+}
+
+static inline float f32_from_bits(uint32_t b) {
+    float f;
+    memcpy(&f, &b, 4);
+    return f;
+}
+
+/* kern.rs:220-235 - the reference's own exponential: Cody-Waite reduction and a degree-7 Taylor polynomial,
+ * clamped to [-87, 88]. */
+EXPORT float or_exp1(float x) {
+    x = clampf(x, -87.0f, 88.0f);
+    float n = floorf(x * OR_LOG2E + 0.5f);
+    float r = (x - n * OR_LN2_HI) - n * OR_LN2_LO;
+    float p = 1.0f / 5040.0f;
+    p = p * r + 1.0f / 720.0f;
+    p = p * r + 1.0f / 120.0f;
+    p = p * r + 1.0f / 24.0f;
+    p = p * r + 1.0f / 6.0f;
+    p = p * r + 0.5f;
+    p = p * r + 1.0f;
+    p = p * r + 1.0f;
+    return p * f32_from_bits(((uint32_t)((int32_t)n + 127)) << 23);
+}
+
+/* kern.rs:256-282 - erf by Abramowitz and Stegun 7.1.26, and its power series below 0.5. */
+EXPORT float or_erf1(float x) {
+    float a = fabsf(x);
+    float t = 1.0f / (1.0f + 0.3275911f * a);
+    float p = 1.0614054f;
+    p = p * t - 1.4531521f;
+    p = p * t + 1.4214138f;
+    p = p * t - 0.28449674f;
+    p = p * t + 0.2548296f;
+    float far = copysignf(1.0f - p * t * or_exp1(-a * a), x);
+    float x2 = x * x;
+    float q = -1.0f / 1320.0f;
+    q = q * x2 + 1.0f / 216.0f;
+    q = q * x2 - 1.0f / 42.0f;
+    q = q * x2 + 0.1f;
+    q = q * x2 - 1.0f / 3.0f;
+    q = q * x2 + 1.0f;
+    float near = q * x * 1.12837916709551257390f; /* FRAC_2_SQRT_PI */
+    return a < 0.5f ? near : far;
+}
+
+/* kern.rs:285-290 */
+EXPORT float or_gelu1(float v) { return 0.5f * v * (1.0f + or_erf1(v * 0.70710678118654752440f)); }
+
+static void gelu_inplace(float *x, int n) {
+    for (int i = 0; i < n; i++) x[i] = or_gelu1(x[i]);
+}
+
+/* kern.rs:292-297 */
+EXPORT float or_tanh1(float x) {
+    float e = or_exp1(2.0f * clampf(x, -10.0f, 10.0f));
+    return (e - 1.0f) / (e + 1.0f);
+}
+
+/* kern.rs:42-61 - dot with four running sums (lane order simplified to one chain per sum) */
+static float dot(const float *a, const float *b, int n) {
+    float s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+    int i = 0;
+    for (; i + 4 <= n; i += 4) {
+        s0 = fmaf(a[i], b[i], s0);
+        s1 = fmaf(a[i + 1], b[i + 1], s1);
+        s2 = fmaf(a[i + 2], b[i + 2], s2);
+        s3 = fmaf(a[i + 3], b[i + 3], s3);
+    }
+    float s = (s0 + s1) + (s2 + s3);
+    for (; i < n; i++) s += a[i] * b[i];
+    return s;
+}
+
+/* kern.rs:95-150 matvec, kern.rs:154-159 linear: y = w x (+ b), w is [out][in] */
+static void linear(const float *w, const float *b, const float *x, int in, int out, float *y) {
+    for (int o = 0; o < out; o++) {
+        float v = dot(w + (size_t)o * in, x, in);
+        y[o] = b ? v + b[o] : v;
+    }
+}
+
+/* kern.rs:357-376 - layer norm over the whole vector, eps 1e-5, biased variance */
+static void layer_norm(const float *x, const float *w, const float *b, int n, float *y) {
+    float s = 0;
+    for (int i = 0; i < n; i++) s += x[i];
+    float mean = s / (float)n;
+    float q = 0;
+    for (int i = 0; i < n; i++) {
+        float d = x[i] - mean;
+        q = fmaf(d, d, q);
+    }
+    float var = q / (float)n;
+    float inv = 1.0f / sqrtf(var + 1e-5f);
+    for (int i = 0; i < n; i++) y[i] = (x[i] - mean) * inv * w[i] + b[i];
+}
+
+/* kern.rs:163-197 weighted_sum: acc[i] += sum_r wts[r] * rows[r][i], rows taken four at a time */
+static void weighted_sum(const float *wts, const float *rows, int nrows, int n, float *acc) {
+    int r = 0;
+    for (; r + 4 <= nrows; r += 4) {
+        const float *r0 = rows + (size_t)r * n, *r1 = r0 + n, *r2 = r1 + n, *r3 = r2 + n;
+        for (int i = 0; i < n; i++) {
+            float a = fmaf(wts[r], r0[i], acc[i]);
+            float bb = wts[r + 1] * r1[i];
+            a = fmaf(wts[r + 2], r2[i], a);
+            bb = fmaf(wts[r + 3], r3[i], bb);
+            acc[i] = a + bb;
+        }
+    }
+    for (; r < nrows; r++)
+        for (int i = 0; i < n; i++) acc[i] = fmaf(wts[r], rows[(size_t)r * n + i], acc[i]);
+}
+
+/* kern.rs:302-323 weighted_sum_int, for 16- and 8-bit rows */
+#define WEIGHTED_SUM_INT(NAME, T)                                                                                 \
+    static void NAME(const float *wts, const T *rows, int nrows, int n, float *acc) {                             \
+        int r = 0;                                                                                                \
+        for (; r + 4 <= nrows; r += 4) {                                                                          \
+            const T *r0 = rows + (size_t)r * n, *r1 = r0 + n, *r2 = r1 + n, *r3 = r2 + n;                        \
+            for (int i = 0; i < n; i++)                                                                           \
+                acc[i] += (wts[r] * (float)r0[i] + wts[r + 1] * (float)r1[i]) +                                    \
+                          (wts[r + 2] * (float)r2[i] + wts[r + 3] * (float)r3[i]);                                 \
+        }                                                                                                         \
+        for (; r < nrows; r++)                                                                                    \
+            for (int i = 0; i < n; i++) acc[i] += wts[r] * (float)rows[(size_t)r * n + i];                       \
+    }
+WEIGHTED_SUM_INT(weighted_sum_i16, int16_t)
+WEIGHTED_SUM_INT(weighted_sum_i8, int8_t)
+
+/* kern.rs:328-353 matvec_int: y[j] = rows[j] . x with sixteen running sums */
+#define MATVEC_INT(NAME, T)                                                                                       \
+    static void NAME(const T *rows, const float *x, int n, int nout, float *y) {                                  \
+        for (int j = 0; j < nout; j++) {                                                                          \
+            const T *row = rows + (size_t)j * n;                                                                  \
+            float a[16] = {0};                                                                                    \
+            int i = 0;                                                                                            \
+            for (; i + 16 <= n; i += 16)                                                                          \
+                for (int l = 0; l < 16; l++) a[l] += (float)row[i + l] * x[i + l];                                \
+            float s = 0;                                                                                          \
+            for (int l = 0; l < 8; l++) s += a[l] + a[l + 8];                                                     \
+            for (; i < n; i++) s += (float)row[i] * x[i];                                                         \
+            y[j] = s;                                                                                             \
+        }                                                                                                         \
+    }
+MATVEC_INT(matvec_i16, int16_t)
+MATVEC_INT(matvec_i8, int8_t)
+
+/* kern.rs:95-150 matvec over f32 rows (values [hd][r] times weights [r]) */
+static void matvec(const float *w, const float *x, int n, int nout, float *y) {
+    for (int j = 0; j < nout; j++) y[j] = dot(w + (size_t)j * n, x, n);
+}
+
+/* kern.rs:201-212 */
+static float vmax(const float *x, int n) {
+    float m = -INFINITY;
+    for (int i = 0; i < n; i++) m = x[i] > m ? x[i] : m;
+    return m;
+}
+
+/* kern.rs:239-254 exp_shift_sum: x[i] = e^(x[i] - shift), eight lane sums */
+static float exp_shift_sum(float *x, int n, float shift) {
+    float s[8] = {0};
+    int i = 0;
+    for (; i + 8 <= n; i += 8)
+        for (int l = 0; l < 8; l++) {
+            x[i + l] = or_exp1(x[i + l] - shift);
+            s[l] += x[i + l];
+        }
+    float t = 0;
+    for (int l = 0; l < 8; l++) t += s[l];
+    for (; i < n; i++) {
+        x[i] = or_exp1(x[i] - shift);
+        t += x[i];
+    }
+    return t;
+}
+
+/* ---- the model as the oracle sees it ----------------------------------------------------------------------- */
+
+/* One in-context block (model.rs:27-98); `wkv`/`bkv` are in_proj rows d..3d (fit only), `sb*` the scalable
+ * softmax's base MLP (model.rs:15-24; fit-time query_scale only). */
+typedef struct {
+    const float *n1w, *n1b, *wq, *bq, *q0w, *q0b, *q2w, *q2b, *wo, *bo, *n2w, *n2b, *w1, *b1, *w2, *b2;
+    const float *wkv, *bkv, *sb0w, *sb0b, *sb2w, *sb2b;
+} or_layer;
+
+typedef struct {
+    int d, heads, ff, hid, layers, dff, outs, max_classes;
+    const or_layer *layer;
+    const float *lnw, *lnb, *dec0w, *dec0b, *dec2w, *dec2b;
+    const float *icl_y; /* classifier: [classes][d] (model.rs:163-177); regression: [weight d][bias d] */
+} or_model;
+
+/* fit.rs:103-127: bytes of one stored chunk of `rc` rows */
+EXPORT size_t or_record(int kv, int d, int rc) {
+    int w = kv == 0 ? 4 : (kv == 1 ? 2 : 1);
+    return (size_t)2 * d * rc * w + (kv == 0 ? 0 : (size_t)8 * d);
+}
+
+/* nn.rs:97-107 Block::query_scale: the scalable softmax's length term times 1/sqrt(head width) */
+EXPORT void or_query_scale(const or_model *m, int l, int n, float *out) {
+    const or_layer *b = &m->layer[l];
+    int d = m->d, hd = d / m->heads, hid = m->hid;
+    float inv = 1.0f / sqrtf((float)hd);
+    float logn = logf((float)(n > 1 ? n : 1));
+    float *h = (float *)malloc(sizeof(float) * hid);
+    for (int i = 0; i < hid; i++) h[i] = b->sb0w[i] * logn + b->sb0b[i];
+    gelu_inplace(h, hid);
+    linear(b->sb2w, b->sb2b, h, hid, d, out);
+    for (int i = 0; i < d; i++) out[i] *= inv;
+    free(h);
+}
+
+/* nn.rs:130-152 query: q = scale * (Wq norm1(x) + bq), modulated per head by the query MLP */
+static void query(const or_model *m, int l, const float *scale, const float *x, float *q, float *t, float *h64, float *mm) {
+    const or_layer *b = &m->layer[l];
+    int d = m->d, hd = d / m->heads;
+    layer_norm(x, b->n1w, b->n1b, d, t);
+    linear(b->wq, b->bq, t, d, d, q);
+    for (int h = 0; h < m->heads; h++) {
+        float *qh = q + h * hd;
+        const float *sh = scale + h * hd;
+        linear(b->q0w, b->q0b, qh, hd, m->hid, h64);
+        gelu_inplace(h64, m->hid);
+        linear(b->q2w, b->q2b, h64, m->hid, hd, mm);
+        for (int i = 0; i < hd; i++) qh[i] *= sh[i] * (1.0f + or_tanh1(mm[i]));
+    }
+}
+
+EXPORT void or_query(const or_model *m, int l, const float *scale, const float *x, float *q) {
+    float *t = malloc(sizeof(float) * m->d), *h64 = malloc(sizeof(float) * m->hid), *mm = malloc(sizeof(float) * m->d);
+    query(m, l, scale, x, q, t, h64, mm);
+    free(t), free(h64), free(mm);
+}
+
+/* ---- nn.rs:166-287 Soft: the streaming softmax ------------------------------------------------------------- */
+
+typedef struct {
+    int heads, d;
+    float *m, *s, *acc;
+} soft;
+
+static void soft_reset(soft *s) {
+    for (int h = 0; h < s->heads; h++) s->m[h] = -INFINITY, s->s[h] = 0;
+    memset(s->acc, 0, sizeof(float) * s->d);
+}
+
+/* rescale for a new running maximum (nn.rs:207-215) */
+static void soft_top(soft *st, int h, int hd, float top) {
+    if (top > st->m[h]) {
+        if (st->s[h] > 0) {
+            float f = or_exp1(st->m[h] - top);
+            st->s[h] *= f;
+            for (int i = 0; i < hd; i++) st->acc[h * hd + i] *= f;
+        }
+        st->m[h] = top;
+    }
+}
+
+/* nn.rs:194-228 update_scaled for float keys/values (vs = NULL) */
+static void soft_update_f32(soft *st, const float *q, const float *kt, const float *vt, int r, float *sc, float *tmp) {
+    int hd = st->d / st->heads;
+    for (int h = 0; h < st->heads; h++) {
+        const float *k = kt + (size_t)h * hd * r, *v = vt + (size_t)h * hd * r;
+        memset(sc, 0, sizeof(float) * r);
+        weighted_sum(q + h * hd, k, hd, r, sc);
+        soft_top(st, h, hd, vmax(sc, r));
+        st->s[h] += exp_shift_sum(sc, r, st->m[h]);
+        matvec(v, sc, r, hd, tmp);
+        for (int i = 0; i < hd; i++) st->acc[h * hd + i] += tmp[i];
+    }
+}
+
+/* nn.rs:233-258 update_int: q already multiplied by the keys' scales, vs the values' scales */
+#define SOFT_UPDATE_INT(NAME, T, WS, MV)                                                                          \
+    static void NAME(soft *st, const float *q, const T *kt, const T *vt, const float *vs, int r, float *sc,       \
+                     float *tmp) {                                                                                \
+        int hd = st->d / st->heads;                                                                               \
+        for (int h = 0; h < st->heads; h++) {                                                                     \
+            const T *k = kt + (size_t)h * hd * r, *v = vt + (size_t)h * hd * r;                                   \
+            memset(sc, 0, sizeof(float) * r);                                                                     \
+            WS(q + h * hd, k, hd, r, sc);                                                                         \
+            soft_top(st, h, hd, vmax(sc, r));                                                                     \
+            st->s[h] += exp_shift_sum(sc, r, st->m[h]);                                                           \
+            MV(v, sc, r, hd, tmp);                                                                                \
+            for (int i = 0; i < hd; i++) st->acc[h * hd + i] += tmp[i] * vs[h * hd + i];                          \
+        }                                                                                                         \
+    }
+SOFT_UPDATE_INT(soft_update_i16, int16_t, weighted_sum_i16, matvec_i16)
+SOFT_UPDATE_INT(soft_update_i8, int8_t, weighted_sum_i8, matvec_i8)
+
+/* nn.rs:261-276 merge */
+static void soft_merge(soft *a, const soft *o) {
+    int hd = a->d / a->heads;
+    for (int h = 0; h < a->heads; h++) {
+        if (o->s[h] <= 0) continue;
+        float top = a->m[h] > o->m[h] ? a->m[h] : o->m[h];
+        float fa = a->s[h] > 0 ? or_exp1(a->m[h] - top) : 0.0f;
+        float fb = or_exp1(o->m[h] - top);
+        a->s[h] = a->s[h] * fa + o->s[h] * fb;
+        for (int i = h * hd; i < (h + 1) * hd; i++) a->acc[i] = a->acc[i] * fa + o->acc[i] * fb;
+        a->m[h] = top;
+    }
+}
+
+/* nn.rs:280-286 finish */
+static void soft_finish(soft *st) {
+    int hd = st->d / st->heads;
+    for (int h = 0; h < st->heads; h++) {
+        float inv = 1.0f / st->s[h];
+        for (int i = 0; i < hd; i++) st->acc[h * hd + i] *= inv;
+    }
+}
+
+/* One stored chunk seen in place (predict.rs:459-480): feed it to a running softmax. `qs` is scratch for the
+ * query times the keys' scales (predict.rs:486-497). */
+static void soft_chunk(soft *st, int kv, const uint8_t *rec, int rc, const float *q, float *qs, float *sc, float *tmp) {
+    int d = st->d;
+    if (kv == 0) {
+        const float *kt = (const float *)rec;
+        soft_update_f32(st, q, kt, kt + (size_t)d * rc, rc, sc, tmp);
+        return;
+    }
+    const float *scales = (const float *)rec;
+    for (int i = 0; i < d; i++) qs[i] = q[i] * scales[i];
+    const uint8_t *body = rec + (size_t)8 * d;
+    if (kv == 1) {
+        const int16_t *kt = (const int16_t *)body;
+        soft_update_i16(st, qs, kt, kt + (size_t)d * rc, scales + d, rc, sc, tmp);
+    } else {
+        const int8_t *kt = (const int8_t *)body;
+        soft_update_i8(st, qs, kt, kt + (size_t)d * rc, scales + d, rc, sc, tmp);
+    }
+}
+
+/* Attention of one query against one layer's stored cache, chunks [c0, c1) (predict.rs:431-520 for one reader).
+ * Leaves the running state unfinished so ranges can be merged (predict.rs:521-532). */
+static void attend_range(soft *st, int kv, const uint8_t *layer, int rows, int chunk, int c0, int c1, const float *q,
+                         float *qs, float *sc, float *tmp) {
+    size_t full = or_record(kv, st->d, chunk);
+    for (int ci = c0; ci < c1; ci++) {
+        int rc = rows - ci * chunk < chunk ? rows - ci * chunk : chunk;
+        soft_chunk(st, kv, layer + (size_t)ci * full, rc, q, qs, sc, tmp);
+    }
+}
+
+/* AttendCached::attend semantics (predict.rs:63-66): attention outputs [n][d] for scaled queries [n][d] against
+ * one layer of the cache, split over `parts` readers merged as key_threads does (predict.rs:398-409, 521-532). */
+typedef struct {
+    int kv, d, heads, rows, chunk, parts, n_chunks;
+    const uint8_t *layer;
+    const float *q;
+    float *out;
+} attend_job;
+
+static void attend_one(void *ctx, int r) {
+    const attend_job *j = (const attend_job *)ctx;
+    int d = j->d, heads = j->heads;
+    soft a, b;
+    a.heads = b.heads = heads, a.d = b.d = d;
+    a.m = malloc(sizeof(float) * heads), a.s = malloc(sizeof(float) * heads), a.acc = malloc(sizeof(float) * d);
+    b.m = malloc(sizeof(float) * heads), b.s = malloc(sizeof(float) * heads), b.acc = malloc(sizeof(float) * d);
+    float *qs = malloc(sizeof(float) * d), *sc = malloc(sizeof(float) * j->chunk), *tmp = malloc(sizeof(float) * d);
+    soft_reset(&a);
+    int per = (j->n_chunks + j->parts - 1) / j->parts;
+    for (int p = 0; p < j->parts; p++) {
+        int c0 = p * per, c1 = (p + 1) * per < j->n_chunks ? (p + 1) * per : j->n_chunks;
+        if (c0 >= c1) continue;
+        if (p == 0) {
+            attend_range(&a, j->kv, j->layer, j->rows, j->chunk, c0, c1, j->q + (size_t)r * d, qs, sc, tmp);
+        } else {
+            soft_reset(&b);
+            attend_range(&b, j->kv, j->layer, j->rows, j->chunk, c0, c1, j->q + (size_t)r * d, qs, sc, tmp);
+            soft_merge(&a, &b);
+        }
+    }
+    soft_finish(&a);
+    memcpy(j->out + (size_t)r * d, a.acc, sizeof(float) * d);
+    free(a.m), free(a.s), free(a.acc), free(b.m), free(b.s), free(b.acc), free(qs), free(sc), free(tmp);
+}
+
+EXPORT void or_attend(int kv, int d, int heads, const uint8_t *layer, int rows, int chunk, const float *q, int n,
+                      int parts, float *out) {
+    attend_job j;
+    j.kv = kv, j.d = d, j.heads = heads, j.rows = rows, j.chunk = chunk, j.layer = layer, j.q = q, j.out = out;
+    j.n_chunks = (rows + chunk - 1) / chunk;
+    j.parts = parts < 1 ? 1 : (parts > j.n_chunks ? j.n_chunks : parts);
+    par_for(n, attend_one, &j);
+}
+
+/* ---- predict.rs:381-586 in_context: the whole in-context stage ------------------------------------------- */
+
+typedef struct {
+    const or_model *m;
+    int l;
+    const float *scale, *att;
+    float *h, *q, *logits;
+    int out_n;
+} rows_job;
+
+/* nn.rs:130-152 for one row */
+static void query_one(void *ctx, int r) {
+    const rows_job *j = (const rows_job *)ctx;
+    const or_model *m = j->m;
+    float *t = malloc(sizeof(float) * m->d), *h64 = malloc(sizeof(float) * m->hid), *mm = malloc(sizeof(float) * m->d);
+    query(m, j->l, j->scale, j->h + (size_t)r * m->d, j->q + (size_t)r * m->d, t, h64, mm);
+    free(t), free(h64), free(mm);
+}
+
+/* predict.rs:542-568 for one row: out-projection and residual, then feed-forward and residual */
+static void tail_one(void *ctx, int r) {
+    const rows_job *j = (const rows_job *)ctx;
+    const or_model *m = j->m;
+    const or_layer *b = &m->layer[j->l];
+    int d = m->d, ff = m->ff;
+    float *hr = j->h + (size_t)r * d;
+    float *t = malloc(sizeof(float) * (d > ff ? d : ff)), *mid = malloc(sizeof(float) * ff);
+    linear(b->wo, b->bo, j->att + (size_t)r * d, d, d, t);
+    for (int i = 0; i < d; i++) hr[i] += t[i];
+    layer_norm(hr, b->n2w, b->n2b, d, t);
+    linear(b->w1, b->b1, t, d, ff, mid);
+    gelu_inplace(mid, ff);
+    linear(b->w2, b->b2, mid, ff, d, t);
+    for (int i = 0; i < d; i++) hr[i] += t[i];
+    free(t), free(mid);
+}
+
+/* predict.rs:570-584 decoder for one row */
+static void decode_one(void *ctx, int r) {
+    const rows_job *j = (const rows_job *)ctx;
+    const or_model *m = j->m;
+    int d = m->d, dff = m->dff;
+    float *t = malloc(sizeof(float) * d), *hid = malloc(sizeof(float) * dff), *all = malloc(sizeof(float) * m->outs);
+    layer_norm(j->h + (size_t)r * d, m->lnw, m->lnb, d, t);
+    linear(m->dec0w, m->dec0b, t, d, dff, hid);
+    gelu_inplace(hid, dff);
+    linear(m->dec2w, m->dec2b, hid, dff, m->outs, all);
+    memcpy(j->logits + (size_t)r * j->out_n, all, sizeof(float) * j->out_n);
+    free(t), free(hid), free(all);
+}
+
+/* Row representations h [n][d] (consumed) to the first `out_n` decoder outputs per row. `layers[l]` is the
+ * stored n{node}_kv{l} tensor, `scales` the stored n{node}_scale [L][d]. `parts` > 1 splits the training rows as
+ * key_threads does. */
+EXPORT void or_in_context(const or_model *m, int kv, const uint8_t *const *layers, const float *scales, int rows,
+                          int chunk, float *h, int n, int out_n, int parts, float *logits) {
+    int d = m->d;
+    float *q = malloc(sizeof(float) * (size_t)n * d);
+    float *att = malloc(sizeof(float) * (size_t)n * d);
+    rows_job j;
+    j.m = m, j.h = h, j.q = q, j.att = att, j.logits = logits, j.out_n = out_n;
+    for (int l = 0; l < m->layers; l++) {
+        j.l = l, j.scale = scales + (size_t)l * d;
+        par_for(n, query_one, &j);
+        or_attend(kv, d, m->heads, layers[l], rows, chunk, q, n, parts, att);
+        par_for(n, tail_one, &j);
+    }
+    par_for(n, decode_one, &j);
+    free(q), free(att);
+}
+
+/* ---- fit.rs:549-576 pack: one chunk of keys and values in its stored form --------------------------------- */
+
+static inline int16_t sat_i16(float v) {
+    if (v != v) return 0; /* Rust `as` maps NaN to 0 and saturates */
+    if (v >= 32767.0f) return 32767;
+    if (v <= -32768.0f) return -32768;
+    return (int16_t)v;
+}
+static inline int8_t sat_i8(float v) {
+    if (v != v) return 0;
+    if (v >= 127.0f) return 127;
+    if (v <= -128.0f) return -128;
+    return (int8_t)v;
+}
+
+/* `c` is [2d][rc] floats (keys then values, dimension-major); writes or_record(kv, d, rc) bytes. */
+EXPORT void or_pack(int kv, int d, int rc, const float *c, uint8_t *rec) {
+    if (kv == 0) {
+        memcpy(rec, c, sizeof(float) * 2 * (size_t)d * rc);
+        return;
+    }
+    float top = kv == 1 ? 32767.0f : 127.0f;
+    float *scales = (float *)malloc(sizeof(float) * 2 * d);
+    uint8_t *body = rec + (size_t)8 * d;
+    for (int j = 0; j < 2 * d; j++) {
+        const float *row = c + (size_t)j * rc;
+        float big = 0.0f;
+        for (int i = 0; i < rc; i++) {
+            float a = fabsf(row[i]);
+            big = a > big ? a : big; /* f32::max ignores NaN */
+        }
+        float s = big > 0.0f ? big / top : 1.0f;
+        scales[j] = s;
+        float inv = 1.0f / s;
+        if (kv == 1) {
+            int16_t *o = (int16_t *)(body + (size_t)2 * j * rc);
+            for (int i = 0; i < rc; i++) o[i] = sat_i16(roundf(row[i] * inv));
+        } else {
+            int8_t *o = (int8_t *)(body + (size_t)j * rc);
+            for (int i = 0; i < rc; i++) o[i] = sat_i8(roundf(row[i] * inv));
+        }
+    }
+    memcpy(rec, scales, sizeof(float) * 2 * d);
+    free(scales);
+}
+
+/* predict.rs:590-629 layer_rows: one layer's cache widened to floats, row by row: k, v [rows][d] */
+EXPORT void or_layer_rows(int kv, int d, const uint8_t *layer, int rows, int chunk, float *k, float *v) {
+    size_t full = or_record(kv, d, chunk);
+    for (int ci = 0, r0 = 0; r0 < rows; ci++, r0 += chunk) {
+        int rc = rows - r0 < chunk ? rows - r0 : chunk;
+        const uint8_t *rec = layer + (size_t)ci * full;
+        for (int j = 0; j < 2 * d; j++)
+            for (int r = 0; r < rc; r++) {
+                size_t i = (size_t)j * rc + r;
+                float val;
+                if (kv == 0)
+                    val = ((const float *)rec)[i];
+                else {
+                    const float *sc = (const float *)rec;
+                    const uint8_t *body = rec + (size_t)8 * d;
+                    float in = kv == 1 ? (float)((const int16_t *)body)[i] : (float)((const int8_t *)body)[i];
+                    val = in * sc[j];
+                }
+                if (j < d)
+                    k[(size_t)(r0 + r) * d + j] = val;
+                else
+                    v[(size_t)(r0 + r) * d + j - d] = val;
+            }
+    }
+}
+
+/* ---- fit.rs:577-747: the in-context stage of fitting (the producer of the cache) ------------------------- */
+
+/* model.rs:185-200 add_y */
+EXPORT void or_add_y(const or_model *m, const float *y, int n, float *h) {
+    int d = m->d;
+    for (int r = 0; r < n; r++) {
+        float *cell = h + (size_t)r * d;
+        if (m->max_classes > 0) {
+            const float *row = m->icl_y + (size_t)((int)y[r]) * d;
+            for (int i = 0; i < d; i++) cell[i] += row[i];
+        } else {
+            for (int i = 0; i < d; i++) cell[i] += m->icl_y[i] * y[r] + m->icl_y[d + i];
+        }
+    }
+}
+
+typedef struct {
+    const or_model *m;
+    const or_layer *b;
+    const float *h;
+    float *kvf;
+    uint8_t *out;
+    int rows, chunk, kv;
+    size_t full;
+} kv_job;
+
+/* fit.rs:633-653 for one chunk: keys and values of its rows, dimension-major, then packed */
+static void kv_chunk(void *ctx, int ci) {
+    const kv_job *j = (const kv_job *)ctx;
+    int d = j->m->d, r0 = ci * j->chunk, rc = j->rows - r0 < j->chunk ? j->rows - r0 : j->chunk;
+    float *kt = j->kvf + 2 * (size_t)d * r0, *vt = kt + (size_t)d * rc;
+    float *t = malloc(sizeof(float) * d), *two = malloc(sizeof(float) * 2 * d);
+    for (int r = 0; r < rc; r++) {
+        layer_norm(j->h + (size_t)(r0 + r) * d, j->b->n1w, j->b->n1b, d, t);
+        linear(j->b->wkv, j->b->bkv, t, d, 2 * d, two);
+        for (int c = 0; c < d; c++) kt[(size_t)c * rc + r] = two[c], vt[(size_t)c * rc + r] = two[d + c];
+    }
+    or_pack(j->kv, d, rc, kt, j->out + (size_t)ci * j->full);
+    free(t), free(two);
+}
+
+/* Training rows h [rows][d] (target embedding already added, consumed) to every layer's stored keys and values
+ * (`out[l]` receives the whole n{j}_kv{l} tensor) and the query scales [L][d] (n{j}_scale). The in-memory
+ * path of fit.rs:627-745: keys/values of each chunk packed as written, the layer's attention over the exact
+ * float keys/values. */
+EXPORT void or_icl_fit(const or_model *m, float *h, int rows, int chunk, int kv, uint8_t *const *out, float *scales) {
+    int d = m->d;
+    float *kvf = malloc(sizeof(float) * 2 * (size_t)rows * d); /* chunks of [K: d][rc], [V: d][rc], f32 */
+    float *qall = malloc(sizeof(float) * (size_t)rows * d);
+    float *att = malloc(sizeof(float) * (size_t)rows * d);
+    kv_job kj;
+    kj.m = m, kj.h = h, kj.kvf = kvf, kj.rows = rows, kj.chunk = chunk, kj.kv = kv, kj.full = or_record(kv, d, chunk);
+    rows_job rj;
+    rj.m = m, rj.h = h, rj.q = qall, rj.att = att, rj.logits = NULL, rj.out_n = 0;
+    for (int l = 0; l < m->layers; l++) {
+        float *scale = scales + (size_t)l * d;
+        or_query_scale(m, l, rows, scale);
+        kj.b = &m->layer[l], kj.out = out[l];
+        par_for((rows + chunk - 1) / chunk, kv_chunk, &kj);
+        if (l + 1 == m->layers) break;
+        rj.l = l, rj.scale = scale;
+        par_for(rows, query_one, &rj);
+        or_attend(0, d, m->heads, (const uint8_t *)kvf, rows, chunk, qall, rows, 1, att);
+        par_for(rows, tail_one, &rj);
+    }
+    free(kvf), free(qall), free(att);
+}
+
+/* ---- table.rs heads ------------------------------------------------------------------------------------------ */
+
+/* table.rs:265-269: add one member's logits (in its relabelled class order) to the sums, in f64 */
+EXPORT void or_add_member(double *sums, const float *logits, int n, int classes, int stride, const int32_t *member_classes) {
+    for (int r = 0; r < n; r++)
+        for (int c = 0; c < classes; c++) sums[(size_t)r * classes + c] += (double)logits[(size_t)r * stride + member_classes[c]];
+}
+
+/* table.rs:70-78 finish_proba */
+EXPORT void or_finish_proba(double *sums, int n, int classes, int members, double temperature) {
+    double inv = 1.0 / ((double)members * temperature);
+    for (int r = 0; r < n; r++) {
+        double *row = sums + (size_t)r * classes;
+        double top = -1.7976931348623157e308;
+        for (int c = 0; c < classes; c++) top = row[c] > top ? row[c] : top;
+        double sum = 0;
+        for (int c = 0; c < classes; c++) row[c] = exp((row[c] - top) * inv);
+        for (int c = 0; c < classes; c++) sum += row[c];
+        for (int c = 0; c < classes; c++) row[c] /= sum;
+    }
+}
+
+/* f32 total order key (f32::total_cmp) */
+static inline uint32_t total_key(float f) {
+    uint32_t b;
+    memcpy(&b, &f, 4);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+static int cmp_total(const void *a, const void *b) {
+    uint32_t x = total_key(*(const float *)a), y = total_key(*(const float *)b);
+    return x < y ? -1 : x > y;
+}
+
+typedef struct {
+    float *q, *levels;
+    int n;
+    float tl0, tl1, tr0, tr1;
+} qdist;
+
+/* table.rs:300-317 QuantileDist::new */
+static void qdist_new(qdist *dd, float *q, float *levels, int n) {
+    qsort(q, n, sizeof(float), cmp_total);
+    for (int i = 0; i < n; i++) levels[i] = (float)(i + 1) / (float)(n + 1);
+    int k = n / 4 < 20 ? n / 4 : 20;
+    if (k < 1) k = 1;
+    float ln_l[20], ln_r[20];
+    for (int i = 0; i < k; i++) {
+        float a = levels[i] > 1e-6f ? levels[i] : 1e-6f;
+        ln_l[i] = logf(a);
+        float b = 1.0f - levels[n - k + i];
+        ln_r[i] = logf(b > 1e-6f ? b : 1e-6f);
+    }
+    float sl[2];
+    for (int side = 0; side < 2; side++) {
+        const float *xs = side == 0 ? ln_l : ln_r, *ys = side == 0 ? q : q + n - k;
+        float sx = 0, sy = 0;
+        for (int i = 0; i < k; i++) sx += xs[i];
+        for (int i = 0; i < k; i++) sy += ys[i];
+        float mx = sx / (float)k, my = sy / (float)k;
+        float cov = 0, var = 0;
+        for (int i = 0; i < k; i++) cov += (xs[i] - mx) * (ys[i] - my);
+        cov /= (float)k;
+        for (int i = 0; i < k; i++) var += (xs[i] - mx) * (xs[i] - mx);
+        var /= (float)k;
+        float s = fabsf(cov / (var > 1e-6f ? var : 1e-6f));
+        sl[side] = clampf(s, 0.01f, 100.0f);
+    }
+    float bl = sl[0], br = sl[1];
+    dd->q = q, dd->levels = levels, dd->n = n;
+    dd->tl0 = bl;
+    dd->tl1 = q[0] - bl * logf(levels[0] > 1e-6f ? levels[0] : 1e-6f);
+    dd->tr0 = -br;
+    float lr = levels[n - 1] < 1.0f - 1e-6f ? levels[n - 1] : 1.0f - 1e-6f;
+    dd->tr1 = q[n - 1] + br * logf(1.0f - lr);
+}
+
+/* table.rs:319-345 */
+static float qdist_mean(const qdist *dd) {
+    float s = 0;
+    for (int i = 0; i < dd->n; i++) s += dd->q[i];
+    return s / (float)dd->n;
+}
+static float qdist_variance(const qdist *dd) {
+    float m = qdist_mean(dd), s = 0;
+    for (int i = 0; i < dd->n; i++) s += (dd->q[i] - m) * (dd->q[i] - m);
+    return s / (float)(dd->n - 1);
+}
+static float qdist_icdf(const qdist *dd, float alpha) {
+    int n = dd->n;
+    if (alpha < dd->levels[0]) return dd->tl0 * logf(alpha > 1e-6f ? alpha : 1e-6f) + dd->tl1;
+    if (alpha > dd->levels[n - 1]) {
+        float b = 1.0f - alpha;
+        return dd->tr0 * logf(b > 1e-6f ? b : 1e-6f) + dd->tr1;
+    }
+    if (alpha >= dd->levels[n - 1]) return dd->q[n - 1];
+    int pp = 0; /* partition_point over levels[..n-1] of (l <= alpha) */
+    while (pp < n - 1 && dd->levels[pp] <= alpha) pp++;
+    int i = pp > 0 ? pp - 1 : 0;
+    if (i > n - 2) i = n - 2;
+    float den = dd->levels[i + 1] - dd->levels[i];
+    float t = (alpha - dd->levels[i]) / (den > 1e-6f ? den : 1e-6f);
+    t = clampf(t, 0.0f, 1.0f);
+    return dd->q[i] + t * (dd->q[i + 1] - dd->q[i]);
+}
+
+typedef struct {
+    const float *qout;
+    int nq, stride, na;
+    const double *alphas;
+    double tmean, tscale, *mean, *variance, *median, *quantiles;
+} reg_job;
+
+static void reg_one(void *ctx, int r) {
+    const reg_job *j = (const reg_job *)ctx;
+    float *q = malloc(sizeof(float) * j->nq), *lv = malloc(sizeof(float) * j->nq);
+    memcpy(q, j->qout + (size_t)r * j->stride, sizeof(float) * j->nq);
+    qdist dd;
+    qdist_new(&dd, q, lv, j->nq);
+#define BACK(v) ((double)(v) * j->tscale + j->tmean)
+    j->mean[r] += BACK(qdist_mean(&dd));
+    j->variance[r] += BACK(qdist_variance(&dd));
+    j->median[r] += BACK(qdist_icdf(&dd, 0.5f));
+    for (int a = 0; a < j->na; a++) j->quantiles[(size_t)r * j->na + a] += BACK(qdist_icdf(&dd, (float)j->alphas[a]));
+#undef BACK
+    free(q), free(lv);
+}
+
+/* table.rs:457-496 (one member's share): quantile outputs [n][nq] to mean, variance, median and the quantiles at
+ * `alphas`, back-transformed (v * scale + mean) and added to the f64 outputs; the caller divides by the member
+ * count at the end (table.rs:491-494). */
+EXPORT void or_regression_add(const float *qout, int n, int nq, int stride, const double *alphas, int na,
+                              double target_mean, double target_scale, double *mean, double *variance,
+                              double *median, double *quantiles) {
+    reg_job j;
+    j.qout = qout, j.nq = nq, j.stride = stride, j.na = na, j.alphas = alphas, j.tmean = target_mean;
+    j.tscale = target_scale, j.mean = mean, j.variance = variance, j.median = median, j.quantiles = quantiles;
+    par_for(n, reg_one, &j);
+}

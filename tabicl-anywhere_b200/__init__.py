@@ -1,0 +1,333 @@
+"""B200 backend for tabicl-anywhere's prediction hot path: the Python binding of the C ABI (include/tabicl_b200.h).
+
+The objects mirror the reference's accelerator side (src/gpu.rs, src/predict.rs:63-79):
+
+* `Gpu` - one device (gpu::Gpu)
+* `GpuWeights` - the in-context weights on it (gpu::GpuWeights)
+* `VramModel` - one fitted problem's key/value cache resident on it (gpu::VramModel)
+* `CudaAttend` - the `AttendCached` implementation: `attend`, `stage`, `rows`, each returning None to decline
+
+Everything computes on the GPU through libtabicl_b200.so; there is no CPU path here. The library is built in-tree
+by build.py (sm_100a); importing this package does not build it.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+from . import tirs  # noqa: F401  (bundle reader/writer for callers)
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libtabicl_b200.so")
+
+OK, DECLINED = 0, 1
+KV_F32, KV_I16, KV_I8 = 0, 1, 2
+_c_int, _c_size, _c_void, _c_float_p = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p, ctypes.POINTER(ctypes.c_float)
+
+
+class TcuError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"tabicl_b200 error {code}: {msg}")
+        self.code = code
+
+
+class IclShape(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("d", "heads", "layers", "ff", "hid", "dec_ff", "outs", "max_classes")]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+_lib = None
+
+
+def lib():
+    """The loaded C library (fails loudly if it is not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is not built: run python tabicl-anywhere_b200/build.py")
+    L = ctypes.CDLL(LIB_PATH)
+    P = ctypes.POINTER
+    sig = {
+        "tcu_open": (_c_int, [_c_int, P(_c_void)]),
+        "tcu_close": (None, [_c_void]),
+        "tcu_last_error": (ctypes.c_char_p, [_c_void]),
+        "tcu_launches": (ctypes.c_uint64, [_c_void]),
+        "tcu_weights_new": (_c_int, [_c_void, P(IclShape), _c_int, P(_c_void)]),
+        "tcu_weights_put": (_c_int, [_c_void, ctypes.c_char_p, _c_int, _c_void, _c_size]),
+        "tcu_weights_ready": (_c_int, [_c_void]),
+        "tcu_weights_from_bundle": (_c_int, [_c_void, ctypes.c_char_p, _c_int, P(_c_void)]),
+        "tcu_weights_shape": (_c_int, [_c_void, P(IclShape)]),
+        "tcu_weights_free": (None, [_c_void]),
+        "tcu_model_new": (_c_int, [_c_void, P(ctypes.c_int32), ctypes.c_int32, ctypes.c_int32, P(_c_void)]),
+        "tcu_model_put_scales": (_c_int, [_c_void, _c_float_p, _c_size]),
+        "tcu_model_put_layer": (_c_int, [_c_void, _c_int, _c_size, _c_void, _c_size]),
+        "tcu_model_from_bundle": (_c_int, [_c_void, ctypes.c_char_p, ctypes.c_char_p, _c_int, P(_c_void)]),
+        "tcu_model_bytes": (_c_size, [_c_void]),
+        "tcu_model_get_layer": (_c_int, [_c_void, _c_int, _c_void, _c_size]),
+        "tcu_model_get_scales": (_c_int, [_c_void, _c_float_p, _c_size]),
+        "tcu_model_free": (None, [_c_void]),
+        "tcu_attend": (_c_int, [_c_void, _c_int, _c_float_p, _c_int, _c_int, _c_int, _c_float_p]),
+        "tcu_stage": (_c_int, [_c_void, _c_float_p, _c_int, _c_int, _c_int, _c_float_p]),
+        "tcu_attend_device": (_c_int, [_c_void, _c_int, _c_void, _c_int, _c_void, _c_void]),
+        "tcu_stage_device": (_c_int, [_c_void, _c_void, _c_int, _c_int, _c_void, _c_void]),
+        "tcu_class_head_device": (_c_int, [_c_void, _c_void, _c_int, _c_int, _c_int, _c_void, _c_void, _c_int, _c_int,
+                                           ctypes.c_double]),
+        "tcu_regression_head_device": (_c_int, [_c_void, _c_void, _c_int, _c_int, _c_int, _c_void, _c_int,
+                                                ctypes.c_double, ctypes.c_double, _c_void, _c_void, _c_void, _c_void]),
+        "tcu_fit_icl_device": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_int, P(_c_void)]),
+        "tcu_pack_device": (_c_int, [_c_void, _c_int, _c_int, _c_int, _c_void, _c_void]),
+        "tcu_record": (_c_size, [_c_int, _c_int, _c_int]),
+        "tcu_profile": (_c_int, [_c_void, _c_int, P(ctypes.c_double), P(ctypes.c_uint64)]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype, f.argtypes = res, args
+    _lib = L
+    return L
+
+
+def exported_symbols():
+    """Names of the entry points this binding declares (every one is in include/tabicl_b200.h)."""
+    lib()
+    return [n for n in dir(_lib) if n.startswith("tcu_")]
+
+
+def record(kv, d, rc):
+    """Bytes of one stored chunk of rc rows (src/fit.rs:124-126)."""
+    return int(lib().tcu_record(kv, d, rc))
+
+
+def _f32p(a):
+    return a.ctypes.data_as(_c_float_p)
+
+
+class Gpu:
+    """One device (gpu::Gpu, src/gpu.rs:725-747)."""
+
+    def __init__(self, device=0):
+        self._h = _c_void()
+        r = lib().tcu_open(device, ctypes.byref(self._h))
+        if r != OK:
+            raise TcuError(r, f"cannot open CUDA device {device}")
+        self.device = device
+
+    def check(self, r):
+        if r < 0:
+            raise TcuError(r, self.last_error)
+        return r
+
+    @property
+    def last_error(self):
+        return lib().tcu_last_error(self._h).decode()
+
+    @property
+    def launches(self):
+        return int(lib().tcu_launches(self._h))
+
+    def profile(self, enable):
+        """Start (or stop) event timing of the attention passes; returns (total ms, passes) since the last call."""
+        ms, n = ctypes.c_double(), ctypes.c_uint64()
+        self.check(lib().tcu_profile(self._h, int(enable), ctypes.byref(ms), ctypes.byref(n)))
+        return ms.value, n.value
+
+    def close(self):
+        if self._h:
+            lib().tcu_close(self._h)
+            self._h = _c_void()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # heads (src/table.rs) on device buffers given as raw pointers (e.g. torch tensors' data_ptr())
+    def class_head(self, logits_ptr, rows, classes, stride, member_classes_ptr, sums_ptr, finish=False, members=1,
+                   temperature=0.9):
+        return self.check(lib().tcu_class_head_device(self._h, logits_ptr, rows, classes, stride, member_classes_ptr,
+                                                      sums_ptr, int(finish), members, temperature))
+
+    def regression_head(self, qout_ptr, rows, nq, stride, alphas_ptr, na, target_mean, target_scale, mean_ptr,
+                        var_ptr, median_ptr, quant_ptr):
+        return self.check(lib().tcu_regression_head_device(self._h, qout_ptr, rows, nq, stride, alphas_ptr, na,
+                                                           target_mean, target_scale, mean_ptr, var_ptr, median_ptr,
+                                                           quant_ptr))
+
+    def pack(self, kv, d, rc, c_ptr, rec_ptr):
+        return self.check(lib().tcu_pack_device(self._h, kv, d, rc, c_ptr, rec_ptr))
+
+
+class GpuWeights:
+    """The in-context weights on the device (gpu::GpuWeights, src/gpu.rs:1838-2028)."""
+
+    def __init__(self, gpu, handle):
+        self.gpu, self._h = gpu, handle
+
+    @staticmethod
+    def from_bundle(gpu, path, for_fit=False):
+        h = _c_void()
+        gpu.check(lib().tcu_weights_from_bundle(gpu._h, os.fsencode(path), int(for_fit), ctypes.byref(h)))
+        return GpuWeights(gpu, h)
+
+    @staticmethod
+    def from_tensors(gpu, shape, tensors, for_fit=False):
+        """`shape`: dict of IclShape fields; `tensors`: bundle name -> float32/float16 array."""
+        h = _c_void()
+        s = IclShape(**shape)
+        gpu.check(lib().tcu_weights_new(gpu._h, ctypes.byref(s), int(for_fit), ctypes.byref(h)))
+        w = GpuWeights(gpu, h)
+        for name, a in tensors.items():
+            a = np.ascontiguousarray(a)
+            dt = 1 if a.dtype == np.float16 else 0
+            if dt == 0:
+                a = np.ascontiguousarray(a, dtype=np.float32)
+            gpu.check(lib().tcu_weights_put(h, name.encode(), dt, a.ctypes.data, a.size))
+        gpu.check(lib().tcu_weights_ready(h))
+        return w
+
+    @property
+    def shape(self):
+        s = IclShape()
+        self.gpu.check(lib().tcu_weights_shape(self._h, ctypes.byref(s)))
+        return s.as_dict()
+
+    def free(self):
+        if self._h:
+            lib().tcu_weights_free(self._h)
+            self._h = _c_void()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class VramModel:
+    """One fitted problem's cache resident on the device (gpu::VramModel, src/gpu.rs:2033-2116)."""
+
+    def __init__(self, weights, handle):
+        self.weights, self.gpu, self._h = weights, weights.gpu, handle
+        self.d = weights.shape["d"]
+
+    @staticmethod
+    def from_bundle(weights, path, prefix="", node=0):
+        h = _c_void()
+        weights.gpu.check(lib().tcu_model_from_bundle(weights._h, os.fsencode(path), prefix.encode(), node,
+                                                      ctypes.byref(h)))
+        return VramModel(weights, h)
+
+    @staticmethod
+    def from_parts(weights, meta, node_rows, node_k, scales, layers):
+        """`meta`: the member's 7 meta ints; `scales` [layers][d] floats; `layers`: each layer's stored bytes."""
+        h = _c_void()
+        meta = np.ascontiguousarray(meta, dtype=np.int32)
+        g = weights.gpu
+        g.check(lib().tcu_model_new(weights._h, meta.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), node_rows, node_k,
+                                    ctypes.byref(h)))
+        m = VramModel(weights, h)
+        sc = np.ascontiguousarray(scales, dtype=np.float32).reshape(-1)
+        g.check(lib().tcu_model_put_scales(h, _f32p(sc), sc.size))
+        for l, b in enumerate(layers):
+            b = np.frombuffer(bytes(b), dtype=np.uint8)
+            g.check(lib().tcu_model_put_layer(h, l, 0, b.ctypes.data, b.size))
+        return m
+
+    @property
+    def nbytes(self):
+        return int(lib().tcu_model_bytes(self._h))
+
+    def attend(self, layer, q):
+        q = np.ascontiguousarray(q, dtype=np.float32).reshape(-1, self.d)
+        out = np.empty_like(q)
+        s = self.weights.shape
+        self.gpu.check(lib().tcu_attend(self._h, layer, _f32p(q), q.shape[0], self.d, s["heads"], _f32p(out)))
+        return out
+
+    def stage(self, h, out_n, out=None):
+        """AttendCached::stage on host buffers: [rows][d] representations to [rows][out_n] decoder outputs
+        (`out`, if given, is filled: pinned host buffers make the copies faster)."""
+        h = np.ascontiguousarray(h, dtype=np.float32).reshape(-1, self.d)
+        if out is None:
+            out = np.empty((h.shape[0], out_n), dtype=np.float32)
+        assert out.dtype == np.float32 and out.flags.c_contiguous and out.size == h.shape[0] * out_n
+        self.gpu.check(lib().tcu_stage(self._h, _f32p(h), h.shape[0], self.d, out_n, _f32p(out)))
+        return out
+
+    def attend_device(self, layer, q_ptr, rows, out_ptr, stream=None):
+        return self.gpu.check(lib().tcu_attend_device(self._h, layer, q_ptr, rows, out_ptr, stream))
+
+    def stage_device(self, h_ptr, rows, out_n, out_ptr, stream=None):
+        return self.gpu.check(lib().tcu_stage_device(self._h, h_ptr, rows, out_n, out_ptr, stream))
+
+    def layer_bytes(self, layer, nbytes):
+        out = np.empty(nbytes, dtype=np.uint8)
+        self.gpu.check(lib().tcu_model_get_layer(self._h, layer, out.ctypes.data, nbytes))
+        return out
+
+    def scales(self):
+        s = self.weights.shape
+        out = np.empty(s["layers"] * s["d"], dtype=np.float32)
+        self.gpu.check(lib().tcu_model_get_scales(self._h, _f32p(out), out.size))
+        return out.reshape(s["layers"], s["d"])
+
+    def free(self):
+        if self._h:
+            lib().tcu_model_free(self._h)
+            self._h = _c_void()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def fit_icl(weights, h_ptr, y_ptr, rows, chunk=256, kv=KV_F32):
+    """Fitting's in-context stage on the device (src/fit.rs:577-747): training rows h (device [rows][d], consumed)
+    and targets y (device [rows] float) to a resident cache."""
+    h = _c_void()
+    weights.gpu.check(lib().tcu_fit_icl_device(weights._h, h_ptr, y_ptr, rows, chunk, kv, ctypes.byref(h)))
+    return VramModel(weights, h)
+
+
+class CudaAttend:
+    """The `AttendCached` implementation (src/predict.rs:63-79) over the members of one fitted bundle.
+
+    Each member's problem is loaded on first use (VramHandle::resident, src/gpu.rs:2674-2700 loads it on a thread
+    and declines meanwhile; here the load happens in the call). Device failures decline (None) and are counted,
+    as VramHandle::or_cpu does (src/gpu.rs:2658-2671).
+    """
+
+    def __init__(self, weights, bundle_path):
+        self.weights, self.path = weights, bundle_path
+        self.models = {}
+        self.fallbacks = 0
+        self.last_error = None
+
+    def _model(self, prefix, node):
+        key = (prefix, node)
+        if key not in self.models:
+            self.models[key] = VramModel.from_bundle(self.weights, self.path, prefix, node)
+        return self.models[key]
+
+    def _or_cpu(self, f):
+        try:
+            return f()
+        except TcuError as e:
+            self.fallbacks += 1
+            self.last_error = str(e)
+            return None
+
+    def attend(self, prefix, node, layer, q, d, heads):
+        return self._or_cpu(lambda: self._model(prefix, node).attend(layer, q))
+
+    def stage(self, prefix, node, h, d, out_n):
+        return self._or_cpu(lambda: self._model(prefix, node).stage(h, out_n))
+
+    def rows(self, prefix, x, out_n):
+        # the column and row stages are not on the device yet: decline, the caller's CPU path does them
+        return None

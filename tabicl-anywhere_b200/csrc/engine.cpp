@@ -1,0 +1,901 @@
+// Host side of the B200 backend: the context, the in-context weights on the device, resident caches, the stage
+// and attention drivers (the AttendCached hook, src/predict.rs:63-79 of tabicl-anywhere), fitting's in-context
+// stage on the device, and the C ABI of include/tabicl_b200.h.
+#include "../../include/tabicl_b200.h"
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+#include "tirs.hpp"
+
+namespace tcu {
+
+struct Error {
+    int code;
+    std::string msg;
+};
+
+#define CU(call)                                                                                     \
+    do {                                                                                             \
+        cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess) throw Error{e_ == cudaErrorMemoryAllocation ? TCU_ERR_MEMORY : TCU_ERR_CUDA, \
+                                           std::string(#call) + ": " + cudaGetErrorString(e_)};      \
+    } while (0)
+
+static void fail(int code, const std::string &m) { throw Error{code, m}; }
+
+// Device memory owned by a handle.
+struct DevBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf &) = delete;
+    DevBuf &operator=(const DevBuf &) = delete;
+    ~DevBuf() { release(); }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr, bytes = 0;
+    }
+    void ensure(size_t n) {
+        if (n <= bytes) return;
+        release();
+        CU(cudaMalloc(&p, n));
+        bytes = n;
+    }
+    template <typename T>
+    T *as() const {
+        return reinterpret_cast<T *>(p);
+    }
+};
+
+}  // namespace tcu
+
+using namespace tcu;
+
+struct tcu_ctx {
+    int device = 0;
+    int sms = 148;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    std::recursive_mutex mu;
+    uint64_t launches = 0;
+    // optional event timing of the attention launches (tcu_profile): pairs of events, read after the fact
+    bool prof = false;
+    std::vector<cudaEvent_t> prof_events;
+    size_t prof_used = 0;
+};
+
+// Device pointers of one in-context block (src/model.rs:27-98), plus what fitting adds.
+struct LayerPtrs {
+    const float *n1w, *n1b, *wq, *bq, *q0w, *q0b, *q2w, *q2b, *wo, *bo, *n2w, *n2b, *w1, *b1, *w2, *b2;
+    const float *wkv, *bkv;  // fit only: in_proj rows d..3d
+};
+
+struct tcu_weights {
+    tcu_ctx *ctx = nullptr;
+    tcu_icl_shape shape{};
+    bool for_fit = false;
+    std::map<std::string, std::vector<float>> host;  // as put, widened to f32
+    DevBuf dev;
+    std::vector<LayerPtrs> layer;
+    const float *lnw = nullptr, *lnb = nullptr, *dec0w = nullptr, *dec0b = nullptr, *dec2w = nullptr, *dec2b = nullptr;
+    const float *icl_y = nullptr;  // fit: class table (model.rs:163-177)
+    bool ready = false;
+    // fit-time query scale pieces (the base MLP of the scalable softmax), kept on the host: nn.rs:97-107
+    std::vector<std::vector<float>> sb0w, sb0b, sb2w, sb2b;
+};
+
+struct tcu_model {
+    tcu_weights *w = nullptr;
+    int rows = 0, chunk = 0, kv = 0, classes = 0, features = 0;
+    size_t full = 0, layer_bytes = 0, layer_stride = 0;
+    DevBuf layers, scales, items, tiles;
+    int nitems = 0, ntiles = 0;
+    std::vector<bool> have_layer;
+    bool have_scales = false;
+    // working memory, grown to the largest call so far
+    DevBuf h, q, att, mid, stats, out, part_ms, part_acc;
+};
+
+namespace tcu {
+
+static int status_of(tcu_ctx *ctx, const Error &e) {
+    if (ctx) ctx->err = e.msg;
+    return e.code;
+}
+
+template <typename F>
+static int guarded(tcu_ctx *ctx, F f) {
+    if (!ctx) return TCU_ERR_ARG;
+    std::lock_guard<std::recursive_mutex> lock(ctx->mu);
+    try {
+        CU(cudaSetDevice(ctx->device));
+        int r = f();
+        return r;
+    } catch (const Error &e) {
+        return status_of(ctx, e);
+    } catch (const BundleError &e) {
+        ctx->err = e.what();
+        return e.code;
+    } catch (const std::bad_alloc &) {
+        ctx->err = "host memory exhausted";
+        return TCU_ERR_MEMORY;
+    } catch (const std::exception &e) {
+        ctx->err = e.what();
+        return TCU_ERR_ARG;
+    }
+}
+
+// ---- host restatement of the fit-time query scale (nn.rs:97-107), with the reference's own formulas --------
+
+static float h_exp1(float x) {
+    x = x < -87.0f ? -87.0f : (x > 88.0f ? 88.0f : x);
+    volatile float t = x * 1.44269504088896340736f;  // keep the multiply and add unfused, as the reference does
+    float n = std::floor(t + 0.5f);
+    volatile float a = n * 0.6933594f;
+    volatile float b = n * -2.1219444e-4f;
+    float r = (x - a) - b;
+    float p = 1.0f / 5040.0f;
+    p = p * r + 1.0f / 720.0f;
+    p = p * r + 1.0f / 120.0f;
+    p = p * r + 1.0f / 24.0f;
+    p = p * r + 1.0f / 6.0f;
+    p = p * r + 0.5f;
+    p = p * r + 1.0f;
+    p = p * r + 1.0f;
+    uint32_t bits = ((uint32_t)((int32_t)n + 127)) << 23;
+    float sc;
+    std::memcpy(&sc, &bits, 4);
+    return p * sc;
+}
+static float h_erf1(float x) {
+    float a = std::fabs(x);
+    float t = 1.0f / (1.0f + 0.3275911f * a);
+    float p = 1.0614054f;
+    p = p * t - 1.4531521f;
+    p = p * t + 1.4214138f;
+    p = p * t - 0.28449674f;
+    p = p * t + 0.2548296f;
+    float far = std::copysign(1.0f - p * t * h_exp1(-a * a), x);
+    float x2 = x * x;
+    float q = -1.0f / 1320.0f;
+    q = q * x2 + 1.0f / 216.0f;
+    q = q * x2 - 1.0f / 42.0f;
+    q = q * x2 + 0.1f;
+    q = q * x2 - 1.0f / 3.0f;
+    q = q * x2 + 1.0f;
+    float near = q * x * 1.12837916709551257390f;
+    return a < 0.5f ? near : far;
+}
+static float h_gelu(float v) { return 0.5f * v * (1.0f + h_erf1(v * 0.70710678118654752440f)); }
+
+static std::vector<float> query_scale(const tcu_weights *w, int l, int n) {
+    const int d = w->shape.d, hd = d / w->shape.heads;
+    const auto &b0w = w->sb0w[l], &b0b = w->sb0b[l], &b2w = w->sb2w[l], &b2b = w->sb2b[l];
+    const int hid = (int)b0b.size();
+    float inv = 1.0f / std::sqrt((float)hd);
+    float logn = std::log((float)(n > 1 ? n : 1));
+    std::vector<float> h(hid), out(d);
+    for (int i = 0; i < hid; i++) h[i] = h_gelu(b0w[i] * logn + b0b[i]);
+    for (int o = 0; o < d; o++) {
+        float s = 0.f;
+        for (int i = 0; i < hid; i++) s += b2w[(size_t)o * hid + i] * h[i];
+        out[o] = (s + b2b[o]) * inv;
+    }
+    return out;
+}
+
+// ---- weights ---------------------------------------------------------------------------------------------------
+
+static std::string blk(int l, const char *name) { return "icl_predictor.tf_icl.blocks." + std::to_string(l) + "." + name; }
+
+static const std::vector<float> &need(const tcu_weights *w, const std::string &name, size_t count) {
+    auto it = w->host.find(name);
+    if (it == w->host.end()) fail(TCU_ERR_STATE, "weights: tensor " + name + " was never put");
+    if (it->second.size() != count)
+        fail(TCU_ERR_FORMAT, "weights: " + name + " has " + std::to_string(it->second.size()) + " values, expected " + std::to_string(count));
+    return it->second;
+}
+
+static std::vector<float> opt_zero(const tcu_weights *w, const std::string &name, size_t count) {
+    auto it = w->host.find(name);
+    if (it == w->host.end()) return std::vector<float>(count, 0.f);  // a layer norm trained without bias
+    if (it->second.size() != count) fail(TCU_ERR_FORMAT, "weights: " + name + " has the wrong length");
+    return it->second;
+}
+
+static int weights_ready(tcu_weights *w) {
+    const auto &s = w->shape;
+    const int d = s.d, L = s.layers, ff = s.ff, hid = s.hid, hd = d / s.heads, dff = s.dec_ff, outs = s.outs;
+    // gather every tensor in device order, each 256-byte aligned
+    std::vector<std::pair<std::vector<float>, const float **>> parts;
+    std::vector<float> flat;
+    std::vector<size_t> offs;
+    auto add = [&](const std::vector<float> &v) {
+        size_t at = (flat.size() + 63) / 64 * 64;
+        flat.resize(at + v.size());
+        std::memcpy(flat.data() + at, v.data(), v.size() * sizeof(float));
+        offs.push_back(at);
+        return offs.size() - 1;
+    };
+    struct LIdx {
+        size_t n1w, n1b, wq, bq, q0w, q0b, q2w, q2b, wo, bo, n2w, n2b, w1, b1, w2, b2, wkv, bkv;
+    };
+    std::vector<LIdx> li(L);
+    w->sb0w.assign(L, {}), w->sb0b.assign(L, {}), w->sb2w.assign(L, {}), w->sb2b.assign(L, {});
+    for (int l = 0; l < L; l++) {
+        const auto &inw = need(w, blk(l, "attn.in_proj_weight"), (size_t)3 * d * d);
+        const auto &inb = need(w, blk(l, "attn.in_proj_bias"), (size_t)3 * d);
+        LIdx &x = li[l];
+        x.n1w = add(need(w, blk(l, "norm1.weight"), d));
+        x.n1b = add(opt_zero(w, blk(l, "norm1.bias"), d));
+        x.wq = add(std::vector<float>(inw.begin(), inw.begin() + (size_t)d * d));
+        x.bq = add(std::vector<float>(inb.begin(), inb.begin() + d));
+        x.q0w = add(need(w, blk(l, "attn.ssmax_layer.query_mlp.0.weight"), (size_t)hid * hd));
+        x.q0b = add(need(w, blk(l, "attn.ssmax_layer.query_mlp.0.bias"), hid));
+        x.q2w = add(need(w, blk(l, "attn.ssmax_layer.query_mlp.2.weight"), (size_t)hd * hid));
+        x.q2b = add(need(w, blk(l, "attn.ssmax_layer.query_mlp.2.bias"), hd));
+        x.wo = add(need(w, blk(l, "attn.out_proj.weight"), (size_t)d * d));
+        x.bo = add(need(w, blk(l, "attn.out_proj.bias"), d));
+        x.n2w = add(need(w, blk(l, "norm2.weight"), d));
+        x.n2b = add(opt_zero(w, blk(l, "norm2.bias"), d));
+        x.w1 = add(need(w, blk(l, "linear1.weight"), (size_t)ff * d));
+        x.b1 = add(need(w, blk(l, "linear1.bias"), ff));
+        x.w2 = add(need(w, blk(l, "linear2.weight"), (size_t)d * ff));
+        x.b2 = add(need(w, blk(l, "linear2.bias"), d));
+        if (w->for_fit) {
+            x.wkv = add(std::vector<float>(inw.begin() + (size_t)d * d, inw.end()));
+            x.bkv = add(std::vector<float>(inb.begin() + d, inb.end()));
+            auto b0b = w->host.find(blk(l, "attn.ssmax_layer.base_mlp.0.bias"));
+            if (b0b == w->host.end()) fail(TCU_ERR_STATE, "weights: the scalable softmax's base MLP is needed to fit");
+            const size_t bh = b0b->second.size();
+            w->sb0w[l] = need(w, blk(l, "attn.ssmax_layer.base_mlp.0.weight"), bh);
+            w->sb0b[l] = b0b->second;
+            w->sb2w[l] = need(w, blk(l, "attn.ssmax_layer.base_mlp.2.weight"), (size_t)d * bh);
+            w->sb2b[l] = need(w, blk(l, "attn.ssmax_layer.base_mlp.2.bias"), d);
+        }
+    }
+    size_t i_lnw = add(need(w, "icl_predictor.ln.weight", d));
+    size_t i_lnb = add(opt_zero(w, "icl_predictor.ln.bias", d));
+    size_t i_d0w = add(need(w, "icl_predictor.decoder.0.weight", (size_t)dff * d));
+    size_t i_d0b = add(need(w, "icl_predictor.decoder.0.bias", dff));
+    size_t i_d2w = add(need(w, "icl_predictor.decoder.2.weight", (size_t)outs * dff));
+    size_t i_d2b = add(need(w, "icl_predictor.decoder.2.bias", outs));
+    size_t i_y = 0;
+    if (w->for_fit) {
+        // model.rs:163-177 class_table: one embedding row per class, or [weight][bias] for regression
+        const int mc = s.max_classes;
+        const auto &yw = need(w, "icl_predictor.y_encoder.weight", (size_t)d * (mc > 0 ? mc : 1));
+        const auto &yb = need(w, "icl_predictor.y_encoder.bias", d);
+        std::vector<float> t;
+        if (mc == 0) {
+            t = yw;
+            t.insert(t.end(), yb.begin(), yb.end());
+        } else {
+            t.assign((size_t)mc * d, 0.f);
+            for (int c = 0; c < mc; c++)
+                for (int o = 0; o < d; o++) t[(size_t)c * d + o] = yw[(size_t)o * mc + c] + yb[o];
+        }
+        i_y = add(t);
+    }
+    w->dev.ensure(flat.size() * sizeof(float));
+    CU(cudaMemcpy(w->dev.p, flat.data(), flat.size() * sizeof(float), cudaMemcpyHostToDevice));
+    const float *base = w->dev.as<float>();
+    auto P = [&](size_t idx) { return base + offs[idx]; };
+    w->layer.resize(L);
+    for (int l = 0; l < L; l++) {
+        const LIdx &x = li[l];
+        LayerPtrs &p = w->layer[l];
+        p = LayerPtrs{P(x.n1w), P(x.n1b), P(x.wq), P(x.bq), P(x.q0w), P(x.q0b), P(x.q2w), P(x.q2b), P(x.wo), P(x.bo),
+                      P(x.n2w), P(x.n2b), P(x.w1), P(x.b1), P(x.w2), P(x.b2), nullptr, nullptr};
+        if (w->for_fit) p.wkv = P(x.wkv), p.bkv = P(x.bkv);
+    }
+    w->lnw = P(i_lnw), w->lnb = P(i_lnb), w->dec0w = P(i_d0w), w->dec0b = P(i_d0b), w->dec2w = P(i_d2w), w->dec2b = P(i_d2b);
+    w->icl_y = w->for_fit ? P(i_y) : nullptr;
+    w->host.clear();
+    w->ready = true;
+    return TCU_OK;
+}
+
+// model.rs:157-161 cfg_value: the text after "key": up to the next comma or brace, quotes trimmed
+static std::string cfg_value(const std::string &cfg, const std::string &key) {
+    size_t at = cfg.find("\"" + key + "\"");
+    if (at == std::string::npos) return "(missing)";
+    size_t colon = cfg.find(':', at);
+    if (colon == std::string::npos) return "(missing)";
+    size_t end = cfg.find_first_of(",}", colon + 1);
+    std::string v = cfg.substr(colon + 1, end == std::string::npos ? std::string::npos : end - colon - 1);
+    size_t a = v.find_first_not_of(" \t\n\""), b = v.find_last_not_of(" \t\n\"");
+    return a == std::string::npos ? "" : v.substr(a, b - a + 1);
+}
+
+// ---- resident caches ------------------------------------------------------------------------------------------
+
+static size_t layer_bytes_of(int kv, int d, int rows, int chunk) {
+    // fit.rs:234 raw_entries: full chunks, then the remainder's record
+    return (size_t)(rows / chunk) * record_bytes(kv, d, chunk) + (rows % chunk ? record_bytes(kv, d, rows % chunk) : 0);
+}
+
+static void model_init(tcu_model *m, tcu_weights *w, int rows, int chunk, int kv, int classes) {
+    const int d = w->shape.d, L = w->shape.layers;
+    if (rows <= 0 || chunk < 1 || kv < 0 || kv > 2) fail(TCU_ERR_ARG, "cache: bad rows, chunk or kv format");
+    m->w = w, m->rows = rows, m->chunk = chunk, m->kv = kv, m->classes = classes;
+    m->full = record_bytes(kv, d, chunk);
+    m->layer_bytes = layer_bytes_of(kv, d, rows, chunk);
+    m->layer_stride = (m->layer_bytes + 255) / 256 * 256;
+    m->layers.ensure(m->layer_stride * L);
+    m->scales.ensure(sizeof(float) * (size_t)L * d);
+    m->have_layer.assign(L, false);
+    // decode items and flash tiles: the same for every layer and head
+    const int ks = decode_keys_per_item(kv);
+    std::vector<int2> items;
+    std::vector<int4> tiles;
+    for (int ci = 0, r0 = 0; r0 < rows; ci++, r0 += chunk) {
+        int rc = std::min(chunk, rows - r0);
+        for (int k0 = 0; k0 < rc; k0 += ks) items.push_back(make_int2(ci, k0));
+        for (int k0 = 0; k0 < rc; k0 += FLASH_KEYS) tiles.push_back(make_int4(ci, k0, std::min(FLASH_KEYS, rc - k0), 0));
+    }
+    m->nitems = (int)items.size(), m->ntiles = (int)tiles.size();
+    m->items.ensure(items.size() * sizeof(int2));
+    m->tiles.ensure(tiles.size() * sizeof(int4));
+    CU(cudaMemcpy(m->items.p, items.data(), items.size() * sizeof(int2), cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(m->tiles.p, tiles.data(), tiles.size() * sizeof(int4), cudaMemcpyHostToDevice));
+}
+
+static const uint8_t *layer_ptr(const tcu_model *m, int l) { return m->layers.as<uint8_t>() + m->layer_stride * (size_t)l; }
+
+static void check_ready(const tcu_model *m) {
+    if (!m->w->ready) fail(TCU_ERR_STATE, "weights not ready");
+    if (!m->have_scales) fail(TCU_ERR_STATE, "cache: query scales were never put");
+    for (size_t l = 0; l < m->have_layer.size(); l++)
+        if (!m->have_layer[l]) fail(TCU_ERR_STATE, "cache: layer " + std::to_string(l) + " was never put");
+}
+
+// ---- the in-context stage -----------------------------------------------------------------------------------
+
+struct Launch {
+    tcu_ctx *ctx;
+    cudaStream_t s;
+    void operator()(cudaError_t e, const char *what) const {
+        if (e != cudaSuccess) fail(TCU_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+    }
+};
+
+// flash-path splits of the training rows: enough blocks for two per SM, at most 64 parts
+static int flash_splits(const tcu_ctx *ctx, int R, int heads, int ntiles) {
+    const int blocks = (R + FLASH_ROWS - 1) / FLASH_ROWS * heads;
+    int splits = (2 * ctx->sms + blocks - 1) / blocks;
+    splits = std::max(1, std::min({splits, ntiles, 64}));
+    const int per = (ntiles + splits - 1) / splits;
+    return (ntiles + per - 1) / per;
+}
+
+static void ensure_work(tcu_model *m, int R) {
+    const auto &s = m->w->shape;
+    const size_t d = s.d, H = s.heads;
+    const size_t wide = (size_t)std::max(s.ff, s.dec_ff);
+    m->q.ensure(sizeof(float) * R * d);
+    m->att.ensure(sizeof(float) * R * d);
+    m->mid.ensure(sizeof(float) * R * wide);
+    m->stats.ensure(sizeof(float) * R * 2);
+    const int splits = flash_splits(m->w->ctx, R, s.heads, m->ntiles);
+    const size_t pr = R <= 32 ? (size_t)m->nitems : (splits > 1 ? (size_t)splits : 0);
+    if (pr) {
+        m->part_ms.ensure(sizeof(float) * pr * R * H * 2);
+        m->part_acc.ensure(sizeof(float) * pr * R * d);
+    }
+}
+
+// attention of R scaled queries q (device, [R][d]) against a layer given in stored form; out [R][d]
+static void attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int rows, int chunk, int kv, const int2 *items,
+                         int nitems, const int4 *tiles, int ntiles, const float *q, int R, float *out, cudaStream_t s) {
+    const auto &sh = m->w->shape;
+    AttnArgs a;
+    a.layer = layer, a.rows = rows, a.chunk = chunk, a.d = sh.d, a.heads = sh.heads;
+    a.full = record_bytes(kv, sh.d, chunk);
+    a.q = q, a.ldq = sh.d, a.R = R, a.out = out, a.ldo = sh.d;
+    a.part_ms = m->part_ms.as<float>(), a.part_acc = m->part_acc.as<float>();
+    const int hd = sh.d / sh.heads;
+    Launch ck{ctx, s};
+    cudaEvent_t ev_end = nullptr;
+    if (ctx->prof) {
+        if (ctx->prof_used + 2 > ctx->prof_events.size()) {
+            for (int i = 0; i < 64; i++) {
+                cudaEvent_t e;
+                CU(cudaEventCreate(&e));
+                ctx->prof_events.push_back(e);
+            }
+        }
+        CU(cudaEventRecord(ctx->prof_events[ctx->prof_used], s));
+        ev_end = ctx->prof_events[ctx->prof_used + 1];
+        ctx->prof_used += 2;
+    }
+    struct End {
+        cudaEvent_t e;
+        cudaStream_t s;
+        ~End() {
+            if (e) cudaEventRecord(e, s);
+        }
+    } end_mark{ev_end, s};
+    if (R <= 32) {
+        a.items = items, a.nitems = nitems;
+        ck(launch_attend_decode(kv, hd, a, s, &ctx->launches), "attend (decode)");
+    } else {
+        a.tiles = tiles, a.ntiles = ntiles;
+        const int splits = flash_splits(ctx, R, sh.heads, ntiles);
+        a.tiles_per_split = (ntiles + splits - 1) / splits;
+        a.splits = (ntiles + a.tiles_per_split - 1) / a.tiles_per_split;
+        ck(launch_attend_flash(kv, hd, a, s, &ctx->launches), "attend (flash)");
+    }
+}
+
+static void linear(tcu_ctx *ctx, tcu_model *m, const float *x, int ldx, int R, int K, const float *lnw, const float *lnb,
+                   const float *W, const float *b, int N, float *y, int ldy, int act, int accumulate, cudaStream_t s) {
+    LinArgs a;
+    a.x = x, a.ldx = ldx, a.M = R, a.K = K, a.lnw = lnw, a.lnb = lnb, a.W = W, a.bias = b, a.N = N, a.y = y, a.ldy = ldy;
+    a.act = act, a.accumulate = accumulate;
+    Launch{ctx, s}(launch_linear(a, m->stats.as<float>(), s, &ctx->launches), "linear");
+}
+
+// predict.rs:413-568 one layer for R rows whose representations are h (device, [R][d], updated in place)
+static void query_rows(tcu_ctx *ctx, tcu_model *m, int l, const float *scale, const float *h, int R, float *q, cudaStream_t s) {
+    const auto &sh = m->w->shape;
+    const LayerPtrs &p = m->w->layer[l];
+    const int d = sh.d;
+    linear(ctx, m, h, d, R, d, p.n1w, p.n1b, p.wq, p.bq, d, q, d, 0, 0, s);  // nn.rs:136-137
+    Launch{ctx, s}(launch_ssmax(q, R, d, sh.heads, sh.hid, p.q0w, p.q0b, p.q2w, p.q2b, scale, s, &ctx->launches), "ssmax");
+}
+
+static void block_tail(tcu_ctx *ctx, tcu_model *m, int l, float *h, const float *att, int R, cudaStream_t s) {
+    const auto &sh = m->w->shape;
+    const LayerPtrs &p = m->w->layer[l];
+    const int d = sh.d, ff = sh.ff;
+    linear(ctx, m, att, d, R, d, nullptr, nullptr, p.wo, p.bo, d, h, d, 0, 1, s);                    // predict.rs:542-551
+    linear(ctx, m, h, d, R, d, p.n2w, p.n2b, p.w1, p.b1, ff, m->mid.as<float>(), ff, 1, 0, s);      // predict.rs:552-559
+    linear(ctx, m, m->mid.as<float>(), ff, R, ff, nullptr, nullptr, p.w2, p.b2, d, h, d, 0, 1, s);   // predict.rs:560-568
+}
+
+static void stage(tcu_ctx *ctx, tcu_model *m, float *h, int R, int out_n, float *out, cudaStream_t s) {
+    check_ready(m);
+    const auto &sh = m->w->shape;
+    const int d = sh.d, L = sh.layers, dff = sh.dec_ff;
+    if (out_n < 1 || out_n > sh.outs) fail(TCU_ERR_ARG, "stage: out_n must be 1..decoder outputs");
+    ensure_work(m, R);
+    const float *scales = m->scales.as<float>();
+    for (int l = 0; l < L; l++) {
+        query_rows(ctx, m, l, scales + (size_t)l * d, h, R, m->q.as<float>(), s);
+        attend_layer(ctx, m, layer_ptr(m, l), m->rows, m->chunk, m->kv, m->items.as<int2>(), m->nitems, m->tiles.as<int4>(),
+                     m->ntiles, m->q.as<float>(), R, m->att.as<float>(), s);
+        block_tail(ctx, m, l, h, m->att.as<float>(), R, s);
+    }
+    // predict.rs:570-584 decoder: only the first out_n outputs are computed (each output is its own row)
+    linear(ctx, m, h, d, R, d, m->w->lnw, m->w->lnb, m->w->dec0w, m->w->dec0b, dff, m->mid.as<float>(), dff, 1, 0, s);
+    linear(ctx, m, m->mid.as<float>(), dff, R, dff, nullptr, nullptr, m->w->dec2w, m->w->dec2b, out_n, out, out_n, 0, 0, s);
+}
+
+// fit.rs:577-747 in-memory path on the device
+static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, int chunk, int kv) {
+    tcu_ctx *ctx = w->ctx;
+    if (!w->for_fit || !w->ready) fail(TCU_ERR_STATE, "fit: weights must be made with for_fit and be ready");
+    if (chunk < 8) chunk = 8;  // fit.rs:226
+    std::unique_ptr<tcu_model> m(new tcu_model());
+    model_init(m.get(), w, rows, chunk, kv, w->shape.outs);
+    const auto &sh = w->shape;
+    const int d = sh.d, L = sh.layers;
+    cudaStream_t s = ctx->stream;
+    ensure_work(m.get(), rows);
+    DevBuf lnh, kvT, kvf, items32, tiles64;
+    lnh.ensure(sizeof(float) * (size_t)rows * d);
+    kvT.ensure(sizeof(float) * (size_t)rows * 2 * d);
+    kvf.ensure(layer_bytes_of(0, d, rows, chunk));
+    Launch ck{ctx, s};
+    ck(launch_add_y(h, y, rows, d, sh.max_classes, w->icl_y, s, &ctx->launches), "add_y");
+    // the float view of a layer (for the training rows' own attention) has its own items/tiles: same chunking
+    std::vector<float> scales((size_t)L * d);
+    for (int l = 0; l < L; l++) {
+        const LayerPtrs &p = w->layer[l];
+        auto sc = query_scale(w, l, rows);
+        std::memcpy(scales.data() + (size_t)l * d, sc.data(), sizeof(float) * d);
+        CU(cudaMemcpyAsync(m->scales.as<float>() + (size_t)l * d, sc.data(), sizeof(float) * d, cudaMemcpyHostToDevice, s));
+        ck(launch_ln_apply(h, rows, d, p.n1w, p.n1b, lnh.as<float>(), s, &ctx->launches), "norm1");
+        // keys and values, coordinate-major: kvT[j][r] = Wkv[j] . LN(h_r) + bkv[j]
+        LinArgs a;
+        a.x = p.wkv, a.ldx = d, a.M = 2 * d, a.K = d, a.W = lnh.as<float>(), a.N = rows, a.bias = p.bkv, a.bias_on_m = 1;
+        a.y = kvT.as<float>(), a.ldy = rows;
+        ck(launch_linear(a, m->stats.as<float>(), s, &ctx->launches), "key/value projection");
+        ck(launch_pack(kvT.as<float>(), rows, d, rows, chunk, kv, m->layers.as<uint8_t>() + m->layer_stride * l, s, &ctx->launches), "pack");
+        m->have_layer[l] = true;
+        if (l + 1 == L) break;  // fit.rs:664-666
+        if (kv != 0) ck(launch_pack(kvT.as<float>(), rows, d, rows, chunk, 0, kvf.as<uint8_t>(), s, &ctx->launches), "pack f32");
+        const uint8_t *fl = kv == 0 ? layer_ptr(m.get(), l) : kvf.as<uint8_t>();
+        query_rows(ctx, m.get(), l, m->scales.as<float>() + (size_t)l * d, h, rows, m->q.as<float>(), s);
+        // the f32 view has the same chunking, and flash tiles depend only on chunking
+        attend_layer(ctx, m.get(), fl, rows, chunk, 0, nullptr, 0, m->tiles.as<int4>(), m->ntiles, m->q.as<float>(), rows,
+                     m->att.as<float>(), s);
+        block_tail(ctx, m.get(), l, h, m->att.as<float>(), rows, s);
+    }
+    CU(cudaStreamSynchronize(s));
+    m->have_scales = true;
+    return m.release();
+}
+
+}  // namespace tcu
+
+// ---- C ABI ------------------------------------------------------------------------------------------------------
+
+extern "C" {
+
+int tcu_open(int device, tcu_ctx **out) {
+    if (!out) return TCU_ERR_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return TCU_ERR_CUDA;
+    std::unique_ptr<tcu_ctx> ctx(new tcu_ctx());
+    ctx->device = device;
+    int r = guarded(ctx.get(), [&]() -> int {
+        CU(cudaDeviceGetAttribute(&ctx->sms, cudaDevAttrMultiProcessorCount, device));
+        CU(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
+        CU(kernels_init());
+        return TCU_OK;
+    });
+    if (r != TCU_OK) return r;
+    *out = ctx.release();
+    return TCU_OK;
+}
+
+void tcu_close(tcu_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    for (auto e : ctx->prof_events) cudaEventDestroy(e);
+    delete ctx;
+}
+
+const char *tcu_last_error(const tcu_ctx *ctx) { return ctx ? ctx->err.c_str() : "no context"; }
+
+uint64_t tcu_launches(const tcu_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+int tcu_weights_new(tcu_ctx *ctx, const tcu_icl_shape *shape, int for_fit, tcu_weights **out) {
+    return guarded(ctx, [&]() -> int {
+        if (!shape || !out) fail(TCU_ERR_ARG, "weights_new: null argument");
+        const auto &s = *shape;
+        if (s.d <= 0 || s.heads <= 0 || s.d % s.heads || s.layers <= 0 || s.ff <= 0 || s.hid <= 0 || s.dec_ff <= 0 || s.outs <= 0)
+            fail(TCU_ERR_ARG, "weights_new: bad shape");
+        const int hd = s.d / s.heads;
+        if (hd != 8 && hd != 16 && hd != 32 && hd != 64 && hd != 128) fail(TCU_ERR_ARG, "weights_new: head width must be 8, 16, 32, 64 or 128");
+        if (s.d % 4 || s.ff % 4 || s.dec_ff % 4) fail(TCU_ERR_ARG, "weights_new: widths must be multiples of 4");
+        auto *w = new tcu_weights();
+        w->ctx = ctx, w->shape = s, w->for_fit = for_fit != 0;
+        *out = w;
+        return TCU_OK;
+    });
+}
+
+int tcu_weights_put(tcu_weights *w, const char *name, int dtype, const void *data, size_t count) {
+    if (!w) return TCU_ERR_ARG;
+    return guarded(w->ctx, [&]() -> int {
+        if (!name || (!data && count)) fail(TCU_ERR_ARG, "weights_put: null argument");
+        if (w->ready) fail(TCU_ERR_STATE, "weights_put: weights already uploaded");
+        std::vector<float> v(count);
+        if (dtype == 0)
+            std::memcpy(v.data(), data, count * sizeof(float));
+        else if (dtype == 1)
+            for (size_t i = 0; i < count; i++) v[i] = f16_to_f32(reinterpret_cast<const uint16_t *>(data)[i]);
+        else
+            fail(TCU_ERR_ARG, "weights_put: dtype must be 0 (float32) or 1 (float16)");
+        w->host[name] = std::move(v);
+        return TCU_OK;
+    });
+}
+
+int tcu_weights_ready(tcu_weights *w) {
+    if (!w) return TCU_ERR_ARG;
+    return guarded(w->ctx, [&]() -> int { return weights_ready(w); });
+}
+
+int tcu_weights_from_bundle(tcu_ctx *ctx, const char *path, int for_fit, tcu_weights **out) {
+    return guarded(ctx, [&]() -> int {
+        if (!path || !out) fail(TCU_ERR_ARG, "weights_from_bundle: null argument");
+        auto b = Bundle::open(path);
+        auto cfgb = b->bytes("config.json");
+        std::string cfg(cfgb.begin(), cfgb.end());
+        // model.rs:204-219: only the TabICLv2 layout this path implements
+        const char *want[][2] = {{"col_feature_group", "same"}, {"col_affine", "false"}, {"col_target_aware", "true"},
+                                 {"col_ssmax", "qassmax-mlp-elementwise"}, {"icl_ssmax", "qassmax-mlp-elementwise"},
+                                 {"row_rope_interleaved", "false"}, {"norm_first", "true"}, {"activation", "gelu"}};
+        for (auto &kv : want) {
+            std::string got = cfg_value(cfg, kv[0]);
+            if (got != kv[1]) fail(TCU_ERR_FORMAT, std::string("unsupported checkpoint: ") + kv[0] + " is " + got + ", this backend implements " + kv[1]);
+        }
+        auto num = [&](const char *k) {
+            std::string v = cfg_value(cfg, k);
+            char *end = nullptr;
+            long x = std::strtol(v.c_str(), &end, 10);
+            if (v.empty() || *end) fail(TCU_ERR_FORMAT, std::string("config has no number ") + k);
+            return (int)x;
+        };
+        tcu_icl_shape s{};
+        s.heads = num("icl_nhead"), s.layers = num("icl_num_blocks"), s.max_classes = num("max_classes");
+        s.d = (int)b->entry("icl_predictor.ln.weight").len();
+        s.ff = (int)b->entry(blk(0, "linear1.bias")).len();
+        s.hid = (int)b->entry(blk(0, "attn.ssmax_layer.query_mlp.0.bias")).len();
+        s.dec_ff = (int)b->entry("icl_predictor.decoder.0.bias").len();
+        s.outs = (int)b->entry("icl_predictor.decoder.2.bias").len();
+        tcu_weights *w = nullptr;
+        int r = tcu_weights_new(ctx, &s, for_fit, &w);
+        if (r != TCU_OK) return r;
+        std::unique_ptr<tcu_weights> guard(w);
+        for (const auto &e : b->entries())
+            if (e.name.rfind("icl_predictor.", 0) == 0 && (e.dtype == "float32" || e.dtype == "float16")) w->host[e.name] = b->f32s(e.name);
+        weights_ready(w);
+        *out = guard.release();
+        return TCU_OK;
+    });
+}
+
+int tcu_weights_shape(const tcu_weights *w, tcu_icl_shape *out) {
+    if (!w || !out) return TCU_ERR_ARG;
+    *out = w->shape;
+    return TCU_OK;
+}
+
+void tcu_weights_free(tcu_weights *w) {
+    if (!w) return;
+    std::lock_guard<std::recursive_mutex> lock(w->ctx->mu);
+    cudaSetDevice(w->ctx->device);
+    delete w;
+}
+
+int tcu_model_new(tcu_weights *w, const int32_t meta[7], int32_t node_rows, int32_t node_k, tcu_model **out) {
+    if (!w) return TCU_ERR_ARG;
+    return guarded(w->ctx, [&]() -> int {
+        if (!meta || !out) fail(TCU_ERR_ARG, "model_new: null argument");
+        if (!w->ready) fail(TCU_ERR_STATE, "model_new: weights not ready");
+        std::unique_ptr<tcu_model> m(new tcu_model());
+        // meta = [rows, features, classes, chunk, kv, digits, nodes] (fit.rs:291)
+        if (meta[4] < 0 || meta[4] > 2) fail(TCU_ERR_FORMAT, "meta: unknown key/value format " + std::to_string(meta[4]));
+        model_init(m.get(), w, node_rows, meta[3], meta[4], node_k);
+        m->features = meta[1];
+        *out = m.release();
+        return TCU_OK;
+    });
+}
+
+int tcu_model_put_scales(tcu_model *m, const float *scales, size_t count) {
+    if (!m) return TCU_ERR_ARG;
+    return guarded(m->w->ctx, [&]() -> int {
+        const size_t want = (size_t)m->w->shape.layers * m->w->shape.d;
+        if (!scales || count != want) fail(TCU_ERR_ARG, "model_put_scales: expected layers * d floats");
+        CU(cudaMemcpy(m->scales.p, scales, sizeof(float) * want, cudaMemcpyHostToDevice));
+        m->have_scales = true;
+        return TCU_OK;
+    });
+}
+
+int tcu_model_put_layer(tcu_model *m, int layer, size_t offset, const void *bytes, size_t nbytes) {
+    if (!m) return TCU_ERR_ARG;
+    return guarded(m->w->ctx, [&]() -> int {
+        if (layer < 0 || layer >= m->w->shape.layers) fail(TCU_ERR_ARG, "model_put_layer: no such layer");
+        if (!bytes || offset + nbytes > m->layer_bytes) fail(TCU_ERR_ARG, "model_put_layer: range past the layer's " + std::to_string(m->layer_bytes) + " bytes");
+        CU(cudaMemcpy(m->layers.as<uint8_t>() + m->layer_stride * layer + offset, bytes, nbytes, cudaMemcpyHostToDevice));
+        if (offset + nbytes == m->layer_bytes) m->have_layer[layer] = true;
+        return TCU_OK;
+    });
+}
+
+int tcu_model_from_bundle(tcu_weights *w, const char *path, const char *prefix, int node, tcu_model **out) {
+    if (!w) return TCU_ERR_ARG;
+    return guarded(w->ctx, [&]() -> int {
+        if (!path || !prefix || !out) fail(TCU_ERR_ARG, "model_from_bundle: null argument");
+        auto b = Bundle::open(path);
+        std::string p(prefix);
+        auto meta = b->i32s(p + "meta");
+        auto tree = b->i32s(p + "tree");
+        if (meta.size() != 7) fail(TCU_ERR_FORMAT, p + "meta is damaged");
+        // predict.rs:141-148: per node [leaf, rows, k, map...]
+        size_t at = 0;
+        int node_rows = -1, node_k = -1;
+        for (int i = 0; i < meta[6]; i++) {
+            if (at + 3 > tree.size()) fail(TCU_ERR_FORMAT, p + "tree is damaged");
+            if (i == node) node_rows = tree[at + 1], node_k = tree[at + 2];
+            at += 3 + (size_t)tree[at + 2];
+        }
+        if (node_rows < 0) fail(TCU_ERR_ARG, "model_from_bundle: no such node");
+        tcu_model *m = nullptr;
+        int r = tcu_model_new(w, meta.data(), node_rows, node_k, &m);
+        if (r != TCU_OK) return r;
+        std::unique_ptr<tcu_model> guard(m);
+        auto sc = b->f32s(p + "n" + std::to_string(node) + "_scale");
+        r = tcu_model_put_scales(m, sc.data(), sc.size());
+        if (r != TCU_OK) return r;
+        for (int l = 0; l < w->shape.layers; l++) {
+            std::string name = p + "n" + std::to_string(node) + "_kv" + std::to_string(l);
+            const Entry &e = b->entry(name);
+            if (e.nbytes != m->layer_bytes) fail(TCU_ERR_FORMAT, name + ": " + std::to_string(e.nbytes) + " bytes, expected " + std::to_string(m->layer_bytes));
+            auto bytes = b->bytes(name);
+            r = tcu_model_put_layer(m, l, 0, bytes.data(), bytes.size());
+            if (r != TCU_OK) return r;
+        }
+        *out = guard.release();
+        return TCU_OK;
+    });
+}
+
+size_t tcu_model_bytes(const tcu_model *m) {
+    if (!m) return 0;
+    return m->layers.bytes + m->scales.bytes + m->items.bytes + m->tiles.bytes;
+}
+
+int tcu_model_get_layer(const tcu_model *m, int layer, void *bytes, size_t nbytes) {
+    if (!m) return TCU_ERR_ARG;
+    return guarded(m->w->ctx, [&]() -> int {
+        if (layer < 0 || layer >= m->w->shape.layers || nbytes != m->layer_bytes || !bytes) fail(TCU_ERR_ARG, "model_get_layer: bad layer or size");
+        CU(cudaMemcpy(bytes, layer_ptr(m, layer), nbytes, cudaMemcpyDeviceToHost));
+        return TCU_OK;
+    });
+}
+
+int tcu_model_get_scales(const tcu_model *m, float *scales, size_t count) {
+    if (!m) return TCU_ERR_ARG;
+    return guarded(m->w->ctx, [&]() -> int {
+        const size_t want = (size_t)m->w->shape.layers * m->w->shape.d;
+        if (!scales || count != want) fail(TCU_ERR_ARG, "model_get_scales: expected layers * d floats");
+        CU(cudaMemcpy(scales, m->scales.p, sizeof(float) * want, cudaMemcpyDeviceToHost));
+        return TCU_OK;
+    });
+}
+
+void tcu_model_free(tcu_model *m) {
+    if (!m) return;
+    std::lock_guard<std::recursive_mutex> lock(m->w->ctx->mu);
+    cudaSetDevice(m->w->ctx->device);
+    delete m;
+}
+
+int tcu_attend_device(tcu_model *m, int layer, const float *q, int rows, float *out, void *stream) {
+    if (!m) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->w->ctx;
+    return guarded(ctx, [&]() -> int {
+        check_ready(m);
+        if (layer < 0 || layer >= m->w->shape.layers || rows < 0 || (rows && (!q || !out))) fail(TCU_ERR_ARG, "attend: bad argument");
+        if (rows == 0) return TCU_OK;
+        cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+        ensure_work(m, rows);
+        attend_layer(ctx, m, layer_ptr(m, layer), m->rows, m->chunk, m->kv, m->items.as<int2>(), m->nitems, m->tiles.as<int4>(),
+                     m->ntiles, q, rows, out, s);
+        return TCU_OK;
+    });
+}
+
+int tcu_stage_device(tcu_model *m, const float *h, int rows, int out_n, float *out, void *stream) {
+    if (!m) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->w->ctx;
+    return guarded(ctx, [&]() -> int {
+        if (rows < 0 || (rows && (!h || !out))) fail(TCU_ERR_ARG, "stage: bad argument");
+        if (rows == 0) return TCU_OK;
+        cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+        const size_t n = (size_t)rows * m->w->shape.d;
+        m->h.ensure(sizeof(float) * n);
+        if (h != m->h.as<float>()) CU(cudaMemcpyAsync(m->h.p, h, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+        stage(ctx, m, m->h.as<float>(), rows, out_n, out, s);
+        return TCU_OK;
+    });
+}
+
+int tcu_attend(tcu_model *m, int layer, const float *q, int rows, int d, int heads, float *out) {
+    if (!m) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->w->ctx;
+    return guarded(ctx, [&]() -> int {
+        if (d != m->w->shape.d || heads != m->w->shape.heads) fail(TCU_ERR_ARG, "attend: d or heads differ from the weights'");
+        if (rows < 0 || (rows && (!q || !out))) fail(TCU_ERR_ARG, "attend: bad argument");
+        if (rows == 0) return TCU_OK;
+        check_ready(m);
+        const size_t n = (size_t)rows * d;
+        m->h.ensure(sizeof(float) * n);
+        m->out.ensure(sizeof(float) * n);
+        cudaStream_t s = ctx->stream;
+        CU(cudaMemcpyAsync(m->h.p, q, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+        int r = tcu_attend_device(m, layer, m->h.as<float>(), rows, m->out.as<float>(), s);
+        if (r != TCU_OK) return r;
+        CU(cudaMemcpyAsync(out, m->out.p, sizeof(float) * n, cudaMemcpyDeviceToHost, s));
+        CU(cudaStreamSynchronize(s));
+        return TCU_OK;
+    });
+}
+
+int tcu_stage(tcu_model *m, const float *h, int rows, int d, int out_n, float *out) {
+    if (!m) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->w->ctx;
+    return guarded(ctx, [&]() -> int {
+        if (d != m->w->shape.d) fail(TCU_ERR_ARG, "stage: d differs from the weights'");
+        if (rows < 0 || (rows && (!h || !out))) fail(TCU_ERR_ARG, "stage: bad argument");
+        if (rows == 0) return TCU_OK;
+        m->h.ensure(sizeof(float) * (size_t)rows * d);
+        m->out.ensure(sizeof(float) * (size_t)rows * out_n);
+        cudaStream_t s = ctx->stream;
+        CU(cudaMemcpyAsync(m->h.p, h, sizeof(float) * (size_t)rows * d, cudaMemcpyHostToDevice, s));
+        stage(ctx, m, m->h.as<float>(), rows, out_n, m->out.as<float>(), s);
+        CU(cudaMemcpyAsync(out, m->out.p, sizeof(float) * (size_t)rows * out_n, cudaMemcpyDeviceToHost, s));
+        CU(cudaStreamSynchronize(s));
+        return TCU_OK;
+    });
+}
+
+int tcu_class_head_device(tcu_ctx *ctx, const float *logits, int rows, int classes, int stride,
+                          const int32_t *member_classes, double *sums, int finish, int members, double temperature) {
+    return guarded(ctx, [&]() -> int {
+        if (rows < 0 || classes < 1 || stride < classes || (rows && (!logits || !member_classes || !sums))) fail(TCU_ERR_ARG, "class_head: bad argument");
+        if (finish && (members < 1 || !(temperature > 0))) fail(TCU_ERR_ARG, "class_head: members and temperature must be positive");
+        if (rows == 0) return TCU_OK;
+        Launch{ctx, ctx->stream}(launch_class_head(logits, rows, classes, stride, member_classes, sums, finish, members, temperature,
+                                                   ctx->stream, &ctx->launches),
+                                 "class head");
+        CU(cudaStreamSynchronize(ctx->stream));
+        return TCU_OK;
+    });
+}
+
+int tcu_regression_head_device(tcu_ctx *ctx, const float *qout, int rows, int nq, int stride, const double *alphas,
+                               int na, double target_mean, double target_scale, double *mean, double *variance,
+                               double *median, double *quantiles) {
+    return guarded(ctx, [&]() -> int {
+        if (rows < 0 || nq < 2 || nq > 4096 || stride < nq || na < 0) fail(TCU_ERR_ARG, "regression_head: bad sizes (2 <= nq <= 4096)");
+        if (rows && (!qout || !mean || !variance || !median || (na && (!alphas || !quantiles)))) fail(TCU_ERR_ARG, "regression_head: null argument");
+        if (rows == 0) return TCU_OK;
+        Launch{ctx, ctx->stream}(launch_regression_head(qout, rows, nq, stride, alphas, na, target_mean, target_scale, mean, variance,
+                                                        median, quantiles, ctx->stream, &ctx->launches),
+                                 "regression head");
+        CU(cudaStreamSynchronize(ctx->stream));
+        return TCU_OK;
+    });
+}
+
+int tcu_fit_icl_device(tcu_weights *w, float *h, const float *y, int rows, int chunk, int kv, tcu_model **out) {
+    if (!w) return TCU_ERR_ARG;
+    return guarded(w->ctx, [&]() -> int {
+        if (!h || !y || !out || rows < 1 || kv < 0 || kv > 2) fail(TCU_ERR_ARG, "fit_icl: bad argument");
+        *out = fit_icl(w, h, y, rows, chunk, kv);
+        return TCU_OK;
+    });
+}
+
+int tcu_pack_device(tcu_ctx *ctx, int kv, int d, int rc, const float *c, void *rec) {
+    return guarded(ctx, [&]() -> int {
+        if (kv < 0 || kv > 2 || d < 1 || rc < 1 || !c || !rec) fail(TCU_ERR_ARG, "pack: bad argument");
+        Launch{ctx, ctx->stream}(launch_pack(c, rc, d, rc, rc, kv, reinterpret_cast<uint8_t *>(rec), ctx->stream, &ctx->launches), "pack");
+        CU(cudaStreamSynchronize(ctx->stream));
+        return TCU_OK;
+    });
+}
+
+size_t tcu_record(int kv, int d, int rc) { return record_bytes(kv, d, rc); }
+
+int tcu_profile(tcu_ctx *ctx, int enable, double *attend_ms, uint64_t *attend_launches) {
+    return guarded(ctx, [&]() -> int {
+        if (attend_ms || attend_launches) {
+            CU(cudaDeviceSynchronize());
+            double ms = 0;
+            for (size_t i = 0; i + 1 < ctx->prof_used; i += 2) {
+                float t = 0;
+                CU(cudaEventElapsedTime(&t, ctx->prof_events[i], ctx->prof_events[i + 1]));
+                ms += t;
+            }
+            if (attend_ms) *attend_ms = ms;
+            if (attend_launches) *attend_launches = ctx->prof_used / 2;
+        }
+        ctx->prof = enable != 0;
+        ctx->prof_used = 0;
+        return TCU_OK;
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,81 @@
+// Launch interface of the prediction-path kernels (kernels.cu). All launches are asynchronous on `stream`.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <vector_types.h>
+
+namespace tcu {
+
+// y (=|+=) act(W LN?(x) + b): x [M][K] (row stride ldx), W [N][K], y [M][N] (row stride ldy).
+struct LinArgs {
+    const float *x = nullptr;
+    int ldx = 0, M = 0, K = 0;
+    const float *lnw = nullptr, *lnb = nullptr;  // LayerNorm of each input row first (eps 1e-5), if set
+    const float *stats = nullptr;                // [M][2] mean, 1/sigma of the input rows (tiled path)
+    const float *W = nullptr, *bias = nullptr;
+    int N = 0;
+    float *y = nullptr;
+    int ldy = 0;
+    int act = 0;         // 1: GELU (kern.rs:285-290)
+    int accumulate = 0;  // 1: y += result (residual)
+    int bias_on_m = 0;   // bias indexed by the row of y (used when y is a transposed product)
+};
+
+// Attention of scaled queries against one layer's stored chunks (fit.rs:6-11 layout, read in place).
+struct AttnArgs {
+    const uint8_t *layer = nullptr;
+    int rows = 0, chunk = 0, d = 0, heads = 0;
+    size_t full = 0;               // bytes of a full chunk record
+    const int2 *items = nullptr;   // decode: (chunk, first key) per item
+    int nitems = 0;
+    const int4 *tiles = nullptr;   // flash: (chunk, first key, keys) per 64-key tile
+    int ntiles = 0, tiles_per_split = 0, splits = 1;
+    const float *q = nullptr;      // [R][d] scaled queries (row stride ldq)
+    int ldq = 0, R = 0;
+    float *part_ms = nullptr;      // [parts][R][heads][2]: running max, weight sum
+    float *part_acc = nullptr;     // [parts][R][d]: weighted value sums
+    float *out = nullptr;          // [R][d] finished outputs (row stride ldo)
+    int ldo = 0;
+};
+
+#ifdef __CUDACC__
+#define TCU_HD __host__ __device__
+#else
+#define TCU_HD
+#endif
+
+// fit.rs:124-126 record: bytes of one stored chunk of rc rows
+TCU_HD inline size_t record_bytes(int kv, int d, int rc) {
+    int w = kv == 0 ? 4 : (kv == 1 ? 2 : 1);
+    return (size_t)2 * d * rc * w + (kv == 0 ? 0 : (size_t)8 * d);
+}
+
+// Rows of keys per decode item for a stored format (f32 32, i16 64, i8 64).
+int decode_keys_per_item(int kv);
+constexpr int FLASH_KEYS = 64;  // keys per flash tile
+constexpr int FLASH_ROWS = 64;  // query rows per flash block
+
+cudaError_t launch_linear(const LinArgs &a, float *stats_scratch, cudaStream_t s, uint64_t *launches);
+cudaError_t launch_ln_apply(const float *x, int M, int K, const float *w, const float *b, float *y, cudaStream_t s,
+                            uint64_t *launches);
+cudaError_t launch_ssmax(float *q, int R, int d, int heads, int hid, const float *q0w, const float *q0b,
+                         const float *q2w, const float *q2b, const float *scale, cudaStream_t s, uint64_t *launches);
+// keys-parallel split attention for few rows, then the merge into out
+cudaError_t launch_attend_decode(int kv, int hd, const AttnArgs &a, cudaStream_t s, uint64_t *launches);
+// row-blocked attention for many rows; merges itself when splits == 1, else writes parts
+cudaError_t launch_attend_flash(int kv, int hd, const AttnArgs &a, cudaStream_t s, uint64_t *launches);
+cudaError_t launch_attend_merge(const AttnArgs &a, int parts, cudaStream_t s, uint64_t *launches);
+cudaError_t launch_pack(const float *kvT, int ld, int d, int rows, int chunk, int kv, uint8_t *out, cudaStream_t s,
+                        uint64_t *launches);
+cudaError_t launch_add_y(float *h, const float *y, int rows, int d, int max_classes, const float *table,
+                         cudaStream_t s, uint64_t *launches);
+cudaError_t launch_class_head(const float *logits, int rows, int classes, int stride, const int32_t *member_classes,
+                              double *sums, int finish, int members, double temperature, cudaStream_t s,
+                              uint64_t *launches);
+cudaError_t launch_regression_head(const float *qout, int rows, int nq, int stride, const double *alphas, int na,
+                                   double tmean, double tscale, double *mean, double *var, double *median,
+                                   double *quant, cudaStream_t s, uint64_t *launches);
+cudaError_t kernels_init();
+
+}  // namespace tcu
