@@ -227,7 +227,9 @@ def main():
     R = a.rows
     h = torch.from_numpy(synth.row_reps(R, d, 100 + rank)).cuda()
     out = torch.empty((R, classes), device="cuda")
-    stream = torch.cuda.current_stream()
+    # an explicit stream: the library's NULL stream means its own, so events must sit on the stream it is given
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     sp = stream.cuda_stream
 
     def step():
@@ -329,7 +331,7 @@ def main():
                          cfg["icl_num_blocks"], cfg["max_classes"])
         layers = [vm.layer_bytes(l, layer_bytes) for l in range(m.layers)]
         rps, n, dt, threads = oracle_rows_per_s(m, a.kv, layers, vm.scales(), a.train_rows,
-                                                synth.row_reps(512, d, 200), 12.0)
+                                                synth.row_reps(8192, d, 200), 12.0)
         line["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": threads, "kind": "port",
                                 "sample": f"{n} test rows of the same workload through the oracle's in-context "
                                           f"stage, {dt:.1f} s"}

@@ -18,7 +18,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-O3", "-std=c++17", "-lineinfo",
     "-gencode", "arch=compute_100a,code=sm_100a",
-    "-Xcompiler", "-fPIC,-O3,-fvisibility=hidden",
+    "-Xcompiler", "-fPIC,-O3,-fvisibility=hidden,-ffp-contract=off",
     "-cudart", "static",
     "--expt-relaxed-constexpr",
 ]

@@ -7,6 +7,7 @@
 
 #include <cmath>
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -62,6 +63,7 @@ struct DevBuf {
 using namespace tcu;
 
 struct tcu_ctx {
+    std::atomic<int> refs{1};  // the caller's handle plus one per live weights object
     int device = 0;
     int sms = 148;
     cudaStream_t stream = nullptr;
@@ -81,6 +83,7 @@ struct LayerPtrs {
 };
 
 struct tcu_weights {
+    std::atomic<int> refs{1};  // the caller's handle plus one per live model
     tcu_ctx *ctx = nullptr;
     tcu_icl_shape shape{};
     bool for_fit = false;
@@ -105,6 +108,40 @@ struct tcu_model {
     // working memory, grown to the largest call so far
     DevBuf h, q, att, mid, stats, out, part_ms, part_acc;
 };
+
+// ---- handle lifetimes: a context lives while its weights do, weights while their models do --------------------
+
+static void ctx_release(tcu_ctx *ctx) {
+    if (--ctx->refs > 0) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    for (auto e : ctx->prof_events) cudaEventDestroy(e);
+    delete ctx;
+}
+
+static void weights_release(tcu_weights *w) {
+    if (--w->refs > 0) return;
+    tcu_ctx *ctx = w->ctx;
+    {
+        std::lock_guard<std::recursive_mutex> lock(ctx->mu);
+        cudaSetDevice(ctx->device);
+        delete w;
+    }
+    ctx_release(ctx);
+}
+
+struct ModelDel {
+    void operator()(tcu_model *m) const {
+        tcu_weights *w = m->w;
+        delete m;
+        if (w) weights_release(w);
+    }
+};
+using ModelPtr = std::unique_ptr<tcu_model, ModelDel>;
+struct WeightsDel {
+    void operator()(tcu_weights *w) const { weights_release(w); }
+};
+using WeightsPtr = std::unique_ptr<tcu_weights, WeightsDel>;
 
 namespace tcu {
 
@@ -187,8 +224,18 @@ static std::vector<float> query_scale(const tcu_weights *w, int l, int n) {
     std::vector<float> h(hid), out(d);
     for (int i = 0; i < hid; i++) h[i] = h_gelu(b0w[i] * logn + b0b[i]);
     for (int o = 0; o < d; o++) {
-        float s = 0.f;
-        for (int i = 0; i < hid; i++) s += b2w[(size_t)o * hid + i] * h[i];
+        // kern.rs:42-61 dot: four running sums of fused products, then the remainder
+        const float *w = b2w.data() + (size_t)o * hid;
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        int i = 0;
+        for (; i + 4 <= hid; i += 4) {
+            s0 = std::fma(w[i], h[i], s0);
+            s1 = std::fma(w[i + 1], h[i + 1], s1);
+            s2 = std::fma(w[i + 2], h[i + 2], s2);
+            s3 = std::fma(w[i + 3], h[i + 3], s3);
+        }
+        float s = (s0 + s1) + (s2 + s3);
+        for (; i < hid; i++) s += w[i] * h[i];
         out[o] = (s + b2b[o]) * inv;
     }
     return out;
@@ -326,9 +373,11 @@ static size_t layer_bytes_of(int kv, int d, int rows, int chunk) {
 }
 
 static void model_init(tcu_model *m, tcu_weights *w, int rows, int chunk, int kv, int classes) {
+    m->w = w;
+    w->refs++;  // released by tcu_model_free, or by ModelDel when creation fails
     const int d = w->shape.d, L = w->shape.layers;
     if (rows <= 0 || chunk < 1 || kv < 0 || kv > 2) fail(TCU_ERR_ARG, "cache: bad rows, chunk or kv format");
-    m->w = w, m->rows = rows, m->chunk = chunk, m->kv = kv, m->classes = classes;
+    m->rows = rows, m->chunk = chunk, m->kv = kv, m->classes = classes;
     m->full = record_bytes(kv, d, chunk);
     m->layer_bytes = layer_bytes_of(kv, d, rows, chunk);
     m->layer_stride = (m->layer_bytes + 255) / 256 * 256;
@@ -487,7 +536,7 @@ static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, in
     tcu_ctx *ctx = w->ctx;
     if (!w->for_fit || !w->ready) fail(TCU_ERR_STATE, "fit: weights must be made with for_fit and be ready");
     if (chunk < 8) chunk = 8;  // fit.rs:226
-    std::unique_ptr<tcu_model> m(new tcu_model());
+    ModelPtr m(new tcu_model());
     model_init(m.get(), w, rows, chunk, kv, w->shape.outs);
     const auto &sh = w->shape;
     const int d = sh.d, L = sh.layers;
@@ -553,11 +602,7 @@ int tcu_open(int device, tcu_ctx **out) {
 }
 
 void tcu_close(tcu_ctx *ctx) {
-    if (!ctx) return;
-    cudaSetDevice(ctx->device);
-    if (ctx->stream) cudaStreamDestroy(ctx->stream);
-    for (auto e : ctx->prof_events) cudaEventDestroy(e);
-    delete ctx;
+    if (ctx) ctx_release(ctx);
 }
 
 const char *tcu_last_error(const tcu_ctx *ctx) { return ctx ? ctx->err.c_str() : "no context"; }
@@ -575,6 +620,7 @@ int tcu_weights_new(tcu_ctx *ctx, const tcu_icl_shape *shape, int for_fit, tcu_w
         if (s.d % 4 || s.ff % 4 || s.dec_ff % 4) fail(TCU_ERR_ARG, "weights_new: widths must be multiples of 4");
         auto *w = new tcu_weights();
         w->ctx = ctx, w->shape = s, w->for_fit = for_fit != 0;
+        ctx->refs++;
         *out = w;
         return TCU_OK;
     });
@@ -633,7 +679,7 @@ int tcu_weights_from_bundle(tcu_ctx *ctx, const char *path, int for_fit, tcu_wei
         tcu_weights *w = nullptr;
         int r = tcu_weights_new(ctx, &s, for_fit, &w);
         if (r != TCU_OK) return r;
-        std::unique_ptr<tcu_weights> guard(w);
+        WeightsPtr guard(w);
         for (const auto &e : b->entries())
             if (e.name.rfind("icl_predictor.", 0) == 0 && (e.dtype == "float32" || e.dtype == "float16")) w->host[e.name] = b->f32s(e.name);
         weights_ready(w);
@@ -649,10 +695,7 @@ int tcu_weights_shape(const tcu_weights *w, tcu_icl_shape *out) {
 }
 
 void tcu_weights_free(tcu_weights *w) {
-    if (!w) return;
-    std::lock_guard<std::recursive_mutex> lock(w->ctx->mu);
-    cudaSetDevice(w->ctx->device);
-    delete w;
+    if (w) weights_release(w);
 }
 
 int tcu_model_new(tcu_weights *w, const int32_t meta[7], int32_t node_rows, int32_t node_k, tcu_model **out) {
@@ -660,7 +703,7 @@ int tcu_model_new(tcu_weights *w, const int32_t meta[7], int32_t node_rows, int3
     return guarded(w->ctx, [&]() -> int {
         if (!meta || !out) fail(TCU_ERR_ARG, "model_new: null argument");
         if (!w->ready) fail(TCU_ERR_STATE, "model_new: weights not ready");
-        std::unique_ptr<tcu_model> m(new tcu_model());
+        ModelPtr m(new tcu_model());
         // meta = [rows, features, classes, chunk, kv, digits, nodes] (fit.rs:291)
         if (meta[4] < 0 || meta[4] > 2) fail(TCU_ERR_FORMAT, "meta: unknown key/value format " + std::to_string(meta[4]));
         model_init(m.get(), w, node_rows, meta[3], meta[4], node_k);
@@ -713,7 +756,7 @@ int tcu_model_from_bundle(tcu_weights *w, const char *path, const char *prefix, 
         tcu_model *m = nullptr;
         int r = tcu_model_new(w, meta.data(), node_rows, node_k, &m);
         if (r != TCU_OK) return r;
-        std::unique_ptr<tcu_model> guard(m);
+        ModelPtr guard(m);
         auto sc = b->f32s(p + "n" + std::to_string(node) + "_scale");
         r = tcu_model_put_scales(m, sc.data(), sc.size());
         if (r != TCU_OK) return r;
@@ -756,9 +799,13 @@ int tcu_model_get_scales(const tcu_model *m, float *scales, size_t count) {
 
 void tcu_model_free(tcu_model *m) {
     if (!m) return;
-    std::lock_guard<std::recursive_mutex> lock(m->w->ctx->mu);
-    cudaSetDevice(m->w->ctx->device);
-    delete m;
+    tcu_weights *w = m->w;
+    {
+        std::lock_guard<std::recursive_mutex> lock(w->ctx->mu);
+        cudaSetDevice(w->ctx->device);
+        delete m;
+    }
+    weights_release(w);
 }
 
 int tcu_attend_device(tcu_model *m, int layer, const float *q, int rows, float *out, void *stream) {

@@ -6,6 +6,8 @@
 #include "device.cuh"
 
 #include <cfloat>
+#include <map>
+#include <mutex>
 
 namespace tcu {
 
@@ -19,8 +21,9 @@ namespace tcu {
 // Few rows (M <= 8): the rows sit in shared memory (LayerNorm applied there, two-pass as kern.rs:357-376), one
 // warp per output reads that output's weight row once with 16-byte loads and serves every row.
 template <int RM>
-__global__ void __launch_bounds__(256) k_gemv(LinArgs a) {
+__global__ void __launch_bounds__(128) k_gemv(LinArgs a) {
     extern __shared__ __align__(16) float xs[];  // [RM][K]
+    constexpr int WARPS = 4, MAXV = 8;           // a lane holds up to 8 16-byte pieces of its weight row (K <= 1024)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int R = a.M, K = a.K;
     for (int i = tid; i < R * K; i += blockDim.x) {
@@ -29,7 +32,7 @@ __global__ void __launch_bounds__(256) k_gemv(LinArgs a) {
     }
     __syncthreads();
     if (a.lnw) {
-        for (int r = warp; r < R; r += 8) {
+        for (int r = warp; r < R; r += WARPS) {
             float *row = xs + r * K;
             float s = 0.f;
             for (int k = lane; k < K; k += 32) s += row[k];
@@ -45,13 +48,12 @@ __global__ void __launch_bounds__(256) k_gemv(LinArgs a) {
         __syncthreads();
     }
     const uint64_t pol = policy_evict_last();
-    for (int o = blockIdx.x * 8 + warp; o < a.N; o += gridDim.x * 8) {
+    for (int o = blockIdx.x * WARPS + warp; o < a.N; o += gridDim.x * WARPS) {
         float acc[RM];
 #pragma unroll
         for (int r = 0; r < RM; r++) acc[r] = 0.f;
         const float *w = a.W + (size_t)o * K;
-        for (int k = lane * 4; k < K; k += 128) {
-            float4 wv = ld_weight4(w + k, pol);
+        auto step = [&](const float4 &wv, int k) {
 #pragma unroll
             for (int r = 0; r < RM; r++) {
                 if (r < R) {
@@ -62,6 +64,18 @@ __global__ void __launch_bounds__(256) k_gemv(LinArgs a) {
                     acc[r] = fmaf(wv.w, xv.w, acc[r]);
                 }
             }
+        };
+        if (K <= 128 * MAXV) {
+            // every load of the row issued before the first multiply
+            float4 wv[MAXV];
+#pragma unroll
+            for (int v = 0; v < MAXV; v++)
+                if (lane * 4 + v * 128 < K) wv[v] = ld_weight4(w + lane * 4 + v * 128, pol);
+#pragma unroll
+            for (int v = 0; v < MAXV; v++)
+                if (lane * 4 + v * 128 < K) step(wv[v], lane * 4 + v * 128);
+        } else {
+            for (int k = lane * 4; k < K; k += 128) step(ld_weight4(w + k, pol), k);
         }
 #pragma unroll
         for (int r = 0; r < RM; r++) acc[r] = warp_sum(acc[r]);
@@ -234,6 +248,31 @@ __global__ void __launch_bounds__(256) k_ssmax(float *q, int R, int d, int heads
         for (int t = 0; t < hid; t++) s = fmaf(w[t], x[t], s);
         float mm = s + q2b[j];
         q[(size_t)(r0 + r) * d + h * hd + j] = qs[i] * (scale[h * hd + j] * (1.0f + tanh1(mm)));
+    }
+}
+
+// Few rows: one block per (row, head), weights read straight from L2 by warps (one output per warp step).
+__global__ void __launch_bounds__(256) k_ssmax_rows(float *q, int d, int heads, int hid, const float *q0w,
+                                                    const float *q0b, const float *q2w, const float *q2b,
+                                                    const float *scale) {
+    extern __shared__ float sm[];
+    const int hd = d / heads, r = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float *qs = sm, *hs = sm + hd;
+    float *qp = q + (size_t)r * d + h * hd;
+    for (int j = tid; j < hd; j += blockDim.x) qs[j] = qp[j];
+    __syncthreads();
+    for (int t = warp; t < hid; t += 8) {
+        float s = 0.f;
+        for (int j = lane; j < hd; j += 32) s = fmaf(q0w[(size_t)t * hd + j], qs[j], s);
+        s = warp_sum(s);
+        if (lane == 0) hs[t] = gelu1(s + q0b[t]);
+    }
+    __syncthreads();
+    for (int j = warp; j < hd; j += 8) {
+        float s = 0.f;
+        for (int t = lane; t < hid; t += 32) s = fmaf(q2w[(size_t)j * hid + t], hs[t], s);
+        s = warp_sum(s);
+        if (lane == 0) qp[j] = qs[j] * (scale[h * hd + j] * (1.0f + tanh1(s + q2b[j])));
     }
 }
 
@@ -544,11 +583,13 @@ __global__ void __launch_bounds__(256, 2) k_attend_flash(AttnArgs a) {
     }
 }
 
-// Log-sum-exp merge of the parts of each (row, head) (nn.rs:261-276 merge, then 280-286 finish).
-__global__ void __launch_bounds__(128) k_attend_merge(const float *ms, const float *acc, int P, int R, int H, int d,
+// Log-sum-exp merge of the parts of each (row, head) (nn.rs:261-276 merge, then 280-286 finish). One block of
+// 256 threads per (row, head): the part weights e^(m_p - M) first, then each warp sums a share of the parts
+// with 16-byte loads along the head's values, and the warps' sums meet in shared memory.
+__global__ void __launch_bounds__(256) k_attend_merge(const float *ms, const float *acc, int P, int R, int H, int d,
                                                       float *out, int ldo) {
-    extern __shared__ float wsm[];  // [P]
-    __shared__ float red[4];
+    extern __shared__ __align__(16) float wsm[];  // [P] part weights, then [8][hd] warp sums
+    __shared__ float red[8];
     const int r = blockIdx.x / H, h = blockIdx.x % H, hd = d / H, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float mx = -FLT_MAX;
     for (int p = tid; p < P; p += blockDim.x) {
@@ -558,7 +599,8 @@ __global__ void __launch_bounds__(128) k_attend_merge(const float *ms, const flo
     mx = warp_max(mx);
     if (lane == 0) red[warp] = mx;
     __syncthreads();
-    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float M = red[0];
+    for (int w = 1; w < 8; w++) M = fmaxf(M, red[w]);
     __syncthreads();
     float ssum = 0.f;
     for (int p = tid; p < P; p += blockDim.x) {
@@ -570,11 +612,36 @@ __global__ void __launch_bounds__(128) k_attend_merge(const float *ms, const flo
     ssum = warp_sum(ssum);
     if (lane == 0) red[warp] = ssum;
     __syncthreads();
-    const float inv = 1.0f / ((red[0] + red[1]) + (red[2] + red[3]));
+    float S = 0.f;
+    for (int w = 0; w < 8; w++) S += red[w];
+    const float inv = 1.0f / S;
+    float *wsum = wsm + ((P + 3) & ~3);  // [8][hd]
+    const float *base = acc + (size_t)r * d + h * hd;
+    const size_t pstride = (size_t)R * d;
+    if ((hd & 3) == 0 && ((d & 3) == 0)) {
+        // lanes along the head's values four at a time; warps over the parts
+        for (int j0 = lane * 4; j0 < hd; j0 += 128) {
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+            int p = warp;
+#pragma unroll 4
+            for (; p < P; p += 8) {
+                const float4 v = *reinterpret_cast<const float4 *>(base + p * pstride + j0);
+                const float w = wsm[p];
+                o.x = fmaf(v.x, w, o.x), o.y = fmaf(v.y, w, o.y), o.z = fmaf(v.z, w, o.z), o.w = fmaf(v.w, w, o.w);
+            }
+            *reinterpret_cast<float4 *>(wsum + warp * hd + j0) = o;
+        }
+    } else {
+        for (int j = lane; j < hd; j += 32) {
+            float o = 0.f;
+            for (int p = warp; p < P; p += 8) o = fmaf(base[p * pstride + j], wsm[p], o);
+            wsum[warp * hd + j] = o;
+        }
+    }
+    __syncthreads();
     for (int j = tid; j < hd; j += blockDim.x) {
         float o = 0.f;
-        const float *src = acc + (size_t)r * d + h * hd + j;
-        for (int p = 0; p < P; p++) o = fmaf(src[(size_t)p * R * d], wsm[p], o);
+        for (int w = 0; w < 8; w++) o += wsum[w * hd + j];
         out[(size_t)r * ldo + h * hd + j] = o * inv;
     }
 }
@@ -792,25 +859,34 @@ cudaError_t kernels_init() {
     return cudaSuccess;
 }
 
+// Opt a kernel in to more than 48 KB of dynamic shared memory, once per kernel and size (per process: the
+// attribute is per function; devices of one process share it).
 template <typename K>
 static cudaError_t allow_smem(K kernel, size_t bytes) {
     if (bytes <= 48 * 1024) return cudaSuccess;
-    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    static std::mutex mu;
+    static std::map<const void *, size_t> done;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t &have = done[(const void *)kernel];
+    if (bytes <= have) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) have = bytes;
+    return e;
 }
 
 cudaError_t launch_linear(const LinArgs &a, float *stats_scratch, cudaStream_t s, uint64_t *launches) {
     if (a.M <= 0 || a.N <= 0) return cudaSuccess;
     if (a.M <= 8 && !a.bias_on_m) {
         const size_t smem = (size_t)a.M * a.K * sizeof(float);
-        const int grid = (a.N + 7) / 8;
+        const int grid = (a.N + 3) / 4;
         if (a.M == 1) {
             cudaError_t e = allow_smem(k_gemv<1>, smem);
             if (e != cudaSuccess) return e;
-            k_gemv<1><<<grid, 256, smem, s>>>(a);
+            k_gemv<1><<<grid, 128, smem, s>>>(a);
         } else {
             cudaError_t e = allow_smem(k_gemv<8>, smem);
             if (e != cudaSuccess) return e;
-            k_gemv<8><<<grid, 256, smem, s>>>(a);
+            k_gemv<8><<<grid, 128, smem, s>>>(a);
         }
         TCU_LAUNCHED(launches);
         return cudaGetLastError();
@@ -837,7 +913,12 @@ cudaError_t launch_ln_apply(const float *x, int M, int K, const float *w, const 
 cudaError_t launch_ssmax(float *q, int R, int d, int heads, int hid, const float *q0w, const float *q0b,
                          const float *q2w, const float *q2b, const float *scale, cudaStream_t s, uint64_t *launches) {
     const int hd = d / heads;
-    const int rb = R <= 4 ? R : 16;
+    if (R <= 16) {
+        k_ssmax_rows<<<dim3(R, heads), 256, sizeof(float) * (hd + hid), s>>>(q, d, heads, hid, q0w, q0b, q2w, q2b, scale);
+        TCU_LAUNCHED(launches);
+        return cudaGetLastError();
+    }
+    const int rb = 16;
     const size_t smem = sizeof(float) * ((size_t)hid * (hd + 1) + (size_t)hd * (hid + 1) + (size_t)rb * hd + (size_t)rb * hid);
     cudaError_t e = allow_smem(k_ssmax, smem);
     if (e != cudaSuccess) return e;
@@ -870,10 +951,10 @@ static cudaError_t decode_kv(int hd, const AttnArgs &a, cudaStream_t s) {
 }
 
 cudaError_t launch_attend_merge(const AttnArgs &a, int parts, cudaStream_t s, uint64_t *launches) {
-    const size_t smem = sizeof(float) * (size_t)parts;
+    const size_t smem = sizeof(float) * ((size_t)((parts + 3) & ~3) + 8 * (size_t)(a.d / a.heads));
     cudaError_t e = allow_smem(k_attend_merge, smem);
     if (e != cudaSuccess) return e;
-    k_attend_merge<<<a.R * a.heads, 128, smem, s>>>(a.part_ms, a.part_acc, parts, a.R, a.heads, a.d, a.out, a.ldo);
+    k_attend_merge<<<a.R * a.heads, 256, smem, s>>>(a.part_ms, a.part_acc, parts, a.R, a.heads, a.d, a.out, a.ldo);
     TCU_LAUNCHED(launches);
     return cudaGetLastError();
 }
