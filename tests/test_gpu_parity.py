@@ -118,7 +118,9 @@ def test_rows_are_independent(gpu):
     all_rows = vm.stage(h, 10)
     for lo, hi in [(0, 1), (10, 14), (40, 80), (149, 150)]:
         part = vm.stage(h[lo:hi], 10)
-        assert np.abs(part - all_rows[lo:hi]).max() < 1e-5
+        # few rows take the keys-parallel path, many the row-blocked one: sums in another order
+        assert np.abs(part - all_rows[lo:hi]).max() < STAGE
+        assert np.abs(softmax(part) - softmax(all_rows[lo:hi])).max() < 1e-6
 
 
 def test_regression_outputs(gpu):
