@@ -137,6 +137,26 @@ TCU_API int tcu_pack_device(tcu_ctx *ctx, int kv, int d, int rc, const float *c,
 /* Bytes of a stored chunk of rc rows (src/fit.rs:124-126). */
 TCU_API size_t tcu_record(int kv, int d, int rc);
 
+/* Few-row attention that allocates nothing (no counterpart in the reference; an addition for callers that cannot
+ * call cudaMalloc: code running while a CUDA graph is captured, hosts whose device memory belongs to an arena or
+ * another runtime's allocator, and real-time paths that cannot accept an allocation's latency or failure).
+ * Same result as tcu_attend_device: the attention outputs out [nq][d] (device) of scaled queries q [nq][d]
+ * (device) against one layer's stored keys/values `layer` (device, the n{j}_kv{l} bytes of `rows` cached rows in
+ * chunks of `chunk`, format kv), queued on `stream` (a cudaStream_t; NULL = the legacy default stream). No
+ * context or handle is needed. Its scratch is one static device array of TCU_NOALLOC_SCRATCH_BYTES (16 MiB) in
+ * every context that loads this library, kept until the process exits; a call is refused with TCU_ERR_ARG (and a
+ * message in `err`, if given) when nq > TCU_NOALLOC_MAX_ROWS, when the cache has more than TCU_NOALLOC_MAX_ITEMS
+ * key slices of 32-64 rows, or when the work does not fit the scratch (it fits 32 query rows at 10,000 cached
+ * rows of width 512 stored as i16, about 4 at 100,000). The first call on each device looks the scratch's address up (with that device current): make
+ * it before any stream capture. Every call shares the scratch and it keeps the last call's contents (each call
+ * writes all it reads, so nothing must start at zero): calls that overlap on the GPU - on two streams, or from
+ * two threads - race and give wrong answers; serialise them. */
+#define TCU_NOALLOC_SCRATCH_BYTES (16 << 20)
+#define TCU_NOALLOC_MAX_ROWS 32
+#define TCU_NOALLOC_MAX_ITEMS 8192
+TCU_API int tcu_attend_noalloc(int kv, int d, int heads, const void *layer, int rows, int chunk, const float *q, int nq,
+                               float *out, void *stream, char *err, size_t err_cap);
+
 /* Measurement hook (no counterpart in the reference, which times stages with wall clocks, src/predict.rs:20-56):
  * while enabled, every attention pass (one layer's attention kernels) is bracketed by CUDA events on its stream.
  * A call reads the total device time and count of the passes since the last call (when the pointers are set,

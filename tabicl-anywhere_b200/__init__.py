@@ -81,6 +81,8 @@ def lib():
         "tcu_pack_device": (_c_int, [_c_void, _c_int, _c_int, _c_int, _c_void, _c_void]),
         "tcu_record": (_c_size, [_c_int, _c_int, _c_int]),
         "tcu_profile": (_c_int, [_c_void, _c_int, P(ctypes.c_double), P(ctypes.c_uint64)]),
+        "tcu_attend_noalloc": (_c_int, [_c_int, _c_int, _c_int, _c_void, _c_int, _c_int, _c_void, _c_int, _c_void,
+                                        _c_void, ctypes.c_char_p, _c_size]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -284,6 +286,18 @@ class VramModel:
             self.free()
         except Exception:
             pass
+
+
+def attend_noalloc(kv, d, heads, layer_ptr, rows, chunk, q_ptr, nq, out_ptr, stream=None):
+    """Few-row attention against one layer's stored keys/values on device buffers, allocating nothing: for
+    callers that cannot allocate device memory at call time (during CUDA graph capture, under an external
+    arena or allocator, on real-time paths). Its scratch is one static 16 MiB device array shared by every call:
+    calls must not overlap on the GPU. Raises TcuError with the library's message when refused."""
+    buf = ctypes.create_string_buffer(512)
+    r = lib().tcu_attend_noalloc(kv, d, heads, layer_ptr, rows, chunk, q_ptr, nq, out_ptr, stream, buf, 512)
+    if r != OK:
+        raise TcuError(r, buf.value.decode())
+    return r
 
 
 def fit_icl(weights, h_ptr, y_ptr, rows, chunk=256, kv=KV_F32):

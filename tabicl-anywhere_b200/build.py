@@ -12,7 +12,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libtabicl_b200.so")
-SOURCES = ["kernels.cu", "engine.cpp", "tirs.cpp"]
+SOURCES = ["kernels.cu", "engine.cpp", "tirs.cpp", "noalloc.cu"]
 HEADERS = ["device.cuh", "kernels.cuh", "tirs.hpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
