@@ -235,6 +235,9 @@ def main():
     def step():
         vm.stage_device(h.data_ptr(), R, classes, out.data_ptr(), sp)
 
+    # warm-up with attention timing on: the stage graph with its timing events is captured here, not in the
+    # timed region
+    gpu.profile(True)
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize()
@@ -284,8 +287,10 @@ def main():
     h1 = h[:1].contiguous()
     o1 = out[:1].contiguous()
     lat = []
+    gpu.profile(True)
     for _ in range(5):
         vm.stage_device(h1.data_ptr(), 1, classes, o1.data_ptr(), sp)
+    torch.cuda.synchronize()
     gpu.profile(True)
     for _ in range(a.latency_reps):
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -157,10 +157,16 @@ TCU_API size_t tcu_record(int kv, int d, int rc);
 TCU_API int tcu_attend_noalloc(int kv, int d, int heads, const void *layer, int rows, int chunk, const float *q, int nq,
                                float *out, void *stream, char *err, size_t err_cap);
 
+/* Self-test of the tensor-core path (no counterpart in the reference): small exact products on the tcgen05 units
+ * against CUDA cores, for every operand layout the attention uses. *max_err is the largest difference (0 when
+ * the layouts are right), or -1 if the matrix units never answered. */
+TCU_API int tcu_selftest_mma(tcu_ctx *ctx, double *max_err);
+
 /* Measurement hook (no counterpart in the reference, which times stages with wall clocks, src/predict.rs:20-56):
  * while enabled, every attention pass (one layer's attention kernels) is bracketed by CUDA events on its stream.
  * A call reads the total device time and count of the passes since the last call (when the pointers are set,
- * after synchronising the device), then enables or disables timing and starts a new count. */
+ * after synchronising the device), then enables or disables timing and starts a new count. Stages replayed from
+ * a CUDA graph re-record the same events each replay, so for them the count covers the last replay. */
 TCU_API int tcu_profile(tcu_ctx *ctx, int enable, double *attend_ms, uint64_t *attend_launches);
 
 #ifdef __cplusplus

@@ -81,6 +81,7 @@ def lib():
         "tcu_pack_device": (_c_int, [_c_void, _c_int, _c_int, _c_int, _c_void, _c_void]),
         "tcu_record": (_c_size, [_c_int, _c_int, _c_int]),
         "tcu_profile": (_c_int, [_c_void, _c_int, P(ctypes.c_double), P(ctypes.c_uint64)]),
+        "tcu_selftest_mma": (_c_int, [_c_void, P(ctypes.c_double)]),
         "tcu_attend_noalloc": (_c_int, [_c_int, _c_int, _c_int, _c_void, _c_int, _c_int, _c_void, _c_int, _c_void,
                                         _c_void, ctypes.c_char_p, _c_size]),
     }
@@ -157,6 +158,12 @@ class Gpu:
         return self.check(lib().tcu_regression_head_device(self._h, qout_ptr, rows, nq, stride, alphas_ptr, na,
                                                            target_mean, target_scale, mean_ptr, var_ptr, median_ptr,
                                                            quant_ptr))
+
+    def selftest_mma(self):
+        """Largest error of exact small products on the tensor cores (0.0 when the operand layouts are right)."""
+        e = ctypes.c_double()
+        self.check(lib().tcu_selftest_mma(self._h, ctypes.byref(e)))
+        return e.value
 
     def pack(self, kv, d, rc, c_ptr, rec_ptr):
         return self.check(lib().tcu_pack_device(self._h, kv, d, rc, c_ptr, rec_ptr))

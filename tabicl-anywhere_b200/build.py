@@ -12,8 +12,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libtabicl_b200.so")
-SOURCES = ["kernels.cu", "engine.cpp", "tirs.cpp", "noalloc.cu"]
-HEADERS = ["device.cuh", "kernels.cuh", "tirs.hpp"]
+SOURCES = ["kernels.cu", "attend_tc.cu", "engine.cpp", "tirs.cpp", "noalloc.cu"]
+HEADERS = ["device.cuh", "kernels.cuh", "tirs.hpp", "tc.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-O3", "-std=c++17", "-lineinfo",

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <algorithm>
 #include <atomic>
 #include <cstring>
@@ -46,11 +47,13 @@ struct DevBuf {
         if (p) cudaFree(p);
         p = nullptr, bytes = 0;
     }
-    void ensure(size_t n) {
-        if (n <= bytes) return;
+    // grow to at least n bytes; true when the buffer moved (its old contents and address are gone)
+    bool ensure(size_t n) {
+        if (n <= bytes) return false;
         release();
         CU(cudaMalloc(&p, n));
         bytes = n;
+        return true;
     }
     template <typename T>
     T *as() const {
@@ -74,6 +77,8 @@ struct tcu_ctx {
     bool prof = false;
     std::vector<cudaEvent_t> prof_events;
     size_t prof_used = 0;
+    int *dev_err = nullptr;       // set by kernels that gave up waiting (tensor-core attention)
+    unsigned *dev_scan = nullptr; // scratch of the per-layer magnitude scan
 };
 
 // Device pointers of one in-context block (src/model.rs:27-98), plus what fitting adds.
@@ -105,8 +110,23 @@ struct tcu_model {
     int nitems = 0, ntiles = 0;
     std::vector<bool> have_layer;
     bool have_scales = false;
+    // tensor-core attention: per layer, power-of-two scalings that keep keys and values inside f16
+    std::vector<int> tc_eK, tc_eV;
+    bool tc_scanned = false;
     // working memory, grown to the largest call so far
     DevBuf h, q, att, mid, stats, out, part_ms, part_acc;
+    // the stage captured as CUDA graphs, one per (rows, outputs, profiling), over the buffers above
+    struct Graph {
+        int R, out_n;
+        bool prof;
+        cudaGraphExec_t exec;
+        uint64_t launches;  // kernels one replay runs
+        size_t prof_events; // timing events it records (from index 0 of the context's events), when profiling
+    };
+    std::vector<Graph> graphs;
+    ~tcu_model() {
+        for (auto &g : graphs) cudaGraphExecDestroy(g.exec);
+    }
 };
 
 // ---- handle lifetimes: a context lives while its weights do, weights while their models do --------------------
@@ -116,6 +136,8 @@ static void ctx_release(tcu_ctx *ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     for (auto e : ctx->prof_events) cudaEventDestroy(e);
+    if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->dev_scan) cudaFree(ctx->dev_scan);
     delete ctx;
 }
 
@@ -428,25 +450,59 @@ static int flash_splits(const tcu_ctx *ctx, int R, int heads, int ntiles) {
     return (ntiles + per - 1) / per;
 }
 
+// Which attention kernel takes R rows, and in how many parts of the training rows.
+enum class Path { Decode, Flash, Tensor };
+struct Plan {
+    Path path;
+    int splits;  // parts (decode: items)
+};
+static bool tc_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("TCU_TENSOR_CORES");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+static Plan attend_plan(const tcu_ctx *ctx, int R, int heads, int hd, int nitems, int ntiles) {
+    if (R <= 32) return {Path::Decode, nitems};
+    if (hd == 128 && tc_enabled()) {
+        // one wave of one block per SM: 128 rows x head blocks, each over a share of the key tiles
+        const int blocks = (R + 127) / 128 * heads;
+        int splits = std::max(1, std::min(ntiles, ctx->sms / blocks));
+        const int per = (ntiles + splits - 1) / splits;
+        return {Path::Tensor, (ntiles + per - 1) / per};
+    }
+    return {Path::Flash, flash_splits(ctx, R, heads, ntiles)};
+}
+
+static void drop_graphs(tcu_model *m) {
+    for (auto &g : m->graphs) cudaGraphExecDestroy(g.exec);
+    m->graphs.clear();
+}
+
+// Grow the working memory for R rows; captured graphs point into it, so they go when any buffer moves.
 static void ensure_work(tcu_model *m, int R) {
     const auto &s = m->w->shape;
     const size_t d = s.d, H = s.heads;
     const size_t wide = (size_t)std::max(s.ff, s.dec_ff);
-    m->q.ensure(sizeof(float) * R * d);
-    m->att.ensure(sizeof(float) * R * d);
-    m->mid.ensure(sizeof(float) * R * wide);
-    m->stats.ensure(sizeof(float) * R * 2);
-    const int splits = flash_splits(m->w->ctx, R, s.heads, m->ntiles);
-    const size_t pr = R <= 32 ? (size_t)m->nitems : (splits > 1 ? (size_t)splits : 0);
+    bool moved = false;
+    moved |= m->q.ensure(sizeof(float) * R * d);
+    moved |= m->att.ensure(sizeof(float) * R * d);
+    moved |= m->mid.ensure(sizeof(float) * R * wide);
+    moved |= m->stats.ensure(sizeof(float) * R * 2);
+    const Plan plan = attend_plan(m->w->ctx, R, s.heads, s.d / s.heads, m->nitems, m->ntiles);
+    const size_t pr = plan.path == Path::Decode ? (size_t)m->nitems : (plan.splits > 1 ? (size_t)plan.splits : 0);
     if (pr) {
-        m->part_ms.ensure(sizeof(float) * pr * R * H * 2);
-        m->part_acc.ensure(sizeof(float) * pr * R * d);
+        moved |= m->part_ms.ensure(sizeof(float) * pr * R * H * 2);
+        moved |= m->part_acc.ensure(sizeof(float) * pr * R * d);
     }
+    if (moved) drop_graphs(m);
 }
 
 // attention of R scaled queries q (device, [R][d]) against a layer given in stored form; out [R][d]
 static void attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int rows, int chunk, int kv, const int2 *items,
-                         int nitems, const int4 *tiles, int ntiles, const float *q, int R, float *out, cudaStream_t s) {
+                         int nitems, const int4 *tiles, int ntiles, const float *q, int R, float *out, cudaStream_t s,
+                         int eK = 0, int eV = 0) {
     const auto &sh = m->w->shape;
     AttnArgs a;
     a.layer = layer, a.rows = rows, a.chunk = chunk, a.d = sh.d, a.heads = sh.heads;
@@ -456,6 +512,7 @@ static void attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int r
     const int hd = sh.d / sh.heads;
     Launch ck{ctx, s};
     cudaEvent_t ev_end = nullptr;
+    unsigned ev_flags = cudaEventRecordDefault;
     if (ctx->prof) {
         if (ctx->prof_used + 2 > ctx->prof_events.size()) {
             for (int i = 0; i < 64; i++) {
@@ -464,26 +521,35 @@ static void attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int r
                 ctx->prof_events.push_back(e);
             }
         }
-        CU(cudaEventRecord(ctx->prof_events[ctx->prof_used], s));
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        CU(cudaStreamIsCapturing(s, &cs));
+        ev_flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault;
+        CU(cudaEventRecordWithFlags(ctx->prof_events[ctx->prof_used], s, ev_flags));
         ev_end = ctx->prof_events[ctx->prof_used + 1];
         ctx->prof_used += 2;
     }
     struct End {
         cudaEvent_t e;
         cudaStream_t s;
+        unsigned flags;
         ~End() {
-            if (e) cudaEventRecord(e, s);
+            if (e) cudaEventRecordWithFlags(e, s, flags);
         }
-    } end_mark{ev_end, s};
-    if (R <= 32) {
+    } end_mark{ev_end, s, ev_flags};
+    const Plan plan = attend_plan(ctx, R, sh.heads, hd, nitems, ntiles);
+    if (plan.path == Path::Decode) {
         a.items = items, a.nitems = nitems;
         ck(launch_attend_decode(kv, hd, a, s, &ctx->launches), "attend (decode)");
     } else {
         a.tiles = tiles, a.ntiles = ntiles;
-        const int splits = flash_splits(ctx, R, sh.heads, ntiles);
-        a.tiles_per_split = (ntiles + splits - 1) / splits;
+        a.tiles_per_split = (ntiles + plan.splits - 1) / plan.splits;
         a.splits = (ntiles + a.tiles_per_split - 1) / a.tiles_per_split;
-        ck(launch_attend_flash(kv, hd, a, s, &ctx->launches), "attend (flash)");
+        if (plan.path == Path::Tensor) {
+            a.tc_eK = eK, a.tc_eV = eV, a.err = ctx->dev_err;
+            ck(launch_attend_tc(kv, a, s, &ctx->launches), "attend (tensor cores)");
+        } else {
+            ck(launch_attend_flash(kv, hd, a, s, &ctx->launches), "attend (flash)");
+        }
     }
 }
 
@@ -493,6 +559,38 @@ static void linear(tcu_ctx *ctx, tcu_model *m, const float *x, int ldx, int R, i
     a.x = x, a.ldx = ldx, a.M = R, a.K = K, a.lnw = lnw, a.lnb = lnb, a.W = W, a.bias = b, a.N = N, a.y = y, a.ldy = ldy;
     a.act = act, a.accumulate = accumulate;
     Launch{ctx, s}(launch_linear(a, m->stats.as<float>(), s, &ctx->launches), "linear");
+}
+
+// A kernel that gave up waiting left a flag: report it once, and clear it.
+static void check_device_error(tcu_ctx *ctx) {
+    int flag = 0;
+    CU(cudaMemcpy(&flag, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (flag) {
+        CU(cudaMemset(ctx->dev_err, 0, sizeof(int)));
+        fail(TCU_ERR_CUDA, "tensor-core attention gave up waiting for its matrix units; outputs of that call are invalid");
+    }
+}
+
+// Largest |key| and |value| of a stored layer -> the tensor cores' power-of-two scalings (synchronises).
+static void scan_layer(tcu_ctx *ctx, const uint8_t *layer, int rows, int chunk, int d, int kv, cudaStream_t s, int &eK,
+                       int &eV) {
+    Launch{ctx, s}(launch_absmax_layer(layer, rows, chunk, d, kv, ctx->dev_scan, s, &ctx->launches), "scan");
+    unsigned bits[2];
+    CU(cudaMemcpyAsync(bits, ctx->dev_scan, sizeof(bits), cudaMemcpyDeviceToHost, s));
+    CU(cudaStreamSynchronize(s));
+    float mk, mv;
+    std::memcpy(&mk, &bits[0], 4), std::memcpy(&mv, &bits[1], 4);
+    if (!std::isfinite(mk) || !std::isfinite(mv)) fail(TCU_ERR_FORMAT, "cache holds a non-finite key or value");
+    eK = tc_exponent(mk), eV = tc_exponent(mv);
+}
+
+static void scan_model(tcu_ctx *ctx, tcu_model *m, cudaStream_t s) {
+    if (m->tc_scanned) return;
+    const int L = m->w->shape.layers;
+    m->tc_eK.assign(L, 0), m->tc_eV.assign(L, 0);
+    for (int l = 0; l < L; l++)
+        scan_layer(ctx, layer_ptr(m, l), m->rows, m->chunk, m->w->shape.d, m->kv, s, m->tc_eK[l], m->tc_eV[l]);
+    m->tc_scanned = true;
 }
 
 // predict.rs:413-568 one layer for R rows whose representations are h (device, [R][d], updated in place)
@@ -523,12 +621,70 @@ static void stage(tcu_ctx *ctx, tcu_model *m, float *h, int R, int out_n, float 
     for (int l = 0; l < L; l++) {
         query_rows(ctx, m, l, scales + (size_t)l * d, h, R, m->q.as<float>(), s);
         attend_layer(ctx, m, layer_ptr(m, l), m->rows, m->chunk, m->kv, m->items.as<int2>(), m->nitems, m->tiles.as<int4>(),
-                     m->ntiles, m->q.as<float>(), R, m->att.as<float>(), s);
+                     m->ntiles, m->q.as<float>(), R, m->att.as<float>(), s, m->tc_eK[l], m->tc_eV[l]);
         block_tail(ctx, m, l, h, m->att.as<float>(), R, s);
     }
     // predict.rs:570-584 decoder: only the first out_n outputs are computed (each output is its own row)
     linear(ctx, m, h, d, R, d, m->w->lnw, m->w->lnb, m->w->dec0w, m->w->dec0b, dff, m->mid.as<float>(), dff, 1, 0, s);
     linear(ctx, m, m->mid.as<float>(), dff, R, dff, nullptr, nullptr, m->w->dec2w, m->w->dec2b, out_n, out, out_n, 0, 0, s);
+}
+
+// The stage on the model's own buffers (m->h in, m->out out), replayed from a CUDA graph captured on the context
+// stream the first time a (rows, outputs, profiling) combination is seen. TCU_GRAPHS=0 runs it eagerly.
+static void stage_replay(tcu_ctx *ctx, tcu_model *m, int R, int out_n, cudaStream_t s) {
+    static const bool use_graphs = [] {
+        const char *e = getenv("TCU_GRAPHS");
+        return !(e && e[0] == '0');
+    }();
+    scan_model(ctx, m, ctx->stream);  // once per model, before any capture
+    ensure_work(m, R);
+    if (m->out.ensure(sizeof(float) * (size_t)R * out_n)) drop_graphs(m);
+    if (!use_graphs) {
+        stage(ctx, m, m->h.as<float>(), R, out_n, m->out.as<float>(), s);
+        return;
+    }
+    for (auto &g : m->graphs) {
+        if (g.R == R && g.out_n == out_n && g.prof == ctx->prof) {
+            CU(cudaGraphLaunch(g.exec, s));
+            ctx->launches += g.launches;
+            // a profiled graph re-records its own events: the profile then holds its last replay's passes
+            if (g.prof) ctx->prof_used = std::max(ctx->prof_used, g.prof_events);
+            return;
+        }
+    }
+    cudaStream_t cs = ctx->stream;
+    const uint64_t before = ctx->launches;
+    if (ctx->prof) ctx->prof_used = 0;  // a profiled graph owns the first events of the context
+    CU(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    cudaGraph_t graph = nullptr;
+    try {
+        stage(ctx, m, m->h.as<float>(), R, out_n, m->out.as<float>(), cs);
+    } catch (...) {
+        cudaStreamEndCapture(cs, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        throw;
+    }
+    CU(cudaStreamEndCapture(cs, &graph));
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    CU(e);
+    tcu_model::Graph g{R, out_n, ctx->prof, exec, ctx->launches - before, ctx->prof ? ctx->prof_used : 0};
+    // a profiled graph keeps its events for good: drop other profiled graphs, which used the same ones
+    if (g.prof) {
+        for (auto it = m->graphs.begin(); it != m->graphs.end();) {
+            if (it->prof) {
+                cudaGraphExecDestroy(it->exec);
+                it = m->graphs.erase(it);
+            } else {
+                ++it;
+            }
+        }
+    }
+    m->graphs.push_back(g);
+    // the capture itself ran nothing: count the replay's kernels
+    ctx->launches = before + g.launches;
+    CU(cudaGraphLaunch(exec, s));
 }
 
 // fit.rs:577-747 in-memory path on the device
@@ -566,10 +722,12 @@ static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, in
         if (l + 1 == L) break;  // fit.rs:664-666
         if (kv != 0) ck(launch_pack(kvT.as<float>(), rows, d, rows, chunk, 0, kvf.as<uint8_t>(), s, &ctx->launches), "pack f32");
         const uint8_t *fl = kv == 0 ? layer_ptr(m.get(), l) : kvf.as<uint8_t>();
+        int eK = 0, eV = 0;
+        scan_layer(ctx, fl, rows, chunk, d, 0, s, eK, eV);
         query_rows(ctx, m.get(), l, m->scales.as<float>() + (size_t)l * d, h, rows, m->q.as<float>(), s);
         // the f32 view has the same chunking, and flash tiles depend only on chunking
         attend_layer(ctx, m.get(), fl, rows, chunk, 0, nullptr, 0, m->tiles.as<int4>(), m->ntiles, m->q.as<float>(), rows,
-                     m->att.as<float>(), s);
+                     m->att.as<float>(), s, eK, eV);
         block_tail(ctx, m.get(), l, h, m->att.as<float>(), rows, s);
     }
     CU(cudaStreamSynchronize(s));
@@ -593,6 +751,9 @@ int tcu_open(int device, tcu_ctx **out) {
     int r = guarded(ctx.get(), [&]() -> int {
         CU(cudaDeviceGetAttribute(&ctx->sms, cudaDevAttrMultiProcessorCount, device));
         CU(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
+        CU(cudaMalloc(&ctx->dev_err, sizeof(int)));
+        CU(cudaMemset(ctx->dev_err, 0, sizeof(int)));
+        CU(cudaMalloc(&ctx->dev_scan, 2 * sizeof(unsigned)));
         CU(kernels_init());
         return TCU_OK;
     });
@@ -731,6 +892,7 @@ int tcu_model_put_layer(tcu_model *m, int layer, size_t offset, const void *byte
         if (!bytes || offset + nbytes > m->layer_bytes) fail(TCU_ERR_ARG, "model_put_layer: range past the layer's " + std::to_string(m->layer_bytes) + " bytes");
         CU(cudaMemcpy(m->layers.as<uint8_t>() + m->layer_stride * layer + offset, bytes, nbytes, cudaMemcpyHostToDevice));
         if (offset + nbytes == m->layer_bytes) m->have_layer[layer] = true;
+        m->tc_scanned = false;
         return TCU_OK;
     });
 }
@@ -816,9 +978,10 @@ int tcu_attend_device(tcu_model *m, int layer, const float *q, int rows, float *
         if (layer < 0 || layer >= m->w->shape.layers || rows < 0 || (rows && (!q || !out))) fail(TCU_ERR_ARG, "attend: bad argument");
         if (rows == 0) return TCU_OK;
         cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+        scan_model(ctx, m, ctx->stream);
         ensure_work(m, rows);
         attend_layer(ctx, m, layer_ptr(m, layer), m->rows, m->chunk, m->kv, m->items.as<int2>(), m->nitems, m->tiles.as<int4>(),
-                     m->ntiles, q, rows, out, s);
+                     m->ntiles, q, rows, out, s, m->tc_eK[layer], m->tc_eV[layer]);
         return TCU_OK;
     });
 }
@@ -830,10 +993,13 @@ int tcu_stage_device(tcu_model *m, const float *h, int rows, int out_n, float *o
         if (rows < 0 || (rows && (!h || !out))) fail(TCU_ERR_ARG, "stage: bad argument");
         if (rows == 0) return TCU_OK;
         cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+        check_ready(m);
+        if (out_n < 1 || out_n > m->w->shape.outs) fail(TCU_ERR_ARG, "stage: out_n must be 1..decoder outputs");
         const size_t n = (size_t)rows * m->w->shape.d;
-        m->h.ensure(sizeof(float) * n);
-        if (h != m->h.as<float>()) CU(cudaMemcpyAsync(m->h.p, h, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
-        stage(ctx, m, m->h.as<float>(), rows, out_n, out, s);
+        if (m->h.ensure(sizeof(float) * n)) drop_graphs(m);
+        CU(cudaMemcpyAsync(m->h.p, h, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+        stage_replay(ctx, m, rows, out_n, s);
+        CU(cudaMemcpyAsync(out, m->out.p, sizeof(float) * (size_t)rows * out_n, cudaMemcpyDeviceToDevice, s));
         return TCU_OK;
     });
 }
@@ -855,6 +1021,7 @@ int tcu_attend(tcu_model *m, int layer, const float *q, int rows, int d, int hea
         if (r != TCU_OK) return r;
         CU(cudaMemcpyAsync(out, m->out.p, sizeof(float) * n, cudaMemcpyDeviceToHost, s));
         CU(cudaStreamSynchronize(s));
+        check_device_error(ctx);
         return TCU_OK;
     });
 }
@@ -866,13 +1033,15 @@ int tcu_stage(tcu_model *m, const float *h, int rows, int d, int out_n, float *o
         if (d != m->w->shape.d) fail(TCU_ERR_ARG, "stage: d differs from the weights'");
         if (rows < 0 || (rows && (!h || !out))) fail(TCU_ERR_ARG, "stage: bad argument");
         if (rows == 0) return TCU_OK;
-        m->h.ensure(sizeof(float) * (size_t)rows * d);
-        m->out.ensure(sizeof(float) * (size_t)rows * out_n);
+        check_ready(m);
+        if (out_n < 1 || out_n > m->w->shape.outs) fail(TCU_ERR_ARG, "stage: out_n must be 1..decoder outputs");
+        if (m->h.ensure(sizeof(float) * (size_t)rows * d)) drop_graphs(m);
         cudaStream_t s = ctx->stream;
         CU(cudaMemcpyAsync(m->h.p, h, sizeof(float) * (size_t)rows * d, cudaMemcpyHostToDevice, s));
-        stage(ctx, m, m->h.as<float>(), rows, out_n, m->out.as<float>(), s);
+        stage_replay(ctx, m, rows, out_n, s);
         CU(cudaMemcpyAsync(out, m->out.p, sizeof(float) * (size_t)rows * out_n, cudaMemcpyDeviceToHost, s));
         CU(cudaStreamSynchronize(s));
+        check_device_error(ctx);
         return TCU_OK;
     });
 }
@@ -925,6 +1094,24 @@ int tcu_pack_device(tcu_ctx *ctx, int kv, int d, int rc, const float *c, void *r
 }
 
 size_t tcu_record(int kv, int d, int rc) { return record_bytes(kv, d, rc); }
+
+int tcu_selftest_mma(tcu_ctx *ctx, double *max_err) {
+    return guarded(ctx, [&]() -> int {
+        if (!max_err) fail(TCU_ERR_ARG, "selftest: null argument");
+        float *res = nullptr;
+        CU(cudaMalloc(&res, 2 * sizeof(float)));
+        cudaError_t e = launch_tc_selftest(res, ctx->stream);
+        unsigned bits[2] = {0, 0};
+        if (e == cudaSuccess) e = cudaMemcpyAsync(bits, res, sizeof(bits), cudaMemcpyDeviceToHost, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        cudaFree(res);
+        CU(e);
+        float worst;
+        std::memcpy(&worst, &bits[0], 4);
+        *max_err = bits[1] ? -1.0 : (double)worst;
+        return TCU_OK;
+    });
+}
 
 int tcu_profile(tcu_ctx *ctx, int enable, double *attend_ms, uint64_t *attend_launches) {
     return guarded(ctx, [&]() -> int {

@@ -37,6 +37,8 @@ struct AttnArgs {
     float *part_acc = nullptr;     // [parts][R][d]: weighted value sums
     float *out = nullptr;          // [R][d] finished outputs (row stride ldo)
     int ldo = 0;
+    int tc_eK = 0, tc_eV = 0;      // tensor-core path: power-of-two scalings of the keys and values
+    int *err = nullptr;            // set to 1 when a kernel gave up waiting
 };
 
 #ifdef __CUDACC__
@@ -77,5 +79,16 @@ cudaError_t launch_regression_head(const float *qout, int rows, int nq, int stri
                                    double tmean, double tscale, double *mean, double *var, double *median,
                                    double *quant, cudaStream_t s, uint64_t *launches);
 cudaError_t kernels_init();
+
+// Tensor-core attention (head width 128, many rows): merges itself when splits == 1, else writes parts.
+cudaError_t launch_attend_tc(int kv, const AttnArgs &a, cudaStream_t s, uint64_t *launches);
+size_t attend_tc_smem();
+// Largest |key| and |value| of a layer, as float bits, into out[0], out[1].
+cudaError_t launch_absmax_layer(const uint8_t *layer, int rows, int chunk, int d, int kv, unsigned *out, cudaStream_t s,
+                                uint64_t *launches);
+// Power-of-two exponent e with mx * 2^e < 2^14 (0 for mx = 0).
+int tc_exponent(float mx);
+// Self-test of the tensor-core operand layouts: result[0] = largest error (float), result[1] = 1 if a wait gave up.
+cudaError_t launch_tc_selftest(float *result, cudaStream_t s);
 
 }  // namespace tcu

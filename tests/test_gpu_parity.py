@@ -33,6 +33,11 @@ def _meta(rows, chunk, kv, classes):
     return [rows, 7, classes, chunk, kv, 1, 1]
 
 
+def test_tensor_core_operand_layouts(gpu):
+    """Exact small-integer products on the tcgen05 units equal CUDA-core sums for every operand layout used."""
+    assert gpu.selftest_mma() == 0.0
+
+
 # ---- the reference's tiny classifier and PyTorch's golden numbers -----------------------------------------------
 
 @pytest.mark.parametrize("kv", [0, 1, 2])
@@ -121,6 +126,21 @@ def test_rows_are_independent(gpu):
         # few rows take the keys-parallel path, many the row-blocked one: sums in another order
         assert np.abs(part - all_rows[lo:hi]).max() < STAGE
         assert np.abs(softmax(part) - softmax(all_rows[lo:hi])).max() < 1e-6
+
+
+def test_graph_replays_and_regrowth(gpu):
+    """The stage is captured as a CUDA graph per row count and replayed; growing the working memory for a larger
+    call must not leave earlier graphs pointing at freed buffers."""
+    cfg, wt, m, caches, scales = _synthetic("full", 2, 400, 256, 1, seed=41)
+    w = _weights(gpu, cfg, wt)
+    vm = tcu.VramModel.from_parts(w, _meta(400, 256, 1, 10), 400, 10, scales, caches)
+    h5, h70 = synth.row_reps(5, m.d, 42), synth.row_reps(70, m.d, 43)
+    first = vm.stage(h5, 10)
+    assert np.array_equal(vm.stage(h5, 10), first)      # replay
+    big = vm.stage(h70, 10)                              # buffers grow: graphs dropped
+    assert np.array_equal(vm.stage(h5, 10), first)      # recaptured on the new buffers
+    assert np.abs(big - oracle.in_context(m, 1, caches, scales, 400, 256, h70, 10)).max() < STAGE
+    assert np.abs(vm.stage(h5, 3) - first[:, :3]).max() == 0.0  # fewer outputs: its own graph
 
 
 def test_regression_outputs(gpu):
