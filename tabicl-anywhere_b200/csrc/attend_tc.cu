@@ -54,15 +54,19 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
     __half *Vlo = Vhi + HD * BK;
     __half *Phi = Vlo + HD * BK;                      // [BQ][BK keys] K-major
     __half *Plo = Phi + BQ * BK;
-    uint64_t *mbar = reinterpret_cast<uint64_t *>(Plo + BQ * BK);  // [0] S ready, [1] O updated
+    uint64_t *mbar = reinterpret_cast<uint64_t *>(Plo + BQ * BK);  // [0] S ready, [1] P V ready
     uint32_t *tslot = reinterpret_cast<uint32_t *>(mbar + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
     float *qscale = reinterpret_cast<float *>(tslot + 4);  // [BQ] 2^e of each row's query
+    float *fr = qscale + BQ;                               // [BQ] this tile's rescale factor of each row
+    float *lrow = fr + BQ;                                 // [BQ] final weight sums
+    float *mrow = lrow + BQ;                               // [BQ] final maxima
 
     const int tid = threadIdx.x, warp = tid >> 5;
     const int h = blockIdx.y, split = blockIdx.z, r0 = blockIdx.x * BQ, d = a.d, H = gridDim.y;
     if (warp == 0) {
-        tmem_alloc(tslot, 256);
+        // S: hi*hi in columns 0-63, cross terms 64-127; one tile's P V: hi*hi 128-255, cross terms 256-383
+        tmem_alloc(tslot, 512);
         tmem_relinquish();
     }
     if (tid == 0) {
@@ -90,10 +94,10 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
-    const uint32_t tmem = *tslot, tS = tmem, tO = tmem + 64;
-    // queries, split
+    const uint32_t tmem = *tslot, tShh = tmem, tSx = tmem + 64, tOhh = tmem + 128, tOx = tmem + 256;
+    // queries, split; consecutive threads take consecutive rows so their 16-byte stores are contiguous
     for (int i = tid; i < BQ * (HD / 8); i += 256) {
-        const int m = i / (HD / 8), j0 = (i % (HD / 8)) * 8, r = r0 + m;
+        const int m = i % BQ, j0 = (i / BQ) * 8, r = r0 + m;
         float v[8];
         if (r < a.R) {
             const float4 *qp = reinterpret_cast<const float4 *>(a.q + (size_t)r * a.ldq + h * HD + j0);
@@ -106,23 +110,20 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
         put8(Qhi, Qlo, kmajor_off(m, j0, BQ), v, qscale[m]);
     }
     const float kscale = pow2f(a.tc_eK), vscale = pow2f(a.tc_eV);
-    const float s_unscale_k = pow2f(-a.tc_eK);
-    const float row_unscale = tid < BQ ? pow2f(-erow) * s_unscale_k : 1.f;
+    const float row_unscale = tid < BQ ? pow2f(-erow) * pow2f(-a.tc_eK) : 1.f;
     const uint32_t idS = idesc_f16(BQ, BK, 0, 1), idO = idesc_f16(BQ, HD, 0, 0);
+    // every thread's share of O: row (warp % 4) * 32 + lane, columns (warp / 4) * 64 + [0, 64)
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const int orow = (warp & 3) * 32 + (tid & 31), ocol = (warp >> 2) * 64;
+    float o[64];
+#pragma unroll
+    for (int e = 0; e < 64; e++) o[e] = 0.f;
     float mrun = -FLT_MAX, lrun = 0.f;
     uint32_t ps = 0, po = 0;
     const int t0 = split * a.tiles_per_split, t1 = min(a.ntiles, t0 + a.tiles_per_split);
     const uint64_t pol = policy_evict_first();
-    bool issued_o = false;
+    bool any = false;
     for (int t = t0; t < t1; t++) {
-        if (t > t0) {
-            // the previous tile's P V product must be done before V and P are overwritten
-            if (!mbar_wait(&mbar[1], po, TC_WAIT_CYCLES)) *abort_flag = 1;
-            po ^= 1;
-        }
-        __syncthreads();
-        if (*abort_flag) break;
         const int4 tile = a.tiles[t];
         const int ci = tile.x, k0 = tile.y, len = tile.z;
         const int rc = min(a.chunk, a.rows - ci * a.chunk);
@@ -134,31 +135,26 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
         const size_t rowb = (size_t)rc * W;
         const bool fast = len == BK && ((((uintptr_t)kb) | ((uintptr_t)vb) | rowb) & 15) == 0;
         if (fast) {
-            for (int i = tid; i < HD * VPR; i += 256) {
-                const int j = i / VPR, vv = i % VPR;
-                const uint4 rk = ld_stream16(kb + j * rowb + vv * 16, pol);
-                const uint4 rv = ld_stream16(vb + j * rowb + vv * 16, pol);
+            // consecutive threads take consecutive dims (contiguous shared-memory stores in both layouts), each
+            // reading a 32-byte run of its dim's keys
+            for (int i = tid; i < HD * VPR / 2; i += 256) {
+                const int j = i % HD, vp = i / HD;
                 const float ks = (KV ? sc[h * HD + j] : 1.f) * kscale;
                 const float vs = (KV ? sc[d + h * HD + j] : 1.f) * vscale;
-                constexpr int G = EPV < 8 ? EPV : 8;  // keys per write group (4 for f32, else 8)
+                const uint4 rk0 = ld_stream16(kb + j * rowb + vp * 32, pol), rk1 = ld_stream16(kb + j * rowb + vp * 32 + 16, pol);
+                const uint4 rv0 = ld_stream16(vb + j * rowb + vp * 32, pol), rv1 = ld_stream16(vb + j * rowb + vp * 32 + 16, pol);
 #pragma unroll
-                for (int g = 0; g < EPV; g += G) {
-                    const int key = vv * EPV + g;
+                for (int g = 0; g < 2 * EPV; g += 8) {
                     float fk[8], fv[8];
 #pragma unroll
-                    for (int e = 0; e < 8; e++) fk[e] = fv[e] = 0.f;
-#pragma unroll
-                    for (int e = 0; e < G; e++) fk[e] = unpack<KV>(rk, g + e) * ks, fv[e] = unpack<KV>(rv, g + e) * vs;
-                    if (G == 8) {
-                        put8(Khi, Klo, mnmajor_off(key, j, BK), fk, 1.f);
-                        put8(Vhi, Vlo, kmajor_off(j, key, HD), fv, 1.f);
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < G; e++) {
-                            split_f16(fk[e], Khi[mnmajor_off(key + e, j, BK)], Klo[mnmajor_off(key + e, j, BK)]);
-                            split_f16(fv[e], Vhi[kmajor_off(j, key + e, HD)], Vlo[kmajor_off(j, key + e, HD)]);
-                        }
+                    for (int e = 0; e < 8; e++) {
+                        const int x = g + e;  // element within the 32-byte run
+                        fk[e] = (x < EPV ? unpack<KV>(rk0, x) : unpack<KV>(rk1, x - EPV)) * ks;
+                        fv[e] = (x < EPV ? unpack<KV>(rv0, x) : unpack<KV>(rv1, x - EPV)) * vs;
                     }
+                    const int key = vp * 2 * EPV + g;
+                    put8(Khi, Klo, mnmajor_off(key, j, BK), fk, 1.f);
+                    put8(Vhi, Vlo, kmajor_off(j, key, HD), fv, 1.f);
                 }
             }
         } else {
@@ -178,12 +174,12 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
         if (tid == 0) {
             fence_after_sync();
 #pragma unroll
+            for (int s = 0; s < HD / 16; s++)
+                mma_f16(tShh, kstep_desc(Qhi, BQ, s), kstep_desc(Khi, BK, s), idS, s > 0 ? 1u : 0u);
+#pragma unroll
             for (int s = 0; s < HD / 16; s++) {
-                const uint64_t qh = kstep_desc(Qhi, BQ, s), ql = kstep_desc(Qlo, BQ, s);
-                const uint64_t kh = kstep_desc(Khi, BK, s), kl = kstep_desc(Klo, BK, s);
-                mma_f16(tS, qh, kh, idS, s > 0);
-                mma_f16(tS, qh, kl, idS, 1);
-                mma_f16(tS, ql, kh, idS, 1);
+                mma_f16(tSx, kstep_desc(Qhi, BQ, s), kstep_desc(Klo, BK, s), idS, s > 0 ? 1u : 0u);
+                mma_f16(tSx, kstep_desc(Qlo, BQ, s), kstep_desc(Khi, BK, s), idS, 1);
             }
             mma_commit(&mbar[0]);
         }
@@ -192,13 +188,14 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
             if (!ok) *abort_flag = 1;
             fence_after_sync();
             float s[64];
-            {
-                float v0[32], v1[32];
-                tmem_ld32(tS + lane_base, v0);
-                tmem_ld32(tS + lane_base + 32, v1);
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                float x[32], y[32];
+                tmem_ld32(tShh + lane_base + 32 * c, x);
+                tmem_ld32(tSx + lane_base + 32 * c, y);
                 tmem_wait_ld();
 #pragma unroll
-                for (int k = 0; k < 32; k++) s[k] = v0[k] * row_unscale, s[32 + k] = v1[k] * row_unscale;
+                for (int k = 0; k < 32; k++) s[32 * c + k] = (x[k] + y[k]) * row_unscale;
             }
             float mx = -FLT_MAX;
 #pragma unroll
@@ -213,29 +210,15 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
                 s[k] = p * 16384.f;  // 2^14: small weights stay normal in f16
                 psum += p;
             }
-            const bool rescale = lrun > 0.f && f != 1.f;
             lrun = lrun * f + psum;
             mrun = mnew;
-            const int row = tid;
+            fr[tid] = f;
 #pragma unroll
             for (int g = 0; g < 8; g++) {
                 float v[8];
 #pragma unroll
                 for (int e = 0; e < 8; e++) v[e] = s[g * 8 + e];
-                put8(Phi, Plo, kmajor_off(row, g * 8, BQ), v, 1.f);
-            }
-            if (__any_sync(0xffffffffu, rescale) && ok) {
-                const float fr = rescale ? f : 1.f;
-#pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    float o[32];
-                    tmem_ld32(tO + lane_base + 32 * c, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int k = 0; k < 32; k++) o[k] *= fr;
-                    tmem_st32(tO + lane_base + 32 * c, o);
-                }
-                tmem_wait_st();
+                put8(Phi, Plo, kmajor_off(tid, g * 8, BQ), v, 1.f);
             }
         }
         ps ^= 1;
@@ -246,63 +229,66 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
         if (tid == 0) {
             fence_after_sync();
 #pragma unroll
+            for (int s = 0; s < BK / 16; s++)
+                mma_f16(tOhh, kstep_desc(Phi, BQ, s), kstep_desc(Vhi, HD, s), idO, s > 0 ? 1u : 0u);
+#pragma unroll
             for (int s = 0; s < BK / 16; s++) {
-                const uint64_t ph = kstep_desc(Phi, BQ, s), pl = kstep_desc(Plo, BQ, s);
-                const uint64_t vh = kstep_desc(Vhi, HD, s), vl = kstep_desc(Vlo, HD, s);
-                mma_f16(tO, ph, vh, idO, (t > t0 || s > 0) ? 1u : 0u);
-                mma_f16(tO, ph, vl, idO, 1);
-                mma_f16(tO, pl, vh, idO, 1);
+                mma_f16(tOx, kstep_desc(Phi, BQ, s), kstep_desc(Vlo, HD, s), idO, s > 0 ? 1u : 0u);
+                mma_f16(tOx, kstep_desc(Plo, BQ, s), kstep_desc(Vhi, HD, s), idO, 1);
             }
             mma_commit(&mbar[1]);
         }
-        issued_o = true;
-    }
-    // the last P V product, then each row's output
-    bool have_o = false;
-    if (issued_o && !*abort_flag) {
-        have_o = mbar_wait(&mbar[1], po, TC_WAIT_CYCLES);
-        if (!have_o) *abort_flag = 1;
-    }
-    fence_after_sync();
-    if (warp < 4 && have_o) {
-        const int r = r0 + tid;
-        const float oun = pow2f(-14 - a.tc_eV);
-        for (int c = 0; c < 4; c++) {
-            float o[32];
-            tmem_ld32(tO + lane_base + 32 * c, o);
-            tmem_wait_ld();
-            if (r < a.R) {
-                if (a.splits == 1) {
-                    const float inv = 1.0f / lrun;
-                    float *dst = a.out + (size_t)r * a.ldo + h * HD + 32 * c;
+        // every thread folds this tile's P V into its share of O: O = O * f + (hi*hi + cross terms)
+        const bool okO = mbar_wait(&mbar[1], po, TC_WAIT_CYCLES);
+        po ^= 1;
+        if (!okO) *abort_flag = 1;
+        fence_after_sync();
+        if (okO) {
+            const float f = fr[orow];
 #pragma unroll
-                    for (int k = 0; k < 32; k++) dst[k] = o[k] * oun * inv;
-                } else {
-                    float *dst = a.part_acc + ((size_t)split * a.R + r) * d + h * HD + 32 * c;
+            for (int c = 0; c < 2; c++) {
+                float x[32], y[32];
+                tmem_ld32(tOhh + lane_base + ocol + 32 * c, x);
+                tmem_ld32(tOx + lane_base + ocol + 32 * c, y);
+                tmem_wait_ld();
 #pragma unroll
-                    for (int k = 0; k < 32; k++) dst[k] = o[k] * oun;
-                }
+                for (int k = 0; k < 32; k++) o[32 * c + k] = fmaf(o[32 * c + k], f, x[k] + y[k]);
             }
         }
-        if (r < a.R && a.splits > 1) {
-            float *ms = a.part_ms + (((size_t)split * a.R + r) * H + h) * 2;
-            ms[0] = mrun, ms[1] = lrun;
+        any = true;
+        fence_before_sync();
+        __syncthreads();
+        if (*abort_flag) break;
+    }
+    if (tid < BQ) lrow[tid] = lrun, mrow[tid] = mrun;
+    __syncthreads();
+    const bool ok = any && !*abort_flag;
+    const int r = r0 + orow;
+    if (r < a.R) {
+        const float oun = pow2f(-14 - a.tc_eV);
+        if (a.splits == 1) {
+            const float inv = ok ? 1.0f / lrow[orow] : 0.f;
+            float *dst = a.out + (size_t)r * a.ldo + h * HD + ocol;
+#pragma unroll
+            for (int k = 0; k < 64; k++) dst[k] = o[k] * oun * inv;
+        } else {
+            float *dst = a.part_acc + ((size_t)split * a.R + r) * d + h * HD + ocol;
+#pragma unroll
+            for (int k = 0; k < 64; k++) dst[k] = ok ? o[k] * oun : 0.f;
+            if (ocol == 0) {
+                float *ms = a.part_ms + (((size_t)split * a.R + r) * H + h) * 2;
+                ms[0] = ok ? mrow[orow] : -FLT_MAX, ms[1] = ok ? lrow[orow] : 0.f;
+            }
         }
-    } else if (warp < 4 && a.splits > 1 && r0 + tid < a.R) {
-        // a split with no tiles (or one that gave up) contributes nothing
-        float *ms = a.part_ms + (((size_t)split * a.R + r0 + tid) * H + h) * 2;
-        ms[0] = -FLT_MAX, ms[1] = 0.f;
-        float *dst = a.part_acc + ((size_t)split * a.R + r0 + tid) * d + h * HD;
-        for (int k = 0; k < HD; k++) dst[k] = 0.f;
     }
     if (*abort_flag && tid == 0 && a.err) atomicExch(a.err, 1);
     fence_before_sync();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, 256);
+    if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 size_t attend_tc_smem() {
-    return sizeof(__half) * (2 * 128 * 128 + 2 * 64 * 128 + 2 * 128 * 64 + 2 * 128 * 64) + 64 + sizeof(float) * 128 + 64;
+    return sizeof(__half) * (2 * 128 * 128 + 2 * 64 * 128 + 2 * 128 * 64 + 2 * 128 * 64) + 64 + sizeof(float) * 4 * 128 + 64;
 }
 
 cudaError_t launch_attend_tc(int kv, const AttnArgs &a, cudaStream_t s, uint64_t *launches) {

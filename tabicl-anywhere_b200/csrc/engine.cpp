@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <algorithm>
+#include <array>
 #include <atomic>
 #include <cstring>
 #include <map>
@@ -81,10 +82,17 @@ struct tcu_ctx {
     unsigned *dev_scan = nullptr; // scratch of the per-layer magnitude scan
 };
 
+// A weight matrix [N][K] split once for the tensor cores: f16 hi + lo (bit patterns) of W * 2^e(n), and 2^-e(n).
+struct SplitW {
+    const uint16_t *hi = nullptr, *lo = nullptr;
+    const float *unscale = nullptr;
+};
+
 // Device pointers of one in-context block (src/model.rs:27-98), plus what fitting adds.
 struct LayerPtrs {
     const float *n1w, *n1b, *wq, *bq, *q0w, *q0b, *q2w, *q2b, *wo, *bo, *n2w, *n2b, *w1, *b1, *w2, *b2;
     const float *wkv, *bkv;  // fit only: in_proj rows d..3d
+    SplitW tq, to, t1, t2, tkv;
 };
 
 struct tcu_weights {
@@ -93,9 +101,10 @@ struct tcu_weights {
     tcu_icl_shape shape{};
     bool for_fit = false;
     std::map<std::string, std::vector<float>> host;  // as put, widened to f32
-    DevBuf dev;
+    DevBuf dev, dev16;
     std::vector<LayerPtrs> layer;
     const float *lnw = nullptr, *lnb = nullptr, *dec0w = nullptr, *dec0b = nullptr, *dec2w = nullptr, *dec2b = nullptr;
+    SplitW tdec0, tdec2;
     const float *icl_y = nullptr;  // fit: class table (model.rs:163-177)
     bool ready = false;
     // fit-time query scale pieces (the base MLP of the scalable softmax), kept on the host: nn.rs:97-107
@@ -356,10 +365,55 @@ static int weights_ready(tcu_weights *w) {
         }
         i_y = add(t);
     }
+    // tensor-core copies of the linear layers' weights: f16 hi + lo per row, scaled to stay inside f16
+    std::vector<uint16_t> half;
+    struct SplitIdx {
+        size_t hi, lo, unscale;
+    };
+    auto split = [&](const float *src_in, int N, int K) {
+        const std::vector<float> src_copy(src_in, src_in + (size_t)N * K);  // add() below may move `flat`
+        const float *src = src_copy.data();
+        SplitIdx ix;
+        ix.hi = (half.size() + 127) / 128 * 128;
+        ix.lo = ix.hi + (size_t)N * K;
+        half.resize(ix.lo + (size_t)N * K);
+        std::vector<float> un(N);
+        for (int n = 0; n < N; n++) {
+            const float *row = src + (size_t)n * K;
+            float mx = 0.f;
+            for (int k = 0; k < K; k++) mx = std::max(mx, std::fabs(row[k]));
+            const int e = tc_exponent(mx);
+            const float sc = std::ldexp(1.0f, e);
+            un[n] = std::ldexp(1.0f, -e);
+            for (int k = 0; k < K; k++) {
+                const float x = row[k] * sc;  // exact: a power of two
+                const uint16_t h = f32_to_f16(x);
+                half[ix.hi + (size_t)n * K + k] = h;
+                half[ix.lo + (size_t)n * K + k] = f32_to_f16(x - f16_to_f32(h));
+            }
+        }
+        ix.unscale = add(un);
+        return ix;
+    };
+    std::vector<std::array<SplitIdx, 5>> lsplit(L);
+    for (int l = 0; l < L; l++) {
+        const LIdx &x = li[l];
+        lsplit[l][0] = split(flat.data() + offs[x.wq], d, d);
+        lsplit[l][1] = split(flat.data() + offs[x.wo], d, d);
+        lsplit[l][2] = split(flat.data() + offs[x.w1], ff, d);
+        lsplit[l][3] = split(flat.data() + offs[x.w2], d, ff);
+        if (w->for_fit) lsplit[l][4] = split(flat.data() + offs[x.wkv], 2 * d, d);
+    }
+    const SplitIdx s_dec0 = split(flat.data() + offs[i_d0w], dff, d);
+    const SplitIdx s_dec2 = split(flat.data() + offs[i_d2w], outs, dff);
     w->dev.ensure(flat.size() * sizeof(float));
     CU(cudaMemcpy(w->dev.p, flat.data(), flat.size() * sizeof(float), cudaMemcpyHostToDevice));
+    w->dev16.ensure(half.size() * sizeof(uint16_t));
+    CU(cudaMemcpy(w->dev16.p, half.data(), half.size() * sizeof(uint16_t), cudaMemcpyHostToDevice));
     const float *base = w->dev.as<float>();
+    const uint16_t *hbase = w->dev16.as<uint16_t>();
     auto P = [&](size_t idx) { return base + offs[idx]; };
+    auto S = [&](const SplitIdx &ix) { return SplitW{hbase + ix.hi, hbase + ix.lo, base + offs[ix.unscale]}; };
     w->layer.resize(L);
     for (int l = 0; l < L; l++) {
         const LIdx &x = li[l];
@@ -367,8 +421,11 @@ static int weights_ready(tcu_weights *w) {
         p = LayerPtrs{P(x.n1w), P(x.n1b), P(x.wq), P(x.bq), P(x.q0w), P(x.q0b), P(x.q2w), P(x.q2b), P(x.wo), P(x.bo),
                       P(x.n2w), P(x.n2b), P(x.w1), P(x.b1), P(x.w2), P(x.b2), nullptr, nullptr};
         if (w->for_fit) p.wkv = P(x.wkv), p.bkv = P(x.bkv);
+        p.tq = S(lsplit[l][0]), p.to = S(lsplit[l][1]), p.t1 = S(lsplit[l][2]), p.t2 = S(lsplit[l][3]);
+        if (w->for_fit) p.tkv = S(lsplit[l][4]);
     }
     w->lnw = P(i_lnw), w->lnb = P(i_lnb), w->dec0w = P(i_d0w), w->dec0b = P(i_d0b), w->dec2w = P(i_d2w), w->dec2b = P(i_d2b);
+    w->tdec0 = S(s_dec0), w->tdec2 = S(s_dec2);
     w->icl_y = w->for_fit ? P(i_y) : nullptr;
     w->host.clear();
     w->ready = true;
@@ -489,7 +546,7 @@ static void ensure_work(tcu_model *m, int R) {
     moved |= m->q.ensure(sizeof(float) * R * d);
     moved |= m->att.ensure(sizeof(float) * R * d);
     moved |= m->mid.ensure(sizeof(float) * R * wide);
-    moved |= m->stats.ensure(sizeof(float) * R * 2);
+    moved |= m->stats.ensure(sizeof(float) * R * 4);
     const Plan plan = attend_plan(m->w->ctx, R, s.heads, s.d / s.heads, m->nitems, m->ntiles);
     const size_t pr = plan.path == Path::Decode ? (size_t)m->nitems : (plan.splits > 1 ? (size_t)plan.splits : 0);
     if (pr) {
@@ -554,10 +611,12 @@ static void attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int r
 }
 
 static void linear(tcu_ctx *ctx, tcu_model *m, const float *x, int ldx, int R, int K, const float *lnw, const float *lnb,
-                   const float *W, const float *b, int N, float *y, int ldy, int act, int accumulate, cudaStream_t s) {
+                   const float *W, const float *b, int N, float *y, int ldy, int act, int accumulate, cudaStream_t s,
+                   const SplitW &tw = SplitW(), int transpose_out = 0) {
     LinArgs a;
     a.x = x, a.ldx = ldx, a.M = R, a.K = K, a.lnw = lnw, a.lnb = lnb, a.W = W, a.bias = b, a.N = N, a.y = y, a.ldy = ldy;
-    a.act = act, a.accumulate = accumulate;
+    a.act = act, a.accumulate = accumulate, a.transpose_out = transpose_out;
+    a.tc_whi = tw.hi, a.tc_wlo = tw.lo, a.tc_wunscale = tw.unscale, a.err = ctx->dev_err;
     Launch{ctx, s}(launch_linear(a, m->stats.as<float>(), s, &ctx->launches), "linear");
 }
 
@@ -598,7 +657,7 @@ static void query_rows(tcu_ctx *ctx, tcu_model *m, int l, const float *scale, co
     const auto &sh = m->w->shape;
     const LayerPtrs &p = m->w->layer[l];
     const int d = sh.d;
-    linear(ctx, m, h, d, R, d, p.n1w, p.n1b, p.wq, p.bq, d, q, d, 0, 0, s);  // nn.rs:136-137
+    linear(ctx, m, h, d, R, d, p.n1w, p.n1b, p.wq, p.bq, d, q, d, 0, 0, s, p.tq);  // nn.rs:136-137
     Launch{ctx, s}(launch_ssmax(q, R, d, sh.heads, sh.hid, p.q0w, p.q0b, p.q2w, p.q2b, scale, s, &ctx->launches), "ssmax");
 }
 
@@ -606,9 +665,9 @@ static void block_tail(tcu_ctx *ctx, tcu_model *m, int l, float *h, const float 
     const auto &sh = m->w->shape;
     const LayerPtrs &p = m->w->layer[l];
     const int d = sh.d, ff = sh.ff;
-    linear(ctx, m, att, d, R, d, nullptr, nullptr, p.wo, p.bo, d, h, d, 0, 1, s);                    // predict.rs:542-551
-    linear(ctx, m, h, d, R, d, p.n2w, p.n2b, p.w1, p.b1, ff, m->mid.as<float>(), ff, 1, 0, s);      // predict.rs:552-559
-    linear(ctx, m, m->mid.as<float>(), ff, R, ff, nullptr, nullptr, p.w2, p.b2, d, h, d, 0, 1, s);   // predict.rs:560-568
+    linear(ctx, m, att, d, R, d, nullptr, nullptr, p.wo, p.bo, d, h, d, 0, 1, s, p.to);                    // predict.rs:542-551
+    linear(ctx, m, h, d, R, d, p.n2w, p.n2b, p.w1, p.b1, ff, m->mid.as<float>(), ff, 1, 0, s, p.t1);      // predict.rs:552-559
+    linear(ctx, m, m->mid.as<float>(), ff, R, ff, nullptr, nullptr, p.w2, p.b2, d, h, d, 0, 1, s, p.t2);   // predict.rs:560-568
 }
 
 static void stage(tcu_ctx *ctx, tcu_model *m, float *h, int R, int out_n, float *out, cudaStream_t s) {
@@ -625,8 +684,9 @@ static void stage(tcu_ctx *ctx, tcu_model *m, float *h, int R, int out_n, float 
         block_tail(ctx, m, l, h, m->att.as<float>(), R, s);
     }
     // predict.rs:570-584 decoder: only the first out_n outputs are computed (each output is its own row)
-    linear(ctx, m, h, d, R, d, m->w->lnw, m->w->lnb, m->w->dec0w, m->w->dec0b, dff, m->mid.as<float>(), dff, 1, 0, s);
-    linear(ctx, m, m->mid.as<float>(), dff, R, dff, nullptr, nullptr, m->w->dec2w, m->w->dec2b, out_n, out, out_n, 0, 0, s);
+    linear(ctx, m, h, d, R, d, m->w->lnw, m->w->lnb, m->w->dec0w, m->w->dec0b, dff, m->mid.as<float>(), dff, 1, 0, s, m->w->tdec0);
+    linear(ctx, m, m->mid.as<float>(), dff, R, dff, nullptr, nullptr, m->w->dec2w, m->w->dec2b, out_n, out, out_n, 0, 0, s,
+           m->w->tdec2);
 }
 
 // The stage on the model's own buffers (m->h in, m->out out), replayed from a CUDA graph captured on the context
@@ -698,8 +758,7 @@ static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, in
     const int d = sh.d, L = sh.layers;
     cudaStream_t s = ctx->stream;
     ensure_work(m.get(), rows);
-    DevBuf lnh, kvT, kvf, items32, tiles64;
-    lnh.ensure(sizeof(float) * (size_t)rows * d);
+    DevBuf kvT, kvf;
     kvT.ensure(sizeof(float) * (size_t)rows * 2 * d);
     kvf.ensure(layer_bytes_of(0, d, rows, chunk));
     Launch ck{ctx, s};
@@ -711,12 +770,8 @@ static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, in
         auto sc = query_scale(w, l, rows);
         std::memcpy(scales.data() + (size_t)l * d, sc.data(), sizeof(float) * d);
         CU(cudaMemcpyAsync(m->scales.as<float>() + (size_t)l * d, sc.data(), sizeof(float) * d, cudaMemcpyHostToDevice, s));
-        ck(launch_ln_apply(h, rows, d, p.n1w, p.n1b, lnh.as<float>(), s, &ctx->launches), "norm1");
-        // keys and values, coordinate-major: kvT[j][r] = Wkv[j] . LN(h_r) + bkv[j]
-        LinArgs a;
-        a.x = p.wkv, a.ldx = d, a.M = 2 * d, a.K = d, a.W = lnh.as<float>(), a.N = rows, a.bias = p.bkv, a.bias_on_m = 1;
-        a.y = kvT.as<float>(), a.ldy = rows;
-        ck(launch_linear(a, m->stats.as<float>(), s, &ctx->launches), "key/value projection");
+        // keys and values, coordinate-major: kvT[j][r] = Wkv[j] . LN1(h_r) + bkv[j] (fit.rs:633-647)
+        linear(ctx, m.get(), h, d, rows, d, p.n1w, p.n1b, p.wkv, p.bkv, 2 * d, kvT.as<float>(), rows, 0, 0, s, p.tkv, 1);
         ck(launch_pack(kvT.as<float>(), rows, d, rows, chunk, kv, m->layers.as<uint8_t>() + m->layer_stride * l, s, &ctx->launches), "pack");
         m->have_layer[l] = true;
         if (l + 1 == L) break;  // fit.rs:664-666

@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(128) k_gemv(LinArgs a) {
                 if (r < R) {
                     float v = acc[r] + b;
                     if (a.act) v = gelu1(v);
-                    float *dst = a.y + (size_t)r * a.ldy + o;
+                    float *dst = a.transpose_out ? a.y + (size_t)o * a.ldy + r : a.y + (size_t)r * a.ldy + o;
                     *dst = a.accumulate ? *dst + v : v;
                 }
             }
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(256, 2) k_gemm(LinArgs a) {
             if (n >= a.N) continue;
             float v = acc[i][j] + (a.bias ? a.bias[a.bias_on_m ? m : n] : 0.f);
             if (a.act) v = gelu1(v);
-            float *dst = a.y + (size_t)m * a.ldy + n;
+            float *dst = a.transpose_out ? a.y + (size_t)n * a.ldy + m : a.y + (size_t)m * a.ldy + n;
             *dst = a.accumulate ? *dst + v : v;
         }
     }
@@ -891,6 +891,8 @@ cudaError_t launch_linear(const LinArgs &a, float *stats_scratch, cudaStream_t s
         TCU_LAUNCHED(launches);
         return cudaGetLastError();
     }
+    if (a.tc_whi && !a.bias_on_m && a.K % 64 == 0 && gemm_tc_enabled())
+        return launch_gemm_tc(a, reinterpret_cast<float4 *>(stats_scratch), s, launches);
     LinArgs b = a;
     if (a.lnw) {
         k_ln_stats<<<(a.M + 7) / 8, 256, 0, s>>>(a.x, a.ldx, a.M, a.K, stats_scratch);

@@ -20,6 +20,11 @@ struct LinArgs {
     int act = 0;         // 1: GELU (kern.rs:285-290)
     int accumulate = 0;  // 1: y += result (residual)
     int bias_on_m = 0;   // bias indexed by the row of y (used when y is a transposed product)
+    int transpose_out = 0;  // write y[n][m] (row stride ldy) instead of y[m][n]
+    // tensor-core path: W split once into f16 hi + lo (bit patterns), scaled per output row by 1 / unscale[n]
+    const uint16_t *tc_whi = nullptr, *tc_wlo = nullptr;
+    const float *tc_wunscale = nullptr;
+    int *err = nullptr;  // set to 1 when a kernel gave up waiting
 };
 
 // Attention of scaled queries against one layer's stored chunks (fit.rs:6-11 layout, read in place).
@@ -58,7 +63,12 @@ int decode_keys_per_item(int kv);
 constexpr int FLASH_KEYS = 64;  // keys per flash tile
 constexpr int FLASH_ROWS = 64;  // query rows per flash block
 
+// stats_scratch: 4 floats per row
 cudaError_t launch_linear(const LinArgs &a, float *stats_scratch, cudaStream_t s, uint64_t *launches);
+// the tensor-core path of launch_linear (M > 8, K a multiple of 64, split weights given)
+cudaError_t launch_gemm_tc(const LinArgs &a, float4 *stats, cudaStream_t s, uint64_t *launches);
+size_t gemm_tc_smem();
+bool gemm_tc_enabled();
 cudaError_t launch_ln_apply(const float *x, int M, int K, const float *w, const float *b, float *y, cudaStream_t s,
                             uint64_t *launches);
 cudaError_t launch_ssmax(float *q, int R, int d, int heads, int hid, const float *q0w, const float *q0b,
