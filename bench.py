@@ -59,6 +59,19 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def ncu_traffic(a):
+    """DRAM bytes (read + write) of one attention launch, from the committed ncu capture of this workload
+    (profiles/ncu_traffic.json); None for any other workload."""
+    if (a.rows, a.kv, a.train_rows) != (2048, 1, 10000):
+        return None
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            t = json.load(f)["attention pass, config 2, 2048 rows, i16, 10000 keys"]
+        return t["dram_bytes_read"] + t["dram_bytes_write"]
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def workload(a):
     return {
         "workload": f"BASELINE config 2: full-size TabICL v2 in-context stage (12 layers, d 512, 4 heads), "
@@ -304,6 +317,7 @@ def main():
     pct = lambda p: lat[min(len(lat) - 1, int(p * len(lat)))]
 
     hbm, bf16, kind = peaks()
+    traffic = ncu_traffic(a)
     layer_bytes = pkg.record(a.kv, d, CHUNK) * (a.train_rows // CHUNK) + (pkg.record(a.kv, d, a.train_rows % CHUNK) if a.train_rows % CHUNK else 0)
     flops_per_pass = 4.0 * a.train_rows * d * R  # QK^T and PV, 2 flops per multiply-add
     per_pass_s = attn_ms / max(attn_passes, 1) / 1e3
@@ -319,7 +333,7 @@ def main():
         "e2e": {"value": e2e, "unit": "rows/s", "h2d_bytes_per_step": R * d * 4, "d2h_bytes_per_step": R * classes * 4},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "achieved": achieved_tf, "peak": bf16, "unit": "TFLOP/s",
-                     "frac": achieved_tf / bf16, "traffic": None, "peak_kind": kind,
+                     "frac": achieved_tf / bf16, "traffic": traffic, "peak_kind": kind,
                      "kernel": "attention pass (one layer, all rows)", "per_launch_ms": per_pass_s * 1e3,
                      "algorithmic_flops_per_launch": flops_per_pass},
         "latency_1row": {"p50_us": pct(0.5), "p10_us": pct(0.1), "p90_us": pct(0.9), "reps": len(lat),
