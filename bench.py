@@ -322,8 +322,15 @@ def main():
     flops_per_pass = 4.0 * a.train_rows * d * R  # QK^T and PV, 2 flops per multiply-add
     per_pass_s = attn_ms / max(attn_passes, 1) / 1e3
     achieved_tf = flops_per_pass / per_pass_s / 1e12
+    # 1-row calls: the one-kernel stage records one timed pass per call (all layers, cache and weights); the
+    # multi-kernel path records one per layer's attention
+    one_kernel = lat_passes <= a.latency_reps
     lat_pass_s = lat_attn_ms / max(lat_passes, 1) / 1e3
-    lat_gbs = layer_bytes / lat_pass_s / 1e9
+    L, ff, dff, hd = shape["layers"], shape["ff"], shape["dec_ff"], d // shape["heads"]
+    weight_bytes = 4 * (L * (2 * d * d + 2 * d * ff + 2 * 64 * hd + 64 + hd + 7 * d + ff)
+                        + 2 * d + dff * d + dff + classes * dff + classes)
+    lat_bytes = L * layer_bytes + weight_bytes if one_kernel else layer_bytes
+    lat_gbs = lat_bytes / lat_pass_s / 1e9
 
     line = {
         "metric": "predicted rows/sec (in-context stage, config 2)", "value": value, "unit": "rows/s",
@@ -339,8 +346,11 @@ def main():
         "latency_1row": {"p50_us": pct(0.5), "p10_us": pct(0.1), "p90_us": pct(0.9), "reps": len(lat),
                          "roofline": {"bound": "hbm", "achieved": lat_gbs, "peak": hbm, "unit": "GB/s",
                                       "frac": lat_gbs / hbm, "peak_kind": kind,
-                                      "kernel": "decode attention pass (one layer, one row)",
-                                      "per_launch_us": lat_pass_s * 1e6, "algorithmic_bytes_per_launch": layer_bytes}},
+                                      "kernel": ("one-kernel stage (all layers and the decoder, one row)" if one_kernel
+                                                 else "decode attention pass (one layer, one row)"),
+                                      "per_launch_us": lat_pass_s * 1e6, "algorithmic_bytes_per_launch": lat_bytes,
+                                      "cache_bytes": L * layer_bytes, "weight_bytes": weight_bytes,
+                                      "p50_gbs": (L * layer_bytes + weight_bytes) / (pct(0.5) * 1e-6) / 1e9}},
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

@@ -70,6 +70,8 @@ struct tcu_ctx {
     std::atomic<int> refs{1};  // the caller's handle plus one per live weights object
     int device = 0;
     int sms = 148;
+    int coop = 0;          // cooperative launches supported
+    size_t smem_optin = 0; // dynamic shared memory a CTA may opt in to
     cudaStream_t stream = nullptr;
     std::string err;
     std::recursive_mutex mu;
@@ -124,6 +126,16 @@ struct tcu_model {
     bool tc_scanned = false;
     // working memory, grown to the largest call so far
     DevBuf h, q, att, mid, stats, out, part_ms, part_acc;
+    // the one-kernel few-row stage: key tiles (head-major), per-layer pointer table, barrier words, partials
+    DevBuf rtiles, rlayers, rsync, rparts_ms, rparts_acc;
+    int rtiles_n = 0, rtiles_per_head = 0;
+    bool rows_built = false;
+    struct RowsPlan {
+        bool done = false;
+        int grid = 0, slots = 0;
+        size_t smem = 0;
+        int part_lo[ROWS_MAX_HEADS] = {}, part_hi[ROWS_MAX_HEADS] = {};
+    } rows_plans[2];  // one row, 2..8 rows
     // the stage captured as CUDA graphs, one per (rows, outputs, profiling), over the buffers above
     struct Graph {
         int R, out_n;
@@ -689,6 +701,125 @@ static void stage(tcu_ctx *ctx, tcu_model *m, float *h, int R, int out_n, float 
            m->w->tdec2);
 }
 
+// ---- the few-row stage as one kernel -------------------------------------------------------------------------
+
+static bool rows_kernel_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("TCU_ROWS_KERNEL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// Key tiles (head-major), the per-layer pointer table and the barrier words, once per model.
+static void rows_build(tcu_model *m) {
+    if (m->rows_built) return;
+    const auto &sh = m->w->shape;
+    const int tk = rows_tile_keys(m->kv), w = m->kv == 0 ? 4 : (m->kv == 1 ? 2 : 1);
+    std::vector<int4> tiles;
+    for (int h = 0; h < sh.heads; h++) {
+        for (int ci = 0, r0 = 0; r0 < m->rows; ci++, r0 += m->chunk) {
+            const int rc = std::min(m->chunk, m->rows - r0);
+            // a coordinate's keys start 16-byte aligned in every chunk of this size: bulk copies
+            const int aligned = (rc * w) % 16 == 0 ? 1 : 0;
+            for (int k0 = 0; k0 < rc; k0 += tk) tiles.push_back(make_int4(ci, k0, std::min(tk, rc - k0), h | aligned << 16));
+        }
+    }
+    m->rtiles_n = (int)tiles.size();
+    m->rtiles_per_head = m->rtiles_n / sh.heads;
+    m->rtiles.ensure(tiles.size() * sizeof(int4));
+    CU(cudaMemcpy(m->rtiles.p, tiles.data(), tiles.size() * sizeof(int4), cudaMemcpyHostToDevice));
+    std::vector<RowsLayer> layers(sh.layers);
+    const float *scales = m->scales.as<float>();
+    for (int l = 0; l < sh.layers; l++) {
+        const LayerPtrs &p = m->w->layer[l];
+        layers[l] = RowsLayer{p.n1w, p.n1b, p.wq, p.bq, p.q0w, p.q0b, p.q2w, p.q2b, p.wo, p.bo, p.n2w, p.n2b,
+                              p.w1, p.b1, p.w2, p.b2, layer_ptr(m, l), scales + (size_t)l * sh.d};
+    }
+    m->rlayers.ensure(layers.size() * sizeof(RowsLayer));
+    CU(cudaMemcpy(m->rlayers.p, layers.data(), layers.size() * sizeof(RowsLayer), cudaMemcpyHostToDevice));
+    m->rsync.ensure(256);
+    CU(cudaMemset(m->rsync.p, 0, 256));
+    m->rows_built = true;
+}
+
+// Whether R rows take the one-kernel stage, and its launch shape: one CTA per SM (at most one per key tile), as
+// many tiles of shared memory as fit.
+static const tcu_model::RowsPlan *rows_plan(tcu_ctx *ctx, tcu_model *m, int R) {
+    const auto &sh = m->w->shape;
+    const int hd = sh.d / sh.heads;
+    if (!rows_kernel_enabled() || !ctx->coop || R < 1 || R > 8) return nullptr;
+    if ((hd != 64 && hd != 128) || sh.hid != 64 || sh.heads > ROWS_MAX_HEADS) return nullptr;
+    for (int k : {sh.d, sh.ff, sh.dec_ff})
+        if (k % 128 || k > 1024) return nullptr;
+    auto &p = m->rows_plans[R > 1 ? 1 : 0];
+    if (!p.done) {
+        p.done = true;
+        rows_build(m);
+        const int want = std::min({ctx->sms, m->rtiles_n, ROWS_MAX_GRID});
+        for (int slots = rows_slots_for(m->kv, hd, R, ctx->smem_optin); slots >= 2; slots--) {
+            const size_t smem = rows_smem(m->kv, hd, R, slots);
+            if (rows_max_grid(m->kv, hd, R, smem, ctx->sms) >= want) {
+                p.grid = want, p.slots = slots, p.smem = smem;
+                break;
+            }
+        }
+        if (p.grid) {
+            // the CTAs holding each head's tiles: CTA c holds tiles [T c / G, T (c + 1) / G)
+            const long long T = m->rtiles_n, G = p.grid;
+            for (int h = 0; h < sh.heads; h++) {
+                const long long first = (long long)h * m->rtiles_per_head, last = first + m->rtiles_per_head - 1;
+                int lo = -1, hi = -1;
+                for (int c = 0; c < p.grid; c++) {
+                    const long long t0 = T * c / G, t1 = T * (c + 1) / G;
+                    if (t0 <= first && first < t1) lo = c;
+                    if (t0 <= last && last < t1) hi = c;
+                }
+                p.part_lo[h] = lo, p.part_hi[h] = hi;
+            }
+        }
+    }
+    return p.grid ? &p : nullptr;
+}
+
+// The stage of R rows (m->h in, m->out out) as one cooperative launch.
+static void stage_rows(tcu_ctx *ctx, tcu_model *m, const tcu_model::RowsPlan &p, int R, int out_n, cudaStream_t s) {
+    const auto &sh = m->w->shape;
+    const int hd = sh.d / sh.heads;
+    ensure_work(m, R);
+    m->rparts_ms.ensure(sizeof(float) * (size_t)p.grid * sh.heads * 8 * 2);
+    m->rparts_acc.ensure(sizeof(float) * (size_t)p.grid * sh.heads * 8 * hd);
+    RowsArgs a;
+    a.layers = m->rlayers.as<RowsLayer>();
+    a.L = sh.layers, a.d = sh.d, a.heads = sh.heads, a.ff = sh.ff, a.dff = sh.dec_ff, a.out_n = out_n, a.R = R;
+    a.lnw = m->w->lnw, a.lnb = m->w->lnb, a.dec0w = m->w->dec0w, a.dec0b = m->w->dec0b;
+    a.dec2w = m->w->dec2w, a.dec2b = m->w->dec2b;
+    a.rows = m->rows, a.chunk = m->chunk, a.full = m->full;
+    a.tiles = m->rtiles.as<int4>(), a.ntiles = m->rtiles_n, a.tiles_per_head = m->rtiles_per_head, a.slots = p.slots;
+    a.h = m->h.as<float>(), a.q = m->q.as<float>(), a.att = m->att.as<float>(), a.mid = m->mid.as<float>();
+    a.out = m->out.as<float>();
+    a.part_ms = m->rparts_ms.as<float>(), a.part_acc = m->rparts_acc.as<float>();
+    a.bar = m->rsync.as<unsigned>(), a.head_cnt = m->rsync.as<int>() + 32, a.err = ctx->dev_err;
+    for (int h = 0; h < sh.heads; h++) a.part_lo[h] = p.part_lo[h], a.part_hi[h] = p.part_hi[h];
+    // a launch that gave up leaves the barrier word dirty: every launch starts from zeros
+    CU(cudaMemsetAsync(m->rsync.p, 0, 256, s));
+    cudaEvent_t ev_end = nullptr;
+    if (ctx->prof) {
+        if (ctx->prof_used + 2 > ctx->prof_events.size()) {
+            for (int i = 0; i < 64; i++) {
+                cudaEvent_t e;
+                CU(cudaEventCreate(&e));
+                ctx->prof_events.push_back(e);
+            }
+        }
+        CU(cudaEventRecord(ctx->prof_events[ctx->prof_used], s));
+        ev_end = ctx->prof_events[ctx->prof_used + 1];
+        ctx->prof_used += 2;
+    }
+    Launch{ctx, s}(launch_stage_rows(m->kv, hd, a, p.grid, p.smem, s, &ctx->launches), "stage (one kernel)");
+    if (ev_end) CU(cudaEventRecord(ev_end, s));
+}
+
 // The stage on the model's own buffers (m->h in, m->out out), replayed from a CUDA graph captured on the context
 // stream the first time a (rows, outputs, profiling) combination is seen. TCU_GRAPHS=0 runs it eagerly.
 static void stage_replay(tcu_ctx *ctx, tcu_model *m, int R, int out_n, cudaStream_t s) {
@@ -696,9 +827,13 @@ static void stage_replay(tcu_ctx *ctx, tcu_model *m, int R, int out_n, cudaStrea
         const char *e = getenv("TCU_GRAPHS");
         return !(e && e[0] == '0');
     }();
+    if (m->out.ensure(sizeof(float) * (size_t)R * out_n)) drop_graphs(m);
+    if (const auto *p = rows_plan(ctx, m, R)) {
+        stage_rows(ctx, m, *p, R, out_n, s);
+        return;
+    }
     scan_model(ctx, m, ctx->stream);  // once per model, before any capture
     ensure_work(m, R);
-    if (m->out.ensure(sizeof(float) * (size_t)R * out_n)) drop_graphs(m);
     if (!use_graphs) {
         stage(ctx, m, m->h.as<float>(), R, out_n, m->out.as<float>(), s);
         return;
@@ -805,6 +940,10 @@ int tcu_open(int device, tcu_ctx **out) {
     ctx->device = device;
     int r = guarded(ctx.get(), [&]() -> int {
         CU(cudaDeviceGetAttribute(&ctx->sms, cudaDevAttrMultiProcessorCount, device));
+        CU(cudaDeviceGetAttribute(&ctx->coop, cudaDevAttrCooperativeLaunch, device));
+        int optin = 0;
+        CU(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+        ctx->smem_optin = (size_t)optin;
         CU(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
         CU(cudaMalloc(&ctx->dev_err, sizeof(int)));
         CU(cudaMemset(ctx->dev_err, 0, sizeof(int)));

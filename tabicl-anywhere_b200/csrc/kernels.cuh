@@ -46,6 +46,45 @@ struct AttnArgs {
     int *err = nullptr;            // set to 1 when a kernel gave up waiting
 };
 
+// The few-row stage in one persistent kernel: per layer, the pointers it reads.
+struct RowsLayer {
+    const float *n1w, *n1b, *wq, *bq, *q0w, *q0b, *q2w, *q2b, *wo, *bo, *n2w, *n2b, *w1, *b1, *w2, *b2;
+    const uint8_t *cache;  // the layer's stored chunks (fit.rs:6-11 layout)
+    const float *scale;    // [d] fit-time query scale of the layer (nn.rs:97-107)
+};
+
+constexpr int ROWS_MAX_HEADS = 16;
+constexpr int ROWS_MAX_GRID = 160;
+
+struct RowsArgs {
+    const RowsLayer *layers = nullptr;  // [L], device memory
+    int L = 0, d = 0, heads = 0, ff = 0, dff = 0, out_n = 0, R = 0;
+    const float *lnw = nullptr, *lnb = nullptr, *dec0w = nullptr, *dec0b = nullptr, *dec2w = nullptr, *dec2b = nullptr;
+    int rows = 0, chunk = 0;
+    size_t full = 0;                    // bytes of a full chunk record
+    // key tiles, head-major: (chunk, first key, keys, head | 1 << 16 when its rows can be bulk-copied)
+    const int4 *tiles = nullptr;
+    int ntiles = 0, tiles_per_head = 0;
+    int slots = 0;                      // tiles of shared memory per CTA
+    float *h = nullptr, *q = nullptr, *att = nullptr, *mid = nullptr, *out = nullptr;
+    float *part_ms = nullptr, *part_acc = nullptr;  // [grid][heads][R] (max, weight sum) and [..][head width]
+    unsigned *bar = nullptr;            // grid barrier word (zero low bits between launches)
+    int *head_cnt = nullptr;            // [heads] arrivals of the CTAs holding each head's tiles
+    int *err = nullptr;                 // set to 1 when a wait gave up
+    int part_lo[ROWS_MAX_HEADS] = {}, part_hi[ROWS_MAX_HEADS] = {};  // CTAs holding each head's tiles
+};
+
+// Keys per tile of the one-kernel stage for a stored format (f32 32, i16 64, i8 64).
+int rows_tile_keys(int kv);
+// Shared memory of the one-kernel stage for R rows with `slots` tiles; slots_for gives the most that fit.
+size_t rows_smem(int kv, int hd, int R, int slots);
+int rows_slots_for(int kv, int hd, int R, size_t smem_max);
+// Largest co-resident grid for that shared memory (0: not launchable).
+int rows_max_grid(int kv, int hd, int R, size_t smem, int sms);
+// Cooperative launch of the one-kernel stage (grid CTAs, all resident at once).
+cudaError_t launch_stage_rows(int kv, int hd, const RowsArgs &a, int grid, size_t smem, cudaStream_t s,
+                              uint64_t *launches);
+
 #ifdef __CUDACC__
 #define TCU_HD __host__ __device__
 #else

@@ -1,0 +1,782 @@
+// The in-context stage (src/predict.rs:381-586) for up to 8 query rows as ONE persistent kernel: one CTA per SM,
+// all resident (cooperative launch), the phases of each layer separated by grid barriers.
+//
+//   A  q = Wq LN1(h) + bq                   (nn.rs:130-137; outputs spread over the CTAs)
+//   B  per head: the query MLP of the scalable softmax (nn.rs:138-149), then attention over this CTA's share
+//      of the key tiles with the online softmax (nn.rs:187-258); the last CTA of a head merges the head's
+//      partial states (nn.rs:261-286) into att
+//   D  h += Wo att + bo                     (predict.rs:542-551)
+//   E  mid = GELU(W1 LN2(h) + b1)           (predict.rs:552-559)
+//   F  h += W2 mid + b2                     (predict.rs:560-568)
+//   then the decoder (predict.rs:570-584).
+//
+// Few rows are latency-bound: each phase is a few microseconds of dependent work. What the kernel overlaps is the
+// cache stream. Every CTA owns a fixed share of each layer's key tiles and keeps a ring of them in shared memory,
+// filled by asynchronous 16-byte copies (cp.async, one commit group per tile, so a tile is ready once the groups
+// committed after it are few enough). A slot is refilled with the next tile of the CTA's sequence as soon as it has
+// been used, so the next layer's keys and values arrive while phases D, E, F and A of this layer run. Loads that do
+// not depend on a barrier (weight rows, biases, LayerNorm and query-MLP weights) are issued before it. Every grid
+// barrier is bounded: one that does not complete within about a second sets the error flag, and every CTA then
+// leaves at its next barrier.
+#include "kernels.cuh"
+#include "device.cuh"
+#include "tc.cuh"
+
+#include <algorithm>
+#include <cfloat>
+#include <mutex>
+
+namespace tcu {
+
+namespace {
+
+constexpr int THREADS = 256, WARPS = 8;
+constexpr int HID = 64;                       // hidden width of the query MLP (nn.rs:124)
+constexpr int KMAX = 1024;                    // widest input of a linear phase
+constexpr long long SPIN_LIMIT = 2000000000;  // cycles, about a second
+
+template <int KV, int HD, int RM>
+struct Cfg {
+    static constexpr int W = KvFmt<KV>::W;
+    static constexpr int VB = KV == 2 ? 8 : 16;  // bytes of a coordinate's row a lane reads
+    static constexpr int EPV = VB / W;            // keys per lane vector: 4, 8, 8
+    static constexpr int TK = 8 * EPV;            // keys per tile: 32, 64, 64
+    static constexpr int ROWB = TK * W;           // bytes of one coordinate's keys in a tile: 128, 128, 64
+    static constexpr int CPR = ROWB / 16;         // 16-byte pieces per row
+    static constexpr int DPT = HD / 32;           // coordinates per thread
+    static constexpr int SLOT = 2 * HD * ROWB + (KV ? 8 * HD : 0);  // keys, values, then key and value scales
+    static constexpr int BMAX = RM == 1 ? 8 : 1;  // tiles under one softmax step
+    static constexpr int BT = BMAX * TK;
+    // scratch (floats), shared by the linear phases and the attention phase
+    static constexpr int QH = 0, QM = QH + RM * HD, RED = QM + RM * HD, PSM = RED + WARPS * RM * BT,
+                         HS = PSM + RM * BT, ALPHA = HS + RM * HID, SINV = ALPHA + 8, LENS = SINV + 8,
+                         WTS = LENS + 8, ATT_END = WTS + RM * ROWS_MAX_GRID;
+    static constexpr int XS = 0, LNW = RM * KMAX, LNB = LNW + KMAX, LIN_END = LNB + KMAX;
+    static constexpr int SCRATCH = ATT_END > LIN_END ? ATT_END : LIN_END;
+    static_assert(WARPS * TK >= 4 * HID && WARPS * TK >= 256, "reduction scratch too small for the query MLP");
+};
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_relaxed_s32(const int *p) {
+    int v;
+    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid barrier on a counter zeroed before the launch: every CTA adds one (release) and waits (acquire) for it to
+// reach the barrier's target, G times its number. Bounded: false (for the whole CTA) when the wait gave up or
+// another CTA raised the error flag.
+__device__ bool grid_sync(const RowsArgs &a, unsigned &target, int *flag_s) {
+    __syncthreads();
+    target += gridDim.x;
+    if (threadIdx.x == 0) {
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+        const long long t0 = clock64();
+        int ok = 1;
+        while (ld_acquire_u32(a.bar) < target) {
+            if (ld_relaxed_s32(a.err) != 0) {
+                ok = 0;
+                break;
+            }
+            if (clock64() - t0 > SPIN_LIMIT) {
+                atomicExch(a.err, 1);
+                ok = 0;
+                break;
+            }
+        }
+        *flag_s = ok;
+    }
+    __syncthreads();
+    return *flag_s != 0;
+}
+
+// 16-byte asynchronous copy global -> shared (L1 bypassed).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Wait until at most `newer` of this thread's commit groups are still in flight.
+__device__ __forceinline__ void cp_async_wait_newer(int newer) {
+    switch (newer) {
+        case 0: cp_async_wait<0>(); break;
+        case 1: cp_async_wait<1>(); break;
+        case 2: cp_async_wait<2>(); break;
+        case 3: cp_async_wait<3>(); break;
+        case 4: cp_async_wait<4>(); break;
+        case 5: cp_async_wait<5>(); break;
+        case 6: cp_async_wait<6>(); break;
+        case 7: cp_async_wait<7>(); break;
+        case 8: cp_async_wait<8>(); break;
+        case 9: cp_async_wait<9>(); break;
+        case 10: cp_async_wait<10>(); break;
+        case 11: cp_async_wait<11>(); break;
+        case 12: cp_async_wait<12>(); break;
+        case 13: cp_async_wait<13>(); break;
+        case 14: cp_async_wait<14>(); break;
+        default: cp_async_wait<0>(); break;
+    }
+}
+
+template <int VB>
+__device__ __forceinline__ uint4 lds_vec(const uint8_t *p) {
+    if (VB == 16) return *reinterpret_cast<const uint4 *>(p);
+    const uint2 v = *reinterpret_cast<const uint2 *>(p);
+    return make_uint4(v.x, v.y, 0u, 0u);
+}
+
+// x[0..7] are this lane's partial sums for rows 0..7; lanes v = 0..7 (low three lane bits) end with the full sum of
+// row v.
+__device__ __forceinline__ float reduce_scatter8(const float (&x)[8], int v) {
+    float y[4], z[2];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float send = (v & 4) ? x[i] : x[i + 4], keep = (v & 4) ? x[i + 4] : x[i];
+        y[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const float send = (v & 2) ? y[i] : y[i + 2], keep = (v & 2) ? y[i + 2] : y[i];
+        z[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+    }
+    const float send = (v & 1) ? z[0] : z[1], keep = (v & 1) ? z[1] : z[0];
+    return keep + __shfl_xor_sync(0xffffffffu, send, 1);
+}
+
+template <int KV, int HD, int RM>
+struct Stage {
+    using C = Cfg<KV, HD, RM>;
+    const RowsArgs &a;
+    uint8_t *ring;
+    float *scr;
+    int *flag_s;
+    int t0, n, total;     // this CTA's tiles [t0, t0 + n) of every layer; total = L n tiles in its sequence
+    int consumed = 0;     // next tile of the sequence to use (those below consumed + slots are issued)
+    unsigned target = 0;  // the grid barrier's next target
+    uint64_t pol_w;
+
+    __device__ Stage(const RowsArgs &a_, uint8_t *smem, int *flag) : a(a_), flag_s(flag) {
+        ring = smem;
+        scr = reinterpret_cast<float *>(smem + (size_t)a.slots * C::SLOT);
+        const int G = gridDim.x, c = blockIdx.x;
+        t0 = (int)((long long)a.ntiles * c / G);
+        n = (int)((long long)a.ntiles * (c + 1) / G) - t0;
+        total = a.L * n;
+        pol_w = policy_evict_last();
+    }
+
+    __device__ __forceinline__ int4 tile_of(int g) const { return a.tiles[t0 + g % n]; }
+    __device__ __forceinline__ bool sync() { return grid_sync(a, target, flag_s); }
+
+    // All threads: start the copies of sequence tile g into its slot, 16 bytes per copy, eight threads along each
+    // coordinate's row, as one commit group (empty for tiles whose rows are not 16-byte aligned: those are copied
+    // when used instead).
+    __device__ void issue(int g) {
+        if (g >= total) return;
+        const int4 tl = tile_of(g);
+        if (!(tl.w >> 16)) {
+            cp_async_commit();
+            return;
+        }
+        const int h = tl.w & 0xffff, ci = tl.x, k0 = tl.y, len = tl.z;
+        const int rc = min(a.chunk, a.rows - ci * a.chunk);
+        const uint8_t *rec = a.layers[g / n].cache + (size_t)ci * a.full;
+        const uint8_t *body = rec + (KV ? 8 * (size_t)a.d : 0);
+        uint8_t *slot = ring + (size_t)(g % a.slots) * C::SLOT;
+        const int pieces = len * C::W / 16;  // of each row
+#pragma unroll
+        for (int it = 0; it < 2 * HD * C::CPR / THREADS; it++) {
+            const int idx = threadIdx.x + it * THREADS;
+            const int row = idx / C::CPR, c = idx % C::CPR;
+            if (c < pieces) {
+                const int coord = row < HD ? h * HD + row : a.d + h * HD + (row - HD);
+                cp_async16(slot + row * C::ROWB + c * 16, body + ((size_t)coord * rc + k0) * C::W + c * 16);
+            }
+        }
+        if (KV && threadIdx.x < HD / 2) {
+            const int i = threadIdx.x;  // 16-byte pieces: key scales, then value scales
+            const size_t off = i < HD / 4 ? (size_t)h * HD * 4 + i * 16 : ((size_t)a.d + h * HD) * 4 + (i - HD / 4) * 16;
+            cp_async16(slot + 2 * HD * C::ROWB + i * 16, rec + off);
+        }
+        cp_async_commit();
+    }
+
+    // All threads: wait for sequence tiles [g0, g0 + nb), the next ones to use; then copy those that could not be
+    // copied asynchronously.
+    __device__ void acquire(int g0, int nb) {
+        const int issued = min(total, consumed + a.slots);
+        cp_async_wait_newer(issued - (g0 + nb));
+        __syncthreads();
+        bool copied = false;
+        for (int b = 0; b < nb; b++) {
+            const int4 tl = tile_of(g0 + b);
+            if (!(tl.w >> 16)) copy_now(g0 + b, tl), copied = true;
+        }
+        if (copied) __syncthreads();
+    }
+
+    __device__ void copy_now(int g, const int4 &tl) {
+        const int s = g % a.slots;
+        // rows not 16-byte aligned: element copies by all threads
+        const int h = tl.w & 0xffff, ci = tl.x, k0 = tl.y, len = tl.z;
+        const int rc = min(a.chunk, a.rows - ci * a.chunk);
+        const uint8_t *rec = a.layers[g / n].cache + (size_t)ci * a.full;
+        const uint8_t *body = rec + (KV ? 8 * (size_t)a.d : 0);
+        uint8_t *slot = ring + (size_t)s * C::SLOT;
+        for (int i = threadIdx.x; i < 2 * HD * len; i += THREADS) {
+            const int row = i / len, e = i - row * len;
+            const int coord = row < HD ? h * HD + row : a.d + h * HD + (row - HD);
+            const uint8_t *src = body + ((size_t)coord * rc + k0 + e) * C::W;
+            uint8_t *dst = slot + (size_t)row * C::ROWB + e * C::W;
+            if (C::W == 4)
+                *reinterpret_cast<uint32_t *>(dst) = __ldg(reinterpret_cast<const uint32_t *>(src));
+            else if (C::W == 2)
+                *reinterpret_cast<uint16_t *>(dst) = __ldg(reinterpret_cast<const unsigned short *>(src));
+            else
+                *dst = __ldg(src);
+        }
+        if (KV) {
+            float *sc = reinterpret_cast<float *>(slot + 2 * HD * C::ROWB);
+            const float *ks = reinterpret_cast<const float *>(rec);
+            for (int i = threadIdx.x; i < 2 * HD; i += THREADS)
+                sc[i] = __ldg(ks + (i < HD ? h * HD + i : a.d + h * HD + (i - HD)));
+        }
+    }
+
+    // Leaving early: this thread's copies still in flight land first.
+    __device__ void drain() { cp_async_wait<0>(); }
+
+    // One linear phase: y[r][o] (=|+=) act(W[o] . LN?(x[r]) + b[o]) for this CTA's outputs o (a contiguous share of
+    // N), one warp per output; the lanes hold 4-float pieces k = 4 lane + 128 v of the weight row, as the few-row
+    // linear kernel does, so both give the same sums. The first output's weights, its bias and the LayerNorm weights
+    // are loaded before the barrier (when `wait`) that makes x ready; x (rows written by other CTAs in this launch)
+    // is read through L2.
+    template <bool LN>
+    __device__ bool linear(bool wait, const float *x, int K, const float *lnw, const float *lnb, const float *W,
+                           const float *b, int N, int act, float *y, int ldy, bool residual) {
+        float *xs = scr + C::XS, *lw_s = scr + C::LNW, *lb_s = scr + C::LNB;
+        const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, R = a.R;
+        const int n0 = (int)((long long)N * blockIdx.x / gridDim.x), n1 = (int)((long long)N * (blockIdx.x + 1) / gridDim.x);
+        const int nv = K >> 7;  // K is a multiple of 128, at most KMAX
+        float4 wv[KMAX / 128];
+        float bias = 0.f;
+        int o = n0 + warp;
+        if (o < n1) {
+            const float *wr = W + (size_t)o * K + lane * 4;
+#pragma unroll
+            for (int v = 0; v < KMAX / 128; v++)
+                if (v < nv) wv[v] = ld_weight4(wr + v * 128, pol_w);
+            if (b) bias = b[o];
+        }
+        float lw[KMAX / THREADS], lb[KMAX / THREADS];
+        if (LN) {
+#pragma unroll
+            for (int i = 0; i < KMAX / THREADS; i++)
+                if (tid + i * THREADS < K) lw[i] = lnw[tid + i * THREADS], lb[i] = lnb[tid + i * THREADS];
+        }
+        if (wait && !sync()) return false;
+        const int k4 = K >> 2;
+        for (int i = tid; i < R * k4; i += THREADS) {
+            const int r = i / k4, c = i - r * k4;
+            reinterpret_cast<float4 *>(xs)[i] = __ldcg(reinterpret_cast<const float4 *>(x + (size_t)r * K) + c);
+        }
+        if (LN) {
+#pragma unroll
+            for (int i = 0; i < KMAX / THREADS; i++)
+                if (tid + i * THREADS < K) lw_s[tid + i * THREADS] = lw[i], lb_s[tid + i * THREADS] = lb[i];
+        }
+        __syncthreads();
+        if (LN) {
+            // kern.rs:357-376, as the few-row linear kernel computes it
+            for (int r = warp; r < R; r += WARPS) {
+                float *row = xs + r * K;
+                float s = 0.f;
+                for (int k = lane; k < K; k += 32) s += row[k];
+                const float mean = warp_sum(s) / (float)K;
+                float q = 0.f;
+                for (int k = lane; k < K; k += 32) {
+                    const float dd = row[k] - mean;
+                    q = fmaf(dd, dd, q);
+                }
+                const float inv = 1.0f / sqrtf(warp_sum(q) / (float)K + 1e-5f);
+                for (int k = lane; k < K; k += 32) row[k] = (row[k] - mean) * inv * lw_s[k] + lb_s[k];
+            }
+            __syncthreads();
+        }
+        for (bool first = true; o < n1; o += WARPS, first = false) {
+            if (!first) {
+                const float *wr = W + (size_t)o * K + lane * 4;
+#pragma unroll
+                for (int v = 0; v < KMAX / 128; v++)
+                    if (v < nv) wv[v] = ld_weight4(wr + v * 128, pol_w);
+                bias = b ? b[o] : 0.f;
+            }
+            float acc[RM];
+#pragma unroll
+            for (int r = 0; r < RM; r++) acc[r] = 0.f;
+#pragma unroll
+            for (int v = 0; v < KMAX / 128; v++) {
+                if (v < nv) {
+#pragma unroll
+                    for (int r = 0; r < RM; r++) {
+                        if (r < R) {
+                            const float4 xv = *reinterpret_cast<const float4 *>(xs + r * K + lane * 4 + v * 128);
+                            acc[r] = fmaf(wv[v].x, xv.x, acc[r]);
+                            acc[r] = fmaf(wv[v].y, xv.y, acc[r]);
+                            acc[r] = fmaf(wv[v].z, xv.z, acc[r]);
+                            acc[r] = fmaf(wv[v].w, xv.w, acc[r]);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < RM; r++) acc[r] = warp_sum(acc[r]);
+            if (lane == 0) {
+#pragma unroll
+                for (int r = 0; r < RM; r++) {
+                    if (r < R) {
+                        float v = acc[r] + bias;
+                        if (act) v = gelu1(v);
+                        float *dst = y + (size_t)r * ldy + o;
+                        *dst = residual ? __ldcg(dst) + v : v;
+                    }
+                }
+            }
+        }
+        return true;
+    }
+
+    // Registers of the query MLP for one head, loaded ahead of use.
+    struct QueryW {
+        float4 w0[HD / 16];       // hidden unit tid % 64, coordinates (tid / 64) HD/4 + [0, HD/4)
+        float4 w2[HID * HD / 1024];  // coordinate tid % HD, hidden units (tid / HD) 64 HD/256 + [0, 64 HD/256)
+        float b0, b2, sc;
+    };
+    __device__ void query_load(const RowsLayer &Ly, int h, QueryW &w) {
+        const int tid = threadIdx.x, u = tid & (HID - 1), p = tid >> 6, j = tid % HD, p2 = tid / HD;
+        constexpr int QJ = HD / 4, QU = HID * HD / THREADS;
+#pragma unroll
+        for (int i = 0; i < QJ / 4; i++) w.w0[i] = ld_weight4(Ly.q0w + (size_t)u * HD + p * QJ + 4 * i, pol_w);
+#pragma unroll
+        for (int i = 0; i < QU / 4; i++) w.w2[i] = ld_weight4(Ly.q2w + (size_t)j * HID + p2 * QU + 4 * i, pol_w);
+        w.b0 = Ly.q0b[u];
+        w.b2 = Ly.q2b[j];
+        w.sc = Ly.scale[h * HD + j];
+    }
+
+    // The query MLP of the scalable softmax for head h (nn.rs:138-149): qm = q_h * scale_h * (1 + tanh(m)).
+    __device__ void query_head(int h, const QueryW &w) {
+        float *qh = scr + C::QH, *qm = scr + C::QM, *red = scr + C::RED, *hs = scr + C::HS;
+        const int tid = threadIdx.x, R = a.R, d = a.d;
+        constexpr int QJ = HD / 4, P2 = THREADS / HD, QU = HID / P2;
+        for (int i = tid; i < RM * HD; i += THREADS) {
+            const int r = i / HD, j = i - r * HD;
+            qh[i] = r < R ? __ldcg(a.q + (size_t)r * d + h * HD + j) : 0.f;
+        }
+        __syncthreads();
+        {
+            const int u = tid & (HID - 1), p = tid >> 6;
+            float acc[RM];
+#pragma unroll
+            for (int r = 0; r < RM; r++) acc[r] = 0.f;
+#pragma unroll
+            for (int i = 0; i < QJ / 4; i++) {
+#pragma unroll
+                for (int r = 0; r < RM; r++) {
+                    const float4 xv = *reinterpret_cast<const float4 *>(qh + r * HD + p * QJ + 4 * i);
+                    acc[r] = fmaf(w.w0[i].x, xv.x, acc[r]);
+                    acc[r] = fmaf(w.w0[i].y, xv.y, acc[r]);
+                    acc[r] = fmaf(w.w0[i].z, xv.z, acc[r]);
+                    acc[r] = fmaf(w.w0[i].w, xv.w, acc[r]);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < RM; r++) red[(p * RM + r) * HID + u] = acc[r];
+        }
+        __syncthreads();
+        for (int i = tid; i < RM * HID; i += THREADS) {
+            const int r = i / HID, u = i - r * HID;  // u = tid % 64: this thread's b0
+            const float s = (red[(0 * RM + r) * HID + u] + red[(1 * RM + r) * HID + u]) +
+                            (red[(2 * RM + r) * HID + u] + red[(3 * RM + r) * HID + u]);
+            hs[i] = gelu1(s + w.b0);
+        }
+        __syncthreads();
+        {
+            const int j = tid % HD, p2 = tid / HD;
+            float acc[RM];
+#pragma unroll
+            for (int r = 0; r < RM; r++) acc[r] = 0.f;
+#pragma unroll
+            for (int i = 0; i < QU / 4; i++) {
+#pragma unroll
+                for (int r = 0; r < RM; r++) {
+                    const float4 xv = *reinterpret_cast<const float4 *>(hs + r * HID + p2 * QU + 4 * i);
+                    acc[r] = fmaf(w.w2[i].x, xv.x, acc[r]);
+                    acc[r] = fmaf(w.w2[i].y, xv.y, acc[r]);
+                    acc[r] = fmaf(w.w2[i].z, xv.z, acc[r]);
+                    acc[r] = fmaf(w.w2[i].w, xv.w, acc[r]);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < RM; r++) red[(p2 * RM + r) * HD + j] = acc[r];
+        }
+        __syncthreads();
+        for (int i = tid; i < RM * HD; i += THREADS) {
+            const int r = i / HD, j = i - r * HD;  // j = tid % HD: this thread's b2 and scale
+            float s = 0.f;
+#pragma unroll
+            for (int q = 0; q < P2; q++) s += red[(q * RM + r) * HD + j];
+            qm[i] = qh[i] * (w.sc * (1.0f + tanh1(s + w.b2)));
+        }
+        __syncthreads();
+    }
+
+    // The last CTA to finish head h: log-sum-exp merge of the head's partial states into att (nn.rs:261-286).
+    __device__ void merge(int h) {
+        float *wts = scr + C::WTS, *sinv = scr + C::SINV;
+        const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, R = a.R, H = a.heads;
+        const int lo = a.part_lo[h], np = a.part_hi[h] - lo + 1;
+        if (warp < R) {
+            const int r = warp;
+            float M = -FLT_MAX;
+            for (int i = lane; i < np; i += 32) M = fmaxf(M, __ldcg(a.part_ms + (((size_t)(lo + i) * H + h) * R + r) * 2));
+            M = warp_max(M);
+            float S = 0.f;
+            for (int i = lane; i < np; i += 32) {
+                const float *ms = a.part_ms + (((size_t)(lo + i) * H + h) * R + r) * 2;
+                const float w = exp1(__ldcg(ms) - M);
+                wts[r * ROWS_MAX_GRID + i] = w;
+                S = fmaf(__ldcg(ms + 1), w, S);
+            }
+            S = warp_sum(S);
+            if (lane == 0) sinv[r] = 1.0f / S;
+        }
+        __syncthreads();
+        for (int i = tid; i < R * HD; i += THREADS) {
+            const int r = i / HD, j = i - r * HD;
+            const float *pa = a.part_acc + (((size_t)lo * H + h) * R + r) * HD + j;
+            const size_t step = (size_t)H * R * HD;
+            float o = 0.f;
+#pragma unroll 8
+            for (int p = 0; p < np; p++) o = fmaf(wts[r * ROWS_MAX_GRID + p], __ldcg(pa + p * step), o);
+            a.att[(size_t)r * a.d + h * HD + j] = o * sinv[r];
+        }
+        __syncthreads();
+    }
+
+    // Phase B of layer l.
+    __device__ bool attend(int l) {
+        const RowsLayer &Ly = a.layers[l];
+        const int Th = a.tiles_per_head;
+        {
+            // the first head's query MLP weights load while the barrier completes
+            QueryW qw;
+            query_load(Ly, t0 / Th, qw);
+            if (!sync()) return false;  // q is ready
+            query_head(t0 / Th, qw);
+        }
+        float *qm = scr + C::QM, *red = scr + C::RED, *psm = scr + C::PSM, *alpha = scr + C::ALPHA;
+        int *lens = reinterpret_cast<int *>(scr + C::LENS);
+        const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, v = tid & 7, jg = tid >> 3, R = a.R;
+        for (int t = t0; t < t0 + n;) {
+            const int h = t / Th, te = min(t0 + n, (h + 1) * Th);
+            if (t != t0) {
+                QueryW qw;
+                query_load(Ly, h, qw);
+                query_head(h, qw);
+            }
+            float m_run = -FLT_MAX, s_run = 0.f;  // row `warp`'s running state, in every lane of that warp
+            float acc[C::DPT];                    // row v (RM 8) or row 0 (lanes v = 0), coordinates jg + 32 i
+#pragma unroll
+            for (int i = 0; i < C::DPT; i++) acc[i] = 0.f;
+            for (bool first = true; t < te; first = false) {
+                // a batch of resident tiles under one softmax step
+                const int nb = min(min(C::BMAX, a.slots), te - t);
+                const int g0 = l * n + (t - t0);
+                if (tid < nb) lens[tid] = tile_of(g0 + tid).z;
+                acquire(g0, nb);
+                // scores: integer keys take the query times the chunk's key scales (predict.rs:486-497)
+                for (int b = 0; b < nb; b++) {
+                    const uint8_t *slot = ring + (size_t)((g0 + b) % a.slots) * C::SLOT;
+                    const float *ksc = reinterpret_cast<const float *>(slot + 2 * HD * C::ROWB);
+                    float sp[RM][C::EPV];
+#pragma unroll
+                    for (int r = 0; r < RM; r++)
+#pragma unroll
+                        for (int e = 0; e < C::EPV; e++) sp[r][e] = 0.f;
+#pragma unroll
+                    for (int i = 0; i < C::DPT; i++) {
+                        const int j = jg + 32 * i;
+                        const uint4 kv = lds_vec<C::VB>(slot + (size_t)j * C::ROWB + v * C::VB);
+                        float qs[RM];
+#pragma unroll
+                        for (int r = 0; r < RM; r++) qs[r] = KV ? qm[r * HD + j] * ksc[j] : qm[r * HD + j];
+#pragma unroll
+                        for (int e = 0; e < C::EPV; e++) {
+                            const float kf = unpack<KV>(kv, e);
+#pragma unroll
+                            for (int r = 0; r < RM; r++) sp[r][e] = fmaf(qs[r], kf, sp[r][e]);
+                        }
+                    }
+#pragma unroll
+                    for (int r = 0; r < RM; r++)
+#pragma unroll
+                        for (int e = 0; e < C::EPV; e++) {
+                            float x = sp[r][e];
+                            x += __shfl_xor_sync(0xffffffffu, x, 8);
+                            x += __shfl_xor_sync(0xffffffffu, x, 16);
+                            sp[r][e] = x;
+                        }
+                    if (lane < 8) {
+#pragma unroll
+                        for (int r = 0; r < RM; r++)
+#pragma unroll
+                            for (int e = 0; e < C::EPV; e++)
+                                red[(warp * RM + r) * C::BT + b * C::TK + v * C::EPV + e] = sp[r][e];
+                    }
+                }
+                __syncthreads();
+                // online softmax, one warp per row, with the reference's rescaling rule (nn.rs:207-215)
+                if (warp < RM) {
+                    const int r = warp;
+                    if (r < R) {
+                        float sc[C::BT / 32];
+                        float mx = -FLT_MAX;
+#pragma unroll
+                        for (int kk = 0; kk < C::BT / 32; kk++) {
+                            const int k = lane + 32 * kk;
+                            const float *rr = red + r * C::BT + k;
+                            const int ws = RM * C::BT;
+                            const float s = ((rr[0] + rr[ws]) + (rr[2 * ws] + rr[3 * ws])) +
+                                            ((rr[4 * ws] + rr[5 * ws]) + (rr[6 * ws] + rr[7 * ws]));
+                            sc[kk] = s;
+                            if (k < nb * C::TK && (k % C::TK) < lens[k / C::TK]) mx = fmaxf(mx, s);
+                        }
+                        mx = warp_max(mx);
+                        float al;
+                        if (first) {
+                            m_run = mx, s_run = 0.f, al = 0.f;
+                        } else if (mx > m_run) {
+                            al = exp1(m_run - mx), m_run = mx;
+                        } else {
+                            al = 1.f;
+                        }
+                        float sum = 0.f;
+#pragma unroll
+                        for (int kk = 0; kk < C::BT / 32; kk++) {
+                            const int k = lane + 32 * kk;
+                            const bool valid = k < nb * C::TK && (k % C::TK) < lens[k / C::TK];
+                            const float pk = valid ? exp1(sc[kk] - m_run) : 0.f;
+                            psm[r * C::BT + k] = pk;
+                            sum += pk;
+                        }
+                        s_run = s_run * al + warp_sum(sum);
+                        if (lane == 0) alpha[r] = al;
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < C::BT / 32; kk++) psm[r * C::BT + lane + 32 * kk] = 0.f;
+                        if (lane == 0) alpha[r] = 1.f;
+                    }
+                }
+                __syncthreads();
+                // weighted values; integer values take the chunk's value scales after the sum (nn.rs:253-256)
+                {
+                    float x[C::DPT][RM];
+#pragma unroll
+                    for (int i = 0; i < C::DPT; i++)
+#pragma unroll
+                        for (int r = 0; r < RM; r++) x[i][r] = 0.f;
+                    for (int b = 0; b < nb; b++) {
+                        const uint8_t *slot = ring + (size_t)((g0 + b) % a.slots) * C::SLOT;
+                        const float *vsc = reinterpret_cast<const float *>(slot + 2 * HD * C::ROWB) + HD;
+                        const int len = lens[b];
+                        float p[RM][C::EPV];
+#pragma unroll
+                        for (int r = 0; r < RM; r++)
+#pragma unroll
+                            for (int e = 0; e < C::EPV; e += 4) {
+                                const float4 pv =
+                                    *reinterpret_cast<const float4 *>(psm + r * C::BT + b * C::TK + v * C::EPV + e);
+                                p[r][e] = pv.x, p[r][e + 1] = pv.y, p[r][e + 2] = pv.z, p[r][e + 3] = pv.w;
+                            }
+#pragma unroll
+                        for (int i = 0; i < C::DPT; i++) {
+                            const int j = jg + 32 * i;
+                            const uint4 vv = lds_vec<C::VB>(slot + (size_t)(HD + j) * C::ROWB + v * C::VB);
+                            float vf[C::EPV];
+#pragma unroll
+                            for (int e = 0; e < C::EPV; e++) vf[e] = v * C::EPV + e < len ? unpack<KV>(vv, e) : 0.f;
+                            const float vs = KV ? vsc[j] : 1.f;
+#pragma unroll
+                            for (int r = 0; r < RM; r++) {
+                                float s = 0.f;
+#pragma unroll
+                                for (int e = 0; e < C::EPV; e++) s = fmaf(p[r][e], vf[e], s);
+                                x[i][r] = KV ? fmaf(s, vs, x[i][r]) : x[i][r] + s;
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < C::DPT; i++) {
+                        float tot;
+                        if constexpr (RM == 8) {
+                            tot = reduce_scatter8(x[i], v);
+                        } else {
+                            tot = x[i][0];
+                            tot += __shfl_xor_sync(0xffffffffu, tot, 1);
+                            tot += __shfl_xor_sync(0xffffffffu, tot, 2);
+                            tot += __shfl_xor_sync(0xffffffffu, tot, 4);
+                        }
+                        const int r = RM == 8 ? v : 0;
+                        if (r < R && (RM == 8 || v == 0)) acc[i] = acc[i] * alpha[r] + tot;
+                    }
+                }
+                __syncthreads();  // the slots and the scratch are free again
+                for (int b = 0; b < nb; b++) issue(g0 + b + a.slots);
+                consumed = g0 + nb;
+                t += nb;
+            }
+            // this CTA's partial state of head h, then the head's arrival count
+            const int pi = blockIdx.x * a.heads + h;
+            if (warp < R && lane == 0) {
+                float *ms = a.part_ms + ((size_t)pi * R + warp) * 2;
+                ms[0] = m_run, ms[1] = s_run;
+            }
+            {
+                const int r = RM == 8 ? v : 0;
+                if (r < R && (RM == 8 || v == 0)) {
+#pragma unroll
+                    for (int i = 0; i < C::DPT; i++) a.part_acc[((size_t)pi * R + r) * HD + jg + 32 * i] = acc[i];
+                }
+            }
+            __syncthreads();
+            if (tid == 0) {
+                __threadfence();
+                const int old = atomicAdd(a.head_cnt + h, 1);
+                *flag_s = old == a.part_hi[h] - a.part_lo[h];
+            }
+            __syncthreads();
+            if (*flag_s) {
+                __threadfence();
+                merge(h);
+            }
+        }
+        return true;
+    }
+};
+
+template <int KV, int HD, int RM>
+__global__ void __launch_bounds__(THREADS, 1) k_stage_rows(const RowsArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ int flag_s;
+    Stage<KV, HD, RM> st(a, smem, &flag_s);
+    const int tid = threadIdx.x, d = a.d;
+    for (int g = 0; g < min(a.slots, st.total); g++) st.issue(g);
+    bool ok = true;
+    for (int l = 0; l < a.L && ok; l++) {
+        const RowsLayer &Ly = a.layers[l];
+        if (blockIdx.x == 0 && tid < a.heads) a.head_cnt[tid] = 0;  // used after the next barrier
+        ok = st.template linear<true>(l > 0, a.h, d, Ly.n1w, Ly.n1b, Ly.wq, Ly.bq, d, 0, a.q, d, false);
+        ok = ok && st.attend(l);
+        ok = ok && st.template linear<false>(true, a.att, d, nullptr, nullptr, Ly.wo, Ly.bo, d, 0, a.h, d, true);
+        ok = ok && st.template linear<true>(true, a.h, d, Ly.n2w, Ly.n2b, Ly.w1, Ly.b1, a.ff, 1, a.mid, a.ff, false);
+        ok = ok && st.template linear<false>(true, a.mid, a.ff, nullptr, nullptr, Ly.w2, Ly.b2, d, 0, a.h, d, true);
+    }
+    ok = ok && st.template linear<true>(true, a.h, d, a.lnw, a.lnb, a.dec0w, a.dec0b, a.dff, 1, a.mid, a.dff, false);
+    ok = ok && st.template linear<false>(true, a.mid, a.dff, nullptr, nullptr, a.dec2w, a.dec2b, a.out_n, 0, a.out,
+                                         a.out_n, false);
+    if (!ok) st.drain();
+}
+
+template <int KV, int HD, int RM>
+size_t smem_of(int slots) {
+    using C = Cfg<KV, HD, RM>;
+    return (size_t)slots * C::SLOT + sizeof(float) * (size_t)C::SCRATCH;
+}
+
+template <int KV, int HD, int RM>
+cudaError_t launch_one(const RowsArgs &a, int grid, size_t smem, cudaStream_t s) {
+    auto kern = k_stage_rows<KV, HD, RM>;
+    static std::mutex mu;
+    static size_t have = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (smem > have) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            have = smem;
+        }
+    }
+    void *args[] = {const_cast<RowsArgs *>(&a)};
+    return cudaLaunchCooperativeKernel((const void *)kern, dim3(grid), dim3(THREADS), args, smem, s);
+}
+
+template <int KV, int HD, int RM>
+int max_grid_one(size_t smem, int sms) {
+    auto kern = k_stage_rows<KV, HD, RM>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    int per = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, THREADS, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return per * sms;
+}
+
+#define TCU_ROWS_CASES(X)                                                                                      \
+    X(0, 128, 1) X(0, 128, 8) X(1, 128, 1) X(1, 128, 8) X(2, 128, 1) X(2, 128, 8) X(0, 64, 1) X(0, 64, 8) X(1, 64, 1) \
+        X(1, 64, 8) X(2, 64, 1) X(2, 64, 8)
+
+}  // namespace
+
+int rows_tile_keys(int kv) { return kv == 0 ? 32 : 64; }
+
+size_t rows_smem(int kv, int hd, int R, int slots) {
+    const int rm = R > 1 ? 8 : 1;
+#define X(K, H, M) \
+    if (kv == K && hd == H && rm == M) return smem_of<K, H, M>(slots);
+    TCU_ROWS_CASES(X)
+#undef X
+    return 0;
+}
+
+int rows_slots_for(int kv, int hd, int R, size_t smem_max) {
+    const size_t base = rows_smem(kv, hd, R, 0), one = rows_smem(kv, hd, R, 1) - base;
+    if (base == 0 || smem_max < base + one) return 0;
+    return (int)std::min<size_t>(16, (smem_max - base) / one);
+}
+
+int rows_max_grid(int kv, int hd, int R, size_t smem, int sms) {
+    const int rm = R > 1 ? 8 : 1;
+#define X(K, H, M) \
+    if (kv == K && hd == H && rm == M) return max_grid_one<K, H, M>(smem, sms);
+    TCU_ROWS_CASES(X)
+#undef X
+    return 0;
+}
+
+cudaError_t launch_stage_rows(int kv, int hd, const RowsArgs &a, int grid, size_t smem, cudaStream_t s,
+                              uint64_t *launches) {
+    const int R = a.R, rm = R > 1 ? 8 : 1;
+    if (R < 1 || R > 8 || grid < 1 || grid > ROWS_MAX_GRID || a.heads > ROWS_MAX_HEADS) return cudaErrorInvalidValue;
+    cudaError_t e = cudaErrorInvalidValue;
+#define X(K, H, M) \
+    if (kv == K && hd == H && rm == M) e = launch_one<K, H, M>(a, grid, smem, s);
+    TCU_ROWS_CASES(X)
+#undef X
+    if (e == cudaSuccess && launches) ++*launches;
+    return e;
+}
+
+}  // namespace tcu

@@ -114,6 +114,25 @@ def test_stage_synthetic(gpu, case, kv):
         assert np.abs(softmax(got) - softmax(want)).max() < PROBA
 
 
+@pytest.mark.parametrize("kv", [0, 1, 2])
+def test_few_rows_run_as_one_kernel(gpu, kv):
+    """Up to 8 rows at head widths 64/128 take the one-kernel stage: one launch per call, every row count 1..8
+    within the stage bar of the CPU path, and bit-identical when repeated."""
+    n, chunk = 1000, 256   # 16-byte aligned chunks (bulk-copied tiles) and a ragged last chunk of 232 rows
+    cfg, wt, m, caches, scales = _synthetic("full", 2, n, chunk, kv, seed=60 + kv)
+    w = _weights(gpu, cfg, wt)
+    vm = tcu.VramModel.from_parts(w, _meta(n, chunk, kv, 10), n, 10, scales, caches)
+    for rows in range(1, 9):
+        h = synth.row_reps(rows, m.d, 70 + rows)
+        before = gpu.launches
+        got = vm.stage(h, 10)
+        assert gpu.launches - before == 1, gpu.launches - before
+        want = oracle.in_context(m, kv, caches, scales, n, chunk, h, 10)
+        assert np.abs(got - want).max() < STAGE, (rows, np.abs(got - want).max())
+        assert np.abs(softmax(got) - softmax(want)).max() < PROBA
+        assert np.array_equal(vm.stage(h, 10), got)
+
+
 def test_rows_are_independent(gpu):
     """A row's answer does not depend on the rows predicted with it (tests/pipeline.rs:122-135)."""
     cfg, wt, m, caches, scales = _synthetic("full", 2, 500, 256, 1, seed=5)
