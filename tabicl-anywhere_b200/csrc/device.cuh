@@ -113,17 +113,21 @@ __device__ __forceinline__ float unpack<0>(const uint4 &v, int e) {
     uint32_t w = e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w;
     return __uint_as_float(w);
 }
+// Integers are widened without the conversion unit (a quarter-rate pipe): with the sign bit flipped, an n-bit
+// value v becomes the unsigned v + 2^(n-1); placed in the low mantissa bits of 2^23 it is the float
+// 2^23 + v + 2^(n-1), and subtracting 2^23 + 2^(n-1) leaves v. Every step is exact (integers below 2^24), so the
+// result equals (float)v bit for bit.
 template <>
 __device__ __forceinline__ float unpack<1>(const uint4 &v, int e) {
-    uint32_t w = (e >> 1) == 0 ? v.x : (e >> 1) == 1 ? v.y : (e >> 1) == 2 ? v.z : v.w;
-    int16_t s = (int16_t)((e & 1) ? (w >> 16) : (w & 0xffffu));
-    return (float)s;
+    const uint32_t w = ((e >> 1) == 0 ? v.x : (e >> 1) == 1 ? v.y : (e >> 1) == 2 ? v.z : v.w) ^ 0x80008000u;
+    const uint32_t f = __byte_perm(w, 0x4B000000u, (e & 1) ? 0x7632u : 0x7610u);
+    return __uint_as_float(f) - 8421376.0f;  // 2^23 + 2^15
 }
 template <>
 __device__ __forceinline__ float unpack<2>(const uint4 &v, int e) {
-    uint32_t w = (e >> 2) == 0 ? v.x : (e >> 2) == 1 ? v.y : (e >> 2) == 2 ? v.z : v.w;
-    int8_t s = (int8_t)((w >> (8 * (e & 3))) & 0xffu);
-    return (float)s;
+    const uint32_t w = ((e >> 2) == 0 ? v.x : (e >> 2) == 1 ? v.y : (e >> 2) == 2 ? v.z : v.w) ^ 0x80808080u;
+    const uint32_t f = __byte_perm(w, 0x4B000000u, 0x7650u | (uint32_t)(e & 3));
+    return __uint_as_float(f) - 8388736.0f;  // 2^23 + 2^7
 }
 
 // One stored element by index (any alignment), for ragged chunk tails.

@@ -4,6 +4,7 @@
 #include "../../include/tabicl_b200.h"
 
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <cmath>
 #include <cstdlib>
@@ -127,7 +128,7 @@ struct tcu_model {
     // working memory, grown to the largest call so far
     DevBuf h, q, att, mid, stats, out, part_ms, part_acc;
     // the one-kernel few-row stage: key tiles (head-major), per-layer pointer table, barrier words, partials
-    DevBuf rtiles, rlayers, rsync, rparts_ms, rparts_acc;
+    DevBuf rtiles, rlayers, rsync, rparts_ms, rparts_acc, rtmaps;
     int rtiles_n = 0, rtiles_per_head = 0;
     bool rows_built = false;
     struct RowsPlan {
@@ -711,18 +712,62 @@ static bool rows_kernel_enabled() {
     return on;
 }
 
-// Key tiles (head-major), the per-layer pointer table and the barrier words, once per model.
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// Key tiles (head-major), the per-layer pointer table, TMA tensor maps and the barrier words, once per model.
+// A stored layer is read in place (fit.rs:6-11): the full chunks as a 3-D byte tensor (a coordinate's keys, the
+// 2d coordinates, the chunks; strides chunk * width and the record size) and the last, shorter chunk as a 2-D one.
+// Boxes are one tile: the tile's keys (in bytes) x one head's coordinates. A chunk whose rows are not a multiple of
+// 16 bytes cannot be described so; its tiles are copied element by element instead.
 static void rows_build(tcu_model *m) {
     if (m->rows_built) return;
     const auto &sh = m->w->shape;
-    const int tk = rows_tile_keys(m->kv), w = m->kv == 0 ? 4 : (m->kv == 1 ? 2 : 1);
+    const int tk = rows_tile_keys(m->kv), w = m->kv == 0 ? 4 : (m->kv == 1 ? 2 : 1), hd = sh.d / sh.heads;
+    const int nfull = m->rows / m->chunk, rem = m->rows % m->chunk;
+    const size_t head = m->kv ? 8 * (size_t)sh.d : 0;
+    bool full_ok = nfull > 0 && (m->chunk * w) % 16 == 0 && m->full % 16 == 0;
+    bool rem_ok = rem > 0 && (rem * w) % 16 == 0 && m->full % 16 == 0;
+    std::vector<CUtensorMap> maps(2 * (size_t)sh.layers);
+    std::memset(maps.data(), 0, maps.size() * sizeof(CUtensorMap));
+    auto encode = tensor_map_encoder();
+    if (!encode) full_ok = rem_ok = false;
+    for (int l = 0; l < sh.layers && (full_ok || rem_ok); l++) {
+        const uint8_t *base = layer_ptr(m, l) + head;
+        const cuuint32_t box[3] = {(cuuint32_t)(tk * w), (cuuint32_t)hd, 1}, one[3] = {1, 1, 1};
+        if (full_ok) {
+            const cuuint64_t dims[3] = {(cuuint64_t)m->chunk * w, 2 * (cuuint64_t)sh.d, (cuuint64_t)nfull};
+            const cuuint64_t strides[2] = {(cuuint64_t)m->chunk * w, (cuuint64_t)m->full};
+            full_ok = encode(&maps[2 * l], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t *>(base), dims, strides,
+                             box, one, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        }
+        if (rem_ok) {
+            const cuuint64_t dims[2] = {(cuuint64_t)rem * w, 2 * (cuuint64_t)sh.d};
+            const cuuint64_t strides[1] = {(cuuint64_t)rem * w};
+            rem_ok = encode(&maps[2 * l + 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                            const_cast<uint8_t *>(base + (size_t)nfull * m->full), dims, strides, box, one,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        }
+    }
+    m->rtmaps.ensure(maps.size() * sizeof(CUtensorMap));
+    CU(cudaMemcpy(m->rtmaps.p, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
     std::vector<int4> tiles;
     for (int h = 0; h < sh.heads; h++) {
         for (int ci = 0, r0 = 0; r0 < m->rows; ci++, r0 += m->chunk) {
             const int rc = std::min(m->chunk, m->rows - r0);
-            // a coordinate's keys start 16-byte aligned in every chunk of this size: bulk copies
-            const int aligned = (rc * w) % 16 == 0 ? 1 : 0;
-            for (int k0 = 0; k0 < rc; k0 += tk) tiles.push_back(make_int4(ci, k0, std::min(tk, rc - k0), h | aligned << 16));
+            const int tma = (ci < nfull ? full_ok : rem_ok) ? 1 : 0;
+            for (int k0 = 0; k0 < rc; k0 += tk) tiles.push_back(make_int4(ci, k0, std::min(tk, rc - k0), h | tma << 16));
         }
     }
     m->rtiles_n = (int)tiles.size();
@@ -749,7 +794,7 @@ static const tcu_model::RowsPlan *rows_plan(tcu_ctx *ctx, tcu_model *m, int R) {
     const auto &sh = m->w->shape;
     const int hd = sh.d / sh.heads;
     if (!rows_kernel_enabled() || !ctx->coop || R < 1 || R > 8) return nullptr;
-    if ((hd != 64 && hd != 128) || sh.hid != 64 || sh.heads > ROWS_MAX_HEADS) return nullptr;
+    if ((hd != 64 && hd != 128) || sh.hid != 64 || sh.heads > ROWS_MAX_HEADS || sh.layers > ROWS_MAX_LAYERS) return nullptr;
     for (int k : {sh.d, sh.ff, sh.dec_ff})
         if (k % 128 || k > 1024) return nullptr;
     auto &p = m->rows_plans[R > 1 ? 1 : 0];
@@ -796,6 +841,7 @@ static void stage_rows(tcu_ctx *ctx, tcu_model *m, const tcu_model::RowsPlan &p,
     a.dec2w = m->w->dec2w, a.dec2b = m->w->dec2b;
     a.rows = m->rows, a.chunk = m->chunk, a.full = m->full;
     a.tiles = m->rtiles.as<int4>(), a.ntiles = m->rtiles_n, a.tiles_per_head = m->rtiles_per_head, a.slots = p.slots;
+    a.tmaps = m->rtmaps.p, a.nfull = m->rows / m->chunk;
     a.h = m->h.as<float>(), a.q = m->q.as<float>(), a.att = m->att.as<float>(), a.mid = m->mid.as<float>();
     a.out = m->out.as<float>();
     a.part_ms = m->rparts_ms.as<float>(), a.part_acc = m->rparts_acc.as<float>();

@@ -54,6 +54,7 @@ struct RowsLayer {
 };
 
 constexpr int ROWS_MAX_HEADS = 16;
+constexpr int ROWS_MAX_LAYERS = 16;
 constexpr int ROWS_MAX_GRID = 160;
 
 struct RowsArgs {
@@ -66,6 +67,10 @@ struct RowsArgs {
     const int4 *tiles = nullptr;
     int ntiles = 0, tiles_per_head = 0;
     int slots = 0;                      // tiles of shared memory per CTA
+    // TMA tensor maps per layer, device memory: [L][2] CUtensorMap (the full chunks as bytes x coordinates x chunks,
+    // then the last, shorter chunk as bytes x coordinates); tiles flagged aligned are loaded through them
+    const void *tmaps = nullptr;
+    int nfull = 0;                      // full chunks per layer
     float *h = nullptr, *q = nullptr, *att = nullptr, *mid = nullptr, *out = nullptr;
     float *part_ms = nullptr, *part_acc = nullptr;  // [grid][heads][R] (max, weight sum) and [..][head width]
     unsigned *bar = nullptr;            // grid barrier word (zero low bits between launches)

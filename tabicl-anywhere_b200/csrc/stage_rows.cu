@@ -12,9 +12,10 @@
 //
 // Few rows are latency-bound: each phase is a few microseconds of dependent work. What the kernel overlaps is the
 // cache stream. Every CTA owns a fixed share of each layer's key tiles and keeps a ring of them in shared memory,
-// filled by asynchronous 16-byte copies (cp.async, one commit group per tile, so a tile is ready once the groups
-// committed after it are few enough). A slot is refilled with the next tile of the CTA's sequence as soon as it has
-// been used, so the next layer's keys and values arrive while phases D, E, F and A of this layer run. Loads that do
+// filled by the tensor memory accelerator: one thread starts two tensor loads (keys, values) and two bulk copies
+// (their scales) per tile, completing on the slot's mbarrier. A slot is refilled with the next tile of the CTA's
+// sequence as soon as it has been used, so the next layer's keys and values arrive while phases D, E, F and A of
+// this layer run. Loads that do
 // not depend on a barrier (weight rows, biases, LayerNorm and query-MLP weights) are issued before it. Every grid
 // barrier is bounded: one that does not complete within about a second sets the error flag, and every CTA then
 // leaves at its next barrier.
@@ -34,6 +35,7 @@ constexpr int THREADS = 256, WARPS = 8;
 constexpr int HID = 64;                       // hidden width of the query MLP (nn.rs:124)
 constexpr int KMAX = 1024;                    // widest input of a linear phase
 constexpr long long SPIN_LIMIT = 2000000000;  // cycles, about a second
+constexpr int TCACHE = 96;                    // a CTA's tile descriptors kept in shared memory
 
 template <int KV, int HD, int RM>
 struct Cfg {
@@ -42,15 +44,15 @@ struct Cfg {
     static constexpr int EPV = VB / W;            // keys per lane vector: 4, 8, 8
     static constexpr int TK = 8 * EPV;            // keys per tile: 32, 64, 64
     static constexpr int ROWB = TK * W;           // bytes of one coordinate's keys in a tile: 128, 128, 64
-    static constexpr int CPR = ROWB / 16;         // 16-byte pieces per row
     static constexpr int DPT = HD / 32;           // coordinates per thread
     static constexpr int SLOT = 2 * HD * ROWB + (KV ? 8 * HD : 0);  // keys, values, then key and value scales
+    static_assert(SLOT % 128 == 0 && (HD * ROWB) % 128 == 0, "tensor-load destinations must be 128-byte aligned");
     static constexpr int BMAX = RM == 1 ? 8 : 1;  // tiles under one softmax step
     static constexpr int BT = BMAX * TK;
     // scratch (floats), shared by the linear phases and the attention phase
     static constexpr int QH = 0, QM = QH + RM * HD, RED = QM + RM * HD, PSM = RED + WARPS * RM * BT,
                          HS = PSM + RM * BT, ALPHA = HS + RM * HID, SINV = ALPHA + 8, LENS = SINV + 8,
-                         WTS = LENS + 8, ATT_END = WTS + RM * ROWS_MAX_GRID;
+                         BMS = LENS + 8, WTS = BMS + 16, ATT_END = WTS + RM * ROWS_MAX_GRID;
     static constexpr int XS = 0, LNW = RM * KMAX, LNB = LNW + KMAX, LIN_END = LNB + KMAX;
     static constexpr int SCRATCH = ATT_END > LIN_END ? ATT_END : LIN_END;
     static_assert(WARPS * TK >= 4 * HID && WARPS * TK >= 256, "reduction scratch too small for the query MLP");
@@ -67,15 +69,21 @@ __device__ __forceinline__ int ld_relaxed_s32(const int *p) {
     return v;
 }
 
-// Grid barrier on a counter zeroed before the launch: every CTA adds one (release) and waits (acquire) for it to
-// reach the barrier's target, G times its number. Bounded: false (for the whole CTA) when the wait gave up or
-// another CTA raised the error flag.
-__device__ bool grid_sync(const RowsArgs &a, unsigned &target, int *flag_s) {
+// Grid barrier on a counter zeroed before the launch, in two halves. arrive(): after a phase's stores, one thread per
+// CTA adds one (release). wait(): one thread waits (acquire) until the counter reaches G times the barrier's number.
+// Work that neither reads what other CTAs write in the phase nor writes what they read (loads of weights, copies
+// of key tiles) goes between the two. The wait is bounded: false (for the whole CTA) when it gave up or another CTA
+// raised the error flag.
+__device__ __forceinline__ void grid_arrive(const RowsArgs &a, unsigned &target) {
     __syncthreads();
     target += gridDim.x;
     if (threadIdx.x == 0) {
         asm volatile("fence.acq_rel.gpu;" ::: "memory");
         asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+    }
+}
+__device__ bool grid_wait(const RowsArgs &a, unsigned target, int *flag_s) {
+    if (threadIdx.x == 0) {
         const long long t0 = clock64();
         int ok = 1;
         while (ld_acquire_u32(a.bar) < target) {
@@ -95,35 +103,35 @@ __device__ bool grid_sync(const RowsArgs &a, unsigned &target, int *flag_s) {
     return *flag_s != 0;
 }
 
-// 16-byte asynchronous copy global -> shared (L1 bypassed).
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_addr(dst)), "l"(src) : "memory");
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *mbar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}\n" ::"r"(
+                     tc::smem_addr(mbar)),
+                 "r"(bytes)
+                 : "memory");
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+// Box of a 3-D / 2-D tensor map (coordinates innermost first) into shared memory, completing on the mbarrier.
+__device__ __forceinline__ void tma_load3(void *dst, const void *tmap, int x, int y, int z, uint64_t *mbar,
+                                          uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(tc::smem_addr(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(tc::smem_addr(mbar)), "l"(pol)
+        : "memory");
 }
-// Wait until at most `newer` of this thread's commit groups are still in flight.
-__device__ __forceinline__ void cp_async_wait_newer(int newer) {
-    switch (newer) {
-        case 0: cp_async_wait<0>(); break;
-        case 1: cp_async_wait<1>(); break;
-        case 2: cp_async_wait<2>(); break;
-        case 3: cp_async_wait<3>(); break;
-        case 4: cp_async_wait<4>(); break;
-        case 5: cp_async_wait<5>(); break;
-        case 6: cp_async_wait<6>(); break;
-        case 7: cp_async_wait<7>(); break;
-        case 8: cp_async_wait<8>(); break;
-        case 9: cp_async_wait<9>(); break;
-        case 10: cp_async_wait<10>(); break;
-        case 11: cp_async_wait<11>(); break;
-        case 12: cp_async_wait<12>(); break;
-        case 13: cp_async_wait<13>(); break;
-        case 14: cp_async_wait<14>(); break;
-        default: cp_async_wait<0>(); break;
-    }
+__device__ __forceinline__ void tma_load2(void *dst, const void *tmap, int x, int y, uint64_t *mbar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(tc::smem_addr(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(tc::smem_addr(mbar)), "l"(pol)
+        : "memory");
+}
+// Contiguous bytes (16-byte aligned, a multiple of 16) into shared memory, completing on the mbarrier.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *mbar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            tc::smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(tc::smem_addr(mbar)), "l"(pol)
+        : "memory");
 }
 
 template <int VB>
@@ -155,72 +163,91 @@ template <int KV, int HD, int RM>
 struct Stage {
     using C = Cfg<KV, HD, RM>;
     const RowsArgs &a;
+    const RowsLayer *lay;  // the per-layer pointers, in shared memory
+    const int4 *tcache;    // this CTA's tile descriptors (the first TCACHE), in shared memory
     uint8_t *ring;
+    uint64_t *mbar;
     float *scr;
     int *flag_s;
     int t0, n, total;     // this CTA's tiles [t0, t0 + n) of every layer; total = L n tiles in its sequence
-    int consumed = 0;     // next tile of the sequence to use (those below consumed + slots are issued)
-    unsigned target = 0;  // the grid barrier's next target
-    uint64_t pol_w;
+    int consumed = 0;     // next tile of the sequence to use
+    int issued = 0;       // tiles of the sequence whose copies have started (at most consumed + slots)
+    unsigned phase = 0;   // per slot, the parity of its mbarrier's next phase
+    unsigned target = 0;  // the grid barrier's latest target
+    uint64_t pol_kv, pol_w;
 
-    __device__ Stage(const RowsArgs &a_, uint8_t *smem, int *flag) : a(a_), flag_s(flag) {
+    __device__ Stage(const RowsArgs &a_, uint8_t *smem_in, int *flag, const RowsLayer *lay_, const int4 *tcache_)
+        : a(a_), lay(lay_), tcache(tcache_), flag_s(flag) {
+        // tensor loads want 128-byte aligned destinations
+        uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_in) + 127) & ~(uintptr_t)127);
         ring = smem;
-        scr = reinterpret_cast<float *>(smem + (size_t)a.slots * C::SLOT);
+        mbar = reinterpret_cast<uint64_t *>(smem + (size_t)a.slots * C::SLOT);
+        scr = reinterpret_cast<float *>(smem + (size_t)a.slots * C::SLOT + 128);
         const int G = gridDim.x, c = blockIdx.x;
         t0 = (int)((long long)a.ntiles * c / G);
         n = (int)((long long)a.ntiles * (c + 1) / G) - t0;
         total = a.L * n;
+        pol_kv = policy_evict_first();
         pol_w = policy_evict_last();
     }
 
-    __device__ __forceinline__ int4 tile_of(int g) const { return a.tiles[t0 + g % n]; }
-    __device__ __forceinline__ bool sync() { return grid_sync(a, target, flag_s); }
+    __device__ __forceinline__ int4 tile_of(int g) const {
+        const int i = g % n;
+        return i < TCACHE ? tcache[i] : a.tiles[t0 + i];
+    }
+    __device__ __forceinline__ void arrive() { grid_arrive(a, target); }
+    __device__ __forceinline__ bool wait() { return grid_wait(a, target, flag_s); }
+    // Start the copies of the next tiles of the sequence, up to `limit`, into the slots that are free.
+    __device__ void issue_upto(int limit) {
+        limit = min(limit, min(total, consumed + a.slots));
+        for (; issued < limit; issued++) issue(issued);
+    }
 
-    // All threads: start the copies of sequence tile g into its slot, 16 bytes per copy, eight threads along each
-    // coordinate's row, as one commit group (empty for tiles whose rows are not 16-byte aligned: those are copied
+    // Thread 0: start the loads of sequence tile g into its slot (tiles whose rows are not 16-byte aligned are copied
     // when used instead).
     __device__ void issue(int g) {
-        if (g >= total) return;
+        if (threadIdx.x != 0 || g >= total) return;
         const int4 tl = tile_of(g);
-        if (!(tl.w >> 16)) {
-            cp_async_commit();
-            return;
-        }
-        const int h = tl.w & 0xffff, ci = tl.x, k0 = tl.y, len = tl.z;
-        const int rc = min(a.chunk, a.rows - ci * a.chunk);
-        const uint8_t *rec = a.layers[g / n].cache + (size_t)ci * a.full;
-        const uint8_t *body = rec + (KV ? 8 * (size_t)a.d : 0);
+        if (!(tl.w >> 16)) return;
+        const int h = tl.w & 0xffff, ci = tl.x, x = tl.y * C::W, l = g / n;
+        const uint8_t *rec = lay[l].cache + (size_t)ci * a.full;
         uint8_t *slot = ring + (size_t)(g % a.slots) * C::SLOT;
-        const int pieces = len * C::W / 16;  // of each row
-#pragma unroll
-        for (int it = 0; it < 2 * HD * C::CPR / THREADS; it++) {
-            const int idx = threadIdx.x + it * THREADS;
-            const int row = idx / C::CPR, c = idx % C::CPR;
-            if (c < pieces) {
-                const int coord = row < HD ? h * HD + row : a.d + h * HD + (row - HD);
-                cp_async16(slot + row * C::ROWB + c * 16, body + ((size_t)coord * rc + k0) * C::W + c * 16);
-            }
+        uint64_t *mb = mbar + g % a.slots;
+        tc::fence_async_smem();  // the slot's earlier reads (generic proxy) before the loads (async proxy)
+        mbar_expect_tx(mb, 2u * HD * C::ROWB + (KV ? 8u * HD : 0u));
+        const uint8_t *maps = reinterpret_cast<const uint8_t *>(a.tmaps) + (size_t)l * 256;
+        if (ci < a.nfull) {
+            tma_load3(slot, maps, x, h * HD, ci, mb, pol_kv);
+            tma_load3(slot + HD * C::ROWB, maps, x, a.d + h * HD, ci, mb, pol_kv);
+        } else {
+            tma_load2(slot, maps + 128, x, h * HD, mb, pol_kv);
+            tma_load2(slot + HD * C::ROWB, maps + 128, x, a.d + h * HD, mb, pol_kv);
         }
-        if (KV && threadIdx.x < HD / 2) {
-            const int i = threadIdx.x;  // 16-byte pieces: key scales, then value scales
-            const size_t off = i < HD / 4 ? (size_t)h * HD * 4 + i * 16 : ((size_t)a.d + h * HD) * 4 + (i - HD / 4) * 16;
-            cp_async16(slot + 2 * HD * C::ROWB + i * 16, rec + off);
+        if (KV) {
+            bulk_load(slot + 2 * HD * C::ROWB, rec + (size_t)h * HD * 4, HD * 4, mb, pol_kv);
+            bulk_load(slot + 2 * HD * C::ROWB + 4 * HD, rec + ((size_t)a.d + h * HD) * 4, HD * 4, mb, pol_kv);
         }
-        cp_async_commit();
     }
 
     // All threads: wait for sequence tiles [g0, g0 + nb), the next ones to use; then copy those that could not be
     // copied asynchronously.
-    __device__ void acquire(int g0, int nb) {
-        const int issued = min(total, consumed + a.slots);
-        cp_async_wait_newer(issued - (g0 + nb));
-        __syncthreads();
-        bool copied = false;
+    __device__ bool acquire(int g0, int nb) {
+        bool ok = true;
         for (int b = 0; b < nb; b++) {
-            const int4 tl = tile_of(g0 + b);
-            if (!(tl.w >> 16)) copy_now(g0 + b, tl), copied = true;
+            const int g = g0 + b, s = g % a.slots;
+            const int4 tl = tile_of(g);
+            if (tl.w >> 16) {
+                ok = tc::mbar_wait(mbar + s, (phase >> s) & 1u, SPIN_LIMIT) && ok;
+                phase ^= 1u << s;
+            } else {
+                copy_now(g, tl);
+            }
         }
-        if (copied) __syncthreads();
+        if (!__syncthreads_and(ok)) {
+            if (threadIdx.x == 0) atomicExch(a.err, 1);
+            return false;
+        }
+        return true;
     }
 
     __device__ void copy_now(int g, const int4 &tl) {
@@ -228,7 +255,7 @@ struct Stage {
         // rows not 16-byte aligned: element copies by all threads
         const int h = tl.w & 0xffff, ci = tl.x, k0 = tl.y, len = tl.z;
         const int rc = min(a.chunk, a.rows - ci * a.chunk);
-        const uint8_t *rec = a.layers[g / n].cache + (size_t)ci * a.full;
+        const uint8_t *rec = lay[g / n].cache + (size_t)ci * a.full;
         const uint8_t *body = rec + (KV ? 8 * (size_t)a.d : 0);
         uint8_t *slot = ring + (size_t)s * C::SLOT;
         for (int i = threadIdx.x; i < 2 * HD * len; i += THREADS) {
@@ -251,8 +278,15 @@ struct Stage {
         }
     }
 
-    // Leaving early: this thread's copies still in flight land first.
-    __device__ void drain() { cp_async_wait<0>(); }
+    // Leaving early: wait (bounded) for this CTA's loads still in flight.
+    __device__ void drain() {
+        for (int g = consumed; g < issued; g++) {
+            if (!(tile_of(g).w >> 16)) continue;
+            const int s = g % a.slots;
+            tc::mbar_wait(mbar + s, (phase >> s) & 1u, SPIN_LIMIT);
+            phase ^= 1u << s;
+        }
+    }
 
     // One linear phase: y[r][o] (=|+=) act(W[o] . LN?(x[r]) + b[o]) for this CTA's outputs o (a contiguous share of
     // N), one warp per output; the lanes hold 4-float pieces k = 4 lane + 128 v of the weight row, as the few-row
@@ -260,7 +294,7 @@ struct Stage {
     // are loaded before the barrier (when `wait`) that makes x ready; x (rows written by other CTAs in this launch)
     // is read through L2.
     template <bool LN>
-    __device__ bool linear(bool wait, const float *x, int K, const float *lnw, const float *lnb, const float *W,
+    __device__ bool linear(bool wait_first, const float *x, int K, const float *lnw, const float *lnb, const float *W,
                            const float *b, int N, int act, float *y, int ldy, bool residual) {
         float *xs = scr + C::XS, *lw_s = scr + C::LNW, *lb_s = scr + C::LNB;
         const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, R = a.R;
@@ -282,7 +316,7 @@ struct Stage {
             for (int i = 0; i < KMAX / THREADS; i++)
                 if (tid + i * THREADS < K) lw[i] = lnw[tid + i * THREADS], lb[i] = lnb[tid + i * THREADS];
         }
-        if (wait && !sync()) return false;
+        if (wait_first && !wait()) return false;
         const int k4 = K >> 2;
         for (int i = tid; i < R * k4; i += THREADS) {
             const int r = i / k4, c = i - r * k4;
@@ -351,6 +385,7 @@ struct Stage {
                 }
             }
         }
+        arrive();
         return true;
     }
 
@@ -439,11 +474,27 @@ struct Stage {
         __syncthreads();
     }
 
-    // The last CTA to finish head h: log-sum-exp merge of the head's partial states into att (nn.rs:261-286).
+    // The last CTA to finish head h: log-sum-exp merge of the head's partial states into att (nn.rs:261-286). The
+    // partial sums are loaded first (all in flight at once), the part weights computed meanwhile.
     __device__ void merge(int h) {
-        float *wts = scr + C::WTS, *sinv = scr + C::SINV;
+        float *wts = scr + C::WTS, *sinv = scr + C::SINV, *half = scr + C::RED;
         const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, R = a.R, H = a.heads;
         const int lo = a.part_lo[h], np = a.part_hi[h] - lo + 1;
+        const size_t step = (size_t)H * R * HD;  // between the parts of consecutive CTAs
+        const int outs = R * HD, groups = outs <= THREADS / 2 ? THREADS / outs : 1;
+        constexpr int MP = 24;
+        // thread: output (r, j) and a group of the parts (p = gi + groups k)
+        const int oi = tid % outs, gi = tid / outs;
+        const bool fast = groups > 1 && gi < groups;
+        float v[MP];
+        if (fast) {
+            const float *pa = a.part_acc + ((size_t)lo * H + h) * R * HD + oi;
+#pragma unroll
+            for (int k = 0; k < MP; k++) {
+                const int p = gi + groups * k;
+                v[k] = p < np ? __ldcg(pa + p * step) : 0.f;
+            }
+        }
         if (warp < R) {
             const int r = warp;
             float M = -FLT_MAX;
@@ -460,27 +511,48 @@ struct Stage {
             if (lane == 0) sinv[r] = 1.0f / S;
         }
         __syncthreads();
-        for (int i = tid; i < R * HD; i += THREADS) {
-            const int r = i / HD, j = i - r * HD;
-            const float *pa = a.part_acc + (((size_t)lo * H + h) * R + r) * HD + j;
-            const size_t step = (size_t)H * R * HD;
-            float o = 0.f;
+        if (groups > 1) {
+            if (fast) {
+                const int r = oi / HD;
+                const float *pa = a.part_acc + ((size_t)lo * H + h) * R * HD + oi;
+                float o = 0.f;
+#pragma unroll
+                for (int k = 0; k < MP; k++) {
+                    const int p = gi + groups * k;
+                    if (p < np) o = fmaf(wts[r * ROWS_MAX_GRID + p], v[k], o);
+                }
+                for (int p = gi + groups * MP; p < np; p += groups) o = fmaf(wts[r * ROWS_MAX_GRID + p], __ldcg(pa + p * step), o);
+                half[gi * outs + oi] = o;
+            }
+            __syncthreads();
+            for (int i = tid; i < outs; i += THREADS) {
+                float o = 0.f;
+                for (int g = 0; g < groups; g++) o += half[g * outs + i];
+                const int r = i / HD, j = i - r * HD;
+                a.att[(size_t)r * a.d + h * HD + j] = o * sinv[r];
+            }
+        } else {
+            for (int i = tid; i < outs; i += THREADS) {
+                const int r = i / HD, j = i - r * HD;
+                const float *pa = a.part_acc + (((size_t)lo * H + h) * R + r) * HD + j;
+                float o = 0.f;
 #pragma unroll 8
-            for (int p = 0; p < np; p++) o = fmaf(wts[r * ROWS_MAX_GRID + p], __ldcg(pa + p * step), o);
-            a.att[(size_t)r * a.d + h * HD + j] = o * sinv[r];
+                for (int p = 0; p < np; p++) o = fmaf(wts[r * ROWS_MAX_GRID + p], __ldcg(pa + p * step), o);
+                a.att[(size_t)r * a.d + h * HD + j] = o * sinv[r];
+            }
         }
         __syncthreads();
     }
 
     // Phase B of layer l.
     __device__ bool attend(int l) {
-        const RowsLayer &Ly = a.layers[l];
+        const RowsLayer &Ly = lay[l];
         const int Th = a.tiles_per_head;
         {
             // the first head's query MLP weights load while the barrier completes
             QueryW qw;
             query_load(Ly, t0 / Th, qw);
-            if (!sync()) return false;  // q is ready
+            if (!wait()) return false;  // q is ready
             query_head(t0 / Th, qw);
         }
         float *qm = scr + C::QM, *red = scr + C::RED, *psm = scr + C::PSM, *alpha = scr + C::ALPHA;
@@ -502,7 +574,7 @@ struct Stage {
                 const int nb = min(min(C::BMAX, a.slots), te - t);
                 const int g0 = l * n + (t - t0);
                 if (tid < nb) lens[tid] = tile_of(g0 + tid).z;
-                acquire(g0, nb);
+                if (!acquire(g0, nb)) return false;
                 // scores: integer keys take the query times the chunk's key scales (predict.rs:486-497)
                 for (int b = 0; b < nb; b++) {
                     const uint8_t *slot = ring + (size_t)((g0 + b) % a.slots) * C::SLOT;
@@ -544,49 +616,93 @@ struct Stage {
                     }
                 }
                 __syncthreads();
-                // online softmax, one warp per row, with the reference's rescaling rule (nn.rs:207-215)
-                if (warp < RM) {
-                    const int r = warp;
-                    if (r < R) {
-                        float sc[C::BT / 32];
-                        float mx = -FLT_MAX;
+                // online softmax with the reference's rescaling rule (nn.rs:207-215): one row over all eight warps, or
+                // one warp per row
+                float al_one = 1.f;
+                if constexpr (RM == 1) {
+                    float *bm = scr + C::BMS, *bs = bm + 8;
+                    constexpr int KPT = C::BT / THREADS > 0 ? C::BT / THREADS : 1;
+                    float sc[KPT];
+                    bool ok[KPT];
+                    float mx = -FLT_MAX;
 #pragma unroll
-                        for (int kk = 0; kk < C::BT / 32; kk++) {
-                            const int k = lane + 32 * kk;
-                            const float *rr = red + r * C::BT + k;
-                            const int ws = RM * C::BT;
-                            const float s = ((rr[0] + rr[ws]) + (rr[2 * ws] + rr[3 * ws])) +
-                                            ((rr[4 * ws] + rr[5 * ws]) + (rr[6 * ws] + rr[7 * ws]));
-                            sc[kk] = s;
-                            if (k < nb * C::TK && (k % C::TK) < lens[k / C::TK]) mx = fmaxf(mx, s);
+                    for (int q = 0; q < KPT; q++) {
+                        const int k = tid + THREADS * q;
+                        ok[q] = k < C::BT && k < nb * C::TK && (k % C::TK) < lens[k / C::TK];
+                        float s = 0.f;
+                        if (k < C::BT) {
+                            const float *rr = red + k;
+                            s = ((rr[0] + rr[C::BT]) + (rr[2 * C::BT] + rr[3 * C::BT])) +
+                                ((rr[4 * C::BT] + rr[5 * C::BT]) + (rr[6 * C::BT] + rr[7 * C::BT]));
                         }
-                        mx = warp_max(mx);
-                        float al;
-                        if (first) {
-                            m_run = mx, s_run = 0.f, al = 0.f;
-                        } else if (mx > m_run) {
-                            al = exp1(m_run - mx), m_run = mx;
-                        } else {
-                            al = 1.f;
-                        }
-                        float sum = 0.f;
-#pragma unroll
-                        for (int kk = 0; kk < C::BT / 32; kk++) {
-                            const int k = lane + 32 * kk;
-                            const bool valid = k < nb * C::TK && (k % C::TK) < lens[k / C::TK];
-                            const float pk = valid ? exp1(sc[kk] - m_run) : 0.f;
-                            psm[r * C::BT + k] = pk;
-                            sum += pk;
-                        }
-                        s_run = s_run * al + warp_sum(sum);
-                        if (lane == 0) alpha[r] = al;
-                    } else {
-#pragma unroll
-                        for (int kk = 0; kk < C::BT / 32; kk++) psm[r * C::BT + lane + 32 * kk] = 0.f;
-                        if (lane == 0) alpha[r] = 1.f;
+                        sc[q] = s;
+                        if (ok[q]) mx = fmaxf(mx, s);
                     }
+                    mx = warp_max(mx);
+                    if (lane == 0) bm[warp] = mx;
+                    __syncthreads();
+                    mx = fmaxf(fmaxf(fmaxf(bm[0], bm[1]), fmaxf(bm[2], bm[3])), fmaxf(fmaxf(bm[4], bm[5]), fmaxf(bm[6], bm[7])));
+                    if (first) {
+                        m_run = mx, s_run = 0.f, al_one = 0.f;
+                    } else if (mx > m_run) {
+                        al_one = exp1(m_run - mx), m_run = mx;
+                    }
+                    float sum = 0.f;
+#pragma unroll
+                    for (int q = 0; q < KPT; q++) {
+                        const int k = tid + THREADS * q;
+                        const float pk = ok[q] ? exp1(sc[q] - m_run) : 0.f;
+                        if (k < C::BT) psm[k] = pk;
+                        sum += pk;
+                    }
+                    sum = warp_sum(sum);
+                    if (lane == 0) bs[warp] = sum;
+                    __syncthreads();
+                    s_run = s_run * al_one + (((bs[0] + bs[1]) + (bs[2] + bs[3])) + ((bs[4] + bs[5]) + (bs[6] + bs[7])));
+                } else {
+                    if (warp < RM) {
+                        const int r = warp;
+                        if (r < R) {
+                            float sc[C::BT / 32];
+                            float mx = -FLT_MAX;
+#pragma unroll
+                            for (int kk = 0; kk < C::BT / 32; kk++) {
+                                const int k = lane + 32 * kk;
+                                const float *rr = red + r * C::BT + k;
+                                const int ws = RM * C::BT;
+                                const float s = ((rr[0] + rr[ws]) + (rr[2 * ws] + rr[3 * ws])) +
+                                                ((rr[4 * ws] + rr[5 * ws]) + (rr[6 * ws] + rr[7 * ws]));
+                                sc[kk] = s;
+                                if (k < nb * C::TK && (k % C::TK) < lens[k / C::TK]) mx = fmaxf(mx, s);
+                            }
+                            mx = warp_max(mx);
+                            float al;
+                            if (first) {
+                                m_run = mx, s_run = 0.f, al = 0.f;
+                            } else if (mx > m_run) {
+                                al = exp1(m_run - mx), m_run = mx;
+                            } else {
+                                al = 1.f;
+                            }
+                            float sum = 0.f;
+#pragma unroll
+                            for (int kk = 0; kk < C::BT / 32; kk++) {
+                                const int k = lane + 32 * kk;
+                                const bool valid = k < nb * C::TK && (k % C::TK) < lens[k / C::TK];
+                                const float pk = valid ? exp1(sc[kk] - m_run) : 0.f;
+                                psm[r * C::BT + k] = pk;
+                                sum += pk;
+                            }
+                            s_run = s_run * al + warp_sum(sum);
+                            if (lane == 0) alpha[r] = al;
+                        } else {
+#pragma unroll
+                            for (int kk = 0; kk < C::BT / 32; kk++) psm[r * C::BT + lane + 32 * kk] = 0.f;
+                            if (lane == 0) alpha[r] = 1.f;
+                        }
+                    }
+                    __syncthreads();
                 }
-                __syncthreads();
                 // weighted values; integer values take the chunk's value scales after the sum (nn.rs:253-256)
                 {
                     float x[C::DPT][RM];
@@ -636,13 +752,13 @@ struct Stage {
                             tot += __shfl_xor_sync(0xffffffffu, tot, 4);
                         }
                         const int r = RM == 8 ? v : 0;
-                        if (r < R && (RM == 8 || v == 0)) acc[i] = acc[i] * alpha[r] + tot;
+                        if (r < R && (RM == 8 || v == 0)) acc[i] = acc[i] * (RM == 1 ? al_one : alpha[r]) + tot;
                     }
                 }
                 __syncthreads();  // the slots and the scratch are free again
-                for (int b = 0; b < nb; b++) issue(g0 + b + a.slots);
                 consumed = g0 + nb;
                 t += nb;
+                issue_upto((l + 1) * n);  // this layer's later tiles now; the next layer's after the barrier arrival
             }
             // this CTA's partial state of head h, then the head's arrival count
             const int pi = blockIdx.x * a.heads + h;
@@ -669,6 +785,8 @@ struct Stage {
                 merge(h);
             }
         }
+        arrive();
+        issue_upto(total);
         return true;
     }
 };
@@ -677,12 +795,26 @@ template <int KV, int HD, int RM>
 __global__ void __launch_bounds__(THREADS, 1) k_stage_rows(const RowsArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ int flag_s;
-    Stage<KV, HD, RM> st(a, smem, &flag_s);
+    __shared__ RowsLayer lay[ROWS_MAX_LAYERS];
+    __shared__ int4 tcache[TCACHE];
+    Stage<KV, HD, RM> st(a, smem, &flag_s, lay, tcache);
     const int tid = threadIdx.x, d = a.d;
-    for (int g = 0; g < min(a.slots, st.total); g++) st.issue(g);
+    if (tid == 0) {
+        for (int i = 0; i < a.slots; i++) tc::mbar_init(st.mbar + i, 1);
+        tc::mbar_init_fence();
+    }
+    // the pointer table and this CTA's tile descriptors, read once
+    {
+        const unsigned long long *src = reinterpret_cast<const unsigned long long *>(a.layers);
+        unsigned long long *dst = reinterpret_cast<unsigned long long *>(lay);
+        for (int i = tid; i < a.L * (int)(sizeof(RowsLayer) / 8); i += THREADS) dst[i] = src[i];
+        for (int i = tid; i < min(st.n, TCACHE); i += THREADS) tcache[i] = a.tiles[st.t0 + i];
+    }
+    __syncthreads();
+    st.issue_upto(st.total);
     bool ok = true;
     for (int l = 0; l < a.L && ok; l++) {
-        const RowsLayer &Ly = a.layers[l];
+        const RowsLayer &Ly = lay[l];
         if (blockIdx.x == 0 && tid < a.heads) a.head_cnt[tid] = 0;  // used after the next barrier
         ok = st.template linear<true>(l > 0, a.h, d, Ly.n1w, Ly.n1b, Ly.wq, Ly.bq, d, 0, a.q, d, false);
         ok = ok && st.attend(l);
@@ -699,7 +831,7 @@ __global__ void __launch_bounds__(THREADS, 1) k_stage_rows(const RowsArgs a) {
 template <int KV, int HD, int RM>
 size_t smem_of(int slots) {
     using C = Cfg<KV, HD, RM>;
-    return (size_t)slots * C::SLOT + sizeof(float) * (size_t)C::SCRATCH;
+    return 128 + (size_t)slots * C::SLOT + 128 + sizeof(float) * (size_t)C::SCRATCH;
 }
 
 template <int KV, int HD, int RM>
