@@ -169,6 +169,39 @@ TCU_API int tcu_selftest_mma(tcu_ctx *ctx, double *max_err);
  * a CUDA graph re-record the same events each replay, so for them the count covers the last replay. */
 TCU_API int tcu_profile(tcu_ctx *ctx, int enable, double *attend_ms, uint64_t *attend_launches);
 
+/* ---- several devices (no counterpart in the reference, which runs on one device) ----------------------------------
+ *
+ * A cache too large for one device, or wanted faster, is split along its training rows: device g holds whole chunks
+ * [c0_g, c1_g) of every layer (tcu_model_slice). The chunk records are unchanged, so a shard is an ordinary cache of
+ * fewer rows; it keeps the full cache's query scales (they depend on the full row count, src/nn.rs:97-107). In the
+ * stage each device attends over its own rows and the partial softmax states (max, weight sum, weighted values;
+ * src/nn.rs:187-286) are merged over all devices after every layer: an all-reduce (max) of the maxima, a rescale to
+ * the common max, an all-reduce (sum) of the states, a division. Everything else runs on every device alike.
+ *
+ * tcu_comm wraps an NCCL communicator over the devices (libnccl.so.2 is loaded when the first one is made). Rank 0
+ * makes the id with tcu_comm_unique_id and passes it to the other ranks out of band (torch.distributed, MPI, a
+ * file); every rank then calls tcu_comm_init with it, which returns once all have joined. Every rank must take the
+ * same collective steps in the same order: call the sharded stage with the same rows and out_n everywhere. */
+typedef struct tcu_comm tcu_comm;
+#define TCU_COMM_ID_BYTES 128
+TCU_API int tcu_comm_unique_id(uint8_t id[TCU_COMM_ID_BYTES]);
+TCU_API int tcu_comm_init(tcu_ctx *ctx, const uint8_t id[TCU_COMM_ID_BYTES], int nranks, int rank, tcu_comm **out);
+TCU_API void tcu_comm_free(tcu_comm *c);
+/* Sum `count` doubles over all ranks in place (device buffer), e.g. per-rank class-logit sums of ensemble members
+ * placed one per device. Queued on `stream` (NULL: the context's stream). */
+TCU_API int tcu_comm_allreduce_f64(tcu_comm *c, double *buf, size_t count, void *stream);
+/* Wait up to timeout_ms for `stream` (NULL: the context's stream); on timeout the communicator is aborted, so that
+ * collectives still waiting for a lost rank end, and TCU_ERR_CUDA is returned. The communicator is unusable after. */
+TCU_API int tcu_comm_wait(tcu_comm *c, void *stream, int timeout_ms);
+
+/* A new resident cache holding chunks [first_chunk, first_chunk + nchunks) of `m` (device-to-device copies) with
+ * m's query scales. */
+TCU_API int tcu_model_slice(const tcu_model *m, int first_chunk, int nchunks, tcu_model **out);
+/* The stage of `rows` rows (h, out device buffers as in tcu_stage_device) with the attention of every layer merged
+ * over the ranks of `c`; `m` holds this rank's shard. Queued on `stream` (NULL: the context's stream). */
+TCU_API int tcu_stage_sharded_device(tcu_model *m, tcu_comm *c, const float *h, int rows, int out_n, float *out,
+                                     void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -84,6 +84,13 @@ def lib():
         "tcu_selftest_mma": (_c_int, [_c_void, P(ctypes.c_double)]),
         "tcu_attend_noalloc": (_c_int, [_c_int, _c_int, _c_int, _c_void, _c_int, _c_int, _c_void, _c_int, _c_void,
                                         _c_void, ctypes.c_char_p, _c_size]),
+        "tcu_comm_unique_id": (_c_int, [ctypes.c_char_p]),
+        "tcu_comm_init": (_c_int, [_c_void, ctypes.c_char_p, _c_int, _c_int, P(_c_void)]),
+        "tcu_comm_free": (None, [_c_void]),
+        "tcu_comm_allreduce_f64": (_c_int, [_c_void, _c_void, _c_size, _c_void]),
+        "tcu_comm_wait": (_c_int, [_c_void, _c_void, _c_int]),
+        "tcu_model_slice": (_c_int, [_c_void, _c_int, _c_int, P(_c_void)]),
+        "tcu_stage_sharded_device": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_void, _c_void]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -272,6 +279,16 @@ class VramModel:
     def stage_device(self, h_ptr, rows, out_n, out_ptr, stream=None):
         return self.gpu.check(lib().tcu_stage_device(self._h, h_ptr, rows, out_n, out_ptr, stream))
 
+    def slice(self, first_chunk, nchunks):
+        """A new resident cache of chunks [first_chunk, first_chunk + nchunks) (a shard of the training rows)."""
+        h = _c_void()
+        self.gpu.check(lib().tcu_model_slice(self._h, first_chunk, nchunks, ctypes.byref(h)))
+        return VramModel(self.weights, h)
+
+    def stage_sharded_device(self, comm, h_ptr, rows, out_n, out_ptr, stream=None):
+        """The stage with this cache one shard of the training rows: every layer's attention merged over `comm`."""
+        return self.gpu.check(lib().tcu_stage_sharded_device(self._h, comm._h, h_ptr, rows, out_n, out_ptr, stream))
+
     def layer_bytes(self, layer, nbytes):
         out = np.empty(nbytes, dtype=np.uint8)
         self.gpu.check(lib().tcu_model_get_layer(self._h, layer, out.ctypes.data, nbytes))
@@ -293,6 +310,53 @@ class VramModel:
             self.free()
         except Exception:
             pass
+
+
+COMM_ID_BYTES = 128
+
+
+def comm_unique_id():
+    """A fresh id for a communicator over several devices (make it on rank 0, hand it to the others)."""
+    buf = ctypes.create_string_buffer(COMM_ID_BYTES)
+    r = lib().tcu_comm_unique_id(buf)
+    if r != OK:
+        raise TcuError(r, "cannot make a communicator id (is libnccl.so.2 installed?)")
+    return buf.raw
+
+
+class Comm:
+    """A communicator over the devices of several processes, one rank per device (no reference counterpart)."""
+
+    def __init__(self, gpu, uid, nranks, rank):
+        assert len(uid) == COMM_ID_BYTES
+        self.gpu, self._h = gpu, _c_void()
+        gpu.check(lib().tcu_comm_init(gpu._h, uid, nranks, rank, ctypes.byref(self._h)))
+        self.nranks, self.rank = nranks, rank
+
+    def allreduce_f64(self, ptr, count, stream=None):
+        return self.gpu.check(lib().tcu_comm_allreduce_f64(self._h, ptr, count, stream))
+
+    def wait(self, timeout_ms, stream=None):
+        return self.gpu.check(lib().tcu_comm_wait(self._h, stream, int(timeout_ms)))
+
+    def free(self):
+        if self._h:
+            lib().tcu_comm_free(self._h)
+            self._h = _c_void()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def shard_chunks(nchunks, world, rank):
+    """Rank `rank`'s contiguous share (first chunk, chunks) of `nchunks` stored chunks over `world` devices: the
+    first nchunks % world ranks take one more."""
+    base, extra = divmod(nchunks, world)
+    first = rank * base + min(rank, extra)
+    return first, base + (1 if rank < extra else 0)
 
 
 def attend_noalloc(kv, d, heads, layer_ptr, rows, chunk, q_ptr, nq, out_ptr, stream=None):

@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
     const int r = r0 + orow;
     if (r < a.R) {
         const float oun = pow2f(-14 - a.tc_eV);
-        if (a.splits == 1) {
+        if (a.splits == 1 && !a.parts_only) {
             const float inv = ok ? 1.0f / lrow[orow] : 0.f;
             float *dst = a.out + (size_t)r * a.ldo + h * HD + ocol;
 #pragma unroll
@@ -309,7 +309,7 @@ cudaError_t launch_attend_tc(int kv, const AttnArgs &a, cudaStream_t s, uint64_t
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (launches) ++*launches;
-    if (a.splits > 1) return launch_attend_merge(a, a.splits, s, launches);
+    if (a.splits > 1 && !a.parts_only) return launch_attend_merge(a, a.splits, s, launches);
     return cudaSuccess;
 }
 

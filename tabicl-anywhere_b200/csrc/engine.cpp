@@ -5,6 +5,11 @@
 
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <thread>
 
 #include <cmath>
 #include <cstdlib>
@@ -127,6 +132,7 @@ struct tcu_model {
     bool tc_scanned = false;
     // working memory, grown to the largest call so far
     DevBuf h, q, att, mid, stats, out, part_ms, part_acc;
+    DevBuf sh_m, sh_mall, sh_packed;  // the cross-device merge: local maxima, their maximum, (values, weight sums)
     // the one-kernel few-row stage: key tiles (head-major), per-layer pointer table, barrier words, partials
     DevBuf rtiles, rlayers, rsync, rparts_ms, rparts_acc, rtmaps;
     int rtiles_n = 0, rtiles_per_head = 0;
@@ -149,6 +155,45 @@ struct tcu_model {
     ~tcu_model() {
         for (auto &g : graphs) cudaGraphExecDestroy(g.exec);
     }
+};
+
+// NCCL, loaded when the first communicator is made (the library does not link it).
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+    const char *(*error_string)(ncclResult_t) = nullptr;
+    std::string why;
+};
+static const NcclApi &nccl_api() {
+    static const NcclApi api = [] {
+        NcclApi a;
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            a.why = std::string("cannot load libnccl.so.2: ") + dlerror();
+            return a;
+        }
+        a.get_unique_id = reinterpret_cast<decltype(a.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+        a.comm_init_rank = reinterpret_cast<decltype(a.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+        a.comm_destroy = reinterpret_cast<decltype(a.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+        a.comm_abort = reinterpret_cast<decltype(a.comm_abort)>(dlsym(h, "ncclCommAbort"));
+        a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
+        a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
+        if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.comm_abort || !a.all_reduce || !a.error_string)
+            a.why = "libnccl.so.2 lacks an entry point";
+        return a;
+    }();
+    return api;
+}
+
+struct tcu_comm {
+    tcu_ctx *ctx = nullptr;
+    ncclComm_t comm = nullptr;
+    int nranks = 1, rank = 0;
+    bool aborted = false;
 };
 
 // ---- handle lifetimes: a context lives while its weights do, weights while their models do --------------------
@@ -561,7 +606,7 @@ static void ensure_work(tcu_model *m, int R) {
     moved |= m->mid.ensure(sizeof(float) * R * wide);
     moved |= m->stats.ensure(sizeof(float) * R * 4);
     const Plan plan = attend_plan(m->w->ctx, R, s.heads, s.d / s.heads, m->nitems, m->ntiles);
-    const size_t pr = plan.path == Path::Decode ? (size_t)m->nitems : (plan.splits > 1 ? (size_t)plan.splits : 0);
+    const size_t pr = plan.path == Path::Decode ? (size_t)m->nitems : (size_t)plan.splits;  // parts, when left
     if (pr) {
         moved |= m->part_ms.ensure(sizeof(float) * pr * R * H * 2);
         moved |= m->part_acc.ensure(sizeof(float) * pr * R * d);
@@ -570,15 +615,17 @@ static void ensure_work(tcu_model *m, int R) {
 }
 
 // attention of R scaled queries q (device, [R][d]) against a layer given in stored form; out [R][d]
-static void attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int rows, int chunk, int kv, const int2 *items,
-                         int nitems, const int4 *tiles, int ntiles, const float *q, int R, float *out, cudaStream_t s,
-                         int eK = 0, int eV = 0) {
+// Returns the number of parts left in part_ms / part_acc when parts_only (the outputs are not finished then).
+static int attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int rows, int chunk, int kv, const int2 *items,
+                        int nitems, const int4 *tiles, int ntiles, const float *q, int R, float *out, cudaStream_t s,
+                        int eK = 0, int eV = 0, bool parts_only = false) {
     const auto &sh = m->w->shape;
     AttnArgs a;
     a.layer = layer, a.rows = rows, a.chunk = chunk, a.d = sh.d, a.heads = sh.heads;
     a.full = record_bytes(kv, sh.d, chunk);
     a.q = q, a.ldq = sh.d, a.R = R, a.out = out, a.ldo = sh.d;
     a.part_ms = m->part_ms.as<float>(), a.part_acc = m->part_acc.as<float>();
+    a.parts_only = parts_only ? 1 : 0;
     const int hd = sh.d / sh.heads;
     Launch ck{ctx, s};
     cudaEvent_t ev_end = nullptr;
@@ -610,17 +657,18 @@ static void attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int r
     if (plan.path == Path::Decode) {
         a.items = items, a.nitems = nitems;
         ck(launch_attend_decode(kv, hd, a, s, &ctx->launches), "attend (decode)");
-    } else {
-        a.tiles = tiles, a.ntiles = ntiles;
-        a.tiles_per_split = (ntiles + plan.splits - 1) / plan.splits;
-        a.splits = (ntiles + a.tiles_per_split - 1) / a.tiles_per_split;
-        if (plan.path == Path::Tensor) {
-            a.tc_eK = eK, a.tc_eV = eV, a.err = ctx->dev_err;
-            ck(launch_attend_tc(kv, a, s, &ctx->launches), "attend (tensor cores)");
-        } else {
-            ck(launch_attend_flash(kv, hd, a, s, &ctx->launches), "attend (flash)");
-        }
+        return parts_only ? nitems : 0;
     }
+    a.tiles = tiles, a.ntiles = ntiles;
+    a.tiles_per_split = (ntiles + plan.splits - 1) / plan.splits;
+    a.splits = (ntiles + a.tiles_per_split - 1) / a.tiles_per_split;
+    if (plan.path == Path::Tensor) {
+        a.tc_eK = eK, a.tc_eV = eV, a.err = ctx->dev_err;
+        ck(launch_attend_tc(kv, a, s, &ctx->launches), "attend (tensor cores)");
+    } else {
+        ck(launch_attend_flash(kv, hd, a, s, &ctx->launches), "attend (flash)");
+    }
+    return parts_only ? a.splits : 0;
 }
 
 static void linear(tcu_ctx *ctx, tcu_model *m, const float *x, int ldx, int R, int K, const float *lnw, const float *lnb,
@@ -926,6 +974,49 @@ static void stage_replay(tcu_ctx *ctx, tcu_model *m, int R, int out_n, cudaStrea
     // the capture itself ran nothing: count the replay's kernels
     ctx->launches = before + g.launches;
     CU(cudaGraphLaunch(exec, s));
+}
+
+// ---- training rows split across devices -----------------------------------------------------------------------
+
+static void nccl_check(ncclResult_t r, const char *what) {
+    if (r != ncclSuccess) fail(TCU_ERR_CUDA, std::string(what) + ": " + nccl_api().error_string(r));
+}
+
+// The stage with every layer's attention merged over the ranks of c (m holds this rank's rows; m->h in, m->out out).
+static void stage_sharded(tcu_ctx *ctx, tcu_model *m, tcu_comm *c, int R, int out_n, cudaStream_t s) {
+    check_ready(m);
+    const auto &sh = m->w->shape;
+    const int d = sh.d, H = sh.heads, L = sh.layers, dff = sh.dec_ff;
+    if (out_n < 1 || out_n > sh.outs) fail(TCU_ERR_ARG, "stage: out_n must be 1..decoder outputs");
+    if (c->aborted) fail(TCU_ERR_STATE, "communicator was aborted");
+    scan_model(ctx, m, ctx->stream);
+    ensure_work(m, R);
+    if (m->out.ensure(sizeof(float) * (size_t)R * out_n)) drop_graphs(m);
+    m->sh_m.ensure(sizeof(float) * (size_t)R * H);
+    m->sh_mall.ensure(sizeof(float) * (size_t)R * H);
+    m->sh_packed.ensure(sizeof(float) * (size_t)R * (d + H));
+    const auto &api = nccl_api();
+    Launch ck{ctx, s};
+    const float *scales = m->scales.as<float>();
+    float *h = m->h.as<float>(), *q = m->q.as<float>(), *att = m->att.as<float>();
+    for (int l = 0; l < L; l++) {
+        query_rows(ctx, m, l, scales + (size_t)l * d, h, R, q, s);
+        const int parts = attend_layer(ctx, m, layer_ptr(m, l), m->rows, m->chunk, m->kv, m->items.as<int2>(), m->nitems,
+                                       m->tiles.as<int4>(), m->ntiles, q, R, att, s, m->tc_eK[l], m->tc_eV[l], true);
+        AttnArgs a;
+        a.R = R, a.heads = H, a.d = d, a.part_ms = m->part_ms.as<float>(), a.part_acc = m->part_acc.as<float>();
+        ck(launch_merge_local(a, parts, m->sh_m.as<float>(), m->sh_packed.as<float>(), s, &ctx->launches), "merge (local)");
+        nccl_check(api.all_reduce(m->sh_m.p, m->sh_mall.p, (size_t)R * H, ncclFloat32, ncclMax, c->comm, s), "all-reduce (max)");
+        ck(launch_merge_rescale(m->sh_m.as<float>(), m->sh_mall.as<float>(), R, H, d, m->sh_packed.as<float>(), s,
+                                &ctx->launches), "merge (rescale)");
+        nccl_check(api.all_reduce(m->sh_packed.p, m->sh_packed.p, (size_t)R * (d + H), ncclFloat32, ncclSum, c->comm, s),
+                   "all-reduce (sum)");
+        ck(launch_merge_finish(m->sh_packed.as<float>(), R, H, d, att, d, s, &ctx->launches), "merge (finish)");
+        block_tail(ctx, m, l, h, att, R, s);
+    }
+    linear(ctx, m, h, d, R, d, m->w->lnw, m->w->lnb, m->w->dec0w, m->w->dec0b, dff, m->mid.as<float>(), dff, 1, 0, s, m->w->tdec0);
+    linear(ctx, m, m->mid.as<float>(), dff, R, dff, nullptr, nullptr, m->w->dec2w, m->w->dec2b, out_n, m->out.as<float>(),
+           out_n, 0, 0, s, m->w->tdec2);
 }
 
 // fit.rs:577-747 in-memory path on the device
@@ -1349,6 +1440,117 @@ int tcu_selftest_mma(tcu_ctx *ctx, double *max_err) {
         float worst;
         std::memcpy(&worst, &bits[0], 4);
         *max_err = bits[1] ? -1.0 : (double)worst;
+        return TCU_OK;
+    });
+}
+
+int tcu_comm_unique_id(uint8_t id[TCU_COMM_ID_BYTES]) {
+    if (!id) return TCU_ERR_ARG;
+    const auto &api = nccl_api();
+    if (!api.why.empty()) return TCU_ERR_STATE;
+    static_assert(sizeof(ncclUniqueId) == TCU_COMM_ID_BYTES, "NCCL unique id size");
+    ncclUniqueId u;
+    if (api.get_unique_id(&u) != ncclSuccess) return TCU_ERR_CUDA;
+    std::memcpy(id, &u, sizeof(u));
+    return TCU_OK;
+}
+
+int tcu_comm_init(tcu_ctx *ctx, const uint8_t id[TCU_COMM_ID_BYTES], int nranks, int rank, tcu_comm **out) {
+    return guarded(ctx, [&]() -> int {
+        if (!id || !out || nranks < 1 || rank < 0 || rank >= nranks) fail(TCU_ERR_ARG, "comm_init: bad argument");
+        const auto &api = nccl_api();
+        if (!api.why.empty()) fail(TCU_ERR_STATE, api.why);
+        std::unique_ptr<tcu_comm> c(new tcu_comm());
+        c->ctx = ctx, c->nranks = nranks, c->rank = rank;
+        ncclUniqueId u;
+        std::memcpy(&u, id, sizeof(u));
+        nccl_check(api.comm_init_rank(&c->comm, nranks, u, rank), "comm_init");
+        ctx->refs++;  // released by tcu_comm_free
+        *out = c.release();
+        return TCU_OK;
+    });
+}
+
+void tcu_comm_free(tcu_comm *c) {
+    if (!c) return;
+    tcu_ctx *ctx = c->ctx;
+    {
+        std::lock_guard<std::recursive_mutex> lock(ctx->mu);
+        cudaSetDevice(ctx->device);
+        if (c->comm) (c->aborted ? nccl_api().comm_abort : nccl_api().comm_destroy)(c->comm);
+        delete c;
+    }
+    ctx_release(ctx);
+}
+
+int tcu_comm_allreduce_f64(tcu_comm *c, double *buf, size_t count, void *stream) {
+    if (!c) return TCU_ERR_ARG;
+    return guarded(c->ctx, [&]() -> int {
+        if (!buf && count) fail(TCU_ERR_ARG, "allreduce: null buffer");
+        if (c->aborted) fail(TCU_ERR_STATE, "communicator was aborted");
+        cudaStream_t s = stream ? (cudaStream_t)stream : c->ctx->stream;
+        nccl_check(nccl_api().all_reduce(buf, buf, count, ncclFloat64, ncclSum, c->comm, s), "all-reduce (f64)");
+        return TCU_OK;
+    });
+}
+
+int tcu_comm_wait(tcu_comm *c, void *stream, int timeout_ms) {
+    if (!c) return TCU_ERR_ARG;
+    return guarded(c->ctx, [&]() -> int {
+        cudaStream_t s = stream ? (cudaStream_t)stream : c->ctx->stream;
+        const auto t0 = std::chrono::steady_clock::now();
+        for (;;) {
+            const cudaError_t e = cudaStreamQuery(s);
+            if (e == cudaSuccess) return TCU_OK;
+            if (e != cudaErrorNotReady) CU(e);
+            if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms)) {
+                // a rank that never arrives leaves NCCL's kernels waiting: aborting the communicator ends them
+                nccl_api().comm_abort(c->comm);
+                c->comm = nullptr, c->aborted = true;
+                fail(TCU_ERR_CUDA, "collective did not complete within " + std::to_string(timeout_ms) + " ms; communicator aborted");
+            }
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+        }
+    });
+}
+
+int tcu_model_slice(const tcu_model *m, int first_chunk, int nchunks, tcu_model **out) {
+    if (!m) return TCU_ERR_ARG;
+    return guarded(m->w->ctx, [&]() -> int {
+        const int total = (m->rows + m->chunk - 1) / m->chunk;
+        if (!out || first_chunk < 0 || nchunks < 1 || first_chunk + nchunks > total) fail(TCU_ERR_ARG, "model_slice: chunk range outside the cache");
+        check_ready(m);
+        const int r0 = first_chunk * m->chunk, r1 = std::min(m->rows, (first_chunk + nchunks) * m->chunk);
+        ModelPtr s(new tcu_model());
+        model_init(s.get(), m->w, r1 - r0, m->chunk, m->kv, m->classes);
+        s->features = m->features;
+        const auto &sh = m->w->shape;
+        for (int l = 0; l < sh.layers; l++) {
+            // whole chunk records: a shard's bytes are one contiguous range of the layer
+            CU(cudaMemcpy(s->layers.as<uint8_t>() + s->layer_stride * l, layer_ptr(m, l) + (size_t)first_chunk * m->full,
+                          s->layer_bytes, cudaMemcpyDeviceToDevice));
+            s->have_layer[l] = true;
+        }
+        CU(cudaMemcpy(s->scales.p, m->scales.p, sizeof(float) * (size_t)sh.layers * sh.d, cudaMemcpyDeviceToDevice));
+        s->have_scales = true;
+        *out = s.release();
+        return TCU_OK;
+    });
+}
+
+int tcu_stage_sharded_device(tcu_model *m, tcu_comm *c, const float *h, int rows, int out_n, float *out, void *stream) {
+    if (!m || !c) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->w->ctx;
+    return guarded(ctx, [&]() -> int {
+        if (c->ctx != ctx) fail(TCU_ERR_ARG, "stage_sharded: communicator and cache belong to different contexts");
+        if (rows < 0 || (rows && (!h || !out))) fail(TCU_ERR_ARG, "stage_sharded: bad argument");
+        if (rows == 0) return TCU_OK;
+        cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+        const size_t n = (size_t)rows * m->w->shape.d;
+        if (m->h.ensure(sizeof(float) * n)) drop_graphs(m);
+        CU(cudaMemcpyAsync(m->h.p, h, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+        stage_sharded(ctx, m, c, rows, out_n, s);
+        CU(cudaMemcpyAsync(out, m->out.p, sizeof(float) * (size_t)rows * out_n, cudaMemcpyDeviceToDevice, s));
         return TCU_OK;
     });
 }

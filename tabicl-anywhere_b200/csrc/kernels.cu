@@ -568,7 +568,7 @@ __global__ void __launch_bounds__(256, 2) k_attend_flash(AttnArgs a) {
     for (int i = 0; i < 4; i++) {
         const int r = r0 + 4 * tr + i;
         if (r >= a.R) continue;
-        if (a.splits == 1) {
+        if (a.splits == 1 && !a.parts_only) {
             const float inv = 1.0f / lrun[i];
 #pragma unroll
             for (int e = 0; e < OD; e++) a.out[(size_t)r * a.ldo + h * HD + tk * OD + e] = o[i][e] * inv;
@@ -644,6 +644,75 @@ __global__ void __launch_bounds__(256) k_attend_merge(const float *ms, const flo
         for (int w = 0; w < 8; w++) o += wsum[w * hd + j];
         out[(size_t)r * ldo + h * hd + j] = o * inv;
     }
+}
+
+// Training rows split across devices: this device's parts of each (row, head) into one state, as the merge above
+// but without the division: packed[r][h hd + j] = sum_p w_p acc_p, packed[r][d + h] = sum_p w_p s_p, m[r][h] = M.
+__global__ void __launch_bounds__(256) k_merge_local(const float *ms, const float *acc, int P, int R, int H, int d,
+                                                     float *m_out, float *packed) {
+    extern __shared__ __align__(16) float wsm[];  // [P] part weights, then [8][hd] warp sums
+    __shared__ float red[8];
+    const int r = blockIdx.x / H, h = blockIdx.x % H, hd = d / H, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float mx = -FLT_MAX;
+    for (int p = tid; p < P; p += blockDim.x) {
+        const float *q = ms + (((size_t)p * R + r) * H + h) * 2;
+        if (q[1] > 0.f) mx = fmaxf(mx, q[0]);
+    }
+    mx = warp_max(mx);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    float M = red[0];
+    for (int w = 1; w < 8; w++) M = fmaxf(M, red[w]);
+    __syncthreads();
+    float ssum = 0.f;
+    for (int p = tid; p < P; p += blockDim.x) {
+        const float *q = ms + (((size_t)p * R + r) * H + h) * 2;
+        const float w = q[1] > 0.f ? exp1(q[0] - M) : 0.f;
+        wsm[p] = w;
+        ssum = fmaf(q[1], w, ssum);
+    }
+    ssum = warp_sum(ssum);
+    if (lane == 0) red[warp] = ssum;
+    __syncthreads();
+    float S = 0.f;
+    for (int w = 0; w < 8; w++) S += red[w];
+    float *wsum = wsm + ((P + 3) & ~3);  // [8][hd]
+    const float *base = acc + (size_t)r * d + h * hd;
+    const size_t pstride = (size_t)R * d;
+    for (int j = lane; j < hd; j += 32) {
+        float o = 0.f;
+        for (int p = warp; p < P; p += 8) o = fmaf(base[p * pstride + j], wsm[p], o);
+        wsum[warp * hd + j] = o;
+    }
+    __syncthreads();
+    float *dst = packed + (size_t)r * (d + H);
+    for (int j = tid; j < hd; j += blockDim.x) {
+        float o = 0.f;
+        for (int w = 0; w < 8; w++) o += wsum[w * hd + j];
+        dst[h * hd + j] = o;
+    }
+    if (tid == 0) {
+        dst[d + h] = S;
+        m_out[(size_t)r * H + h] = S > 0.f ? M : -FLT_MAX;
+    }
+}
+
+// Scale this device's state to the maximum over devices (a device without keys for the row has weight 0).
+__global__ void k_merge_rescale(const float *m_local, const float *m_all, int R, int H, int d, float *packed) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x, w = (size_t)d + H;
+    if (i >= (size_t)R * w) return;
+    const int r = (int)(i / w), c = (int)(i % w), h = c < d ? c / (d / H) : c - d;
+    const float ml = m_local[(size_t)r * H + h];
+    packed[i] *= ml > -FLT_MAX ? exp1(ml - m_all[(size_t)r * H + h]) : 0.f;
+}
+
+// nn.rs:280-286 finish: weighted values / weight sum.
+__global__ void k_merge_finish(const float *packed, int R, int H, int d, float *out, int ldo) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)R * d) return;
+    const int r = (int)(i / d), c = (int)(i % d);
+    const float *p = packed + (size_t)r * (d + H);
+    out[(size_t)r * ldo + c] = p[c] / p[d + c / (d / H)];
 }
 
 // ---- fitting's chunk packer (fit.rs:549-576) ---------------------------------------------------------------
@@ -965,6 +1034,7 @@ cudaError_t launch_attend_decode(int kv, int hd, const AttnArgs &a, cudaStream_t
     cudaError_t e = kv == 0 ? decode_kv<0>(hd, a, s) : kv == 1 ? decode_kv<1>(hd, a, s) : decode_kv<2>(hd, a, s);
     if (e != cudaSuccess) return e;
     TCU_LAUNCHED(launches);
+    if (a.parts_only) return cudaSuccess;
     return launch_attend_merge(a, a.nitems, s, launches);
 }
 
@@ -994,8 +1064,33 @@ cudaError_t launch_attend_flash(int kv, int hd, const AttnArgs &a, cudaStream_t 
     cudaError_t e = kv == 0 ? flash_kv<0>(hd, a, s) : kv == 1 ? flash_kv<1>(hd, a, s) : flash_kv<2>(hd, a, s);
     if (e != cudaSuccess) return e;
     TCU_LAUNCHED(launches);
-    if (a.splits > 1) return launch_attend_merge(a, a.splits, s, launches);
+    if (a.splits > 1 && !a.parts_only) return launch_attend_merge(a, a.splits, s, launches);
     return cudaSuccess;
+}
+
+cudaError_t launch_merge_local(const AttnArgs &a, int parts, float *m, float *packed, cudaStream_t s, uint64_t *launches) {
+    const size_t smem = sizeof(float) * ((size_t)((parts + 3) & ~3) + 8 * (size_t)(a.d / a.heads));
+    cudaError_t e = allow_smem(k_merge_local, smem);
+    if (e != cudaSuccess) return e;
+    k_merge_local<<<a.R * a.heads, 256, smem, s>>>(a.part_ms, a.part_acc, parts, a.R, a.heads, a.d, m, packed);
+    TCU_LAUNCHED(launches);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge_rescale(const float *m_local, const float *m_all, int R, int H, int d, float *packed,
+                                 cudaStream_t s, uint64_t *launches) {
+    const size_t n = (size_t)R * (d + H);
+    k_merge_rescale<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m_local, m_all, R, H, d, packed);
+    TCU_LAUNCHED(launches);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge_finish(const float *packed, int R, int H, int d, float *out, int ldo, cudaStream_t s,
+                                uint64_t *launches) {
+    const size_t n = (size_t)R * d;
+    k_merge_finish<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(packed, R, H, d, out, ldo);
+    TCU_LAUNCHED(launches);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_pack(const float *kvT, int ld, int d, int rows, int chunk, int kv, uint8_t *out, cudaStream_t s,

@@ -44,6 +44,7 @@ struct AttnArgs {
     int ldo = 0;
     int tc_eK = 0, tc_eV = 0;      // tensor-core path: power-of-two scalings of the keys and values
     int *err = nullptr;            // set to 1 when a kernel gave up waiting
+    int parts_only = 0;            // 1: always leave parts (no merge), even with a single split
 };
 
 // The few-row stage in one persistent kernel: per layer, the pointers it reads.
@@ -122,6 +123,15 @@ cudaError_t launch_attend_decode(int kv, int hd, const AttnArgs &a, cudaStream_t
 // row-blocked attention for many rows; merges itself when splits == 1, else writes parts
 cudaError_t launch_attend_flash(int kv, int hd, const AttnArgs &a, cudaStream_t s, uint64_t *launches);
 cudaError_t launch_attend_merge(const AttnArgs &a, int parts, cudaStream_t s, uint64_t *launches);
+// Attention over training rows split across devices (nn.rs:261-286 merge, in three steps around two all-reduces):
+// this device's parts into one unnormalised state per (row, head): m [R][H] its max, packed [R][d + H] the weighted
+// values then the weight sums; after the maxima are reduced (max) over devices, scale to the common max; after the
+// states are summed over devices, divide.
+cudaError_t launch_merge_local(const AttnArgs &a, int parts, float *m, float *packed, cudaStream_t s, uint64_t *launches);
+cudaError_t launch_merge_rescale(const float *m_local, const float *m_all, int R, int H, int d, float *packed,
+                                 cudaStream_t s, uint64_t *launches);
+cudaError_t launch_merge_finish(const float *packed, int R, int H, int d, float *out, int ldo, cudaStream_t s,
+                                uint64_t *launches);
 cudaError_t launch_pack(const float *kvT, int ld, int d, int rows, int chunk, int kv, uint8_t *out, cudaStream_t s,
                         uint64_t *launches);
 cudaError_t launch_add_y(float *h, const float *y, int rows, int d, int max_classes, const float *table,

@@ -1,0 +1,134 @@
+"""One rank of a multi-process test (run by tests/test_multi_rank.py and tests/test_gpu_multi.py as subprocesses).
+
+    python tests/multi_rank.py MODE RANK WORLD PORT
+
+MODE
+  merge-cpu  gloo on CPU: the cross-device attention merge (max all-reduce, rescale, sum all-reduce, divide) on
+             shards of a random cache, in numpy, against attention over the whole cache (src/nn.rs:187-286).
+  stage-gpu  one GPU per rank: the sharded stage through the C ABI against the oracle's stage over the whole
+             cache, and the f64 all-reduce of ensemble members' class-logit sums.
+Prints one JSON line with the rank's result.
+"""
+import json
+import os
+import sys
+from datetime import timedelta
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+
+
+def init(rank, world, port):
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    return dist
+
+
+def shard_chunks(nchunks, world, rank):
+    base, extra = divmod(nchunks, world)
+    return rank * base + min(rank, extra), base + (1 if rank < extra else 0)
+
+
+def merge_cpu(rank, world, port):
+    import torch
+    dist = init(rank, world, port)
+    rng = np.random.default_rng(7)
+    R, H, hd, n, chunk = 5, 4, 16, 333, 40
+    d = H * hd
+    q = rng.normal(0, 1, (R, d))
+    k = rng.normal(0, 1, (n, d))
+    v = rng.normal(0, 1, (n, d))
+    nchunks = (n + chunk - 1) // chunk
+    c0, nc = shard_chunks(nchunks, world, rank)
+    lo, hi = c0 * chunk, min(n, (c0 + nc) * chunk)
+    # this rank's unnormalised state per (row, head)
+    m_loc = np.full((R, H), -np.inf)
+    packed = np.zeros((R, d + H))
+    for h in range(H):
+        sl = slice(h * hd, (h + 1) * hd)
+        sc = q[:, sl] @ k[lo:hi, sl].T
+        m = sc.max(1)
+        p = np.exp(sc - m[:, None])
+        m_loc[:, h] = m
+        packed[:, sl] = p @ v[lo:hi, sl]
+        packed[:, d + h] = p.sum(1)
+    mt = torch.from_numpy(m_loc.copy())
+    dist.all_reduce(mt, op=dist.ReduceOp.MAX)
+    m_all = mt.numpy()
+    w = np.exp(m_loc - m_all)
+    for h in range(H):
+        packed[:, h * hd:(h + 1) * hd] *= w[:, h:h + 1]
+        packed[:, d + h] *= w[:, h]
+    pt = torch.from_numpy(packed)
+    dist.all_reduce(pt, op=dist.ReduceOp.SUM)
+    packed = pt.numpy()
+    att = np.concatenate([packed[:, h * hd:(h + 1) * hd] / packed[:, d + h:d + h + 1] for h in range(H)], 1)
+    want = np.zeros((R, d))
+    for h in range(H):
+        sl = slice(h * hd, (h + 1) * hd)
+        sc = q[:, sl] @ k[:, sl].T
+        p = np.exp(sc - sc.max(1, keepdims=True))
+        want[:, sl] = (p / p.sum(1, keepdims=True)) @ v[:, sl]
+    rows = torch.tensor([hi - lo])
+    dist.all_reduce(rows)
+    dist.destroy_process_group()
+    return {"rank": rank, "err": float(np.abs(att - want).max()), "rows_total": int(rows.item()), "rows": hi - lo}
+
+
+def stage_gpu(rank, world, port):
+    import torch
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from conftest import load_package
+    tcu = load_package()
+    from tabicl_anywhere_b200 import synth
+    import oracle
+    dist = init(rank, world, port)
+    torch.cuda.set_device(rank)
+    gpu = tcu.Gpu(rank)
+    uid = torch.zeros(tcu.COMM_ID_BYTES, dtype=torch.uint8)
+    if rank == 0:
+        uid = torch.frombuffer(bytearray(tcu.comm_unique_id()), dtype=torch.uint8)
+    dist.broadcast(uid, 0)
+    comm = tcu.Comm(gpu, bytes(uid.numpy().tobytes()), world, rank)
+    out = {"rank": rank, "stage": {}}
+    for kv in (1, 2):
+        cfg = synth.config("full", icl_num_blocks=2)
+        wt = synth.weights(cfg, seed=30 + kv, std=0.08)
+        m = oracle.Model({k: v for k, v in wt.items() if k.startswith("icl_predictor.")}, cfg["icl_nhead"], 2,
+                         cfg["max_classes"])
+        n, chunk = 1500, 256
+        caches, scales = oracle.icl_fit(m, synth.row_reps(n, m.d, 31), synth.labels(n, 10, 32), chunk, kv)
+        w = tcu.GpuWeights.from_tensors(gpu, synth.icl_shape(cfg), {k: v for k, v in wt.items() if k.startswith("icl_")})
+        full = tcu.VramModel.from_parts(w, [n, 7, 10, chunk, kv, 1, 1], n, 10, scales, caches)
+        c0, nc = tcu.shard_chunks((n + chunk - 1) // chunk, world, rank)
+        shard = full.slice(c0, nc)
+        for rows in (1, 5, 70):
+            h = synth.row_reps(rows, m.d, 40 + rows)
+            hd_ = torch.from_numpy(h).cuda()
+            o = torch.empty((rows, 10), device="cuda")
+            shard.stage_sharded_device(comm, hd_.data_ptr(), rows, 10, o.data_ptr(), torch.cuda.current_stream().cuda_stream)
+            comm.wait(30000, torch.cuda.current_stream().cuda_stream)
+            got = o.cpu().numpy()
+            want = oracle.in_context(m, kv, caches, scales, n, chunk, h, 10)
+            out["stage"][f"kv{kv}_r{rows}"] = float(np.abs(got - want).max())
+        shard.free(), full.free(), w.free()
+    # ensemble members one per device: each rank's member logit sums, summed over ranks in f64
+    sums = torch.full((6, 3), float(rank + 1), dtype=torch.float64, device="cuda")
+    comm.allreduce_f64(sums.data_ptr(), sums.numel(), torch.cuda.current_stream().cuda_stream)
+    comm.wait(30000, torch.cuda.current_stream().cuda_stream)
+    out["allreduce_f64"] = float(sums[0, 0].item())
+    torch.cuda.synchronize()
+    comm.free()
+    gpu.close()
+    dist.destroy_process_group()
+    return out
+
+
+if __name__ == "__main__":
+    mode, rank, world, port = sys.argv[1], int(sys.argv[2]), int(sys.argv[3]), int(sys.argv[4])
+    res = {"merge-cpu": merge_cpu, "stage-gpu": stage_gpu}[mode](rank, world, port)
+    print(json.dumps(res), flush=True)

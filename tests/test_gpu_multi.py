@@ -1,0 +1,24 @@
+"""Two devices (skipped with fewer): the sharded stage through the C ABI, each rank holding half of the training
+rows' chunks, equals the CPU path's stage over the whole cache within the stage bar; the f64 all-reduce used for
+ensemble members' class-logit sums adds every rank's sums."""
+import os
+
+import pytest
+
+from test_multi_rank import run_ranks
+
+pytestmark = pytest.mark.gpu
+
+STAGE = 5e-5
+
+
+def test_sharded_stage_on_two_gpus():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    outs = run_ranks("stage-gpu", 2, timeout=900, env=env)
+    for o in outs:
+        for k, err in o["stage"].items():
+            assert err < STAGE, (o["rank"], k, err)
+        assert o["allreduce_f64"] == 3.0
