@@ -42,6 +42,7 @@ def args():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--latency-reps", type=int, default=100)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-multi", action="store_true", help="skip the config 3 (members) and 4 (sharded) passes")
     return p.parse_args()
 
 
@@ -207,6 +208,108 @@ def reference_arm(a):
     return 0
 
 
+# ---- configs 3 and 4: ensemble members one per device, one large cache split along its training rows -----------
+
+def ev_time(stream, fn, reps):
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def max_over_ranks(x, world):
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return x
+    t = torch.tensor([x], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def multi_configs(pkg, synth, gpu, w, d, world, rank, stream, comm):
+    """BASELINE config 3 (8-member f32 ensemble, 10k-row caches, 65,536 test rows; members placed round-robin on the
+    devices, class-logit sums all-reduced in f64) and config 4 (100k-row i8 cache, 4,096 test rows, training rows
+    split over the devices with the attention merged every layer). One warm-up and one timed pass each (CUDA events,
+    max over ranks). Synthetic: seeded N(0,1) row representations, uniform labels; each member's cache is fitted
+    on the device from its own seeded rows (standing in for the per-member feature permutation)."""
+    import torch
+    sp = stream.cuda_stream
+    res = {}
+    # config 3
+    M, N3, R3, classes = 8, 10000, 65536, 10
+    mine = [m for m in range(M) if m % world == rank]
+    models = []
+    for m in mine:
+        htr = torch.from_numpy(synth.row_reps(N3, d, 300 + m)).cuda()
+        ytr = torch.from_numpy(synth.labels(N3, classes, 400 + m)).cuda()
+        models.append(pkg.fit_icl(w, htr.data_ptr(), ytr.data_ptr(), N3, CHUNK, 0))
+        del htr, ytr
+    h3 = torch.from_numpy(synth.row_reps(R3, d, 500)).cuda()
+    logits = torch.empty((R3, classes), device="cuda")
+    sums = torch.zeros((R3, classes), dtype=torch.float64, device="cuda")
+    maps = [torch.tensor([(c + m) % classes for c in range(classes)], dtype=torch.int32, device="cuda") for m in mine]
+
+    def members_pass():
+        sums.zero_()
+        for vm, mc in zip(models, maps):
+            vm.stage_device(h3.data_ptr(), R3, classes, logits.data_ptr(), sp)
+            stream.synchronize()  # the class head runs (and waits) on the library's own stream
+            gpu.class_head(logits.data_ptr(), R3, classes, classes, mc.data_ptr(), sums.data_ptr())
+        if comm is not None:
+            comm.allreduce_f64(sums.data_ptr(), sums.numel(), sp)
+
+    members_pass()
+    torch.cuda.synchronize()
+    ms3 = max_over_ranks(ev_time(stream, members_pass, 1), world)
+    flops3 = 4.0 * N3 * d * 12 * R3 * M
+    res["config3_members"] = {
+        "workload": "BASELINE config 3: 8-member ensemble, f32 caches of 10,000 rows, 65,536 test rows, members "
+                    "round-robin over the devices, class-logit sums all-reduced (f64)",
+        "ms_per_pass": ms3, "rows_per_s": R3 / (ms3 / 1e3), "member_rows_per_s": R3 * M / (ms3 / 1e3),
+        "attention_tflops_per_gpu": flops3 / world / (ms3 / 1e3) / 1e12, "members_per_gpu": len(mine)}
+    for vm in models:
+        vm.free()
+    del h3, logits, sums
+    # config 4
+    N4, R4 = 100000, 4096
+    htr = torch.from_numpy(synth.row_reps(N4, d, 600)).cuda()
+    ytr = torch.from_numpy(synth.labels(N4, classes, 601)).cuda()
+    full = pkg.fit_icl(w, htr.data_ptr(), ytr.data_ptr(), N4, CHUNK, 2)
+    del htr, ytr
+    nchunks = (N4 + CHUNK - 1) // CHUNK
+    if world > 1:
+        first, count = pkg.shard_chunks(nchunks, world, rank)
+        vm4 = full.slice(first, count)
+        full.free()
+    else:
+        vm4 = full
+    h4 = torch.from_numpy(synth.row_reps(R4, d, 602)).cuda()
+    o4 = torch.empty((R4, classes), device="cuda")
+
+    def sharded_pass():
+        if world > 1:
+            vm4.stage_sharded_device(comm, h4.data_ptr(), R4, classes, o4.data_ptr(), sp)
+        else:
+            vm4.stage_device(h4.data_ptr(), R4, classes, o4.data_ptr(), sp)
+
+    sharded_pass()
+    torch.cuda.synchronize()
+    ms4 = max_over_ranks(ev_time(stream, sharded_pass, 2), world)
+    flops4 = 4.0 * N4 * d * 12 * R4
+    res["config4_sharded"] = {
+        "workload": "BASELINE config 4: 100,000-row i8 cache (1.25 GB), 4,096 test rows, training rows split over "
+                    "the devices, attention merged every layer (all-reduce max, rescale, all-reduce sum)",
+        "ms_per_pass": ms4, "rows_per_s": R4 / (ms4 / 1e3),
+        "attention_tflops_per_gpu": flops4 / world / (ms4 / 1e3) / 1e12, "shard_rows": N4 // world}
+    vm4.free()
+    return res
+
+
 # ---- our arm ---------------------------------------------------------------------------------------------------
 
 def main():
@@ -353,6 +456,19 @@ def main():
                                       "p50_gbs": (L * layer_bytes + weight_bytes) / (pct(0.5) * 1e-6) / 1e9}},
         "clocks": clocks.summary(),
     }
+    if not a.no_multi:
+        comm = None
+        if world > 1:
+            uid = torch.zeros(pkg.COMM_ID_BYTES, dtype=torch.uint8, device="cuda")
+            if rank == 0:
+                uid.copy_(torch.frombuffer(bytearray(pkg.comm_unique_id()), dtype=torch.uint8))
+            dist.broadcast(uid, 0)
+            comm = pkg.Comm(gpu, bytes(uid.cpu().numpy().tobytes()), world, rank)
+        line["multi"] = multi_configs(pkg, synth, gpu, w, d, world, rank, stream, comm)
+        if comm is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            comm.free()
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle
