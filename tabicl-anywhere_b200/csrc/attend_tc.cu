@@ -1,14 +1,9 @@
 // Attention of many query rows on the 5th-generation tensor cores (tcgen05), at f32 accuracy.
 //
-// One CTA takes 128 query rows of one head and a range of 64-key tiles of the stored cache (chunks read in place,
-// integer formats dequantised as they are staged). Every f32 operand is split into two f16 values (x = hi + lo,
-// about 22 significant bits) after a power-of-two scaling that keeps it inside the f16 range, and each product is
-// taken as hi*hi + hi*lo + lo*hi in f32 accumulators in tensor memory:
-//   S = Q K^T: Q [128 rows x 128] K-major, K [64 keys x 128] keys-contiguous (as stored), S in TMEM columns 0-63;
-//   O += P V^T: P [128 x 64 keys] K-major, V [128 dims x 64 keys] keys-contiguous (as stored), O in columns 64-191.
-// The softmax is online across tiles (nn.rs:207-215 rule): each of the 128 threads of warps 0-3 owns one query
-// row (its TMEM lane), so a row's maximum and sum need no shuffles; O is rescaled in TMEM only when the running
-// maximum rises. One thread issues the MMAs; mbarrier waits are bounded and record a failure instead of hanging.
+// Every f32 operand is split into two f16 values (x = hi + lo, about 22 significant bits) after a power-of-two
+// scaling that keeps it inside the f16 range, and each product is taken as hi*hi + hi*lo + lo*hi with f32
+// accumulators in tensor memory. The stored keys and values are widened and split once per model into 64-key tiles
+// in exactly the layout the MMAs read (k_tc_tiles); the attention kernel moves them with bulk copies.
 #include <cfloat>
 #include <cmath>
 
@@ -42,41 +37,147 @@ __device__ __forceinline__ void put8(__half *hi, __half *lo, int off, const floa
     *reinterpret_cast<uint4 *>(lo + off) = *reinterpret_cast<const uint4 *>(l);
 }
 
+// e^x on the special-function unit: 2^(x log2 e), relative error about 1e-6 for the softmax's arguments (x <= 0,
+// |x| < 30 where the weight matters). The tensor-core path's softmax uses it to keep the FMA pipe free; its results
+// stay within the stage bar of the reference's exp (kern.rs:220-235).
+__device__ __forceinline__ float exp_sfu(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x * 1.44269504088896340736f));
+    return y;
+}
+
+// Eight values as f16 hi + lo (x = hi + lo), two at a time.
+__device__ __forceinline__ void put8x2(__half *hi, __half *lo, int off, const float (&v)[8]) {
+    __align__(16) __half2 h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        h[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+        const float2 b = __half22float2(h[e]);
+        l[e] = __floats2half2_rn(v[2 * e] - b.x, v[2 * e + 1] - b.y);
+    }
+    *reinterpret_cast<uint4 *>(hi + off) = *reinterpret_cast<const uint4 *>(h);
+    *reinterpret_cast<uint4 *>(lo + off) = *reinterpret_cast<const uint4 *>(l);
+}
+
+constexpr int TC_HD = 128, TC_BQ = 128, TC_BK = FLASH_KEYS;
+constexpr size_t TC_BLOCK = (size_t)TC_BK * TC_HD;  // halves of one operand block (keys hi, keys lo, values hi, lo)
+
+size_t tc_tile_bytes() { return 4 * TC_BLOCK * sizeof(__half); }
+
+// One tile (64 keys x one head) of a stored layer in the tensor cores' operand form, written once per model:
+// [keys hi][keys lo][values hi][values lo], each 64 x 128 f16 in the core-matrix layout the MMAs read from shared
+// memory (keys MN-major, values K-major). Integers are widened exactly and multiplied by their chunk's scale
+// (predict.rs:486-497 for keys; nn.rs:253-256 for values, the same product taken per element), then by the layer's
+// power of two and split into hi + lo. Keys past a ragged tile's end are zero.
+template <int KV>
+__global__ void __launch_bounds__(256) k_tc_tiles(AttnArgs a, __half *out) {
+    constexpr int HD = TC_HD, BK = TC_BK, W = KvFmt<KV>::W, EPV = KvFmt<KV>::EPV, VPR = BK / EPV;
+    const int t = blockIdx.x, h = blockIdx.y, H = gridDim.y, tid = threadIdx.x, d = a.d;
+    __half *Khi = out + ((size_t)t * H + h) * 4 * TC_BLOCK, *Klo = Khi + TC_BLOCK, *Vhi = Klo + TC_BLOCK,
+           *Vlo = Vhi + TC_BLOCK;
+    const int4 tile = a.tiles[t];
+    const int ci = tile.x, k0 = tile.y, len = tile.z;
+    const int rc = min(a.chunk, a.rows - ci * a.chunk);
+    const uint8_t *rec = a.layer + (size_t)ci * a.full;
+    const float *sc = reinterpret_cast<const float *>(rec);
+    const uint8_t *body = rec + (KV ? 8 * (size_t)d : 0);
+    const uint8_t *kb = body + ((size_t)h * HD * rc + k0) * W;
+    const uint8_t *vb = body + ((size_t)(d + h * HD) * rc + k0) * W;
+    const size_t rowb = (size_t)rc * W;
+    const float kscale = pow2f(a.tc_eK), vscale = pow2f(a.tc_eV);
+    const bool fast = len == BK && ((((uintptr_t)kb) | ((uintptr_t)vb) | rowb) & 15) == 0;
+    if (fast) {
+        for (int i = tid; i < HD * VPR / 2; i += 256) {
+            const int j = i % HD, vp = i / HD;
+            const float ks = (KV ? sc[h * HD + j] : 1.f) * kscale;
+            const float vs = (KV ? sc[d + h * HD + j] : 1.f) * vscale;
+            const uint4 rk0 = *reinterpret_cast<const uint4 *>(kb + j * rowb + vp * 32);
+            const uint4 rk1 = *reinterpret_cast<const uint4 *>(kb + j * rowb + vp * 32 + 16);
+            const uint4 rv0 = *reinterpret_cast<const uint4 *>(vb + j * rowb + vp * 32);
+            const uint4 rv1 = *reinterpret_cast<const uint4 *>(vb + j * rowb + vp * 32 + 16);
+#pragma unroll
+            for (int g = 0; g < 2 * EPV; g += 8) {
+                float fk[8], fv[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const int x = g + e;
+                    fk[e] = (x < EPV ? unpack<KV>(rk0, x) : unpack<KV>(rk1, x - EPV)) * ks;
+                    fv[e] = (x < EPV ? unpack<KV>(rv0, x) : unpack<KV>(rv1, x - EPV)) * vs;
+                }
+                const int key = vp * 2 * EPV + g;
+                put8(Khi, Klo, mnmajor_off(key, j, BK), fk, 1.f);
+                put8(Vhi, Vlo, kmajor_off(j, key, HD), fv, 1.f);
+            }
+        }
+    } else {
+        for (int i = tid; i < HD * BK; i += 256) {
+            const int j = i / BK, key = i % BK;
+            float fk = 0.f, fv = 0.f;
+            if (key < len) {
+                fk = load_elem<KV>(body, (size_t)(h * HD + j) * rc + k0 + key) * (KV ? sc[h * HD + j] : 1.f);
+                fv = load_elem<KV>(body, (size_t)(d + h * HD + j) * rc + k0 + key) * (KV ? sc[d + h * HD + j] : 1.f);
+            }
+            split_f16(fk * kscale, Khi[mnmajor_off(key, j, BK)], Klo[mnmajor_off(key, j, BK)]);
+            split_f16(fv * vscale, Vhi[kmajor_off(j, key, HD)], Vlo[kmajor_off(j, key, HD)]);
+        }
+    }
+}
+
+// 16-byte aligned contiguous bytes into shared memory, completing on the mbarrier (async proxy).
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *mbar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(mbar))
+                 : "memory");
+}
+__device__ __forceinline__ void expect_tx(uint64_t *mbar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}\n" ::"r"(
+                     smem_addr(mbar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// Attention of 128 query rows x one head over a range of 64-key tiles, with the tiles pre-split (k_tc_tiles):
+//   S = Q K^T: Q [128 x 128] K-major, K [64 keys x 128] MN-major; hi*hi in TMEM columns 0-63, cross terms 64-127
+//   O += P V^T: P [128 x 64 keys] K-major, V [128 x 64 keys] K-major; per tile hi*hi in 128-255, cross 256-383
+// Each tile's four operand blocks arrive by bulk copies into one of two shared-memory stages, two tiles ahead. The
+// online softmax (nn.rs:207-215 rule) runs on all eight warps, two threads per query row (one per half of the
+// keys). While a tile's P V is folded into the registers' O, the next tile's S is already on the tensor cores.
+// Every f32 sum of tensor-core results is taken in registers (fresh accumulators per tile: the units' own f32
+// accumulation is not round-to-nearest). One thread issues the MMAs and copies; every wait is bounded.
 template <int KV>
 __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
-    constexpr int HD = 128, BQ = 128, BK = FLASH_KEYS, W = KvFmt<KV>::W, EPV = KvFmt<KV>::EPV, VPR = BK / EPV;
+    constexpr int HD = TC_HD, BQ = TC_BQ, BK = TC_BK;
     extern __shared__ __align__(1024) uint8_t smraw[];
     __half *Qhi = reinterpret_cast<__half *>(smraw);  // [BQ][HD] K-major
     __half *Qlo = Qhi + BQ * HD;
-    __half *Khi = Qlo + BQ * HD;                      // [BK keys][HD] MN-major
-    __half *Klo = Khi + BK * HD;
-    __half *Vhi = Klo + BK * HD;                      // [HD][BK keys] K-major
-    __half *Vlo = Vhi + HD * BK;
-    __half *Phi = Vlo + HD * BK;                      // [BQ][BK keys] K-major
+    __half *stage0 = Qlo + BQ * HD;                   // two stages of [keys hi][keys lo][values hi][values lo]
+    __half *Phi = stage0 + 2 * 4 * TC_BLOCK;          // [BQ][BK keys] K-major
     __half *Plo = Phi + BQ * BK;
-    uint64_t *mbar = reinterpret_cast<uint64_t *>(Plo + BQ * BK);  // [0] S ready, [1] P V ready
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(mbar + 2);
+    float *fr = reinterpret_cast<float *>(Plo + BQ * BK);  // [BQ] this tile's rescale factor of each row
+    float *redm = fr + BQ;                                 // [2][BQ] half-row maxima
+    float *reds = redm + 2 * BQ;                           // [2][BQ] half-row weight sums
+    uint64_t *mbar = reinterpret_cast<uint64_t *>(reds + 2 * BQ);  // S ready, P V ready, stage 0 loaded, stage 1
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(mbar + 4);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
-    float *qscale = reinterpret_cast<float *>(tslot + 4);  // [BQ] 2^e of each row's query
-    float *fr = qscale + BQ;                               // [BQ] this tile's rescale factor of each row
-    float *lrow = fr + BQ;                                 // [BQ] final weight sums
-    float *mrow = lrow + BQ;                               // [BQ] final maxima
+    float *qscale = reinterpret_cast<float *>(Phi);  // [BQ] 2^e of each row's query (until the first P)
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.y, split = blockIdx.z, r0 = blockIdx.x * BQ, d = a.d, H = gridDim.y;
+    // a query row per (warp % 4, lane); keys / output columns by warp / 4
+    const int row = (warp & 3) * 32 + lane, half = warp >> 2;
+    const int t0 = split * a.tiles_per_split, t1 = min(a.ntiles, t0 + a.tiles_per_split), nt = t1 - t0;
+    const __half *tiles = reinterpret_cast<const __half *>(a.tc_tiles);
     if (warp == 0) {
-        // S: hi*hi in columns 0-63, cross terms 64-127; one tile's P V: hi*hi 128-255, cross terms 256-383
         tmem_alloc(tslot, 512);
         tmem_relinquish();
     }
     if (tid == 0) {
-        mbar_init(&mbar[0], 1);
-        mbar_init(&mbar[1], 1);
+        for (int i = 0; i < 4; i++) mbar_init(&mbar[i], 1);
         mbar_init_fence();
         *abort_flag = 0;
     }
     // each row's query scale: its largest |q| maps below 2^14
-    int erow = 0;
     if (tid < BQ) {
         float mx = 0.f;
         const int r = r0 + tid;
@@ -88,14 +189,22 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
                 mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
             }
         }
-        erow = f16_exponent(mx);
-        qscale[tid] = pow2f(erow);
+        qscale[tid] = pow2f(f16_exponent(mx));
     }
-    fence_before_sync();
     __syncthreads();
-    fence_after_sync();
-    const uint32_t tmem = *tslot, tShh = tmem, tSx = tmem + 64, tOhh = tmem + 128, tOx = tmem + 256;
-    // queries, split; consecutive threads take consecutive rows so their 16-byte stores are contiguous
+    // the first two tiles start loading while the queries are split
+    auto load_tile = [&](int i) {  // thread 0: tile t0 + i into stage i & 1
+        const __half *src = tiles + ((size_t)(t0 + i) * H + h) * 4 * TC_BLOCK;
+        __half *dst = stage0 + (size_t)(i & 1) * 4 * TC_BLOCK;
+        uint64_t *mb = &mbar[2 + (i & 1)];
+        expect_tx(mb, (uint32_t)(4 * TC_BLOCK * sizeof(__half)));
+#pragma unroll
+        for (int b = 0; b < 4; b++) bulk_g2s(dst + b * TC_BLOCK, src + b * TC_BLOCK, (uint32_t)(TC_BLOCK * sizeof(__half)), mb);
+    };
+    if (tid == 0) {
+        if (nt > 0) load_tile(0);
+        if (nt > 1) load_tile(1);
+    }
     for (int i = tid; i < BQ * (HD / 8); i += 256) {
         const int m = i % BQ, j0 = (i / BQ) * 8, r = r0 + m;
         float v[8];
@@ -109,175 +218,168 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
         }
         put8(Qhi, Qlo, kmajor_off(m, j0, BQ), v, qscale[m]);
     }
-    const float kscale = pow2f(a.tc_eK), vscale = pow2f(a.tc_eV);
-    const float row_unscale = tid < BQ ? pow2f(-erow) * pow2f(-a.tc_eK) : 1.f;
+    const float rs = (1.0f / qscale[row]) * pow2f(-a.tc_eK);  // undoes the query's and the keys' scalings
+    fence_async_smem();
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = *tslot, tShh = tmem, tSx = tmem + 64, tOhh = tmem + 128, tOx = tmem + 256;
     const uint32_t idS = idesc_f16(BQ, BK, 0, 1), idO = idesc_f16(BQ, HD, 0, 0);
-    // every thread's share of O: row (warp % 4) * 32 + lane, columns (warp / 4) * 64 + [0, 64)
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const int orow = (warp & 3) * 32 + (tid & 31), ocol = (warp >> 2) * 64;
+    auto issue_S = [&](int i) {  // thread 0: S of tile t0 + i from its stage
+        const __half *K = stage0 + (size_t)(i & 1) * 4 * TC_BLOCK;
+#pragma unroll
+        for (int s = 0; s < HD / 16; s++) mma_f16(tShh, kstep_desc(Qhi, BQ, s), kstep_desc(K, BK, s), idS, s > 0 ? 1u : 0u);
+#pragma unroll
+        for (int s = 0; s < HD / 16; s++) {
+            mma_f16(tSx, kstep_desc(Qhi, BQ, s), kstep_desc(K + TC_BLOCK, BK, s), idS, s > 0 ? 1u : 0u);
+            mma_f16(tSx, kstep_desc(Qlo, BQ, s), kstep_desc(K, BK, s), idS, 1);
+        }
+        mma_commit(&mbar[0]);
+    };
+    uint32_t pS = 0, pO = 0, pK = 0;  // mbarrier parities (pK: bit per stage)
+    int issued = min(nt, 2);  // tiles whose loads were started
+    if (tid == 0 && nt > 0) {
+        if (mbar_wait(&mbar[2], 0, TC_WAIT_CYCLES)) {
+            fence_after_sync();
+            issue_S(0);
+        } else {
+            *abort_flag = 1;
+        }
+        pK = 1;
+    }
     float o[64];
 #pragma unroll
     for (int e = 0; e < 64; e++) o[e] = 0.f;
     float mrun = -FLT_MAX, lrun = 0.f;
-    uint32_t ps = 0, po = 0;
-    const int t0 = split * a.tiles_per_split, t1 = min(a.ntiles, t0 + a.tiles_per_split);
-    const uint64_t pol = policy_evict_first();
     bool any = false;
-    for (int t = t0; t < t1; t++) {
-        const int4 tile = a.tiles[t];
-        const int ci = tile.x, k0 = tile.y, len = tile.z;
-        const int rc = min(a.chunk, a.rows - ci * a.chunk);
-        const uint8_t *rec = a.layer + (size_t)ci * a.full;
-        const float *sc = reinterpret_cast<const float *>(rec);
-        const uint8_t *body = rec + (KV ? 8 * (size_t)d : 0);
-        const uint8_t *kb = body + ((size_t)h * HD * rc + k0) * W;
-        const uint8_t *vb = body + ((size_t)(d + h * HD) * rc + k0) * W;
-        const size_t rowb = (size_t)rc * W;
-        const bool fast = len == BK && ((((uintptr_t)kb) | ((uintptr_t)vb) | rowb) & 15) == 0;
-        if (fast) {
-            // consecutive threads take consecutive dims (contiguous shared-memory stores in both layouts), each
-            // reading a 32-byte run of its dim's keys
-            for (int i = tid; i < HD * VPR / 2; i += 256) {
-                const int j = i % HD, vp = i / HD;
-                const float ks = (KV ? sc[h * HD + j] : 1.f) * kscale;
-                const float vs = (KV ? sc[d + h * HD + j] : 1.f) * vscale;
-                const uint4 rk0 = ld_stream16(kb + j * rowb + vp * 32, pol), rk1 = ld_stream16(kb + j * rowb + vp * 32 + 16, pol);
-                const uint4 rv0 = ld_stream16(vb + j * rowb + vp * 32, pol), rv1 = ld_stream16(vb + j * rowb + vp * 32 + 16, pol);
-#pragma unroll
-                for (int g = 0; g < 2 * EPV; g += 8) {
-                    float fk[8], fv[8];
-#pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        const int x = g + e;  // element within the 32-byte run
-                        fk[e] = (x < EPV ? unpack<KV>(rk0, x) : unpack<KV>(rk1, x - EPV)) * ks;
-                        fv[e] = (x < EPV ? unpack<KV>(rv0, x) : unpack<KV>(rv1, x - EPV)) * vs;
-                    }
-                    const int key = vp * 2 * EPV + g;
-                    put8(Khi, Klo, mnmajor_off(key, j, BK), fk, 1.f);
-                    put8(Vhi, Vlo, kmajor_off(j, key, HD), fv, 1.f);
-                }
-            }
-        } else {
-            for (int i = tid; i < HD * BK; i += 256) {
-                const int j = i / BK, key = i % BK;
-                float fk = 0.f, fv = 0.f;
-                if (key < len) {
-                    fk = load_elem<KV>(body, (size_t)(h * HD + j) * rc + k0 + key) * (KV ? sc[h * HD + j] : 1.f);
-                    fv = load_elem<KV>(body, (size_t)(d + h * HD + j) * rc + k0 + key) * (KV ? sc[d + h * HD + j] : 1.f);
-                }
-                split_f16(fk * kscale, Khi[mnmajor_off(key, j, BK)], Klo[mnmajor_off(key, j, BK)]);
-                split_f16(fv * vscale, Vhi[kmajor_off(j, key, HD)], Vlo[kmajor_off(j, key, HD)]);
-            }
-        }
-        fence_async_smem();
+    int consumed = 0;
+    for (int i = 0; i < nt; i++) {
         __syncthreads();
-        if (tid == 0) {
-            fence_after_sync();
+        if (*abort_flag) break;
+        const int len = a.tiles[t0 + i].z;
+        // (1) the online softmax of S, two threads per row
+        const bool okS = mbar_wait(&mbar[0], pS, TC_WAIT_CYCLES);
+        pS ^= 1;
+        if (!okS) *abort_flag = 1;
+        fence_after_sync();
+        __syncwarp();
+        float s[32];
+        {
+            float x[32], y[32];
+            tmem_ld32(tShh + lane_base + 32 * half, x);
+            tmem_ld32(tSx + lane_base + 32 * half, y);
+            tmem_wait_ld();
 #pragma unroll
-            for (int s = 0; s < HD / 16; s++)
-                mma_f16(tShh, kstep_desc(Qhi, BQ, s), kstep_desc(Khi, BK, s), idS, s > 0 ? 1u : 0u);
-#pragma unroll
-            for (int s = 0; s < HD / 16; s++) {
-                mma_f16(tSx, kstep_desc(Qhi, BQ, s), kstep_desc(Klo, BK, s), idS, s > 0 ? 1u : 0u);
-                mma_f16(tSx, kstep_desc(Qlo, BQ, s), kstep_desc(Khi, BK, s), idS, 1);
-            }
-            mma_commit(&mbar[0]);
+            for (int k = 0; k < 32; k++) s[k] = (x[k] + y[k]) * rs;
         }
-        if (warp < 4) {
-            const bool ok = mbar_wait(&mbar[0], ps, TC_WAIT_CYCLES);
-            if (!ok) *abort_flag = 1;
-            fence_after_sync();
-            float s[64];
+        float mx = -FLT_MAX;
 #pragma unroll
-            for (int c = 0; c < 2; c++) {
-                float x[32], y[32];
-                tmem_ld32(tShh + lane_base + 32 * c, x);
-                tmem_ld32(tSx + lane_base + 32 * c, y);
-                tmem_wait_ld();
+        for (int k = 0; k < 32; k++)
+            if (32 * half + k < len) mx = fmaxf(mx, s[k]);
+        redm[half * BQ + row] = mx;
+        fence_before_sync();
+        __syncthreads();
+        const float mnew = fmaxf(mrun, fmaxf(redm[row], redm[BQ + row]));
+        const float f = lrun > 0.f ? exp_sfu(mrun - mnew) : 0.f;
+        float psum = 0.f;
 #pragma unroll
-                for (int k = 0; k < 32; k++) s[32 * c + k] = (x[k] + y[k]) * row_unscale;
-            }
-            float mx = -FLT_MAX;
-#pragma unroll
-            for (int k = 0; k < 64; k++)
-                if (k < len) mx = fmaxf(mx, s[k]);
-            const float mnew = fmaxf(mrun, mx);
-            const float f = lrun > 0.f ? exp1(mrun - mnew) : 0.f;
-            float psum = 0.f;
-#pragma unroll
-            for (int k = 0; k < 64; k++) {
-                const float p = k < len ? exp1(s[k] - mnew) : 0.f;
-                s[k] = p * 16384.f;  // 2^14: small weights stay normal in f16
-                psum += p;
-            }
-            lrun = lrun * f + psum;
-            mrun = mnew;
-            fr[tid] = f;
-#pragma unroll
-            for (int g = 0; g < 8; g++) {
-                float v[8];
-#pragma unroll
-                for (int e = 0; e < 8; e++) v[e] = s[g * 8 + e];
-                put8(Phi, Plo, kmajor_off(tid, g * 8, BQ), v, 1.f);
-            }
+        for (int k = 0; k < 32; k++) {
+            const float p = 32 * half + k < len ? exp_sfu(s[k] - mnew) : 0.f;
+            s[k] = p * 16384.f;  // 2^14: small weights stay normal in f16
+            psum += p;
         }
-        ps ^= 1;
+        reds[half * BQ + row] = psum;
+        if (half == 0) fr[row] = f;
+#pragma unroll
+        for (int g = 0; g < 4; g++) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = s[g * 8 + e];
+            put8x2(Phi, Plo, kmajor_off(row, 32 * half + g * 8, BQ), v);
+        }
         fence_async_smem();
         fence_before_sync();
         __syncthreads();
-        if (*abort_flag) break;
+        lrun = lrun * f + (reds[row] + reds[BQ + row]);
+        mrun = mnew;
+        // (2) this tile's P V, then the next tile's S (its stage loaded)
         if (tid == 0) {
             fence_after_sync();
+            const __half *V = stage0 + (size_t)(i & 1) * 4 * TC_BLOCK + 2 * TC_BLOCK;
 #pragma unroll
-            for (int s = 0; s < BK / 16; s++)
-                mma_f16(tOhh, kstep_desc(Phi, BQ, s), kstep_desc(Vhi, HD, s), idO, s > 0 ? 1u : 0u);
+            for (int s2 = 0; s2 < BK / 16; s2++)
+                mma_f16(tOhh, kstep_desc(Phi, BQ, s2), kstep_desc(V, HD, s2), idO, s2 > 0 ? 1u : 0u);
 #pragma unroll
-            for (int s = 0; s < BK / 16; s++) {
-                mma_f16(tOx, kstep_desc(Phi, BQ, s), kstep_desc(Vlo, HD, s), idO, s > 0 ? 1u : 0u);
-                mma_f16(tOx, kstep_desc(Plo, BQ, s), kstep_desc(Vhi, HD, s), idO, 1);
+            for (int s2 = 0; s2 < BK / 16; s2++) {
+                mma_f16(tOx, kstep_desc(Phi, BQ, s2), kstep_desc(V + TC_BLOCK, HD, s2), idO, s2 > 0 ? 1u : 0u);
+                mma_f16(tOx, kstep_desc(Plo, BQ, s2), kstep_desc(V, HD, s2), idO, 1);
             }
             mma_commit(&mbar[1]);
+            if (i + 1 < nt) {
+                const int st = (i + 1) & 1;
+                if (mbar_wait(&mbar[2 + st], (pK >> st) & 1u, TC_WAIT_CYCLES)) {
+                    fence_after_sync();
+                    issue_S(i + 1);
+                } else {
+                    *abort_flag = 1;
+                }
+                pK ^= 1u << st;
+            }
         }
-        // every thread folds this tile's P V into its share of O: O = O * f + (hi*hi + cross terms)
-        const bool okO = mbar_wait(&mbar[1], po, TC_WAIT_CYCLES);
-        po ^= 1;
+        // (3) fold this tile's P V into O: O = O * f + (hi*hi + cross terms)
+        const bool okO = mbar_wait(&mbar[1], pO, TC_WAIT_CYCLES);
+        pO ^= 1;
         if (!okO) *abort_flag = 1;
         fence_after_sync();
+        __syncwarp();
         if (okO) {
-            const float f = fr[orow];
+            const float fo = fr[row];
 #pragma unroll
             for (int c = 0; c < 2; c++) {
                 float x[32], y[32];
-                tmem_ld32(tOhh + lane_base + ocol + 32 * c, x);
-                tmem_ld32(tOx + lane_base + ocol + 32 * c, y);
+                tmem_ld32(tOhh + lane_base + 64 * half + 32 * c, x);
+                tmem_ld32(tOx + lane_base + 64 * half + 32 * c, y);
                 tmem_wait_ld();
 #pragma unroll
-                for (int k = 0; k < 32; k++) o[32 * c + k] = fmaf(o[32 * c + k], f, x[k] + y[k]);
+                for (int k = 0; k < 32; k++) o[32 * c + k] = fmaf(o[32 * c + k], fo, x[k] + y[k]);
             }
         }
         any = true;
+        consumed = i + 1;
         fence_before_sync();
         __syncthreads();
-        if (*abort_flag) break;
+        // (4) this tile's stage is free (its S and P V are done): the tile two ahead goes there
+        if (tid == 0 && i + 2 < nt && !*abort_flag) {
+            load_tile(i + 2);
+            issued = i + 3;
+        }
     }
-    if (tid < BQ) lrow[tid] = lrun, mrow[tid] = mrun;
-    __syncthreads();
+    // leaving early: loads still in flight land before the shared memory is given up
+    if (tid == 0) {
+        for (int i = max(consumed + 1, 1); i < issued; i++) {
+            const int st = i & 1;
+            mbar_wait(&mbar[2 + st], (pK >> st) & 1u, TC_WAIT_CYCLES);
+            pK ^= 1u << st;
+        }
+    }
     const bool ok = any && !*abort_flag;
-    const int r = r0 + orow;
+    const int r = r0 + row;
     if (r < a.R) {
         const float oun = pow2f(-14 - a.tc_eV);
+        const int col = 64 * half;
         if (a.splits == 1 && !a.parts_only) {
-            const float inv = ok ? 1.0f / lrow[orow] : 0.f;
-            float *dst = a.out + (size_t)r * a.ldo + h * HD + ocol;
+            const float inv = ok ? 1.0f / lrun : 0.f;
+            float *dst = a.out + (size_t)r * a.ldo + h * HD + col;
 #pragma unroll
             for (int k = 0; k < 64; k++) dst[k] = o[k] * oun * inv;
         } else {
-            float *dst = a.part_acc + ((size_t)split * a.R + r) * d + h * HD + ocol;
+            float *dst = a.part_acc + ((size_t)split * a.R + r) * d + h * HD + col;
 #pragma unroll
             for (int k = 0; k < 64; k++) dst[k] = ok ? o[k] * oun : 0.f;
-            if (ocol == 0) {
+            if (half == 0) {
                 float *ms = a.part_ms + (((size_t)split * a.R + r) * H + h) * 2;
-                ms[0] = ok ? mrow[orow] : -FLT_MAX, ms[1] = ok ? lrow[orow] : 0.f;
+                ms[0] = ok ? mrun : -FLT_MAX, ms[1] = ok ? lrun : 0.f;
             }
         }
     }
@@ -288,10 +390,25 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
 }
 
 size_t attend_tc_smem() {
-    return sizeof(__half) * (2 * 128 * 128 + 2 * 64 * 128 + 2 * 128 * 64 + 2 * 128 * 64) + 64 + sizeof(float) * 4 * 128 + 64;
+    return sizeof(__half) * (2 * TC_BQ * TC_HD + 2 * 4 * TC_BLOCK + 2 * TC_BQ * TC_BK) + sizeof(float) * 5 * TC_BQ +
+           4 * sizeof(uint64_t) + 16;
+}
+
+cudaError_t launch_tc_tiles(int kv, const AttnArgs &a, void *out, cudaStream_t s, uint64_t *launches) {
+    dim3 grid(a.ntiles, a.heads);
+    __half *o = reinterpret_cast<__half *>(out);
+    if (kv == 0)
+        k_tc_tiles<0><<<grid, 256, 0, s>>>(a, o);
+    else if (kv == 1)
+        k_tc_tiles<1><<<grid, 256, 0, s>>>(a, o);
+    else
+        k_tc_tiles<2><<<grid, 256, 0, s>>>(a, o);
+    if (launches) ++*launches;
+    return cudaGetLastError();
 }
 
 cudaError_t launch_attend_tc(int kv, const AttnArgs &a, cudaStream_t s, uint64_t *launches) {
+    if (!a.tc_tiles) return cudaErrorInvalidValue;
     const size_t smem = attend_tc_smem();
     dim3 grid((a.R + 127) / 128, a.heads, a.splits);
     cudaError_t e = cudaSuccess;

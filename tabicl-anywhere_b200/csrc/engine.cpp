@@ -130,6 +130,7 @@ struct tcu_model {
     // tensor-core attention: per layer, power-of-two scalings that keep keys and values inside f16
     std::vector<int> tc_eK, tc_eV;
     bool tc_scanned = false;
+    DevBuf tctiles;  // every layer's keys and values as pre-split tensor-core tiles (head width 128)
     // working memory, grown to the largest call so far
     DevBuf h, q, att, mid, stats, out, part_ms, part_acc;
     DevBuf sh_m, sh_mall, sh_packed;  // the cross-device merge: local maxima, their maximum, (values, weight sums)
@@ -581,11 +582,19 @@ static bool tc_enabled() {
 static Plan attend_plan(const tcu_ctx *ctx, int R, int heads, int hd, int nitems, int ntiles) {
     if (R <= 32) return {Path::Decode, nitems};
     if (hd == 128 && tc_enabled()) {
-        // one wave of one block per SM: 128 rows x head blocks, each over a share of the key tiles
+        // one block per SM at a time: (128 rows x head) blocks, each over a share of the key tiles; the split count
+        // that minimises waves x (tiles per block + a block's fixed cost, about 4 tiles: staging its queries,
+        // writing and merging its part); ties: fewer splits
         const int blocks = (R + 127) / 128 * heads;
-        int splits = std::max(1, std::min(ntiles, ctx->sms / blocks));
-        const int per = (ntiles + splits - 1) / splits;
-        return {Path::Tensor, (ntiles + per - 1) / per};
+        int best = 1;
+        long long best_cost = -1;
+        for (int sp = 1; sp <= std::min(ntiles, 64); sp++) {
+            const int per = (ntiles + sp - 1) / sp, used = (ntiles + per - 1) / per;
+            const long long waves = ((long long)blocks * used + ctx->sms - 1) / ctx->sms;
+            const long long cost = waves * (per + (used > 1 ? 4 : 0));
+            if (best_cost < 0 || cost < best_cost) best_cost = cost, best = used;
+        }
+        return {Path::Tensor, best};
     }
     return {Path::Flash, flash_splits(ctx, R, heads, ntiles)};
 }
@@ -618,7 +627,7 @@ static void ensure_work(tcu_model *m, int R) {
 // Returns the number of parts left in part_ms / part_acc when parts_only (the outputs are not finished then).
 static int attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int rows, int chunk, int kv, const int2 *items,
                         int nitems, const int4 *tiles, int ntiles, const float *q, int R, float *out, cudaStream_t s,
-                        int eK = 0, int eV = 0, bool parts_only = false) {
+                        int eK = 0, int eV = 0, bool parts_only = false, const void *tc_tiles = nullptr) {
     const auto &sh = m->w->shape;
     AttnArgs a;
     a.layer = layer, a.rows = rows, a.chunk = chunk, a.d = sh.d, a.heads = sh.heads;
@@ -663,7 +672,8 @@ static int attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int ro
     a.tiles_per_split = (ntiles + plan.splits - 1) / plan.splits;
     a.splits = (ntiles + a.tiles_per_split - 1) / a.tiles_per_split;
     if (plan.path == Path::Tensor) {
-        a.tc_eK = eK, a.tc_eV = eV, a.err = ctx->dev_err;
+        if (!tc_tiles) fail(TCU_ERR_STATE, "attend: tensor-core tiles were not built");
+        a.tc_eK = eK, a.tc_eV = eV, a.err = ctx->dev_err, a.tc_tiles = tc_tiles;
         ck(launch_attend_tc(kv, a, s, &ctx->launches), "attend (tensor cores)");
     } else {
         ck(launch_attend_flash(kv, hd, a, s, &ctx->launches), "attend (flash)");
@@ -704,12 +714,36 @@ static void scan_layer(tcu_ctx *ctx, const uint8_t *layer, int rows, int chunk, 
     eK = tc_exponent(mk), eV = tc_exponent(mv);
 }
 
+// The tensor-core tiles of one stored layer (its scalings eK, eV) into out: tc_tile_bytes() per (tile, head).
+static void build_tc_tiles(tcu_ctx *ctx, const tcu_model *m, const uint8_t *layer, int kv, int eK, int eV, void *out,
+                           cudaStream_t s) {
+    const auto &sh = m->w->shape;
+    AttnArgs a;
+    a.layer = layer, a.rows = m->rows, a.chunk = m->chunk, a.d = sh.d, a.heads = sh.heads;
+    a.full = record_bytes(kv, sh.d, m->chunk);
+    a.tiles = m->tiles.as<int4>(), a.ntiles = m->ntiles, a.tc_eK = eK, a.tc_eV = eV;
+    Launch{ctx, s}(launch_tc_tiles(kv, a, out, s, &ctx->launches), "tensor-core tiles");
+}
+
+static bool tc_shape(const tcu_model *m) { return m->w->shape.d / m->w->shape.heads == 128 && tc_enabled(); }
+static size_t tc_layer_bytes(const tcu_model *m) { return (size_t)m->ntiles * m->w->shape.heads * tc_tile_bytes(); }
+static const void *tc_tiles_of(const tcu_model *m, int l) {
+    return m->tctiles.p ? m->tctiles.as<uint8_t>() + tc_layer_bytes(m) * l : nullptr;
+}
+
 static void scan_model(tcu_ctx *ctx, tcu_model *m, cudaStream_t s) {
     if (m->tc_scanned) return;
     const int L = m->w->shape.layers;
     m->tc_eK.assign(L, 0), m->tc_eV.assign(L, 0);
     for (int l = 0; l < L; l++)
         scan_layer(ctx, layer_ptr(m, l), m->rows, m->chunk, m->w->shape.d, m->kv, s, m->tc_eK[l], m->tc_eV[l]);
+    if (tc_shape(m)) {
+        m->tctiles.ensure(tc_layer_bytes(m) * L);
+        for (int l = 0; l < L; l++)
+            build_tc_tiles(ctx, m, layer_ptr(m, l), m->kv, m->tc_eK[l], m->tc_eV[l],
+                           m->tctiles.as<uint8_t>() + tc_layer_bytes(m) * l, s);
+        CU(cudaStreamSynchronize(s));
+    }
     m->tc_scanned = true;
 }
 
@@ -741,7 +775,7 @@ static void stage(tcu_ctx *ctx, tcu_model *m, float *h, int R, int out_n, float 
     for (int l = 0; l < L; l++) {
         query_rows(ctx, m, l, scales + (size_t)l * d, h, R, m->q.as<float>(), s);
         attend_layer(ctx, m, layer_ptr(m, l), m->rows, m->chunk, m->kv, m->items.as<int2>(), m->nitems, m->tiles.as<int4>(),
-                     m->ntiles, m->q.as<float>(), R, m->att.as<float>(), s, m->tc_eK[l], m->tc_eV[l]);
+                     m->ntiles, m->q.as<float>(), R, m->att.as<float>(), s, m->tc_eK[l], m->tc_eV[l], false, tc_tiles_of(m, l));
         block_tail(ctx, m, l, h, m->att.as<float>(), R, s);
     }
     // predict.rs:570-584 decoder: only the first out_n outputs are computed (each output is its own row)
@@ -1002,7 +1036,8 @@ static void stage_sharded(tcu_ctx *ctx, tcu_model *m, tcu_comm *c, int R, int ou
     for (int l = 0; l < L; l++) {
         query_rows(ctx, m, l, scales + (size_t)l * d, h, R, q, s);
         const int parts = attend_layer(ctx, m, layer_ptr(m, l), m->rows, m->chunk, m->kv, m->items.as<int2>(), m->nitems,
-                                       m->tiles.as<int4>(), m->ntiles, q, R, att, s, m->tc_eK[l], m->tc_eV[l], true);
+                                       m->tiles.as<int4>(), m->ntiles, q, R, att, s, m->tc_eK[l], m->tc_eV[l], true,
+                                       tc_tiles_of(m, l));
         AttnArgs a;
         a.R = R, a.heads = H, a.d = d, a.part_ms = m->part_ms.as<float>(), a.part_acc = m->part_acc.as<float>();
         ck(launch_merge_local(a, parts, m->sh_m.as<float>(), m->sh_packed.as<float>(), s, &ctx->launches), "merge (local)");
@@ -1030,7 +1065,7 @@ static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, in
     const int d = sh.d, L = sh.layers;
     cudaStream_t s = ctx->stream;
     ensure_work(m.get(), rows);
-    DevBuf kvT, kvf;
+    DevBuf kvT, kvf, fit_tiles;
     kvT.ensure(sizeof(float) * (size_t)rows * 2 * d);
     kvf.ensure(layer_bytes_of(0, d, rows, chunk));
     Launch ck{ctx, s};
@@ -1051,10 +1086,16 @@ static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, in
         const uint8_t *fl = kv == 0 ? layer_ptr(m.get(), l) : kvf.as<uint8_t>();
         int eK = 0, eV = 0;
         scan_layer(ctx, fl, rows, chunk, d, 0, s, eK, eV);
+        const void *ft = nullptr;
+        if (tc_shape(m.get())) {
+            fit_tiles.ensure(tc_layer_bytes(m.get()));
+            build_tc_tiles(ctx, m.get(), fl, 0, eK, eV, fit_tiles.p, s);
+            ft = fit_tiles.p;
+        }
         query_rows(ctx, m.get(), l, m->scales.as<float>() + (size_t)l * d, h, rows, m->q.as<float>(), s);
         // the f32 view has the same chunking, and flash tiles depend only on chunking
         attend_layer(ctx, m.get(), fl, rows, chunk, 0, nullptr, 0, m->tiles.as<int4>(), m->ntiles, m->q.as<float>(), rows,
-                     m->att.as<float>(), s, eK, eV);
+                     m->att.as<float>(), s, eK, eV, false, ft);
         block_tail(ctx, m.get(), l, h, m->att.as<float>(), rows, s);
     }
     CU(cudaStreamSynchronize(s));
@@ -1312,7 +1353,7 @@ int tcu_attend_device(tcu_model *m, int layer, const float *q, int rows, float *
         scan_model(ctx, m, ctx->stream);
         ensure_work(m, rows);
         attend_layer(ctx, m, layer_ptr(m, layer), m->rows, m->chunk, m->kv, m->items.as<int2>(), m->nitems, m->tiles.as<int4>(),
-                     m->ntiles, q, rows, out, s, m->tc_eK[layer], m->tc_eV[layer]);
+                     m->ntiles, q, rows, out, s, m->tc_eK[layer], m->tc_eV[layer], false, tc_tiles_of(m, layer));
         return TCU_OK;
     });
 }

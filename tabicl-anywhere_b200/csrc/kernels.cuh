@@ -45,6 +45,7 @@ struct AttnArgs {
     int tc_eK = 0, tc_eV = 0;      // tensor-core path: power-of-two scalings of the keys and values
     int *err = nullptr;            // set to 1 when a kernel gave up waiting
     int parts_only = 0;            // 1: always leave parts (no merge), even with a single split
+    const void *tc_tiles = nullptr;  // tensor-core path: the layer's tiles pre-split by launch_tc_tiles
 };
 
 // The few-row stage in one persistent kernel: per layer, the pointers it reads.
@@ -147,6 +148,11 @@ cudaError_t kernels_init();
 // Tensor-core attention (head width 128, many rows): merges itself when splits == 1, else writes parts.
 cudaError_t launch_attend_tc(int kv, const AttnArgs &a, cudaStream_t s, uint64_t *launches);
 size_t attend_tc_smem();
+// The layer's keys and values as pre-split operand tiles for the tensor-core attention: one per (64-key tile of
+// a.tiles, head), tc_tile_bytes() each, [tile][head] order (uses a.layer, rows, chunk, d, heads, full, tiles,
+// ntiles, tc_eK, tc_eV).
+cudaError_t launch_tc_tiles(int kv, const AttnArgs &a, void *out, cudaStream_t s, uint64_t *launches);
+size_t tc_tile_bytes();
 // Largest |key| and |value| of a layer, as float bits, into out[0], out[1].
 cudaError_t launch_absmax_layer(const uint8_t *layer, int rows, int chunk, int d, int kv, unsigned *out, cudaStream_t s,
                                 uint64_t *launches);
