@@ -66,7 +66,7 @@ size_t tc_tile_bytes() { return 4 * TC_BLOCK * sizeof(__half); }
 
 // One tile (64 keys x one head) of a stored layer in the tensor cores' operand form, written once per model:
 // [keys hi][keys lo][values hi][values lo], each 64 x 128 f16 in the core-matrix layout the MMAs read from shared
-// memory (keys MN-major, values K-major). Integers are widened exactly and multiplied by their chunk's scale
+// memory, both K-major (a key's coordinates together for S = Q K^T; a coordinate's keys together for P V). Integers are widened exactly and multiplied by their chunk's scale
 // (predict.rs:486-497 for keys; nn.rs:253-256 for values, the same product taken per element), then by the layer's
 // power of two and split into hi + lo. Keys past a ragged tile's end are zero.
 template <int KV>
@@ -105,7 +105,9 @@ __global__ void __launch_bounds__(256) k_tc_tiles(AttnArgs a, __half *out) {
                     fv[e] = (x < EPV ? unpack<KV>(rv0, x) : unpack<KV>(rv1, x - EPV)) * vs;
                 }
                 const int key = vp * 2 * EPV + g;
-                put8(Khi, Klo, mnmajor_off(key, j, BK), fk, 1.f);
+#pragma unroll
+                for (int e = 0; e < 8; e++)
+                    split_f16(fk[e], Khi[kmajor_off(key + e, j, BK)], Klo[kmajor_off(key + e, j, BK)]);
                 put8(Vhi, Vlo, kmajor_off(j, key, HD), fv, 1.f);
             }
         }
@@ -117,7 +119,7 @@ __global__ void __launch_bounds__(256) k_tc_tiles(AttnArgs a, __half *out) {
                 fk = load_elem<KV>(body, (size_t)(h * HD + j) * rc + k0 + key) * (KV ? sc[h * HD + j] : 1.f);
                 fv = load_elem<KV>(body, (size_t)(d + h * HD + j) * rc + k0 + key) * (KV ? sc[d + h * HD + j] : 1.f);
             }
-            split_f16(fk * kscale, Khi[mnmajor_off(key, j, BK)], Klo[mnmajor_off(key, j, BK)]);
+            split_f16(fk * kscale, Khi[kmajor_off(key, j, BK)], Klo[kmajor_off(key, j, BK)]);
             split_f16(fv * vscale, Vhi[kmajor_off(j, key, HD)], Vlo[kmajor_off(j, key, HD)]);
         }
     }
@@ -138,42 +140,69 @@ __device__ __forceinline__ void expect_tx(uint64_t *mbar, uint32_t bytes) {
 }
 
 // Attention of 128 query rows x one head over a range of 64-key tiles, with the tiles pre-split (k_tc_tiles):
-//   S = Q K^T: Q [128 x 128] K-major, K [64 keys x 128] MN-major; hi*hi in TMEM columns 0-63, cross terms 64-127
-//   O += P V^T: P [128 x 64 keys] K-major, V [128 x 64 keys] K-major; per tile hi*hi in 128-255, cross 256-383
-// Each tile's four operand blocks arrive by bulk copies into one of two shared-memory stages, two tiles ahead. The
-// online softmax (nn.rs:207-215 rule) runs on all eight warps, two threads per query row (one per half of the
-// keys). While a tile's P V is folded into the registers' O, the next tile's S is already on the tensor cores.
-// Every f32 sum of tensor-core results is taken in registers (fresh accumulators per tile: the units' own f32
-// accumulation is not round-to-nearest). One thread issues the MMAs and copies; every wait is bounded.
+//   S = Q K^T: Q [128 x 128] K-major, K [64 keys x 128] MN-major; two S buffers in TMEM (columns 0-127, 128-255),
+//              hi*hi in the first 64 columns of a buffer, cross terms in the next 64
+//   O += P V^T: P [128 x 64 keys] K-major, V [128 x 64 keys] K-major; per tile hi*hi in 256-383, cross 384-511
+// Warp-specialised: warps 0-7 compute (the online softmax, nn.rs:207-215 rule, two threads per query row; the fold
+// of each tile's P V into O held in registers), one thread of warp 8 issues every MMA, one thread of warp 9 the bulk
+// copies of the key and value halves of each tile into two-slot rings. They hand over through mbarriers only (the
+// two producers in separate warps, so neither's waiting holds the other up), and the tensor cores work on tile
+// i + 1's scores while the softmax of tile i runs. Every f32 sum of tensor-core results is taken
+// in registers (fresh accumulators per tile: the units' own f32 accumulation is not round-to-nearest). Every wait
+// is bounded; a wait that gives up raises the block's abort flag and everyone leaves.
+constexpr int TC_THREADS = 320;  // eight compute warps, an MMA warp and a load warp
+
+// Named barrier 1 over the 256 compute threads, returning the AND of p over them (every compute thread takes the
+// same branch after it).
+__device__ __forceinline__ bool compute_all(bool p) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}\n"
+                 : "=r"(r)
+                 : "r"((uint32_t)p)
+                 : "memory");
+    return r != 0;
+}
+
 template <int KV>
-__global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
+__global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
     constexpr int HD = TC_HD, BQ = TC_BQ, BK = TC_BK;
     extern __shared__ __align__(1024) uint8_t smraw[];
     __half *Qhi = reinterpret_cast<__half *>(smraw);  // [BQ][HD] K-major
     __half *Qlo = Qhi + BQ * HD;
-    __half *stage0 = Qlo + BQ * HD;                   // two stages of [keys hi][keys lo][values hi][values lo]
-    __half *Phi = stage0 + 2 * 4 * TC_BLOCK;          // [BQ][BK keys] K-major
+    __half *Kring = Qlo + BQ * HD;                    // two slots of [keys hi][keys lo]
+    __half *Vring = Kring + 2 * 2 * TC_BLOCK;         // two slots of [values hi][values lo]
+    __half *Phi = Vring + 2 * 2 * TC_BLOCK;           // [BQ][BK keys] K-major
     __half *Plo = Phi + BQ * BK;
     float *fr = reinterpret_cast<float *>(Plo + BQ * BK);  // [BQ] this tile's rescale factor of each row
     float *redm = fr + BQ;                                 // [2][BQ] half-row maxima
     float *reds = redm + 2 * BQ;                           // [2][BQ] half-row weight sums
-    uint64_t *mbar = reinterpret_cast<uint64_t *>(reds + 2 * BQ);  // S ready, P V ready, stage 0 loaded, stage 1
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(mbar + 4);
+    uint64_t *mb = reinterpret_cast<uint64_t *>(reds + 2 * BQ);
+    uint64_t *mS = mb, *mSfree = mb + 2, *mK = mb + 4, *mV = mb + 6, *mP = mb + 8, *mPV = mb + 9, *mO = mb + 10,
+             *mDone = mb + 11;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(mb + 12);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
     float *qscale = reinterpret_cast<float *>(Phi);  // [BQ] 2^e of each row's query (until the first P)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.y, split = blockIdx.z, r0 = blockIdx.x * BQ, d = a.d, H = gridDim.y;
-    // a query row per (warp % 4, lane); keys / output columns by warp / 4
-    const int row = (warp & 3) * 32 + lane, half = warp >> 2;
     const int t0 = split * a.tiles_per_split, t1 = min(a.ntiles, t0 + a.tiles_per_split), nt = t1 - t0;
     const __half *tiles = reinterpret_cast<const __half *>(a.tc_tiles);
+    const bool producer = warp >= 8;
     if (warp == 0) {
         tmem_alloc(tslot, 512);
         tmem_relinquish();
     }
     if (tid == 0) {
-        for (int i = 0; i < 4; i++) mbar_init(&mbar[i], 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&mS[i], 1);
+            mbar_init(&mSfree[i], 256);
+            mbar_init(&mK[i], 1);
+            mbar_init(&mV[i], 1);
+        }
+        mbar_init(mP, 256);
+        mbar_init(mPV, 1);
+        mbar_init(mO, 256);
+        mbar_init(mDone, 1);
         mbar_init_fence();
         *abort_flag = 0;
     }
@@ -192,20 +221,19 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
         qscale[tid] = pow2f(f16_exponent(mx));
     }
     __syncthreads();
-    // the first two tiles start loading while the queries are split
-    auto load_tile = [&](int i) {  // thread 0: tile t0 + i into stage i & 1
-        const __half *src = tiles + ((size_t)(t0 + i) * H + h) * 4 * TC_BLOCK;
-        __half *dst = stage0 + (size_t)(i & 1) * 4 * TC_BLOCK;
-        uint64_t *mb = &mbar[2 + (i & 1)];
-        expect_tx(mb, (uint32_t)(4 * TC_BLOCK * sizeof(__half)));
-#pragma unroll
-        for (int b = 0; b < 4; b++) bulk_g2s(dst + b * TC_BLOCK, src + b * TC_BLOCK, (uint32_t)(TC_BLOCK * sizeof(__half)), mb);
+    const uint32_t half_bytes = (uint32_t)(2 * TC_BLOCK * sizeof(__half));
+    auto load = [&](int i, bool values) {  // producer thread: the key or value halves of tile t0 + i into slot i & 1
+        const __half *src = tiles + ((size_t)(t0 + i) * H + h) * 4 * TC_BLOCK + (values ? 2 * TC_BLOCK : 0);
+        __half *dst = (values ? Vring : Kring) + (size_t)(i & 1) * 2 * TC_BLOCK;
+        uint64_t *m = values ? &mV[i & 1] : &mK[i & 1];
+        expect_tx(m, half_bytes);
+        bulk_g2s(dst, src, half_bytes / 2, m);
+        bulk_g2s(dst + TC_BLOCK, src + TC_BLOCK, half_bytes / 2, m);
     };
-    if (tid == 0) {
-        if (nt > 0) load_tile(0);
-        if (nt > 1) load_tile(1);
+    if (warp == 9 && lane == 0) {
+        for (int i = 0; i < min(nt, 2); i++) load(i, false), load(i, true);
     }
-    for (int i = tid; i < BQ * (HD / 8); i += 256) {
+    for (int i = tid; i < BQ * (HD / 8); i += TC_THREADS) {
         const int m = i % BQ, j0 = (i / BQ) * 8, r = r0 + m;
         float v[8];
         if (r < a.R) {
@@ -218,154 +246,185 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
         }
         put8(Qhi, Qlo, kmajor_off(m, j0, BQ), v, qscale[m]);
     }
-    const float rs = (1.0f / qscale[row]) * pow2f(-a.tc_eK);  // undoes the query's and the keys' scalings
+    const int row = (warp & 3) * 32 + lane, half = (warp >> 2) & 1;
+    const float rs = producer ? 1.f : (1.0f / qscale[row]) * pow2f(-a.tc_eK);  // undoes both scalings
     fence_async_smem();
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
-    const uint32_t tmem = *tslot, tShh = tmem, tSx = tmem + 64, tOhh = tmem + 128, tOx = tmem + 256;
-    const uint32_t idS = idesc_f16(BQ, BK, 0, 1), idO = idesc_f16(BQ, HD, 0, 0);
+    const uint32_t tmem = *tslot, tO = tmem + 256;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    auto issue_S = [&](int i) {  // thread 0: S of tile t0 + i from its stage
-        const __half *K = stage0 + (size_t)(i & 1) * 4 * TC_BLOCK;
-#pragma unroll
-        for (int s = 0; s < HD / 16; s++) mma_f16(tShh, kstep_desc(Qhi, BQ, s), kstep_desc(K, BK, s), idS, s > 0 ? 1u : 0u);
-#pragma unroll
-        for (int s = 0; s < HD / 16; s++) {
-            mma_f16(tSx, kstep_desc(Qhi, BQ, s), kstep_desc(K + TC_BLOCK, BK, s), idS, s > 0 ? 1u : 0u);
-            mma_f16(tSx, kstep_desc(Qlo, BQ, s), kstep_desc(K, BK, s), idS, 1);
-        }
-        mma_commit(&mbar[0]);
-    };
-    uint32_t pS = 0, pO = 0, pK = 0;  // mbarrier parities (pK: bit per stage)
-    int issued = min(nt, 2);  // tiles whose loads were started
-    if (tid == 0 && nt > 0) {
-        if (mbar_wait(&mbar[2], 0, TC_WAIT_CYCLES)) {
-            fence_after_sync();
-            issue_S(0);
-        } else {
-            *abort_flag = 1;
-        }
-        pK = 1;
-    }
     float o[64];
 #pragma unroll
     for (int e = 0; e < 64; e++) o[e] = 0.f;
     float mrun = -FLT_MAX, lrun = 0.f;
     bool any = false;
-    int consumed = 0;
-    for (int i = 0; i < nt; i++) {
-        __syncthreads();
-        if (*abort_flag) break;
-        const int len = a.tiles[t0 + i].z;
-        // (1) the online softmax of S, two threads per row
-        const bool okS = mbar_wait(&mbar[0], pS, TC_WAIT_CYCLES);
-        pS ^= 1;
-        if (!okS) *abort_flag = 1;
-        fence_after_sync();
-        __syncwarp();
-        float s[32];
-        {
-            float x[32], y[32];
-            tmem_ld32(tShh + lane_base + 32 * half, x);
-            tmem_ld32(tSx + lane_base + 32 * half, y);
-            tmem_wait_ld();
-#pragma unroll
-            for (int k = 0; k < 32; k++) s[k] = (x[k] + y[k]) * rs;
-        }
-        float mx = -FLT_MAX;
-#pragma unroll
-        for (int k = 0; k < 32; k++)
-            if (32 * half + k < len) mx = fmaxf(mx, s[k]);
-        redm[half * BQ + row] = mx;
-        fence_before_sync();
-        __syncthreads();
-        const float mnew = fmaxf(mrun, fmaxf(redm[row], redm[BQ + row]));
-        const float f = lrun > 0.f ? exp_sfu(mrun - mnew) : 0.f;
-        float psum = 0.f;
-#pragma unroll
-        for (int k = 0; k < 32; k++) {
-            const float p = 32 * half + k < len ? exp_sfu(s[k] - mnew) : 0.f;
-            s[k] = p * 16384.f;  // 2^14: small weights stay normal in f16
-            psum += p;
-        }
-        reds[half * BQ + row] = psum;
-        if (half == 0) fr[row] = f;
-#pragma unroll
-        for (int g = 0; g < 4; g++) {
-            float v[8];
-#pragma unroll
-            for (int e = 0; e < 8; e++) v[e] = s[g * 8 + e];
-            put8x2(Phi, Plo, kmajor_off(row, 32 * half + g * 8, BQ), v);
-        }
-        fence_async_smem();
-        fence_before_sync();
-        __syncthreads();
-        lrun = lrun * f + (reds[row] + reds[BQ + row]);
-        mrun = mnew;
-        // (2) this tile's P V, then the next tile's S (its stage loaded)
-        if (tid == 0) {
-            fence_after_sync();
-            const __half *V = stage0 + (size_t)(i & 1) * 4 * TC_BLOCK + 2 * TC_BLOCK;
-#pragma unroll
-            for (int s2 = 0; s2 < BK / 16; s2++)
-                mma_f16(tOhh, kstep_desc(Phi, BQ, s2), kstep_desc(V, HD, s2), idO, s2 > 0 ? 1u : 0u);
-#pragma unroll
-            for (int s2 = 0; s2 < BK / 16; s2++) {
-                mma_f16(tOx, kstep_desc(Phi, BQ, s2), kstep_desc(V + TC_BLOCK, HD, s2), idO, s2 > 0 ? 1u : 0u);
-                mma_f16(tOx, kstep_desc(Plo, BQ, s2), kstep_desc(V, HD, s2), idO, 1);
+
+    if (producer) {
+        auto wait = [&](uint64_t *m, uint32_t parity) {
+            if (*abort_flag) return false;
+            if (!mbar_wait(m, parity, TC_WAIT_CYCLES)) {
+                *abort_flag = 1;
+                return false;
             }
-            mma_commit(&mbar[1]);
-            if (i + 1 < nt) {
-                const int st = (i + 1) & 1;
-                if (mbar_wait(&mbar[2 + st], (pK >> st) & 1u, TC_WAIT_CYCLES)) {
-                    fence_after_sync();
-                    issue_S(i + 1);
-                } else {
-                    *abort_flag = 1;
+            return true;
+        };
+        if (warp == 8 && lane == 0) {
+            // the MMA thread: waits only for what its next MMAs read
+            const uint32_t idS = idesc_f16(BQ, BK, 0, 0), idO = idesc_f16(BQ, HD, 0, 0);
+            // Descriptors: K-step k of an operand is its k = 0 descriptor plus k times the step of its start address
+            // (the address sits in the low bits, in 16-byte units), so each MMA costs one add, not a recomputation.
+            const uint64_t dQh = kstep_desc(Qhi, BQ, 0), dQl = kstep_desc(Qlo, BQ, 0);
+            const uint64_t dK0 = kstep_desc(Kring, BK, 0), dV0 = kstep_desc(Vring, HD, 0);
+            const uint64_t dPh = kstep_desc(Phi, BQ, 0), dPl = kstep_desc(Plo, BQ, 0);
+            const uint64_t stQ = (2 * (BQ / 8) * 128) >> 4, stK = (2 * (BK / 8) * 128) >> 4, stV = (2 * (HD / 8) * 128) >> 4;
+            const uint64_t lo_off = (TC_BLOCK * sizeof(__half)) >> 4, slot_off = (2 * TC_BLOCK * sizeof(__half)) >> 4;
+            auto issue_S = [&](int i) {
+                const uint32_t tS = tmem + 128 * (i & 1);
+                const uint64_t dKh = dK0 + (i & 1) * slot_off, dKl = dKh + lo_off;
+                fence_after_sync();
+#pragma unroll
+                for (int k = 0; k < HD / 16; k++) {
+                    mma_f16(tS, dQh + k * stQ, dKh + k * stK, idS, k > 0 ? 1u : 0u);
+                    mma_f16(tS + 64, dQh + k * stQ, dKl + k * stK, idS, k > 0 ? 1u : 0u);
+                    mma_f16(tS + 64, dQl + k * stQ, dKh + k * stK, idS, 1);
                 }
-                pK ^= 1u << st;
+                mma_commit(&mS[i & 1]);
+            };
+            bool ok = true;
+            for (int i = 0; i < min(nt, 2) && ok; i++) {
+                ok = wait(&mK[i & 1], 0);
+                if (ok) issue_S(i);
             }
-        }
-        // (3) fold this tile's P V into O: O = O * f + (hi*hi + cross terms)
-        const bool okO = mbar_wait(&mbar[1], pO, TC_WAIT_CYCLES);
-        pO ^= 1;
-        if (!okO) *abort_flag = 1;
-        fence_after_sync();
-        __syncwarp();
-        if (okO) {
-            const float fo = fr[row];
+            for (int i = 0; i < nt && ok; i++) {
+                const int b = i & 1;
+                const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+                // P V of tile i: its P written, its values here, O's accumulators folded
+                if (!(ok = wait(mP, (uint32_t)i & 1u))) break;
+                if (!(ok = wait(&mV[b], ph))) break;
+                if (i > 0 && !(ok = wait(mO, (uint32_t)(i - 1) & 1u))) break;
+                fence_after_sync();
+                {
+                    const uint64_t dVh = dV0 + b * slot_off, dVl = dVh + lo_off;
 #pragma unroll
-            for (int c = 0; c < 2; c++) {
+                    for (int k = 0; k < BK / 16; k++) {
+                        mma_f16(tO, dPh + k * stQ, dVh + k * stV, idO, k > 0 ? 1u : 0u);
+                        mma_f16(tO + 128, dPh + k * stQ, dVl + k * stV, idO, k > 0 ? 1u : 0u);
+                        mma_f16(tO + 128, dPl + k * stQ, dVh + k * stV, idO, 1);
+                    }
+                    mma_commit(mPV);
+                }
+                // S of tile i + 2 into the buffer the softmax of tile i has read, from its keys
+                if (i + 2 < nt) {
+                    if (!(ok = wait(&mSfree[b], ph))) break;
+                    if (!(ok = wait(&mK[b], (uint32_t)((i + 2) >> 1) & 1u))) break;
+                    issue_S(i + 2);
+                }
+            }
+            // every MMA completes before the block lets go of tensor memory
+            mma_commit(mDone);
+            mbar_wait(mDone, 0, TC_WAIT_CYCLES);
+        } else if (warp == 9 && lane == 0) {
+            // the load thread: tile i + 2's keys where tile i's were once S(i) is done, its values once P V(i) is
+            int ki = min(nt, 2), vi = min(nt, 2);  // key / value loads started
+            for (int i = 0; i + 2 < nt; i++) {
+                const int b = i & 1;
+                if (!wait(&mS[b], (uint32_t)(i >> 1) & 1u)) break;
+                load(i + 2, false);
+                ki = i + 3;
+                if (!wait(mPV, (uint32_t)i & 1u)) break;
+                load(i + 2, true);
+                vi = i + 3;
+            }
+            // the last load into each slot lands before the block lets go of shared memory
+            for (int j = max(0, ki - 2); j < ki; j++) mbar_wait(&mK[j & 1], (uint32_t)(j >> 1) & 1u, TC_WAIT_CYCLES);
+            for (int j = max(0, vi - 2); j < vi; j++) mbar_wait(&mV[j & 1], (uint32_t)(j >> 1) & 1u, TC_WAIT_CYCLES);
+        }
+    } else {
+        bool alive = true;
+        for (int i = 0; i < nt; i++) {
+            const int b = i & 1;
+            const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+            const int len = a.tiles[t0 + i].z;
+            // (1) the online softmax of S(i), two threads per row; the compute warps leave together or not at all
+            const bool okS = alive && !*abort_flag && mbar_wait(&mS[b], ph, TC_WAIT_CYCLES);
+            if (!compute_all(okS)) {
+                if (tid == 0) *abort_flag = 1;
+                alive = false;
+                break;
+            }
+            fence_after_sync();
+            __syncwarp();
+            float s[32];
+            {
                 float x[32], y[32];
-                tmem_ld32(tOhh + lane_base + 64 * half + 32 * c, x);
-                tmem_ld32(tOx + lane_base + 64 * half + 32 * c, y);
+                const uint32_t tS = tmem + 128 * b + lane_base + 32 * half;
+                tmem_ld32(tS, x);
+                tmem_ld32(tS + 64, y);
                 tmem_wait_ld();
 #pragma unroll
-                for (int k = 0; k < 32; k++) o[32 * c + k] = fmaf(o[32 * c + k], fo, x[k] + y[k]);
+                for (int k = 0; k < 32; k++) s[k] = (x[k] + y[k]) * rs;
             }
+            fence_before_sync();
+            mbar_arrive(&mSfree[b]);
+            float mx = -FLT_MAX;
+#pragma unroll
+            for (int k = 0; k < 32; k++)
+                if (32 * half + k < len) mx = fmaxf(mx, s[k]);
+            redm[half * BQ + row] = mx;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            const float mnew = fmaxf(mrun, fmaxf(redm[row], redm[BQ + row]));
+            const float f = lrun > 0.f ? exp_sfu(mrun - mnew) : 0.f;
+            float psum = 0.f;
+#pragma unroll
+            for (int k = 0; k < 32; k++) {
+                const float p = 32 * half + k < len ? exp_sfu(s[k] - mnew) : 0.f;
+                s[k] = p * 16384.f;  // 2^14: small weights stay normal in f16
+                psum += p;
+            }
+            reds[half * BQ + row] = psum;
+            if (half == 0) fr[row] = f;
+#pragma unroll
+            for (int g = 0; g < 4; g++) {
+                float v[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[e] = s[g * 8 + e];
+                put8x2(Phi, Plo, kmajor_off(row, 32 * half + g * 8, BQ), v);
+            }
+            fence_async_smem();
+            mbar_arrive(mP);
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            lrun = lrun * f + (reds[row] + reds[BQ + row]);
+            mrun = mnew;
+            // (2) fold P V(i) into O: O = O * f + (hi*hi + cross terms); a failed wait is voted on at the next step
+            alive = mbar_wait(mPV, (uint32_t)i & 1u, TC_WAIT_CYCLES);
+            fence_after_sync();
+            __syncwarp();
+            if (alive) {
+                const float fo = fr[row];
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    float x[32], y[32];
+                    tmem_ld32(tO + lane_base + 64 * half + 32 * c, x);
+                    tmem_ld32(tO + 128 + lane_base + 64 * half + 32 * c, y);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int k = 0; k < 32; k++) o[32 * c + k] = fmaf(o[32 * c + k], fo, x[k] + y[k]);
+                }
+            }
+            fence_before_sync();
+            mbar_arrive(mO);
+            any = true;
         }
-        any = true;
-        consumed = i + 1;
-        fence_before_sync();
-        __syncthreads();
-        // (4) this tile's stage is free (its S and P V are done): the tile two ahead goes there
-        if (tid == 0 && i + 2 < nt && !*abort_flag) {
-            load_tile(i + 2);
-            issued = i + 3;
+        if (!compute_all(alive)) {
+            if (tid == 0) *abort_flag = 1;
         }
     }
-    // leaving early: loads still in flight land before the shared memory is given up
-    if (tid == 0) {
-        for (int i = max(consumed + 1, 1); i < issued; i++) {
-            const int st = i & 1;
-            mbar_wait(&mbar[2 + st], (pK >> st) & 1u, TC_WAIT_CYCLES);
-            pK ^= 1u << st;
-        }
-    }
+    fence_before_sync();
+    __syncthreads();
     const bool ok = any && !*abort_flag;
     const int r = r0 + row;
-    if (r < a.R) {
+    if (!producer && r < a.R) {
         const float oun = pow2f(-14 - a.tc_eV);
         const int col = 64 * half;
         if (a.splits == 1 && !a.parts_only) {
@@ -384,14 +443,12 @@ __global__ void __launch_bounds__(256, 1) k_attend_tc(AttnArgs a) {
         }
     }
     if (*abort_flag && tid == 0 && a.err) atomicExch(a.err, 1);
-    fence_before_sync();
-    __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 size_t attend_tc_smem() {
     return sizeof(__half) * (2 * TC_BQ * TC_HD + 2 * 4 * TC_BLOCK + 2 * TC_BQ * TC_BK) + sizeof(float) * 5 * TC_BQ +
-           4 * sizeof(uint64_t) + 16;
+           12 * sizeof(uint64_t) + 16;
 }
 
 cudaError_t launch_tc_tiles(int kv, const AttnArgs &a, void *out, cudaStream_t s, uint64_t *launches) {
@@ -414,13 +471,13 @@ cudaError_t launch_attend_tc(int kv, const AttnArgs &a, cudaStream_t s, uint64_t
     cudaError_t e = cudaSuccess;
     if (kv == 0) {
         e = cudaFuncSetAttribute(k_attend_tc<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e == cudaSuccess) k_attend_tc<0><<<grid, 256, smem, s>>>(a);
+        if (e == cudaSuccess) k_attend_tc<0><<<grid, TC_THREADS, smem, s>>>(a);
     } else if (kv == 1) {
         e = cudaFuncSetAttribute(k_attend_tc<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e == cudaSuccess) k_attend_tc<1><<<grid, 256, smem, s>>>(a);
+        if (e == cudaSuccess) k_attend_tc<1><<<grid, TC_THREADS, smem, s>>>(a);
     } else {
         e = cudaFuncSetAttribute(k_attend_tc<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e == cudaSuccess) k_attend_tc<2><<<grid, 256, smem, s>>>(a);
+        if (e == cudaSuccess) k_attend_tc<2><<<grid, TC_THREADS, smem, s>>>(a);
     }
     if (e != cudaSuccess) return e;
     e = cudaGetLastError();

@@ -61,6 +61,10 @@ __device__ __forceinline__ void mbar_init(uint64_t *mbar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(mbar)), "r"(count) : "memory");
 }
 __device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+// One arrival (release) on the mbarrier by this thread.
+__device__ __forceinline__ void mbar_arrive(uint64_t *mbar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}\n" ::"r"(smem_addr(mbar)) : "memory");
+}
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *mbar, uint32_t parity) {
     uint32_t ok;
