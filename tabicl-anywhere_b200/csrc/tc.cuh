@@ -76,9 +76,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *mbar, uint32_t parity) {
     return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *mbar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(mbar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Wait for the mbarrier phase with the given parity to complete, giving up after about `cycles` clock cycles
-// (false: the caller records the failure and leaves without hanging the GPU).
+// (false: the caller records the failure and leaves without hanging the GPU). A phase already complete is seen by
+// one non-blocking test.
 __device__ __forceinline__ bool mbar_wait(uint64_t *mbar, uint32_t parity, long long cycles) {
+    if (mbar_test_wait(mbar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(mbar, parity)) {
         if (clock64() - t0 > cycles) return false;
