@@ -100,7 +100,7 @@ struct SplitW {
 struct LayerPtrs {
     const float *n1w, *n1b, *wq, *bq, *q0w, *q0b, *q2w, *q2b, *wo, *bo, *n2w, *n2b, *w1, *b1, *w2, *b2;
     const float *wkv, *bkv;  // fit only: in_proj rows d..3d
-    SplitW tq, to, t1, t2, tkv;
+    SplitW tq, to, t1, t2, tkv, tq0, tq2;  // tq0 / tq2: the query MLP (hid x hd, hd x hid)
 };
 
 struct tcu_weights {
@@ -132,7 +132,7 @@ struct tcu_model {
     bool tc_scanned = false;
     DevBuf tctiles;  // every layer's keys and values as pre-split tensor-core tiles (head width 128)
     // working memory, grown to the largest call so far
-    DevBuf h, q, att, mid, stats, out, part_ms, part_acc;
+    DevBuf h, q, att, mid, stats, out, part_ms, part_acc, ssm;  // ssm: the query MLP's hidden units and outputs
     DevBuf sh_m, sh_mall, sh_packed;  // the cross-device merge: local maxima, their maximum, (values, weight sums)
     // the one-kernel few-row stage: key tiles (head-major), per-layer pointer table, barrier words, partials
     DevBuf rtiles, rlayers, rsync, rparts_ms, rparts_acc, rtmaps;
@@ -454,7 +454,7 @@ static int weights_ready(tcu_weights *w) {
         ix.unscale = add(un);
         return ix;
     };
-    std::vector<std::array<SplitIdx, 5>> lsplit(L);
+    std::vector<std::array<SplitIdx, 7>> lsplit(L);
     for (int l = 0; l < L; l++) {
         const LIdx &x = li[l];
         lsplit[l][0] = split(flat.data() + offs[x.wq], d, d);
@@ -462,6 +462,8 @@ static int weights_ready(tcu_weights *w) {
         lsplit[l][2] = split(flat.data() + offs[x.w1], ff, d);
         lsplit[l][3] = split(flat.data() + offs[x.w2], d, ff);
         if (w->for_fit) lsplit[l][4] = split(flat.data() + offs[x.wkv], 2 * d, d);
+        lsplit[l][5] = split(flat.data() + offs[x.q0w], hid, hd);
+        lsplit[l][6] = split(flat.data() + offs[x.q2w], hd, hid);
     }
     const SplitIdx s_dec0 = split(flat.data() + offs[i_d0w], dff, d);
     const SplitIdx s_dec2 = split(flat.data() + offs[i_d2w], outs, dff);
@@ -482,6 +484,7 @@ static int weights_ready(tcu_weights *w) {
         if (w->for_fit) p.wkv = P(x.wkv), p.bkv = P(x.bkv);
         p.tq = S(lsplit[l][0]), p.to = S(lsplit[l][1]), p.t1 = S(lsplit[l][2]), p.t2 = S(lsplit[l][3]);
         if (w->for_fit) p.tkv = S(lsplit[l][4]);
+        p.tq0 = S(lsplit[l][5]), p.tq2 = S(lsplit[l][6]);
     }
     w->lnw = P(i_lnw), w->lnb = P(i_lnb), w->dec0w = P(i_d0w), w->dec0b = P(i_d0b), w->dec2w = P(i_d2w), w->dec2b = P(i_d2b);
     w->tdec0 = S(s_dec0), w->tdec2 = S(s_dec2);
@@ -613,7 +616,8 @@ static void ensure_work(tcu_model *m, int R) {
     moved |= m->q.ensure(sizeof(float) * R * d);
     moved |= m->att.ensure(sizeof(float) * R * d);
     moved |= m->mid.ensure(sizeof(float) * R * wide);
-    moved |= m->stats.ensure(sizeof(float) * R * 4);
+    moved |= m->stats.ensure(sizeof(float) * R * 4 * std::max<size_t>(H, 1));  // per row, or per (row, head)
+    if (R > 16) moved |= m->ssm.ensure(sizeof(float) * R * (H * (size_t)s.hid + d));
     const Plan plan = attend_plan(m->w->ctx, R, s.heads, s.d / s.heads, m->nitems, m->ntiles);
     const size_t pr = plan.path == Path::Decode ? (size_t)m->nitems : (size_t)plan.splits;  // parts, when left
     if (pr) {
@@ -753,7 +757,17 @@ static void query_rows(tcu_ctx *ctx, tcu_model *m, int l, const float *scale, co
     const LayerPtrs &p = m->w->layer[l];
     const int d = sh.d;
     linear(ctx, m, h, d, R, d, p.n1w, p.n1b, p.wq, p.bq, d, q, d, 0, 0, s, p.tq);  // nn.rs:136-137
-    Launch{ctx, s}(launch_ssmax(q, R, d, sh.heads, sh.hid, p.q0w, p.q0b, p.q2w, p.q2b, scale, s, &ctx->launches), "ssmax");
+    if (R <= 16) {
+        Launch{ctx, s}(launch_ssmax(q, R, d, sh.heads, sh.hid, p.q0w, p.q0b, p.q2w, p.q2b, scale, s, &ctx->launches), "ssmax");
+        return;
+    }
+    // nn.rs:138-149 over all (row, head) pairs at once: q viewed as [R * heads][hd] (a row's heads are contiguous),
+    // m = W2 GELU(W0 q_h + b0) + b2 as two linear layers, then q_h *= scale_h (1 + tanh m)
+    const int H = sh.heads, hd = d / H, hid = sh.hid;
+    float *hs = m->ssm.as<float>(), *mm = hs + (size_t)R * H * hid;
+    linear(ctx, m, q, hd, R * H, hd, nullptr, nullptr, p.q0w, p.q0b, hid, hs, hid, 1, 0, s, p.tq0);
+    linear(ctx, m, hs, hid, R * H, hid, nullptr, nullptr, p.q2w, p.q2b, hd, mm, hd, 0, 0, s, p.tq2);
+    Launch{ctx, s}(launch_ssmax_apply(q, mm, scale, R, d, s, &ctx->launches), "ssmax (apply)");
 }
 
 static void block_tail(tcu_ctx *ctx, tcu_model *m, int l, float *h, const float *att, int R, cudaStream_t s) {

@@ -276,6 +276,13 @@ __global__ void __launch_bounds__(256) k_ssmax_rows(float *q, int d, int heads, 
     }
 }
 
+// q_h *= scale_h * (1 + tanh(m)) for every (row, coordinate), m the query MLP's output (nn.rs:148).
+__global__ void k_ssmax_apply(float *q, const float *m, const float *scale, int R, int d) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)R * d) return;
+    q[i] = q[i] * (scale[i % d] * (1.0f + tanh1(m[i])));
+}
+
 // ---- attention over the stored cache ------------------------------------------------------------------------
 
 // A 16-byte vector of stored elements from any alignment, zero past `len` (ragged chunk tails).
@@ -995,6 +1002,14 @@ cudaError_t launch_ssmax(float *q, int R, int d, int heads, int hid, const float
     if (e != cudaSuccess) return e;
     dim3 grid((R + rb - 1) / rb, heads);
     k_ssmax<<<grid, 256, smem, s>>>(q, R, d, heads, hid, q0w, q0b, q2w, q2b, scale, rb);
+    TCU_LAUNCHED(launches);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ssmax_apply(float *q, const float *m, const float *scale, int R, int d, cudaStream_t s,
+                               uint64_t *launches) {
+    const size_t n = (size_t)R * d;
+    k_ssmax_apply<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, m, scale, R, d);
     TCU_LAUNCHED(launches);
     return cudaGetLastError();
 }

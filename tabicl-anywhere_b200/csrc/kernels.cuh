@@ -119,6 +119,9 @@ cudaError_t launch_ln_apply(const float *x, int M, int K, const float *w, const 
                             uint64_t *launches);
 cudaError_t launch_ssmax(float *q, int R, int d, int heads, int hid, const float *q0w, const float *q0b,
                          const float *q2w, const float *q2b, const float *scale, cudaStream_t s, uint64_t *launches);
+// q *= scale (1 + tanh(m)) elementwise over [R][d] (scale indexed by coordinate)
+cudaError_t launch_ssmax_apply(float *q, const float *m, const float *scale, int R, int d, cudaStream_t s,
+                               uint64_t *launches);
 // keys-parallel split attention for few rows, then the merge into out
 cudaError_t launch_attend_decode(int kv, int hd, const AttnArgs &a, cudaStream_t s, uint64_t *launches);
 // row-blocked attention for many rows; merges itself when splits == 1, else writes parts
