@@ -90,9 +90,10 @@ struct tcu_ctx {
     unsigned *dev_scan = nullptr; // scratch of the per-layer magnitude scan
 };
 
-// A weight matrix [N][K] split once for the tensor cores: f16 hi + lo (bit patterns) of W * 2^e(n), and 2^-e(n).
+// A weight matrix [N][K] split once for the tensor cores: f16 hi + lo (bit patterns) of W * 2^e(n) in 128 x 64
+// blocks (tc_block_off), and 2^-e(n). No blocks when K is not a multiple of 64.
 struct SplitW {
-    const uint16_t *hi = nullptr, *lo = nullptr;
+    const uint16_t *tiles = nullptr;
     const float *unscale = nullptr;
 };
 
@@ -132,7 +133,7 @@ struct tcu_model {
     bool tc_scanned = false;
     DevBuf tctiles;  // every layer's keys and values as pre-split tensor-core tiles (head width 128)
     // working memory, grown to the largest call so far
-    DevBuf h, q, att, mid, stats, out, part_ms, part_acc, ssm;  // ssm: the query MLP's hidden units and outputs
+    DevBuf h, q, att, mid, stats, out, part_ms, part_acc, ssm, atiles;  // atiles: rows split for the tensor cores  // ssm: the query MLP's hidden units and outputs
     DevBuf sh_m, sh_mall, sh_packed;  // the cross-device merge: local maxima, their maximum, (values, weight sums)
     // the one-kernel few-row stage: key tiles (head-major), per-layer pointer table, barrier words, partials
     DevBuf rtiles, rlayers, rsync, rparts_ms, rparts_acc, rtmaps;
@@ -427,15 +428,18 @@ static int weights_ready(tcu_weights *w) {
     // tensor-core copies of the linear layers' weights: f16 hi + lo per row, scaled to stay inside f16
     std::vector<uint16_t> half;
     struct SplitIdx {
-        size_t hi, lo, unscale;
+        size_t tiles, unscale;
+        bool on;
     };
     auto split = [&](const float *src_in, int N, int K) {
+        SplitIdx ix{0, 0, K % 64 == 0};
+        if (!ix.on) return ix;
         const std::vector<float> src_copy(src_in, src_in + (size_t)N * K);  // add() below may move `flat`
         const float *src = src_copy.data();
-        SplitIdx ix;
-        ix.hi = (half.size() + 127) / 128 * 128;
-        ix.lo = ix.hi + (size_t)N * K;
-        half.resize(ix.lo + (size_t)N * K);
+        const int nts = (N + 127) / 128, nk = K / 64;
+        const size_t blk = 128 * 64;
+        ix.tiles = (half.size() + 127) / 128 * 128;
+        half.resize(ix.tiles + (size_t)nts * nk * 2 * blk, 0);  // rows past N stay zero
         std::vector<float> un(N);
         for (int n = 0; n < N; n++) {
             const float *row = src + (size_t)n * K;
@@ -447,8 +451,10 @@ static int weights_ready(tcu_weights *w) {
             for (int k = 0; k < K; k++) {
                 const float x = row[k] * sc;  // exact: a power of two
                 const uint16_t h = f32_to_f16(x);
-                half[ix.hi + (size_t)n * K + k] = h;
-                half[ix.lo + (size_t)n * K + k] = f32_to_f16(x - f16_to_f32(h));
+                uint16_t *b = half.data() + ix.tiles + ((size_t)(n / 128) * nk + k / 64) * 2 * blk;
+                const size_t off = tc_block_off(n, k);
+                b[off] = h;
+                b[blk + off] = f32_to_f16(x - f16_to_f32(h));
             }
         }
         ix.unscale = add(un);
@@ -474,7 +480,7 @@ static int weights_ready(tcu_weights *w) {
     const float *base = w->dev.as<float>();
     const uint16_t *hbase = w->dev16.as<uint16_t>();
     auto P = [&](size_t idx) { return base + offs[idx]; };
-    auto S = [&](const SplitIdx &ix) { return SplitW{hbase + ix.hi, hbase + ix.lo, base + offs[ix.unscale]}; };
+    auto S = [&](const SplitIdx &ix) { return ix.on ? SplitW{hbase + ix.tiles, base + offs[ix.unscale]} : SplitW(); };
     w->layer.resize(L);
     for (int l = 0; l < L; l++) {
         const LIdx &x = li[l];
@@ -618,6 +624,11 @@ static void ensure_work(tcu_model *m, int R) {
     moved |= m->mid.ensure(sizeof(float) * R * wide);
     moved |= m->stats.ensure(sizeof(float) * R * 4 * std::max<size_t>(H, 1));  // per row, or per (row, head)
     if (R > 16) moved |= m->ssm.ensure(sizeof(float) * R * (H * (size_t)s.hid + d));
+    if (R > 8) {
+        size_t at = tc_split_bytes(R, (int)std::max<size_t>(d, wide));
+        if (R > 16) at = std::max(at, tc_split_bytes(R * (int)H, std::max(s.d / s.heads, s.hid)));
+        moved |= m->atiles.ensure(at);
+    }
     const Plan plan = attend_plan(m->w->ctx, R, s.heads, s.d / s.heads, m->nitems, m->ntiles);
     const size_t pr = plan.path == Path::Decode ? (size_t)m->nitems : (size_t)plan.splits;  // parts, when left
     if (pr) {
@@ -691,7 +702,8 @@ static void linear(tcu_ctx *ctx, tcu_model *m, const float *x, int ldx, int R, i
     LinArgs a;
     a.x = x, a.ldx = ldx, a.M = R, a.K = K, a.lnw = lnw, a.lnb = lnb, a.W = W, a.bias = b, a.N = N, a.y = y, a.ldy = ldy;
     a.act = act, a.accumulate = accumulate, a.transpose_out = transpose_out;
-    a.tc_whi = tw.hi, a.tc_wlo = tw.lo, a.tc_wunscale = tw.unscale, a.err = ctx->dev_err;
+    a.tc_wtiles = tw.tiles, a.tc_wunscale = tw.unscale, a.err = ctx->dev_err;
+    a.tc_atiles = m->atiles.p, a.tc_atiles_bytes = m->atiles.bytes;
     Launch{ctx, s}(launch_linear(a, m->stats.as<float>(), s, &ctx->launches), "linear");
 }
 

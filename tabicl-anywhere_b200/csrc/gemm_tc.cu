@@ -1,11 +1,16 @@
 // Linear layers of many rows on the tensor cores (tcgen05) at f32 accuracy: y (=|+=) act(W LN?(x) + b).
 //
-// A CTA computes a 128-row x 128-output tile, K in chunks of 64 staged twice-buffered in shared memory.
-// Activations are split into f16 hi + lo on the fly after a power-of-two scaling per row (from a stats pass that
-// also gives the LayerNorm's mean and 1/sigma); weights were split once at upload with a scaling per output row.
-// The product is taken as hi*hi + hi*lo + lo*hi in one f32 accumulator in tensor memory; the epilogue undoes the
-// two scalings, adds the bias, applies GELU and the residual, and writes through shared memory so that stores
-// are coalesced (also when the output is written transposed).
+// Both operands reach the kernel already split into f16 hi + lo (x = hi + lo, about 22 significant bits) and laid
+// out in 128 x 64 blocks exactly as the MMAs read them from shared memory:
+//   weights - once, at upload, with a power-of-two scaling per output row (the engine's weight upload);
+//   activations - per call by k_split_rows, which also applies the LayerNorm (kern.rs:357-376) and a power-of-two
+//   scaling per row.
+// A CTA computes a 128-row x 128-output tile. Warp-specialised: one thread bulk-copies each 64-wide chunk of K (the
+// activation and weight blocks, 64 KB) into a three-slot ring; one thread issues the chunk's MMAs (hi*hi into one
+// fresh accumulator, the two cross terms into another: the tensor cores' f32 accumulation is not round-to-nearest,
+// so no accumulator sees more than 12 steps); eight warps add each chunk's accumulators into registers with
+// ordinary f32 arithmetic while the next chunk multiplies. The epilogue undoes the scalings, adds the bias, applies
+// GELU and the residual, and writes through shared memory so stores are coalesced (also transposed).
 #include <cfloat>
 #include <cstdlib>
 
@@ -18,190 +23,234 @@ namespace tcu {
 using namespace tc;
 
 constexpr long long GEMM_WAIT_CYCLES = 2000000000ll;
+constexpr int GBM = 128, GBN = 128, GBK = 64, GSTAGES = 3, GTHREADS = 320;
+constexpr size_t GBLOCK = (size_t)GBM * GBK;  // halves in one operand block (hi or lo)
 
 __device__ __forceinline__ float p2(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
 
-// Per row: LayerNorm mean and 1/sigma (when lnw is set, else 0 and 1), then the power-of-two scale that keeps the
-// row's largest transformed magnitude below 2^14 and its inverse: stats[m] = {mean, rstd, scale, unscale}.
-__global__ void k_row_stats_tc(const float *x, int ldx, int M, int K, const float *lnw, const float *lnb, float4 *stats) {
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (row >= M) return;
-    const float *p = x + (size_t)row * ldx;
-    float mean = 0.f, inv = 1.f;
-    if (lnw) {
-        float s = 0.f;
-        for (int k = lane; k < K; k += 32) s += p[k];
-        mean = warp_sum(s) / (float)K;
-        float q = 0.f;
-        for (int k = lane; k < K; k += 32) {
-            float dd = p[k] - mean;
-            q = fmaf(dd, dd, q);
+size_t tc_split_bytes(int rows, int K) { return (size_t)((rows + GBM - 1) / GBM) * (size_t)(K / GBK) * 2 * GBLOCK * 2; }
+
+// Eight rows per block. Per row (one warp): the LayerNorm's mean and 1/sigma (when lnw is set; kern.rs:357-376, two
+// passes), and the power-of-two scale that keeps the row's largest transformed magnitude below 2^14;
+// stats[m] = {mean, rstd, scale, 1 / scale}. Then the rows, transformed and scaled, split into f16 hi + lo in their
+// 128 x 64 blocks: tiles[(m / 128) * (K / 64) + k / 64] = [hi block][lo block], element (m % 128, k % 64) at its
+// core-matrix offset. Eight consecutive threads write the eight rows of one core matrix (128 contiguous bytes).
+// Rows from M up to the next multiple of 128 are written as zeros.
+__global__ void __launch_bounds__(256) k_split_rows(const float *x, int ldx, int M, int K, const float *lnw,
+                                                    const float *lnb, float4 *stats, __half *tiles) {
+    __shared__ float sh_mean[8], sh_inv[8], sh_sc[8];
+    const int r0 = blockIdx.x * 8, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    {
+        const int row = r0 + warp;
+        const bool real = row < M;
+        const float *p = x + (size_t)(real ? row : 0) * ldx;
+        float mean = 0.f, inv = 1.f, mx = 0.f;
+        if (real) {
+            if (lnw) {
+                float s = 0.f;
+                for (int k = lane * 4; k < K; k += 128) {
+                    const float4 v = *reinterpret_cast<const float4 *>(p + k);
+                    s += (v.x + v.y) + (v.z + v.w);
+                }
+                mean = warp_sum(s) / (float)K;
+                float q = 0.f;
+                for (int k = lane; k < K; k += 32) {
+                    const float dd = p[k] - mean;
+                    q = fmaf(dd, dd, q);
+                }
+                inv = 1.0f / sqrtf(warp_sum(q) / (float)K + 1e-5f);
+            }
+            for (int k = lane; k < K; k += 32) {
+                const float v = lnw ? (p[k] - mean) * inv * lnw[k] + lnb[k] : p[k];
+                mx = fmaxf(mx, fabsf(v));
+            }
+            mx = warp_max(mx);
         }
-        inv = 1.0f / sqrtf(warp_sum(q) / (float)K + 1e-5f);
-    }
-    float mx = 0.f;
-    for (int k = lane; k < K; k += 32) {
-        const float v = lnw ? (p[k] - mean) * inv * lnw[k] + lnb[k] : p[k];
-        mx = fmaxf(mx, fabsf(v));
-    }
-    mx = warp_max(mx);
-    if (lane == 0) {
         int e = 0;
         if (mx > 0.f) {
-            const int ex = (int)((__float_as_uint(mx) >> 23) & 0xff) - 126;
-            e = 14 - ex;
+            e = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xff) - 126);  // mx < 2^(14 - e)
             e = e < -120 ? -120 : (e > 120 ? 120 : e);
         }
-        stats[row] = make_float4(mean, inv, p2(e), p2(-e));
+        if (lane == 0) {
+            sh_mean[warp] = mean, sh_inv[warp] = inv, sh_sc[warp] = real ? p2(e) : 0.f;
+            if (real) stats[row] = make_float4(mean, inv, p2(e), p2(-e));
+        }
+    }
+    __syncthreads();
+    const int nk = K / GBK, mt = r0 / GBM;
+    for (int i = threadIdx.x; i < K; i += 256) {  // i = (group of 8 along K) * 8 + row
+        const int r = i & 7, k = (i >> 3) * 8, row = r0 + r;
+        const float sc = sh_sc[r];
+        float v[8];
+        if (row < M) {
+            const float *p = x + (size_t)row * ldx + k;
+            const float4 x0 = *reinterpret_cast<const float4 *>(p), x1 = *reinterpret_cast<const float4 *>(p + 4);
+            v[0] = x0.x, v[1] = x0.y, v[2] = x0.z, v[3] = x0.w, v[4] = x1.x, v[5] = x1.y, v[6] = x1.z, v[7] = x1.w;
+            if (lnw) {
+                const float mean = sh_mean[r], inv = sh_inv[r];
+#pragma unroll
+                for (int j = 0; j < 8; j++) v[j] = (v[j] - mean) * inv * lnw[k + j] + lnb[k + j];
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = 0.f;
+        }
+        __align__(16) __half hh[8], ll[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) split_f16(v[j] * sc, hh[j], ll[j]);
+        __half *blk = tiles + ((size_t)mt * nk + k / GBK) * 2 * GBLOCK;
+        const int off = kmajor_off(row % GBM, k % GBK, GBM);
+        *reinterpret_cast<uint4 *>(blk + off) = *reinterpret_cast<const uint4 *>(hh);
+        *reinterpret_cast<uint4 *>(blk + GBLOCK + off) = *reinterpret_cast<const uint4 *>(ll);
     }
 }
 
-// The tensor cores' f32 accumulation is not rounded to nearest, so a long run of accumulations into one
-// accumulator drifts by about an ulp per step. Each 64-wide chunk of K therefore gets fresh accumulators - the
-// large hi*hi products in one, the small cross terms in another - and the chunks are added in registers with
-// ordinary f32 arithmetic: at most four truncating steps on the large terms.
-__global__ void __launch_bounds__(256, 1) k_gemm_tc(LinArgs a, const float4 *stats) {
-    constexpr int BM = 128, BN = 128, BK = 64;
+__device__ __forceinline__ void g_bulk(void *dst, const void *src, uint32_t bytes, uint64_t *mbar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(mbar))
+                 : "memory");
+}
+__device__ __forceinline__ void g_expect(uint64_t *mbar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}\n" ::"r"(
+                     smem_addr(mbar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4 *stats) {
     extern __shared__ __align__(1024) uint8_t smraw[];
-    __half *Ah = reinterpret_cast<__half *>(smraw);  // [2 stages][BM][BK] K-major, hi
-    __half *Al = Ah + 2 * BM * BK;                    // lo
-    __half *Wh = Al + 2 * BM * BK;                    // [2][BN][BK]
-    __half *Wl = Wh + 2 * BN * BK;
-    uint64_t *mbar = reinterpret_cast<uint64_t *>(Wl + 2 * BN * BK);  // [2]
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(mbar + 2);
+    // ring of GSTAGES slots: [A hi][A lo][W hi][W lo], each GBLOCK halves
+    __half *ring = reinterpret_cast<__half *>(smraw);
+    uint64_t *mb = reinterpret_cast<uint64_t *>(ring + (size_t)GSTAGES * 4 * GBLOCK);
+    uint64_t *mFull = mb, *mEmpty = mb + GSTAGES, *mT = mb + 2 * GSTAGES, *mTfree = mT + 2, *mDone = mTfree + 2;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(mDone + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
 
-    const int tid = threadIdx.x, warp = tid >> 5;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nt = blockIdx.x, mt = blockIdx.y, m0 = mt * GBM, n0 = nt * GBN;
+    const int nk = a.K / GBK;
     if (warp == 0) {
-        tmem_alloc(tslot, 512);  // [2 chunks] x (hi*hi accumulator, cross-term accumulator) x 128 columns
+        tmem_alloc(tslot, 512);  // two chunk buffers x (hi*hi accumulator, cross-term accumulator) x 128 columns
         tmem_relinquish();
     }
     if (tid == 0) {
-        mbar_init(&mbar[0], 1);
-        mbar_init(&mbar[1], 1);
+        for (int i = 0; i < GSTAGES; i++) mbar_init(&mFull[i], 1), mbar_init(&mEmpty[i], 1);
+        for (int i = 0; i < 2; i++) mbar_init(&mT[i], 1), mbar_init(&mTfree[i], 256);
+        mbar_init(mDone, 1);
         mbar_init_fence();
         *abort_flag = 0;
     }
-    // this thread's staging row (A) and output row (W) stay fixed: 256 threads, 128 rows
-    const int sm = tid % BM, kq = tid / BM;  // kq: which 8-column groups (kq, kq + 2, ...)
-    const int am = m0 + sm, wn = n0 + sm;
-    float4 st = make_float4(0.f, 1.f, 0.f, 0.f);
-    if (am < a.M) st = stats[am];
-    const float *arow = a.x + (size_t)(am < a.M ? am : 0) * a.ldx;
-    const __half *wh_row = reinterpret_cast<const __half *>(a.tc_whi) + (size_t)(wn < a.N ? wn : 0) * a.K;
-    const __half *wl_row = reinterpret_cast<const __half *>(a.tc_wlo) + (size_t)(wn < a.N ? wn : 0) * a.K;
-    auto stage = [&](int c, int buf) {
-        __half *ah = Ah + buf * BM * BK, *al = Al + buf * BM * BK, *wh = Wh + buf * BN * BK, *wl = Wl + buf * BN * BK;
-#pragma unroll
-        for (int g = kq; g < BK / 8; g += 2) {
-            const int k = c * BK + g * 8;
-            float v[8];
-            if (am < a.M) {
-                const float4 x0 = *reinterpret_cast<const float4 *>(arow + k), x1 = *reinterpret_cast<const float4 *>(arow + k + 4);
-                v[0] = x0.x, v[1] = x0.y, v[2] = x0.z, v[3] = x0.w, v[4] = x1.x, v[5] = x1.y, v[6] = x1.z, v[7] = x1.w;
-                if (a.lnw) {
-#pragma unroll
-                    for (int e = 0; e < 8; e++) v[e] = (v[e] - st.x) * st.y * a.lnw[k + e] + a.lnb[k + e];
-                }
-            } else {
-#pragma unroll
-                for (int e = 0; e < 8; e++) v[e] = 0.f;
-            }
-            __align__(16) __half hh[8], ll[8];
-#pragma unroll
-            for (int e = 0; e < 8; e++) split_f16(v[e] * st.z, hh[e], ll[e]);
-            const int off = kmajor_off(sm, g * 8, BM);
-            *reinterpret_cast<uint4 *>(ah + off) = *reinterpret_cast<const uint4 *>(hh);
-            *reinterpret_cast<uint4 *>(al + off) = *reinterpret_cast<const uint4 *>(ll);
-            uint4 whv = make_uint4(0u, 0u, 0u, 0u), wlv = whv;
-            if (wn < a.N) {
-                whv = __ldg(reinterpret_cast<const uint4 *>(wh_row + k));
-                wlv = __ldg(reinterpret_cast<const uint4 *>(wl_row + k));
-            }
-            const int woff = kmajor_off(sm, g * 8, BN);
-            *reinterpret_cast<uint4 *>(wh + woff) = whv;
-            *reinterpret_cast<uint4 *>(wl + woff) = wlv;
-        }
-    };
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = *tslot;
-    const uint32_t id = idesc_f16(BM, BN, 0, 0);
-    const int nk = a.K / BK;
-    // this thread's share of the accumulators: lane (row) warp%4 * 32 + lane, columns (warp / 4) * 64 + [0, 64)
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const int col0 = (warp >> 2) * 64;
+    const __half *A = reinterpret_cast<const __half *>(a.tc_atiles) + (size_t)mt * nk * 2 * GBLOCK;
+    const __half *Wt = reinterpret_cast<const __half *>(a.tc_wtiles) + (size_t)nt * nk * 2 * GBLOCK;
+    const uint32_t chunk_half_bytes = (uint32_t)(2 * GBLOCK * sizeof(__half));  // hi + lo of one operand
+    auto wait = [&](uint64_t *m, uint32_t parity) {
+        if (*abort_flag) return false;
+        if (!mbar_wait(m, parity, GEMM_WAIT_CYCLES)) {
+            *abort_flag = 1;
+            return false;
+        }
+        return true;
+    };
     float sum[64];
 #pragma unroll
     for (int e = 0; e < 64; e++) sum[e] = 0.f;
-    uint32_t parity[2] = {0u, 0u};
-    bool ok = true;
-    stage(0, 0);
-    fence_async_smem();
-    __syncthreads();
-    for (int c = 0; c < nk; c++) {
-        const int buf = c & 1;
-        const uint32_t t_hh = tmem + buf * 128, t_x = tmem + 256 + buf * 128;
-        if (tid == 0) {
+    const int col0 = ((warp >> 2) & 1) * 64;
+    if (warp == 9) {
+        // the load thread: chunk c into slot c % GSTAGES once the MMAs of chunk c - GSTAGES have read it
+        if (lane == 0) {
+            int issued = 0;
+            for (int c = 0; c < nk; c++) {
+                const int s = c % GSTAGES;
+                if (c >= GSTAGES && !wait(&mEmpty[s], (uint32_t)((c / GSTAGES) - 1) & 1u)) break;
+                __half *dst = ring + (size_t)s * 4 * GBLOCK;
+                g_expect(&mFull[s], 2 * chunk_half_bytes);
+                g_bulk(dst, A + (size_t)c * 2 * GBLOCK, chunk_half_bytes, &mFull[s]);
+                g_bulk(dst + 2 * GBLOCK, Wt + (size_t)c * 2 * GBLOCK, chunk_half_bytes, &mFull[s]);
+                issued = c + 1;
+            }
+            // the last loads land before the block lets go of shared memory
+            for (int c = max(0, issued - GSTAGES); c < issued; c++)
+                mbar_wait(&mFull[c % GSTAGES], (uint32_t)(c / GSTAGES) & 1u, GEMM_WAIT_CYCLES);
+        }
+    } else if (warp == 8) {
+        // the MMA thread
+        if (lane == 0) {
+            const uint32_t id = idesc_f16(GBM, GBN, 0, 0);
+            const uint64_t d0 = kstep_desc(ring, GBM, 0);
+            const uint64_t st = (2 * (GBM / 8) * 128) >> 4, blk = (GBLOCK * sizeof(__half)) >> 4;
+            const uint64_t slot = (4 * GBLOCK * sizeof(__half)) >> 4;
+            for (int c = 0; c < nk; c++) {
+                const int s = c % GSTAGES, b = c & 1;
+                if (!wait(&mFull[s], (uint32_t)(c / GSTAGES) & 1u)) break;
+                if (c >= 2 && !wait(&mTfree[b], (uint32_t)((c >> 1) - 1) & 1u)) break;
+                fence_after_sync();
+                const uint64_t dAh = d0 + s * slot, dAl = dAh + blk, dWh = dAl + blk, dWl = dWh + blk;
+                const uint32_t thh = tmem + b * 128, tx = tmem + 256 + b * 128;
+#pragma unroll
+                for (int k = 0; k < GBK / 16; k++) {
+                    mma_f16(thh, dAh + k * st, dWh + k * st, id, k > 0 ? 1u : 0u);
+                    mma_f16(tx, dAh + k * st, dWl + k * st, id, k > 0 ? 1u : 0u);
+                    mma_f16(tx, dAl + k * st, dWh + k * st, id, 1);
+                }
+                mma_commit(&mEmpty[s]);
+                mma_commit(&mT[b]);
+            }
+            mma_commit(mDone);
+            mbar_wait(mDone, 0, GEMM_WAIT_CYCLES);
+        }
+    } else {
+        // eight warps: lane (row) (warp % 4) * 32 + lane, columns col0 + [0, 64) of every chunk's accumulators
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        for (int c = 0; c < nk; c++) {
+            const int b = c & 1;
+            const bool okc = !*abort_flag && mbar_wait(&mT[b], (uint32_t)(c >> 1) & 1u, GEMM_WAIT_CYCLES);
+            if (!okc) *abort_flag = 1;
             fence_after_sync();
-            const __half *ah = Ah + buf * BM * BK, *al = Al + buf * BM * BK, *wh = Wh + buf * BN * BK, *wl = Wl + buf * BN * BK;
+            __syncwarp();
+            if (okc) {
 #pragma unroll
-            for (int s = 0; s < BK / 16; s++)
-                mma_f16(t_hh, kstep_desc(ah, BM, s), kstep_desc(wh, BN, s), id, s > 0 ? 1u : 0u);
+                for (int h2 = 0; h2 < 2; h2++) {
+                    float x[32], y[32];
+                    tmem_ld32(tmem + b * 128 + lane_base + col0 + 32 * h2, x);
+                    tmem_ld32(tmem + 256 + b * 128 + lane_base + col0 + 32 * h2, y);
+                    tmem_wait_ld();
 #pragma unroll
-            for (int s = 0; s < BK / 16; s++) {
-                mma_f16(t_x, kstep_desc(ah, BM, s), kstep_desc(wl, BN, s), id, s > 0 ? 1u : 0u);
-                mma_f16(t_x, kstep_desc(al, BM, s), kstep_desc(wh, BN, s), id, 1);
+                    for (int e = 0; e < 32; e++) sum[32 * h2 + e] += x[e] + y[e];
+                }
             }
-            mma_commit(&mbar[buf]);
+            fence_before_sync();
+            mbar_arrive(&mTfree[b]);
+            if (!okc) break;
         }
-        // the next chunk is staged while this one multiplies (its buffer's last readers finished last round)
-        if (c + 1 < nk) {
-            stage(c + 1, (c + 1) & 1);
-            fence_async_smem();
-        }
-        ok = mbar_wait(&mbar[buf], parity[buf], GEMM_WAIT_CYCLES);
-        parity[buf] ^= 1;
-        if (!ok) *abort_flag = 1;
-        fence_after_sync();
-        if (ok) {
-#pragma unroll
-            for (int h2 = 0; h2 < 2; h2++) {
-                float x[32], y[32];
-                tmem_ld32(t_hh + lane_base + col0 + 32 * h2, x);
-                tmem_ld32(t_x + lane_base + col0 + 32 * h2, y);
-                tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 32; e++) sum[32 * h2 + e] += x[e] + y[e];
-            }
-        }
-        fence_before_sync();
-        __syncthreads();
-        if (*abort_flag) break;
     }
-    ok = !*abort_flag;
-    // epilogue through shared memory (reusing the operand buffers) so that global stores are coalesced
-    float *ostage = reinterpret_cast<float *>(smraw);  // [BM][BN + 1]
-    {
-        const int m = (warp & 3) * 32 + (tid & 31);
+    fence_before_sync();
+    __syncthreads();
+    const bool ok = !*abort_flag;
+    // epilogue through shared memory (the ring: every load has landed and every MMA finished)
+    float *ostage = reinterpret_cast<float *>(smraw);  // [GBM][GBN + 1]
+    if (warp < 8) {
+        const int m = (warp & 3) * 32 + lane;
         const float un = m0 + m < a.M ? stats[m0 + m].w : 0.f;
 #pragma unroll
-        for (int e = 0; e < 64; e++) ostage[m * (BN + 1) + col0 + e] = sum[e] * un;
+        for (int e = 0; e < 64; e++) ostage[m * (GBN + 1) + col0 + e] = sum[e] * un;
     }
     __syncthreads();
     if (ok) {
-        for (int i = tid; i < BM * BN; i += 256) {
+        for (int i = tid; i < GBM * GBN; i += GTHREADS) {
             int m, e;
             if (a.transpose_out) {
-                m = i % BM, e = i / BM;  // consecutive threads: consecutive rows -> consecutive addresses
+                m = i % GBM, e = i / GBM;  // consecutive threads: consecutive rows -> consecutive addresses
             } else {
-                e = i % BN, m = i / BN;
+                e = i % GBN, m = i / GBN;
             }
             const int gm = m0 + m, gn = n0 + e;
             if (gm >= a.M || gn >= a.N) continue;
-            float v = ostage[m * (BN + 1) + e] * a.tc_wunscale[gn] + (a.bias ? a.bias[gn] : 0.f);
+            float v = ostage[m * (GBN + 1) + e] * a.tc_wunscale[gn] + (a.bias ? a.bias[gn] : 0.f);
             if (a.act) v = gelu1(v);
             float *dst = a.transpose_out ? a.y + (size_t)gn * a.ldy + gm : a.y + (size_t)gm * a.ldy + gn;
             *dst = a.accumulate ? *dst + v : v;
@@ -221,10 +270,12 @@ bool gemm_tc_enabled() {
     return on;
 }
 
-size_t gemm_tc_smem() { return sizeof(__half) * (4 * 128 * 64 + 4 * 128 * 64) + 64; }
+size_t gemm_tc_smem() { return sizeof(__half) * (size_t)GSTAGES * 4 * GBLOCK + 16 * sizeof(uint64_t) + 16; }
 
 cudaError_t launch_gemm_tc(const LinArgs &a, float4 *stats, cudaStream_t s, uint64_t *launches) {
-    k_row_stats_tc<<<(a.M + 7) / 8, 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats);
+    if (!a.tc_wtiles || !a.tc_atiles || a.K % GBK) return cudaErrorInvalidValue;
+    k_split_rows<<<(a.M + GBM - 1) / GBM * (GBM / 8), 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats,
+                                                                       reinterpret_cast<__half *>(a.tc_atiles));
     if (launches) ++*launches;
     const size_t smem = gemm_tc_smem();
     static bool attr = false;
@@ -233,8 +284,8 @@ cudaError_t launch_gemm_tc(const LinArgs &a, float4 *stats, cudaStream_t s, uint
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    dim3 grid((a.N + 127) / 128, (a.M + 127) / 128);
-    k_gemm_tc<<<grid, 256, smem, s>>>(a, stats);
+    dim3 grid((a.N + GBN - 1) / GBN, (a.M + GBM - 1) / GBM);
+    k_gemm_tc<<<grid, GTHREADS, smem, s>>>(a, stats);
     if (launches) ++*launches;
     return cudaGetLastError();
 }

@@ -21,9 +21,13 @@ struct LinArgs {
     int accumulate = 0;  // 1: y += result (residual)
     int bias_on_m = 0;   // bias indexed by the row of y (used when y is a transposed product)
     int transpose_out = 0;  // write y[n][m] (row stride ldy) instead of y[m][n]
-    // tensor-core path: W split once into f16 hi + lo (bit patterns), scaled per output row by 1 / unscale[n]
-    const uint16_t *tc_whi = nullptr, *tc_wlo = nullptr;
+    // tensor-core path: W split once into f16 hi + lo, scaled per output row by 1 / unscale[n], in 128 x 64 blocks
+    // ([N / 128][K / 64][hi 128 x 64][lo 128 x 64], core-matrix order); tc_atiles: scratch of tc_split_bytes(M, K)
+    // bytes for the split input rows
+    const void *tc_wtiles = nullptr;
     const float *tc_wunscale = nullptr;
+    void *tc_atiles = nullptr;
+    size_t tc_atiles_bytes = 0;
     int *err = nullptr;  // set to 1 when a kernel gave up waiting
 };
 
@@ -113,6 +117,10 @@ constexpr int FLASH_ROWS = 64;  // query rows per flash block
 cudaError_t launch_linear(const LinArgs &a, float *stats_scratch, cudaStream_t s, uint64_t *launches);
 // the tensor-core path of launch_linear (M > 8, K a multiple of 64, split weights given)
 cudaError_t launch_gemm_tc(const LinArgs &a, float4 *stats, cudaStream_t s, uint64_t *launches);
+// bytes of rows x K values split into f16 hi + lo blocks of 128 rows x 64 (rows rounded up to 128)
+size_t tc_split_bytes(int rows, int K);
+// element offset of (n, k) inside one 128 x 64 block of the tiled weights
+inline size_t tc_block_off(int n, int k) { return (size_t)((((k & 63) >> 3) * 16 + ((n & 127) >> 3)) * 64 + (n & 7) * 8 + (k & 7)); }
 size_t gemm_tc_smem();
 bool gemm_tc_enabled();
 cudaError_t launch_ln_apply(const float *x, int M, int K, const float *w, const float *b, float *y, cudaStream_t s,
