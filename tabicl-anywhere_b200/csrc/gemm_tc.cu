@@ -1,16 +1,18 @@
 // Linear layers of many rows on the tensor cores (tcgen05) at f32 accuracy: y (=|+=) act(W LN?(x) + b).
 //
 // Both operands reach the kernel already split into f16 hi + lo (x = hi + lo, about 22 significant bits) and laid
-// out in 128 x 64 blocks exactly as the MMAs read them from shared memory:
+// out in blocks of 128 rows x 64 of K exactly as the MMAs read them from shared memory (tc_block_off: groups of 8
+// rows outermost, so any 64-row half of a block is contiguous):
 //   weights - once, at upload, with a power-of-two scaling per output row (the engine's weight upload);
 //   activations - per call by k_split_rows, which also applies the LayerNorm (kern.rs:357-376) and a power-of-two
 //   scaling per row.
-// A CTA computes a 128-row x 128-output tile. Warp-specialised: one thread bulk-copies each 64-wide chunk of K (the
-// activation and weight blocks, 64 KB) into a three-slot ring; one thread issues the chunk's MMAs (hi*hi into one
-// fresh accumulator, the two cross terms into another: the tensor cores' f32 accumulation is not round-to-nearest,
-// so no accumulator sees more than 12 steps); eight warps add each chunk's accumulators into registers with
-// ordinary f32 arithmetic while the next chunk multiplies. The epilogue undoes the scalings, adds the bias, applies
-// GELU and the residual, and writes through shared memory so stores are coalesced (also transposed).
+// A CTA computes a 128-row x BN-output tile (BN 128, or 64 when 128-wide tiles would leave most SMs idle).
+// Warp-specialised: one thread bulk-copies each 64-wide chunk of K (the activation and weight blocks) into a ring;
+// one thread issues the chunk's MMAs (hi*hi, hi*lo, lo*hi) into a fresh accumulator (one of four in TMEM: the tensor
+// cores' f32 accumulation is not round-to-nearest, so no accumulator sees more than 12 steps); eight warps add each
+// chunk's accumulator into registers with ordinary f32 arithmetic while later chunks multiply. The epilogue undoes
+// the scalings, adds the bias, applies GELU and the residual, and writes through shared memory so that stores are
+// coalesced (also when transposed).
 #include <cfloat>
 #include <cstdlib>
 
@@ -23,8 +25,19 @@ namespace tcu {
 using namespace tc;
 
 constexpr long long GEMM_WAIT_CYCLES = 2000000000ll;
-constexpr int GBM = 128, GBN = 128, GBK = 64, GSTAGES = 3, GTHREADS = 320;
+constexpr int GBM = 128, GBK = 64, GTHREADS = 320, GBUFS = 4;
 constexpr size_t GBLOCK = (size_t)GBM * GBK;  // halves in one operand block (hi or lo)
+template <int BN>
+struct GemmShape {
+    static constexpr int STAGES = BN == 128 ? 3 : 4;
+    static constexpr uint32_t A_BYTES = 2 * GBLOCK * sizeof(__half);            // hi + lo of 128 rows
+    static constexpr uint32_t W_BYTES = 2 * (uint32_t)BN * GBK * sizeof(__half);  // hi + lo of BN rows
+    static constexpr uint32_t SLOT = A_BYTES + W_BYTES;
+    static constexpr size_t SMEM = (size_t)STAGES * SLOT + 1024;  // + barriers, TMEM slot, flag, row unscales
+};
+// element offset of (row, k) in a 128 x 64 block: 8-row groups outermost, then 8-wide groups of K, then the
+// 8 x 8 core matrix (rows of 16 bytes)
+__host__ __device__ __forceinline__ int blk_off(int r, int k) { return (((r >> 3) * 8 + (k >> 3)) << 6) + ((r & 7) << 3) + (k & 7); }
 
 __device__ __forceinline__ float p2(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
 
@@ -99,7 +112,7 @@ __global__ void __launch_bounds__(256) k_split_rows(const float *x, int ldx, int
 #pragma unroll
         for (int j = 0; j < 8; j++) split_f16(v[j] * sc, hh[j], ll[j]);
         __half *blk = tiles + ((size_t)mt * nk + k / GBK) * 2 * GBLOCK;
-        const int off = kmajor_off(row % GBM, k % GBK, GBM);
+        const int off = blk_off(row % GBM, k % GBK);
         *reinterpret_cast<uint4 *>(blk + off) = *reinterpret_cast<const uint4 *>(hh);
         *reinterpret_cast<uint4 *>(blk + GBLOCK + off) = *reinterpret_cast<const uint4 *>(ll);
     }
@@ -118,36 +131,41 @@ __device__ __forceinline__ void g_expect(uint64_t *mbar, uint32_t bytes) {
                  : "memory");
 }
 
+template <int BN>
 __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4 *stats) {
+    using G = GemmShape<BN>;
+    constexpr int S = G::STAGES, HALF = BN / 2;
     extern __shared__ __align__(1024) uint8_t smraw[];
-    // ring of GSTAGES slots: [A hi][A lo][W hi][W lo], each GBLOCK halves
-    __half *ring = reinterpret_cast<__half *>(smraw);
-    uint64_t *mb = reinterpret_cast<uint64_t *>(ring + (size_t)GSTAGES * 4 * GBLOCK);
-    uint64_t *mFull = mb, *mEmpty = mb + GSTAGES, *mT = mb + 2 * GSTAGES, *mTfree = mT + 2, *mDone = mTfree + 2;
+    // ring of S slots: [A hi][A lo][W hi][W lo]
+    uint64_t *mb = reinterpret_cast<uint64_t *>(smraw + (size_t)S * G::SLOT);
+    uint64_t *mFull = mb, *mEmpty = mb + S, *mT = mb + 2 * S, *mTfree = mT + GBUFS, *mDone = mTfree + GBUFS;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(mDone + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
+    float *un_row = reinterpret_cast<float *>(tslot + 2);  // [GBM]: the rows' unscale (epilogue)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nt = blockIdx.x, mt = blockIdx.y, m0 = mt * GBM, n0 = nt * GBN;
+    const int nt = blockIdx.x, mt = blockIdx.y, m0 = mt * GBM, n0 = nt * BN;
     const int nk = a.K / GBK;
     if (warp == 0) {
-        tmem_alloc(tslot, 512);  // two chunk buffers x (hi*hi accumulator, cross-term accumulator) x 128 columns
+        tmem_alloc(tslot, GBUFS * BN);  // four chunk accumulators of BN columns
         tmem_relinquish();
     }
     if (tid == 0) {
-        for (int i = 0; i < GSTAGES; i++) mbar_init(&mFull[i], 1), mbar_init(&mEmpty[i], 1);
-        for (int i = 0; i < 2; i++) mbar_init(&mT[i], 1), mbar_init(&mTfree[i], 256);
+        for (int i = 0; i < S; i++) mbar_init(&mFull[i], 1), mbar_init(&mEmpty[i], 1);
+        for (int i = 0; i < GBUFS; i++) mbar_init(&mT[i], 1), mbar_init(&mTfree[i], 256);
         mbar_init(mDone, 1);
         mbar_init_fence();
         *abort_flag = 0;
     }
+    if (tid < GBM) un_row[tid] = m0 + tid < a.M ? stats[m0 + tid].w : 0.f;
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = *tslot;
-    const __half *A = reinterpret_cast<const __half *>(a.tc_atiles) + (size_t)mt * nk * 2 * GBLOCK;
-    const __half *Wt = reinterpret_cast<const __half *>(a.tc_wtiles) + (size_t)nt * nk * 2 * GBLOCK;
-    const uint32_t chunk_half_bytes = (uint32_t)(2 * GBLOCK * sizeof(__half));  // hi + lo of one operand
+    const uint8_t *A = reinterpret_cast<const uint8_t *>(a.tc_atiles) + (size_t)mt * nk * G::A_BYTES;
+    // weights are stored in 128-row blocks; a 64-wide tile is the first or second half of each hi and lo block
+    const uint8_t *Wt = reinterpret_cast<const uint8_t *>(a.tc_wtiles) + (size_t)(n0 / GBM) * nk * 2 * GBLOCK * 2 +
+                        (size_t)(n0 % GBM) * GBK * 2;
     auto wait = [&](uint64_t *m, uint32_t parity) {
         if (*abort_flag) return false;
         if (!mbar_wait(m, parity, GEMM_WAIT_CYCLES)) {
@@ -156,46 +174,53 @@ __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4
         }
         return true;
     };
-    float sum[64];
+    float sum[HALF];
 #pragma unroll
-    for (int e = 0; e < 64; e++) sum[e] = 0.f;
-    const int col0 = ((warp >> 2) & 1) * 64;
+    for (int e = 0; e < HALF; e++) sum[e] = 0.f;
+    const int col0 = ((warp >> 2) & 1) * HALF;
     if (warp == 9) {
-        // the load thread: chunk c into slot c % GSTAGES once the MMAs of chunk c - GSTAGES have read it
+        // the load thread: chunk c into slot c % S once the MMAs of chunk c - S have read it
         if (lane == 0) {
             int issued = 0;
             for (int c = 0; c < nk; c++) {
-                const int s = c % GSTAGES;
-                if (c >= GSTAGES && !wait(&mEmpty[s], (uint32_t)((c / GSTAGES) - 1) & 1u)) break;
-                __half *dst = ring + (size_t)s * 4 * GBLOCK;
-                g_expect(&mFull[s], 2 * chunk_half_bytes);
-                g_bulk(dst, A + (size_t)c * 2 * GBLOCK, chunk_half_bytes, &mFull[s]);
-                g_bulk(dst + 2 * GBLOCK, Wt + (size_t)c * 2 * GBLOCK, chunk_half_bytes, &mFull[s]);
+                const int s = c % S;
+                if (c >= S && !wait(&mEmpty[s], (uint32_t)((c / S) - 1) & 1u)) break;
+                uint8_t *dst = smraw + (size_t)s * G::SLOT;
+                const uint8_t *wsrc = Wt + (size_t)c * 2 * GBLOCK * 2;
+                g_expect(&mFull[s], G::SLOT);
+                g_bulk(dst, A + (size_t)c * G::A_BYTES, G::A_BYTES, &mFull[s]);
+                if (BN == GBM) {
+                    g_bulk(dst + G::A_BYTES, wsrc, G::W_BYTES, &mFull[s]);
+                } else {
+                    g_bulk(dst + G::A_BYTES, wsrc, G::W_BYTES / 2, &mFull[s]);
+                    g_bulk(dst + G::A_BYTES + G::W_BYTES / 2, wsrc + GBLOCK * 2, G::W_BYTES / 2, &mFull[s]);
+                }
                 issued = c + 1;
             }
             // the last loads land before the block lets go of shared memory
-            for (int c = max(0, issued - GSTAGES); c < issued; c++)
-                mbar_wait(&mFull[c % GSTAGES], (uint32_t)(c / GSTAGES) & 1u, GEMM_WAIT_CYCLES);
+            for (int c = max(0, issued - S); c < issued; c++)
+                mbar_wait(&mFull[c % S], (uint32_t)(c / S) & 1u, GEMM_WAIT_CYCLES);
         }
     } else if (warp == 8) {
         // the MMA thread
         if (lane == 0) {
-            const uint32_t id = idesc_f16(GBM, GBN, 0, 0);
-            const uint64_t d0 = kstep_desc(ring, GBM, 0);
-            const uint64_t st = (2 * (GBM / 8) * 128) >> 4, blk = (GBLOCK * sizeof(__half)) >> 4;
-            const uint64_t slot = (4 * GBLOCK * sizeof(__half)) >> 4;
+            const uint32_t id = idesc_f16(GBM, BN, 0, 0);
+            // K-major, no swizzle: core matrices 128 B apart along K (LBO), 8-row groups 1024 B apart (SBO)
+            const uint64_t d0 = smem_desc(smem_addr(smraw), 128, 1024);
+            const uint64_t st = 256 >> 4;  // one K-step of 16: two core matrices along K
             for (int c = 0; c < nk; c++) {
-                const int s = c % GSTAGES, b = c & 1;
-                if (!wait(&mFull[s], (uint32_t)(c / GSTAGES) & 1u)) break;
-                if (c >= 2 && !wait(&mTfree[b], (uint32_t)((c >> 1) - 1) & 1u)) break;
+                const int s = c % S, b = c % GBUFS;
+                if (!wait(&mFull[s], (uint32_t)(c / S) & 1u)) break;
+                if (c >= GBUFS && !wait(&mTfree[b], (uint32_t)((c / GBUFS) - 1) & 1u)) break;
                 fence_after_sync();
-                const uint64_t dAh = d0 + s * slot, dAl = dAh + blk, dWh = dAl + blk, dWl = dWh + blk;
-                const uint32_t thh = tmem + b * 128, tx = tmem + 256 + b * 128;
+                const uint64_t dAh = d0 + ((s * G::SLOT) >> 4), dAl = dAh + ((GBLOCK * 2) >> 4);
+                const uint64_t dWh = dAh + (G::A_BYTES >> 4), dWl = dWh + ((G::W_BYTES / 2) >> 4);
+                const uint32_t t = tmem + b * BN;
 #pragma unroll
                 for (int k = 0; k < GBK / 16; k++) {
-                    mma_f16(thh, dAh + k * st, dWh + k * st, id, k > 0 ? 1u : 0u);
-                    mma_f16(tx, dAh + k * st, dWl + k * st, id, k > 0 ? 1u : 0u);
-                    mma_f16(tx, dAl + k * st, dWh + k * st, id, 1);
+                    mma_f16(t, dAh + k * st, dWh + k * st, id, k > 0 ? 1u : 0u);
+                    mma_f16(t, dAh + k * st, dWl + k * st, id, 1);
+                    mma_f16(t, dAl + k * st, dWh + k * st, id, 1);
                 }
                 mma_commit(&mEmpty[s]);
                 mma_commit(&mT[b]);
@@ -204,23 +229,22 @@ __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4
             mbar_wait(mDone, 0, GEMM_WAIT_CYCLES);
         }
     } else {
-        // eight warps: lane (row) (warp % 4) * 32 + lane, columns col0 + [0, 64) of every chunk's accumulators
+        // eight warps: lane (row) (warp % 4) * 32 + lane, columns col0 + [0, BN / 2) of every chunk's accumulator
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         for (int c = 0; c < nk; c++) {
-            const int b = c & 1;
-            const bool okc = !*abort_flag && mbar_wait(&mT[b], (uint32_t)(c >> 1) & 1u, GEMM_WAIT_CYCLES);
+            const int b = c % GBUFS;
+            bool okc = !*abort_flag && mbar_wait(&mT[b], (uint32_t)(c / GBUFS) & 1u, GEMM_WAIT_CYCLES);
+            okc = __all_sync(0xffffffffu, okc);  // tcgen05.ld is warp-wide
             if (!okc) *abort_flag = 1;
             fence_after_sync();
-            __syncwarp();
             if (okc) {
 #pragma unroll
-                for (int h2 = 0; h2 < 2; h2++) {
-                    float x[32], y[32];
-                    tmem_ld32(tmem + b * 128 + lane_base + col0 + 32 * h2, x);
-                    tmem_ld32(tmem + 256 + b * 128 + lane_base + col0 + 32 * h2, y);
+                for (int h2 = 0; h2 < HALF / 32; h2++) {
+                    float x[32];
+                    tmem_ld32(tmem + b * BN + lane_base + col0 + 32 * h2, x);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 32; e++) sum[32 * h2 + e] += x[e] + y[e];
+                    for (int e = 0; e < 32; e++) sum[32 * h2 + e] += x[e];
                 }
             }
             fence_before_sync();
@@ -232,34 +256,50 @@ __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4
     __syncthreads();
     const bool ok = !*abort_flag;
     // epilogue through shared memory (the ring: every load has landed and every MMA finished)
-    float *ostage = reinterpret_cast<float *>(smraw);  // [GBM][GBN + 1]
+    float *ostage = reinterpret_cast<float *>(smraw);  // [GBM][BN + 1]
     if (warp < 8) {
         const int m = (warp & 3) * 32 + lane;
-        const float un = m0 + m < a.M ? stats[m0 + m].w : 0.f;
+        const float un = un_row[m];
 #pragma unroll
-        for (int e = 0; e < 64; e++) ostage[m * (GBN + 1) + col0 + e] = sum[e] * un;
+        for (int e = 0; e < HALF; e++) ostage[m * (BN + 1) + col0 + e] = sum[e] * un;
     }
     __syncthreads();
-    if (ok) {
-        for (int i = tid; i < GBM * GBN; i += GTHREADS) {
-            int m, e;
-            if (a.transpose_out) {
-                m = i % GBM, e = i / GBM;  // consecutive threads: consecutive rows -> consecutive addresses
-            } else {
-                e = i % GBN, m = i / GBN;
+    if (ok && warp < 8) {
+        if (a.transpose_out) {
+            // thread: row m (consecutive threads, consecutive addresses), columns e0, e0 + 2, ...
+            const int m = tid & (GBM - 1), gm = m0 + m;
+            if (gm < a.M) {
+#pragma unroll 4
+                for (int e = tid >> 7; e < BN; e += 2) {
+                    const int gn = n0 + e;
+                    if (gn >= a.N) break;
+                    float v = ostage[m * (BN + 1) + e] * a.tc_wunscale[gn] + (a.bias ? a.bias[gn] : 0.f);
+                    if (a.act) v = gelu1(v);
+                    float *dst = a.y + (size_t)gn * a.ldy + gm;
+                    *dst = a.accumulate ? *dst + v : v;
+                }
             }
-            const int gm = m0 + m, gn = n0 + e;
-            if (gm >= a.M || gn >= a.N) continue;
-            float v = ostage[m * (GBN + 1) + e] * a.tc_wunscale[gn] + (a.bias ? a.bias[gn] : 0.f);
-            if (a.act) v = gelu1(v);
-            float *dst = a.transpose_out ? a.y + (size_t)gn * a.ldy + gm : a.y + (size_t)gm * a.ldy + gn;
-            *dst = a.accumulate ? *dst + v : v;
+        } else {
+            // thread: column e (consecutive threads, consecutive addresses), rows r0, r0 + 256 / BN, ...
+            constexpr int RSTEP = 256 / BN;
+            const int e = tid % BN, gn = n0 + e;
+            if (gn < a.N) {
+                const float ws = a.tc_wunscale[gn], bs = a.bias ? a.bias[gn] : 0.f;
+                const int mend = min(GBM, a.M - m0);
+#pragma unroll 8
+                for (int m = tid / BN; m < mend; m += RSTEP) {
+                    float v = ostage[m * (BN + 1) + e] * ws + bs;
+                    if (a.act) v = gelu1(v);
+                    float *dst = a.y + (size_t)(m0 + m) * a.ldy + gn;
+                    *dst = a.accumulate ? *dst + v : v;
+                }
+            }
         }
     }
     if (!ok && tid == 0 && a.err) atomicExch(a.err, 1);
     fence_before_sync();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, 512);
+    if (warp == 0) tmem_dealloc(tmem, GBUFS * BN);
 }
 
 bool gemm_tc_enabled() {
@@ -270,24 +310,42 @@ bool gemm_tc_enabled() {
     return on;
 }
 
-size_t gemm_tc_smem() { return sizeof(__half) * (size_t)GSTAGES * 4 * GBLOCK + 16 * sizeof(uint64_t) + 16; }
+size_t gemm_tc_smem() { return GemmShape<128>::SMEM; }
+
+// 64-wide tiles when 128-wide ones would fill at most half of the SMs
+static int gemm_bn(int M, int N) {
+    static const int forced = [] {
+        const char *e = getenv("TCU_GEMM_BN");
+        return e ? atoi(e) : 0;
+    }();
+    if (forced == 64 || forced == 128) return forced;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return (long)((M + GBM - 1) / GBM) * ((N + 127) / 128) * 2 <= sms ? 64 : 128;
+}
+
+template <int BN>
+static cudaError_t launch_bn(const LinArgs &a, float4 *stats, cudaStream_t s) {
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)GemmShape<BN>::SMEM);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    dim3 grid((a.N + BN - 1) / BN, (a.M + GBM - 1) / GBM);
+    k_gemm_tc<BN><<<grid, GTHREADS, GemmShape<BN>::SMEM, s>>>(a, stats);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_gemm_tc(const LinArgs &a, float4 *stats, cudaStream_t s, uint64_t *launches) {
     if (!a.tc_wtiles || !a.tc_atiles || a.K % GBK) return cudaErrorInvalidValue;
     k_split_rows<<<(a.M + GBM - 1) / GBM * (GBM / 8), 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats,
                                                                        reinterpret_cast<__half *>(a.tc_atiles));
     if (launches) ++*launches;
-    const size_t smem = gemm_tc_smem();
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
-    dim3 grid((a.N + GBN - 1) / GBN, (a.M + GBM - 1) / GBM);
-    k_gemm_tc<<<grid, GTHREADS, smem, s>>>(a, stats);
+    const cudaError_t e = gemm_bn(a.M, a.N) == 64 ? launch_bn<64>(a, stats, s) : launch_bn<128>(a, stats, s);
     if (launches) ++*launches;
-    return cudaGetLastError();
+    return e;
 }
 
 }  // namespace tcu

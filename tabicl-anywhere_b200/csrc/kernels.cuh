@@ -119,8 +119,9 @@ cudaError_t launch_linear(const LinArgs &a, float *stats_scratch, cudaStream_t s
 cudaError_t launch_gemm_tc(const LinArgs &a, float4 *stats, cudaStream_t s, uint64_t *launches);
 // bytes of rows x K values split into f16 hi + lo blocks of 128 rows x 64 (rows rounded up to 128)
 size_t tc_split_bytes(int rows, int K);
-// element offset of (n, k) inside one 128 x 64 block of the tiled weights
-inline size_t tc_block_off(int n, int k) { return (size_t)((((k & 63) >> 3) * 16 + ((n & 127) >> 3)) * 64 + (n & 7) * 8 + (k & 7)); }
+// element offset of (n, k) inside one 128 x 64 block of the tiled weights: 8-row groups outermost, then 8-wide
+// groups of K, then the 8 x 8 core matrix
+inline size_t tc_block_off(int n, int k) { return (size_t)((((n & 127) >> 3) * 8 + ((k & 63) >> 3)) * 64 + (n & 7) * 8 + (k & 7)); }
 size_t gemm_tc_smem();
 bool gemm_tc_enabled();
 cudaError_t launch_ln_apply(const float *x, int M, int K, const float *w, const float *b, float *y, cudaStream_t s,
