@@ -139,316 +139,419 @@ __device__ __forceinline__ void expect_tx(uint64_t *mbar, uint32_t bytes) {
                  : "memory");
 }
 
-// Attention of 128 query rows x one head over a range of 64-key tiles, with the tiles pre-split (k_tc_tiles):
-//   S = Q K^T: Q [128 x 128] K-major, K [64 keys x 128] MN-major; two S buffers in TMEM (columns 0-127, 128-255),
-//              hi*hi in the first 64 columns of a buffer, cross terms in the next 64
-//   O += P V^T: P [128 x 64 keys] K-major, V [128 x 64 keys] K-major; per tile hi*hi in 256-383, cross 384-511
-// Warp-specialised: warps 0-7 compute (the online softmax, nn.rs:207-215 rule, two threads per query row; the fold
-// of each tile's P V into O held in registers), one thread of warp 8 issues every MMA, one thread of warp 9 the bulk
-// copies of the key and value halves of each tile into two-slot rings. They hand over through mbarriers only (the
-// two producers in separate warps, so neither's waiting holds the other up), and the tensor cores work on tile
-// i + 1's scores while the softmax of tile i runs. Every f32 sum of tensor-core results is taken
-// in registers (fresh accumulators per tile: the units' own f32 accumulation is not round-to-nearest). Every wait
-// is bounded; a wait that gives up raises the block's abort flag and everyone leaves.
-constexpr int TC_THREADS = 320;  // eight compute warps, an MMA warp and a load warp
-
-// Named barrier 1 over the 256 compute threads, returning the AND of p over them (every compute thread takes the
-// same branch after it).
-__device__ __forceinline__ bool compute_all(bool p) {
-    uint32_t r;
-    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}\n"
-                 : "=r"(r)
-                 : "r"((uint32_t)p)
-                 : "memory");
-    return r != 0;
-}
+// Attention of 128 query rows x one head over a range of 64-key tiles, with the tiles pre-split (k_tc_tiles).
+// Tensor memory, 512 columns, one query row per lane:
+//   [0, 128)    Q: hi in 0-63, lo in 64-127 (f16 pairs, element 2c in the low half of column c): the A operand of
+//               S = Q K^T (K [64 keys x 128] K-major in shared memory)
+//   [128, 256)  S of two tiles, 64 columns each
+//   [256, 512)  P V^T of two tiles, 128 columns each (P [128 rows x 64 keys] of two tiles and V [128 x 64 keys],
+//               K-major in shared memory)
+// Roles: warps 0-3 run the online softmax (one thread per query row, the nn.rs:207-215 rule), warps 4-7 fold each
+// tile's P V into O held in registers (O = O f + P V), one thread of warp 8 issues every MMA, one thread of warp 9
+// bulk-copies keys and values into two-slot rings. They hand over through mbarriers only: S(i + 2) and P V(i) run
+// on the tensor cores while the softmax of tile i + 1 runs, and the fold of tile i while P V(i + 1) runs. Each
+// product is hi*hi + hi*lo + lo*hi with the two cross terms accumulated first, so the tensor cores' f32
+// accumulation (not round-to-nearest) adds only 8 (S) or 4 (P V) steps of full magnitude; every sum across tiles is
+// taken in registers. Every wait is bounded; a wait that gives up raises the block's abort flag and everyone leaves.
+constexpr int TC_THREADS = 320;  // four softmax warps, four fold warps, an MMA warp and a load warp
+constexpr uint32_t TM_Q = 0, TM_S = 128, TM_O = 256;
 
 template <int KV>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
     constexpr int HD = TC_HD, BQ = TC_BQ, BK = TC_BK;
     extern __shared__ __align__(1024) uint8_t smraw[];
-    __half *Qhi = reinterpret_cast<__half *>(smraw);  // [BQ][HD] K-major
-    __half *Qlo = Qhi + BQ * HD;
-    __half *Kring = Qlo + BQ * HD;                    // two slots of [keys hi][keys lo]
-    __half *Vring = Kring + 2 * 2 * TC_BLOCK;         // two slots of [values hi][values lo]
-    __half *Phi = Vring + 2 * 2 * TC_BLOCK;           // [BQ][BK keys] K-major
-    __half *Plo = Phi + BQ * BK;
-    float *fr = reinterpret_cast<float *>(Plo + BQ * BK);  // [BQ] this tile's rescale factor of each row
-    float *redm = fr + BQ;                                 // [2][BQ] half-row maxima
-    float *reds = redm + 2 * BQ;                           // [2][BQ] half-row weight sums
-    uint64_t *mb = reinterpret_cast<uint64_t *>(reds + 2 * BQ);
-    uint64_t *mS = mb, *mSfree = mb + 2, *mK = mb + 4, *mV = mb + 6, *mP = mb + 8, *mPV = mb + 9, *mO = mb + 10,
-             *mDone = mb + 11;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(mb + 12);
+    __half *Kring = reinterpret_cast<__half *>(smraw);  // two slots of [keys hi][keys lo]
+    __half *Vring = Kring + 2 * 2 * TC_BLOCK;           // two slots of [values hi][values lo]
+    __half *Pbuf = Vring + 2 * 2 * TC_BLOCK;            // two buffers of [P hi][P lo], each [BQ][BK keys] K-major
+    float *fr = reinterpret_cast<float *>(Pbuf + 2 * 2 * BQ * BK);  // [4][BQ]: tile i's rescale factors in i % 4
+    float *rowx = fr + 4 * BQ;  // [3][BQ]: each row's m, l and 1 / l at the end
+    uint64_t *mb = reinterpret_cast<uint64_t *>(rowx + 3 * BQ);
+    uint64_t *mK = mb, *mV = mb + 2, *mKfree = mb + 4, *mVfree = mb + 6, *mS = mb + 8, *mSfree = mb + 10,
+             *mPV = mb + 12, *mOfree = mb + 14, *mF = mb + 16, *mP = mb + 20, *mDone = mb + 22;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(mb + 23);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
-    float *qscale = reinterpret_cast<float *>(Phi);  // [BQ] 2^e of each row's query (until the first P)
+    float *qmax = reinterpret_cast<float *>(Pbuf);     // [2][BQ] query halves' maxima, before the first P
+    float *ostage = reinterpret_cast<float *>(Kring);  // [BQ][HD + 1] after the last fold
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.y, split = blockIdx.z, r0 = blockIdx.x * BQ, d = a.d, H = gridDim.y;
-    const int t0 = split * a.tiles_per_split, t1 = min(a.ntiles, t0 + a.tiles_per_split), nt = t1 - t0;
+    const int t0 = split * a.tiles_per_split, t1 = min(a.ntiles, t0 + a.tiles_per_split), nt = max(0, t1 - t0);
     const __half *tiles = reinterpret_cast<const __half *>(a.tc_tiles);
-    const bool producer = warp >= 8;
+    const int row = tid & (BQ - 1), part = (tid >> 7) & 1;  // compute threads: query row; softmax (0) or fold (1)
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     if (warp == 0) {
         tmem_alloc(tslot, 512);
         tmem_relinquish();
     }
     if (tid == 0) {
         for (int i = 0; i < 2; i++) {
-            mbar_init(&mS[i], 1);
-            mbar_init(&mSfree[i], 256);
-            mbar_init(&mK[i], 1);
-            mbar_init(&mV[i], 1);
+            mbar_init(&mK[i], 1), mbar_init(&mV[i], 1), mbar_init(&mKfree[i], 1), mbar_init(&mVfree[i], 1);
+            mbar_init(&mS[i], 1), mbar_init(&mSfree[i], BQ), mbar_init(&mPV[i], 1), mbar_init(&mOfree[i], BQ);
         }
-        mbar_init(mP, 256);
-        mbar_init(mPV, 1);
-        mbar_init(mO, 256);
+        for (int i = 0; i < 4; i++) mbar_init(&mF[i], BQ);
+        mbar_init(&mP[0], BQ), mbar_init(&mP[1], BQ);
         mbar_init(mDone, 1);
         mbar_init_fence();
         *abort_flag = 0;
     }
-    // each row's query scale: its largest |q| maps below 2^14
-    if (tid < BQ) {
+    // each compute thread: half of its row's query (head columns 64 * part + [0, 64)) and its largest magnitude
+    float qv[64];
+    if (tid < 2 * BQ) {
+        const int r = r0 + row;
         float mx = 0.f;
-        const int r = r0 + tid;
         if (r < a.R) {
-            const float4 *qp = reinterpret_cast<const float4 *>(a.q + (size_t)r * a.ldq + h * HD);
-#pragma unroll 4
-            for (int j = 0; j < HD / 4; j++) {
-                float4 v = qp[j];
+            const float4 *qp = reinterpret_cast<const float4 *>(a.q + (size_t)r * a.ldq + h * HD + 64 * part);
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const float4 v = qp[j];
+                qv[4 * j] = v.x, qv[4 * j + 1] = v.y, qv[4 * j + 2] = v.z, qv[4 * j + 3] = v.w;
                 mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
             }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 64; j++) qv[j] = 0.f;
         }
-        qscale[tid] = pow2f(f16_exponent(mx));
+        qmax[part * BQ + row] = mx;
     }
+    fence_before_sync();
     __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = *tslot;
     const uint32_t half_bytes = (uint32_t)(2 * TC_BLOCK * sizeof(__half));
-    auto load = [&](int i, bool values) {  // producer thread: the key or value halves of tile t0 + i into slot i & 1
+    auto load = [&](int i, bool values) {  // the load thread: keys or values of tile t0 + i into slot i & 1
         const __half *src = tiles + ((size_t)(t0 + i) * H + h) * 4 * TC_BLOCK + (values ? 2 * TC_BLOCK : 0);
         __half *dst = (values ? Vring : Kring) + (size_t)(i & 1) * 2 * TC_BLOCK;
         uint64_t *m = values ? &mV[i & 1] : &mK[i & 1];
         expect_tx(m, half_bytes);
-        bulk_g2s(dst, src, half_bytes / 2, m);
-        bulk_g2s(dst + TC_BLOCK, src + TC_BLOCK, half_bytes / 2, m);
+        bulk_g2s(dst, src, half_bytes, m);
     };
     if (warp == 9 && lane == 0) {
         for (int i = 0; i < min(nt, 2); i++) load(i, false), load(i, true);
     }
-    for (int i = tid; i < BQ * (HD / 8); i += TC_THREADS) {
-        const int m = i % BQ, j0 = (i / BQ) * 8, r = r0 + m;
-        float v[8];
-        if (r < a.R) {
-            const float4 *qp = reinterpret_cast<const float4 *>(a.q + (size_t)r * a.ldq + h * HD + j0);
-            float4 x = qp[0], y = qp[1];
-            v[0] = x.x, v[1] = x.y, v[2] = x.z, v[3] = x.w, v[4] = y.x, v[5] = y.y, v[6] = y.z, v[7] = y.w;
-        } else {
+    // the row's query scale (its largest |q| maps below 2^14); Q split into TMEM
+    float rs = 1.f;
+    if (tid < 2 * BQ) {
+        const float qs = pow2f(f16_exponent(fmaxf(qmax[row], qmax[BQ + row])));
+        rs = (1.0f / qs) * pow2f(-a.tc_eK);  // undoes both scalings of S
+        uint32_t hi[32], lo[32];
 #pragma unroll
-            for (int e = 0; e < 8; e++) v[e] = 0.f;
-        }
-        put8(Qhi, Qlo, kmajor_off(m, j0, BQ), v, qscale[m]);
+        for (int c = 0; c < 32; c++) split_pair(qv[2 * c] * qs, qv[2 * c + 1] * qs, hi[c], lo[c]);
+        tmem_st32u(tmem + lane_base + TM_Q + 32 * part, hi);
+        tmem_st32u(tmem + lane_base + TM_Q + 64 + 32 * part, lo);
+        tmem_wait_st();
     }
-    const int row = (warp & 3) * 32 + lane, half = (warp >> 2) & 1;
-    const float rs = producer ? 1.f : (1.0f / qscale[row]) * pow2f(-a.tc_eK);  // undoes both scalings
-    fence_async_smem();
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
-    const uint32_t tmem = *tslot, tO = tmem + 256;
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    float o[64];
-#pragma unroll
-    for (int e = 0; e < 64; e++) o[e] = 0.f;
-    float mrun = -FLT_MAX, lrun = 0.f;
-    bool any = false;
 
-    if (producer) {
-        auto wait = [&](uint64_t *m, uint32_t parity) {
-            if (*abort_flag) return false;
-            if (!mbar_wait(m, parity, TC_WAIT_CYCLES)) {
-                *abort_flag = 1;
-                return false;
-            }
-            return true;
-        };
-        if (warp == 8 && lane == 0) {
+    auto wait = [&](uint64_t *m, uint32_t parity) {
+        if (mbar_test_wait(m, parity)) return true;
+        if (*abort_flag) return false;
+        if (!mbar_wait(m, parity, TC_WAIT_CYCLES)) {
+            *abort_flag = 1;
+            return false;
+        }
+        return true;
+    };
+    // warp-uniform wait (the tcgen05 loads and stores after it are warp-wide)
+    auto wait_warp = [&](uint64_t *m, uint32_t parity) {
+        bool okw = mbar_test_wait(m, parity) || (!*abort_flag && mbar_wait(m, parity, TC_WAIT_CYCLES));
+        okw = __all_sync(0xffffffffu, okw);
+        if (!okw) *abort_flag = 1;
+        return okw;
+    };
+
+    if (warp == 8) {
+        if (lane == 0) {
             // the MMA thread: waits only for what its next MMAs read
             const uint32_t idS = idesc_f16(BQ, BK, 0, 0), idO = idesc_f16(BQ, HD, 0, 0);
-            // Descriptors: K-step k of an operand is its k = 0 descriptor plus k times the step of its start address
-            // (the address sits in the low bits, in 16-byte units), so each MMA costs one add, not a recomputation.
-            const uint64_t dQh = kstep_desc(Qhi, BQ, 0), dQl = kstep_desc(Qlo, BQ, 0);
-            const uint64_t dK0 = kstep_desc(Kring, BK, 0), dV0 = kstep_desc(Vring, HD, 0);
-            const uint64_t dPh = kstep_desc(Phi, BQ, 0), dPl = kstep_desc(Plo, BQ, 0);
-            const uint64_t stQ = (2 * (BQ / 8) * 128) >> 4, stK = (2 * (BK / 8) * 128) >> 4, stV = (2 * (HD / 8) * 128) >> 4;
+            const uint64_t dK0 = kstep_desc(Kring, BK, 0), dV0 = kstep_desc(Vring, HD, 0), dP0 = kstep_desc(Pbuf, BQ, 0);
+            const uint64_t stP = (2 * (BQ / 8) * 128) >> 4, stK = (2 * (BK / 8) * 128) >> 4, stV = (2 * (HD / 8) * 128) >> 4;
+            const uint64_t pblk = (BQ * BK * sizeof(__half)) >> 4;  // P hi to P lo, and one P buffer to the next / 2
             const uint64_t lo_off = (TC_BLOCK * sizeof(__half)) >> 4, slot_off = (2 * TC_BLOCK * sizeof(__half)) >> 4;
-            auto issue_S = [&](int i) {
-                const uint32_t tS = tmem + 128 * (i & 1);
+            auto issue_S = [&](int i) {  // S(i) into buffer i & 1 from key slot i & 1
+                const uint32_t tS = tmem + TM_S + 64 * (i & 1);
                 const uint64_t dKh = dK0 + (i & 1) * slot_off, dKl = dKh + lo_off;
                 fence_after_sync();
 #pragma unroll
-                for (int k = 0; k < HD / 16; k++) {
-                    mma_f16(tS, dQh + k * stQ, dKh + k * stK, idS, k > 0 ? 1u : 0u);
-                    mma_f16(tS + 64, dQh + k * stQ, dKl + k * stK, idS, k > 0 ? 1u : 0u);
-                    mma_f16(tS + 64, dQl + k * stQ, dKh + k * stK, idS, 1);
-                }
+                for (int k = 0; k < HD / 16; k++) mma_f16_ta(tS, tmem + TM_Q + 8 * k, dKl + k * stK, idS, k > 0 ? 1u : 0u);
+#pragma unroll
+                for (int k = 0; k < HD / 16; k++) mma_f16_ta(tS, tmem + TM_Q + 64 + 8 * k, dKh + k * stK, idS, 1);
+#pragma unroll
+                for (int k = 0; k < HD / 16; k++) mma_f16_ta(tS, tmem + TM_Q + 8 * k, dKh + k * stK, idS, 1);
                 mma_commit(&mS[i & 1]);
+                mma_commit(&mKfree[i & 1]);
+            };
+            auto issue_PV = [&](int i) {  // P V(i) into buffer i & 1 from P buffer i & 1 and value slot i & 1
+                const uint32_t tO = tmem + TM_O + 128 * (i & 1);
+                const uint64_t dVh = dV0 + (i & 1) * slot_off, dVl = dVh + lo_off;
+                const uint64_t dPh = dP0 + (i & 1) * 2 * pblk, dPl = dPh + pblk;
+                fence_after_sync();
+#pragma unroll
+                for (int k = 0; k < BK / 16; k++) mma_f16(tO, dPh + k * stP, dVl + k * stV, idO, k > 0 ? 1u : 0u);
+#pragma unroll
+                for (int k = 0; k < BK / 16; k++) mma_f16(tO, dPl + k * stP, dVh + k * stV, idO, 1);
+#pragma unroll
+                for (int k = 0; k < BK / 16; k++) mma_f16(tO, dPh + k * stP, dVh + k * stV, idO, 1);
+                mma_commit(&mPV[i & 1]);
+                mma_commit(&mVfree[i & 1]);
             };
             bool ok = true;
             for (int i = 0; i < min(nt, 2) && ok; i++) {
-                ok = wait(&mK[i & 1], 0);
+                ok = wait(&mK[i], 0);
                 if (ok) issue_S(i);
             }
             for (int i = 0; i < nt && ok; i++) {
                 const int b = i & 1;
                 const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-                // P V of tile i: its P written, its values here, O's accumulators folded
-                if (!(ok = wait(mP, (uint32_t)i & 1u))) break;
-                if (!(ok = wait(&mV[b], ph))) break;
-                if (i > 0 && !(ok = wait(mO, (uint32_t)(i - 1) & 1u))) break;
-                fence_after_sync();
+                // P V of tile i: its P written, its values here, the fold of P V(i - 2) done (the three tests
+                // issued together; a blocking wait only for one that is not complete yet)
                 {
-                    const uint64_t dVh = dV0 + b * slot_off, dVl = dVh + lo_off;
-#pragma unroll
-                    for (int k = 0; k < BK / 16; k++) {
-                        mma_f16(tO, dPh + k * stQ, dVh + k * stV, idO, k > 0 ? 1u : 0u);
-                        mma_f16(tO + 128, dPh + k * stQ, dVl + k * stV, idO, k > 0 ? 1u : 0u);
-                        mma_f16(tO + 128, dPl + k * stQ, dVh + k * stV, idO, 1);
-                    }
-                    mma_commit(mPV);
+                    const bool p = mbar_test_wait(&mP[b], ph), v = mbar_test_wait(&mV[b], ph);
+                    const bool o = i < 2 || mbar_test_wait(&mOfree[b], ph ^ 1u);
+                    if (!p && !(ok = wait(&mP[b], ph))) break;
+                    if (!v && !(ok = wait(&mV[b], ph))) break;
+                    if (!o && !(ok = wait(&mOfree[b], ph ^ 1u))) break;
                 }
-                // S of tile i + 2 into the buffer the softmax of tile i has read, from its keys
+                issue_PV(i);
+                // S of tile i + 2 into the buffer the softmax of tile i has read
                 if (i + 2 < nt) {
-                    if (!(ok = wait(&mSfree[b], ph))) break;
-                    if (!(ok = wait(&mK[b], (uint32_t)((i + 2) >> 1) & 1u))) break;
+                    const bool f = mbar_test_wait(&mSfree[b], ph), k = mbar_test_wait(&mK[b], ph ^ 1u);
+                    if (!f && !(ok = wait(&mSfree[b], ph))) break;
+                    if (!k && !(ok = wait(&mK[b], ph ^ 1u))) break;
                     issue_S(i + 2);
                 }
             }
             // every MMA completes before the block lets go of tensor memory
             mma_commit(mDone);
             mbar_wait(mDone, 0, TC_WAIT_CYCLES);
-        } else if (warp == 9 && lane == 0) {
-            // the load thread: tile i + 2's keys where tile i's were once S(i) is done, its values once P V(i) is
-            int ki = min(nt, 2), vi = min(nt, 2);  // key / value loads started
+        }
+    } else if (warp == 9) {
+        if (lane == 0) {
+            // the load thread: tile i + 2's keys into tile i's slot once S(i) is done, its values once P V(i) is
+            int kl = min(nt, 2), vl = kl;  // key / value loads started
             for (int i = 0; i + 2 < nt; i++) {
-                const int b = i & 1;
-                if (!wait(&mS[b], (uint32_t)(i >> 1) & 1u)) break;
+                const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+                if (!wait(&mKfree[i & 1], ph)) break;
                 load(i + 2, false);
-                ki = i + 3;
-                if (!wait(mPV, (uint32_t)i & 1u)) break;
+                kl = i + 3;
+                if (!wait(&mVfree[i & 1], ph)) break;
                 load(i + 2, true);
-                vi = i + 3;
+                vl = i + 3;
             }
             // the last load into each slot lands before the block lets go of shared memory
-            for (int j = max(0, ki - 2); j < ki; j++) mbar_wait(&mK[j & 1], (uint32_t)(j >> 1) & 1u, TC_WAIT_CYCLES);
-            for (int j = max(0, vi - 2); j < vi; j++) mbar_wait(&mV[j & 1], (uint32_t)(j >> 1) & 1u, TC_WAIT_CYCLES);
+            for (int j = max(0, kl - 2); j < kl; j++) mbar_wait(&mK[j & 1], (uint32_t)(j >> 1) & 1u, TC_WAIT_CYCLES);
+            for (int j = max(0, vl - 2); j < vl; j++) mbar_wait(&mV[j & 1], (uint32_t)(j >> 1) & 1u, TC_WAIT_CYCLES);
         }
-    } else {
-        bool alive = true;
+    } else if (part == 0) {
+        // softmax: S(i) -> P(i) = e^(S - m) (scaled by 2^14 so small weights stay normal in f16) and the factor f
+        float mrun = -FLT_MAX, lrun = 0.f;
         for (int i = 0; i < nt; i++) {
             const int b = i & 1;
-            const uint32_t ph = (uint32_t)(i >> 1) & 1u;
             const int len = a.tiles[t0 + i].z;
-            // (1) the online softmax of S(i), two threads per row; the compute warps leave together or not at all
-            const bool okS = alive && !*abort_flag && mbar_wait(&mS[b], ph, TC_WAIT_CYCLES);
-            if (!compute_all(okS)) {
-                if (tid == 0) *abort_flag = 1;
-                alive = false;
-                break;
-            }
+            if (!wait_warp(&mS[b], (uint32_t)(i >> 1) & 1u)) break;
             fence_after_sync();
-            __syncwarp();
-            float s[32];
+            float s[64];
             {
                 float x[32], y[32];
-                const uint32_t tS = tmem + 128 * b + lane_base + 32 * half;
-                tmem_ld32(tS, x);
-                tmem_ld32(tS + 64, y);
+                tmem_ld32(tmem + lane_base + TM_S + 64 * b, x);
+                tmem_ld32(tmem + lane_base + TM_S + 64 * b + 32, y);
                 tmem_wait_ld();
 #pragma unroll
-                for (int k = 0; k < 32; k++) s[k] = (x[k] + y[k]) * rs;
+                for (int k = 0; k < 32; k++) s[k] = x[k], s[32 + k] = y[k];
             }
             fence_before_sync();
             mbar_arrive(&mSfree[b]);
+            // the scores are s * rs (rs > 0, so the largest raw score gives the largest score)
             float mx = -FLT_MAX;
+            if (len == BK) {
 #pragma unroll
-            for (int k = 0; k < 32; k++)
-                if (32 * half + k < len) mx = fmaxf(mx, s[k]);
-            redm[half * BQ + row] = mx;
-            asm volatile("bar.sync 1, 256;" ::: "memory");
-            const float mnew = fmaxf(mrun, fmaxf(redm[row], redm[BQ + row]));
+                for (int k = 0; k < 64; k++) mx = fmaxf(mx, s[k]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 64; k++)
+                    if (k < len) mx = fmaxf(mx, s[k]);
+            }
+            const float mnew = fmaxf(mrun, mx * rs);
             const float f = lrun > 0.f ? exp_sfu(mrun - mnew) : 0.f;
+            // p 2^14 = 2^(s rs log2 e - (mnew log2 e - 14)): one FMA and one ex2 per weight (2^14 keeps small
+            // weights normal in f16)
+            const float c1 = rs * 1.44269504088896340736f, c0 = mnew * 1.44269504088896340736f - 14.f;
             float psum = 0.f;
 #pragma unroll
-            for (int k = 0; k < 32; k++) {
-                const float p = 32 * half + k < len ? exp_sfu(s[k] - mnew) : 0.f;
-                s[k] = p * 16384.f;  // 2^14: small weights stay normal in f16
-                psum += p;
+            for (int k = 0; k < 64; k++) {
+                float p;
+                asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(fmaf(s[k], c1, -c0)));
+                s[k] = (len == BK || k < len) ? p : 0.f;
+                psum += s[k];
             }
-            reds[half * BQ + row] = psum;
-            if (half == 0) fr[row] = f;
+            psum *= 1.0f / 16384.f;
+            // P(i) replaces P(i - 2) once P V(i - 2) has read it
+            if (i >= 2 && !wait_warp(&mPV[b], (uint32_t)((i - 2) >> 1) & 1u)) break;
+            __half *Phi = Pbuf + (size_t)b * 2 * BQ * BK, *Plo = Phi + BQ * BK;
 #pragma unroll
-            for (int g = 0; g < 4; g++) {
+            for (int g = 0; g < 8; g++) {
                 float v[8];
 #pragma unroll
                 for (int e = 0; e < 8; e++) v[e] = s[g * 8 + e];
-                put8x2(Phi, Plo, kmajor_off(row, 32 * half + g * 8, BQ), v);
+                put8x2(Phi, Plo, kmajor_off(row, g * 8, BQ), v);
             }
+            fr[(i & 3) * BQ + row] = f;
             fence_async_smem();
-            mbar_arrive(mP);
-            asm volatile("bar.sync 1, 256;" ::: "memory");
-            lrun = lrun * f + (reds[row] + reds[BQ + row]);
+            fence_before_sync();
+            mbar_arrive(&mP[b]);
+            mbar_arrive(&mF[i & 3]);
+            lrun = lrun * f + psum;
             mrun = mnew;
-            // (2) fold P V(i) into O: O = O * f + (hi*hi + cross terms); a failed wait is voted on at the next step
-            alive = mbar_wait(mPV, (uint32_t)i & 1u, TC_WAIT_CYCLES);
+        }
+        rowx[row] = mrun, rowx[BQ + row] = lrun, rowx[2 * BQ + row] = lrun > 0.f ? 1.0f / lrun : 0.f;
+    } else if (warp < 8) {
+        // fold: O = O f(i) + P V(i), in registers
+        float o[128];
+#pragma unroll
+        for (int e = 0; e < 128; e++) o[e] = 0.f;
+        for (int i = 0; i < nt; i++) {
+            const int b = i & 1;
+            if (!wait_warp(&mPV[b], (uint32_t)(i >> 1) & 1u)) break;
+            if (!wait_warp(&mF[i & 3], (uint32_t)(i >> 2) & 1u)) break;
             fence_after_sync();
-            __syncwarp();
-            if (alive) {
-                const float fo = fr[row];
+            const float f = fr[(i & 3) * BQ + row];
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    float x[32], y[32];
-                    tmem_ld32(tO + lane_base + 64 * half + 32 * c, x);
-                    tmem_ld32(tO + 128 + lane_base + 64 * half + 32 * c, y);
-                    tmem_wait_ld();
+            for (int c = 0; c < 4; c++) {
+                float x[32];
+                tmem_ld32(tmem + lane_base + TM_O + 128 * b + 32 * c, x);
+                tmem_wait_ld();
 #pragma unroll
-                    for (int k = 0; k < 32; k++) o[32 * c + k] = fmaf(o[32 * c + k], fo, x[k] + y[k]);
-                }
+                for (int k = 0; k < 32; k++) o[32 * c + k] = fmaf(o[32 * c + k], f, x[k]);
             }
             fence_before_sync();
-            mbar_arrive(mO);
-            any = true;
+            mbar_arrive(&mOfree[b]);
         }
-        if (!compute_all(alive)) {
-            if (tid == 0) *abort_flag = 1;
-        }
+        // after the last fold no MMA or load touches the key and value rings (on an abort the rows are not used)
+#pragma unroll
+        for (int k = 0; k < HD; k++) ostage[row * (HD + 1) + k] = o[k];
     }
     fence_before_sync();
     __syncthreads();
-    const bool ok = any && !*abort_flag;
-    const int r = r0 + row;
-    if (!producer && r < a.R) {
+    const bool ok = nt > 0 && !*abort_flag;
+    if (tid < 2 * BQ) {
         const float oun = pow2f(-14 - a.tc_eV);
-        const int col = 64 * half;
-        if (a.splits == 1 && !a.parts_only) {
-            const float inv = ok ? 1.0f / lrun : 0.f;
-            float *dst = a.out + (size_t)r * a.ldo + h * HD + col;
-#pragma unroll
-            for (int k = 0; k < 64; k++) dst[k] = o[k] * oun * inv;
-        } else {
-            float *dst = a.part_acc + ((size_t)split * a.R + r) * d + h * HD + col;
-#pragma unroll
-            for (int k = 0; k < 64; k++) dst[k] = ok ? o[k] * oun : 0.f;
-            if (half == 0) {
-                float *ms = a.part_ms + (((size_t)split * a.R + r) * H + h) * 2;
-                ms[0] = ok ? mrun : -FLT_MAX, ms[1] = ok ? lrun : 0.f;
+        const bool whole = a.splits == 1 && !a.parts_only;
+        for (int idx = tid; idx < BQ * HD; idx += 2 * BQ) {
+            const int m = idx / HD, k = idx % HD, r = r0 + m;
+            if (r >= a.R) break;  // rows grow with idx
+            const float v = ostage[m * (HD + 1) + k] * oun;
+            if (whole) {
+                a.out[(size_t)r * a.ldo + h * HD + k] = ok ? v * rowx[2 * BQ + m] : 0.f;
+            } else {
+                a.part_acc[((size_t)split * a.R + r) * d + h * HD + k] = ok ? v : 0.f;
+                if (k == 0) {
+                    float *ms = a.part_ms + (((size_t)split * a.R + r) * H + h) * 2;
+                    ms[0] = ok ? rowx[m] : -FLT_MAX, ms[1] = ok ? rowx[BQ + m] : 0.f;
+                }
             }
         }
     }
     if (*abort_flag && tid == 0 && a.err) atomicExch(a.err, 1);
+    // split parts: the last of a (row block, head)'s splits to finish merges them (the log-sum-exp merge of
+    // k_attend_merge, predict.rs:455-478, with the same products and order of sums)
+    if (a.splits > 1 && !a.parts_only && a.merge_cnt) {
+        volatile int *last = abort_flag + 1;
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            int *cnt = a.merge_cnt + blockIdx.x * H + h;
+            const int prev = atomicAdd(cnt, 1);
+            *last = prev == a.splits - 1;
+            if (prev == a.splits - 1) *cnt = 0;  // every split has arrived: ready for the next launch
+        }
+        __syncthreads();
+        if (*last) {
+            __threadfence();
+            const int P = a.splits;
+            float *wts = reinterpret_cast<float *>(Pbuf);  // [P][BQ] part weights, then [BQ] 1 / sums
+            float *winv = wts + P * BQ;
+            if (tid < BQ && r0 + tid < a.R) {
+                const int r = r0 + tid;
+                float M = -FLT_MAX;
+                for (int p = 0; p < P; p++) {
+                    const float *q = a.part_ms + (((size_t)p * a.R + r) * H + h) * 2;
+                    if (__ldcg(q + 1) > 0.f) M = fmaxf(M, __ldcg(q));
+                }
+                float S = 0.f;
+                for (int p = 0; p < P; p++) {
+                    const float *q = a.part_ms + (((size_t)p * a.R + r) * H + h) * 2;
+                    const float l = __ldcg(q + 1), w = l > 0.f ? exp1(__ldcg(q) - M) : 0.f;
+                    wts[p * BQ + tid] = w;
+                    S = __fadd_rn(S, __fmul_rn(l, w));
+                }
+                winv[tid] = 1.0f / S;
+            }
+            __syncthreads();
+            const size_t pstride = (size_t)a.R * d;
+            const float oun = pow2f(-14 - a.tc_eV);
+            if (tid < 2 * BQ && P <= 8) {
+                // four values of a row per thread and step, every part's loads issued before any is used; this
+                // block's own part is still in shared memory
+                constexpr int STEPS = BQ * HD / 4 / (2 * BQ);
+#pragma unroll 1
+                for (int st = 0; st < STEPS; st += 2) {
+                    float4 v[2][8], ownv[2];
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        const int e4 = tid + (st + u) * 2 * BQ, m = e4 / (HD / 4), k0 = (e4 % (HD / 4)) * 4;
+                        const int r = min(r0 + m, a.R - 1);
+                        const float *base = a.part_acc + (size_t)r * d + h * HD + k0;
+#pragma unroll
+                        for (int p = 0; p < 8; p++) {
+                            if (p < P && p != split) v[u][p] = __ldcg(reinterpret_cast<const float4 *>(base + p * pstride));
+                        }
+                        const float *own = ostage + m * (HD + 1) + k0;
+                        ownv[u] = make_float4(own[0] * oun, own[1] * oun, own[2] * oun, own[3] * oun);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        const int e4 = tid + (st + u) * 2 * BQ, m = e4 / (HD / 4), k0 = (e4 % (HD / 4)) * 4, r = r0 + m;
+                        if (r >= a.R) continue;
+                        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int p = 0; p < 8; p++) {
+                            if (p < P) {
+                                const float4 x = p == split ? ownv[u] : v[u][p];
+                                const float w = wts[p * BQ + m];
+                                o.x = __fadd_rn(o.x, __fmul_rn(x.x, w)), o.y = __fadd_rn(o.y, __fmul_rn(x.y, w));
+                                o.z = __fadd_rn(o.z, __fmul_rn(x.z, w)), o.w = __fadd_rn(o.w, __fmul_rn(x.w, w));
+                            }
+                        }
+                        const float iv = winv[m];
+                        *reinterpret_cast<float4 *>(a.out + (size_t)r * a.ldo + h * HD + k0) =
+                            make_float4(o.x * iv, o.y * iv, o.z * iv, o.w * iv);
+                    }
+                }
+            } else if (tid < 2 * BQ) {
+                for (int idx = tid; idx < BQ * HD; idx += 2 * BQ) {
+                    const int m = idx / HD, k = idx % HD, r = r0 + m;
+                    if (r >= a.R) break;
+                    const float *base = a.part_acc + (size_t)r * d + h * HD + k;
+                    float o = 0.f;
+                    for (int w = 0; w < 8 && w < P; w++) {
+                        float ow = 0.f;
+                        for (int p = w; p < P; p += 8) ow = fmaf(__ldcg(base + p * pstride), wts[p * BQ + m], ow);
+                        o += ow;
+                    }
+                    a.out[(size_t)r * a.ldo + h * HD + k] = o * winv[m];
+                }
+            }
+        }
+    }
+    fence_before_sync();
+    __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 size_t attend_tc_smem() {
-    return sizeof(__half) * (2 * TC_BQ * TC_HD + 2 * 4 * TC_BLOCK + 2 * TC_BQ * TC_BK) + sizeof(float) * 5 * TC_BQ +
-           12 * sizeof(uint64_t) + 16;
+    return sizeof(__half) * (2 * 4 * TC_BLOCK + 4 * TC_BQ * TC_BK) + sizeof(float) * 7 * TC_BQ + 23 * sizeof(uint64_t) +
+           16;  // the TMEM slot, the abort flag and the last-split flag
 }
 
 cudaError_t launch_tc_tiles(int kv, const AttnArgs &a, void *out, cudaStream_t s, uint64_t *launches) {
@@ -483,7 +586,7 @@ cudaError_t launch_attend_tc(int kv, const AttnArgs &a, cudaStream_t s, uint64_t
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     if (launches) ++*launches;
-    if (a.splits > 1 && !a.parts_only) return launch_attend_merge(a, a.splits, s, launches);
+    if (a.splits > 1 && !a.parts_only && !a.merge_cnt) return launch_attend_merge(a, a.splits, s, launches);
     return cudaSuccess;
 }
 
@@ -534,7 +637,7 @@ int tc_exponent(float mx) {
 // D[128][N] = A[128][128] B[N][128]^T with small-integer f16 values (exact in f32), B K-major or MN-major, on the
 // tensor cores and on CUDA cores; writes the largest difference and whether every wait finished.
 template <int N>
-__global__ void __launch_bounds__(128) k_tc_selftest(int b_mn_major, float *result) {
+__global__ void __launch_bounds__(128) k_tc_selftest(int b_mn_major, int a_tmem, float *result) {
     extern __shared__ __align__(1024) uint8_t smraw[];
     __half *A = reinterpret_cast<__half *>(smraw);  // [128][128] K-major
     __half *B = A + 128 * 128;                       // [N][128]
@@ -564,9 +667,31 @@ __global__ void __launch_bounds__(128) k_tc_selftest(int b_mn_major, float *resu
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = *tslot;
+    if (a_tmem) {
+        // A into columns 128-191, one row per lane: column c holds k = 2c (low half) and 2c + 1
+        const int m = tid;
+        for (int h = 0; h < 2; h++) {
+            uint32_t v[32];
+            for (int c = 0; c < 32; c++) {
+                const int k = 2 * (32 * h + c);
+                const __half2 p = __floats2half2_rn(av(m, k), av(m, k + 1));
+                v[c] = *reinterpret_cast<const uint32_t *>(&p);
+            }
+            tmem_st32u(tmem + ((uint32_t)(warp * 32) << 16) + 128 + 32 * h, v);
+        }
+        tmem_wait_st();
+        fence_before_sync();
+        __syncthreads();
+        fence_after_sync();
+    }
     if (tid == 0) {
         const uint32_t id = idesc_f16(128, N, 0, b_mn_major);
-        for (int s = 0; s < 8; s++) mma_f16(tmem, kstep_desc(A, 128, s), kstep_desc(B, N, s), id, s > 0);
+        for (int s = 0; s < 8; s++) {
+            if (a_tmem)
+                mma_f16_ta(tmem, tmem + 128 + 8 * s, kstep_desc(B, N, s), id, s > 0);
+            else
+                mma_f16(tmem, kstep_desc(A, 128, s), kstep_desc(B, N, s), id, s > 0);
+        }
         mma_commit(mbar);
     }
     const bool ok = mbar_wait(mbar, 0, TC_WAIT_CYCLES);
@@ -604,8 +729,10 @@ cudaError_t launch_tc_selftest(float *result, cudaStream_t s) {
     e = cudaFuncSetAttribute(k_tc_selftest<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem128);
     if (e != cudaSuccess) return e;
     for (int mn = 0; mn < 2; mn++) {
-        k_tc_selftest<64><<<1, 128, smem64, s>>>(mn, result);
-        k_tc_selftest<128><<<1, 128, smem128, s>>>(mn, result);
+        for (int at = 0; at < 2; at++) {
+            k_tc_selftest<64><<<1, 128, smem64, s>>>(mn, at, result);
+            k_tc_selftest<128><<<1, 128, smem128, s>>>(mn, at, result);
+        }
     }
     return cudaGetLastError();
 }

@@ -133,7 +133,9 @@ struct tcu_model {
     bool tc_scanned = false;
     DevBuf tctiles;  // every layer's keys and values as pre-split tensor-core tiles (head width 128)
     // working memory, grown to the largest call so far
-    DevBuf h, q, att, mid, stats, out, part_ms, part_acc, ssm, atiles;  // atiles: rows split for the tensor cores  // ssm: the query MLP's hidden units and outputs
+    // ssm: the query MLP's hidden units and outputs; atiles: rows split for the tensor cores; mcnt: per (128-row
+    // block, head) arrival counters of the tensor-core attention's splits, zero between launches
+    DevBuf h, q, att, mid, stats, out, part_ms, part_acc, ssm, atiles, mcnt;
     DevBuf sh_m, sh_mall, sh_packed;  // the cross-device merge: local maxima, their maximum, (values, weight sums)
     // the one-kernel few-row stage: key tiles (head-major), per-layer pointer table, barrier words, partials
     DevBuf rtiles, rlayers, rsync, rparts_ms, rparts_acc, rtmaps;
@@ -631,6 +633,10 @@ static void ensure_work(tcu_model *m, int R) {
     }
     const Plan plan = attend_plan(m->w->ctx, R, s.heads, s.d / s.heads, m->nitems, m->ntiles);
     const size_t pr = plan.path == Path::Decode ? (size_t)m->nitems : (size_t)plan.splits;  // parts, when left
+    if (m->mcnt.ensure(sizeof(int) * ((size_t)(R + 127) / 128) * std::max<size_t>(H, 1))) {
+        CU(cudaMemset(m->mcnt.p, 0, m->mcnt.bytes));
+        moved = true;
+    }
     if (pr) {
         moved |= m->part_ms.ensure(sizeof(float) * pr * R * H * 2);
         moved |= m->part_acc.ensure(sizeof(float) * pr * R * d);
@@ -689,6 +695,7 @@ static int attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int ro
     if (plan.path == Path::Tensor) {
         if (!tc_tiles) fail(TCU_ERR_STATE, "attend: tensor-core tiles were not built");
         a.tc_eK = eK, a.tc_eV = eV, a.err = ctx->dev_err, a.tc_tiles = tc_tiles;
+        if (m->mcnt.bytes >= sizeof(int) * ((size_t)(R + 127) / 128) * sh.heads) a.merge_cnt = m->mcnt.as<int>();
         ck(launch_attend_tc(kv, a, s, &ctx->launches), "attend (tensor cores)");
     } else {
         ck(launch_attend_flash(kv, hd, a, s, &ctx->launches), "attend (flash)");

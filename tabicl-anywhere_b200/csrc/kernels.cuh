@@ -50,6 +50,8 @@ struct AttnArgs {
     int *err = nullptr;            // set to 1 when a kernel gave up waiting
     int parts_only = 0;            // 1: always leave parts (no merge), even with a single split
     const void *tc_tiles = nullptr;  // tensor-core path: the layer's tiles pre-split by launch_tc_tiles
+    int *merge_cnt = nullptr;  // tensor-core path: [R / 128][heads] arrival counters (zero between launches); when
+                               // set, the last split of each (row block, head) merges the parts itself
 };
 
 // The few-row stage in one persistent kernel: per layer, the pointers it reads.
