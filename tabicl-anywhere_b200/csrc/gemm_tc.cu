@@ -43,78 +43,90 @@ __device__ __forceinline__ float p2(int e) { return __uint_as_float((uint32_t)(e
 
 size_t tc_split_bytes(int rows, int K) { return (size_t)((rows + GBM - 1) / GBM) * (size_t)(K / GBK) * 2 * GBLOCK * 2; }
 
-// Eight rows per block. Per row (one warp): the LayerNorm's mean and 1/sigma (when lnw is set; kern.rs:357-376, two
-// passes), and the power-of-two scale that keeps the row's largest transformed magnitude below 2^14;
-// stats[m] = {mean, rstd, scale, 1 / scale}. Then the rows, transformed and scaled, split into f16 hi + lo in their
-// 128 x 64 blocks: tiles[(m / 128) * (K / 64) + k / 64] = [hi block][lo block], element (m % 128, k % 64) at its
-// core-matrix offset. Eight consecutive threads write the eight rows of one core matrix (128 contiguous bytes).
-// Rows from M up to the next multiple of 128 are written as zeros.
+// Eight rows per block, one warp per row. Each lane holds 8 consecutive values of its row per 256 of K, read once:
+// the LayerNorm's mean and 1/sigma (when lnw is set; kern.rs:357-376, two passes over the held values), the
+// power-of-two scale that keeps the row's largest transformed magnitude below 2^14 (stats[m] = {mean, rstd, scale,
+// 1 / scale}), and the row, transformed and scaled, split into f16 hi + lo in its 128 x 64 blocks:
+// tiles[(m / 128) * (K / 64) + k / 64] = [hi block][lo block], element (m % 128, k % 64) at blk_off. Rows from M up
+// to the next multiple of 128 are written as zeros. NJ = K / 256 rounded up (K up to 2048).
+template <int NJ>
 __global__ void __launch_bounds__(256) k_split_rows(const float *x, int ldx, int M, int K, const float *lnw,
                                                     const float *lnb, float4 *stats, __half *tiles) {
-    __shared__ float sh_mean[8], sh_inv[8], sh_sc[8];
-    const int r0 = blockIdx.x * 8, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    {
-        const int row = r0 + warp;
-        const bool real = row < M;
-        const float *p = x + (size_t)(real ? row : 0) * ldx;
-        float mean = 0.f, inv = 1.f, mx = 0.f;
-        if (real) {
-            if (lnw) {
-                float s = 0.f;
-                for (int k = lane * 4; k < K; k += 128) {
-                    const float4 v = *reinterpret_cast<const float4 *>(p + k);
-                    s += (v.x + v.y) + (v.z + v.w);
-                }
-                mean = warp_sum(s) / (float)K;
-                float q = 0.f;
-                for (int k = lane; k < K; k += 32) {
-                    const float dd = p[k] - mean;
-                    q = fmaf(dd, dd, q);
-                }
-                inv = 1.0f / sqrtf(warp_sum(q) / (float)K + 1e-5f);
-            }
-            for (int k = lane; k < K; k += 32) {
-                const float v = lnw ? (p[k] - mean) * inv * lnw[k] + lnb[k] : p[k];
-                mx = fmaxf(mx, fabsf(v));
-            }
-            mx = warp_max(mx);
-        }
-        int e = 0;
-        if (mx > 0.f) {
-            e = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xff) - 126);  // mx < 2^(14 - e)
-            e = e < -120 ? -120 : (e > 120 ? 120 : e);
-        }
-        if (lane == 0) {
-            sh_mean[warp] = mean, sh_inv[warp] = inv, sh_sc[warp] = real ? p2(e) : 0.f;
-            if (real) stats[row] = make_float4(mean, inv, p2(e), p2(-e));
-        }
-    }
-    __syncthreads();
-    const int nk = K / GBK, mt = r0 / GBM;
-    for (int i = threadIdx.x; i < K; i += 256) {  // i = (group of 8 along K) * 8 + row
-        const int r = i & 7, k = (i >> 3) * 8, row = r0 + r;
-        const float sc = sh_sc[r];
-        float v[8];
-        if (row < M) {
-            const float *p = x + (size_t)row * ldx + k;
-            const float4 x0 = *reinterpret_cast<const float4 *>(p), x1 = *reinterpret_cast<const float4 *>(p + 4);
-            v[0] = x0.x, v[1] = x0.y, v[2] = x0.z, v[3] = x0.w, v[4] = x1.x, v[5] = x1.y, v[6] = x1.z, v[7] = x1.w;
-            if (lnw) {
-                const float mean = sh_mean[r], inv = sh_inv[r];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = blockIdx.x * 8 + warp;
+    const bool real = row < M;
+    const float *p = x + (size_t)(real ? row : 0) * ldx;
+    float v[NJ][8];
 #pragma unroll
-                for (int j = 0; j < 8; j++) v[j] = (v[j] - mean) * inv * lnw[k + j] + lnb[k + j];
-            }
+    for (int j = 0; j < NJ; j++) {
+        const int k = 256 * j + 8 * lane;
+        if (real && k < K) {
+            const float4 x0 = *reinterpret_cast<const float4 *>(p + k), x1 = *reinterpret_cast<const float4 *>(p + k + 4);
+            v[j][0] = x0.x, v[j][1] = x0.y, v[j][2] = x0.z, v[j][3] = x0.w;
+            v[j][4] = x1.x, v[j][5] = x1.y, v[j][6] = x1.z, v[j][7] = x1.w;
         } else {
 #pragma unroll
-            for (int j = 0; j < 8; j++) v[j] = 0.f;
+            for (int e = 0; e < 8; e++) v[j][e] = 0.f;
         }
-        __align__(16) __half hh[8], ll[8];
+    }
+    float mean = 0.f, inv = 1.f;
+    if (lnw) {
+        float s = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; j++) split_f16(v[j] * sc, hh[j], ll[j]);
-        __half *blk = tiles + ((size_t)mt * nk + k / GBK) * 2 * GBLOCK;
-        const int off = blk_off(row % GBM, k % GBK);
-        *reinterpret_cast<uint4 *>(blk + off) = *reinterpret_cast<const uint4 *>(hh);
-        *reinterpret_cast<uint4 *>(blk + GBLOCK + off) = *reinterpret_cast<const uint4 *>(ll);
+        for (int j = 0; j < NJ; j++)
+#pragma unroll
+            for (int e = 0; e < 8; e++) s += v[j][e];
+        mean = warp_sum(s) / (float)K;
+        float q = 0.f;
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            if (256 * j + 8 * lane < K) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const float dd = v[j][e] - mean;
+                    q = fmaf(dd, dd, q);
+                }
+            }
+        }
+        inv = 1.0f / sqrtf(warp_sum(q) / (float)K + 1e-5f);
+#pragma unroll
+        for (int j = 0; j < NJ; j++) {
+            const int k = 256 * j + 8 * lane;
+            if (k < K) {
+                const float4 w0 = *reinterpret_cast<const float4 *>(lnw + k), w1 = *reinterpret_cast<const float4 *>(lnw + k + 4);
+                const float4 b0 = *reinterpret_cast<const float4 *>(lnb + k), b1 = *reinterpret_cast<const float4 *>(lnb + k + 4);
+                const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[j][e] = real ? (v[j][e] - mean) * inv * w[e] + bb[e] : 0.f;
+            }
+        }
+    }
+    float mx = 0.f;
+#pragma unroll
+    for (int j = 0; j < NJ; j++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) mx = fmaxf(mx, fabsf(v[j][e]));
+    mx = warp_max(mx);
+    int ex = 0;
+    if (mx > 0.f) {
+        ex = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xff) - 126);  // mx < 2^(14 - ex)
+        ex = ex < -120 ? -120 : (ex > 120 ? 120 : ex);
+    }
+    const float sc = p2(ex);
+    if (lane == 0 && real) stats[row] = make_float4(mean, inv, sc, p2(-ex));
+    const int nk = K / GBK, mt = row / GBM;
+#pragma unroll
+    for (int j = 0; j < NJ; j++) {
+        const int k = 256 * j + 8 * lane;
+        if (k < K) {
+            __align__(16) __half hh[8], ll[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) split_f16(v[j][e] * sc, hh[e], ll[e]);
+            __half *blk = tiles + ((size_t)mt * nk + k / GBK) * 2 * GBLOCK;
+            const int off = blk_off(row % GBM, k % GBK);
+            *reinterpret_cast<uint4 *>(blk + off) = *reinterpret_cast<const uint4 *>(hh);
+            *reinterpret_cast<uint4 *>(blk + GBLOCK + off) = *reinterpret_cast<const uint4 *>(ll);
+        }
     }
 }
 
@@ -269,14 +281,22 @@ __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4
             // thread: row m (consecutive threads, consecutive addresses), columns e0, e0 + 2, ...
             const int m = tid & (GBM - 1), gm = m0 + m;
             if (gm < a.M) {
-#pragma unroll 4
-                for (int e = tid >> 7; e < BN; e += 2) {
-                    const int gn = n0 + e;
-                    if (gn >= a.N) break;
-                    float v = ostage[m * (BN + 1) + e] * a.tc_wunscale[gn] + (a.bias ? a.bias[gn] : 0.f);
-                    if (a.act) v = gelu1(v);
-                    float *dst = a.y + (size_t)gn * a.ldy + gm;
-                    *dst = a.accumulate ? *dst + v : v;
+                // eight columns at a time: the residual values are all loaded before any result is stored
+                for (int e0 = tid >> 7; e0 < BN; e0 += 16) {
+                    float old[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int gn = n0 + e0 + 2 * j;
+                        old[j] = a.accumulate && e0 + 2 * j < BN && gn < a.N ? a.y[(size_t)gn * a.ldy + gm] : 0.f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int e = e0 + 2 * j, gn = n0 + e;
+                        if (e >= BN || gn >= a.N) break;
+                        float v = ostage[m * (BN + 1) + e] * a.tc_wunscale[gn] + (a.bias ? a.bias[gn] : 0.f);
+                        if (a.act) v = gelu1(v);
+                        a.y[(size_t)gn * a.ldy + gm] = a.accumulate ? old[j] + v : v;
+                    }
                 }
             }
         } else {
@@ -286,12 +306,22 @@ __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4
             if (gn < a.N) {
                 const float ws = a.tc_wunscale[gn], bs = a.bias ? a.bias[gn] : 0.f;
                 const int mend = min(GBM, a.M - m0);
-#pragma unroll 8
-                for (int m = tid / BN; m < mend; m += RSTEP) {
-                    float v = ostage[m * (BN + 1) + e] * ws + bs;
-                    if (a.act) v = gelu1(v);
-                    float *dst = a.y + (size_t)(m0 + m) * a.ldy + gn;
-                    *dst = a.accumulate ? *dst + v : v;
+                // eight rows at a time: the residual values are all loaded before any result is stored
+                for (int mb = tid / BN; mb < mend; mb += 8 * RSTEP) {
+                    float old[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int m = mb + j * RSTEP;
+                        old[j] = a.accumulate && m < mend ? a.y[(size_t)(m0 + m) * a.ldy + gn] : 0.f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int m = mb + j * RSTEP;
+                        if (m >= mend) break;
+                        float v = ostage[m * (BN + 1) + e] * ws + bs;
+                        if (a.act) v = gelu1(v);
+                        a.y[(size_t)(m0 + m) * a.ldy + gn] = a.accumulate ? old[j] + v : v;
+                    }
                 }
             }
         }
@@ -339,9 +369,17 @@ static cudaError_t launch_bn(const LinArgs &a, float4 *stats, cudaStream_t s) {
 }
 
 cudaError_t launch_gemm_tc(const LinArgs &a, float4 *stats, cudaStream_t s, uint64_t *launches) {
-    if (!a.tc_wtiles || !a.tc_atiles || a.K % GBK) return cudaErrorInvalidValue;
-    k_split_rows<<<(a.M + GBM - 1) / GBM * (GBM / 8), 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats,
-                                                                       reinterpret_cast<__half *>(a.tc_atiles));
+    if (!a.tc_wtiles || !a.tc_atiles || a.K % GBK || a.K > 2048) return cudaErrorInvalidValue;
+    const int sblocks = (a.M + GBM - 1) / GBM * (GBM / 8);
+    __half *at = reinterpret_cast<__half *>(a.tc_atiles);
+    if (a.K <= 256)
+        k_split_rows<1><<<sblocks, 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
+    else if (a.K <= 512)
+        k_split_rows<2><<<sblocks, 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
+    else if (a.K <= 1024)
+        k_split_rows<4><<<sblocks, 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
+    else
+        k_split_rows<8><<<sblocks, 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
     if (launches) ++*launches;
     const cudaError_t e = gemm_bn(a.M, a.N) == 64 ? launch_bn<64>(a, stats, s) : launch_bn<128>(a, stats, s);
     if (launches) ++*launches;

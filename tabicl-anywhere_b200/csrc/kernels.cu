@@ -968,6 +968,7 @@ cudaError_t launch_linear(const LinArgs &a, float *stats_scratch, cudaStream_t s
         return cudaGetLastError();
     }
     if (a.tc_wtiles && a.tc_atiles && a.tc_atiles_bytes >= tc_split_bytes(a.M, a.K) && !a.bias_on_m && a.K % 64 == 0 &&
+        a.K <= 2048 &&
         a.ldx % 4 == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0 && gemm_tc_enabled())
         return launch_gemm_tc(a, reinterpret_cast<float4 *>(stats_scratch), s, launches);
     LinArgs b = a;
