@@ -143,34 +143,37 @@ __device__ __forceinline__ void expect_tx(uint64_t *mbar, uint32_t bytes) {
 // Tensor memory, 512 columns, one query row per lane:
 //   [0, 128)    Q: hi in 0-63, lo in 64-127 (f16 pairs, element 2c in the low half of column c): the A operand of
 //               S = Q K^T (K [64 keys x 128] K-major in shared memory)
-//   [128, 256)  S of two tiles, 64 columns each
-//   [256, 512)  P V^T of two tiles, 128 columns each (P [128 rows x 64 keys] of two tiles and V [128 x 64 keys],
-//               K-major in shared memory)
+//   [128, 320)  three S slots of 64 columns. The softmax overwrites S(i) in place with P(i) (hi in the first 32
+//               columns, lo in the next 32, f16 pairs): the A operand of P V^T (V [128 x 64 keys] K-major in shared
+//               memory)
+//   [384, 512)  P V^T of the latest tile
 // Roles: warps 0-3 run the online softmax (one thread per query row, the nn.rs:207-215 rule), warps 4-7 fold each
 // tile's P V into O held in registers (O = O f + P V), one thread of warp 8 issues every MMA, one thread of warp 9
-// bulk-copies keys and values into two-slot rings. They hand over through mbarriers only: S(i + 2) and P V(i) run
-// on the tensor cores while the softmax of tile i + 1 runs, and the fold of tile i while P V(i + 1) runs. Each
-// product is hi*hi + hi*lo + lo*hi with the two cross terms accumulated first, so the tensor cores' f32
-// accumulation (not round-to-nearest) adds only 8 (S) or 4 (P V) steps of full magnitude; every sum across tiles is
-// taken in registers. Every wait is bounded; a wait that gives up raises the block's abort flag and everyone leaves.
+// bulk-copies keys and values into three-slot rings. They hand over through mbarriers only: S(i + 2) runs on the
+// tensor cores while the softmax of tile i + 1 runs, and the fold of tile i while S(i + 2) runs. With both A
+// operands in TMEM the MMAs read only K and V from shared memory. Each product is hi*hi + hi*lo + lo*hi with the
+// two cross terms accumulated first, so the tensor cores' f32 accumulation (not round-to-nearest) adds only 8 (S)
+// or 4 (P V) steps of full magnitude; every sum across tiles is taken in registers. Every wait is bounded; a wait
+// that gives up raises the block's abort flag and everyone leaves.
 constexpr int TC_THREADS = 320;  // four softmax warps, four fold warps, an MMA warp and a load warp
-constexpr uint32_t TM_Q = 0, TM_S = 128, TM_O = 256;
+constexpr int TC_SLOTS = 3;      // S/P slots in TMEM, key and value slots in shared memory
+constexpr uint32_t TM_Q = 0, TM_SP = 128, TM_O = 384;
 
 template <int KV>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
-    constexpr int HD = TC_HD, BQ = TC_BQ, BK = TC_BK;
+    constexpr int HD = TC_HD, BQ = TC_BQ, BK = TC_BK, NS = TC_SLOTS;
     extern __shared__ __align__(1024) uint8_t smraw[];
-    __half *Kring = reinterpret_cast<__half *>(smraw);  // two slots of [keys hi][keys lo]
-    __half *Vring = Kring + 2 * 2 * TC_BLOCK;           // two slots of [values hi][values lo]
-    __half *Pbuf = Vring + 2 * 2 * TC_BLOCK;            // two buffers of [P hi][P lo], each [BQ][BK keys] K-major
-    float *fr = reinterpret_cast<float *>(Pbuf + 2 * 2 * BQ * BK);  // [4][BQ]: tile i's rescale factors in i % 4
+    __half *Kring = reinterpret_cast<__half *>(smraw);                 // NS slots of [keys hi][keys lo]
+    __half *Vring = Kring + NS * 2 * TC_BLOCK;                         // NS slots of [values hi][values lo]
+    float *fr = reinterpret_cast<float *>(Vring + NS * 2 * TC_BLOCK);  // [4][BQ]: tile i's rescale factors in i % 4
     float *rowx = fr + 4 * BQ;  // [3][BQ]: each row's m, l and 1 / l at the end
     uint64_t *mb = reinterpret_cast<uint64_t *>(rowx + 3 * BQ);
-    uint64_t *mK = mb, *mV = mb + 2, *mKfree = mb + 4, *mVfree = mb + 6, *mS = mb + 8, *mSfree = mb + 10,
-             *mPV = mb + 12, *mOfree = mb + 14, *mF = mb + 16, *mP = mb + 20, *mDone = mb + 22;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(mb + 23);
+    uint64_t *mK = mb, *mV = mb + NS, *mKfree = mb + 2 * NS, *mVfree = mb + 3 * NS;
+    uint64_t *mS = mb + 4 * NS, *mP = mb + 5 * NS, *mSlot = mb + 6 * NS;  // S done, P written, P V done, per slot
+    uint64_t *mPV = mb + 7 * NS, *mOfree = mPV + 1, *mF = mPV + 2, *mDone = mPV + 6;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(mPV + 7);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
-    float *qmax = reinterpret_cast<float *>(Pbuf);     // [2][BQ] query halves' maxima, before the first P
+    float *qmax = fr;                                  // [2][BQ] query halves' maxima, before the first factor
     float *ostage = reinterpret_cast<float *>(Kring);  // [BQ][HD + 1] after the last fold
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -184,12 +187,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
         tmem_relinquish();
     }
     if (tid == 0) {
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < NS; i++) {
             mbar_init(&mK[i], 1), mbar_init(&mV[i], 1), mbar_init(&mKfree[i], 1), mbar_init(&mVfree[i], 1);
-            mbar_init(&mS[i], 1), mbar_init(&mSfree[i], BQ), mbar_init(&mPV[i], 1), mbar_init(&mOfree[i], BQ);
+            mbar_init(&mS[i], 1), mbar_init(&mP[i], BQ), mbar_init(&mSlot[i], 1);
         }
+        mbar_init(mPV, 1), mbar_init(mOfree, BQ);
         for (int i = 0; i < 4; i++) mbar_init(&mF[i], BQ);
-        mbar_init(&mP[0], BQ), mbar_init(&mP[1], BQ);
         mbar_init(mDone, 1);
         mbar_init_fence();
         *abort_flag = 0;
@@ -218,15 +221,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
     fence_after_sync();
     const uint32_t tmem = *tslot;
     const uint32_t half_bytes = (uint32_t)(2 * TC_BLOCK * sizeof(__half));
-    auto load = [&](int i, bool values) {  // the load thread: keys or values of tile t0 + i into slot i & 1
+    auto load = [&](int i, bool values) {  // the load thread: keys or values of tile t0 + i into slot i % NS
         const __half *src = tiles + ((size_t)(t0 + i) * H + h) * 4 * TC_BLOCK + (values ? 2 * TC_BLOCK : 0);
-        __half *dst = (values ? Vring : Kring) + (size_t)(i & 1) * 2 * TC_BLOCK;
-        uint64_t *m = values ? &mV[i & 1] : &mK[i & 1];
+        __half *dst = (values ? Vring : Kring) + (size_t)(i % NS) * 2 * TC_BLOCK;
+        uint64_t *m = values ? &mV[i % NS] : &mK[i % NS];
         expect_tx(m, half_bytes);
         bulk_g2s(dst, src, half_bytes, m);
     };
     if (warp == 9 && lane == 0) {
-        for (int i = 0; i < min(nt, 2); i++) load(i, false), load(i, true);
+        for (int i = 0; i < min(nt, NS); i++) load(i, false), load(i, true);
     }
     // the row's query scale (its largest |q| maps below 2^14); Q split into TMEM
     float rs = 1.f;
@@ -263,15 +266,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
 
     if (warp == 8) {
         if (lane == 0) {
-            // the MMA thread: waits only for what its next MMAs read
+            // the MMA thread: waits only for what its next MMAs read or overwrite
             const uint32_t idS = idesc_f16(BQ, BK, 0, 0), idO = idesc_f16(BQ, HD, 0, 0);
-            const uint64_t dK0 = kstep_desc(Kring, BK, 0), dV0 = kstep_desc(Vring, HD, 0), dP0 = kstep_desc(Pbuf, BQ, 0);
-            const uint64_t stP = (2 * (BQ / 8) * 128) >> 4, stK = (2 * (BK / 8) * 128) >> 4, stV = (2 * (HD / 8) * 128) >> 4;
-            const uint64_t pblk = (BQ * BK * sizeof(__half)) >> 4;  // P hi to P lo, and one P buffer to the next / 2
+            const uint64_t dK0 = kstep_desc(Kring, BK, 0), dV0 = kstep_desc(Vring, HD, 0);
+            const uint64_t stK = (2 * (BK / 8) * 128) >> 4, stV = (2 * (HD / 8) * 128) >> 4;
             const uint64_t lo_off = (TC_BLOCK * sizeof(__half)) >> 4, slot_off = (2 * TC_BLOCK * sizeof(__half)) >> 4;
-            auto issue_S = [&](int i) {  // S(i) into buffer i & 1 from key slot i & 1
-                const uint32_t tS = tmem + TM_S + 64 * (i & 1);
-                const uint64_t dKh = dK0 + (i & 1) * slot_off, dKl = dKh + lo_off;
+            auto issue_S = [&](int i) {  // S(i) into TMEM slot i % NS from key slot i % NS
+                const int sl = i % NS;
+                const uint32_t tS = tmem + TM_SP + 64 * sl;
+                const uint64_t dKh = dK0 + sl * slot_off, dKl = dKh + lo_off;
                 fence_after_sync();
 #pragma unroll
                 for (int k = 0; k < HD / 16; k++) mma_f16_ta(tS, tmem + TM_Q + 8 * k, dKl + k * stK, idS, k > 0 ? 1u : 0u);
@@ -279,22 +282,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
                 for (int k = 0; k < HD / 16; k++) mma_f16_ta(tS, tmem + TM_Q + 64 + 8 * k, dKh + k * stK, idS, 1);
 #pragma unroll
                 for (int k = 0; k < HD / 16; k++) mma_f16_ta(tS, tmem + TM_Q + 8 * k, dKh + k * stK, idS, 1);
-                mma_commit(&mS[i & 1]);
-                mma_commit(&mKfree[i & 1]);
+                mma_commit(&mS[sl]);
+                mma_commit(&mKfree[sl]);
             };
-            auto issue_PV = [&](int i) {  // P V(i) into buffer i & 1 from P buffer i & 1 and value slot i & 1
-                const uint32_t tO = tmem + TM_O + 128 * (i & 1);
-                const uint64_t dVh = dV0 + (i & 1) * slot_off, dVl = dVh + lo_off;
-                const uint64_t dPh = dP0 + (i & 1) * 2 * pblk, dPl = dPh + pblk;
+            auto issue_PV = [&](int i) {  // P V(i) from P in TMEM slot i % NS and value slot i % NS
+                const int sl = i % NS;
+                const uint32_t pA = tmem + TM_SP + 64 * sl, tO = tmem + TM_O;
+                const uint64_t dVh = dV0 + sl * slot_off, dVl = dVh + lo_off;
                 fence_after_sync();
 #pragma unroll
-                for (int k = 0; k < BK / 16; k++) mma_f16(tO, dPh + k * stP, dVl + k * stV, idO, k > 0 ? 1u : 0u);
+                for (int k = 0; k < BK / 16; k++) mma_f16_ta(tO, pA + 8 * k, dVl + k * stV, idO, k > 0 ? 1u : 0u);
 #pragma unroll
-                for (int k = 0; k < BK / 16; k++) mma_f16(tO, dPl + k * stP, dVh + k * stV, idO, 1);
+                for (int k = 0; k < BK / 16; k++) mma_f16_ta(tO, pA + 32 + 8 * k, dVh + k * stV, idO, 1);
 #pragma unroll
-                for (int k = 0; k < BK / 16; k++) mma_f16(tO, dPh + k * stP, dVh + k * stV, idO, 1);
-                mma_commit(&mPV[i & 1]);
-                mma_commit(&mVfree[i & 1]);
+                for (int k = 0; k < BK / 16; k++) mma_f16_ta(tO, pA + 8 * k, dVh + k * stV, idO, 1);
+                mma_commit(mPV);
+                mma_commit(&mVfree[sl]);
+                mma_commit(&mSlot[sl]);
             };
             bool ok = true;
             for (int i = 0; i < min(nt, 2) && ok; i++) {
@@ -302,24 +306,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
                 if (ok) issue_S(i);
             }
             for (int i = 0; i < nt && ok; i++) {
-                const int b = i & 1;
-                const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-                // P V of tile i: its P written, its values here, the fold of P V(i - 2) done (the three tests
+                const int sl = i % NS;
+                const uint32_t ph = (uint32_t)(i / NS) & 1u;
+                // P V of tile i: its P written, its values here, the fold of P V(i - 1) done (the three tests
                 // issued together; a blocking wait only for one that is not complete yet)
                 {
-                    const bool p = mbar_test_wait(&mP[b], ph), v = mbar_test_wait(&mV[b], ph);
-                    const bool o = i < 2 || mbar_test_wait(&mOfree[b], ph ^ 1u);
-                    if (!p && !(ok = wait(&mP[b], ph))) break;
-                    if (!v && !(ok = wait(&mV[b], ph))) break;
-                    if (!o && !(ok = wait(&mOfree[b], ph ^ 1u))) break;
+                    const bool p = mbar_test_wait(&mP[sl], ph), v = mbar_test_wait(&mV[sl], ph);
+                    const bool o = i < 1 || mbar_test_wait(mOfree, (uint32_t)(i - 1) & 1u);
+                    if (!p && !(ok = wait(&mP[sl], ph))) break;
+                    if (!v && !(ok = wait(&mV[sl], ph))) break;
+                    if (!o && !(ok = wait(mOfree, (uint32_t)(i - 1) & 1u))) break;
                 }
                 issue_PV(i);
-                // S of tile i + 2 into the buffer the softmax of tile i has read
-                if (i + 2 < nt) {
-                    const bool f = mbar_test_wait(&mSfree[b], ph), k = mbar_test_wait(&mK[b], ph ^ 1u);
-                    if (!f && !(ok = wait(&mSfree[b], ph))) break;
-                    if (!k && !(ok = wait(&mK[b], ph ^ 1u))) break;
-                    issue_S(i + 2);
+                // S of tile j = i + 2 into the slot P V(j - 3) has read, from its keys
+                const int j = i + 2;
+                if (j < nt) {
+                    const int sj = j % NS;
+                    const uint32_t pj = (uint32_t)(j / NS) & 1u;
+                    const bool f = j < NS || mbar_test_wait(&mSlot[sj], pj ^ 1u), k = mbar_test_wait(&mK[sj], pj);
+                    if (!f && !(ok = wait(&mSlot[sj], pj ^ 1u))) break;
+                    if (!k && !(ok = wait(&mK[sj], pj))) break;
+                    issue_S(j);
                 }
             }
             // every MMA completes before the block lets go of tensor memory
@@ -328,40 +335,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
         }
     } else if (warp == 9) {
         if (lane == 0) {
-            // the load thread: tile i + 2's keys into tile i's slot once S(i) is done, its values once P V(i) is
-            int kl = min(nt, 2), vl = kl;  // key / value loads started
-            for (int i = 0; i + 2 < nt; i++) {
-                const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-                if (!wait(&mKfree[i & 1], ph)) break;
-                load(i + 2, false);
-                kl = i + 3;
-                if (!wait(&mVfree[i & 1], ph)) break;
-                load(i + 2, true);
-                vl = i + 3;
+            // the load thread: tile i + NS's keys into tile i's slot once S(i) is done, its values once P V(i) is
+            int kl = min(nt, NS), vl = kl;  // key / value loads started
+            for (int i = 0; i + NS < nt; i++) {
+                const uint32_t ph = (uint32_t)(i / NS) & 1u;
+                if (!wait(&mKfree[i % NS], ph)) break;
+                load(i + NS, false);
+                kl = i + NS + 1;
+                if (!wait(&mVfree[i % NS], ph)) break;
+                load(i + NS, true);
+                vl = i + NS + 1;
             }
             // the last load into each slot lands before the block lets go of shared memory
-            for (int j = max(0, kl - 2); j < kl; j++) mbar_wait(&mK[j & 1], (uint32_t)(j >> 1) & 1u, TC_WAIT_CYCLES);
-            for (int j = max(0, vl - 2); j < vl; j++) mbar_wait(&mV[j & 1], (uint32_t)(j >> 1) & 1u, TC_WAIT_CYCLES);
+            for (int j = max(0, kl - NS); j < kl; j++) mbar_wait(&mK[j % NS], (uint32_t)(j / NS) & 1u, TC_WAIT_CYCLES);
+            for (int j = max(0, vl - NS); j < vl; j++) mbar_wait(&mV[j % NS], (uint32_t)(j / NS) & 1u, TC_WAIT_CYCLES);
         }
     } else if (part == 0) {
-        // softmax: S(i) -> P(i) = e^(S - m) (scaled by 2^14 so small weights stay normal in f16) and the factor f
+        // softmax: S(i) -> P(i) = e^(S - m) (scaled by 2^14 so small weights stay normal in f16), written over S(i)
+        // in its TMEM slot, and the factor f
         float mrun = -FLT_MAX, lrun = 0.f;
         for (int i = 0; i < nt; i++) {
-            const int b = i & 1;
+            const int sl = i % NS;
             const int len = a.tiles[t0 + i].z;
-            if (!wait_warp(&mS[b], (uint32_t)(i >> 1) & 1u)) break;
+            if (!wait_warp(&mS[sl], (uint32_t)(i / NS) & 1u)) break;
             fence_after_sync();
+            const uint32_t tsp = tmem + lane_base + TM_SP + 64 * sl;
             float s[64];
             {
                 float x[32], y[32];
-                tmem_ld32(tmem + lane_base + TM_S + 64 * b, x);
-                tmem_ld32(tmem + lane_base + TM_S + 64 * b + 32, y);
+                tmem_ld32(tsp, x);
+                tmem_ld32(tsp + 32, y);
                 tmem_wait_ld();
 #pragma unroll
                 for (int k = 0; k < 32; k++) s[k] = x[k], s[32 + k] = y[k];
             }
-            fence_before_sync();
-            mbar_arrive(&mSfree[b]);
             // the scores are s * rs (rs > 0, so the largest raw score gives the largest score)
             float mx = -FLT_MAX;
             if (len == BK) {
@@ -386,20 +393,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
                 psum += s[k];
             }
             psum *= 1.0f / 16384.f;
-            // P(i) replaces P(i - 2) once P V(i - 2) has read it
-            if (i >= 2 && !wait_warp(&mPV[b], (uint32_t)((i - 2) >> 1) & 1u)) break;
-            __half *Phi = Pbuf + (size_t)b * 2 * BQ * BK, *Plo = Phi + BQ * BK;
+            uint32_t hi[32], lo[32];
 #pragma unroll
-            for (int g = 0; g < 8; g++) {
-                float v[8];
-#pragma unroll
-                for (int e = 0; e < 8; e++) v[e] = s[g * 8 + e];
-                put8x2(Phi, Plo, kmajor_off(row, g * 8, BQ), v);
-            }
+            for (int c = 0; c < 32; c++) split_pair(s[2 * c], s[2 * c + 1], hi[c], lo[c]);
+            tmem_st32u(tsp, hi);
+            tmem_st32u(tsp + 32, lo);
+            tmem_wait_st();
             fr[(i & 3) * BQ + row] = f;
-            fence_async_smem();
             fence_before_sync();
-            mbar_arrive(&mP[b]);
+            mbar_arrive(&mP[sl]);
             mbar_arrive(&mF[i & 3]);
             lrun = lrun * f + psum;
             mrun = mnew;
@@ -411,21 +413,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
 #pragma unroll
         for (int e = 0; e < 128; e++) o[e] = 0.f;
         for (int i = 0; i < nt; i++) {
-            const int b = i & 1;
-            if (!wait_warp(&mPV[b], (uint32_t)(i >> 1) & 1u)) break;
+            if (!wait_warp(mPV, (uint32_t)i & 1u)) break;
             if (!wait_warp(&mF[i & 3], (uint32_t)(i >> 2) & 1u)) break;
             fence_after_sync();
             const float f = fr[(i & 3) * BQ + row];
 #pragma unroll
             for (int c = 0; c < 4; c++) {
                 float x[32];
-                tmem_ld32(tmem + lane_base + TM_O + 128 * b + 32 * c, x);
+                tmem_ld32(tmem + lane_base + TM_O + 32 * c, x);
                 tmem_wait_ld();
 #pragma unroll
                 for (int k = 0; k < 32; k++) o[32 * c + k] = fmaf(o[32 * c + k], f, x[k]);
             }
             fence_before_sync();
-            mbar_arrive(&mOfree[b]);
+            mbar_arrive(mOfree);
         }
         // after the last fold no MMA or load touches the key and value rings (on an abort the rows are not used)
 #pragma unroll
@@ -469,7 +470,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
         if (*last) {
             __threadfence();
             const int P = a.splits;
-            float *wts = reinterpret_cast<float *>(Pbuf);  // [P][BQ] part weights, then [BQ] 1 / sums
+            float *wts = reinterpret_cast<float *>(Vring);  // [P][BQ] part weights, then [BQ] 1 / sums
             float *winv = wts + P * BQ;
             if (tid < BQ && r0 + tid < a.R) {
                 const int r = r0 + tid;
@@ -550,8 +551,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
 }
 
 size_t attend_tc_smem() {
-    return sizeof(__half) * (2 * 4 * TC_BLOCK + 4 * TC_BQ * TC_BK) + sizeof(float) * 7 * TC_BQ + 23 * sizeof(uint64_t) +
-           16;  // the TMEM slot, the abort flag and the last-split flag
+    return sizeof(__half) * (2 * TC_SLOTS * 2 * TC_BLOCK) + sizeof(float) * 7 * TC_BQ +
+           (7 * TC_SLOTS + 7) * sizeof(uint64_t) + 16;  // + the TMEM slot, the abort flag and the last-split flag
 }
 
 cudaError_t launch_tc_tiles(int kv, const AttnArgs &a, void *out, cudaStream_t s, uint64_t *launches) {

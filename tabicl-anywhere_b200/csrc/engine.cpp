@@ -783,6 +783,15 @@ static void query_rows(tcu_ctx *ctx, tcu_model *m, int l, const float *scale, co
     // nn.rs:138-149 over all (row, head) pairs at once: q viewed as [R * heads][hd] (a row's heads are contiguous),
     // m = W2 GELU(W0 q_h + b0) + b2 as two linear layers, then q_h *= scale_h (1 + tanh m)
     const int H = sh.heads, hd = d / H, hid = sh.hid;
+    if (hd == 128 && hid == 64 && p.tq0.tiles && p.tq2.tiles && gemm_tc_enabled()) {
+        // the whole MLP and the modulation in one tensor-core kernel
+        QmlpArgs qa;
+        qa.q = q, qa.pairs = R * H, qa.heads = H, qa.hd = hd, qa.hid = hid;
+        qa.w0_tiles = p.tq0.tiles, qa.w2_tiles = p.tq2.tiles, qa.w0_unscale = p.tq0.unscale, qa.w2_unscale = p.tq2.unscale;
+        qa.b0 = p.q0b, qa.b2 = p.q2b, qa.scale = scale, qa.err = ctx->dev_err;
+        Launch{ctx, s}(launch_qmlp_tc(qa, s, &ctx->launches), "query MLP (tensor cores)");
+        return;
+    }
     float *hs = m->ssm.as<float>(), *mm = hs + (size_t)R * H * hid;
     linear(ctx, m, q, hd, R * H, hd, nullptr, nullptr, p.q0w, p.q0b, hid, hs, hid, 1, 0, s, p.tq0);
     linear(ctx, m, hs, hid, R * H, hid, nullptr, nullptr, p.q2w, p.q2b, hd, mm, hd, 0, 0, s, p.tq2);

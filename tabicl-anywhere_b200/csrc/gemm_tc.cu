@@ -35,9 +35,7 @@ struct GemmShape {
     static constexpr uint32_t SLOT = A_BYTES + W_BYTES;
     static constexpr size_t SMEM = (size_t)STAGES * SLOT + 1024;  // + barriers, TMEM slot, flag, row unscales
 };
-// element offset of (row, k) in a 128 x 64 block: 8-row groups outermost, then 8-wide groups of K, then the
-// 8 x 8 core matrix (rows of 16 bytes)
-__host__ __device__ __forceinline__ int blk_off(int r, int k) { return (((r >> 3) * 8 + (k >> 3)) << 6) + ((r & 7) << 3) + (k & 7); }
+
 
 __device__ __forceinline__ float p2(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
 

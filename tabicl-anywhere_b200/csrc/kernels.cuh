@@ -31,6 +31,16 @@ struct LinArgs {
     int *err = nullptr;  // set to 1 when a kernel gave up waiting
 };
 
+// The query MLP of many rows (nn.rs:138-149) in one tensor-core kernel: q [pairs][hd] as (row, head) pairs, in place.
+struct QmlpArgs {
+    float *q = nullptr;
+    int pairs = 0, heads = 0, hd = 0, hid = 0;
+    const void *w0_tiles = nullptr, *w2_tiles = nullptr;  // W0 [hid][hd], W2 [hd][hid] split as for the linear layers
+    const float *w0_unscale = nullptr, *w2_unscale = nullptr, *b0 = nullptr, *b2 = nullptr;
+    const float *scale = nullptr;  // [heads * hd] the layer's fit-time query scale
+    int *err = nullptr;
+};
+
 // Attention of scaled queries against one layer's stored chunks (fit.rs:6-11 layout, read in place).
 struct AttnArgs {
     const uint8_t *layer = nullptr;
@@ -131,6 +141,8 @@ cudaError_t launch_ln_apply(const float *x, int M, int K, const float *w, const 
 cudaError_t launch_ssmax(float *q, int R, int d, int heads, int hid, const float *q0w, const float *q0b,
                          const float *q2w, const float *q2b, const float *scale, cudaStream_t s, uint64_t *launches);
 // q *= scale (1 + tanh(m)) elementwise over [R][d] (scale indexed by coordinate)
+// hd 128 and hid 64 only (cudaErrorInvalidValue otherwise)
+cudaError_t launch_qmlp_tc(const QmlpArgs &a, cudaStream_t s, uint64_t *launches);
 cudaError_t launch_ssmax_apply(float *q, const float *m, const float *scale, int R, int d, cudaStream_t s,
                                uint64_t *launches);
 // keys-parallel split attention for few rows, then the merge into out

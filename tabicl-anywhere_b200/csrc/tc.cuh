@@ -127,6 +127,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
+// 16 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
@@ -184,6 +195,11 @@ __device__ __forceinline__ int kmajor_off(int mn, int k, int MN) { return ((k >>
 // MN-major: 8 consecutive mn stay together for each k; core matrices step 128 B along MN (SBO) and N*16 B along K
 // (LBO).
 __device__ __forceinline__ int mnmajor_off(int mn, int k, int MN) { return ((k >> 3) * (MN >> 3) + (mn >> 3)) * 64 + (k & 7) * 8 + (mn & 7); }
+
+// Element offset of (row, k) in a block of rows x 64 of K: 8-row groups outermost, then 8-wide groups of K, then the
+// 8 x 8 core matrix (rows of 16 bytes). As an MMA operand: core matrices 128 B apart along K (LBO), 8-row groups
+// 1024 B apart (SBO); any 64-row part of a block is contiguous.
+__host__ __device__ __forceinline__ int blk_off(int r, int k) { return (((r >> 3) * 8 + (k >> 3)) << 6) + ((r & 7) << 3) + (k & 7); }
 
 // Descriptor of K-step s (16 values of K) of an operand with MN rows, laid out as above from `base`.
 __device__ __forceinline__ uint64_t kstep_desc(const __half *base, int MN, int s) {
