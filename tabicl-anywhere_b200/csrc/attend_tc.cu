@@ -148,14 +148,16 @@ __device__ __forceinline__ void expect_tx(uint64_t *mbar, uint32_t bytes) {
 //               memory)
 //   [384, 512)  P V^T of the latest tile
 // Roles: warps 0-3 run the online softmax (one thread per query row, the nn.rs:207-215 rule), warps 4-7 fold each
-// tile's P V into O held in registers (O = O f + P V), one thread of warp 8 issues every MMA, one thread of warp 9
-// bulk-copies keys and values into three-slot rings. They hand over through mbarriers only: S(i + 2) runs on the
+// tile's P V into O held in registers (O = O f + P V), one thread of warp 8 issues the S MMAs and one of warp 10 the
+// P V MMAs (two issuers: one thread alone cannot keep the tensor pipe fed), one thread of warp 9 bulk-copies keys
+// and values into three-slot rings. They hand over through mbarriers only: S(i + 2) runs on the
 // tensor cores while the softmax of tile i + 1 runs, and the fold of tile i while S(i + 2) runs. With both A
 // operands in TMEM the MMAs read only K and V from shared memory. Each product is hi*hi + hi*lo + lo*hi with the
 // two cross terms accumulated first, so the tensor cores' f32 accumulation (not round-to-nearest) adds only 8 (S)
 // or 4 (P V) steps of full magnitude; every sum across tiles is taken in registers. Every wait is bounded; a wait
 // that gives up raises the block's abort flag and everyone leaves.
-constexpr int TC_THREADS = 320;  // four softmax warps, four fold warps, an MMA warp and a load warp
+// four softmax warps, four fold warps, the S-issuing warp, the load warp and the P V-issuing warp
+constexpr int TC_THREADS = 352;
 constexpr int TC_SLOTS = 3;      // S/P slots in TMEM, key and value slots in shared memory
 constexpr uint32_t TM_Q = 0, TM_SP = 128, TM_O = 384;
 
@@ -170,8 +172,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
     uint64_t *mb = reinterpret_cast<uint64_t *>(rowx + 3 * BQ);
     uint64_t *mK = mb, *mV = mb + NS, *mKfree = mb + 2 * NS, *mVfree = mb + 3 * NS;
     uint64_t *mS = mb + 4 * NS, *mP = mb + 5 * NS, *mSlot = mb + 6 * NS;  // S done, P written, P V done, per slot
-    uint64_t *mPV = mb + 7 * NS, *mOfree = mPV + 1, *mF = mPV + 2, *mDone = mPV + 6;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(mPV + 7);
+    uint64_t *mPV = mb + 7 * NS, *mOfree = mPV + 1, *mF = mPV + 2, *mDone = mPV + 6;  // mDone[2]: per issuer
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(mPV + 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
     float *qmax = fr;                                  // [2][BQ] query halves' maxima, before the first factor
     float *ostage = reinterpret_cast<float *>(Kring);  // [BQ][HD + 1] after the last fold
@@ -193,7 +195,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
         }
         mbar_init(mPV, 1), mbar_init(mOfree, BQ);
         for (int i = 0; i < 4; i++) mbar_init(&mF[i], BQ);
-        mbar_init(mDone, 1);
+        mbar_init(&mDone[0], 1), mbar_init(&mDone[1], 1);
         mbar_init_fence();
         *abort_flag = 0;
     }
@@ -264,9 +266,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
         return okw;
     };
 
-    if (warp == 8) {
+    if (warp == 8 || warp == 10) {
         if (lane == 0) {
-            // the MMA thread: waits only for what its next MMAs read or overwrite
+            // the two MMA threads: each waits only for what its next MMAs read or overwrite
             const uint32_t idS = idesc_f16(BQ, BK, 0, 0), idO = idesc_f16(BQ, HD, 0, 0);
             const uint64_t dK0 = kstep_desc(Kring, BK, 0), dV0 = kstep_desc(Vring, HD, 0);
             const uint64_t stK = (2 * (BK / 8) * 128) >> 4, stV = (2 * (HD / 8) * 128) >> 4;
@@ -301,26 +303,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
                 mma_commit(&mSlot[sl]);
             };
             bool ok = true;
-            for (int i = 0; i < min(nt, 2) && ok; i++) {
-                ok = wait(&mK[i], 0);
-                if (ok) issue_S(i);
-            }
-            for (int i = 0; i < nt && ok; i++) {
-                const int sl = i % NS;
-                const uint32_t ph = (uint32_t)(i / NS) & 1u;
-                // P V of tile i: its P written, its values here, the fold of P V(i - 1) done (the three tests
-                // issued together; a blocking wait only for one that is not complete yet)
-                {
-                    const bool p = mbar_test_wait(&mP[sl], ph), v = mbar_test_wait(&mV[sl], ph);
-                    const bool o = i < 1 || mbar_test_wait(mOfree, (uint32_t)(i - 1) & 1u);
-                    if (!p && !(ok = wait(&mP[sl], ph))) break;
-                    if (!v && !(ok = wait(&mV[sl], ph))) break;
-                    if (!o && !(ok = wait(mOfree, (uint32_t)(i - 1) & 1u))) break;
-                }
-                issue_PV(i);
-                // S of tile j = i + 2 into the slot P V(j - 3) has read, from its keys
-                const int j = i + 2;
-                if (j < nt) {
+            if (warp == 8) {
+                // S(j) into slot j % NS once P V(j - NS) has read that slot, from its keys
+                for (int j = 0; j < nt && ok; j++) {
                     const int sj = j % NS;
                     const uint32_t pj = (uint32_t)(j / NS) & 1u;
                     const bool f = j < NS || mbar_test_wait(&mSlot[sj], pj ^ 1u), k = mbar_test_wait(&mK[sj], pj);
@@ -328,10 +313,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
                     if (!k && !(ok = wait(&mK[sj], pj))) break;
                     issue_S(j);
                 }
+            } else {
+                // P V of tile i: its P written, its values here, the fold of P V(i - 1) done (the three tests issued
+                // together; a blocking wait only for one that is not complete yet)
+                for (int i = 0; i < nt && ok; i++) {
+                    const int sl = i % NS;
+                    const uint32_t ph = (uint32_t)(i / NS) & 1u;
+                    const bool p = mbar_test_wait(&mP[sl], ph), v = mbar_test_wait(&mV[sl], ph);
+                    const bool o = i < 1 || mbar_test_wait(mOfree, (uint32_t)(i - 1) & 1u);
+                    if (!p && !(ok = wait(&mP[sl], ph))) break;
+                    if (!v && !(ok = wait(&mV[sl], ph))) break;
+                    if (!o && !(ok = wait(mOfree, (uint32_t)(i - 1) & 1u))) break;
+                    issue_PV(i);
+                }
             }
-            // every MMA completes before the block lets go of tensor memory
-            mma_commit(mDone);
-            mbar_wait(mDone, 0, TC_WAIT_CYCLES);
+            // every MMA this thread issued completes before the block lets go of tensor memory
+            uint64_t *done = &mDone[warp == 8 ? 0 : 1];
+            mma_commit(done);
+            mbar_wait(done, 0, TC_WAIT_CYCLES);
         }
     } else if (warp == 9) {
         if (lane == 0) {
@@ -552,7 +551,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
 
 size_t attend_tc_smem() {
     return sizeof(__half) * (2 * TC_SLOTS * 2 * TC_BLOCK) + sizeof(float) * 7 * TC_BQ +
-           (7 * TC_SLOTS + 7) * sizeof(uint64_t) + 16;  // + the TMEM slot, the abort flag and the last-split flag
+           (7 * TC_SLOTS + 8) * sizeof(uint64_t) + 16;  // + the TMEM slot, the abort flag and the last-split flag
 }
 
 cudaError_t launch_tc_tiles(int kv, const AttnArgs &a, void *out, cudaStream_t s, uint64_t *launches) {
