@@ -148,16 +148,17 @@ __device__ __forceinline__ void expect_tx(uint64_t *mbar, uint32_t bytes) {
 //               memory)
 //   [384, 512)  P V^T of the latest tile
 // Roles: warps 0-3 run the online softmax (one thread per query row, the nn.rs:207-215 rule), warps 4-7 fold each
-// tile's P V into O held in registers (O = O f + P V), one thread of warp 8 issues the S MMAs and one of warp 10 the
-// P V MMAs (two issuers: one thread alone cannot keep the tensor pipe fed), one thread of warp 9 bulk-copies keys
-// and values into three-slot rings. They hand over through mbarriers only: S(i + 2) runs on the
+// tile's P V into O held in registers (O = O f + P V), one thread each of warps 8 and 11 issues the S MMAs of even
+// and odd tiles and one of warp 10 the P V MMAs (one thread alone cannot keep the tensor pipe fed), one thread of
+// warp 9 bulk-copies keys and values into three-slot rings. They hand over through mbarriers only: S(i + 2) runs on the
 // tensor cores while the softmax of tile i + 1 runs, and the fold of tile i while S(i + 2) runs. With both A
 // operands in TMEM the MMAs read only K and V from shared memory. Each product is hi*hi + hi*lo + lo*hi with the
 // two cross terms accumulated first, so the tensor cores' f32 accumulation (not round-to-nearest) adds only 8 (S)
 // or 4 (P V) steps of full magnitude; every sum across tiles is taken in registers. Every wait is bounded; a wait
 // that gives up raises the block's abort flag and everyone leaves.
-// four softmax warps, four fold warps, the S-issuing warp, the load warp and the P V-issuing warp
-constexpr int TC_THREADS = 352;
+// four softmax warps, four fold warps, two S-issuing warps (even and odd tiles), the load warp and the P V-issuing
+// warp
+constexpr int TC_THREADS = 384;
 constexpr int TC_SLOTS = 3;      // S/P slots in TMEM, key and value slots in shared memory
 constexpr uint32_t TM_Q = 0, TM_SP = 128, TM_O = 384;
 
@@ -172,8 +173,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
     uint64_t *mb = reinterpret_cast<uint64_t *>(rowx + 3 * BQ);
     uint64_t *mK = mb, *mV = mb + NS, *mKfree = mb + 2 * NS, *mVfree = mb + 3 * NS;
     uint64_t *mS = mb + 4 * NS, *mP = mb + 5 * NS, *mSlot = mb + 6 * NS;  // S done, P written, P V done, per slot
-    uint64_t *mPV = mb + 7 * NS, *mOfree = mPV + 1, *mF = mPV + 2, *mDone = mPV + 6;  // mDone[2]: per issuer
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(mPV + 8);
+    uint64_t *mPV = mb + 7 * NS, *mOfree = mPV + 1, *mF = mPV + 2, *mDone = mPV + 6;  // mDone[3]: per issuer
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(mPV + 9);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tslot + 1);
     float *qmax = fr;                                  // [2][BQ] query halves' maxima, before the first factor
     float *ostage = reinterpret_cast<float *>(Kring);  // [BQ][HD + 1] after the last fold
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
         }
         mbar_init(mPV, 1), mbar_init(mOfree, BQ);
         for (int i = 0; i < 4; i++) mbar_init(&mF[i], BQ);
-        mbar_init(&mDone[0], 1), mbar_init(&mDone[1], 1);
+        mbar_init(&mDone[0], 1), mbar_init(&mDone[1], 1), mbar_init(&mDone[2], 1);
         mbar_init_fence();
         *abort_flag = 0;
     }
@@ -266,9 +267,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
         return okw;
     };
 
-    if (warp == 8 || warp == 10) {
+    if (warp == 8 || warp == 10 || warp == 11) {
         if (lane == 0) {
-            // the two MMA threads: each waits only for what its next MMAs read or overwrite
+            // the three MMA threads: each waits only for what its next MMAs read or overwrite
             const uint32_t idS = idesc_f16(BQ, BK, 0, 0), idO = idesc_f16(BQ, HD, 0, 0);
             const uint64_t dK0 = kstep_desc(Kring, BK, 0), dV0 = kstep_desc(Vring, HD, 0);
             const uint64_t stK = (2 * (BK / 8) * 128) >> 4, stV = (2 * (HD / 8) * 128) >> 4;
@@ -303,9 +304,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
                 mma_commit(&mSlot[sl]);
             };
             bool ok = true;
-            if (warp == 8) {
-                // S(j) into slot j % NS once P V(j - NS) has read that slot, from its keys
-                for (int j = 0; j < nt && ok; j++) {
+            if (warp != 10) {
+                // S(j) into slot j % NS once P V(j - NS) has read that slot, from its keys; even j by warp 8, odd j
+                // by warp 11
+                for (int j = warp == 8 ? 0 : 1; j < nt && ok; j += 2) {
                     const int sj = j % NS;
                     const uint32_t pj = (uint32_t)(j / NS) & 1u;
                     const bool f = j < NS || mbar_test_wait(&mSlot[sj], pj ^ 1u), k = mbar_test_wait(&mK[sj], pj);
@@ -328,7 +330,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
                 }
             }
             // every MMA this thread issued completes before the block lets go of tensor memory
-            uint64_t *done = &mDone[warp == 8 ? 0 : 1];
+            uint64_t *done = &mDone[warp == 8 ? 0 : warp == 10 ? 1 : 2];
             mma_commit(done);
             mbar_wait(done, 0, TC_WAIT_CYCLES);
         }
@@ -551,7 +553,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
 
 size_t attend_tc_smem() {
     return sizeof(__half) * (2 * TC_SLOTS * 2 * TC_BLOCK) + sizeof(float) * 7 * TC_BQ +
-           (7 * TC_SLOTS + 8) * sizeof(uint64_t) + 16;  // + the TMEM slot, the abort flag and the last-split flag
+           (7 * TC_SLOTS + 9) * sizeof(uint64_t) + 16;  // + the TMEM slot, the abort flag and the last-split flag
 }
 
 cudaError_t launch_tc_tiles(int kv, const AttnArgs &a, void *out, cudaStream_t s, uint64_t *launches) {
