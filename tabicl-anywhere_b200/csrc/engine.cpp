@@ -145,7 +145,6 @@ struct tcu_model {
         bool done = false;
         int grid = 0, slots = 0;
         size_t smem = 0;
-        int part_lo[ROWS_MAX_HEADS] = {}, part_hi[ROWS_MAX_HEADS] = {};
     } rows_plans[2];  // one row, 2..8 rows
     // the stage captured as CUDA graphs, one per (rows, outputs, profiling), over the buffers above
     struct Graph {
@@ -912,8 +911,8 @@ static void rows_build(tcu_model *m) {
     m->rows_built = true;
 }
 
-// Whether R rows take the one-kernel stage, and its launch shape: one CTA per SM (at most one per key tile), as
-// many tiles of shared memory as fit.
+// Whether R rows take the one-kernel stage, and its launch shape: one CTA per SM, the same number for every head
+// (at most one per key tile of a head), as many tiles of shared memory as fit.
 static const tcu_model::RowsPlan *rows_plan(tcu_ctx *ctx, tcu_model *m, int R) {
     const auto &sh = m->w->shape;
     const int hd = sh.d / sh.heads;
@@ -925,26 +924,14 @@ static const tcu_model::RowsPlan *rows_plan(tcu_ctx *ctx, tcu_model *m, int R) {
     if (!p.done) {
         p.done = true;
         rows_build(m);
-        const int want = std::min({ctx->sms, m->rtiles_n, ROWS_MAX_GRID});
-        for (int slots = rows_slots_for(m->kv, hd, R, ctx->smem_optin); slots >= 2; slots--) {
+        // one head per CTA: the grid is a multiple of the heads, with at least one tile per CTA
+        const int per = std::min(std::min(ctx->sms, ROWS_MAX_GRID) / sh.heads, m->rtiles_per_head);
+        const int want = per * sh.heads;
+        for (int slots = rows_slots_for(m->kv, hd, R, ctx->smem_optin); want > 0 && slots >= 2; slots--) {
             const size_t smem = rows_smem(m->kv, hd, R, slots);
             if (rows_max_grid(m->kv, hd, R, smem, ctx->sms) >= want) {
                 p.grid = want, p.slots = slots, p.smem = smem;
                 break;
-            }
-        }
-        if (p.grid) {
-            // the CTAs holding each head's tiles: CTA c holds tiles [T c / G, T (c + 1) / G)
-            const long long T = m->rtiles_n, G = p.grid;
-            for (int h = 0; h < sh.heads; h++) {
-                const long long first = (long long)h * m->rtiles_per_head, last = first + m->rtiles_per_head - 1;
-                int lo = -1, hi = -1;
-                for (int c = 0; c < p.grid; c++) {
-                    const long long t0 = T * c / G, t1 = T * (c + 1) / G;
-                    if (t0 <= first && first < t1) lo = c;
-                    if (t0 <= last && last < t1) hi = c;
-                }
-                p.part_lo[h] = lo, p.part_hi[h] = hi;
             }
         }
     }
@@ -956,8 +943,8 @@ static void stage_rows(tcu_ctx *ctx, tcu_model *m, const tcu_model::RowsPlan &p,
     const auto &sh = m->w->shape;
     const int hd = sh.d / sh.heads;
     ensure_work(m, R);
-    m->rparts_ms.ensure(sizeof(float) * (size_t)p.grid * sh.heads * 8 * 2);
-    m->rparts_acc.ensure(sizeof(float) * (size_t)p.grid * sh.heads * 8 * hd);
+    m->rparts_ms.ensure(sizeof(float) * (size_t)p.grid * 8 * 2);
+    m->rparts_acc.ensure(sizeof(float) * (size_t)p.grid * 8 * hd);
     RowsArgs a;
     a.layers = m->rlayers.as<RowsLayer>();
     a.L = sh.layers, a.d = sh.d, a.heads = sh.heads, a.ff = sh.ff, a.dff = sh.dec_ff, a.out_n = out_n, a.R = R;
@@ -969,8 +956,7 @@ static void stage_rows(tcu_ctx *ctx, tcu_model *m, const tcu_model::RowsPlan &p,
     a.h = m->h.as<float>(), a.q = m->q.as<float>(), a.att = m->att.as<float>(), a.mid = m->mid.as<float>();
     a.out = m->out.as<float>();
     a.part_ms = m->rparts_ms.as<float>(), a.part_acc = m->rparts_acc.as<float>();
-    a.bar = m->rsync.as<unsigned>(), a.head_cnt = m->rsync.as<int>() + 32, a.err = ctx->dev_err;
-    for (int h = 0; h < sh.heads; h++) a.part_lo[h] = p.part_lo[h], a.part_hi[h] = p.part_hi[h];
+    a.bar = m->rsync.as<unsigned>(), a.err = ctx->dev_err;
     // a launch that gave up leaves the barrier word dirty: every launch starts from zeros
     CU(cudaMemsetAsync(m->rsync.p, 0, 256, s));
     cudaEvent_t ev_end = nullptr;

@@ -90,11 +90,11 @@ struct RowsArgs {
     const void *tmaps = nullptr;
     int nfull = 0;                      // full chunks per layer
     float *h = nullptr, *q = nullptr, *att = nullptr, *mid = nullptr, *out = nullptr;
-    float *part_ms = nullptr, *part_acc = nullptr;  // [grid][heads][R] (max, weight sum) and [..][head width]
+    // per CTA (each holds tiles of one head: CTA c of grid G takes head c / (G / heads)): [grid][R] (max, weight
+    // sum) and [grid][R][head width]
+    float *part_ms = nullptr, *part_acc = nullptr;
     unsigned *bar = nullptr;            // grid barrier word (zero low bits between launches)
-    int *head_cnt = nullptr;            // [heads] arrivals of the CTAs holding each head's tiles
     int *err = nullptr;                 // set to 1 when a wait gave up
-    int part_lo[ROWS_MAX_HEADS] = {}, part_hi[ROWS_MAX_HEADS] = {};  // CTAs holding each head's tiles
 };
 
 // Keys per tile of the one-kernel stage for a stored format (f32 32, i16 64, i8 64).

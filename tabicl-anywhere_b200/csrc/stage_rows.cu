@@ -2,9 +2,9 @@
 // all resident (cooperative launch), the phases of each layer separated by grid barriers.
 //
 //   A  q = Wq LN1(h) + bq                   (nn.rs:130-137; outputs spread over the CTAs)
-//   B  per head: the query MLP of the scalable softmax (nn.rs:138-149), then attention over this CTA's share
-//      of the key tiles with the online softmax (nn.rs:187-258); the last CTA of a head merges the head's
-//      partial states (nn.rs:261-286) into att
+//   B  the query MLP of the scalable softmax (nn.rs:138-149) for this CTA's head, then attention over its share
+//      of the head's key tiles with the online softmax (nn.rs:187-258), leaving one partial state per CTA
+//   C  att = the log-sum-exp merge of each head's partial states (nn.rs:261-286), outputs spread over the CTAs
 //   D  h += Wo att + bo                     (predict.rs:542-551)
 //   E  mid = GELU(W1 LN2(h) + b1)           (predict.rs:552-559)
 //   F  h += W2 mid + b2                     (predict.rs:560-568)
@@ -51,8 +51,8 @@ struct Cfg {
     static constexpr int BT = BMAX * TK;
     // scratch (floats), shared by the linear phases and the attention phase
     static constexpr int QH = 0, QM = QH + RM * HD, RED = QM + RM * HD, PSM = RED + WARPS * RM * BT,
-                         HS = PSM + RM * BT, ALPHA = HS + RM * HID, SINV = ALPHA + 8, LENS = SINV + 8,
-                         BMS = LENS + 8, WTS = BMS + 16, ATT_END = WTS + RM * ROWS_MAX_GRID;
+                         HS = PSM + RM * BT, ALPHA = HS + RM * HID, LENS = ALPHA + 8, BMS = LENS + 8,
+                         ATT_END = BMS + 16;
     static constexpr int XS = 0, LNW = RM * KMAX, LNB = LNW + KMAX, LIN_END = LNB + KMAX;
     static constexpr int SCRATCH = ATT_END > LIN_END ? ATT_END : LIN_END;
     static_assert(WARPS * TK >= 4 * HID && WARPS * TK >= 256, "reduction scratch too small for the query MLP");
@@ -169,6 +169,7 @@ struct Stage {
     uint64_t *mbar;
     float *scr;
     int *flag_s;
+    int head;             // the head whose tiles this CTA holds
     int t0, n, total;     // this CTA's tiles [t0, t0 + n) of every layer; total = L n tiles in its sequence
     int consumed = 0;     // next tile of the sequence to use
     int issued = 0;       // tiles of the sequence whose copies have started (at most consumed + slots)
@@ -183,9 +184,11 @@ struct Stage {
         ring = smem;
         mbar = reinterpret_cast<uint64_t *>(smem + (size_t)a.slots * C::SLOT);
         scr = reinterpret_cast<float *>(smem + (size_t)a.slots * C::SLOT + 128);
-        const int G = gridDim.x, c = blockIdx.x;
-        t0 = (int)((long long)a.ntiles * c / G);
-        n = (int)((long long)a.ntiles * (c + 1) / G) - t0;
+        // G / heads CTAs per head; CTA c takes an equal share of head c / (G / heads)'s tiles (head-major list)
+        const int per = gridDim.x / a.heads, i = blockIdx.x % per, Th = a.tiles_per_head;
+        head = blockIdx.x / per;
+        t0 = head * Th + (int)((long long)Th * i / per);
+        n = head * Th + (int)((long long)Th * (i + 1) / per) - t0;
         total = a.L * n;
         pol_kv = policy_evict_first();
         pol_w = policy_evict_last();
@@ -474,97 +477,82 @@ struct Stage {
         __syncthreads();
     }
 
-    // The last CTA to finish head h: log-sum-exp merge of the head's partial states into att (nn.rs:261-286). The
-    // partial sums are loaded first (all in flight at once), the part weights computed meanwhile.
-    __device__ void merge(int h) {
-        float *wts = scr + C::WTS, *sinv = scr + C::SINV, *half = scr + C::RED;
-        const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, R = a.R, H = a.heads;
-        const int lo = a.part_lo[h], np = a.part_hi[h] - lo + 1;
-        const size_t step = (size_t)H * R * HD;  // between the parts of consecutive CTAs
-        const int outs = R * HD, groups = outs <= THREADS / 2 ? THREADS / outs : 1;
-        constexpr int MP = 24;
-        // thread: output (r, j) and a group of the parts (p = gi + groups k)
-        const int oi = tid % outs, gi = tid / outs;
-        const bool fast = groups > 1 && gi < groups;
-        float v[MP];
-        if (fast) {
-            const float *pa = a.part_acc + ((size_t)lo * H + h) * R * HD + oi;
-#pragma unroll
-            for (int k = 0; k < MP; k++) {
-                const int p = gi + groups * k;
-                v[k] = p < np ? __ldcg(pa + p * step) : 0.f;
-            }
-        }
-        if (warp < R) {
-            const int r = warp;
+    // Phase C: the log-sum-exp merge of the partial states (nn.rs:261-286) into att, spread over the CTAs: CTA c takes
+    // the outputs (row, coordinate) [R d c / G, R d (c + 1) / G). TPO threads share an output, each with every
+    // TPO-th part of the output's head (the first MPT of them loaded all at once, any further ones after); M is the
+    // largest part maximum and att = sum_p e^(m_p - M) acc_p / sum_p e^(m_p - M) s_p. A part of no keys
+    // (m -FLT_MAX, s 0, acc 0) adds zero.
+    __device__ bool merge_parts() {
+        constexpr int TPO = 8, OPP = THREADS / TPO, MPT = 6;
+        if (!wait()) return false;  // every partial state is written
+        const int tid = threadIdx.x, sub = tid % TPO, G = gridDim.x, R = a.R, d = a.d, per = G / a.heads;
+        const int nout = R * d, o0 = (int)((long long)nout * blockIdx.x / G),
+                  o1 = (int)((long long)nout * (blockIdx.x + 1) / G);
+        for (int ob = o0; ob < o1; ob += OPP) {
+            const int o = ob + tid / TPO;
+            const bool live = o < o1;
+            const int r = live ? o / d : 0, coord = live ? o - r * d : 0, h = coord / HD, j = coord - h * HD;
+            const int p0 = h * per;
+            float mv[MPT], sv[MPT], av[MPT];
             float M = -FLT_MAX;
-            for (int i = lane; i < np; i += 32) M = fmaxf(M, __ldcg(a.part_ms + (((size_t)(lo + i) * H + h) * R + r) * 2));
-            M = warp_max(M);
-            float S = 0.f;
-            for (int i = lane; i < np; i += 32) {
-                const float *ms = a.part_ms + (((size_t)(lo + i) * H + h) * R + r) * 2;
-                const float w = exp1(__ldcg(ms) - M);
-                wts[r * ROWS_MAX_GRID + i] = w;
-                S = fmaf(__ldcg(ms + 1), w, S);
-            }
-            S = warp_sum(S);
-            if (lane == 0) sinv[r] = 1.0f / S;
-        }
-        __syncthreads();
-        if (groups > 1) {
-            if (fast) {
-                const int r = oi / HD;
-                const float *pa = a.part_acc + ((size_t)lo * H + h) * R * HD + oi;
-                float o = 0.f;
 #pragma unroll
-                for (int k = 0; k < MP; k++) {
-                    const int p = gi + groups * k;
-                    if (p < np) o = fmaf(wts[r * ROWS_MAX_GRID + p], v[k], o);
+            for (int k = 0; k < MPT; k++) {
+                const int p = sub + TPO * k;
+                mv[k] = -FLT_MAX, sv[k] = 0.f, av[k] = 0.f;
+                if (live && p < per) {
+                    const float *ms = a.part_ms + ((size_t)(p0 + p) * R + r) * 2;
+                    mv[k] = __ldcg(ms), sv[k] = __ldcg(ms + 1);
+                    av[k] = __ldcg(a.part_acc + ((size_t)(p0 + p) * R + r) * HD + j);
                 }
-                for (int p = gi + groups * MP; p < np; p += groups) o = fmaf(wts[r * ROWS_MAX_GRID + p], __ldcg(pa + p * step), o);
-                half[gi * outs + oi] = o;
             }
-            __syncthreads();
-            for (int i = tid; i < outs; i += THREADS) {
-                float o = 0.f;
-                for (int g = 0; g < groups; g++) o += half[g * outs + i];
-                const int r = i / HD, j = i - r * HD;
-                a.att[(size_t)r * a.d + h * HD + j] = o * sinv[r];
+#pragma unroll
+            for (int k = 0; k < MPT; k++) M = fmaxf(M, mv[k]);
+            const float *ms_r = a.part_ms + (size_t)r * 2;
+            const float *acc_r = a.part_acc + (size_t)r * HD + j;
+            for (int p = sub + TPO * MPT; live && p < per; p += TPO) M = fmaxf(M, __ldcg(ms_r + (size_t)(p0 + p) * R * 2));
+#pragma unroll
+            for (int m = 1; m < TPO; m <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, m));
+            float S = 0.f, O = 0.f;
+#pragma unroll
+            for (int k = 0; k < MPT; k++) {
+                if (sub + TPO * k < per) {
+                    const float w = exp1(mv[k] - M);
+                    S = fmaf(sv[k], w, S);
+                    O = fmaf(av[k], w, O);
+                }
             }
-        } else {
-            for (int i = tid; i < outs; i += THREADS) {
-                const int r = i / HD, j = i - r * HD;
-                const float *pa = a.part_acc + (((size_t)lo * H + h) * R + r) * HD + j;
-                float o = 0.f;
-#pragma unroll 8
-                for (int p = 0; p < np; p++) o = fmaf(wts[r * ROWS_MAX_GRID + p], __ldcg(pa + p * step), o);
-                a.att[(size_t)r * a.d + h * HD + j] = o * sinv[r];
+            for (int p = sub + TPO * MPT; live && p < per; p += TPO) {
+                const float w = exp1(__ldcg(ms_r + (size_t)(p0 + p) * R * 2) - M);
+                S = fmaf(__ldcg(ms_r + (size_t)(p0 + p) * R * 2 + 1), w, S);
+                O = fmaf(__ldcg(acc_r + (size_t)(p0 + p) * R * HD), w, O);
             }
+#pragma unroll
+            for (int m = 1; m < TPO; m <<= 1) {
+                S += __shfl_xor_sync(0xffffffffu, S, m);
+                O += __shfl_xor_sync(0xffffffffu, O, m);
+            }
+            if (live && sub == 0) a.att[(size_t)r * d + coord] = O * (1.0f / S);
         }
-        __syncthreads();
+        arrive();
+        return true;
     }
 
-    // Phase B of layer l.
+    // Phase B of layer l: the query MLP of this CTA's head, attention over its tiles, its partial state.
     __device__ bool attend(int l) {
         const RowsLayer &Ly = lay[l];
-        const int Th = a.tiles_per_head;
         {
-            // the first head's query MLP weights load while the barrier completes
+            // the query MLP weights load while the barrier completes
             QueryW qw;
-            query_load(Ly, t0 / Th, qw);
+            query_load(Ly, head, qw);
             if (!wait()) return false;  // q is ready
-            query_head(t0 / Th, qw);
+            query_head(head, qw);
         }
         float *qm = scr + C::QM, *red = scr + C::RED, *psm = scr + C::PSM, *alpha = scr + C::ALPHA;
         int *lens = reinterpret_cast<int *>(scr + C::LENS);
         const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, v = tid & 7, jg = tid >> 3, R = a.R;
-        for (int t = t0; t < t0 + n;) {
-            const int h = t / Th, te = min(t0 + n, (h + 1) * Th);
-            if (t != t0) {
-                QueryW qw;
-                query_load(Ly, h, qw);
-                query_head(h, qw);
-            }
+        {
+            const int te = t0 + n;
+            int t = t0;
             float m_run = -FLT_MAX, s_run = 0.f;  // row `warp`'s running state, in every lane of that warp
             float acc[C::DPT];                    // row v (RM 8) or row 0 (lanes v = 0), coordinates jg + 32 i
 #pragma unroll
@@ -760,8 +748,8 @@ struct Stage {
                 t += nb;
                 issue_upto((l + 1) * n);  // this layer's later tiles now; the next layer's after the barrier arrival
             }
-            // this CTA's partial state of head h, then the head's arrival count
-            const int pi = blockIdx.x * a.heads + h;
+            // this CTA's partial state
+            const int pi = blockIdx.x;
             if (warp < R && lane == 0) {
                 float *ms = a.part_ms + ((size_t)pi * R + warp) * 2;
                 ms[0] = m_run, ms[1] = s_run;
@@ -772,17 +760,6 @@ struct Stage {
 #pragma unroll
                     for (int i = 0; i < C::DPT; i++) a.part_acc[((size_t)pi * R + r) * HD + jg + 32 * i] = acc[i];
                 }
-            }
-            __syncthreads();
-            if (tid == 0) {
-                __threadfence();
-                const int old = atomicAdd(a.head_cnt + h, 1);
-                *flag_s = old == a.part_hi[h] - a.part_lo[h];
-            }
-            __syncthreads();
-            if (*flag_s) {
-                __threadfence();
-                merge(h);
             }
         }
         arrive();
@@ -815,9 +792,9 @@ __global__ void __launch_bounds__(THREADS, 1) k_stage_rows(const RowsArgs a) {
     bool ok = true;
     for (int l = 0; l < a.L && ok; l++) {
         const RowsLayer &Ly = lay[l];
-        if (blockIdx.x == 0 && tid < a.heads) a.head_cnt[tid] = 0;  // used after the next barrier
         ok = st.template linear<true>(l > 0, a.h, d, Ly.n1w, Ly.n1b, Ly.wq, Ly.bq, d, 0, a.q, d, false);
         ok = ok && st.attend(l);
+        ok = ok && st.merge_parts();
         ok = ok && st.template linear<false>(true, a.att, d, nullptr, nullptr, Ly.wo, Ly.bo, d, 0, a.h, d, true);
         ok = ok && st.template linear<true>(true, a.h, d, Ly.n2w, Ly.n2b, Ly.w1, Ly.b1, a.ff, 1, a.mid, a.ff, false);
         ok = ok && st.template linear<false>(true, a.mid, a.ff, nullptr, nullptr, Ly.w2, Ly.b2, d, 0, a.h, d, true);
