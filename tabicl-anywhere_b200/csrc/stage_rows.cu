@@ -53,7 +53,7 @@ struct Cfg {
     static constexpr int QH = 0, QM = QH + RM * HD, RED = QM + RM * HD, PSM = RED + WARPS * RM * BT,
                          HS = PSM + RM * BT, ALPHA = HS + RM * HID, LENS = ALPHA + 8, BMS = LENS + 8,
                          ATT_END = BMS + 16;
-    static constexpr int XS = 0, LNW = RM * KMAX, LNB = LNW + KMAX, LIN_END = LNB + KMAX;
+    static constexpr int XS = 0, LNW = RM * KMAX, LNB = LNW + KMAX, LRED = LNB + KMAX, LIN_END = LRED + 2 * WARPS;
     static constexpr int SCRATCH = ATT_END > LIN_END ? ATT_END : LIN_END;
     static_assert(WARPS * TK >= 4 * HID && WARPS * TK >= 256, "reduction scratch too small for the query MLP");
 };
@@ -232,15 +232,16 @@ struct Stage {
         }
     }
 
-    // All threads: wait for sequence tiles [g0, g0 + nb), the next ones to use; then copy those that could not be
-    // copied asynchronously.
+    // All threads: wait for sequence tiles [g0, g0 + nb), the next ones to use (thread 0 waits on the slots'
+    // mbarriers, the CTA barrier below passes the completed copies on to the other threads); then copy those that
+    // could not be copied asynchronously.
     __device__ bool acquire(int g0, int nb) {
         bool ok = true;
         for (int b = 0; b < nb; b++) {
             const int g = g0 + b, s = g % a.slots;
             const int4 tl = tile_of(g);
             if (tl.w >> 16) {
-                ok = tc::mbar_wait(mbar + s, (phase >> s) & 1u, SPIN_LIMIT) && ok;
+                if (threadIdx.x == 0) ok = tc::mbar_wait(mbar + s, (phase >> s) & 1u, SPIN_LIMIT) && ok;
                 phase ^= 1u << s;
             } else {
                 copy_now(g, tl);
@@ -296,9 +297,8 @@ struct Stage {
     // linear kernel does, so both give the same sums. The first output's weights, its bias and the LayerNorm weights
     // are loaded before the barrier (when `wait`) that makes x ready; x (rows written by other CTAs in this launch)
     // is read through L2.
-    template <bool LN>
-    __device__ bool linear(bool wait_first, const float *x, int K, const float *lnw, const float *lnb, const float *W,
-                           const float *b, int N, int act, float *y, int ldy, bool residual) {
+    __device__ bool linear(bool LN, bool wait_first, const float *x, int K, const float *lnw, const float *lnb,
+                           const float *W, const float *b, int N, int act, float *y, int ldy, bool residual) {
         float *xs = scr + C::XS, *lw_s = scr + C::LNW, *lb_s = scr + C::LNB;
         const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, R = a.R;
         const int n0 = (int)((long long)N * blockIdx.x / gridDim.x), n1 = (int)((long long)N * (blockIdx.x + 1) / gridDim.x);
@@ -331,7 +331,29 @@ struct Stage {
                 if (tid + i * THREADS < K) lw_s[tid + i * THREADS] = lw[i], lb_s[tid + i * THREADS] = lb[i];
         }
         __syncthreads();
-        if (LN) {
+        if (LN && RM == 1) {
+            // kern.rs:357-376 for the one row, by all warps: mean, then the mean square deviation, then the scaling
+            float *lred = scr + C::LRED;
+            float sum = 0.f;
+            for (int k = tid; k < K; k += THREADS) sum += xs[k];
+            sum = warp_sum(sum);
+            if (lane == 0) lred[warp] = sum;
+            __syncthreads();
+            const float mean = (((lred[0] + lred[1]) + (lred[2] + lred[3])) + ((lred[4] + lred[5]) + (lred[6] + lred[7]))) / (float)K;
+            float q = 0.f;
+            for (int k = tid; k < K; k += THREADS) {
+                const float dd = xs[k] - mean;
+                q = fmaf(dd, dd, q);
+            }
+            q = warp_sum(q);
+            if (lane == 0) lred[WARPS + warp] = q;
+            __syncthreads();
+            const float *lq = lred + WARPS;
+            const float var = (((lq[0] + lq[1]) + (lq[2] + lq[3])) + ((lq[4] + lq[5]) + (lq[6] + lq[7]))) / (float)K;
+            const float inv = 1.0f / sqrtf(var + 1e-5f);
+            for (int k = tid; k < K; k += THREADS) xs[k] = (xs[k] - mean) * inv * lw_s[k] + lb_s[k];
+            __syncthreads();
+        } else if (LN) {
             // kern.rs:357-376, as the few-row linear kernel computes it
             for (int r = warp; r < R; r += WARPS) {
                 float *row = xs + r * K;
@@ -537,16 +559,11 @@ struct Stage {
         return true;
     }
 
-    // Phase B of layer l: the query MLP of this CTA's head, attention over its tiles, its partial state.
-    __device__ bool attend(int l) {
-        const RowsLayer &Ly = lay[l];
-        {
-            // the query MLP weights load while the barrier completes
-            QueryW qw;
-            query_load(Ly, head, qw);
-            if (!wait()) return false;  // q is ready
-            query_head(head, qw);
-        }
+    // Phase B of layer l: the query MLP of this CTA's head (its weights qw loaded before phase A), attention over its
+    // tiles, its partial state.
+    __device__ bool attend(int l, const QueryW &qw) {
+        if (!wait()) return false;  // q is ready
+        query_head(head, qw);
         float *qm = scr + C::QM, *red = scr + C::RED, *psm = scr + C::PSM, *alpha = scr + C::ALPHA;
         int *lens = reinterpret_cast<int *>(scr + C::LENS);
         const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, v = tid & 7, jg = tid >> 3, R = a.R;
@@ -789,19 +806,34 @@ __global__ void __launch_bounds__(THREADS, 1) k_stage_rows(const RowsArgs a) {
     }
     __syncthreads();
     st.issue_upto(st.total);
+    // Every linear phase (A, D, E, F of each layer, then the decoder's two layers) runs the one inlined linear body
+    // from this loop, so the loop's code stays small.
     bool ok = true;
-    for (int l = 0; l < a.L && ok; l++) {
-        const RowsLayer &Ly = lay[l];
-        ok = st.template linear<true>(l > 0, a.h, d, Ly.n1w, Ly.n1b, Ly.wq, Ly.bq, d, 0, a.q, d, false);
-        ok = ok && st.attend(l);
-        ok = ok && st.merge_parts();
-        ok = ok && st.template linear<false>(true, a.att, d, nullptr, nullptr, Ly.wo, Ly.bo, d, 0, a.h, d, true);
-        ok = ok && st.template linear<true>(true, a.h, d, Ly.n2w, Ly.n2b, Ly.w1, Ly.b1, a.ff, 1, a.mid, a.ff, false);
-        ok = ok && st.template linear<false>(true, a.mid, a.ff, nullptr, nullptr, Ly.w2, Ly.b2, d, 0, a.h, d, true);
+    typename Stage<KV, HD, RM>::QueryW qw;
+    const int L = a.L;
+    for (int step = 0; step < 4 * L + 2 && ok; step++) {
+        const int l = step >> 2, ph = step & 3;
+        if (step < 4 * L) {
+            const RowsLayer &Ly = lay[l];
+            if (ph == 0) st.query_load(Ly, st.head, qw);  // the query MLP's weights load while phase A runs
+            if (ph == 1) {
+                ok = st.attend(l, qw) && st.merge_parts();
+                if (!ok) break;
+            }
+            const float *x = ph == 1 ? a.att : ph == 3 ? a.mid : a.h;
+            const float *W = ph == 0 ? Ly.wq : ph == 1 ? Ly.wo : ph == 2 ? Ly.w1 : Ly.w2;
+            const float *b = ph == 0 ? Ly.bq : ph == 1 ? Ly.bo : ph == 2 ? Ly.b1 : Ly.b2;
+            const int N = ph == 2 ? a.ff : d;
+            float *y = ph == 0 ? a.q : ph == 2 ? a.mid : a.h;
+            ok = st.linear(ph == 0 || ph == 2, step > 0, x, ph == 3 ? a.ff : d, ph == 0 ? Ly.n1w : Ly.n2w,
+                           ph == 0 ? Ly.n1b : Ly.n2b, W, b, N, ph == 2, y, N, ph == 1 || ph == 3);
+        } else {
+            const bool first = ph == 0;
+            const int N = first ? a.dff : a.out_n;
+            ok = st.linear(first, true, first ? a.h : a.mid, first ? d : a.dff, a.lnw, a.lnb, first ? a.dec0w : a.dec2w,
+                           first ? a.dec0b : a.dec2b, N, first, first ? a.mid : a.out, N, false);
+        }
     }
-    ok = ok && st.template linear<true>(true, a.h, d, a.lnw, a.lnb, a.dec0w, a.dec0b, a.dff, 1, a.mid, a.dff, false);
-    ok = ok && st.template linear<false>(true, a.mid, a.dff, nullptr, nullptr, a.dec2w, a.dec2b, a.out_n, 0, a.out,
-                                         a.out_n, false);
     if (!ok) st.drain();
 }
 
