@@ -173,6 +173,8 @@ struct Stage {
     int t0, n, total;     // this CTA's tiles [t0, t0 + n) of every layer; total = L n tiles in its sequence
     int consumed = 0;     // next tile of the sequence to use
     int issued = 0;       // tiles of the sequence whose copies have started (at most consumed + slots)
+    // kept step by step instead of divided out: consumed's slot; issued's layer, index in its layer and slot
+    int cons_s = 0, iss_l = 0, iss_i = 0, iss_s = 0;
     unsigned phase = 0;   // per slot, the parity of its mbarrier's next phase
     unsigned target = 0;  // the grid barrier's latest target
     uint64_t pol_kv, pol_w;
@@ -194,28 +196,33 @@ struct Stage {
         pol_w = policy_evict_last();
     }
 
-    __device__ __forceinline__ int4 tile_of(int g) const {
-        const int i = g % n;
-        return i < TCACHE ? tcache[i] : a.tiles[t0 + i];
-    }
+    // Descriptor of this CTA's tile i of a layer.
+    __device__ __forceinline__ int4 tile_at(int i) const { return i < TCACHE ? tcache[i] : a.tiles[t0 + i]; }
+    __device__ __forceinline__ int4 tile_of(int g) const { return tile_at(g % n); }
+    // Slot s + b of the ring (b < slots).
+    __device__ __forceinline__ int slot_add(int s, int b) const { return s + b >= a.slots ? s + b - a.slots : s + b; }
     __device__ __forceinline__ void arrive() { grid_arrive(a, target); }
     __device__ __forceinline__ bool wait() { return grid_wait(a, target, flag_s); }
     // Start the copies of the next tiles of the sequence, up to `limit`, into the slots that are free.
     __device__ void issue_upto(int limit) {
         limit = min(limit, min(total, consumed + a.slots));
-        for (; issued < limit; issued++) issue(issued);
+        for (; issued < limit; issued++) {
+            issue(iss_l, iss_i, iss_s);
+            if (++iss_i == n) iss_i = 0, iss_l++;
+            iss_s = slot_add(iss_s, 1);
+        }
     }
 
-    // Thread 0: start the loads of sequence tile g into its slot (tiles whose rows are not 16-byte aligned are copied
+    // Thread 0: start the loads of tile i of layer l into slot s (tiles whose rows are not 16-byte aligned are copied
     // when used instead).
-    __device__ void issue(int g) {
-        if (threadIdx.x != 0 || g >= total) return;
-        const int4 tl = tile_of(g);
+    __device__ void issue(int l, int i, int s) {
+        if (threadIdx.x != 0) return;
+        const int4 tl = tile_at(i);
         if (!(tl.w >> 16)) return;
-        const int h = tl.w & 0xffff, ci = tl.x, x = tl.y * C::W, l = g / n;
+        const int h = tl.w & 0xffff, ci = tl.x, x = tl.y * C::W;
         const uint8_t *rec = lay[l].cache + (size_t)ci * a.full;
-        uint8_t *slot = ring + (size_t)(g % a.slots) * C::SLOT;
-        uint64_t *mb = mbar + g % a.slots;
+        uint8_t *slot = ring + (size_t)s * C::SLOT;
+        uint64_t *mb = mbar + s;
         tc::fence_async_smem();  // the slot's earlier reads (generic proxy) before the loads (async proxy)
         mbar_expect_tx(mb, 2u * HD * C::ROWB + (KV ? 8u * HD : 0u));
         const uint8_t *maps = reinterpret_cast<const uint8_t *>(a.tmaps) + (size_t)l * 256;
@@ -232,19 +239,19 @@ struct Stage {
         }
     }
 
-    // All threads: wait for sequence tiles [g0, g0 + nb), the next ones to use (thread 0 waits on the slots'
-    // mbarriers, the CTA barrier below passes the completed copies on to the other threads); then copy those that
-    // could not be copied asynchronously.
-    __device__ bool acquire(int g0, int nb) {
+    // All threads: wait for the next nb tiles to use, tiles i0.. of layer l in the slots from cons_s (thread b waits on
+    // tile b's mbarrier, the CTA barrier below passes the completed copies on to the other threads); then copy those
+    // that could not be copied asynchronously.
+    __device__ bool acquire(int l, int i0, int nb) {
         bool ok = true;
         for (int b = 0; b < nb; b++) {
-            const int g = g0 + b, s = g % a.slots;
-            const int4 tl = tile_of(g);
+            const int s = slot_add(cons_s, b);
+            const int4 tl = tile_at(i0 + b);
             if (tl.w >> 16) {
-                if (threadIdx.x == 0) ok = tc::mbar_wait(mbar + s, (phase >> s) & 1u, SPIN_LIMIT) && ok;
+                if (threadIdx.x == b) ok = tc::mbar_wait(mbar + s, (phase >> s) & 1u, SPIN_LIMIT);
                 phase ^= 1u << s;
             } else {
-                copy_now(g, tl);
+                copy_now(l, s, tl);
             }
         }
         if (!__syncthreads_and(ok)) {
@@ -254,12 +261,11 @@ struct Stage {
         return true;
     }
 
-    __device__ void copy_now(int g, const int4 &tl) {
-        const int s = g % a.slots;
+    __device__ void copy_now(int l, int s, const int4 &tl) {
         // rows not 16-byte aligned: element copies by all threads
         const int h = tl.w & 0xffff, ci = tl.x, k0 = tl.y, len = tl.z;
         const int rc = min(a.chunk, a.rows - ci * a.chunk);
-        const uint8_t *rec = lay[g / n].cache + (size_t)ci * a.full;
+        const uint8_t *rec = lay[l].cache + (size_t)ci * a.full;
         const uint8_t *body = rec + (KV ? 8 * (size_t)a.d : 0);
         uint8_t *slot = ring + (size_t)s * C::SLOT;
         for (int i = threadIdx.x; i < 2 * HD * len; i += THREADS) {
@@ -578,11 +584,11 @@ struct Stage {
                 // a batch of resident tiles under one softmax step
                 const int nb = min(min(C::BMAX, a.slots), te - t);
                 const int g0 = l * n + (t - t0);
-                if (tid < nb) lens[tid] = tile_of(g0 + tid).z;
-                if (!acquire(g0, nb)) return false;
+                if (tid < nb) lens[tid] = tile_at(t - t0 + tid).z;
+                if (!acquire(l, t - t0, nb)) return false;
                 // scores: integer keys take the query times the chunk's key scales (predict.rs:486-497)
                 for (int b = 0; b < nb; b++) {
-                    const uint8_t *slot = ring + (size_t)((g0 + b) % a.slots) * C::SLOT;
+                    const uint8_t *slot = ring + (size_t)slot_add(cons_s, b) * C::SLOT;
                     const float *ksc = reinterpret_cast<const float *>(slot + 2 * HD * C::ROWB);
                     float sp[RM][C::EPV];
 #pragma unroll
@@ -716,7 +722,7 @@ struct Stage {
 #pragma unroll
                         for (int r = 0; r < RM; r++) x[i][r] = 0.f;
                     for (int b = 0; b < nb; b++) {
-                        const uint8_t *slot = ring + (size_t)((g0 + b) % a.slots) * C::SLOT;
+                        const uint8_t *slot = ring + (size_t)slot_add(cons_s, b) * C::SLOT;
                         const float *vsc = reinterpret_cast<const float *>(slot + 2 * HD * C::ROWB) + HD;
                         const int len = lens[b];
                         float p[RM][C::EPV];
@@ -762,6 +768,7 @@ struct Stage {
                 }
                 __syncthreads();  // the slots and the scratch are free again
                 consumed = g0 + nb;
+                cons_s = slot_add(cons_s, nb);
                 t += nb;
                 issue_upto((l + 1) * n);  // this layer's later tiles now; the next layer's after the barrier arrival
             }
