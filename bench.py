@@ -419,6 +419,25 @@ def main():
     lat.sort()
     pct = lambda p: lat[min(len(lat) - 1, int(p * len(lat)))]
 
+    # the other call sizes BASELINE config 2 names (64 and 256 rows), and 8 (the largest one-kernel call): p50 of
+    # CUDA events around each call, device buffers
+    sizes = []
+    for rs in (8, 64, 256):
+        hr, orr = h[:rs].contiguous(), out[:rs].contiguous()
+        for _ in range(3):
+            vm.stage_device(hr.data_ptr(), rs, classes, orr.data_ptr(), sp)
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(20):
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            vm.stage_device(hr.data_ptr(), rs, classes, orr.data_ptr(), sp)
+            s1.record(stream)
+            s1.synchronize()
+            ts.append(s0.elapsed_time(s1) * 1e3)
+        ts.sort()
+        sizes.append({"rows": rs, "p50_us": ts[len(ts) // 2], "rows_per_s": rs / (ts[len(ts) // 2] * 1e-6)})
+
     hbm, bf16, kind = peaks()
     traffic = ncu_traffic(a)
     layer_bytes = pkg.record(a.kv, d, CHUNK) * (a.train_rows // CHUNK) + (pkg.record(a.kv, d, a.train_rows % CHUNK) if a.train_rows % CHUNK else 0)
@@ -454,6 +473,7 @@ def main():
                                       "per_launch_us": lat_pass_s * 1e6, "algorithmic_bytes_per_launch": lat_bytes,
                                       "cache_bytes": L * layer_bytes, "weight_bytes": weight_bytes,
                                       "p50_gbs": (L * layer_bytes + weight_bytes) / (pct(0.5) * 1e-6) / 1e9}},
+        "latency_rows": sizes,
         "clocks": clocks.summary(),
     }
     if not a.no_multi:

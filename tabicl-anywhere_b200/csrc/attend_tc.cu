@@ -474,74 +474,91 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
             float *wts = reinterpret_cast<float *>(Vring);  // [P][BQ] part weights, then [BQ] 1 / sums
             float *winv = wts + P * BQ;
             if (tid < BQ && r0 + tid < a.R) {
+                // eight parts' (max, weight sum) pairs in flight at a time
                 const int r = r0 + tid;
+                const float2 *msr = reinterpret_cast<const float2 *>(a.part_ms) + (size_t)r * H + h;
+                const size_t mstep = (size_t)a.R * H;
                 float M = -FLT_MAX;
-                for (int p = 0; p < P; p++) {
-                    const float *q = a.part_ms + (((size_t)p * a.R + r) * H + h) * 2;
-                    if (__ldcg(q + 1) > 0.f) M = fmaxf(M, __ldcg(q));
+                for (int p0 = 0; p0 < P; p0 += 8) {
+                    float2 ms[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++)
+                        if (p0 + u < P) ms[u] = __ldcg(msr + (p0 + u) * mstep);
+#pragma unroll
+                    for (int u = 0; u < 8; u++)
+                        if (p0 + u < P && ms[u].y > 0.f) M = fmaxf(M, ms[u].x);
                 }
                 float S = 0.f;
-                for (int p = 0; p < P; p++) {
-                    const float *q = a.part_ms + (((size_t)p * a.R + r) * H + h) * 2;
-                    const float l = __ldcg(q + 1), w = l > 0.f ? exp1(__ldcg(q) - M) : 0.f;
-                    wts[p * BQ + tid] = w;
-                    S = __fadd_rn(S, __fmul_rn(l, w));
+                for (int p0 = 0; p0 < P; p0 += 8) {
+                    float2 ms[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++)
+                        if (p0 + u < P) ms[u] = __ldcg(msr + (p0 + u) * mstep);
+#pragma unroll
+                    for (int u = 0; u < 8; u++) {
+                        if (p0 + u < P) {
+                            const float l = ms[u].y, w = l > 0.f ? exp1(ms[u].x - M) : 0.f;
+                            wts[(p0 + u) * BQ + tid] = w;
+                            S = __fadd_rn(S, __fmul_rn(l, w));
+                        }
+                    }
                 }
                 winv[tid] = 1.0f / S;
             }
             __syncthreads();
             const size_t pstride = (size_t)a.R * d;
             const float oun = pow2f(-14 - a.tc_eV);
-            if (tid < 2 * BQ && P <= 8) {
-                // four values of a row per thread and step, every part's loads issued before any is used; this
-                // block's own part is still in shared memory
+            if (tid < 2 * BQ) {
+                // four values of a row per thread and step, two steps at a time; the parts in groups of eight, every
+                // load of a group issued before any is used, summed in part order; this block's own part is still in
+                // shared memory
                 constexpr int STEPS = BQ * HD / 4 / (2 * BQ);
 #pragma unroll 1
                 for (int st = 0; st < STEPS; st += 2) {
-                    float4 v[2][8], ownv[2];
+                    float4 o[2], ownv[2];
+                    const float *base[2];
+                    int mm[2];
 #pragma unroll
                     for (int u = 0; u < 2; u++) {
                         const int e4 = tid + (st + u) * 2 * BQ, m = e4 / (HD / 4), k0 = (e4 % (HD / 4)) * 4;
                         const int r = min(r0 + m, a.R - 1);
-                        const float *base = a.part_acc + (size_t)r * d + h * HD + k0;
-#pragma unroll
-                        for (int p = 0; p < 8; p++) {
-                            if (p < P && p != split) v[u][p] = __ldcg(reinterpret_cast<const float4 *>(base + p * pstride));
-                        }
+                        base[u] = a.part_acc + (size_t)r * d + h * HD + k0;
+                        mm[u] = m;
                         const float *own = ostage + m * (HD + 1) + k0;
                         ownv[u] = make_float4(own[0] * oun, own[1] * oun, own[2] * oun, own[3] * oun);
+                        o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+#pragma unroll 1
+                    for (int p0 = 0; p0 < P; p0 += 8) {
+                        float4 v[2][8];
+#pragma unroll
+                        for (int u = 0; u < 2; u++)
+#pragma unroll
+                            for (int q = 0; q < 8; q++) {
+                                const int p = p0 + q;
+                                if (p < P && p != split) v[u][q] = __ldcg(reinterpret_cast<const float4 *>(base[u] + p * pstride));
+                            }
+#pragma unroll
+                        for (int u = 0; u < 2; u++)
+#pragma unroll
+                            for (int q = 0; q < 8; q++) {
+                                const int p = p0 + q;
+                                if (p < P) {
+                                    const float4 x = p == split ? ownv[u] : v[u][q];
+                                    const float w = wts[p * BQ + mm[u]];
+                                    o[u].x = __fadd_rn(o[u].x, __fmul_rn(x.x, w)), o[u].y = __fadd_rn(o[u].y, __fmul_rn(x.y, w));
+                                    o[u].z = __fadd_rn(o[u].z, __fmul_rn(x.z, w)), o[u].w = __fadd_rn(o[u].w, __fmul_rn(x.w, w));
+                                }
+                            }
                     }
 #pragma unroll
                     for (int u = 0; u < 2; u++) {
-                        const int e4 = tid + (st + u) * 2 * BQ, m = e4 / (HD / 4), k0 = (e4 % (HD / 4)) * 4, r = r0 + m;
+                        const int e4 = tid + (st + u) * 2 * BQ, m = mm[u], k0 = (e4 % (HD / 4)) * 4, r = r0 + m;
                         if (r >= a.R) continue;
-                        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                        for (int p = 0; p < 8; p++) {
-                            if (p < P) {
-                                const float4 x = p == split ? ownv[u] : v[u][p];
-                                const float w = wts[p * BQ + m];
-                                o.x = __fadd_rn(o.x, __fmul_rn(x.x, w)), o.y = __fadd_rn(o.y, __fmul_rn(x.y, w));
-                                o.z = __fadd_rn(o.z, __fmul_rn(x.z, w)), o.w = __fadd_rn(o.w, __fmul_rn(x.w, w));
-                            }
-                        }
                         const float iv = winv[m];
                         *reinterpret_cast<float4 *>(a.out + (size_t)r * a.ldo + h * HD + k0) =
-                            make_float4(o.x * iv, o.y * iv, o.z * iv, o.w * iv);
+                            make_float4(o[u].x * iv, o[u].y * iv, o[u].z * iv, o[u].w * iv);
                     }
-                }
-            } else if (tid < 2 * BQ) {
-                for (int idx = tid; idx < BQ * HD; idx += 2 * BQ) {
-                    const int m = idx / HD, k = idx % HD, r = r0 + m;
-                    if (r >= a.R) break;
-                    const float *base = a.part_acc + (size_t)r * d + h * HD + k;
-                    float o = 0.f;
-                    for (int w = 0; w < 8 && w < P; w++) {
-                        float ow = 0.f;
-                        for (int p = w; p < P; p += 8) ow = fmaf(__ldcg(base + p * pstride), wts[p * BQ + m], ow);
-                        o += ow;
-                    }
-                    a.out[(size_t)r * a.ldo + h * HD + k] = o * winv[m];
                 }
             }
         }
