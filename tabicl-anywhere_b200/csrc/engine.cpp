@@ -694,7 +694,10 @@ static int attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int ro
     if (plan.path == Path::Tensor) {
         if (!tc_tiles) fail(TCU_ERR_STATE, "attend: tensor-core tiles were not built");
         a.tc_eK = eK, a.tc_eV = eV, a.err = ctx->dev_err, a.tc_tiles = tc_tiles;
-        if (m->mcnt.bytes >= sizeof(int) * ((size_t)(R + 127) / 128) * sh.heads) a.merge_cnt = m->mcnt.as<int>();
+        // up to eight splits the last split of a (row block, head) merges them inside the kernel; more parts are
+        // merged by k_attend_merge, one block per (row, head), instead of by a few CTAs reading them all
+        if (a.splits <= 8 && m->mcnt.bytes >= sizeof(int) * ((size_t)(R + 127) / 128) * sh.heads)
+            a.merge_cnt = m->mcnt.as<int>();
         ck(launch_attend_tc(kv, a, s, &ctx->launches), "attend (tensor cores)");
     } else {
         ck(launch_attend_flash(kv, hd, a, s, &ctx->launches), "attend (flash)");
@@ -775,7 +778,9 @@ static void query_rows(tcu_ctx *ctx, tcu_model *m, int l, const float *scale, co
     const LayerPtrs &p = m->w->layer[l];
     const int d = sh.d;
     linear(ctx, m, h, d, R, d, p.n1w, p.n1b, p.wq, p.bq, d, q, d, 0, 0, s, p.tq);  // nn.rs:136-137
-    if (R <= 16) {
+    if (R <= 64) {
+        // few rows: the SIMT kernels (one block per (row, head), or per 16 rows and a head) spread over more SMs than
+        // the tensor-core kernel's 128-pair CTAs would
         Launch{ctx, s}(launch_ssmax(q, R, d, sh.heads, sh.hid, p.q0w, p.q0b, p.q2w, p.q2b, scale, s, &ctx->launches), "ssmax");
         return;
     }
