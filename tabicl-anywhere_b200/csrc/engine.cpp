@@ -590,8 +590,11 @@ static bool tc_enabled() {
     return on;
 }
 static Plan attend_plan(const tcu_ctx *ctx, int R, int heads, int hd, int nitems, int ntiles) {
-    if (R <= 32) return {Path::Decode, nitems};
-    if (hd == 128 && tc_enabled()) {
+    // the tensor-core kernel from 9 rows (head width 128); the split-K decode kernel below that, and up to 32 rows
+    // at other head widths
+    const bool tensor = hd == 128 && tc_enabled();
+    if (R <= (tensor ? 8 : 32)) return {Path::Decode, nitems};
+    if (tensor) {
         // one block per SM at a time: (128 rows x head) blocks, each over a share of the key tiles; the split count
         // that minimises waves x (tiles per block + a block's fixed cost, about 4 tiles: staging its queries,
         // writing and merging its part); ties: fewer splits
