@@ -259,6 +259,48 @@ __global__ void __launch_bounds__(256) k_ssmax_rows(float *q, int d, int heads, 
     const int hd = d / heads, r = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float *qs = sm, *hs = sm + hd;
     float *qp = q + (size_t)r * d + h * hd;
+    if (hd == 128 && hid == 64) {
+        // the configs' shape: every weight a warp needs is loaded before q, all in flight at once; each output's
+        // sum is taken in the same order as the general loops below
+        float w0[8][4], w2[16][2], b0[8], b2[16], sc[16];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+#pragma unroll
+            for (int k = 0; k < 4; k++) w0[i][k] = __ldg(q0w + (size_t)(warp + 8 * i) * 128 + lane + 32 * k);
+            b0[i] = __ldg(q0b + warp + 8 * i);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+#pragma unroll
+            for (int k = 0; k < 2; k++) w2[i][k] = __ldg(q2w + (size_t)(warp + 8 * i) * 64 + lane + 32 * k);
+            b2[i] = __ldg(q2b + warp + 8 * i);
+            sc[i] = __ldg(scale + h * 128 + warp + 8 * i);
+        }
+        if (tid < 128) qs[tid] = qp[tid];
+        __syncthreads();
+        float x[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) x[k] = qs[lane + 32 * k];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float s = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; k++) s = fmaf(w0[i][k], x[k], s);
+            s = warp_sum(s);
+            if (lane == 0) hs[warp + 8 * i] = gelu1(s + b0[i]);
+        }
+        __syncthreads();
+        const float y0 = hs[lane], y1 = hs[lane + 32];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            float s = fmaf(w2[i][0], y0, 0.f);
+            s = fmaf(w2[i][1], y1, s);
+            s = warp_sum(s);
+            const int j = warp + 8 * i;
+            if (lane == 0) qp[j] = qs[j] * (sc[i] * (1.0f + tanh1(s + b2[i])));
+        }
+        return;
+    }
     for (int j = tid; j < hd; j += blockDim.x) qs[j] = qp[j];
     __syncthreads();
     for (int t = warp; t < hid; t += 8) {
@@ -993,7 +1035,8 @@ cudaError_t launch_ln_apply(const float *x, int M, int K, const float *w, const 
 cudaError_t launch_ssmax(float *q, int R, int d, int heads, int hid, const float *q0w, const float *q0b,
                          const float *q2w, const float *q2b, const float *scale, cudaStream_t s, uint64_t *launches) {
     const int hd = d / heads;
-    if (R <= 16) {
+    // one block per (row, head) for few rows, and up to 64 rows at the shape whose weights it loads all at once
+    if (R <= 16 || (R <= 64 && hd == 128 && hid == 64)) {
         k_ssmax_rows<<<dim3(R, heads), 256, sizeof(float) * (hd + hid), s>>>(q, d, heads, hid, q0w, q0b, q2w, q2b, scale);
         TCU_LAUNCHED(launches);
         return cudaGetLastError();
