@@ -781,9 +781,9 @@ static void query_rows(tcu_ctx *ctx, tcu_model *m, int l, const float *scale, co
     const LayerPtrs &p = m->w->layer[l];
     const int d = sh.d;
     linear(ctx, m, h, d, R, d, p.n1w, p.n1b, p.wq, p.bq, d, q, d, 0, 0, s, p.tq);  // nn.rs:136-137
-    if (R <= 64) {
-        // few rows: the SIMT kernels (one block per (row, head), or per 16 rows and a head) spread over more SMs than
-        // the tensor-core kernel's 128-pair CTAs would
+    if (R <= 128) {
+        // up to 128 rows: the SIMT kernels (one block per (row, head), or per 16 rows and a head) spread over more SMs
+        // than the tensor-core kernel's 128-pair CTAs would
         Launch{ctx, s}(launch_ssmax(q, R, d, sh.heads, sh.hid, p.q0w, p.q0b, p.q2w, p.q2b, scale, s, &ctx->launches), "ssmax");
         return;
     }

@@ -1035,8 +1035,8 @@ cudaError_t launch_ln_apply(const float *x, int M, int K, const float *w, const 
 cudaError_t launch_ssmax(float *q, int R, int d, int heads, int hid, const float *q0w, const float *q0b,
                          const float *q2w, const float *q2b, const float *scale, cudaStream_t s, uint64_t *launches) {
     const int hd = d / heads;
-    // one block per (row, head) for few rows, and up to 64 rows at the shape whose weights it loads all at once
-    if (R <= 16 || (R <= 64 && hd == 128 && hid == 64)) {
+    // one block per (row, head) for few rows, and up to 128 rows at the shape whose weights it loads all at once
+    if (R <= 16 || (R <= 128 && hd == 128 && hid == 64)) {
         k_ssmax_rows<<<dim3(R, heads), 256, sizeof(float) * (hd + hid), s>>>(q, d, heads, hid, q0w, q0b, q2w, q2b, scale);
         TCU_LAUNCHED(launches);
         return cudaGetLastError();
