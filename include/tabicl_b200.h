@@ -107,9 +107,19 @@ TCU_API int tcu_attend(tcu_model *m, int layer, const float *q, int rows, int d,
  * row [rows][out_n]. Host buffers; h is not modified. */
 TCU_API int tcu_stage(tcu_model *m, const float *h, int rows, int d, int out_n, float *out);
 /* The same two on device buffers, queued on `stream` (a cudaStream_t; NULL = the context's stream); inputs are
- * not modified. */
+ * not modified. Their kernels run after the call returns: a kernel that gives up a bounded wait (a lost matrix
+ * unit, a copy that never lands) marks the outputs of the calls queued since as invalid, and that is reported by
+ * the next call on the context, by tcu_sync, or by a host-buffer form (TCU_ERR_CUDA, `tcu_last_error` naming the
+ * wait). The context stays usable: the next call starts clean. */
 TCU_API int tcu_attend_device(tcu_model *m, int layer, const float *q, int rows, float *out, void *stream);
 TCU_API int tcu_stage_device(tcu_model *m, const float *h, int rows, int out_n, float *out, void *stream);
+/* Wait for `stream` (NULL = the context's stream) and report kernels that gave up since the last report
+ * (TCU_ERR_CUDA), as cudaStreamSynchronize plus a check; no counterpart in the reference, whose card calls block. */
+TCU_API int tcu_sync(tcu_ctx *ctx, void *stream);
+/* Test hook (no counterpart in the reference): the next one-kernel stage launch on this context starts as if a
+ * wait had given up, so that the give-up path (every CTA leaving at its next barrier after its copies land) and
+ * its report can be exercised without making any wait run out. */
+TCU_API int tcu_debug_abort_next(tcu_ctx *ctx);
 
 /* ---- heads (src/table.rs) ------------------------------------------------------------------------------------ */
 
@@ -136,6 +146,11 @@ TCU_API int tcu_fit_icl_device(tcu_weights *w, float *h, const float *y, int row
 TCU_API int tcu_pack_device(tcu_ctx *ctx, int kv, int d, int rc, const float *c, void *rec);
 /* Bytes of a stored chunk of rc rows (src/fit.rs:124-126). */
 TCU_API size_t tcu_record(int kv, int d, int rc);
+/* The accelerator load helper `layer_rows` (src/predict.rs:590-629) on the device: one layer's stored chunks
+ * `layer` (device, `rows` cached rows in chunks of `chunk`, format kv) widened to keys k and values v [rows][d]
+ * (device floats; integers times their coordinate's scale), with the same vector widening the attention kernels
+ * read the cache through. Synchronises the context stream. */
+TCU_API int tcu_layer_rows_device(tcu_ctx *ctx, int kv, int d, const void *layer, int rows, int chunk, float *k, float *v);
 
 /* Few-row attention that allocates nothing (no counterpart in the reference; an addition for callers that cannot
  * call cudaMalloc: code running while a CUDA graph is captured, hosts whose device memory belongs to an arena or
@@ -147,8 +162,9 @@ TCU_API size_t tcu_record(int kv, int d, int rc);
  * every context that loads this library, kept until the process exits; a call is refused with TCU_ERR_ARG (and a
  * message in `err`, if given) when nq > TCU_NOALLOC_MAX_ROWS, when the cache has more than TCU_NOALLOC_MAX_ITEMS
  * key slices of 32-64 rows, or when the work does not fit the scratch (it fits 32 query rows at 10,000 cached
- * rows of width 512 stored as i16, about 4 at 100,000). The first call on each device looks the scratch's address up (with that device current): make
- * it before any stream capture. Every call shares the scratch and it keeps the last call's contents (each call
+ * rows of width 512 stored as i16, about 4 at 100,000), or when `layer`, `q` or `out` is not 4-byte aligned (the
+ * chunk records' scales and the queries are read as floats). The first call on each device looks the scratch's
+ * address up (with that device current): make it before any stream capture. Every call shares the scratch and it keeps the last call's contents (each call
  * writes all it reads, so nothing must start at zero): calls that overlap on the GPU - on two streams, or from
  * two threads - race and give wrong answers; serialise them. */
 #define TCU_NOALLOC_SCRATCH_BYTES (16 << 20)

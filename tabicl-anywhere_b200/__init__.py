@@ -80,6 +80,9 @@ def lib():
         "tcu_fit_icl_device": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_int, P(_c_void)]),
         "tcu_pack_device": (_c_int, [_c_void, _c_int, _c_int, _c_int, _c_void, _c_void]),
         "tcu_record": (_c_size, [_c_int, _c_int, _c_int]),
+        "tcu_layer_rows_device": (_c_int, [_c_void, _c_int, _c_int, _c_void, _c_int, _c_int, _c_void, _c_void]),
+        "tcu_sync": (_c_int, [_c_void, _c_void]),
+        "tcu_debug_abort_next": (_c_int, [_c_void]),
         "tcu_profile": (_c_int, [_c_void, _c_int, P(ctypes.c_double), P(ctypes.c_uint64)]),
         "tcu_selftest_mma": (_c_int, [_c_void, P(ctypes.c_double)]),
         "tcu_attend_noalloc": (_c_int, [_c_int, _c_int, _c_int, _c_void, _c_int, _c_int, _c_void, _c_int, _c_void,
@@ -175,6 +178,19 @@ class Gpu:
     def pack(self, kv, d, rc, c_ptr, rec_ptr):
         return self.check(lib().tcu_pack_device(self._h, kv, d, rc, c_ptr, rec_ptr))
 
+    def layer_rows(self, kv, d, layer_ptr, rows, chunk, k_ptr, v_ptr):
+        """predict.rs:590-629 on device buffers: stored chunks to keys and values [rows][d] floats."""
+        return self.check(lib().tcu_layer_rows_device(self._h, kv, d, layer_ptr, rows, chunk, k_ptr, v_ptr))
+
+    def sync(self, stream=None):
+        """Wait for `stream` (None: the context's) and raise if kernels gave up a bounded wait since the last
+        report."""
+        return self.check(lib().tcu_sync(self._h, stream))
+
+    def debug_abort_next(self):
+        """Test hook: the next one-kernel stage launch starts as if a wait had given up."""
+        return self.check(lib().tcu_debug_abort_next(self._h))
+
 
 class GpuWeights:
     """The in-context weights on the device (gpu::GpuWeights, src/gpu.rs:1838-2028)."""
@@ -256,21 +272,30 @@ class VramModel:
     def nbytes(self):
         return int(lib().tcu_model_bytes(self._h))
 
-    def attend(self, layer, q):
-        q = np.ascontiguousarray(q, dtype=np.float32).reshape(-1, self.d)
+    def attend(self, layer, q, d=None, heads=None):
+        """AttendCached::attend on host buffers: scaled queries [rows][d] to attention outputs [rows][d]. `d` and
+        `heads` are the caller's (the library refuses ones that are not the weights')."""
+        d = self.d if d is None else d
+        heads = self.weights.shape["heads"] if heads is None else heads
+        q = np.ascontiguousarray(q, dtype=np.float32).reshape(-1)
+        if q.size % d:
+            raise TcuError(-1, f"attend: {q.size} query values are not rows of width {d}")
         out = np.empty_like(q)
-        s = self.weights.shape
-        self.gpu.check(lib().tcu_attend(self._h, layer, _f32p(q), q.shape[0], self.d, s["heads"], _f32p(out)))
-        return out
+        self.gpu.check(lib().tcu_attend(self._h, layer, _f32p(q), q.size // d, d, heads, _f32p(out)))
+        return out.reshape(-1, d)
 
-    def stage(self, h, out_n, out=None):
+    def stage(self, h, out_n, out=None, d=None):
         """AttendCached::stage on host buffers: [rows][d] representations to [rows][out_n] decoder outputs
         (`out`, if given, is filled: pinned host buffers make the copies faster)."""
-        h = np.ascontiguousarray(h, dtype=np.float32).reshape(-1, self.d)
+        d = self.d if d is None else d
+        h = np.ascontiguousarray(h, dtype=np.float32).reshape(-1)
+        if h.size % d:
+            raise TcuError(-1, f"stage: {h.size} values are not rows of width {d}")
+        rows = h.size // d
         if out is None:
-            out = np.empty((h.shape[0], out_n), dtype=np.float32)
-        assert out.dtype == np.float32 and out.flags.c_contiguous and out.size == h.shape[0] * out_n
-        self.gpu.check(lib().tcu_stage(self._h, _f32p(h), h.shape[0], self.d, out_n, _f32p(out)))
+            out = np.empty((rows, out_n), dtype=np.float32)
+        assert out.dtype == np.float32 and out.flags.c_contiguous and out.size == rows * out_n
+        self.gpu.check(lib().tcu_stage(self._h, _f32p(h), rows, d, out_n, _f32p(out)))
         return out
 
     def attend_device(self, layer, q_ptr, rows, out_ptr, stream=None):
@@ -408,10 +433,10 @@ class CudaAttend:
             return None
 
     def attend(self, prefix, node, layer, q, d, heads):
-        return self._or_cpu(lambda: self._model(prefix, node).attend(layer, q))
+        return self._or_cpu(lambda: self._model(prefix, node).attend(layer, q, d, heads))
 
     def stage(self, prefix, node, h, d, out_n):
-        return self._or_cpu(lambda: self._model(prefix, node).stage(h, out_n))
+        return self._or_cpu(lambda: self._model(prefix, node).stage(h, out_n, d=d))
 
     def rows(self, prefix, x, out_n):
         # the column and row stages are not on the device yet: decline, the caller's CPU path does them

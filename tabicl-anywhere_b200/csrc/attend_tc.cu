@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
             }
         }
     }
-    if (*abort_flag && tid == 0 && a.err) atomicExch(a.err, 1);
+    if (*abort_flag && tid == 0 && a.err) *reinterpret_cast<volatile int *>(a.err) = 1;  // a report slot in host memory
     // split parts: the last of a (row block, head)'s splits to finish merges them (the log-sum-exp merge of
     // k_attend_merge, predict.rs:455-478, with the same products and order of sums)
     if (a.splits > 1 && !a.parts_only && a.merge_cnt) {
@@ -592,13 +592,13 @@ cudaError_t launch_attend_tc(int kv, const AttnArgs &a, cudaStream_t s, uint64_t
     dim3 grid((a.R + 127) / 128, a.heads, a.splits);
     cudaError_t e = cudaSuccess;
     if (kv == 0) {
-        e = cudaFuncSetAttribute(k_attend_tc<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        e = allow_dynamic_smem((const void *)k_attend_tc<0>, smem);
         if (e == cudaSuccess) k_attend_tc<0><<<grid, TC_THREADS, smem, s>>>(a);
     } else if (kv == 1) {
-        e = cudaFuncSetAttribute(k_attend_tc<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        e = allow_dynamic_smem((const void *)k_attend_tc<1>, smem);
         if (e == cudaSuccess) k_attend_tc<1><<<grid, TC_THREADS, smem, s>>>(a);
     } else {
-        e = cudaFuncSetAttribute(k_attend_tc<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        e = allow_dynamic_smem((const void *)k_attend_tc<2>, smem);
         if (e == cudaSuccess) k_attend_tc<2><<<grid, TC_THREADS, smem, s>>>(a);
     }
     if (e != cudaSuccess) return e;

@@ -86,9 +86,20 @@ struct tcu_ctx {
     bool prof = false;
     std::vector<cudaEvent_t> prof_events;
     size_t prof_used = 0;
-    int *dev_err = nullptr;       // set by kernels that gave up waiting (tensor-core attention)
-    unsigned *dev_scan = nullptr; // scratch of the per-layer magnitude scan
+    // Report slots of kernels that gave up a bounded wait, in pinned host memory mapped into the device (kernels
+    // store 1 into their slot; the host reads them without synchronising): ERR_SLOTS ints, see err_slot_names.
+    int *err_host = nullptr;
+    int *err_mapped = nullptr;     // the same slots' device address
+    bool abort_next = false;       // test hook: the next one-kernel stage launch starts aborted
+    unsigned *dev_scan = nullptr;  // scratch of the per-layer magnitude scan
 };
+
+// Which wait each report slot stands for.
+enum { ERR_ATTEND_TC = 0, ERR_GEMM_TC = 1, ERR_QMLP_TC = 2, ERR_ROWS = 3, ERR_SLOTS = 8 };
+static const char *const err_slot_names[6] = {
+    "tensor-core attention (matrix-unit or copy wait)", "tensor-core linear layer (matrix-unit or copy wait)",
+    "tensor-core query MLP (matrix-unit wait)", "one-kernel stage (grid barrier)", "one-kernel stage (key tile copy)",
+    "one-kernel stage (left after another CTA gave up)"};
 
 // A weight matrix [N][K] split once for the tensor cores: f16 hi + lo (bit patterns) of W * 2^e(n) in 128 x 64
 // blocks (tc_block_off), and 2^-e(n). No blocks when K is not a multiple of 64.
@@ -206,7 +217,7 @@ static void ctx_release(tcu_ctx *ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     for (auto e : ctx->prof_events) cudaEventDestroy(e);
-    if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->err_host) cudaFreeHost(ctx->err_host);
     if (ctx->dev_scan) cudaFree(ctx->dev_scan);
     delete ctx;
 }
@@ -696,7 +707,7 @@ static int attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int ro
     a.splits = (ntiles + a.tiles_per_split - 1) / a.tiles_per_split;
     if (plan.path == Path::Tensor) {
         if (!tc_tiles) fail(TCU_ERR_STATE, "attend: tensor-core tiles were not built");
-        a.tc_eK = eK, a.tc_eV = eV, a.err = ctx->dev_err, a.tc_tiles = tc_tiles;
+        a.tc_eK = eK, a.tc_eV = eV, a.err = ctx->err_mapped + ERR_ATTEND_TC, a.tc_tiles = tc_tiles;
         // up to eight splits the last split of a (row block, head) merges them inside the kernel; more parts are
         // merged by k_attend_merge, one block per (row, head), instead of by a few CTAs reading them all
         if (a.splits <= 8 && m->mcnt.bytes >= sizeof(int) * ((size_t)(R + 127) / 128) * sh.heads)
@@ -714,19 +725,26 @@ static void linear(tcu_ctx *ctx, tcu_model *m, const float *x, int ldx, int R, i
     LinArgs a;
     a.x = x, a.ldx = ldx, a.M = R, a.K = K, a.lnw = lnw, a.lnb = lnb, a.W = W, a.bias = b, a.N = N, a.y = y, a.ldy = ldy;
     a.act = act, a.accumulate = accumulate, a.transpose_out = transpose_out;
-    a.tc_wtiles = tw.tiles, a.tc_wunscale = tw.unscale, a.err = ctx->dev_err;
+    a.tc_wtiles = tw.tiles, a.tc_wunscale = tw.unscale, a.err = ctx->err_mapped + ERR_GEMM_TC;
     a.tc_atiles = m->atiles.p, a.tc_atiles_bytes = m->atiles.bytes;
     Launch{ctx, s}(launch_linear(a, m->stats.as<float>(), s, &ctx->launches), "linear");
 }
 
-// A kernel that gave up waiting left a flag: report it once, and clear it.
+// Kernels that gave up a bounded wait stored 1 into their report slots: report them once (naming the waits), and
+// clear them. The slots are host memory, so this needs no synchronisation; a call still running on the device
+// reports at a later check.
 static void check_device_error(tcu_ctx *ctx) {
-    int flag = 0;
-    CU(cudaMemcpy(&flag, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (flag) {
-        CU(cudaMemset(ctx->dev_err, 0, sizeof(int)));
-        fail(TCU_ERR_CUDA, "tensor-core attention gave up waiting for its matrix units; outputs of that call are invalid");
+    volatile int *slot = ctx->err_host;
+    std::string which;
+    for (int i = 0; i < 6; i++) {
+        if (slot[i]) {
+            slot[i] = 0;
+            which += (which.empty() ? "" : "; ") + std::string(err_slot_names[i]);
+        }
     }
+    if (!which.empty())
+        fail(TCU_ERR_CUDA, "kernels gave up a bounded wait: " + which +
+                               ". Outputs of the calls queued since the last report are invalid");
 }
 
 // Largest |key| and |value| of a stored layer -> the tensor cores' power-of-two scalings (synchronises).
@@ -795,7 +813,7 @@ static void query_rows(tcu_ctx *ctx, tcu_model *m, int l, const float *scale, co
         QmlpArgs qa;
         qa.q = q, qa.pairs = R * H, qa.heads = H, qa.hd = hd, qa.hid = hid;
         qa.w0_tiles = p.tq0.tiles, qa.w2_tiles = p.tq2.tiles, qa.w0_unscale = p.tq0.unscale, qa.w2_unscale = p.tq2.unscale;
-        qa.b0 = p.q0b, qa.b2 = p.q2b, qa.scale = scale, qa.err = ctx->dev_err;
+        qa.b0 = p.q0b, qa.b2 = p.q2b, qa.scale = scale, qa.err = ctx->err_mapped + ERR_QMLP_TC;
         Launch{ctx, s}(launch_qmlp_tc(qa, s, &ctx->launches), "query MLP (tensor cores)");
         return;
     }
@@ -964,9 +982,17 @@ static void stage_rows(tcu_ctx *ctx, tcu_model *m, const tcu_model::RowsPlan &p,
     a.h = m->h.as<float>(), a.q = m->q.as<float>(), a.att = m->att.as<float>(), a.mid = m->mid.as<float>();
     a.out = m->out.as<float>();
     a.part_ms = m->rparts_ms.as<float>(), a.part_acc = m->rparts_acc.as<float>();
-    a.bar = m->rsync.as<unsigned>(), a.err = ctx->dev_err;
-    // a launch that gave up leaves the barrier word dirty: every launch starts from zeros
+    // the barrier word at byte 0, the launch's abort word at byte 128 (its own line); every launch starts from
+    // zeros, so one that gave up leaves nothing behind
+    a.bar = m->rsync.as<unsigned>(), a.err = reinterpret_cast<int *>(m->rsync.as<uint8_t>() + 128);
+    a.err_report = ctx->err_mapped + ERR_ROWS;
     CU(cudaMemsetAsync(m->rsync.p, 0, 256, s));
+    if (ctx->abort_next) {
+        // test hook: start with the abort word set, as if a wait had given up; every CTA leaves at its first
+        // barrier after its first phase and waits for its copies in flight
+        CU(cudaMemsetAsync(a.err, 1, sizeof(int), s));
+        ctx->abort_next = false;
+    }
     cudaEvent_t ev_end = nullptr;
     if (ctx->prof) {
         if (ctx->prof_used + 2 > ctx->prof_events.size()) {
@@ -1135,6 +1161,7 @@ static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, in
         block_tail(ctx, m.get(), l, h, m->att.as<float>(), rows, s);
     }
     CU(cudaStreamSynchronize(s));
+    check_device_error(ctx);
     m->have_scales = true;
     return m.release();
 }
@@ -1159,8 +1186,9 @@ int tcu_open(int device, tcu_ctx **out) {
         CU(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
         ctx->smem_optin = (size_t)optin;
         CU(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
-        CU(cudaMalloc(&ctx->dev_err, sizeof(int)));
-        CU(cudaMemset(ctx->dev_err, 0, sizeof(int)));
+        CU(cudaHostAlloc((void **)&ctx->err_host, ERR_SLOTS * sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable));
+        std::memset(ctx->err_host, 0, ERR_SLOTS * sizeof(int));
+        CU(cudaHostGetDevicePointer((void **)&ctx->err_mapped, ctx->err_host, 0));
         CU(cudaMalloc(&ctx->dev_scan, 2 * sizeof(unsigned)));
         CU(kernels_init());
         return TCU_OK;
@@ -1382,6 +1410,7 @@ int tcu_attend_device(tcu_model *m, int layer, const float *q, int rows, float *
     if (!m) return TCU_ERR_ARG;
     tcu_ctx *ctx = m->w->ctx;
     return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);  // an earlier call's kernels that gave up are reported by the next call
         check_ready(m);
         if (layer < 0 || layer >= m->w->shape.layers || rows < 0 || (rows && (!q || !out))) fail(TCU_ERR_ARG, "attend: bad argument");
         if (rows == 0) return TCU_OK;
@@ -1398,6 +1427,7 @@ int tcu_stage_device(tcu_model *m, const float *h, int rows, int out_n, float *o
     if (!m) return TCU_ERR_ARG;
     tcu_ctx *ctx = m->w->ctx;
     return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
         if (rows < 0 || (rows && (!h || !out))) fail(TCU_ERR_ARG, "stage: bad argument");
         if (rows == 0) return TCU_OK;
         cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
@@ -1416,6 +1446,7 @@ int tcu_attend(tcu_model *m, int layer, const float *q, int rows, int d, int hea
     if (!m) return TCU_ERR_ARG;
     tcu_ctx *ctx = m->w->ctx;
     return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
         if (d != m->w->shape.d || heads != m->w->shape.heads) fail(TCU_ERR_ARG, "attend: d or heads differ from the weights'");
         if (rows < 0 || (rows && (!q || !out))) fail(TCU_ERR_ARG, "attend: bad argument");
         if (rows == 0) return TCU_OK;
@@ -1438,6 +1469,7 @@ int tcu_stage(tcu_model *m, const float *h, int rows, int d, int out_n, float *o
     if (!m) return TCU_ERR_ARG;
     tcu_ctx *ctx = m->w->ctx;
     return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
         if (d != m->w->shape.d) fail(TCU_ERR_ARG, "stage: d differs from the weights'");
         if (rows < 0 || (rows && (!h || !out))) fail(TCU_ERR_ARG, "stage: bad argument");
         if (rows == 0) return TCU_OK;
@@ -1502,6 +1534,19 @@ int tcu_pack_device(tcu_ctx *ctx, int kv, int d, int rc, const float *c, void *r
 }
 
 size_t tcu_record(int kv, int d, int rc) { return record_bytes(kv, d, rc); }
+
+int tcu_layer_rows_device(tcu_ctx *ctx, int kv, int d, const void *layer, int rows, int chunk, float *k, float *v) {
+    return guarded(ctx, [&]() -> int {
+        if (kv < 0 || kv > 2 || d < 4 || d % 4 || rows < 1 || chunk < 1 || !layer || !k || !v)
+            fail(TCU_ERR_ARG, "layer_rows: bad argument");
+        if ((uintptr_t)layer & 3) fail(TCU_ERR_ARG, "layer_rows: layer must be 4-byte aligned");
+        Launch{ctx, ctx->stream}(launch_layer_rows(kv, reinterpret_cast<const uint8_t *>(layer), rows, chunk, d, k, v,
+                                                   ctx->stream, &ctx->launches),
+                                 "layer_rows");
+        CU(cudaStreamSynchronize(ctx->stream));
+        return TCU_OK;
+    });
+}
 
 int tcu_selftest_mma(tcu_ctx *ctx, double *max_err) {
     return guarded(ctx, [&]() -> int {
@@ -1619,6 +1664,7 @@ int tcu_stage_sharded_device(tcu_model *m, tcu_comm *c, const float *h, int rows
     if (!m || !c) return TCU_ERR_ARG;
     tcu_ctx *ctx = m->w->ctx;
     return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
         if (c->ctx != ctx) fail(TCU_ERR_ARG, "stage_sharded: communicator and cache belong to different contexts");
         if (rows < 0 || (rows && (!h || !out))) fail(TCU_ERR_ARG, "stage_sharded: bad argument");
         if (rows == 0) return TCU_OK;
@@ -1628,6 +1674,21 @@ int tcu_stage_sharded_device(tcu_model *m, tcu_comm *c, const float *h, int rows
         CU(cudaMemcpyAsync(m->h.p, h, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
         stage_sharded(ctx, m, c, rows, out_n, s);
         CU(cudaMemcpyAsync(out, m->out.p, sizeof(float) * (size_t)rows * out_n, cudaMemcpyDeviceToDevice, s));
+        return TCU_OK;
+    });
+}
+
+int tcu_sync(tcu_ctx *ctx, void *stream) {
+    return guarded(ctx, [&]() -> int {
+        CU(cudaStreamSynchronize(stream ? (cudaStream_t)stream : ctx->stream));
+        check_device_error(ctx);
+        return TCU_OK;
+    });
+}
+
+int tcu_debug_abort_next(tcu_ctx *ctx) {
+    return guarded(ctx, [&]() -> int {
+        ctx->abort_next = true;
         return TCU_OK;
     });
 }

@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4
             }
         }
     }
-    if (!ok && tid == 0 && a.err) atomicExch(a.err, 1);
+    if (!ok && tid == 0 && a.err) *reinterpret_cast<volatile int *>(a.err) = 1;  // a report slot in host memory
     fence_before_sync();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, GBUFS * BN);
@@ -354,13 +354,8 @@ static int gemm_bn(int M, int N) {
 
 template <int BN>
 static cudaError_t launch_bn(const LinArgs &a, float4 *stats, cudaStream_t s) {
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)GemmShape<BN>::SMEM);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    cudaError_t e = allow_dynamic_smem((const void *)k_gemm_tc<BN>, GemmShape<BN>::SMEM);
+    if (e != cudaSuccess) return e;
     dim3 grid((a.N + BN - 1) / BN, (a.M + GBM - 1) / GBM);
     k_gemm_tc<BN><<<grid, GTHREADS, GemmShape<BN>::SMEM, s>>>(a, stats);
     return cudaGetLastError();

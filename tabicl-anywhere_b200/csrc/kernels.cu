@@ -977,19 +977,25 @@ cudaError_t kernels_init() {
     return cudaSuccess;
 }
 
-// Opt a kernel in to more than 48 KB of dynamic shared memory, once per kernel and size (per process: the
-// attribute is per function; devices of one process share it).
-template <typename K>
-static cudaError_t allow_smem(K kernel, size_t bytes) {
+// Opt a kernel in to more than 48 KB of dynamic shared memory, once per (device, kernel) and size: the attribute
+// belongs to the function on the current device, so a second device of the same process needs its own.
+cudaError_t allow_dynamic_smem(const void *kernel, size_t bytes) {
     if (bytes <= 48 * 1024) return cudaSuccess;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
     static std::mutex mu;
-    static std::map<const void *, size_t> done;
+    static std::map<std::pair<int, const void *>, size_t> done;
     std::lock_guard<std::mutex> lock(mu);
-    size_t &have = done[(const void *)kernel];
+    size_t &have = done[{dev, kernel}];
     if (bytes <= have) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     if (e == cudaSuccess) have = bytes;
     return e;
+}
+template <typename K>
+static cudaError_t allow_smem(K kernel, size_t bytes) {
+    return allow_dynamic_smem((const void *)kernel, bytes);
 }
 
 cudaError_t launch_linear(const LinArgs &a, float *stats_scratch, cudaStream_t s, uint64_t *launches) {
@@ -1149,6 +1155,49 @@ cudaError_t launch_merge_finish(const float *packed, int R, int H, int d, float 
                                 uint64_t *launches) {
     const size_t n = (size_t)R * d;
     k_merge_finish<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(packed, R, H, d, out, ldo);
+    TCU_LAUNCHED(launches);
+    return cudaGetLastError();
+}
+
+// predict.rs:590-629 layer_rows on the device: one layer's stored chunks widened to keys and values [rows][d]
+// (value times its coordinate's scale for integer formats, one f32 multiply as the CPU does). Block (chunk,
+// coordinate); each thread widens one 16-byte vector of the coordinate's row with the attention kernels' own
+// unpack<KV>, or single elements where the row is not 16-byte aligned or ends inside the vector.
+template <int KV>
+__global__ void k_layer_rows(const uint8_t *layer, int rows, int chunk, int d, size_t full, float *k, float *v) {
+    constexpr int W = KvFmt<KV>::W, EPV = 16 / W;
+    const int ci = blockIdx.x, j = blockIdx.y;
+    const int r0 = ci * chunk, rc = min(chunk, rows - r0);
+    const uint8_t *rec = layer + (size_t)ci * full;
+    const float scale = KV ? reinterpret_cast<const float *>(rec)[j] : 1.f;
+    const uint8_t *row = rec + (KV ? 8 * (size_t)d : 0) + (size_t)j * rc * W;
+    float *dst = j < d ? k + (size_t)r0 * d + j : v + (size_t)r0 * d + (j - d);
+    for (int e0 = threadIdx.x * EPV; e0 < rc; e0 += blockDim.x * EPV) {
+        const uint8_t *p = row + (size_t)e0 * W;
+        if (e0 + EPV <= rc && ((uintptr_t)p & 15) == 0) {
+            const uint4 vec = __ldg(reinterpret_cast<const uint4 *>(p));
+#pragma unroll
+            for (int e = 0; e < EPV; e++) {
+                const float x = unpack<KV>(vec, e);
+                dst[(size_t)(e0 + e) * d] = KV ? x * scale : x;
+            }
+        } else {
+            for (int e = e0; e < min(e0 + EPV, rc); e++) {
+                const float x = load_elem<KV>(row, e);
+                dst[(size_t)e * d] = KV ? x * scale : x;
+            }
+        }
+    }
+}
+
+cudaError_t launch_layer_rows(int kv, const uint8_t *layer, int rows, int chunk, int d, float *k, float *v, cudaStream_t s,
+                              uint64_t *launches) {
+    if (rows < 1 || chunk < 1 || d < 1 || kv < 0 || kv > 2) return cudaErrorInvalidValue;
+    const dim3 grid((rows + chunk - 1) / chunk, 2 * d);
+    const size_t full = record_bytes(kv, d, chunk);
+    if (kv == 0) k_layer_rows<0><<<grid, 64, 0, s>>>(layer, rows, chunk, d, full, k, v);
+    else if (kv == 1) k_layer_rows<1><<<grid, 64, 0, s>>>(layer, rows, chunk, d, full, k, v);
+    else k_layer_rows<2><<<grid, 64, 0, s>>>(layer, rows, chunk, d, full, k, v);
     TCU_LAUNCHED(launches);
     return cudaGetLastError();
 }

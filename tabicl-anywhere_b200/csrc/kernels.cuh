@@ -28,7 +28,7 @@ struct LinArgs {
     const float *tc_wunscale = nullptr;
     void *tc_atiles = nullptr;
     size_t tc_atiles_bytes = 0;
-    int *err = nullptr;  // set to 1 when a kernel gave up waiting
+    int *err = nullptr;  // report slot (host memory, mapped): set to 1 when the kernel gave up waiting
 };
 
 // The query MLP of many rows (nn.rs:138-149) in one tensor-core kernel: q [pairs][hd] as (row, head) pairs, in place.
@@ -38,7 +38,7 @@ struct QmlpArgs {
     const void *w0_tiles = nullptr, *w2_tiles = nullptr;  // W0 [hid][hd], W2 [hd][hid] split as for the linear layers
     const float *w0_unscale = nullptr, *w2_unscale = nullptr, *b0 = nullptr, *b2 = nullptr;
     const float *scale = nullptr;  // [heads * hd] the layer's fit-time query scale
-    int *err = nullptr;
+    int *err = nullptr;  // report slot (host memory, mapped): set to 1 when the kernel gave up waiting
 };
 
 // Attention of scaled queries against one layer's stored chunks (fit.rs:6-11 layout, read in place).
@@ -57,7 +57,7 @@ struct AttnArgs {
     float *out = nullptr;          // [R][d] finished outputs (row stride ldo)
     int ldo = 0;
     int tc_eK = 0, tc_eV = 0;      // tensor-core path: power-of-two scalings of the keys and values
-    int *err = nullptr;            // set to 1 when a kernel gave up waiting
+    int *err = nullptr;            // report slot (host memory, mapped): set to 1 when the kernel gave up waiting
     int parts_only = 0;            // 1: always leave parts (no merge), even with a single split
     const void *tc_tiles = nullptr;  // tensor-core path: the layer's tiles pre-split by launch_tc_tiles
     int *merge_cnt = nullptr;  // tensor-core path: [R / 128][heads] arrival counters (zero between launches); when
@@ -94,7 +94,10 @@ struct RowsArgs {
     // sum) and [grid][R][head width]
     float *part_ms = nullptr, *part_acc = nullptr;
     unsigned *bar = nullptr;            // grid barrier word (zero low bits between launches)
-    int *err = nullptr;                 // set to 1 when a wait gave up
+    int *err = nullptr;                 // abort word (device memory, zeroed before each launch): set when a wait
+                                        // gave up, every CTA then leaves at its next barrier
+    int *err_report = nullptr;          // report slots (host memory, mapped): [0] a grid barrier gave up, [1] a
+                                        // tile's copy did not arrive, [2] the CTA left because another gave up
 };
 
 // Keys per tile of the one-kernel stage for a stored format (f32 32, i16 64, i8 64).
@@ -161,6 +164,9 @@ cudaError_t launch_merge_finish(const float *packed, int R, int H, int d, float 
                                 uint64_t *launches);
 cudaError_t launch_pack(const float *kvT, int ld, int d, int rows, int chunk, int kv, uint8_t *out, cudaStream_t s,
                         uint64_t *launches);
+// predict.rs:590-629: a layer's stored chunks widened to k, v [rows][d] (integers times their scales)
+cudaError_t launch_layer_rows(int kv, const uint8_t *layer, int rows, int chunk, int d, float *k, float *v, cudaStream_t s,
+                              uint64_t *launches);
 cudaError_t launch_add_y(float *h, const float *y, int rows, int d, int max_classes, const float *table,
                          cudaStream_t s, uint64_t *launches);
 cudaError_t launch_class_head(const float *logits, int rows, int classes, int stride, const int32_t *member_classes,
@@ -170,6 +176,9 @@ cudaError_t launch_regression_head(const float *qout, int rows, int nq, int stri
                                    double tmean, double tscale, double *mean, double *var, double *median,
                                    double *quant, cudaStream_t s, uint64_t *launches);
 cudaError_t kernels_init();
+// Opt `kernel` in to `bytes` of dynamic shared memory on the current device (the attribute is per function and
+// device); remembered per (device, kernel), so repeated calls cost a map lookup.
+cudaError_t allow_dynamic_smem(const void *kernel, size_t bytes);
 
 // Tensor-core attention (head width 128, many rows): merges itself when splits == 1, else writes parts.
 cudaError_t launch_attend_tc(int kv, const AttnArgs &a, cudaStream_t s, uint64_t *launches);

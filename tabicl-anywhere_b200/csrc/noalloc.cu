@@ -66,6 +66,9 @@ extern "C" int tcu_attend_noalloc(int kv, int d, int heads, const void *layer, i
     if (rows < 1 || chunk < 1) return bad("rows and chunk must be at least 1");
     if (nq < 1 || nq > TCU_NOALLOC_MAX_ROWS) return bad("query rows must be 1..32");
     if (!layer || !q || !out) return bad("null pointer");
+    // chunk records are read through float pointers (their scales) and so are the queries and outputs: a
+    // misaligned pointer would fault the context instead of being refused
+    if (((uintptr_t)layer | (uintptr_t)q | (uintptr_t)out) & 3) return bad("layer, q and out must be 4-byte aligned");
     // the scratch holds the work list and, per item and query row, (max, sum) per head plus d weighted values
     const int ks = decode_keys_per_item(kv);
     const int per_chunk = (chunk + ks - 1) / ks;

@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(QM_THREADS, 1) k_qmlp_tc(QmlpArgs a) {
             }
         }
     }
-    if (*abort_flag && tid == 0 && a.err) atomicExch(a.err, 1);
+    if (*abort_flag && tid == 0 && a.err) *reinterpret_cast<volatile int *>(a.err) = 1;  // a report slot in host memory
     fence_before_sync();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 256);
@@ -251,7 +251,7 @@ cudaError_t launch_qmlp_tc(const QmlpArgs &a, cudaStream_t s, uint64_t *launches
     if (a.hd != QM_HD || a.hid != QM_HID || !a.w0_tiles || !a.w2_tiles) return cudaErrorInvalidValue;
     const size_t smem = qmlp_tc_smem(a.heads);
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(k_qmlp_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = allow_dynamic_smem((const void *)k_qmlp_tc, smem);
     if (e != cudaSuccess) return e;
     k_qmlp_tc<<<(a.pairs + QM_ROWS - 1) / QM_ROWS, QM_THREADS, smem, s>>>(a);
     if (launches) ++*launches;

@@ -88,11 +88,14 @@ __device__ bool grid_wait(const RowsArgs &a, unsigned target, int *flag_s) {
         int ok = 1;
         while (ld_acquire_u32(a.bar) < target) {
             if (ld_relaxed_s32(a.err) != 0) {
+                // another CTA gave up (or the launch was started aborted): leave, and say why
+                if (a.err_report) reinterpret_cast<volatile int *>(a.err_report)[2] = 1;
                 ok = 0;
                 break;
             }
             if (clock64() - t0 > SPIN_LIMIT) {
                 atomicExch(a.err, 1);
+                if (a.err_report) reinterpret_cast<volatile int *>(a.err_report)[0] = 1;
                 ok = 0;
                 break;
             }
@@ -255,7 +258,10 @@ struct Stage {
             }
         }
         if (!__syncthreads_and(ok)) {
-            if (threadIdx.x == 0) atomicExch(a.err, 1);
+            if (threadIdx.x == 0) {
+                atomicExch(a.err, 1);
+                if (a.err_report) reinterpret_cast<volatile int *>(a.err_report)[1] = 1;
+            }
             return false;
         }
         return true;
@@ -853,16 +859,8 @@ size_t smem_of(int slots) {
 template <int KV, int HD, int RM>
 cudaError_t launch_one(const RowsArgs &a, int grid, size_t smem, cudaStream_t s) {
     auto kern = k_stage_rows<KV, HD, RM>;
-    static std::mutex mu;
-    static size_t have = 0;
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if (smem > have) {
-            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
-            have = smem;
-        }
-    }
+    cudaError_t e = allow_dynamic_smem((const void *)kern, smem);
+    if (e != cudaSuccess) return e;
     void *args[] = {const_cast<RowsArgs *>(&a)};
     return cudaLaunchCooperativeKernel((const void *)kern, dim3(grid), dim3(THREADS), args, smem, s);
 }

@@ -199,6 +199,28 @@ def test_pack_is_bit_exact(gpu, kv):
 
 
 @pytest.mark.parametrize("kv", [0, 1, 2])
+def test_integer_unpacking_is_bit_exact(gpu, kv):
+    """predict.rs:590-629 layer_rows through the device's own widening (the vector unpack the attention kernels
+    read the cache with): equal bit for bit to the CPU path, with full 16-byte-aligned chunks, ragged last chunks,
+    and chunks whose rows are not 16-byte aligned."""
+    import torch
+    rng = np.random.default_rng(30 + kv)
+    for d, rows, chunk in [(512, 700, 256), (32, 333, 37), (16, 101, 48), (64, 9, 8)]:
+        k = (rng.standard_normal((rows, d)) * rng.uniform(0.1, 30, (1, d))).astype(np.float32)
+        v = (rng.standard_normal((rows, d)) * rng.uniform(0.1, 30, (1, d))).astype(np.float32)
+        k[:, 0] = 0.0                       # an all-zero coordinate: scale 1
+        v[:, 1] = np.round(v[:, 1])         # exact integers and halves
+        layer = oracle.pack_layer(kv, d, k, v, chunk)
+        wk, wv = oracle.layer_rows(kv, d, layer, rows, chunk)
+        ld = torch.from_numpy(np.frombuffer(bytes(layer), np.uint8).copy()).cuda()
+        gk = torch.full((rows, d), float("nan"), device="cuda")
+        gv = torch.full((rows, d), float("nan"), device="cuda")
+        gpu.layer_rows(kv, d, ld.data_ptr(), rows, chunk, gk.data_ptr(), gv.data_ptr())
+        assert np.array_equal(gk.cpu().numpy().view(np.uint32), wk.view(np.uint32)), (d, rows, chunk)
+        assert np.array_equal(gv.cpu().numpy().view(np.uint32), wv.view(np.uint32)), (d, rows, chunk)
+
+
+@pytest.mark.parametrize("kv", [0, 1, 2])
 def test_fit_on_device_matches_oracle(gpu, kv):
     import torch
     cfg = synth.config("full", icl_num_blocks=2)

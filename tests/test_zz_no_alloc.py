@@ -61,3 +61,9 @@ def test_noalloc_refuses_what_does_not_fit():
     with pytest.raises(tcu.TcuError) as e:
         tcu.attend_noalloc(0, 512, 4, x.data_ptr(), 10 ** 6, 256, x.data_ptr(), 1, x.data_ptr())
     assert "8192" in str(e.value)
+    # a misaligned pointer is refused before anything is launched (the records' scales are read as floats)
+    for args in [(x.data_ptr() + 2, x.data_ptr(), x.data_ptr()), (x.data_ptr(), x.data_ptr() + 1, x.data_ptr()),
+                 (x.data_ptr(), x.data_ptr(), x.data_ptr() + 6)]:
+        with pytest.raises(tcu.TcuError) as e:
+            tcu.attend_noalloc(1, 512, 4, args[0], 100, 256, args[1], 1, args[2])
+        assert e.value.code == -1 and "aligned" in str(e.value)
