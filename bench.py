@@ -142,18 +142,19 @@ class Clocks:
 
 # ---- the CPU leg: the oracle (a restatement of the reference's CPU path) ----------------------------------------
 
-def oracle_rows_per_s(model, kv, layers, scales, rows, h, target_s):
+def oracle_rows_per_s(model, kv, layers, scales, rows, h, target_s, outs=None):
     """Time the oracle's in-context stage on a bounded sample sized to about target_s seconds of CPU work."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
+    outs = outs or model.outs
     threads = oracle.threads()
     n = max(1, threads)
     t0 = time.perf_counter()
-    oracle.in_context(model, kv, layers, scales, rows, CHUNK, h[:n], model.outs)
+    oracle.in_context(model, kv, layers, scales, rows, CHUNK, h[:n], outs)
     dt = time.perf_counter() - t0
     n2 = int(min(h.shape[0], max(n, n * target_s / max(dt, 1e-3))))
     t0 = time.perf_counter()
-    oracle.in_context(model, kv, layers, scales, rows, CHUNK, h[:n2], model.outs)
+    oracle.in_context(model, kv, layers, scales, rows, CHUNK, h[:n2], outs)
     dt2 = time.perf_counter() - t0
     return n2 / dt2, n2, dt2, threads
 
@@ -199,8 +200,9 @@ def reference_arm(a):
         "impl": "reference", "metric": "predicted rows/sec (in-context stage, config 2)", "value": v,
         "unit": "rows/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": dt / a.steps * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic", "config": workload(a),
+        "dtype": "f32", "data": "synthetic", "config": dict(workload(a), parallelism=f"replicas{a.gpus}"),
         "cpu_baseline": {"value": v, "unit": "rows/s", "cores": threads, "kind": "port", "sample": sample},
+        "rows_timed_per_step": step_rows,
         "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "C restatement of the reference CPU path (oracle/): the reference is Rust and cargo is absent",
     }))
@@ -231,65 +233,139 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
-def multi_configs(pkg, synth, gpu, w, d, world, rank, stream, comm):
-    """BASELINE config 3 (8-member f32 ensemble, 10k-row caches, 65,536 test rows; members placed round-robin on the
-    devices, class-logit sums all-reduced in f64) and config 4 (100k-row i8 cache, 4,096 test rows, training rows
-    split over the devices with the attention merged every layer). One warm-up and one timed pass each (CUDA events,
-    max over ranks). Synthetic: seeded N(0,1) row representations, uniform labels; each member's cache is fitted
-    on the device from its own seeded rows (standing in for the per-member feature permutation)."""
+def stage_flops_per_row(N, d, L, ff, hid, heads, dff, outs):
+    """Algorithmic flops of one test row through the in-context stage (2 per multiply-add): attention 4 N d per
+    layer; Wq, Wo, the query MLP, W1, W2 per layer; the decoder."""
+    hd = d // heads
+    per_layer = 4.0 * N * d + 2.0 * (2 * d * d + 2 * d * ff + heads * 2 * hid * hd)
+    return L * per_layer + 2.0 * (d * dff + dff * outs)
+
+
+def multi_configs(pkg, synth, gpu, w, d, world, rank, stream, comm, a, bf16):
+    """BASELINE configs 3, 4 and 5. One warm-up and one timed pass each (CUDA events, max over ranks).
+
+    * config 3: an 8-member f32 ensemble of 10,000-row caches, 65,536 test rows; members placed round-robin on the
+      devices, class-logit sums all-reduced in f64. Rank 0 then re-fits every member alone and sums a slice of rows
+      in member order (table.rs:242-272): `max_diff_vs_sequential` is the largest difference of those sums.
+    * config 4: a 100,000-row i8 cache, 4,096 test rows, training rows split over the devices with the attention
+      merged every layer. At N > 1 rank 0 also keeps the whole cache and runs the unsharded stage on a slice of
+      rows: `max_diff_vs_unsharded`.
+    * config 5: the regressor (999 quantile outputs) over a 50,000-row i16 cache, 8,192 test rows, then the
+      quantile head (mean, variance, median, 5% and 95%); on every rank, as replicas. Rank 0 compares a slice of
+      rows with the oracle (`max_diff_vs_oracle`, in units of the target's spread).
+
+    Synthetic: seeded N(0,1) row representations, uniform labels (config 5: standard normal targets); each
+    member's cache is fitted on the device from its own seeded rows (standing in for the per-member feature
+    permutation). At N = 1 rank 0 also times the oracle on a bounded sample of each (`cpu_baseline`)."""
     import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
     sp = stream.cuda_stream
     res = {}
-    # config 3
+    L, ff, hid, heads, dff = 12, 1024, 64, 4, 1024
+    cfg = synth.config("full")
+    wt = synth.weights(cfg, seed=0)
+    om = None
+    if rank == 0:
+        om = oracle.Model({k: v for k, v in wt.items() if k.startswith("icl_predictor.")}, cfg["icl_nhead"],
+                          cfg["icl_num_blocks"], cfg["max_classes"])
+
+    def fit(n, kv, seed, classes=10, weights=w):
+        htr = torch.from_numpy(synth.row_reps(n, d, seed)).cuda()
+        if classes:
+            y = synth.labels(n, classes, seed + 100)
+        else:
+            y = np.random.default_rng(seed + 100).standard_normal(n).astype(np.float32)
+        ytr = torch.from_numpy(y).cuda()
+        vm = pkg.fit_icl(weights, htr.data_ptr(), ytr.data_ptr(), n, CHUNK, kv)
+        del htr, ytr
+        return vm
+
+    def layer_len(kv, n):
+        return pkg.record(kv, d, CHUNK) * (n // CHUNK) + (pkg.record(kv, d, n % CHUNK) if n % CHUNK else 0)
+
+    def cpu_sample(vm, kv, n, h, target_s, model=None, outs=10):
+        model = model or om
+        layers = [vm.layer_bytes(l, layer_len(kv, n)) for l in range(L)]
+        rps, rows, dt, threads = oracle_rows_per_s(model, kv, layers, vm.scales(), n, h, target_s, outs)
+        return {"value": rps, "unit": "rows/s", "cores": threads, "kind": "port",
+                "sample": f"{rows} test rows through the oracle's in-context stage, {dt:.1f} s"}
+
+    # ---- config 3 ----
     M, N3, R3, classes = 8, 10000, 65536, 10
     mine = [m for m in range(M) if m % world == rank]
-    models = []
-    for m in mine:
-        htr = torch.from_numpy(synth.row_reps(N3, d, 300 + m)).cuda()
-        ytr = torch.from_numpy(synth.labels(N3, classes, 400 + m)).cuda()
-        models.append(pkg.fit_icl(w, htr.data_ptr(), ytr.data_ptr(), N3, CHUNK, 0))
-        del htr, ytr
+    models = [fit(N3, 0, 300 + m) for m in mine]
     h3 = torch.from_numpy(synth.row_reps(R3, d, 500)).cuda()
     logits = torch.empty((R3, classes), device="cuda")
     sums = torch.zeros((R3, classes), dtype=torch.float64, device="cuda")
-    maps = [torch.tensor([(c + m) % classes for c in range(classes)], dtype=torch.int32, device="cuda") for m in mine]
+    maps = {m: torch.tensor([(c + m) % classes for c in range(classes)], dtype=torch.int32, device="cuda") for m in range(M)}
 
     def members_pass():
         sums.zero_()
-        for vm, mc in zip(models, maps):
+        for vm, m in zip(models, mine):
             vm.stage_device(h3.data_ptr(), R3, classes, logits.data_ptr(), sp)
             stream.synchronize()  # the class head runs (and waits) on the library's own stream
-            gpu.class_head(logits.data_ptr(), R3, classes, classes, mc.data_ptr(), sums.data_ptr())
+            gpu.class_head(logits.data_ptr(), R3, classes, classes, maps[m].data_ptr(), sums.data_ptr())
         if comm is not None:
             comm.allreduce_f64(sums.data_ptr(), sums.numel(), sp)
 
     members_pass()
     torch.cuda.synchronize()
     ms3 = max_over_ranks(ev_time(stream, members_pass, 1), world)
-    flops3 = 4.0 * N3 * d * 12 * R3 * M
-    res["config3_members"] = {
-        "workload": "BASELINE config 3: 8-member ensemble, f32 caches of 10,000 rows, 65,536 test rows, members "
-                    "round-robin over the devices, class-logit sums all-reduced (f64)",
-        "ms_per_pass": ms3, "rows_per_s": R3 / (ms3 / 1e3), "member_rows_per_s": R3 * M / (ms3 / 1e3),
-        "attention_tflops_per_gpu": flops3 / world / (ms3 / 1e3) / 1e12, "members_per_gpu": len(mine)}
+    fl3 = stage_flops_per_row(N3, d, L, ff, hid, heads, dff, classes) * R3 * M / world
+    r3 = {"workload": "BASELINE config 3: 8-member ensemble, f32 caches of 10,000 rows, 65,536 test rows, members "
+                      "round-robin over the devices, class-logit sums all-reduced (f64)",
+          "ms_per_pass": ms3, "rows_per_s": R3 / (ms3 / 1e3), "member_rows_per_s": R3 * M / (ms3 / 1e3),
+          "reading": "rows_per_s counts a row once for all 8 members (reading A); member_rows_per_s counts each "
+                     "member's row (reading B)",
+          "attention_tflops_per_gpu": 4.0 * N3 * d * L * R3 * M / world / (ms3 / 1e3) / 1e12,
+          "roofline": {"bound": "tensor", "achieved": fl3 / (ms3 / 1e3) / 1e12, "peak": bf16, "unit": "TFLOP/s",
+                       "frac": fl3 / (ms3 / 1e3) / 1e12 / bf16, "what": "whole stage per GPU, algorithmic flops"},
+          "members_per_gpu": len(mine)}
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        r3["cpu_baseline"] = cpu_sample(models[0], 0, N3, synth.row_reps(4096, d, 501), 6.0)
     for vm in models:
         vm.free()
+    if rank == 0:
+        # every member alone, in member order, on a slice of rows: the all-reduced sums must agree
+        S = 256
+        seq = torch.zeros((S, classes), dtype=torch.float64, device="cuda")
+        lg = torch.empty((S, classes), device="cuda")
+        for m in range(M):
+            vm = fit(N3, 0, 300 + m)
+            vm.stage_device(h3.data_ptr(), S, classes, lg.data_ptr(), sp)
+            stream.synchronize()
+            gpu.class_head(lg.data_ptr(), S, classes, classes, maps[m].data_ptr(), seq.data_ptr())
+            vm.free()
+        torch.cuda.synchronize()
+        r3["max_diff_vs_sequential"] = float((seq - sums[:S]).abs().max().item())
+        r3["max_abs_sum"] = float(seq.abs().max().item())
+    res["config3_members"] = r3
     del h3, logits, sums
-    # config 4
+
+    # ---- config 4 ----
     N4, R4 = 100000, 4096
-    htr = torch.from_numpy(synth.row_reps(N4, d, 600)).cuda()
-    ytr = torch.from_numpy(synth.labels(N4, classes, 601)).cuda()
-    full = pkg.fit_icl(w, htr.data_ptr(), ytr.data_ptr(), N4, CHUNK, 2)
-    del htr, ytr
+    full = fit(N4, 2, 600)
     nchunks = (N4 + CHUNK - 1) // CHUNK
+    h4 = torch.from_numpy(synth.row_reps(R4, d, 602)).cuda()
+    o4 = torch.empty((R4, classes), device="cuda")
+    ref = None
     if world > 1:
         first, count = pkg.shard_chunks(nchunks, world, rank)
         vm4 = full.slice(first, count)
+        if rank == 0:
+            S = 256
+            ref = torch.empty((S, classes), device="cuda")
+            full.stage_device(h4.data_ptr(), S, classes, ref.data_ptr(), sp)
+            torch.cuda.synchronize()
+            # and the oracle on the whole cache for a few of those rows (the unsharded stage may agree bit for bit:
+            # differences in the attention far below the residual stream's rounding step vanish in h += Wo att)
+            layers4 = [full.layer_bytes(l, layer_len(2, N4)) for l in range(L)]
+            want4 = oracle.in_context(om, 2, layers4, full.scales(), N4, CHUNK, h4[:16].cpu().numpy(), classes)
+            del layers4
         full.free()
     else:
         vm4 = full
-    h4 = torch.from_numpy(synth.row_reps(R4, d, 602)).cuda()
-    o4 = torch.empty((R4, classes), device="cuda")
 
     def sharded_pass():
         if world > 1:
@@ -300,14 +376,110 @@ def multi_configs(pkg, synth, gpu, w, d, world, rank, stream, comm):
     sharded_pass()
     torch.cuda.synchronize()
     ms4 = max_over_ranks(ev_time(stream, sharded_pass, 2), world)
-    flops4 = 4.0 * N4 * d * 12 * R4
-    res["config4_sharded"] = {
-        "workload": "BASELINE config 4: 100,000-row i8 cache (1.25 GB), 4,096 test rows, training rows split over "
-                    "the devices, attention merged every layer (all-reduce max, rescale, all-reduce sum)",
-        "ms_per_pass": ms4, "rows_per_s": R4 / (ms4 / 1e3),
-        "attention_tflops_per_gpu": flops4 / world / (ms4 / 1e3) / 1e12, "shard_rows": N4 // world}
+    fl4 = stage_flops_per_row(N4, d, L, ff, hid, heads, dff, classes) * R4
+    r4 = {"workload": "BASELINE config 4: 100,000-row i8 cache (1.25 GB), 4,096 test rows, training rows split over "
+                      "the devices, attention merged every layer (all-reduce max, rescale, all-reduce sum)",
+          "ms_per_pass": ms4, "rows_per_s": R4 / (ms4 / 1e3),
+          "attention_tflops_per_gpu": 4.0 * N4 * d * L * R4 / world / (ms4 / 1e3) / 1e12,
+          "roofline": {"bound": "tensor", "achieved": fl4 / world / (ms4 / 1e3) / 1e12, "peak": bf16,
+                       "unit": "TFLOP/s", "frac": fl4 / world / (ms4 / 1e3) / 1e12 / bf16,
+                       "what": "whole stage per GPU, algorithmic flops (dense layers counted once)"},
+          "shard_rows": N4 // world}
+    if ref is not None:
+        r4["max_diff_vs_unsharded"] = float((o4[:ref.shape[0]] - ref).abs().max().item())
+        r4["max_diff_vs_oracle"] = float(np.abs(o4[:16].cpu().numpy() - want4).max())
+        r4["max_abs_output"] = float(ref.abs().max().item())
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        r4["cpu_baseline"] = cpu_sample(vm4, 2, N4, synth.row_reps(1024, d, 603), 6.0)
+    res["config4_sharded"] = r4
     vm4.free()
+    del h4, o4
+
+    # ---- config 5 ----
+    cfg5 = synth.config("full", regression=True)
+    wt5 = synth.weights(cfg5, seed=5)
+    w5 = pkg.GpuWeights.from_tensors(gpu, synth.icl_shape(cfg5), {k: v for k, v in wt5.items() if k.startswith("icl_")},
+                                     for_fit=True)
+    N5, R5, NQ = 50000, 8192, 999
+    vm5 = fit(N5, 1, 700, classes=0, weights=w5)
+    h5 = torch.from_numpy(synth.row_reps(R5, d, 701 + rank)).cuda()
+    q5 = torch.empty((R5, NQ), device="cuda")
+    alphas = torch.tensor([0.05, 0.95], dtype=torch.float64, device="cuda")
+    outs5 = {k: torch.zeros(R5, dtype=torch.float64, device="cuda") for k in ("mean", "variance", "median")}
+    qs5 = torch.zeros((R5, 2), dtype=torch.float64, device="cuda")
+    tmean, tscale = 0.0, 1.0
+
+    def regress_pass():
+        for t in outs5.values():
+            t.zero_()
+        qs5.zero_()
+        vm5.stage_device(h5.data_ptr(), R5, NQ, q5.data_ptr(), sp)
+        stream.synchronize()
+        gpu.regression_head(q5.data_ptr(), R5, NQ, NQ, alphas.data_ptr(), 2, tmean, tscale, outs5["mean"].data_ptr(),
+                            outs5["variance"].data_ptr(), outs5["median"].data_ptr(), qs5.data_ptr())
+
+    regress_pass()
+    torch.cuda.synchronize()
+    ms5 = max_over_ranks(ev_time(stream, regress_pass, 1), world)
+    fl5 = stage_flops_per_row(N5, d, L, ff, hid, heads, dff, NQ) * R5
+    r5 = {"workload": "BASELINE config 5: regressor, 50,000-row i16 cache (1.24 GB), 8,192 test rows, 999 quantile "
+                      "outputs, then mean, variance, median and the 5%/95% quantiles (replicas on every device)",
+          "ms_per_pass": ms5, "rows_per_s": R5 * world / (ms5 / 1e3),
+          "roofline": {"bound": "tensor", "achieved": fl5 / (ms5 / 1e3) / 1e12, "peak": bf16, "unit": "TFLOP/s",
+                       "frac": fl5 / (ms5 / 1e3) / 1e12 / bf16, "what": "stage and head per GPU, algorithmic flops"},
+          "cache": "i16 (the reference's Kv has no f16 code: run as its i16 cache)"}
+    if rank == 0:
+        om5 = oracle.Model({k: v for k, v in wt5.items() if k.startswith("icl_predictor.")}, cfg5["icl_nhead"],
+                           cfg5["icl_num_blocks"], 0)
+        S = 64
+        layers5 = [vm5.layer_bytes(l, layer_len(1, N5)) for l in range(L)]
+        want = oracle.in_context(om5, 1, layers5, vm5.scales(), N5, CHUNK, h5[:S].cpu().numpy(), NQ)
+        got = q5[:S].cpu().numpy()
+        acc = oracle.regression_add(want, np.array([0.05, 0.95]), tmean, tscale)
+        dev = {k: t[:S].cpu().numpy() for k, t in outs5.items()}
+        r5["max_diff_vs_oracle"] = {
+            "quantile_outputs": float(np.abs(got - want).max()),
+            "mean": float(np.abs(dev["mean"] - acc["mean"]).max()),
+            "median": float(np.abs(dev["median"] - acc["median"]).max()),
+            "q05_q95": float(np.abs(qs5[:S].cpu().numpy() - acc["quantiles"]).max()),
+            "rows": S, "target_spread": tscale}
+        if world == 1 and not a.no_cpu_baseline:
+            r5["cpu_baseline"] = cpu_sample(vm5, 1, N5, h5.cpu().numpy(), 6.0, model=om5, outs=NQ)
+    res["config5_regressor"] = r5
+    vm5.free(), w5.free()
     return res
+
+
+def fit_baseline(pkg, synth, w, d, a):
+    """Fitting's in-context stage (fit.rs:577-747): the device fit of config 2's 10,000 rows (CUDA events), and the
+    oracle's fit on the host cores on a bounded sample of the same rows."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    cfg = synth.config("full")
+    wt = synth.weights(cfg, seed=0)
+    om = oracle.Model({k: v for k, v in wt.items() if k.startswith("icl_predictor.")}, cfg["icl_nhead"],
+                      cfg["icl_num_blocks"], cfg["max_classes"])
+    out = {}
+    for n in (a.train_rows, 2048):
+        hr = synth.row_reps(n, d, 1)
+        y = synth.labels(n, 10, 2)
+        hd, yd = torch.from_numpy(hr).cuda(), torch.from_numpy(y).cuda()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        vm = pkg.fit_icl(w, hd.data_ptr(), yd.data_ptr(), n, CHUNK, a.kv)  # synchronises at its end
+        out[f"device_{n}_rows_s"] = time.perf_counter() - t0
+        vm.free()
+    n = 2048
+    t0 = time.perf_counter()
+    oracle.icl_fit(om, synth.row_reps(n, d, 1), synth.labels(n, 10, 2), CHUNK, a.kv)
+    dt = time.perf_counter() - t0
+    out["cpu_baseline"] = {"value": n / dt, "unit": "training rows/s", "cores": oracle.threads(), "kind": "port",
+                           "sample": f"the oracle's in-context fit of {n} rows (12 layers, {KV_NAME[a.kv]} cache), "
+                                     f"{dt:.1f} s; its cost grows with the square of the rows"}
+    out["device_vs_cpu_at_2048_rows"] = dt / out["device_2048_rows_s"]
+    out["what"] = "fitting's in-context stage only (the column and row stages of fit are not on the device)"
+    return out
 
 
 # ---- our arm ---------------------------------------------------------------------------------------------------
@@ -484,7 +656,7 @@ def main():
                 uid.copy_(torch.frombuffer(bytearray(pkg.comm_unique_id()), dtype=torch.uint8))
             dist.broadcast(uid, 0)
             comm = pkg.Comm(gpu, bytes(uid.cpu().numpy().tobytes()), world, rank)
-        line["multi"] = multi_configs(pkg, synth, gpu, w, d, world, rank, stream, comm)
+        line["multi"] = multi_configs(pkg, synth, gpu, w, d, world, rank, stream, comm, a, bf16)
         if comm is not None:
             torch.cuda.synchronize()
             dist.barrier()
@@ -500,6 +672,7 @@ def main():
         line["cpu_baseline"] = {"value": rps, "unit": "rows/s", "cores": threads, "kind": "port",
                                 "sample": f"{n} test rows of the same workload through the oracle's in-context "
                                           f"stage, {dt:.1f} s"}
+        line["fit"] = fit_baseline(pkg, synth, w, d, a)
     if rank == 0:
         print(json.dumps(line))
     vm.free(), w.free(), gpu.close()
