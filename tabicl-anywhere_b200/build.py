@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libtabicl_b200.so")
 SOURCES = ["kernels.cu", "attend_tc.cu", "gemm_tc.cu", "stage_rows.cu", "qmlp_tc.cu", "engine.cpp", "tirs.cpp", "noalloc.cu"]
-HEADERS = ["device.cuh", "kernels.cuh", "tirs.hpp", "tc.cuh"]
+HEADERS = ["device.cuh", "kernels.cuh", "tirs.hpp", "tc.cuh", "stage_common.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-O3", "-std=c++17", "-lineinfo",
@@ -40,12 +40,17 @@ def build(force=False, verbose=False):
     objs = []
     bdir = os.path.join(HERE, "_build")
     os.makedirs(bdir, exist_ok=True)
+    # an object is rebuilt when it is older than its source, any header or this script
+    newest_dep = max(os.path.getmtime(p) for p in [os.path.join(CSRC, h) for h in HEADERS] +
+                     [os.path.join(HERE, "..", "include", "tabicl_b200.h"), os.path.abspath(__file__)])
     for src in SOURCES:
         obj = os.path.join(bdir, src + ".o")
-        cmd = [NVCC, *FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
-        if verbose:
-            print(" ".join(cmd))
-        subprocess.run(cmd, check=True)
+        path = os.path.join(CSRC, src)
+        if force or not os.path.exists(obj) or os.path.getmtime(obj) < max(newest_dep, os.path.getmtime(path)):
+            cmd = [NVCC, *FLAGS, "-c", path, "-o", obj]
+            if verbose:
+                print(" ".join(cmd))
+            subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = LIB + ".tmp"
     cmd = [NVCC, *FLAGS, "-shared", *objs, "-o", tmp]

@@ -21,6 +21,7 @@
 // leaves at its next barrier.
 #include "kernels.cuh"
 #include "device.cuh"
+#include "stage_common.cuh"
 #include "tc.cuh"
 
 #include <algorithm>
@@ -38,15 +39,9 @@ constexpr long long SPIN_LIMIT = 2000000000;  // cycles, about a second
 constexpr int TCACHE = 96;                    // a CTA's tile descriptors kept in shared memory
 
 template <int KV, int HD, int RM>
-struct Cfg {
-    static constexpr int W = KvFmt<KV>::W;
-    static constexpr int VB = KV == 2 ? 8 : 16;  // bytes of a coordinate's row a lane reads
-    static constexpr int EPV = VB / W;            // keys per lane vector: 4, 8, 8
-    static constexpr int TK = 8 * EPV;            // keys per tile: 32, 64, 64
-    static constexpr int ROWB = TK * W;           // bytes of one coordinate's keys in a tile: 128, 128, 64
-    static constexpr int DPT = HD / 32;           // coordinates per thread
-    static constexpr int SLOT = 2 * HD * ROWB + (KV ? 8 * HD : 0);  // keys, values, then key and value scales
-    static_assert(SLOT % 128 == 0 && (HD * ROWB) % 128 == 0, "tensor-load destinations must be 128-byte aligned");
+struct Cfg : TileFmt<KV, HD> {
+    using F = TileFmt<KV, HD>;
+    using F::W, F::VB, F::EPV, F::TK, F::ROWB, F::DPT, F::SLOT;
     static constexpr int BMAX = RM == 1 ? 8 : 1;  // tiles under one softmax step
     static constexpr int BT = BMAX * TK;
     // scratch (floats), shared by the linear phases and the attention phase
@@ -57,17 +52,6 @@ struct Cfg {
     static constexpr int SCRATCH = ATT_END > LIN_END ? ATT_END : LIN_END;
     static_assert(WARPS * TK >= 4 * HID && WARPS * TK >= 256, "reduction scratch too small for the query MLP");
 };
-
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ int ld_relaxed_s32(const int *p) {
-    int v;
-    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 // Grid barrier on a counter zeroed before the launch, in two halves. arrive(): after a phase's stores, one thread per
 // CTA adds one (release). wait(): one thread waits (acquire) until the counter reaches G times the barrier's number.
@@ -104,62 +88,6 @@ __device__ bool grid_wait(const RowsArgs &a, unsigned target, int *flag_s) {
     }
     __syncthreads();
     return *flag_s != 0;
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *mbar, uint32_t bytes) {
-    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}\n" ::"r"(
-                     tc::smem_addr(mbar)),
-                 "r"(bytes)
-                 : "memory");
-}
-// Box of a 3-D / 2-D tensor map (coordinates innermost first) into shared memory, completing on the mbarrier.
-__device__ __forceinline__ void tma_load3(void *dst, const void *tmap, int x, int y, int z, uint64_t *mbar,
-                                          uint64_t pol) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(tc::smem_addr(dst)),
-        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(tc::smem_addr(mbar)), "l"(pol)
-        : "memory");
-}
-__device__ __forceinline__ void tma_load2(void *dst, const void *tmap, int x, int y, uint64_t *mbar, uint64_t pol) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(tc::smem_addr(dst)),
-        "l"(tmap), "r"(x), "r"(y), "r"(tc::smem_addr(mbar)), "l"(pol)
-        : "memory");
-}
-// Contiguous bytes (16-byte aligned, a multiple of 16) into shared memory, completing on the mbarrier.
-__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *mbar, uint64_t pol) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-            tc::smem_addr(dst)),
-        "l"(src), "r"(bytes), "r"(tc::smem_addr(mbar)), "l"(pol)
-        : "memory");
-}
-
-template <int VB>
-__device__ __forceinline__ uint4 lds_vec(const uint8_t *p) {
-    if (VB == 16) return *reinterpret_cast<const uint4 *>(p);
-    const uint2 v = *reinterpret_cast<const uint2 *>(p);
-    return make_uint4(v.x, v.y, 0u, 0u);
-}
-
-// x[0..7] are this lane's partial sums for rows 0..7; lanes v = 0..7 (low three lane bits) end with the full sum of
-// row v.
-__device__ __forceinline__ float reduce_scatter8(const float (&x)[8], int v) {
-    float y[4], z[2];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const float send = (v & 4) ? x[i] : x[i + 4], keep = (v & 4) ? x[i + 4] : x[i];
-        y[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-        const float send = (v & 2) ? y[i] : y[i + 2], keep = (v & 2) ? y[i + 2] : y[i];
-        z[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-    }
-    const float send = (v & 1) ? z[0] : z[1], keep = (v & 1) ? z[1] : z[0];
-    return keep + __shfl_xor_sync(0xffffffffu, send, 1);
 }
 
 template <int KV, int HD, int RM>
@@ -226,7 +154,8 @@ struct Stage {
         const uint8_t *rec = lay[l].cache + (size_t)ci * a.full;
         uint8_t *slot = ring + (size_t)s * C::SLOT;
         uint64_t *mb = mbar + s;
-        tc::fence_async_smem();  // the slot's earlier reads (generic proxy) before the loads (async proxy)
+        // no proxy fence: the slot was only read (ordinary loads, done before the CTA barrier that freed it); a proxy
+        // fence here would wait for every copy still in flight, so that the tiles would arrive one after another
         mbar_expect_tx(mb, 2u * HD * C::ROWB + (KV ? 8u * HD : 0u));
         const uint8_t *maps = reinterpret_cast<const uint8_t *>(a.tmaps) + (size_t)l * 256;
         if (ci < a.nfull) {

@@ -170,6 +170,14 @@ def test_give_up_is_reported_and_the_next_call_recovers(gpu):
     vm.stage_device(hd.data_ptr(), 3, 10, out.data_ptr())
     gpu.sync()
     assert np.array_equal(out.cpu().numpy(), want)
+    # one row (the one-kernel stage's one-row form): the same report and recovery
+    one = vm.stage(ht[:1], 10)
+    assert np.abs(one - oracle.in_context(m, kv, layers, scales, n, chunk, ht[:1], 10)).max() < STAGE
+    gpu.debug_abort_next()
+    with pytest.raises(tcu.TcuError) as e:
+        vm.stage(ht[:1], 10)
+    assert e.value.code == -3 and "left after another CTA gave up" in str(e.value)
+    assert np.array_equal(vm.stage(ht[:1], 10), one)
     vm.free(), w.free()
 
 
