@@ -50,6 +50,17 @@ class OrModel(ctypes.Structure):
                 ("dec2b", _fp), ("icl_y", _fp)]
 
 
+class OrCBlock(ctypes.Structure):
+    _fields_ = [(n, _fp) for n in ("n1w", "n1b", "inw", "inb", "ow", "ob", "n2w", "n2b", "w1", "b1", "w2", "b2")] + \
+               [("ff", ctypes.c_int)]
+
+
+class OrRowsModel(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("e", "group", "inds", "cls", "col_heads", "row_heads", "ncol", "nrow")] + \
+               [("in_w", _fp), ("in_b", _fp), ("col", _P(OrCBlock)), ("cls_tokens", _fp), ("row", _P(OrCBlock)),
+                ("rope_freqs", _fp), ("out_lnw", _fp), ("out_lnb", _fp)]
+
+
 def lib():
     global _lib
     if _lib is None:
@@ -73,6 +84,8 @@ def lib():
             "or_add_member": (None, [_P(d), _fp, i, i, i, _P(ctypes.c_int32)]),
             "or_finish_proba": (None, [_P(d), i, i, i, d]),
             "or_regression_add": (None, [_fp, i, i, i, _P(d), i, d, d, _P(d), _P(d), _P(d), _P(d)]),
+            "or_embed": (None, [_P(OrRowsModel), _fp, i, i, _fp, i, _fp]),
+            "or_represent": (None, [_P(OrRowsModel), _fp, i, i, _fp]),
             "or_threads": (i, []),
             "or_set_threads": (None, [i]),
         }
@@ -151,6 +164,80 @@ class Model:
         out = np.empty(self.d, np.float32)
         lib().or_query_scale(self.ref, l, n, _p(out))
         return out
+
+
+class RowsModel:
+    """The column and row stages of a weight bundle as the oracle sees them (src/model.rs:199-245: the column
+    blocks' second attention, the class tokens, the row blocks, the rotary frequencies, the final LayerNorm)."""
+
+    def __init__(self, tensors, cfg):
+        g = lambda n: np.ascontiguousarray(tensors[n], dtype=np.float32).reshape(-1)
+        self._keep = []
+        keep = self._keep
+
+        def k(a):
+            a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+            keep.append(a)
+            return _p(a)
+
+        e = g("col_embedder.in_linear.bias").size
+
+        def block(p):
+            b = OrCBlock()
+            opt = lambda n: g(p + n) if p + n in tensors else np.zeros(e, np.float32)
+            b.n1w, b.n1b = k(g(p + "norm1.weight")), k(opt("norm1.bias"))
+            b.inw, b.inb = k(g(p + "attn.in_proj_weight")), k(g(p + "attn.in_proj_bias"))
+            b.ow, b.ob = k(g(p + "attn.out_proj.weight")), k(g(p + "attn.out_proj.bias"))
+            b.n2w, b.n2b = k(g(p + "norm2.weight")), k(opt("norm2.bias"))
+            b.w1, b.b1 = k(g(p + "linear1.weight")), k(g(p + "linear1.bias"))
+            b.w2, b.b2 = k(g(p + "linear2.weight")), k(g(p + "linear2.bias"))
+            b.ff = g(p + "linear1.bias").size
+            return b
+
+        ncol, nrow = cfg["col_num_blocks"], cfg["row_num_blocks"]
+        cols = (OrCBlock * ncol)(*[block(f"col_embedder.tf_col.blocks.{i}.multihead_attn2.") for i in range(ncol)])
+        rows = (OrCBlock * nrow)(*[block(f"row_interactor.tf_row.blocks.{i}.") for i in range(nrow)])
+        self._blocks = (cols, rows)
+        m = OrRowsModel()
+        m.e, m.group, m.inds, m.cls = e, cfg["col_feature_group_size"], cfg["col_num_inds"], cfg["row_num_cls"]
+        m.col_heads, m.row_heads, m.ncol, m.nrow = cfg["col_nhead"], cfg["row_nhead"], ncol, nrow
+        m.in_w, m.in_b = k(g("col_embedder.in_linear.weight")), k(g("col_embedder.in_linear.bias"))
+        m.col, m.row = ctypes.cast(cols, _P(OrCBlock)), ctypes.cast(rows, _P(OrCBlock))
+        m.cls_tokens, m.rope_freqs = k(g("row_interactor.cls_tokens")), k(g("row_interactor.tf_row.rope.freqs"))
+        m.out_lnw = k(g("row_interactor.out_ln.weight"))
+        m.out_lnb = k(g("row_interactor.out_ln.bias") if "row_interactor.out_ln.bias" in tensors else np.zeros(e, np.float32))
+        self.m = m
+        self.e, self.cls, self.inds, self.ncol, self.nrow = e, m.cls, m.inds, ncol, nrow
+
+    @property
+    def ref(self):
+        return ctypes.byref(self.m)
+
+
+def rows_model_from_bundle(b):
+    import json
+    cfg = json.loads(bytes(b["config.json"]).decode())
+    return RowsModel({n: b[n] for n in b.names() if n.startswith(("col_embedder.", "row_interactor."))}, cfg)
+
+
+def embed(rm, x, col_kv, digits=1):
+    """predict.rs:282-353: normalised test rows x [n][features] to tokens [n][cls + features][e]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, feats = x.shape
+    ck = np.ascontiguousarray(col_kv, dtype=np.float32).reshape(-1)
+    assert ck.size == feats * digits * rm.ncol * 2 * rm.e * rm.inds
+    tok = np.empty((n, rm.cls + feats, rm.e), np.float32)
+    lib().or_embed(rm.ref, _p(x), n, feats, _p(ck), digits, _p(tok))
+    return tok
+
+
+def represent(rm, tok):
+    """predict.rs:356-372: tokens [n][tokens][e] to row representations [n][cls e]."""
+    tok = np.array(tok, dtype=np.float32)  # a copy: consumed
+    n, tokens, e = tok.shape
+    rep = np.empty((n, rm.cls * e), np.float32)
+    lib().or_represent(rm.ref, _p(tok), n, tokens, _p(rep))
+    return rep
 
 
 def model_from_bundle(b):

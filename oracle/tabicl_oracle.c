@@ -821,3 +821,202 @@ EXPORT void or_regression_add(const float *qout, int n, int nq, int stride, cons
     j.tscale = target_scale, j.mean = mean, j.variance = variance, j.median = median, j.quantiles = quantiles;
     par_for(n, reg_one, &j);
 }
+
+/* ---- the column and row stages of prediction (predict.rs:282-372, nn.rs:291-419) --------------------------- */
+
+/* One pre-norm block of the column or row stage (model.rs:27-98 Block): in_w is [3e][e] (the query's rows first),
+ * no scalable softmax (the column stage's second attention and the row blocks have none). */
+typedef struct {
+    const float *n1w, *n1b, *inw, *inb, *ow, *ob, *n2w, *n2b, *w1, *b1, *w2, *b2;
+    int ff;
+} or_cblock;
+
+typedef struct {
+    int e, group, inds, cls, col_heads, row_heads, ncol, nrow;
+    const float *in_w, *in_b;         /* col_embedder.in_linear: [e][group], [e] */
+    const or_cblock *col;             /* the column blocks' second attention (multihead_attn2), ncol */
+    const float *cls_tokens;          /* [cls][e] */
+    const or_cblock *row;             /* nrow */
+    const float *rope_freqs;          /* [row head width / 2] */
+    const float *out_lnw, *out_lnb;   /* row_interactor.out_ln: [e] */
+} or_rows_model;
+
+/* nn.rs:156-164 feed_forward: x += l2(gelu(l1(norm2 x))); t [e], h [ff] scratch */
+static void feed_forward_c(const or_cblock *b, int e, float *x, float *t, float *h) {
+    layer_norm(x, b->n2w, b->n2b, e, t);
+    linear(b->w1, b->b1, t, e, b->ff, h);
+    gelu_inplace(h, b->ff);
+    linear(b->w2, b->b2, h, b->ff, e, t);
+    for (int i = 0; i < e; i++) x[i] += t[i];
+}
+
+/* nn.rs:289-302 cached_block: x against n fixed keys/values kt, vt ([e][n]), queries scaled by `scale` (no
+ * scalable softmax: nn.rs:136-141), then out-projection, residual and feed-forward. */
+static void cached_block(const or_cblock *b, int e, int heads, const float *scale, const float *kt, const float *vt, int n,
+                         float *x, float *t, float *q, float *h, float *sc, float *tmp, soft *st) {
+    layer_norm(x, b->n1w, b->n1b, e, t);
+    linear(b->inw, b->inb, t, e, e, q);
+    for (int i = 0; i < e; i++) q[i] *= scale[i];
+    soft_reset(st);
+    soft_update_f32(st, q, kt, vt, n, sc, tmp);
+    soft_finish(st);
+    linear(b->ow, b->ob, st->acc, e, e, t);
+    for (int i = 0; i < e; i++) x[i] += t[i];
+    feed_forward_c(b, e, x, t, h);
+}
+
+/* nn.rs:422-429 group_values: the features one, two, four, ... places to the right of g, wrapping round */
+static void group_values(const float *row, int feats, int g, int size, float *out) {
+    for (int i = 0; i < size; i++) out[i] = row[(g + (1 << i)) % feats];
+}
+
+typedef struct {
+    const or_rows_model *m;
+    const float *x, *col_kv;
+    int feats, digits;
+    float *tok;
+} embed_job;
+
+static void embed_one(void *ctx, int r) {
+    const embed_job *j = (const embed_job *)ctx;
+    const or_rows_model *m = j->m;
+    const int e = m->e, inds = m->inds, nb = m->ncol, tokens = m->cls + j->feats, hd = e / m->col_heads;
+    int ffmax = 0;
+    for (int b = 0; b < nb; b++) ffmax = m->col[b].ff > ffmax ? m->col[b].ff : ffmax;
+    float *tok = j->tok + (size_t)r * tokens * e;
+    memcpy(tok, m->cls_tokens, sizeof(float) * m->cls * e);
+    float *scale = malloc(sizeof(float) * e), *t = malloc(sizeof(float) * e), *q = malloc(sizeof(float) * e);
+    float *h = malloc(sizeof(float) * ffmax), *sc = malloc(sizeof(float) * inds), *tmp = malloc(sizeof(float) * hd);
+    float *plain = malloc(sizeof(float) * e), *sum = malloc(sizeof(float) * e), *one = malloc(sizeof(float) * e);
+    float vals[8];
+    soft st;
+    st.heads = m->col_heads, st.d = e;
+    st.m = malloc(sizeof(float) * m->col_heads), st.s = malloc(sizeof(float) * m->col_heads), st.acc = malloc(sizeof(float) * e);
+    for (int i = 0; i < e; i++) scale[i] = 1.0f / sqrtf((float)hd);
+    const size_t per = (size_t)2 * e * inds, rec = (size_t)j->digits * nb * per;
+    for (int g = 0; g < j->feats; g++) {
+        float *cell = tok + (size_t)(m->cls + g) * e;
+        group_values(j->x + (size_t)r * j->feats, j->feats, g, m->group, vals);
+        int missing = 1;
+        for (int i = 0; i < m->group; i++) missing &= vals[i] == -100.0f;
+        if (missing)
+            for (int i = 0; i < e; i++) cell[i] = -100.0f;
+        else
+            linear(m->in_w, m->in_b, vals, m->group, e, cell);
+        const float *recs = j->col_kv + (size_t)g * rec;
+        if (j->digits == 1) {
+            for (int b = 0; b < nb; b++)
+                cached_block(&m->col[b], e, m->col_heads, scale, recs + b * per, recs + b * per + (size_t)e * inds, inds, cell,
+                             t, q, h, sc, tmp, &st);
+        } else {
+            /* once per label digit, then the average (predict.rs:326-346) */
+            memcpy(plain, cell, sizeof(float) * e);
+            memset(sum, 0, sizeof(float) * e);
+            for (int dg = 0; dg < j->digits; dg++) {
+                memcpy(one, plain, sizeof(float) * e);
+                for (int b = 0; b < nb; b++) {
+                    const float *at = recs + (size_t)(dg * nb + b) * per;
+                    cached_block(&m->col[b], e, m->col_heads, scale, at, at + (size_t)e * inds, inds, one, t, q, h, sc, tmp, &st);
+                }
+                for (int i = 0; i < e; i++) sum[i] += one[i];
+            }
+            for (int i = 0; i < e; i++) cell[i] = sum[i] / (float)j->digits;
+        }
+    }
+    free(scale), free(t), free(q), free(h), free(sc), free(tmp), free(plain), free(sum), free(one);
+    free(st.m), free(st.s), free(st.acc);
+}
+
+/* predict.rs:282-353 embed: test rows x [n][feats] (normalised, missing cells -100) to their tokens
+ * [n][cls + feats][e], class tokens first; col_kv as fit.rs:230 stores it: [feats][digits][blocks][2][e][inds]. */
+EXPORT void or_embed(const or_rows_model *m, const float *x, int n, int feats, const float *col_kv, int digits, float *tok) {
+    embed_job j;
+    j.m = m, j.x = x, j.col_kv = col_kv, j.feats = feats, j.digits = digits, j.tok = tok;
+    par_for(n, embed_one, &j);
+}
+
+typedef struct {
+    const or_rows_model *m;
+    float *tok, *rep;
+    int tokens;
+    const float *cosv, *sinv;
+} represent_job;
+
+/* nn.rs:357-419 row_forward for one row */
+static void represent_one(void *ctx, int r) {
+    const represent_job *jb = (const represent_job *)ctx;
+    const or_rows_model *m = jb->m;
+    const int d = m->e, heads = m->row_heads, hd = d / heads, half = hd / 2, tokens = jb->tokens;
+    const float inv = 1.0f / sqrtf((float)hd);
+    int ffmax = 0;
+    for (int b = 0; b < m->nrow; b++) ffmax = m->row[b].ff > ffmax ? m->row[b].ff : ffmax;
+    float *tok = jb->tok + (size_t)r * tokens * d, *out = jb->rep + (size_t)r * m->cls * d;
+    float *tn = malloc(sizeof(float) * d), *qkv = malloc(sizeof(float) * 3 * d);
+    float *q = malloc(sizeof(float) * tokens * d), *kt = malloc(sizeof(float) * tokens * d), *vt = malloc(sizeof(float) * tokens * d);
+    float *nw = malloc(sizeof(float) * tokens * d), *sc = malloc(sizeof(float) * tokens), *att = malloc(sizeof(float) * d);
+    float *tmp = malloc(sizeof(float) * hd), *h = malloc(sizeof(float) * ffmax);
+    for (int bi = 0; bi < m->nrow; bi++) {
+        const or_cblock *b = &m->row[bi];
+        const int nq = bi == m->nrow - 1 ? m->cls : tokens;
+        for (int t = 0; t < tokens; t++) {
+            layer_norm(tok + (size_t)t * d, b->n1w, b->n1b, d, tn);
+            if (t < nq)
+                linear(b->inw, b->inb, tn, d, 3 * d, qkv);
+            else
+                linear(b->inw + (size_t)d * d, b->inb + d, tn, d, 2 * d, qkv + d);
+            const float *cs = jb->cosv + (size_t)t * half, *sn = jb->sinv + (size_t)t * half;
+            for (int hh = 0; hh < heads; hh++) {
+                if (t < nq) {
+                    const float *src = qkv + hh * hd;
+                    float *dst = q + (size_t)t * d + hh * hd;
+                    for (int i = 0; i < half; i++) {
+                        const float a = src[i], c = src[i + half];
+                        dst[i] = (a * cs[i] - c * sn[i]) * inv;
+                        dst[i + half] = (c * cs[i] + a * sn[i]) * inv;
+                    }
+                }
+                const float *src = qkv + d + hh * hd;
+                for (int i = 0; i < half; i++) {
+                    const float a = src[i], c = src[i + half];
+                    kt[(size_t)(hh * hd + i) * tokens + t] = a * cs[i] - c * sn[i];
+                    kt[(size_t)(hh * hd + i + half) * tokens + t] = c * cs[i] + a * sn[i];
+                }
+            }
+            for (int jj = 0; jj < d; jj++) vt[(size_t)jj * tokens + t] = qkv[2 * d + jj];
+        }
+        for (int t = 0; t < nq; t++) {
+            for (int hh = 0; hh < heads; hh++) {
+                const float *ks = kt + (size_t)hh * hd * tokens, *vs = vt + (size_t)hh * hd * tokens;
+                memset(sc, 0, sizeof(float) * tokens);
+                weighted_sum(q + (size_t)t * d + hh * hd, ks, hd, tokens, sc);
+                const float top = vmax(sc, tokens);
+                const float s = 1.0f / exp_shift_sum(sc, tokens, top);
+                matvec(vs, sc, tokens, hd, tmp);
+                for (int i = 0; i < hd; i++) att[hh * hd + i] = tmp[i] * s;
+            }
+            float *x = nw + (size_t)t * d;
+            linear(b->ow, b->ob, att, d, d, x);
+            for (int i = 0; i < d; i++) x[i] += tok[(size_t)t * d + i];
+            feed_forward_c(b, d, x, tn, h);
+        }
+        memcpy(tok, nw, sizeof(float) * (size_t)nq * d);
+    }
+    for (int c = 0; c < m->cls; c++) layer_norm(tok + (size_t)c * d, m->out_lnw, m->out_lnb, d, out + (size_t)c * d);
+    free(tn), free(qkv), free(q), free(kt), free(vt), free(nw), free(sc), free(att), free(tmp), free(h);
+}
+
+/* predict.rs:356-372 represent: tokens [n][tokens][e] (consumed) to row representations [n][cls e]; the rotary
+ * tables of nn.rs:304-321 (cos and sin of position times frequency, in f32). */
+EXPORT void or_represent(const or_rows_model *m, float *tok, int n, int tokens, float *rep) {
+    const int half = m->e / m->row_heads / 2;
+    float *cosv = malloc(sizeof(float) * tokens * half), *sinv = malloc(sizeof(float) * tokens * half);
+    for (int p = 0; p < tokens; p++)
+        for (int i = 0; i < half; i++) {
+            const float a = (float)p * m->rope_freqs[i];
+            cosv[p * half + i] = cosf(a), sinv[p * half + i] = sinf(a);
+        }
+    represent_job j;
+    j.m = m, j.tok = tok, j.rep = rep, j.tokens = tokens, j.cosv = cosv, j.sinv = sinv;
+    par_for(n, represent_one, &j);
+    free(cosv), free(sinv);
+}

@@ -54,6 +54,21 @@ def to_rows(ref, heads, n, hd):
     return np.ascontiguousarray(np.asarray(ref, np.float32).reshape(heads, n, hd).transpose(1, 0, 2).reshape(n, heads * hd))
 
 
+def golden_col_kv(fx, rm, heads):
+    """The reference dump's column-stage keys/values (col_k{b}, col_v{b}: [columns][heads][inducing][head width],
+    class-token columns first) as a fitted bundle's col_kv stores them (fit.rs:230): [features][1][blocks][2][e][inds]
+    (tests/reference.rs:56-72 reorders the same way)."""
+    feats = fx["x_test"].shape[1]
+    e, inds = rm.e, rm.inds
+    ck = np.zeros((feats, 1, rm.ncol, 2, e, inds), np.float32)
+    for b in range(rm.ncol):
+        for which, kind in enumerate(("col_k", "col_v")):
+            r = np.asarray(fx[f"{kind}{b}"], np.float32)
+            for g in range(feats):
+                ck[g, 0, b, which] = r[g + rm.cls].transpose(0, 2, 1).reshape(e, inds)
+    return ck
+
+
 @pytest.fixture(scope="session")
 def tiny():
     """The reference's tiny classifier and its golden in-context numbers (tests/golden, from tests/data)."""
@@ -65,5 +80,9 @@ def tiny():
     k = [to_rows(fx[f"icl_k{l}"], m.heads, n, hd) for l in range(m.layers)]
     v = [to_rows(fx[f"icl_v{l}"], m.heads, n, hd) for l in range(m.layers)]
     scales = np.stack([m.query_scale(l, n) for l in range(m.layers)])
+    rm = oracle.rows_model_from_bundle(wb)
+    cfg = __import__("json").loads(bytes(wb["config.json"]).decode())
     return dict(wb=wb, fx=fx, m=m, n=n, k=k, v=v, scales=scales, path=os.path.join(GOLDEN, "tiny-clf.tirs"),
-                test_rep=np.array(fx["test_rep"], np.float32), logits=np.array(fx["logits"], np.float32))
+                test_rep=np.array(fx["test_rep"], np.float32), logits=np.array(fx["logits"], np.float32),
+                rm=rm, col_kv=golden_col_kv(fx, rm, cfg["col_nhead"]), x_test=np.array(fx["x_test"], np.float32),
+                test_emb=np.array(fx["test_emb"], np.float32))

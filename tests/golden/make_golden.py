@@ -6,9 +6,11 @@ tabicl-anywhere repository is available; the outputs are committed and the GPU b
 * tiny-clf.tirs / tiny-reg.tirs: the reference's tiny random TabICL checkpoints (tests/data/tiny-{clf,reg}.ckpt,
   made by its tools/make_tiny.py) as weight bundles: every tensor of the state dict as float32 plus
   config.json, the layout its tools/export_weights.py writes.
-* tiny-raw-icl.tirs: the in-context part of the reference's golden dump tests/data/tiny-raw.tirs (PyTorch
+* tiny-raw-icl.tirs: the prediction side of the reference's golden dump tests/data/tiny-raw.tirs (PyTorch
   TabICL's own numbers for the tiny classifier): training and test row representations, training labels, the
-  in-context keys/values of every layer ([heads][rows][head width]) and the logits.
+  in-context keys/values of every layer ([heads][rows][head width]) and the logits; and for the column and row
+  stages the normalised test rows, the column stage's cached keys/values of every block ([columns][heads][inducing
+  points][head width], the class-token columns first) and the test rows' tokens after the column stage.
 """
 import json
 import os
@@ -39,8 +41,8 @@ def main(ref):
     weights(os.path.join(data, "tiny-clf.ckpt"), os.path.join(HERE, "tiny-clf.tirs"))
     weights(os.path.join(data, "tiny-reg.ckpt"), os.path.join(HERE, "tiny-reg.tirs"))
     raw = tirs.Bundle(os.path.join(data, "tiny-raw.tirs"))
-    keep = ["train_rep", "y_train", "test_rep", "logits"]
-    keep += [n for n in raw.names() if n.startswith("icl_k") or n.startswith("icl_v")]
+    keep = ["train_rep", "y_train", "test_rep", "logits", "x_test", "test_emb"]
+    keep += [n for n in raw.names() if n.startswith(("icl_k", "icl_v", "col_k", "col_v"))]
     out = os.path.join(HERE, "tiny-raw-icl.tirs")
     tirs.write(out, {n: np.array(raw[n]) for n in keep})
     print(out, keep)

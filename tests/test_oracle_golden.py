@@ -205,3 +205,49 @@ def test_quantile_distribution():
             assert abs(acc["quantiles"][r, a] - (float(qs[a]) * 2.0 + 50.0)) < 1e-3
     # a straight line of quantiles: the median is its middle
     assert abs(acc["median"][4] - 50.0) < 1e-5
+
+
+# ---- the column and row stages (predict.rs:282-372) against PyTorch's numbers ------------------------------------
+
+TINY = 5e-5  # tests/reference.rs:148
+
+
+def test_column_stage_matches_reference(tiny):
+    """embed on the dump's normalised test rows and its column-stage cache gives the dump's test embeddings
+    (the feature cells; tests/reference.rs:96-105 compares the same part), the class tokens first."""
+    t = tiny
+    rm = t["rm"]
+    tok = oracle.embed(rm, t["x_test"], t["col_kv"])
+    assert np.abs(tok[:, rm.cls:] - t["test_emb"][:, rm.cls:]).max() < TINY
+    assert np.array_equal(tok[:, :rm.cls], np.broadcast_to(np.asarray(t["wb"]["row_interactor.cls_tokens"]).reshape(rm.cls, rm.e), tok[:, :rm.cls].shape))
+
+
+def test_row_stage_matches_reference(tiny):
+    t = tiny
+    rm = t["rm"]
+    tok = oracle.embed(rm, t["x_test"], t["col_kv"])
+    rep = oracle.represent(rm, tok)
+    assert np.abs(rep - t["test_rep"]).max() < TINY
+
+
+def test_normalised_rows_to_logits(tiny):
+    """The whole prediction of one member from normalised features: column stage, row stage, in-context stage on
+    the dump's in-context cache, against the dump's logits (tests/reference.rs:107-116)."""
+    t = tiny
+    rm, m = t["rm"], t["m"]
+    rep = oracle.represent(rm, oracle.embed(rm, t["x_test"], t["col_kv"]))
+    layers = [oracle.pack_layer(0, m.d, t["k"][l], t["v"][l], 48) for l in range(m.layers)]
+    logits = oracle.in_context(m, 0, layers, t["scales"], t["n"], 48, rep, t["logits"].shape[1])
+    assert np.abs(logits - t["logits"]).max() < TINY
+
+
+def test_digit_average_of_identical_caches_is_the_plain_stage(tiny):
+    """With several label digits the column stage runs once per digit and averages (predict.rs:326-346): the same
+    cache for every digit gives the one-digit answer up to the average's rounding."""
+    t = tiny
+    rm = t["rm"]
+    one = oracle.embed(rm, t["x_test"], t["col_kv"])
+    ck = t["col_kv"]
+    three = np.concatenate([ck, ck, ck], axis=1)
+    got = oracle.embed(rm, t["x_test"], three, digits=3)
+    assert np.abs(got - one).max() < 1e-5
