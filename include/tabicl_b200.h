@@ -53,6 +53,13 @@ typedef struct {
     int32_t d, heads, layers, ff, hid, dec_ff, outs, max_classes;
 } tcu_icl_shape;
 
+/* Sizes of the column and row stages (src/model.rs:199-245): width e, features per group, inducing points, class
+ * tokens, heads of the column stage's attention and of the row blocks, column blocks (ISABs) and row blocks, and
+ * their feed-forward widths (linear1 rows). */
+typedef struct {
+    int32_t e, group, inds, cls, col_heads, row_heads, col_blocks, row_blocks, col_ff, row_ff;
+} tcu_rows_shape;
+
 /* ---- context ---------------------------------------------------------------------------------------------- */
 
 /* Open device `device` (gpu::Gpu::new_async, src/gpu.rs:930-971). */
@@ -77,6 +84,12 @@ TCU_API int tcu_weights_ready(tcu_weights *w);
 /* The whole of the above from a weight bundle file (Model::load, src/model.rs:202-272, in-context part). */
 TCU_API int tcu_weights_from_bundle(tcu_ctx *ctx, const char *path, int for_fit, tcu_weights **out);
 TCU_API int tcu_weights_shape(const tcu_weights *w, tcu_icl_shape *out);
+/* Also keep the column and row stages of this shape (their tensors "col_embedder.*" and "row_interactor.*" put with
+ * tcu_weights_put; only the column blocks' second attention is needed, src/model.rs:226-231): call before
+ * tcu_weights_ready. tcu_weights_from_bundle does this itself when the bundle has them. */
+TCU_API int tcu_weights_set_rows_shape(tcu_weights *w, const tcu_rows_shape *shape);
+/* The column and row stages' sizes; TCU_DECLINED when the weights have none. */
+TCU_API int tcu_weights_rows_shape(const tcu_weights *w, tcu_rows_shape *out);
 TCU_API void tcu_weights_free(tcu_weights *w);
 
 /* ---- resident caches (VramTier::preload / Gpu::load, src/gpu.rs:2546-2556, 2062-2116) ------------------------ */
@@ -89,7 +102,11 @@ TCU_API int tcu_model_new(tcu_weights *w, const int32_t meta[7], int32_t node_ro
 TCU_API int tcu_model_put_scales(tcu_model *m, const float *scales, size_t count);
 /* Bytes [offset, offset + nbytes) of `n{node}_kv{layer}`, exactly as stored (no repacking; src/fit.rs:224-241). */
 TCU_API int tcu_model_put_layer(tcu_model *m, int layer, size_t offset, const void *bytes, size_t nbytes);
-/* The whole of the above from a fitted bundle file, member `prefix` ("m0/", or "" for a raw fit), problem node. */
+/* The column stage's cache `m{i}/col_kv` (src/fit.rs:230): [features][digits][column blocks][2][e][inds] floats, the
+ * keys then the values ([e][inds] each) of every feature group's inducing points. Needed by the `rows` hook. */
+TCU_API int tcu_model_put_col_kv(tcu_model *m, const float *col_kv, size_t count);
+/* The whole of the above from a fitted bundle file, member `prefix` ("m0/", or "" for a raw fit), problem node
+ * (col_kv too when the bundle holds it). */
 TCU_API int tcu_model_from_bundle(tcu_weights *w, const char *path, const char *prefix, int node, tcu_model **out);
 /* Device bytes the cache holds (Gpu::model_bytes, for tier budgets). */
 TCU_API size_t tcu_model_bytes(const tcu_model *m);
@@ -113,6 +130,19 @@ TCU_API int tcu_stage(tcu_model *m, const float *h, int rows, int d, int out_n, 
  * wait). The context stays usable: the next call starts clean. */
 TCU_API int tcu_attend_device(tcu_model *m, int layer, const float *q, int rows, float *out, void *stream);
 TCU_API int tcu_stage_device(tcu_model *m, const float *h, int rows, int out_n, float *out, void *stream);
+/* `rows`: all three stages for normalised rows x [rows][features] (prep's output, missing cells -100): the column stage
+ * (predict::embed, src/predict.rs:282-353; with several label digits, once per digit and averaged), the row stage
+ * (predict::represent, src/predict.rs:356-372), then the in-context stage; the first out_n decoder outputs per row
+ * [rows][out_n]. Host buffers. TCU_DECLINED when the weights have no column and row stages or the cache no col_kv
+ * (the caller's CPU path answers, as for `stage`). The reference calls this hook only for a member of one node
+ * (src/predict.rs:642-652). */
+TCU_API int tcu_rows(tcu_model *m, const float *x, int rows, int features, int out_n, float *out);
+/* The same on device buffers, queued on `stream` (NULL = the context's stream). */
+TCU_API int tcu_rows_device(tcu_model *m, const float *x, int rows, int out_n, float *out, void *stream);
+/* Its two first stages alone, on device buffers: tokens tok [rows][cls + features][e] of normalised rows x, and row
+ * representations rep [rows][cls e] of tokens (tok is used as scratch). */
+TCU_API int tcu_embed_device(tcu_model *m, const float *x, int rows, float *tok, void *stream);
+TCU_API int tcu_represent_device(tcu_model *m, float *tok, int rows, float *rep, void *stream);
 /* Wait for `stream` (NULL = the context's stream) and report kernels that gave up since the last report
  * (TCU_ERR_CUDA), as cudaStreamSynchronize plus a check; no counterpart in the reference, whose card calls block. */
 TCU_API int tcu_sync(tcu_ctx *ctx, void *stream);

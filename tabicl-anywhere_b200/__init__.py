@@ -38,6 +38,14 @@ class IclShape(ctypes.Structure):
         return {n: getattr(self, n) for n, _ in self._fields_}
 
 
+class RowsShape(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("e", "group", "inds", "cls", "col_heads", "row_heads", "col_blocks",
+                                              "row_blocks", "col_ff", "row_ff")]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
 _lib = None
 
 
@@ -60,6 +68,13 @@ def lib():
         "tcu_weights_ready": (_c_int, [_c_void]),
         "tcu_weights_from_bundle": (_c_int, [_c_void, ctypes.c_char_p, _c_int, P(_c_void)]),
         "tcu_weights_shape": (_c_int, [_c_void, P(IclShape)]),
+        "tcu_weights_set_rows_shape": (_c_int, [_c_void, P(RowsShape)]),
+        "tcu_weights_rows_shape": (_c_int, [_c_void, P(RowsShape)]),
+        "tcu_model_put_col_kv": (_c_int, [_c_void, _c_float_p, _c_size]),
+        "tcu_rows": (_c_int, [_c_void, _c_float_p, _c_int, _c_int, _c_int, _c_float_p]),
+        "tcu_rows_device": (_c_int, [_c_void, _c_void, _c_int, _c_int, _c_void, _c_void]),
+        "tcu_embed_device": (_c_int, [_c_void, _c_void, _c_int, _c_void, _c_void]),
+        "tcu_represent_device": (_c_int, [_c_void, _c_void, _c_int, _c_void, _c_void]),
         "tcu_weights_free": (None, [_c_void]),
         "tcu_model_new": (_c_int, [_c_void, P(ctypes.c_int32), ctypes.c_int32, ctypes.c_int32, P(_c_void)]),
         "tcu_model_put_scales": (_c_int, [_c_void, _c_float_p, _c_size]),
@@ -205,12 +220,16 @@ class GpuWeights:
         return GpuWeights(gpu, h)
 
     @staticmethod
-    def from_tensors(gpu, shape, tensors, for_fit=False):
-        """`shape`: dict of IclShape fields; `tensors`: bundle name -> float32/float16 array."""
+    def from_tensors(gpu, shape, tensors, for_fit=False, rows_shape=None):
+        """`shape`: dict of IclShape fields; `tensors`: bundle name -> float32/float16 array; `rows_shape` (dict of
+        RowsShape fields): also keep the column and row stages (their tensors among `tensors`)."""
         h = _c_void()
         s = IclShape(**shape)
         gpu.check(lib().tcu_weights_new(gpu._h, ctypes.byref(s), int(for_fit), ctypes.byref(h)))
         w = GpuWeights(gpu, h)
+        if rows_shape is not None:
+            rs = RowsShape(**rows_shape)
+            gpu.check(lib().tcu_weights_set_rows_shape(h, ctypes.byref(rs)))
         for name, a in tensors.items():
             a = np.ascontiguousarray(a)
             dt = 1 if a.dtype == np.float16 else 0
@@ -225,6 +244,13 @@ class GpuWeights:
         s = IclShape()
         self.gpu.check(lib().tcu_weights_shape(self._h, ctypes.byref(s)))
         return s.as_dict()
+
+    @property
+    def rows_shape(self):
+        """The column and row stages' sizes, or None when the weights have none."""
+        s = RowsShape()
+        r = self.gpu.check(lib().tcu_weights_rows_shape(self._h, ctypes.byref(s)))
+        return s.as_dict() if r == OK else None
 
     def free(self):
         if self._h:
@@ -253,8 +279,9 @@ class VramModel:
         return VramModel(weights, h)
 
     @staticmethod
-    def from_parts(weights, meta, node_rows, node_k, scales, layers):
-        """`meta`: the member's 7 meta ints; `scales` [layers][d] floats; `layers`: each layer's stored bytes."""
+    def from_parts(weights, meta, node_rows, node_k, scales, layers, col_kv=None):
+        """`meta`: the member's 7 meta ints; `scales` [layers][d] floats; `layers`: each layer's stored bytes; `col_kv`:
+        the column stage's cache (fit.rs:230), for the `rows` hook."""
         h = _c_void()
         meta = np.ascontiguousarray(meta, dtype=np.int32)
         g = weights.gpu
@@ -266,6 +293,10 @@ class VramModel:
         for l, b in enumerate(layers):
             b = np.frombuffer(bytes(b), dtype=np.uint8)
             g.check(lib().tcu_model_put_layer(h, l, 0, b.ctypes.data, b.size))
+        if col_kv is not None:
+            ck = np.ascontiguousarray(col_kv, dtype=np.float32).reshape(-1)
+            g.check(lib().tcu_model_put_col_kv(h, _f32p(ck), ck.size))
+        m.features = int(meta[1])
         return m
 
     @property
@@ -297,6 +328,27 @@ class VramModel:
         assert out.dtype == np.float32 and out.flags.c_contiguous and out.size == rows * out_n
         self.gpu.check(lib().tcu_stage(self._h, _f32p(h), rows, d, out_n, _f32p(out)))
         return out
+
+    def rows(self, x, out_n, out=None):
+        """AttendCached::rows on host buffers: normalised rows [rows][features] through the column, row and in-context
+        stages to [rows][out_n] decoder outputs. Returns None when the library declines (no column and row stages)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n, feats = x.shape
+        if out is None:
+            out = np.empty((n, out_n), dtype=np.float32)
+        r = self.gpu.check(lib().tcu_rows(self._h, _f32p(x), n, feats, out_n, _f32p(out)))
+        return None if r == DECLINED else out
+
+    def rows_device(self, x_ptr, rows, out_n, out_ptr, stream=None):
+        return self.gpu.check(lib().tcu_rows_device(self._h, x_ptr, rows, out_n, out_ptr, stream))
+
+    def embed_device(self, x_ptr, rows, tok_ptr, stream=None):
+        """predict::embed on device buffers: tokens [rows][cls + features][e]."""
+        return self.gpu.check(lib().tcu_embed_device(self._h, x_ptr, rows, tok_ptr, stream))
+
+    def represent_device(self, tok_ptr, rows, rep_ptr, stream=None):
+        """predict::represent on device buffers (the tokens are used as scratch): [rows][cls e]."""
+        return self.gpu.check(lib().tcu_represent_device(self._h, tok_ptr, rows, rep_ptr, stream))
 
     def attend_device(self, layer, q_ptr, rows, out_ptr, stream=None):
         return self.gpu.check(lib().tcu_attend_device(self._h, layer, q_ptr, rows, out_ptr, stream))
@@ -439,5 +491,6 @@ class CudaAttend:
         return self._or_cpu(lambda: self._model(prefix, node).stage(h, out_n, d=d))
 
     def rows(self, prefix, x, out_n):
-        # the column and row stages are not on the device yet: decline, the caller's CPU path does them
-        return None
+        """All three stages for a member of one node (predict.rs:642-652): None when the device declines (no column
+        and row stages in the weights or the cache) or fails, as for the other hooks."""
+        return self._or_cpu(lambda: self._model(prefix, 0).rows(x, out_n))

@@ -115,6 +115,24 @@ struct LayerPtrs {
     SplitW tq, to, t1, t2, tkv, tq0, tq2;  // tq0 / tq2: the query MLP (hid x hd, hd x hid)
 };
 
+// One pre-norm block of the column or row stage on the device (src/model.rs:27-98): in_proj's query rows (column
+// blocks) or all three projections (row blocks), no scalable softmax.
+struct CBlockPtrs {
+    const float *n1w, *n1b, *inw, *inb, *ow, *ob, *n2w, *n2b, *w1, *b1, *w2, *b2;
+    SplitW tin, to, t1, t2;
+    int ff;
+};
+
+// The column and row stages' weights (src/model.rs:199-245), when the bundle has them.
+struct RowsWeights {
+    bool on = false;
+    tcu_rows_shape shape{};
+    const float *in_w = nullptr, *in_b = nullptr, *cls_tokens = nullptr, *out_lnw = nullptr, *out_lnb = nullptr;
+    std::vector<float> rope_freqs;  // host copy: the position tables are made per token count
+    std::vector<CBlockPtrs> col, row;
+    DevBuf dev, dev16;
+};
+
 struct tcu_weights {
     std::atomic<int> refs{1};  // the caller's handle plus one per live model
     tcu_ctx *ctx = nullptr;
@@ -129,11 +147,17 @@ struct tcu_weights {
     bool ready = false;
     // fit-time query scale pieces (the base MLP of the scalable softmax), kept on the host: nn.rs:97-107
     std::vector<std::vector<float>> sb0w, sb0b, sb2w, sb2b;
+    RowsWeights rows;
 };
 
 struct tcu_model {
     tcu_weights *w = nullptr;
-    int rows = 0, chunk = 0, kv = 0, classes = 0, features = 0;
+    int rows = 0, chunk = 0, kv = 0, classes = 0, features = 0, digits = 1, nodes = 1;
+    DevBuf col_kv;  // the column stage's cache [features][digits][blocks][2][e][inds] (fit.rs:230)
+    // the column and row stages' working memory: cells (and the digits' sum), projections, attention, hidden,
+    // tokens, the row stage's projections and key workspace, the position tables of the last token count
+    DevBuf cin, cx, cx0, csum, cq, catt, cmid, ctok, cqkv, ckt, cnew, crope;
+    int crope_T = -1;
     size_t full = 0, layer_bytes = 0, layer_stride = 0;
     DevBuf layers, scales, items, tiles;
     int nitems = 0, ntiles = 0;
@@ -363,20 +387,75 @@ static std::vector<float> opt_zero(const tcu_weights *w, const std::string &name
     return it->second;
 }
 
-static int weights_ready(tcu_weights *w) {
-    const auto &s = w->shape;
-    const int d = s.d, L = s.layers, ff = s.ff, hid = s.hid, hd = d / s.heads, dff = s.dec_ff, outs = s.outs;
-    // gather every tensor in device order, each 256-byte aligned
-    std::vector<std::pair<std::vector<float>, const float **>> parts;
+// Weights gathered for one upload: every tensor in device order, each 256-byte aligned (`flat`), and the f16 hi + lo
+// copies of the matrices the tensor cores take (`half`): W * 2^e(n) per output row n, in 128 x 64 blocks
+// (tc_block_off), rows past N zero; 2^-e(n) beside it in `flat`. No blocks when K is not a multiple of 64.
+struct Packer {
     std::vector<float> flat;
+    std::vector<uint16_t> half;
     std::vector<size_t> offs;
-    auto add = [&](const std::vector<float> &v) {
+    struct SplitIdx {
+        size_t tiles = 0, unscale = 0;
+        bool on = false;
+    };
+    size_t add(const std::vector<float> &v) {
         size_t at = (flat.size() + 63) / 64 * 64;
         flat.resize(at + v.size());
         std::memcpy(flat.data() + at, v.data(), v.size() * sizeof(float));
         offs.push_back(at);
         return offs.size() - 1;
-    };
+    }
+    const float *host(size_t idx) const { return flat.data() + offs[idx]; }
+    SplitIdx split(size_t idx, int N, int K) {
+        SplitIdx ix;
+        ix.on = K % 64 == 0;
+        if (!ix.on) return ix;
+        const std::vector<float> src(host(idx), host(idx) + (size_t)N * K);  // add() below may move `flat`
+        const int nts = (N + 127) / 128, nk = K / 64;
+        const size_t blk = 128 * 64;
+        ix.tiles = (half.size() + 127) / 128 * 128;
+        half.resize(ix.tiles + (size_t)nts * nk * 2 * blk, 0);
+        std::vector<float> un(N);
+        for (int n = 0; n < N; n++) {
+            const float *row = src.data() + (size_t)n * K;
+            float mx = 0.f;
+            for (int k = 0; k < K; k++) mx = std::max(mx, std::fabs(row[k]));
+            const int e = tc_exponent(mx);
+            const float sc = std::ldexp(1.0f, e);
+            un[n] = std::ldexp(1.0f, -e);
+            for (int k = 0; k < K; k++) {
+                const float x = row[k] * sc;  // exact: a power of two
+                const uint16_t h = f32_to_f16(x);
+                uint16_t *b = half.data() + ix.tiles + ((size_t)(n / 128) * nk + k / 64) * 2 * blk;
+                const size_t off = tc_block_off(n, k);
+                b[off] = h;
+                b[blk + off] = f32_to_f16(x - f16_to_f32(h));
+            }
+        }
+        ix.unscale = add(un);
+        return ix;
+    }
+    // copy both to the device; the pointer of an added tensor is then P(idx), of a split matrix S(ix)
+    void upload(DevBuf &dev, DevBuf &dev16) {
+        dev.ensure(flat.size() * sizeof(float));
+        CU(cudaMemcpy(dev.p, flat.data(), flat.size() * sizeof(float), cudaMemcpyHostToDevice));
+        dev16.ensure(std::max<size_t>(half.size(), 1) * sizeof(uint16_t));
+        if (!half.empty()) CU(cudaMemcpy(dev16.p, half.data(), half.size() * sizeof(uint16_t), cudaMemcpyHostToDevice));
+        base = dev.as<float>(), hbase = dev16.as<uint16_t>();
+    }
+    const float *base = nullptr;
+    const uint16_t *hbase = nullptr;
+    const float *P(size_t idx) const { return base + offs[idx]; }
+    SplitW S(const SplitIdx &ix) const { return ix.on ? SplitW{hbase + ix.tiles, base + offs[ix.unscale]} : SplitW(); }
+};
+
+static int rows_ready(tcu_weights *w);
+
+static int weights_ready(tcu_weights *w) {
+    const auto &s = w->shape;
+    const int d = s.d, L = s.layers, ff = s.ff, hid = s.hid, hd = d / s.heads, dff = s.dec_ff, outs = s.outs;
+    Packer pk;
+    auto add = [&](const std::vector<float> &v) { return pk.add(v); };
     struct LIdx {
         size_t n1w, n1b, wq, bq, q0w, q0b, q2w, q2b, wo, bo, n2w, n2b, w1, b1, w2, b2, wkv, bkv;
     };
@@ -438,61 +517,23 @@ static int weights_ready(tcu_weights *w) {
         i_y = add(t);
     }
     // tensor-core copies of the linear layers' weights: f16 hi + lo per row, scaled to stay inside f16
-    std::vector<uint16_t> half;
-    struct SplitIdx {
-        size_t tiles, unscale;
-        bool on;
-    };
-    auto split = [&](const float *src_in, int N, int K) {
-        SplitIdx ix{0, 0, K % 64 == 0};
-        if (!ix.on) return ix;
-        const std::vector<float> src_copy(src_in, src_in + (size_t)N * K);  // add() below may move `flat`
-        const float *src = src_copy.data();
-        const int nts = (N + 127) / 128, nk = K / 64;
-        const size_t blk = 128 * 64;
-        ix.tiles = (half.size() + 127) / 128 * 128;
-        half.resize(ix.tiles + (size_t)nts * nk * 2 * blk, 0);  // rows past N stay zero
-        std::vector<float> un(N);
-        for (int n = 0; n < N; n++) {
-            const float *row = src + (size_t)n * K;
-            float mx = 0.f;
-            for (int k = 0; k < K; k++) mx = std::max(mx, std::fabs(row[k]));
-            const int e = tc_exponent(mx);
-            const float sc = std::ldexp(1.0f, e);
-            un[n] = std::ldexp(1.0f, -e);
-            for (int k = 0; k < K; k++) {
-                const float x = row[k] * sc;  // exact: a power of two
-                const uint16_t h = f32_to_f16(x);
-                uint16_t *b = half.data() + ix.tiles + ((size_t)(n / 128) * nk + k / 64) * 2 * blk;
-                const size_t off = tc_block_off(n, k);
-                b[off] = h;
-                b[blk + off] = f32_to_f16(x - f16_to_f32(h));
-            }
-        }
-        ix.unscale = add(un);
-        return ix;
-    };
+    using SplitIdx = Packer::SplitIdx;
     std::vector<std::array<SplitIdx, 7>> lsplit(L);
     for (int l = 0; l < L; l++) {
         const LIdx &x = li[l];
-        lsplit[l][0] = split(flat.data() + offs[x.wq], d, d);
-        lsplit[l][1] = split(flat.data() + offs[x.wo], d, d);
-        lsplit[l][2] = split(flat.data() + offs[x.w1], ff, d);
-        lsplit[l][3] = split(flat.data() + offs[x.w2], d, ff);
-        if (w->for_fit) lsplit[l][4] = split(flat.data() + offs[x.wkv], 2 * d, d);
-        lsplit[l][5] = split(flat.data() + offs[x.q0w], hid, hd);
-        lsplit[l][6] = split(flat.data() + offs[x.q2w], hd, hid);
+        lsplit[l][0] = pk.split(x.wq, d, d);
+        lsplit[l][1] = pk.split(x.wo, d, d);
+        lsplit[l][2] = pk.split(x.w1, ff, d);
+        lsplit[l][3] = pk.split(x.w2, d, ff);
+        if (w->for_fit) lsplit[l][4] = pk.split(x.wkv, 2 * d, d);
+        lsplit[l][5] = pk.split(x.q0w, hid, hd);
+        lsplit[l][6] = pk.split(x.q2w, hd, hid);
     }
-    const SplitIdx s_dec0 = split(flat.data() + offs[i_d0w], dff, d);
-    const SplitIdx s_dec2 = split(flat.data() + offs[i_d2w], outs, dff);
-    w->dev.ensure(flat.size() * sizeof(float));
-    CU(cudaMemcpy(w->dev.p, flat.data(), flat.size() * sizeof(float), cudaMemcpyHostToDevice));
-    w->dev16.ensure(half.size() * sizeof(uint16_t));
-    CU(cudaMemcpy(w->dev16.p, half.data(), half.size() * sizeof(uint16_t), cudaMemcpyHostToDevice));
-    const float *base = w->dev.as<float>();
-    const uint16_t *hbase = w->dev16.as<uint16_t>();
-    auto P = [&](size_t idx) { return base + offs[idx]; };
-    auto S = [&](const SplitIdx &ix) { return ix.on ? SplitW{hbase + ix.tiles, base + offs[ix.unscale]} : SplitW(); };
+    const SplitIdx s_dec0 = pk.split(i_d0w, dff, d);
+    const SplitIdx s_dec2 = pk.split(i_d2w, outs, dff);
+    pk.upload(w->dev, w->dev16);
+    auto P = [&](size_t idx) { return pk.P(idx); };
+    auto S = [&](const SplitIdx &ix) { return pk.S(ix); };
     w->layer.resize(L);
     for (int l = 0; l < L; l++) {
         const LIdx &x = li[l];
@@ -507,8 +548,67 @@ static int weights_ready(tcu_weights *w) {
     w->lnw = P(i_lnw), w->lnb = P(i_lnb), w->dec0w = P(i_d0w), w->dec0b = P(i_d0b), w->dec2w = P(i_d2w), w->dec2b = P(i_d2b);
     w->tdec0 = S(s_dec0), w->tdec2 = S(s_dec2);
     w->icl_y = w->for_fit ? P(i_y) : nullptr;
+    if (w->rows.on) rows_ready(w);
     w->host.clear();
     w->ready = true;
+    return TCU_OK;
+}
+
+// The column and row stages' tensors (model.rs:199-245; the column blocks' second attention, whose in_proj query
+// rows are all prediction uses, model.rs:226-231) to the device, with tensor-core copies of their matrices.
+static int rows_ready(tcu_weights *w) {
+    RowsWeights &rw = w->rows;
+    const auto &s = rw.shape;
+    const int e = s.e;
+    Packer pk;
+    struct BIdx {
+        size_t n1w, n1b, inw, inb, ow, ob, n2w, n2b, w1, b1, w2, b2;
+        Packer::SplitIdx tin, to, t1, t2;
+        int ff;
+    };
+    auto block = [&](const std::string &p, bool q_only, int ff) {
+        BIdx x;
+        const int nin = q_only ? e : 3 * e;
+        const auto &inw = need(w, p + "attn.in_proj_weight", (size_t)3 * e * e);
+        const auto &inb = need(w, p + "attn.in_proj_bias", (size_t)3 * e);
+        x.n1w = pk.add(need(w, p + "norm1.weight", e));
+        x.n1b = pk.add(opt_zero(w, p + "norm1.bias", e));
+        x.inw = pk.add(std::vector<float>(inw.begin(), inw.begin() + (size_t)nin * e));
+        x.inb = pk.add(std::vector<float>(inb.begin(), inb.begin() + nin));
+        x.ow = pk.add(need(w, p + "attn.out_proj.weight", (size_t)e * e));
+        x.ob = pk.add(need(w, p + "attn.out_proj.bias", e));
+        x.n2w = pk.add(need(w, p + "norm2.weight", e));
+        x.n2b = pk.add(opt_zero(w, p + "norm2.bias", e));
+        x.w1 = pk.add(need(w, p + "linear1.weight", (size_t)ff * e));
+        x.b1 = pk.add(need(w, p + "linear1.bias", ff));
+        x.w2 = pk.add(need(w, p + "linear2.weight", (size_t)e * ff));
+        x.b2 = pk.add(need(w, p + "linear2.bias", e));
+        x.tin = pk.split(x.inw, nin, e), x.to = pk.split(x.ow, e, e);
+        x.t1 = pk.split(x.w1, ff, e), x.t2 = pk.split(x.w2, e, ff);
+        x.ff = ff;
+        return x;
+    };
+    std::vector<BIdx> cb, rb;
+    for (int i = 0; i < s.col_blocks; i++)
+        cb.push_back(block("col_embedder.tf_col.blocks." + std::to_string(i) + ".multihead_attn2.", true, s.col_ff));
+    for (int i = 0; i < s.row_blocks; i++)
+        rb.push_back(block("row_interactor.tf_row.blocks." + std::to_string(i) + ".", false, s.row_ff));
+    const size_t i_inw = pk.add(need(w, "col_embedder.in_linear.weight", (size_t)e * s.group));
+    const size_t i_inb = pk.add(need(w, "col_embedder.in_linear.bias", e));
+    const size_t i_cls = pk.add(need(w, "row_interactor.cls_tokens", (size_t)s.cls * e));
+    const size_t i_lnw = pk.add(need(w, "row_interactor.out_ln.weight", e));
+    const size_t i_lnb = pk.add(opt_zero(w, "row_interactor.out_ln.bias", e));
+    rw.rope_freqs = need(w, "row_interactor.tf_row.rope.freqs", (size_t)e / s.row_heads / 2);
+    pk.upload(rw.dev, rw.dev16);
+    auto ptrs = [&](const BIdx &x) {
+        return CBlockPtrs{pk.P(x.n1w), pk.P(x.n1b), pk.P(x.inw), pk.P(x.inb), pk.P(x.ow), pk.P(x.ob),
+                          pk.P(x.n2w), pk.P(x.n2b), pk.P(x.w1), pk.P(x.b1), pk.P(x.w2), pk.P(x.b2),
+                          pk.S(x.tin), pk.S(x.to), pk.S(x.t1), pk.S(x.t2), x.ff};
+    };
+    rw.col.clear(), rw.row.clear();
+    for (const auto &x : cb) rw.col.push_back(ptrs(x));
+    for (const auto &x : rb) rw.row.push_back(ptrs(x));
+    rw.in_w = pk.P(i_inw), rw.in_b = pk.P(i_inb), rw.cls_tokens = pk.P(i_cls), rw.out_lnw = pk.P(i_lnw), rw.out_lnb = pk.P(i_lnb);
     return TCU_OK;
 }
 
@@ -1072,6 +1172,116 @@ static void stage_replay(tcu_ctx *ctx, tcu_model *m, int R, int out_n, cudaStrea
     CU(cudaGraphLaunch(exec, s));
 }
 
+// ---- the column and row stages (predict.rs:282-372) -------------------------------------------------------------
+
+static void check_rows_ready(const tcu_model *m) {
+    const RowsWeights &rw = m->w->rows;
+    if (!rw.on) fail(TCU_DECLINED, "rows: the weights have no column and row stages");
+    if (!m->col_kv.p) fail(TCU_DECLINED, "rows: the cache has no column-stage keys and values (col_kv was never put)");
+    if (rw.shape.cls * rw.shape.e != m->w->shape.d) fail(TCU_ERR_FORMAT, "rows: class tokens times width differ from the in-context width");
+}
+
+// Grow the linear layers' scratch (row statistics, split rows) for M rows of width up to K; graphs that used the old
+// buffers are dropped.
+static void ensure_linear(tcu_model *m, size_t M, int K) {
+    bool moved = m->stats.ensure(sizeof(float) * 4 * M);
+    moved |= m->atiles.ensure(tc_split_bytes((int)M, K));
+    if (moved) drop_graphs(m);
+}
+
+// predict.rs:282-353 embed: normalised rows x (device [R][F]) to tokens tok (device [R][cls + F][e]). Every cell
+// goes through every column block's second attention against its group's cached inducing points (cached_block,
+// nn.rs:289-302); with several label digits, once per digit from the same starting cell, then the average.
+static void embed(tcu_ctx *ctx, tcu_model *m, const float *x, int R, float *tok, cudaStream_t s) {
+    check_rows_ready(m);
+    const RowsWeights &rw = m->w->rows;
+    const auto &rs = rw.shape;
+    const int e = rs.e, F = m->features, D = m->digits, nb = rs.col_blocks, inds = rs.inds, ff = rs.col_ff;
+    const size_t M = (size_t)R * F, per = (size_t)2 * e * inds, gstride = (size_t)D * nb * per;
+    m->cx.ensure(sizeof(float) * M * e), m->cq.ensure(sizeof(float) * M * e), m->catt.ensure(sizeof(float) * M * e);
+    m->cmid.ensure(sizeof(float) * M * ff);
+    if (D > 1) m->cx0.ensure(sizeof(float) * M * e), m->csum.ensure(sizeof(float) * M * e);
+    ensure_linear(m, M, std::max(e, ff));
+    float *X = m->cx.as<float>(), *Q = m->cq.as<float>(), *A = m->catt.as<float>(), *H = m->cmid.as<float>();
+    Launch ck{ctx, s};
+    ck(launch_col_cells(x, R, F, rs.group, rw.in_w, rw.in_b, e, D > 1 ? m->cx0.as<float>() : X, s, &ctx->launches), "cells");
+    const float scale = 1.0f / std::sqrt((float)(e / rs.col_heads));
+    for (int dg = 0; dg < D; dg++) {
+        if (D > 1) CU(cudaMemcpyAsync(X, m->cx0.p, sizeof(float) * M * e, cudaMemcpyDeviceToDevice, s));
+        for (int b = 0; b < nb; b++) {
+            const CBlockPtrs &B = rw.col[b];
+            linear(ctx, m, X, e, (int)M, e, B.n1w, B.n1b, B.inw, B.inb, e, Q, e, 0, 0, s, B.tin);
+            ck(launch_col_attend(Q, R, F, m->col_kv.as<float>() + (dg * nb + b) * per, gstride, e, inds, rs.col_heads, scale,
+                                 A, s, &ctx->launches),
+               "column attention");
+            linear(ctx, m, A, e, (int)M, e, nullptr, nullptr, B.ow, B.ob, e, X, e, 0, 1, s, B.to);
+            linear(ctx, m, X, e, (int)M, e, B.n2w, B.n2b, B.w1, B.b1, ff, H, ff, 1, 0, s, B.t1);
+            linear(ctx, m, H, ff, (int)M, ff, nullptr, nullptr, B.w2, B.b2, e, X, e, 0, 1, s, B.t2);
+        }
+        if (D > 1) ck(launch_scale_add(m->csum.as<float>(), X, M * e, 1.0f, dg > 0, s, &ctx->launches), "digit sum");
+    }
+    if (D > 1) ck(launch_divide(X, m->csum.as<float>(), M * e, (float)D, s, &ctx->launches), "digit average");
+    ck(launch_tokens(X, rw.cls_tokens, R, F, rs.cls, e, tok, s, &ctx->launches), "tokens");
+}
+
+// predict.rs:356-372 represent: tokens (device [R][T][e], consumed) to row representations rep (device [R][cls e]):
+// the row blocks (nn.rs:357-419; the last one only for the class tokens), then the class tokens' LayerNorm.
+static void represent(tcu_ctx *ctx, tcu_model *m, float *tok, int R, float *rep, cudaStream_t s) {
+    check_rows_ready(m);
+    const RowsWeights &rw = m->w->rows;
+    const auto &rs = rw.shape;
+    const int e = rs.e, T = rs.cls + m->features, heads = rs.row_heads, half = e / heads / 2, ff = rs.row_ff;
+    const size_t M = (size_t)R * T;
+    m->cqkv.ensure(sizeof(float) * M * 3 * e), m->catt.ensure(sizeof(float) * M * e), m->cnew.ensure(sizeof(float) * M * e);
+    m->cmid.ensure(sizeof(float) * M * ff);
+    if (!row_attend_smem(e, T, heads)) m->ckt.ensure(sizeof(float) * row_attend_workspace(R, T, e));
+    ensure_linear(m, M, std::max(e, ff));
+    if (m->crope_T != T) {
+        // nn.rs:309-321: cos and sin of position times frequency, in f32
+        std::vector<float> tab((size_t)2 * T * half);
+        for (int t = 0; t < T; t++)
+            for (int i = 0; i < half; i++) {
+                const float a = (float)t * rw.rope_freqs[i];
+                tab[(size_t)t * half + i] = std::cos(a), tab[(size_t)(T + t) * half + i] = std::sin(a);
+            }
+        m->crope.ensure(sizeof(float) * tab.size());
+        CU(cudaMemcpy(m->crope.p, tab.data(), sizeof(float) * tab.size(), cudaMemcpyHostToDevice));
+        m->crope_T = T;
+    }
+    const float *cs = m->crope.as<float>(), *sn = cs + (size_t)T * half;
+    float *cur = tok, *nxt = m->cnew.as<float>(), *QKV = m->cqkv.as<float>(), *A = m->catt.as<float>(), *H = m->cmid.as<float>();
+    Launch ck{ctx, s};
+    for (int bi = 0; bi < rs.row_blocks; bi++) {
+        const CBlockPtrs &B = rw.row[bi];
+        const bool last = bi + 1 == rs.row_blocks;
+        const int nq = last ? rs.cls : T, MQ = R * nq;
+        linear(ctx, m, cur, e, (int)M, e, B.n1w, B.n1b, B.inw, B.inb, 3 * e, QKV, 3 * e, 0, 0, s, B.tin);
+        ck(launch_row_attend(QKV, R, T, nq, e, heads, cs, sn, m->ckt.as<float>(), A, s, &ctx->launches), "row attention");
+        linear(ctx, m, A, e, MQ, e, nullptr, nullptr, B.ow, B.ob, e, nxt, e, 0, 0, s, B.to);
+        ck(launch_add_rows(nxt, cur, R, nq, T, e, s, &ctx->launches), "row residual");
+        linear(ctx, m, nxt, e, MQ, e, B.n2w, B.n2b, B.w1, B.b1, ff, H, ff, 1, 0, s, B.t1);
+        linear(ctx, m, H, ff, MQ, ff, nullptr, nullptr, B.w2, B.b2, e, nxt, e, 0, 1, s, B.t2);
+        if (!last) std::swap(cur, nxt);  // every token was a query: the new tokens are the next block's input
+    }
+    // the last block left the class tokens [R][cls][e] in nxt: their LayerNorm, laid end to end, is the representation
+    ck(launch_ln_apply(nxt, R * rs.cls, e, rw.out_lnw, rw.out_lnb, rep, s, &ctx->launches), "row LayerNorm");
+}
+
+// predict.rs:638-652: the three stages of a member with one node (the `rows` hook): x (device [R][F]) to the model's
+// out buffer (m->out, [R][out_n]).
+static void rows_stage(tcu_ctx *ctx, tcu_model *m, const float *x, int R, int out_n, cudaStream_t s) {
+    check_ready(m);
+    check_rows_ready(m);
+    if (m->nodes != 1) fail(TCU_DECLINED, "rows: the member has several problems (the class tree); its nodes run one by one");
+    if (out_n < 1 || out_n > m->w->shape.outs) fail(TCU_ERR_ARG, "rows: out_n must be 1..decoder outputs");
+    const auto &rs = m->w->rows.shape;
+    m->ctok.ensure(sizeof(float) * (size_t)R * (rs.cls + m->features) * rs.e);
+    if (m->h.ensure(sizeof(float) * (size_t)R * m->w->shape.d)) drop_graphs(m);
+    embed(ctx, m, x, R, m->ctok.as<float>(), s);
+    represent(ctx, m, m->ctok.as<float>(), R, m->h.as<float>(), s);
+    stage_replay(ctx, m, R, out_n, s);
+}
+
 // ---- training rows split across devices -----------------------------------------------------------------------
 
 static void nccl_check(ncclResult_t r, const char *what) {
@@ -1277,8 +1487,24 @@ int tcu_weights_from_bundle(tcu_ctx *ctx, const char *path, int for_fit, tcu_wei
         int r = tcu_weights_new(ctx, &s, for_fit, &w);
         if (r != TCU_OK) return r;
         WeightsPtr guard(w);
-        for (const auto &e : b->entries())
-            if (e.name.rfind("icl_predictor.", 0) == 0 && (e.dtype == "float32" || e.dtype == "float16")) w->host[e.name] = b->f32s(e.name);
+        const bool rows = b->has("col_embedder.in_linear.weight") && b->has("row_interactor.cls_tokens");
+        if (rows) {
+            // model.rs:220-244: the column and row stages' sizes
+            tcu_rows_shape rs{};
+            rs.e = (int)b->entry("col_embedder.in_linear.bias").len();
+            rs.group = num("col_feature_group_size"), rs.inds = num("col_num_inds"), rs.cls = num("row_num_cls");
+            rs.col_heads = num("col_nhead"), rs.row_heads = num("row_nhead");
+            rs.col_blocks = num("col_num_blocks"), rs.row_blocks = num("row_num_blocks");
+            rs.col_ff = (int)b->entry("col_embedder.tf_col.blocks.0.multihead_attn2.linear1.bias").len();
+            rs.row_ff = (int)b->entry("row_interactor.tf_row.blocks.0.linear1.bias").len();
+            r = tcu_weights_set_rows_shape(w, &rs);
+            if (r != TCU_OK) return r;
+        }
+        for (const auto &e : b->entries()) {
+            const bool want = e.name.rfind("icl_predictor.", 0) == 0 ||
+                              (rows && (e.name.rfind("col_embedder.", 0) == 0 || e.name.rfind("row_interactor.", 0) == 0));
+            if (want && (e.dtype == "float32" || e.dtype == "float16")) w->host[e.name] = b->f32s(e.name);
+        }
         weights_ready(w);
         *out = guard.release();
         return TCU_OK;
@@ -1288,6 +1514,29 @@ int tcu_weights_from_bundle(tcu_ctx *ctx, const char *path, int for_fit, tcu_wei
 int tcu_weights_shape(const tcu_weights *w, tcu_icl_shape *out) {
     if (!w || !out) return TCU_ERR_ARG;
     *out = w->shape;
+    return TCU_OK;
+}
+
+int tcu_weights_set_rows_shape(tcu_weights *w, const tcu_rows_shape *shape) {
+    if (!w) return TCU_ERR_ARG;
+    return guarded(w->ctx, [&]() -> int {
+        if (!shape) fail(TCU_ERR_ARG, "set_rows_shape: null argument");
+        if (w->ready) fail(TCU_ERR_STATE, "set_rows_shape: weights already uploaded");
+        const auto &s = *shape;
+        if (s.e <= 0 || s.group < 1 || s.group > 8 || s.inds < 1 || s.cls < 1 || s.col_heads < 1 || s.row_heads < 1 ||
+            s.e % s.col_heads || s.e % s.row_heads || (s.e / s.row_heads) % 2 || s.col_blocks < 1 || s.row_blocks < 1 ||
+            s.col_ff < 1 || s.row_ff < 1 || s.e % 4)
+            fail(TCU_ERR_ARG, "set_rows_shape: bad shape");
+        if (s.cls * s.e != w->shape.d) fail(TCU_ERR_ARG, "set_rows_shape: class tokens times width must be the in-context width");
+        w->rows.shape = s, w->rows.on = true;
+        return TCU_OK;
+    });
+}
+
+int tcu_weights_rows_shape(const tcu_weights *w, tcu_rows_shape *out) {
+    if (!w || !out) return TCU_ERR_ARG;
+    if (!w->rows.on) return TCU_DECLINED;
+    *out = w->rows.shape;
     return TCU_OK;
 }
 
@@ -1305,6 +1554,7 @@ int tcu_model_new(tcu_weights *w, const int32_t meta[7], int32_t node_rows, int3
         if (meta[4] < 0 || meta[4] > 2) fail(TCU_ERR_FORMAT, "meta: unknown key/value format " + std::to_string(meta[4]));
         model_init(m.get(), w, node_rows, meta[3], meta[4], node_k);
         m->features = meta[1];
+        m->digits = std::max(1, (int)meta[5]), m->nodes = std::max(1, (int)meta[6]);
         *out = m.release();
         return TCU_OK;
     });
@@ -1358,6 +1608,11 @@ int tcu_model_from_bundle(tcu_weights *w, const char *path, const char *prefix, 
         auto sc = b->f32s(p + "n" + std::to_string(node) + "_scale");
         r = tcu_model_put_scales(m, sc.data(), sc.size());
         if (r != TCU_OK) return r;
+        if (w->rows.on && b->has(p + "col_kv")) {
+            auto ck = b->f32s(p + "col_kv");
+            r = tcu_model_put_col_kv(m, ck.data(), ck.size());
+            if (r != TCU_OK) return r;
+        }
         for (int l = 0; l < w->shape.layers; l++) {
             std::string name = p + "n" + std::to_string(node) + "_kv" + std::to_string(l);
             const Entry &e = b->entry(name);
@@ -1373,7 +1628,82 @@ int tcu_model_from_bundle(tcu_weights *w, const char *path, const char *prefix, 
 
 size_t tcu_model_bytes(const tcu_model *m) {
     if (!m) return 0;
-    return m->layers.bytes + m->scales.bytes + m->items.bytes + m->tiles.bytes;
+    return m->layers.bytes + m->scales.bytes + m->items.bytes + m->tiles.bytes + m->col_kv.bytes;
+}
+
+int tcu_model_put_col_kv(tcu_model *m, const float *col_kv, size_t count) {
+    if (!m) return TCU_ERR_ARG;
+    return guarded(m->w->ctx, [&]() -> int {
+        const RowsWeights &rw = m->w->rows;
+        if (!rw.on) fail(TCU_ERR_STATE, "model_put_col_kv: the weights have no column and row stages");
+        const auto &rs = rw.shape;
+        const size_t want = (size_t)m->features * m->digits * rs.col_blocks * 2 * rs.e * rs.inds;
+        if (!col_kv || count != want || m->features < 1)
+            fail(TCU_ERR_ARG, "model_put_col_kv: expected features * digits * column blocks * 2 * e * inducing points = " +
+                                  std::to_string(want) + " floats");
+        m->col_kv.ensure(sizeof(float) * want);
+        CU(cudaMemcpy(m->col_kv.p, col_kv, sizeof(float) * want, cudaMemcpyHostToDevice));
+        return TCU_OK;
+    });
+}
+
+int tcu_embed_device(tcu_model *m, const float *x, int rows, float *tok, void *stream) {
+    if (!m) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->w->ctx;
+    return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
+        if (rows < 0 || (rows && (!x || !tok))) fail(TCU_ERR_ARG, "embed: bad argument");
+        if (rows == 0) return TCU_OK;
+        embed(ctx, m, x, rows, tok, stream ? (cudaStream_t)stream : ctx->stream);
+        return TCU_OK;
+    });
+}
+
+int tcu_represent_device(tcu_model *m, float *tok, int rows, float *rep, void *stream) {
+    if (!m) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->w->ctx;
+    return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
+        if (rows < 0 || (rows && (!tok || !rep))) fail(TCU_ERR_ARG, "represent: bad argument");
+        if (rows == 0) return TCU_OK;
+        represent(ctx, m, tok, rows, rep, stream ? (cudaStream_t)stream : ctx->stream);
+        return TCU_OK;
+    });
+}
+
+int tcu_rows_device(tcu_model *m, const float *x, int rows, int out_n, float *out, void *stream) {
+    if (!m) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->w->ctx;
+    return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
+        if (rows < 0 || (rows && (!x || !out))) fail(TCU_ERR_ARG, "rows: bad argument");
+        if (rows == 0) return TCU_OK;
+        cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+        rows_stage(ctx, m, x, rows, out_n, s);
+        CU(cudaMemcpyAsync(out, m->out.p, sizeof(float) * (size_t)rows * out_n, cudaMemcpyDeviceToDevice, s));
+        return TCU_OK;
+    });
+}
+
+int tcu_rows(tcu_model *m, const float *x, int rows, int features, int out_n, float *out) {
+    if (!m) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->w->ctx;
+    return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
+        if (features != m->features) fail(TCU_ERR_ARG, "rows: features differ from the cache's " + std::to_string(m->features));
+        if (rows < 0 || (rows && (!x || !out))) fail(TCU_ERR_ARG, "rows: bad argument");
+        if (rows == 0) return TCU_OK;
+        check_rows_ready(m);
+        cudaStream_t s = ctx->stream;
+        const size_t n = (size_t)rows * features;
+        m->cin.ensure(sizeof(float) * n);
+        CU(cudaMemcpyAsync(m->cin.p, x, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+        rows_stage(ctx, m, m->cin.as<float>(), rows, out_n, s);
+        CU(cudaMemcpyAsync(out, m->out.p, sizeof(float) * (size_t)rows * out_n, cudaMemcpyDeviceToHost, s));
+        CU(cudaStreamSynchronize(s));
+        check_device_error(ctx);
+        return TCU_OK;
+    });
 }
 
 int tcu_model_get_layer(const tcu_model *m, int layer, void *bytes, size_t nbytes) {

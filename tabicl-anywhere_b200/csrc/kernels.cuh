@@ -176,6 +176,31 @@ cudaError_t launch_regression_head(const float *qout, int rows, int nq, int stri
                                    double tmean, double tscale, double *mean, double *var, double *median,
                                    double *quant, cudaStream_t s, uint64_t *launches);
 cudaError_t kernels_init();
+
+// The column and row stages (rows.cu; src/predict.rs:282-372).
+// Cells X [R * F][e] of normalised rows x [R][F]: in_linear of each feature group, -100 when all are missing.
+cudaError_t launch_col_cells(const float *x, int R, int F, int group, const float *in_w, const float *in_b, int e,
+                             float *X, cudaStream_t s, uint64_t *launches);
+// Attention of the cells' raw query projections Q [R * F][e] (times scale) against group g's cached keys and values
+// ([e][n] each, at kv + g * gstride): att [R * F][e].
+cudaError_t launch_col_attend(const float *Q, int R, int F, const float *kv, size_t gstride, int e, int n, int heads,
+                              float scale, float *att, cudaStream_t s, uint64_t *launches);
+// Rotary attention of the first nq of each row's T tokens over all T: QKV [R * T][3e] -> att [R * nq][e]; position
+// tables cs, sn [T][head width / 2]; `work` (row_attend_workspace floats) when row_attend_smem is 0.
+size_t row_attend_smem(int e, int T, int heads);
+size_t row_attend_workspace(int R, int T, int e);
+cudaError_t launch_row_attend(const float *QKV, int R, int T, int nq, int e, int heads, const float *cs, const float *sn,
+                              float *work, float *att, cudaStream_t s, uint64_t *launches);
+// tok [R][cls + F][e]: the class tokens, then the cells.
+cudaError_t launch_tokens(const float *X, const float *cls_tokens, int R, int F, int cls, int e, float *tok, cudaStream_t s,
+                          uint64_t *launches);
+// y [R][nq][e] += x [R][T][e] (first nq tokens of each row); x [R][T][e] = y for those tokens.
+cudaError_t launch_add_rows(float *y, const float *x, int R, int nq, int T, int e, cudaStream_t s, uint64_t *launches);
+cudaError_t launch_copy_rows(float *x, const float *y, int R, int nq, int T, int e, cudaStream_t s, uint64_t *launches);
+// y = a x (+ y when accumulate); y = x / a.
+cudaError_t launch_scale_add(float *y, const float *x, size_t n, float a, int accumulate, cudaStream_t s,
+                             uint64_t *launches);
+cudaError_t launch_divide(float *y, const float *x, size_t n, float a, cudaStream_t s, uint64_t *launches);
 // Opt `kernel` in to `bytes` of dynamic shared memory on the current device (the attribute is per function and
 // device); remembered per (device, kernel), so repeated calls cost a map lookup.
 cudaError_t allow_dynamic_smem(const void *kernel, size_t bytes);

@@ -96,6 +96,30 @@ def icl_shape(cfg, hid=64):
                 dec_ff=cfg["ff_factor"] * d, outs=mc if mc > 0 else cfg["num_quantiles"], max_classes=mc)
 
 
+def rows_shape(cfg):
+    """The column and row stages' sizes (tcu_rows_shape) of this configuration."""
+    e = cfg["embed_dim"]
+    return dict(e=e, group=cfg["col_feature_group_size"], inds=cfg["col_num_inds"], cls=cfg["row_num_cls"],
+                col_heads=cfg["col_nhead"], row_heads=cfg["row_nhead"], col_blocks=cfg["col_num_blocks"],
+                row_blocks=cfg["row_num_blocks"], col_ff=cfg["ff_factor"] * e, row_ff=cfg["ff_factor"] * e)
+
+
+def features(n, f, seed, missing=0.0):
+    """Seeded normalised feature rows [n][f] ~ N(0, 1) (prep standardises columns, src/prep.rs:4), a fraction
+    `missing` of the cells -100 (prep's marker for a missing value)."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((n, f)).astype(np.float32)
+    if missing:
+        x[rng.random((n, f)) < missing] = -100.0
+    return x
+
+
+def col_kv(features, blocks, e, inds, seed, digits=1):
+    """A seeded stand-in for a fitted member's column-stage cache (fit.rs:230: [features][digits][blocks][2][e][inds];
+    each group's inducing points' keys and values, unit scale)."""
+    return np.random.default_rng(seed).standard_normal((features, digits, blocks, 2, e, inds)).astype(np.float32)
+
+
 def row_reps(n, d, seed):
     """Seeded synthetic row representations [n][d] (unit scale, as the row stage's final LayerNorm leaves them)."""
     return np.random.default_rng(seed).standard_normal((n, d)).astype(np.float32)

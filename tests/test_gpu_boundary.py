@@ -132,7 +132,7 @@ def test_cuda_attend_declines_and_recovers(gpu, tmp_path):
     assert acc.fallbacks == 1 and "m7/meta" in acc.last_error
     assert acc.attend("m0/", 0, 0, np.zeros((2, m.d + 4), np.float32), m.d + 4, m.heads) is None
     assert acc.fallbacks == 2
-    # the column and row stages stay on the caller's CPU path
+    # weights made without the column and row stages: the rows hook declines, the caller's CPU path answers
     assert acc.rows("m0/", np.zeros((2, 5), np.float32), 10) is None
     # and after declining it answers again, with the same numbers
     assert np.array_equal(acc.stage("m0/", 0, ht, m.d, 10), got)
