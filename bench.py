@@ -450,6 +450,91 @@ def multi_configs(pkg, synth, gpu, w, d, world, rank, stream, comm, a, bf16):
     return res
 
 
+def full_predict(pkg, synth, gpu, vm, cfg, wt, a, rank, world, stream, out, classes):
+    """The whole prediction of config 2's member from normalised features (the AttendCached `rows` hook,
+    predict.rs:638-652): the column stage over the 100 feature groups, the row stage over the 104 tokens, the
+    in-context stage. The column-stage cache is a seeded stand-in of the fitted one's shape (the fit's column stage
+    is not on the device); 5% of the cells missing. Device buffers (CUDA events, max over ranks), the stages one by
+    one, and host buffers (tcu_rows, copies timed). At N = 1 rank 0 also times the oracle's whole prediction on a
+    bounded sample."""
+    import torch
+    R, F = a.rows, FEATURES
+    rs = synth.rows_shape(cfg)
+    ck = synth.col_kv(F, rs["col_blocks"], rs["e"], rs["inds"], 7)
+    vm.put_col_kv(ck)
+    xh = synth.features(R, F, 100 + rank, missing=0.05)
+    x = torch.from_numpy(xh).cuda()
+    T, e, d = rs["cls"] + F, rs["e"], rs["cls"] * rs["e"]
+    tok = torch.empty((R, T, e), device="cuda")
+    rep = torch.empty((R, d), device="cuda")
+    sp = stream.cuda_stream
+    torch.cuda.synchronize()
+
+    def step():
+        vm.rows_device(x.data_ptr(), R, classes, out.data_ptr(), sp)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(ev_time(stream, step, a.steps), world)
+    parts = {}
+    for name, fn in (("column", lambda: vm.embed_device(x.data_ptr(), R, tok.data_ptr(), sp)),
+                     ("row", lambda: vm.represent_device(tok.data_ptr(), R, rep.data_ptr(), sp)),
+                     ("in_context", lambda: vm.stage_device(rep.data_ptr(), R, classes, out.data_ptr(), sp))):
+        parts[name + "_ms"] = ev_time(stream, fn, 1)
+    # host buffers through the C ABI, copies in the timed region
+    xp = torch.from_numpy(xh).pin_memory().numpy()
+    op = torch.empty((R, classes), dtype=torch.float32).pin_memory().numpy()
+    vm.rows(xp, classes, out=op)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        vm.rows(xp, classes, out=op)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    # algorithmic flops per row (2 per multiply-add): column stage F blocks x (query, 128-key attention, out, FFN);
+    # row stage per block: keys and values of every token, queries and the rest for the query tokens (the class
+    # tokens only in the last block); in-context stage
+    ncol, nrow, inds, ffc, ffr = rs["col_blocks"], rs["row_blocks"], rs["inds"], rs["col_ff"], rs["row_ff"]
+    col = F * ncol * (2 * e * e + 4 * e * inds + 2 * e * e + 4 * e * ffc)
+    row = 0
+    for bi in range(nrow):
+        nq = rs["cls"] if bi == nrow - 1 else T
+        row += T * 4 * e * e + nq * (2 * e * e + 4 * T * e + 2 * e * e + 4 * e * ffr)
+    icl = stage_flops_per_row(a.train_rows, d, 12, 1024, 64, 4, 1024, classes)
+    res = {"workload": f"config 2 member, whole prediction of {R} rows x {F} normalised features (5% missing): column, "
+                       "row and in-context stages; column-stage cache a seeded stand-in",
+           "rows_per_s": R * world / (ms / 1e3), "ms_per_step": ms, "stages": parts,
+           "e2e": {"value": R * a.steps * world / e2e_s, "unit": "rows/s", "h2d_bytes_per_step": R * F * 4,
+                   "d2h_bytes_per_step": R * classes * 4},
+           "algorithmic_mflop_per_row": {"column": col / 1e6, "row": row / 1e6, "in_context": icl / 1e6}}
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        om = oracle.Model({k: v for k, v in wt.items() if k.startswith("icl_predictor.")}, cfg["icl_nhead"],
+                          cfg["icl_num_blocks"], cfg["max_classes"])
+        orm = oracle.RowsModel({k: v for k, v in wt.items() if k.startswith(("col_embedder.", "row_interactor."))}, cfg)
+        lb = pkg.record(a.kv, d, CHUNK) * (a.train_rows // CHUNK) + (pkg.record(a.kv, d, a.train_rows % CHUNK) if a.train_rows % CHUNK else 0)
+        layers = [vm.layer_bytes(l, lb) for l in range(12)]
+        scales = vm.scales()
+
+        def cpu(n):
+            rep_c = oracle.represent(orm, oracle.embed(orm, xh[:n], ck))
+            return oracle.in_context(om, a.kv, layers, scales, a.train_rows, CHUNK, rep_c, classes)
+
+        n = oracle.threads()
+        t0 = time.perf_counter()
+        cpu(n)
+        dt = time.perf_counter() - t0
+        n2 = int(min(R, max(n, n * 6.0 / max(dt, 1e-3))))
+        t0 = time.perf_counter()
+        want = cpu(n2)
+        dt2 = time.perf_counter() - t0
+        got = vm.rows(xh[:n2], classes)
+        res["max_diff_vs_oracle"] = float(np.abs(got - want).max())
+        res["cpu_baseline"] = {"value": n2 / dt2, "unit": "rows/s", "cores": oracle.threads(), "kind": "port",
+                               "sample": f"{n2} rows through the oracle's column, row and in-context stages, {dt2:.1f} s"}
+    return res
+
+
 def fit_baseline(pkg, synth, w, d, a):
     """Fitting's in-context stage (fit.rs:577-747): the device fit of config 2's 10,000 rows (CUDA events), and the
     oracle's fit on the host cores on a bounded sample of the same rows."""
@@ -505,7 +590,8 @@ def main():
     shape = synth.icl_shape(cfg)
     d = shape["d"]
     gpu = pkg.Gpu(local)
-    w = pkg.GpuWeights.from_tensors(gpu, shape, {k: v for k, v in wt.items() if k.startswith("icl_")}, for_fit=True)
+    # every stage's weights: the in-context ones for the headline, the column and row stages for the full predict
+    w = pkg.GpuWeights.from_tensors(gpu, shape, wt, for_fit=True, rows_shape=synth.rows_shape(cfg))
     # the fitted member: training rows through fitting's in-context stage on the device
     htr = torch.from_numpy(synth.row_reps(a.train_rows, d, 1)).cuda()
     ytr = torch.from_numpy(synth.labels(a.train_rows, 10, 2)).cuda()
@@ -610,6 +696,8 @@ def main():
         ts.sort()
         sizes.append({"rows": rs, "p50_us": ts[len(ts) // 2], "rows_per_s": rs / (ts[len(ts) // 2] * 1e-6)})
 
+    full = full_predict(pkg, synth, gpu, vm, cfg, wt, a, rank, world, stream, out, classes)
+
     hbm, bf16, kind = peaks()
     traffic = ncu_traffic(a)
     layer_bytes = pkg.record(a.kv, d, CHUNK) * (a.train_rows // CHUNK) + (pkg.record(a.kv, d, a.train_rows % CHUNK) if a.train_rows % CHUNK else 0)
@@ -646,6 +734,7 @@ def main():
                                       "cache_bytes": L * layer_bytes, "weight_bytes": weight_bytes,
                                       "p50_gbs": (L * layer_bytes + weight_bytes) / (pct(0.5) * 1e-6) / 1e9}},
         "latency_rows": sizes,
+        "full_predict": full,
         "clocks": clocks.summary(),
     }
     if not a.no_multi:

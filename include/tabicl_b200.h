@@ -103,7 +103,8 @@ TCU_API int tcu_model_put_scales(tcu_model *m, const float *scales, size_t count
 /* Bytes [offset, offset + nbytes) of `n{node}_kv{layer}`, exactly as stored (no repacking; src/fit.rs:224-241). */
 TCU_API int tcu_model_put_layer(tcu_model *m, int layer, size_t offset, const void *bytes, size_t nbytes);
 /* The column stage's cache `m{i}/col_kv` (src/fit.rs:230): [features][digits][column blocks][2][e][inds] floats, the
- * keys then the values ([e][inds] each) of every feature group's inducing points. Needed by the `rows` hook. */
+ * keys then the values ([e][inds] each) of every feature group's inducing points. Needed by the `rows` hook. A cache
+ * made by tcu_fit_icl_device takes its feature count from `count` (one label digit). */
 TCU_API int tcu_model_put_col_kv(tcu_model *m, const float *col_kv, size_t count);
 /* The whole of the above from a fitted bundle file, member `prefix` ("m0/", or "" for a raw fit), problem node
  * (col_kv too when the bundle holds it). */

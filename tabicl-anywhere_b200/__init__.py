@@ -329,6 +329,11 @@ class VramModel:
         self.gpu.check(lib().tcu_stage(self._h, _f32p(h), rows, d, out_n, _f32p(out)))
         return out
 
+    def put_col_kv(self, col_kv):
+        """The column stage's cache (fit.rs:230: [features][digits][blocks][2][e][inds] floats) for the rows hook."""
+        ck = np.ascontiguousarray(col_kv, dtype=np.float32).reshape(-1)
+        self.gpu.check(lib().tcu_model_put_col_kv(self._h, _f32p(ck), ck.size))
+
     def rows(self, x, out_n, out=None):
         """AttendCached::rows on host buffers: normalised rows [rows][features] through the column, row and in-context
         stages to [rows][out_n] decoder outputs. Returns None when the library declines (no column and row stages)."""

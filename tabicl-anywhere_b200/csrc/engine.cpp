@@ -1637,7 +1637,10 @@ int tcu_model_put_col_kv(tcu_model *m, const float *col_kv, size_t count) {
         const RowsWeights &rw = m->w->rows;
         if (!rw.on) fail(TCU_ERR_STATE, "model_put_col_kv: the weights have no column and row stages");
         const auto &rs = rw.shape;
-        const size_t want = (size_t)m->features * m->digits * rs.col_blocks * 2 * rs.e * rs.inds;
+        const size_t per_feature = (size_t)m->digits * rs.col_blocks * 2 * rs.e * rs.inds;
+        // a cache fitted on the device does not know its features: the column cache says how many
+        if (m->features < 1 && count % per_feature == 0) m->features = (int)(count / per_feature);
+        const size_t want = (size_t)m->features * per_feature;
         if (!col_kv || count != want || m->features < 1)
             fail(TCU_ERR_ARG, "model_put_col_kv: expected features * digits * column blocks * 2 * e * inducing points = " +
                                   std::to_string(want) + " floats");
