@@ -106,10 +106,16 @@ TCU_API int tcu_model_put_layer(tcu_model *m, int layer, size_t offset, const vo
  * keys then the values ([e][inds] each) of every feature group's inducing points. Needed by the `rows` hook. A cache
  * made by tcu_fit_icl_device takes its feature count from `count` (one label digit). */
 TCU_API int tcu_model_put_col_kv(tcu_model *m, const float *col_kv, size_t count);
+/* The member's feature count and label digits (meta[1] and meta[5]) for a cache made by tcu_fit_icl_device, before
+ * its col_kv is put (a member of more classes than the model tells apart has several digits, src/fit.rs:159-184). */
+TCU_API int tcu_model_set_columns(tcu_model *m, int features, int digits);
 /* The whole of the above from a fitted bundle file, member `prefix` ("m0/", or "" for a raw fit), problem node
  * (col_kv too when the bundle holds it). */
 TCU_API int tcu_model_from_bundle(tcu_weights *w, const char *path, const char *prefix, int node, tcu_model **out);
-/* Device bytes the cache holds (Gpu::model_bytes, for tier budgets). */
+/* Device bytes the cache holds (Gpu::model_bytes, src/gpu.rs:2064-2068, for tier budgets): the stored records,
+ * scales, column cache and tables, and the tensor-core attention's pre-split copy of the keys and values (head width
+ * 128), counted from creation although the first call builds it. Working memory that grows with the rows of a call
+ * is not counted. */
 TCU_API size_t tcu_model_bytes(const tcu_model *m);
 /* Copy back a layer's stored bytes / the scales (for writing a bundle after a device fit). */
 TCU_API int tcu_model_get_layer(const tcu_model *m, int layer, void *bytes, size_t nbytes);
@@ -151,6 +157,36 @@ TCU_API int tcu_sync(tcu_ctx *ctx, void *stream);
  * wait had given up, so that the give-up path (every CTA leaving at its next barrier after its copies land) and
  * its report can be exercised without making any wait run out. */
 TCU_API int tcu_debug_abort_next(tcu_ctx *ctx);
+
+/* ---- a whole member: its problems and the class tree (src/predict.rs:638-699) ----------------------------------- */
+
+typedef struct tcu_member tcu_member;
+/* A member of n_nodes problems, node i = nodes[i] (each made on the same weights), with its tree `m{i}/tree`
+ * ([leaf, rows, k, map[k]] per node, src/fit.rs:217-220) over `classes` classes. A
+ * leaf's map holds classes, an inner node's its children; the walk starts at node 0; every node's k is at most the
+ * decoder's outputs (its stage returns its first k). Node 0 holds the column stage's
+ * cache (col_kv) for tcu_member_rows. On success the member owns the nodes (tcu_member_free frees them); on failure
+ * they stay the caller's. TCU_ERR_FORMAT for a tree that is damaged, reaches a node twice or names a class or node
+ * out of range. */
+TCU_API int tcu_member_new(tcu_model *const *nodes, int n_nodes, const int32_t *tree, size_t tree_len, int classes,
+                           tcu_member **out);
+/* Every problem of member `prefix` of a fitted bundle (src/predict.rs:138-161), col_kv into node 0. */
+TCU_API int tcu_member_from_bundle(tcu_weights *w, const char *path, const char *prefix, tcu_member **out);
+TCU_API int tcu_member_nodes(const tcu_member *m);
+TCU_API int tcu_member_classes(const tcu_member *m);
+/* Problem `node` (owned by the member), for the per-problem `stage` hook; NULL when out of range. */
+TCU_API tcu_model *tcu_member_node(tcu_member *m, int node);
+TCU_API size_t tcu_member_bytes(const tcu_member *m);
+/* predict_raw's pass (src/predict.rs:638-699) for normalised rows x [rows][features]: the column and row stages once,
+ * the in-context stage of every problem, then for a tree each problem's scores as probabilities (temperature 0.9)
+ * multiplied down the tree and back to scores 0.9 ln(p + 1e-6); a member of one problem returns its decoder outputs
+ * as they are. out [rows][classes]. Host buffers (the `_device` form: device buffers queued on `stream`). */
+TCU_API int tcu_member_rows(tcu_member *m, const float *x, int rows, int features, float *out);
+TCU_API int tcu_member_rows_device(tcu_member *m, const float *x, int rows, float *out, void *stream);
+/* The tree step alone (src/predict.rs:664-692): every problem's scores laid end to end (problem i's [rows][k_i]
+ * after those of problems 0..i-1) to class scores out [rows][classes]. Device buffers. */
+TCU_API int tcu_member_combine_device(tcu_member *m, const float *scores, int rows, float *out, void *stream);
+TCU_API void tcu_member_free(tcu_member *m);
 
 /* ---- heads (src/table.rs) ------------------------------------------------------------------------------------ */
 

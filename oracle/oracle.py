@@ -320,6 +320,53 @@ def icl_fit(model, h, y, chunk, kv):
     return outs, scales
 
 
+def parse_tree(tree, n_nodes):
+    """predict.rs:141-148: per node (leaf, rows, k, map)."""
+    out, at = [], 0
+    for _ in range(n_nodes):
+        leaf, rows, k = (int(v) for v in tree[at:at + 3])
+        out.append((bool(leaf), rows, k, [int(v) for v in tree[at + 3:at + 3 + k]]))
+        at += 3 + k
+    return out
+
+
+def tree_scores(node_scores, tree, n_nodes, classes):
+    """predict.rs:664-692 in f32: every node's scores (node_scores[i], [n][k_i]) to class scores [n][classes]. Per row,
+    each node's scores become probabilities (the largest, from f32::MIN and ignoring NaN, subtracted; exp((v - top) /
+    0.9) summed in order; each over the sum), the recursive walk from node 0 multiplies them down the tree and adds
+    each leaf's share to its classes, and the result goes back to scores as 0.9 ln(p + 1e-6)."""
+    f = np.float32
+    nodes = parse_tree(tree, n_nodes)
+    n = np.asarray(node_scores[0]).shape[0]
+    probs = []
+    for i, (_, _, k, _) in enumerate(nodes):
+        p = np.array(node_scores[i], dtype=np.float32).reshape(n, k)
+        for r in range(n):
+            top = f(-3.4028235e38)
+            for v in p[r]:
+                top = np.fmax(top, v)
+            e = np.exp(((p[r] - top) / f(0.9)).astype(np.float32)).astype(np.float32)
+            total = f(0.0)
+            for v in e:
+                total = f(total + v)
+            p[r] = e / total
+        probs.append(p)
+
+    def walk(ni, r, weight, out):
+        leaf, _, _, mp = nodes[ni]
+        pr = probs[ni][r]
+        for j, target in enumerate(mp):
+            if leaf:
+                out[target] = f(out[target] + f(weight * pr[j]))
+            else:
+                walk(target, r, f(weight * pr[j]), out)
+
+    res = np.zeros((n, classes), np.float32)
+    for r in range(n):
+        walk(0, r, f(1.0), res[r])
+    return (f(0.9) * np.log(res + f(1e-6))).astype(np.float32)
+
+
 def finish_proba(sums, members, temperature):
     s = np.array(sums, dtype=np.float64)
     n, c = s.shape

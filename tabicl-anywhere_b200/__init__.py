@@ -5,6 +5,7 @@ The objects mirror the reference's accelerator side (src/gpu.rs, src/predict.rs:
 * `Gpu` - one device (gpu::Gpu)
 * `GpuWeights` - the in-context weights on it (gpu::GpuWeights)
 * `VramModel` - one fitted problem's key/value cache resident on it (gpu::VramModel)
+* `VramMember` - a fitted member's problems and its class tree, predicted whole (predict::predict_raw)
 * `CudaAttend` - the `AttendCached` implementation: `attend`, `stage`, `rows`, each returning None to decline
 
 Everything computes on the GPU through libtabicl_b200.so; there is no CPU path here. The library is built in-tree
@@ -16,6 +17,7 @@ import os
 import numpy as np
 
 from . import tirs  # noqa: F401  (bundle reader/writer for callers)
+from .plan import Plan  # noqa: F401
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libtabicl_b200.so")
@@ -108,6 +110,17 @@ def lib():
         "tcu_comm_allreduce_f64": (_c_int, [_c_void, _c_void, _c_size, _c_void]),
         "tcu_comm_wait": (_c_int, [_c_void, _c_void, _c_int]),
         "tcu_model_slice": (_c_int, [_c_void, _c_int, _c_int, P(_c_void)]),
+        "tcu_model_set_columns": (_c_int, [_c_void, _c_int, _c_int]),
+        "tcu_member_new": (_c_int, [P(_c_void), _c_int, P(ctypes.c_int32), _c_size, _c_int, P(_c_void)]),
+        "tcu_member_from_bundle": (_c_int, [_c_void, ctypes.c_char_p, ctypes.c_char_p, P(_c_void)]),
+        "tcu_member_nodes": (_c_int, [_c_void]),
+        "tcu_member_classes": (_c_int, [_c_void]),
+        "tcu_member_node": (_c_void, [_c_void, _c_int]),
+        "tcu_member_bytes": (_c_size, [_c_void]),
+        "tcu_member_rows": (_c_int, [_c_void, _c_float_p, _c_int, _c_int, _c_float_p]),
+        "tcu_member_rows_device": (_c_int, [_c_void, _c_void, _c_int, _c_void, _c_void]),
+        "tcu_member_combine_device": (_c_int, [_c_void, _c_void, _c_int, _c_void, _c_void]),
+        "tcu_member_free": (None, [_c_void]),
         "tcu_stage_sharded_device": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_void, _c_void]),
     }
     for name, (res, args) in sig.items():
@@ -267,9 +280,10 @@ class GpuWeights:
 class VramModel:
     """One fitted problem's cache resident on the device (gpu::VramModel, src/gpu.rs:2033-2116)."""
 
-    def __init__(self, weights, handle):
+    def __init__(self, weights, handle, owner=None):
         self.weights, self.gpu, self._h = weights, weights.gpu, handle
         self.d = weights.shape["d"]
+        self._owner = owner  # a VramMember holding this problem (it frees the handle), or None
 
     @staticmethod
     def from_bundle(weights, path, prefix="", node=0):
@@ -383,8 +397,83 @@ class VramModel:
         return out.reshape(s["layers"], s["d"])
 
     def free(self):
-        if self._h:
+        if self._h and self._owner is None:
             lib().tcu_model_free(self._h)
+        self._h = _c_void()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Stats:
+    """The counters of predict::Stats (src/predict.rs) that a pass on the device moves: rows, passes and in-context
+    layers run on the card."""
+
+    def __init__(self):
+        self.rows = self.passes = self.card_layers = 0
+
+
+class VramMember:
+    """A fitted member resident on the device: its problems (one VramModel each, node 0 with the column stage's
+    cache) and its class tree (predict::Cache, src/predict.rs:115-161), predicted whole (src/predict.rs:638-699)."""
+
+    def __init__(self, weights, handle):
+        self.weights, self.gpu, self._h = weights, weights.gpu, handle
+        self.classes = int(lib().tcu_member_classes(handle))
+        self.n_nodes = int(lib().tcu_member_nodes(handle))
+
+    @staticmethod
+    def from_bundle(weights, path, prefix=""):
+        h = _c_void()
+        weights.gpu.check(lib().tcu_member_from_bundle(weights._h, os.fsencode(path), prefix.encode(), ctypes.byref(h)))
+        return VramMember(weights, h)
+
+    @staticmethod
+    def from_nodes(nodes, tree, classes):
+        """The member of problems `nodes` (VramModel, node 0 first; the member takes them over: their handles then
+        belong to it) with tree ints `tree` (Plan.tree) over `classes` classes."""
+        w = nodes[0].weights
+        arr = (_c_void * len(nodes))(*[n._h.value for n in nodes])
+        t = np.ascontiguousarray(tree, dtype=np.int32)
+        h = _c_void()
+        w.gpu.check(lib().tcu_member_new(arr, len(nodes), t.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), t.size,
+                                         int(classes), ctypes.byref(h)))
+        mb = VramMember(w, h)
+        for n in nodes:
+            n._owner = mb
+        return mb
+
+    def node(self, i):
+        """Problem i as a VramModel (valid while the member is)."""
+        p = lib().tcu_member_node(self._h, i)
+        if not p:
+            raise IndexError(i)
+        return VramModel(self.weights, _c_void(p), owner=self)
+
+    @property
+    def nbytes(self):
+        return int(lib().tcu_member_bytes(self._h))
+
+    def rows(self, x, out=None):
+        """Class scores [rows][classes] of normalised rows x [rows][features] (host buffers)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        n, f = x.shape
+        out = np.empty((n, self.classes), dtype=np.float32) if out is None else out
+        self.gpu.check(lib().tcu_member_rows(self._h, _f32p(x), n, f, _f32p(out)))
+        return out
+
+    def rows_device(self, x_ptr, rows, out_ptr, stream=None):
+        return self.gpu.check(lib().tcu_member_rows_device(self._h, x_ptr, rows, out_ptr, stream))
+
+    def combine_device(self, scores_ptr, rows, out_ptr, stream=None):
+        return self.gpu.check(lib().tcu_member_combine_device(self._h, scores_ptr, rows, out_ptr, stream))
+
+    def free(self):
+        if self._h:
+            lib().tcu_member_free(self._h)
             self._h = _c_void()
 
     def __del__(self):
@@ -392,6 +481,53 @@ class VramModel:
             self.free()
         except Exception:
             pass
+
+
+def predict_raw(member, x, rows_per_pass=256, stats=None):
+    """predict::predict_raw (src/predict.rs:631-699) on the device: class scores [n][classes] of n normalised rows x
+    [n][features], in passes of rows_per_pass rows (PredictOpts::rows_per_pass, default 256); each pass runs the
+    column and row stages, every problem's in-context stage and the class tree."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n = x.shape[0]
+    out = np.empty((n, member.classes), dtype=np.float32)
+    step = max(1, int(rows_per_pass))
+    layers = member.weights.shape["layers"] * member.n_nodes
+    for r0 in range(0, n, step):
+        member.rows(x[r0:r0 + step], out=out[r0:r0 + step])
+        if stats is not None:
+            stats.rows += min(step, n - r0)
+            stats.passes += 1
+            stats.card_layers += layers
+    return out
+
+
+def fit_member(weights, h, y, classes, features, col_kv, chunk=256, kv=KV_F32):
+    """The in-context part of fitting one member on the device, for any number of classes: the plan's tree
+    (fit::Plan, src/fit.rs:159-221) and each node fitted on its own rows and targets (src/fit.rs:577-747). h: the
+    training rows' representations [rows][d] (host), y: their classes; col_kv: the member's column-stage cache over
+    `features` features (one copy per label digit of the plan).
+    Returns (VramMember, Plan)."""
+    import torch  # device buffers for the fit
+
+    h = np.ascontiguousarray(h, dtype=np.float32)
+    plan = Plan.new(weights.shape["max_classes"], y, classes)
+    nodes = []
+    try:
+        for nd in plan.nodes:
+            rows = np.arange(len(h)) if nd.rows is None else np.asarray(nd.rows)
+            hd = torch.from_numpy(np.ascontiguousarray(h[rows])).cuda()
+            yd = torch.from_numpy(np.ascontiguousarray(nd.y, dtype=np.float32)).cuda()
+            torch.cuda.synchronize()
+            nodes.append(fit_icl(weights, hd.data_ptr(), yd.data_ptr(), len(rows), chunk, kv))
+            torch.cuda.synchronize()
+        ck = np.ascontiguousarray(col_kv, dtype=np.float32)
+        weights.gpu.check(lib().tcu_model_set_columns(nodes[0]._h, features, len(plan.bases)))
+        nodes[0].put_col_kv(ck)
+        return VramMember.from_nodes(nodes, plan.tree(len(h)), classes), plan
+    except Exception:
+        for m in nodes:
+            m.free()
+        raise
 
 
 COMM_ID_BYTES = 128

@@ -17,6 +17,7 @@
 #include <array>
 #include <atomic>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -1282,6 +1283,124 @@ static void rows_stage(tcu_ctx *ctx, tcu_model *m, const float *x, int R, int ou
     stage_replay(ctx, m, R, out_n, s);
 }
 
+// ---- a member's problems and the class tree (predict.rs:638-699) -------------------------------------------------
+
+// One node of `m{i}/tree` (fit.rs:217-220): [leaf, rows, k, map[k]].
+struct TreeNode {
+    bool leaf;
+    int rows, k;
+    std::vector<int> map;
+};
+
+static std::vector<TreeNode> parse_tree(const int32_t *tree, size_t len, int n_nodes) {
+    if (n_nodes < 1) fail(TCU_ERR_FORMAT, "tree: no nodes");
+    std::vector<TreeNode> out;
+    size_t at = 0;
+    for (int i = 0; i < n_nodes; i++) {
+        if (at + 3 > len || tree[at + 2] < 1 || at + 3 + (size_t)tree[at + 2] > len) fail(TCU_ERR_FORMAT, "tree is damaged");
+        TreeNode n{tree[at] != 0, tree[at + 1], tree[at + 2], {}};
+        n.map.assign(tree + at + 3, tree + at + 3 + n.k);
+        at += 3 + (size_t)n.k;
+        out.push_back(std::move(n));
+    }
+    return out;
+}
+
+}  // namespace tcu
+
+struct tcu_member {
+    tcu_ctx *ctx = nullptr;
+    std::vector<tcu_model *> nodes;  // owned
+    std::vector<TreeNode> tree;
+    int classes = 0;
+    std::vector<int> walk;   // node indices in the order predict.rs:676-687's walk visits them
+    std::vector<int> koff;   // per node: offset of its scores among all problems' [R][k] blocks, in units of R
+    int ksum = 0;
+    DevBuf tnodes, tmap;     // the walk as the combine kernel reads it
+    DevBuf rep, tok, scores, wbuf, out;
+};
+
+namespace tcu {
+
+// The walk of predict.rs:676-687 from node 0: a node, then each child in map order. Checks every target (a leaf's
+// against the classes, an inner node's against the nodes, none reached twice) and lays the walk out for the kernel.
+static void member_tables(tcu_member *mb) {
+    const int n = (int)mb->tree.size();
+    std::vector<int> pos(n, -1);
+    std::function<void(int, int)> visit = [&](int ni, int depth) {
+        if (depth > n || pos[ni] >= 0) fail(TCU_ERR_FORMAT, "tree: node " + std::to_string(ni) + " is reached twice");
+        pos[ni] = (int)mb->walk.size();
+        mb->walk.push_back(ni);
+        const TreeNode &t = mb->tree[ni];
+        for (int c : t.map) {
+            if (t.leaf) {
+                if (c < 0 || c >= mb->classes) fail(TCU_ERR_FORMAT, "tree: class " + std::to_string(c) + " out of range");
+            } else {
+                if (c < 0 || c >= n) fail(TCU_ERR_FORMAT, "tree: child " + std::to_string(c) + " out of range");
+                visit(c, depth + 1);
+            }
+        }
+    };
+    visit(0, 0);
+    mb->koff.assign(n, 0);
+    mb->ksum = 0;
+    for (int i = 0; i < n; i++) mb->koff[i] = mb->ksum, mb->ksum += mb->tree[i].k;
+    std::vector<int4> tn;
+    std::vector<int> tm;
+    for (int ni : mb->walk) {
+        const TreeNode &t = mb->tree[ni];
+        tn.push_back(make_int4(t.k, t.leaf ? 1 : 0, mb->koff[ni], (int)tm.size()));
+        for (int c : t.map) tm.push_back(t.leaf ? c : pos[c]);
+    }
+    mb->tnodes.ensure(tn.size() * sizeof(int4));
+    mb->tmap.ensure(tm.size() * sizeof(int));
+    CU(cudaMemcpy(mb->tnodes.p, tn.data(), tn.size() * sizeof(int4), cudaMemcpyHostToDevice));
+    CU(cudaMemcpy(mb->tmap.p, tm.data(), tm.size() * sizeof(int), cudaMemcpyHostToDevice));
+}
+
+// predict.rs:664-692: every problem's scores (mb->scores, or `scores` laid out the same way) to class scores
+static void member_combine(tcu_ctx *ctx, tcu_member *mb, const float *scores, int R, float *out, cudaStream_t s) {
+    mb->wbuf.ensure(sizeof(float) * (size_t)mb->tree.size() * R);
+    Launch{ctx, s}(launch_tree_combine(scores, mb->tnodes.as<int4>(), mb->tmap.as<int>(), (int)mb->walk.size(), R,
+                                       mb->classes, mb->wbuf.as<float>(), out, s, &ctx->launches),
+                   "class tree");
+}
+
+// predict.rs:638-699 for R normalised rows x (device [R][F]): the column and row stages once (node 0's column cache),
+// every problem's in-context stage, then the tree; the result is left in mb->out [R][classes], or for a member of
+// one problem in node 0's out buffer (returned).
+static const float *member_rows(tcu_ctx *ctx, tcu_member *mb, const float *x, int R, cudaStream_t s) {
+    tcu_model *m0 = mb->nodes[0];
+    for (auto *m : mb->nodes) check_ready(m);
+    check_rows_ready(m0);
+    const auto &rs = m0->w->rows.shape;
+    const size_t hd = sizeof(float) * (size_t)R * m0->w->shape.d;
+    mb->tok.ensure(sizeof(float) * (size_t)R * (rs.cls + m0->features) * rs.e);
+    if (mb->nodes.size() == 1) {
+        if (m0->h.ensure(hd)) drop_graphs(m0);
+        embed(ctx, m0, x, R, mb->tok.as<float>(), s);
+        represent(ctx, m0, mb->tok.as<float>(), R, m0->h.as<float>(), s);
+        stage_replay(ctx, m0, R, mb->tree[0].k, s);
+        return m0->out.as<float>();
+    }
+    mb->rep.ensure(hd);
+    embed(ctx, m0, x, R, mb->tok.as<float>(), s);
+    represent(ctx, m0, mb->tok.as<float>(), R, mb->rep.as<float>(), s);
+    mb->scores.ensure(sizeof(float) * (size_t)R * mb->ksum);
+    for (int ni : mb->walk) {
+        tcu_model *m = mb->nodes[ni];
+        const int k = mb->tree[ni].k;
+        if (m->h.ensure(hd)) drop_graphs(m);
+        CU(cudaMemcpyAsync(m->h.p, mb->rep.p, hd, cudaMemcpyDeviceToDevice, s));  // the stage consumes its rows
+        stage_replay(ctx, m, R, k, s);
+        CU(cudaMemcpyAsync(mb->scores.as<float>() + (size_t)mb->koff[ni] * R, m->out.p, sizeof(float) * (size_t)R * k,
+                           cudaMemcpyDeviceToDevice, s));
+    }
+    mb->out.ensure(sizeof(float) * (size_t)R * mb->classes);
+    member_combine(ctx, mb, mb->scores.as<float>(), R, mb->out.as<float>(), s);
+    return mb->out.as<float>();
+}
+
 // ---- training rows split across devices -----------------------------------------------------------------------
 
 static void nccl_check(ncclResult_t r, const char *what) {
@@ -1337,9 +1456,21 @@ static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, in
     const int d = sh.d, L = sh.layers;
     cudaStream_t s = ctx->stream;
     ensure_work(m.get(), rows);
-    DevBuf kvT, kvf, fit_tiles;
+    DevBuf kvT, kvf, fit_tiles, fit_items;
     kvT.ensure(sizeof(float) * (size_t)rows * 2 * d);
     kvf.ensure(layer_bytes_of(0, d, rows, chunk));
+    // the f32 view's decode items (the few-row attention of a small node reads them): f32 chunking
+    const int2 *items = m->items.as<int2>();
+    int nitems = m->nitems;
+    if (kv != 0) {
+        std::vector<int2> it;
+        const int ks = decode_keys_per_item(0);
+        for (int ci = 0, r0 = 0; r0 < rows; ci++, r0 += chunk)
+            for (int k0 = 0; k0 < std::min(chunk, rows - r0); k0 += ks) it.push_back(make_int2(ci, k0));
+        fit_items.ensure(it.size() * sizeof(int2));
+        CU(cudaMemcpy(fit_items.p, it.data(), it.size() * sizeof(int2), cudaMemcpyHostToDevice));
+        items = fit_items.as<int2>(), nitems = (int)it.size();
+    }
     Launch ck{ctx, s};
     ck(launch_add_y(h, y, rows, d, sh.max_classes, w->icl_y, s, &ctx->launches), "add_y");
     // the float view of a layer (for the training rows' own attention) has its own items/tiles: same chunking
@@ -1366,7 +1497,7 @@ static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, in
         }
         query_rows(ctx, m.get(), l, m->scales.as<float>() + (size_t)l * d, h, rows, m->q.as<float>(), s);
         // the f32 view has the same chunking, and flash tiles depend only on chunking
-        attend_layer(ctx, m.get(), fl, rows, chunk, 0, nullptr, 0, m->tiles.as<int4>(), m->ntiles, m->q.as<float>(), rows,
+        attend_layer(ctx, m.get(), fl, rows, chunk, 0, items, nitems, m->tiles.as<int4>(), m->ntiles, m->q.as<float>(), rows,
                      m->att.as<float>(), s, eK, eV, false, ft);
         block_tail(ctx, m.get(), l, h, m->att.as<float>(), rows, s);
     }
@@ -1583,52 +1714,62 @@ int tcu_model_put_layer(tcu_model *m, int layer, size_t offset, const void *byte
     });
 }
 
+// Problem `node` of member p of bundle b (the col_kv too when with_col and the bundle holds it).
+static tcu_model *load_node(tcu_weights *w, const Bundle &b, const std::string &p, int node, bool with_col) {
+    auto meta = b.i32s(p + "meta");
+    auto tree = b.i32s(p + "tree");
+    if (meta.size() != 7) fail(TCU_ERR_FORMAT, p + "meta is damaged");
+    auto nodes = parse_tree(tree.data(), tree.size(), meta[6]);
+    if (node < 0 || node >= (int)nodes.size()) fail(TCU_ERR_ARG, "model_from_bundle: no such node");
+    auto ok = [&](int r) {
+        if (r != TCU_OK) fail(r, w->ctx->err);
+    };
+    tcu_model *m = nullptr;
+    ok(tcu_model_new(w, meta.data(), nodes[node].rows, nodes[node].k, &m));
+    ModelPtr guard(m);
+    auto sc = b.f32s(p + "n" + std::to_string(node) + "_scale");
+    ok(tcu_model_put_scales(m, sc.data(), sc.size()));
+    if (with_col && w->rows.on && b.has(p + "col_kv")) {
+        auto ck = b.f32s(p + "col_kv");
+        ok(tcu_model_put_col_kv(m, ck.data(), ck.size()));
+    }
+    for (int l = 0; l < w->shape.layers; l++) {
+        std::string name = p + "n" + std::to_string(node) + "_kv" + std::to_string(l);
+        const Entry &e = b.entry(name);
+        if (e.nbytes != m->layer_bytes) fail(TCU_ERR_FORMAT, name + ": " + std::to_string(e.nbytes) + " bytes, expected " + std::to_string(m->layer_bytes));
+        auto bytes = b.bytes(name);
+        ok(tcu_model_put_layer(m, l, 0, bytes.data(), bytes.size()));
+    }
+    return guard.release();
+}
+
 int tcu_model_from_bundle(tcu_weights *w, const char *path, const char *prefix, int node, tcu_model **out) {
     if (!w) return TCU_ERR_ARG;
     return guarded(w->ctx, [&]() -> int {
         if (!path || !prefix || !out) fail(TCU_ERR_ARG, "model_from_bundle: null argument");
         auto b = Bundle::open(path);
-        std::string p(prefix);
-        auto meta = b->i32s(p + "meta");
-        auto tree = b->i32s(p + "tree");
-        if (meta.size() != 7) fail(TCU_ERR_FORMAT, p + "meta is damaged");
-        // predict.rs:141-148: per node [leaf, rows, k, map...]
-        size_t at = 0;
-        int node_rows = -1, node_k = -1;
-        for (int i = 0; i < meta[6]; i++) {
-            if (at + 3 > tree.size()) fail(TCU_ERR_FORMAT, p + "tree is damaged");
-            if (i == node) node_rows = tree[at + 1], node_k = tree[at + 2];
-            at += 3 + (size_t)tree[at + 2];
-        }
-        if (node_rows < 0) fail(TCU_ERR_ARG, "model_from_bundle: no such node");
-        tcu_model *m = nullptr;
-        int r = tcu_model_new(w, meta.data(), node_rows, node_k, &m);
-        if (r != TCU_OK) return r;
-        ModelPtr guard(m);
-        auto sc = b->f32s(p + "n" + std::to_string(node) + "_scale");
-        r = tcu_model_put_scales(m, sc.data(), sc.size());
-        if (r != TCU_OK) return r;
-        if (w->rows.on && b->has(p + "col_kv")) {
-            auto ck = b->f32s(p + "col_kv");
-            r = tcu_model_put_col_kv(m, ck.data(), ck.size());
-            if (r != TCU_OK) return r;
-        }
-        for (int l = 0; l < w->shape.layers; l++) {
-            std::string name = p + "n" + std::to_string(node) + "_kv" + std::to_string(l);
-            const Entry &e = b->entry(name);
-            if (e.nbytes != m->layer_bytes) fail(TCU_ERR_FORMAT, name + ": " + std::to_string(e.nbytes) + " bytes, expected " + std::to_string(m->layer_bytes));
-            auto bytes = b->bytes(name);
-            r = tcu_model_put_layer(m, l, 0, bytes.data(), bytes.size());
-            if (r != TCU_OK) return r;
-        }
-        *out = guard.release();
+        *out = load_node(w, *b, prefix, node, true);
         return TCU_OK;
     });
 }
 
 size_t tcu_model_bytes(const tcu_model *m) {
     if (!m) return 0;
-    return m->layers.bytes + m->scales.bytes + m->items.bytes + m->tiles.bytes + m->col_kv.bytes;
+    // the tensor-core attention's pre-split copy of the keys and values is built by the first call: it is counted
+    // from the start, so that a budget charged at load time holds afterwards
+    const size_t tc = std::max(m->tctiles.bytes, tc_shape(m) ? tc_layer_bytes(m) * m->w->shape.layers : 0);
+    return m->layers.bytes + m->scales.bytes + m->items.bytes + m->tiles.bytes + m->col_kv.bytes + tc + m->rtiles.bytes +
+           m->rtmaps.bytes + m->rlayers.bytes + m->rsync.bytes;
+}
+
+int tcu_model_set_columns(tcu_model *m, int features, int digits) {
+    if (!m) return TCU_ERR_ARG;
+    return guarded(m->w->ctx, [&]() -> int {
+        if (features < 1 || digits < 1) fail(TCU_ERR_ARG, "model_set_columns: features and digits must be positive");
+        if (m->col_kv.p) fail(TCU_ERR_STATE, "model_set_columns: the column cache is already put");
+        m->features = features, m->digits = digits;
+        return TCU_OK;
+    });
 }
 
 int tcu_model_put_col_kv(tcu_model *m, const float *col_kv, size_t count) {
@@ -2009,6 +2150,125 @@ int tcu_stage_sharded_device(tcu_model *m, tcu_comm *c, const float *h, int rows
         CU(cudaMemcpyAsync(out, m->out.p, sizeof(float) * (size_t)rows * out_n, cudaMemcpyDeviceToDevice, s));
         return TCU_OK;
     });
+}
+
+int tcu_member_new(tcu_model *const *nodes, int n_nodes, const int32_t *tree, size_t tree_len, int classes,
+                   tcu_member **out) {
+    if (!nodes || n_nodes < 1 || !nodes[0]) return TCU_ERR_ARG;
+    tcu_ctx *ctx = nodes[0]->w->ctx;
+    return guarded(ctx, [&]() -> int {
+        if (!tree || !out || classes < 1) fail(TCU_ERR_ARG, "member_new: bad argument");
+        std::unique_ptr<tcu_member> mb(new tcu_member());
+        mb->ctx = ctx, mb->classes = classes;
+        mb->tree = parse_tree(tree, tree_len, n_nodes);
+        for (int i = 0; i < n_nodes; i++) {
+            tcu_model *m = nodes[i];
+            if (!m || m->w != nodes[0]->w) fail(TCU_ERR_ARG, "member_new: every node needs the same weights");
+            if (mb->tree[i].k > m->w->shape.outs)
+                fail(TCU_ERR_ARG, "member_new: node " + std::to_string(i) + " has " + std::to_string(mb->tree[i].k) +
+                                      " outputs, more than the decoder's " + std::to_string(m->w->shape.outs));
+            for (int j = 0; j < i; j++)
+                if (nodes[j] == m) fail(TCU_ERR_ARG, "member_new: a node is given twice");
+        }
+        member_tables(mb.get());
+        mb->nodes.assign(nodes, nodes + n_nodes);  // owned from here on
+        *out = mb.release();
+        return TCU_OK;
+    });
+}
+
+int tcu_member_from_bundle(tcu_weights *w, const char *path, const char *prefix, tcu_member **out) {
+    if (!w) return TCU_ERR_ARG;
+    return guarded(w->ctx, [&]() -> int {
+        if (!path || !prefix || !out) fail(TCU_ERR_ARG, "member_from_bundle: null argument");
+        auto b = Bundle::open(path);
+        const std::string p(prefix);
+        auto meta = b->i32s(p + "meta");
+        auto tree = b->i32s(p + "tree");
+        if (meta.size() != 7) fail(TCU_ERR_FORMAT, p + "meta is damaged");
+        std::unique_ptr<tcu_member> mb(new tcu_member());
+        mb->ctx = w->ctx, mb->classes = meta[2];
+        mb->tree = parse_tree(tree.data(), tree.size(), meta[6]);
+        member_tables(mb.get());
+        std::vector<ModelPtr> nodes;
+        for (int i = 0; i < meta[6]; i++) nodes.emplace_back(load_node(w, *b, p, i, i == 0));
+        for (auto &n : nodes) mb->nodes.push_back(n.release());
+        *out = mb.release();
+        return TCU_OK;
+    });
+}
+
+int tcu_member_nodes(const tcu_member *m) { return m ? (int)m->nodes.size() : 0; }
+int tcu_member_classes(const tcu_member *m) { return m ? m->classes : 0; }
+tcu_model *tcu_member_node(tcu_member *m, int node) {
+    return m && node >= 0 && node < (int)m->nodes.size() ? m->nodes[node] : nullptr;
+}
+
+size_t tcu_member_bytes(const tcu_member *m) {
+    if (!m) return 0;
+    size_t n = m->tnodes.bytes + m->tmap.bytes;
+    for (auto *x : m->nodes) n += tcu_model_bytes(x);
+    return n;
+}
+
+int tcu_member_rows_device(tcu_member *m, const float *x, int rows, float *out, void *stream) {
+    if (!m) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->ctx;
+    return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
+        if (rows < 0 || (rows && (!x || !out))) fail(TCU_ERR_ARG, "member_rows: bad argument");
+        if (rows == 0) return TCU_OK;
+        cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+        const float *res = member_rows(ctx, m, x, rows, s);
+        CU(cudaMemcpyAsync(out, res, sizeof(float) * (size_t)rows * m->classes, cudaMemcpyDeviceToDevice, s));
+        return TCU_OK;
+    });
+}
+
+int tcu_member_rows(tcu_member *m, const float *x, int rows, int features, float *out) {
+    if (!m) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->ctx;
+    return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
+        tcu_model *m0 = m->nodes[0];
+        if (features != m0->features) fail(TCU_ERR_ARG, "member_rows: features differ from the cache's " + std::to_string(m0->features));
+        if (rows < 0 || (rows && (!x || !out))) fail(TCU_ERR_ARG, "member_rows: bad argument");
+        if (rows == 0) return TCU_OK;
+        check_rows_ready(m0);
+        cudaStream_t s = ctx->stream;
+        const size_t n = (size_t)rows * features;
+        m0->cin.ensure(sizeof(float) * n);
+        CU(cudaMemcpyAsync(m0->cin.p, x, sizeof(float) * n, cudaMemcpyHostToDevice, s));
+        const float *res = member_rows(ctx, m, m0->cin.as<float>(), rows, s);
+        CU(cudaMemcpyAsync(out, res, sizeof(float) * (size_t)rows * m->classes, cudaMemcpyDeviceToHost, s));
+        CU(cudaStreamSynchronize(s));
+        check_device_error(ctx);
+        return TCU_OK;
+    });
+}
+
+int tcu_member_combine_device(tcu_member *m, const float *scores, int rows, float *out, void *stream) {
+    if (!m) return TCU_ERR_ARG;
+    tcu_ctx *ctx = m->ctx;
+    return guarded(ctx, [&]() -> int {
+        if (rows < 0 || (rows && (!scores || !out))) fail(TCU_ERR_ARG, "member_combine: bad argument");
+        if (rows == 0) return TCU_OK;
+        member_combine(ctx, m, scores, rows, out, stream ? (cudaStream_t)stream : ctx->stream);
+        return TCU_OK;
+    });
+}
+
+void tcu_member_free(tcu_member *m) {
+    if (!m) return;
+    std::vector<tcu_model *> nodes;
+    nodes.swap(m->nodes);
+    {
+        std::lock_guard<std::recursive_mutex> lock(m->ctx->mu);
+        cudaSetDevice(m->ctx->device);
+        delete m;
+    }
+    // each node lets go of the weights (and they of the context) after the member's own buffers are gone
+    for (auto *x : nodes) tcu_model_free(x);
 }
 
 int tcu_sync(tcu_ctx *ctx, void *stream) {

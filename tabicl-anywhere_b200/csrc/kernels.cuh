@@ -201,6 +201,10 @@ cudaError_t launch_copy_rows(float *x, const float *y, int R, int nq, int T, int
 cudaError_t launch_scale_add(float *y, const float *x, size_t n, float a, int accumulate, cudaStream_t s,
                              uint64_t *launches);
 cudaError_t launch_divide(float *y, const float *x, size_t n, float a, cudaStream_t s, uint64_t *launches);
+// The class tree (tree.cu; src/predict.rs:661-692): nodes' scores (node t's [R][k] at logits + nodes[t].z * R) to
+// class scores out [R][classes]; nodes in walk order {k, leaf, score offset, map offset}; wbuf [n_nodes][R].
+cudaError_t launch_tree_combine(const float *logits, const int4 *nodes, const int *map, int n_nodes, int R, int classes,
+                                float *wbuf, float *out, cudaStream_t s, uint64_t *launches);
 // Opt `kernel` in to `bytes` of dynamic shared memory on the current device (the attribute is per function and
 // device); remembered per (device, kernel), so repeated calls cost a map lookup.
 cudaError_t allow_dynamic_smem(const void *kernel, size_t bytes);
