@@ -188,6 +188,73 @@ TCU_API int tcu_member_rows_device(tcu_member *m, const float *x, int rows, floa
 TCU_API int tcu_member_combine_device(tcu_member *m, const float *scores, int rows, float *out, void *stream);
 TCU_API void tcu_member_free(tcu_member *m);
 
+/* ---- the card tier (gpu::VramTier and its handle, src/gpu.rs:2450-2701; the ledger of src/warm.rs:28-115) ------- */
+
+typedef struct tcu_tier tcu_tier;     /* fitted problems resident on one device for many tenants */
+typedef struct tcu_handle tcu_handle; /* one tenant's use of the tier for one fitted bundle: an AttendCached */
+typedef struct tcu_pin tcu_pin;       /* test hook: a problem held as a prediction holds it */
+/* A bundle read through the caller's positional reads (ReadAt, src/store.rs:45-50: a file, memory, object storage,
+ * a sealed bundle decrypted as it is read): read_at fills buf with n bytes at offset and returns 0, nonzero on failure.
+ * Called from the tier's loading threads, possibly at once: it must be safe to call concurrently, and `user` must
+ * outlive the handle and every load it started. */
+typedef struct {
+    void *user;
+    int (*read_at)(void *user, uint64_t offset, void *buf, size_t n);
+    uint64_t size;
+} tcu_source;
+
+/* VramTier::new (gpu.rs:2512-2514): `budget` bytes of fitted problems on the device in all, `tenant_budget` (at most
+ * `budget`) per tenant. background nonzero: a first prediction starts its problem's load on a thread of its own and
+ * declines meanwhile (natively, gpu.rs:2690-2698); zero: the load runs in that call, which then answers (gpu.rs:
+ * 2683-2689). ctx NULL: a tier that only keeps its books (the tcu_tier_debug_* entry points), without a device. */
+TCU_API int tcu_tier_new(tcu_ctx *ctx, size_t budget, size_t tenant_budget, int background, tcu_tier **out);
+/* Waits for loads in flight, then releases every problem not in use (handles must be freed before the tier). */
+TCU_API void tcu_tier_free(tcu_tier *t);
+/* Wait until no load started by a prediction is still running. */
+TCU_API void tcu_tier_wait(tcu_tier *t);
+/* Bytes the tier holds, in all and by `tenant` (problems being loaded included) (gpu.rs:2517-2519). */
+TCU_API void tcu_tier_held(tcu_tier *t, const char *tenant, size_t *all, size_t *mine);
+/* Bytes of `tenant`'s problems that are loaded and ready (gpu.rs:2522-2524). */
+TCU_API size_t tcu_tier_ready(tcu_tier *t, const char *tenant);
+/* Bytes really on the device, in all and of `tenant`: what the tier holds plus what was evicted but is still in use
+ * by a prediction; never more than the budgets (gpu.rs:2528-2531). */
+TCU_API void tcu_tier_on_card(tcu_tier *t, const char *tenant, size_t *all, size_t *mine);
+/* Predictions the device was asked for but declined because it failed, and the last reason (gpu.rs:2504-2506,
+ * 2534-2536): the reason's length (0: none), copied NUL-terminated into buf[n]. */
+TCU_API uint64_t tcu_tier_fallbacks(const tcu_tier *t);
+TCU_API size_t tcu_tier_last_error(tcu_tier *t, char *buf, size_t n);
+/* Release everything `tenant` holds (for `model` only, if not NULL); problems in use by a prediction are released
+ * when it finishes (gpu.rs:2538-2542). */
+TCU_API void tcu_tier_evict(tcu_tier *t, const char *tenant, const char *model);
+/* VramTier::handle (gpu.rs:2545-2547): tenant `tenant`'s use of fitted bundle `model` (a name of the caller's) read
+ * from a file or a source, with weights w (which must outlive the handle and its loads). */
+TCU_API int tcu_tier_handle(tcu_tier *t, const char *tenant, const char *model, const char *bundle_path, tcu_weights *w,
+                            tcu_handle **out);
+TCU_API int tcu_tier_handle_source(tcu_tier *t, const char *tenant, const char *model, const tcu_source *src,
+                                   tcu_weights *w, tcu_handle **out);
+TCU_API void tcu_handle_free(tcu_handle *h);
+/* VramTier::preload (gpu.rs:2550-2558) of problem `node` of member `prefix`, now: 1 resident afterwards, 0 the budgets
+ * do not allow it (now, or ever), < 0 the load failed (tcu_tier_last_error says why). */
+TCU_API int tcu_handle_preload(tcu_handle *h, const char *prefix, int node);
+/* The handle's AttendCached hooks (gpu.rs:2636-2656), host buffers, as tcu_attend / tcu_stage / tcu_rows: TCU_OK, or
+ * TCU_DECLINED when the problem is not resident (its load is started), too large for its tenant, without the column
+ * cache (rows: kept only for a member of one problem and one label digit), or when the device failed (counted in
+ * fallbacks, the reason kept). */
+TCU_API int tcu_handle_attend(tcu_handle *h, const char *prefix, int node, int layer, const float *q, int rows, int d,
+                              int heads, float *out);
+TCU_API int tcu_handle_stage(tcu_handle *h, const char *prefix, int node, const float *x, int rows, int d, int out_n,
+                             float *out);
+TCU_API int tcu_handle_rows(tcu_handle *h, const char *prefix, const float *x, int rows, int features, int out_n,
+                            float *out);
+/* Test hooks (no counterpart in the reference), the tier's books without a device: admit a ready entry of `bytes`
+ * for (tenant, model, prefix, node) through the same claim as a load (1 admitted, 0 no room); hold a ready entry as a
+ * prediction holds its problem (1, or 0 when it is not ready) until unpinned. */
+TCU_API int tcu_tier_debug_admit(tcu_tier *t, const char *tenant, const char *model, const char *prefix, int node,
+                                 size_t bytes);
+TCU_API int tcu_tier_debug_pin(tcu_tier *t, const char *tenant, const char *model, const char *prefix, int node,
+                               tcu_pin **out);
+TCU_API void tcu_tier_debug_unpin(tcu_pin *p);
+
 /* ---- heads (src/table.rs) ------------------------------------------------------------------------------------ */
 
 /* Classifier::logit_sums_async (src/table.rs:265-269) for one member: sums[r][c] += logits[r][classes_of[c]]

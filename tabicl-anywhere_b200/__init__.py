@@ -6,6 +6,7 @@ The objects mirror the reference's accelerator side (src/gpu.rs, src/predict.rs:
 * `GpuWeights` - the in-context weights on it (gpu::GpuWeights)
 * `VramModel` - one fitted problem's key/value cache resident on it (gpu::VramModel)
 * `VramMember` - a fitted member's problems and its class tree, predicted whole (predict::predict_raw)
+* `VramTier` / `VramHandle` - problems resident for many tenants within byte budgets; the handle is an AttendCached
 * `CudaAttend` - the `AttendCached` implementation: `attend`, `stage`, `rows`, each returning None to decline
 
 Everything computes on the GPU through libtabicl_b200.so; there is no CPU path here. The library is built in-tree
@@ -49,6 +50,13 @@ class RowsShape(ctypes.Structure):
 
 
 _lib = None
+
+
+_READ_AT = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_size_t)
+
+
+class _Source(ctypes.Structure):
+    _fields_ = [("user", ctypes.c_void_p), ("read_at", _READ_AT), ("size", ctypes.c_uint64)]
 
 
 def lib():
@@ -121,6 +129,27 @@ def lib():
         "tcu_member_rows_device": (_c_int, [_c_void, _c_void, _c_int, _c_void, _c_void]),
         "tcu_member_combine_device": (_c_int, [_c_void, _c_void, _c_int, _c_void, _c_void]),
         "tcu_member_free": (None, [_c_void]),
+        "tcu_tier_new": (_c_int, [_c_void, _c_size, _c_size, _c_int, P(_c_void)]),
+        "tcu_tier_free": (None, [_c_void]),
+        "tcu_tier_wait": (None, [_c_void]),
+        "tcu_tier_held": (None, [_c_void, ctypes.c_char_p, P(_c_size), P(_c_size)]),
+        "tcu_tier_ready": (_c_size, [_c_void, ctypes.c_char_p]),
+        "tcu_tier_on_card": (None, [_c_void, ctypes.c_char_p, P(_c_size), P(_c_size)]),
+        "tcu_tier_fallbacks": (ctypes.c_uint64, [_c_void]),
+        "tcu_tier_last_error": (_c_size, [_c_void, ctypes.c_char_p, _c_size]),
+        "tcu_tier_evict": (None, [_c_void, ctypes.c_char_p, ctypes.c_char_p]),
+        "tcu_tier_handle": (_c_int, [_c_void, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _c_void, P(_c_void)]),
+        "tcu_tier_handle_source": (_c_int, [_c_void, ctypes.c_char_p, ctypes.c_char_p, P(_Source), _c_void,
+                                            P(_c_void)]),
+        "tcu_handle_free": (None, [_c_void]),
+        "tcu_handle_preload": (_c_int, [_c_void, ctypes.c_char_p, _c_int]),
+        "tcu_handle_attend": (_c_int, [_c_void, ctypes.c_char_p, _c_int, _c_int, _c_float_p, _c_int, _c_int, _c_int,
+                                       _c_float_p]),
+        "tcu_handle_stage": (_c_int, [_c_void, ctypes.c_char_p, _c_int, _c_float_p, _c_int, _c_int, _c_int, _c_float_p]),
+        "tcu_handle_rows": (_c_int, [_c_void, ctypes.c_char_p, _c_float_p, _c_int, _c_int, _c_int, _c_float_p]),
+        "tcu_tier_debug_admit": (_c_int, [_c_void, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _c_int, _c_size]),
+        "tcu_tier_debug_pin": (_c_int, [_c_void, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _c_int, P(_c_void)]),
+        "tcu_tier_debug_unpin": (None, [_c_void]),
         "tcu_stage_sharded_device": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_void, _c_void]),
     }
     for name, (res, args) in sig.items():
@@ -528,6 +557,170 @@ def fit_member(weights, h, y, classes, features, col_kv, chunk=256, kv=KV_F32):
         for m in nodes:
             m.free()
         raise
+
+
+def _b(text):
+    return text.encode() if isinstance(text, str) else text
+
+
+class VramTier:
+    """gpu::VramTier (src/gpu.rs:2486-2626): fitted problems resident on one device for many tenants, within `budget`
+    bytes in all and `tenant_budget` per tenant (the ledger of src/warm.rs:28-115: the least recently used problem
+    makes room, one in use by a prediction is released when it finishes). With background=True a first prediction
+    starts its problem's load on a thread and declines meanwhile; otherwise it loads in the call. gpu=None: a tier
+    that only keeps its books (the debug_* methods), without a device."""
+
+    def __init__(self, gpu, budget, tenant_budget, background=True):
+        self.gpu, self._h = gpu, _c_void()
+        r = lib().tcu_tier_new(gpu._h if gpu is not None else None, int(budget), int(tenant_budget), int(background),
+                               ctypes.byref(self._h))
+        if r != OK:
+            raise TcuError(r, "cannot make a tier")
+
+    def _pair(self, f, tenant):
+        a, b = _c_size(), _c_size()
+        f(self._h, _b(tenant), ctypes.byref(a), ctypes.byref(b))
+        return a.value, b.value
+
+    def held(self, tenant):
+        """Bytes the tier holds, in all and by `tenant` (loads in progress included)."""
+        return self._pair(lib().tcu_tier_held, tenant)
+
+    def ready(self, tenant):
+        return int(lib().tcu_tier_ready(self._h, _b(tenant)))
+
+    def on_card(self, tenant):
+        """Bytes really on the device, in all and of `tenant` (evicted problems still in use included)."""
+        return self._pair(lib().tcu_tier_on_card, tenant)
+
+    @property
+    def fallbacks(self):
+        return int(lib().tcu_tier_fallbacks(self._h))
+
+    def last_error(self):
+        n = lib().tcu_tier_last_error(self._h, None, 0)
+        if not n:
+            return None
+        buf = ctypes.create_string_buffer(n + 1)
+        lib().tcu_tier_last_error(self._h, buf, n + 1)
+        return buf.value.decode(errors="replace")
+
+    def evict(self, tenant, model=None):
+        lib().tcu_tier_evict(self._h, _b(tenant), None if model is None else _b(model))
+
+    def wait(self):
+        """Wait for loads started by predictions."""
+        lib().tcu_tier_wait(self._h)
+
+    def handle(self, tenant, model, bundle, weights):
+        """VramTier::handle: tenant's use of fitted bundle `model` (a name of the caller's), read from `bundle` (a
+        path, or the bundle's bytes, read through a positional-read source), an AttendCached."""
+        return VramHandle(self, tenant, model, bundle, weights)
+
+    def preload(self, tenant, model, bundle, weights, prefix, node):
+        """VramTier::preload: True when problem `node` of member `prefix` is resident afterwards, False when the
+        budgets do not allow it (now, or ever)."""
+        h = self.handle(tenant, model, bundle, weights)
+        try:
+            return h.preload(prefix, node)
+        finally:
+            h.free()
+
+    def debug_admit(self, tenant, model, prefix, node, nbytes):
+        """Test hook: a ready entry of `nbytes` through the same claim as a load; True when admitted."""
+        r = lib().tcu_tier_debug_admit(self._h, _b(tenant), _b(model), _b(prefix), node, int(nbytes))
+        if r < 0:
+            raise TcuError(r, "debug_admit")
+        return r == 1
+
+    def debug_pin(self, tenant, model, prefix, node):
+        """Test hook: hold a ready entry as a prediction holds its problem; returns the pin (or None), released by
+        debug_unpin."""
+        p = _c_void()
+        r = lib().tcu_tier_debug_pin(self._h, _b(tenant), _b(model), _b(prefix), node, ctypes.byref(p))
+        return p if r == 1 else None
+
+    @staticmethod
+    def debug_unpin(pin):
+        lib().tcu_tier_debug_unpin(pin)
+
+    def free(self):
+        if self._h:
+            lib().tcu_tier_free(self._h)
+            self._h = _c_void()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class VramHandle:
+    """VramHandle (src/gpu.rs:2628-2701), the AttendCached implementation over a tier: `attend`, `stage` and `rows`
+    return None to decline (not resident yet, too large for the tenant, or the device failed: counted in the tier's
+    fallbacks)."""
+
+    def __init__(self, tier, tenant, model, bundle, weights):
+        self.tier, self.weights, self._h = tier, weights, _c_void()
+        if isinstance(bundle, (bytes, bytearray, memoryview)):
+            data = np.frombuffer(bundle, dtype=np.uint8)
+
+            def read_at(_user, offset, buf, n):
+                if offset + n > data.size:
+                    return 1
+                ctypes.memmove(buf, data.ctypes.data + offset, n)
+                return 0
+
+            self._keep = (data, _READ_AT(read_at))
+            src = _Source(None, self._keep[1], data.size)
+            r = lib().tcu_tier_handle_source(tier._h, _b(tenant), _b(model), ctypes.byref(src), weights._h,
+                                             ctypes.byref(self._h))
+        else:
+            r = lib().tcu_tier_handle(tier._h, _b(tenant), _b(model), os.fsencode(bundle), weights._h,
+                                      ctypes.byref(self._h))
+        if r != OK:
+            raise TcuError(r, "cannot make a tier handle")
+
+    def preload(self, prefix, node):
+        r = lib().tcu_handle_preload(self._h, _b(prefix), node)
+        if r < 0:
+            raise TcuError(r, self.tier.last_error())
+        return r == 1
+
+    def _answer(self, r, out):
+        if r < 0:
+            raise TcuError(r, self.tier.last_error())
+        return out if r == OK else None
+
+    def attend(self, prefix, node, layer, q, d, heads):
+        q = np.ascontiguousarray(q, dtype=np.float32).reshape(-1, d)
+        out = np.empty_like(q)
+        return self._answer(lib().tcu_handle_attend(self._h, _b(prefix), node, layer, _f32p(q), q.shape[0], d, heads,
+                                                    _f32p(out)), out)
+
+    def stage(self, prefix, node, h, d, out_n):
+        h = np.ascontiguousarray(h, dtype=np.float32).reshape(-1, d)
+        out = np.empty((h.shape[0], out_n), dtype=np.float32)
+        return self._answer(lib().tcu_handle_stage(self._h, _b(prefix), node, _f32p(h), h.shape[0], d, out_n,
+                                                   _f32p(out)), out)
+
+    def rows(self, prefix, x, out_n):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty((x.shape[0], out_n), dtype=np.float32)
+        return self._answer(lib().tcu_handle_rows(self._h, _b(prefix), _f32p(x), x.shape[0], x.shape[1], out_n,
+                                                  _f32p(out)), out)
+
+    def free(self):
+        if self._h:
+            lib().tcu_handle_free(self._h)
+            self._h = _c_void()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 COMM_ID_BYTES = 128

@@ -25,14 +25,10 @@
 #include <vector>
 
 #include "kernels.cuh"
+#include "engine.hpp"
 #include "tirs.hpp"
 
 namespace tcu {
-
-struct Error {
-    int code;
-    std::string msg;
-};
 
 #define CU(call)                                                                                     \
     do {                                                                                             \
@@ -93,6 +89,12 @@ struct tcu_ctx {
     int *err_mapped = nullptr;     // the same slots' device address
     bool abort_next = false;       // test hook: the next one-kernel stage launch starts aborted
     unsigned *dev_scan = nullptr;  // scratch of the per-layer magnitude scan
+    // uploads from bundles: two pinned staging buffers and a stream of their own (a piece is read from the source
+    // while the one before is copied), used by one upload at a time and not under `mu`
+    std::mutex upload_mu;
+    cudaStream_t upload_stream = nullptr;
+    void *pin[2] = {nullptr, nullptr};
+    cudaEvent_t pin_ev[2] = {nullptr, nullptr};
 };
 
 // Which wait each report slot stands for.
@@ -244,6 +246,11 @@ static void ctx_release(tcu_ctx *ctx) {
     for (auto e : ctx->prof_events) cudaEventDestroy(e);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     if (ctx->dev_scan) cudaFree(ctx->dev_scan);
+    for (int i = 0; i < 2; i++) {
+        if (ctx->pin[i]) cudaFreeHost(ctx->pin[i]);
+        if (ctx->pin_ev[i]) cudaEventDestroy(ctx->pin_ev[i]);
+    }
+    if (ctx->upload_stream) cudaStreamDestroy(ctx->upload_stream);
     delete ctx;
 }
 
@@ -630,6 +637,27 @@ static std::string cfg_value(const std::string &cfg, const std::string &key) {
 static size_t layer_bytes_of(int kv, int d, int rows, int chunk) {
     // fit.rs:234 raw_entries: full chunks, then the remainder's record
     return (size_t)(rows / chunk) * record_bytes(kv, d, chunk) + (rows % chunk ? record_bytes(kv, d, rows % chunk) : 0);
+}
+
+static bool tc_enabled();
+
+// Everything a problem of `rows` training rows holds on the device once it has answered a call of each kind: the
+// stored records (each layer on a 256-byte boundary), the query scales, the decode items and key tiles, the column
+// cache, the tensor-core attention's pre-split keys and values (head width 128) and the one-kernel stage's tables.
+static size_t model_bytes_of(const tcu_weights *w, int rows, int chunk, int kv, size_t col_floats) {
+    const int d = w->shape.d, L = w->shape.layers, heads = w->shape.heads;
+    const size_t stride = (layer_bytes_of(kv, d, rows, chunk) + 255) / 256 * 256;
+    const int ks = decode_keys_per_item(kv), tk = rows_tile_keys(kv);
+    size_t nitems = 0, ntiles = 0, nrt = 0;
+    for (int r0 = 0; r0 < rows; r0 += chunk) {
+        const int rc = std::min(chunk, rows - r0);
+        nitems += (rc + ks - 1) / ks, ntiles += (rc + FLASH_KEYS - 1) / FLASH_KEYS, nrt += (rc + tk - 1) / tk;
+    }
+    size_t n = stride * L + sizeof(float) * (size_t)L * d + nitems * sizeof(int2) + ntiles * sizeof(int4) +
+               sizeof(float) * col_floats;
+    if (d / heads == 128 && tc_enabled()) n += ntiles * heads * tc_tile_bytes() * L;
+    n += nrt * heads * sizeof(int4) + 2 * (size_t)L * sizeof(CUtensorMap) + L * sizeof(RowsLayer) + 256;
+    return n;
 }
 
 static void model_init(tcu_model *m, tcu_weights *w, int rows, int chunk, int kv, int classes) {
@@ -1714,34 +1742,133 @@ int tcu_model_put_layer(tcu_model *m, int layer, size_t offset, const void *byte
     });
 }
 
-// Problem `node` of member p of bundle b (the col_kv too when with_col and the bundle holds it).
-static tcu_model *load_node(tcu_weights *w, const Bundle &b, const std::string &p, int node, bool with_col) {
-    auto meta = b.i32s(p + "meta");
-    auto tree = b.i32s(p + "tree");
-    if (meta.size() != 7) fail(TCU_ERR_FORMAT, p + "meta is damaged");
-    auto nodes = parse_tree(tree.data(), tree.size(), meta[6]);
-    if (node < 0 || node >= (int)nodes.size()) fail(TCU_ERR_ARG, "model_from_bundle: no such node");
-    auto ok = [&](int r) {
-        if (r != TCU_OK) fail(r, w->ctx->err);
-    };
-    tcu_model *m = nullptr;
-    ok(tcu_model_new(w, meta.data(), nodes[node].rows, nodes[node].k, &m));
-    ModelPtr guard(m);
-    auto sc = b.f32s(p + "n" + std::to_string(node) + "_scale");
-    ok(tcu_model_put_scales(m, sc.data(), sc.size()));
-    if (with_col && w->rows.on && b.has(p + "col_kv")) {
-        auto ck = b.f32s(p + "col_kv");
-        ok(tcu_model_put_col_kv(m, ck.data(), ck.size()));
+}  // extern "C"
+
+namespace tcu {
+
+static constexpr size_t STAGING_BYTES = 8u << 20;
+
+// The context's staging buffers and upload stream, made at the first upload (with upload_mu held).
+static void ensure_staging(tcu_ctx *ctx) {
+    if (ctx->upload_stream) return;
+    CU(cudaStreamCreateWithFlags(&ctx->upload_stream, cudaStreamNonBlocking));
+    for (int i = 0; i < 2; i++) {
+        CU(cudaHostAlloc(&ctx->pin[i], STAGING_BYTES, cudaHostAllocPortable));
+        CU(cudaEventCreateWithFlags(&ctx->pin_ev[i], cudaEventDisableTiming));
     }
-    for (int l = 0; l < w->shape.layers; l++) {
-        std::string name = p + "n" + std::to_string(node) + "_kv" + std::to_string(l);
+}
+
+// Copy `n` bytes to device memory `dst`, the pieces produced by read(piece, offset, len) into alternating pinned
+// buffers: a buffer is refilled only after its previous copy has landed, so reading and copying overlap. Returns with
+// every copy landed.
+template <typename Read>
+static void staged_upload(tcu_ctx *ctx, void *dst, size_t n, Read read) {
+    std::lock_guard<std::mutex> lk(ctx->upload_mu);
+    ensure_staging(ctx);
+    int i = 0;
+    for (size_t off = 0; off < n; off += STAGING_BYTES, i ^= 1) {
+        const size_t len = std::min(STAGING_BYTES, n - off);
+        CU(cudaEventSynchronize(ctx->pin_ev[i]));
+        read(ctx->pin[i], off, len);
+        CU(cudaMemcpyAsync(static_cast<uint8_t *>(dst) + off, ctx->pin[i], len, cudaMemcpyHostToDevice, ctx->upload_stream));
+        CU(cudaEventRecord(ctx->pin_ev[i], ctx->upload_stream));
+    }
+    CU(cudaStreamSynchronize(ctx->upload_stream));
+}
+
+static void upload_tensor(tcu_ctx *ctx, const Bundle &b, const std::string &name, void *dst, size_t n) {
+    staged_upload(ctx, dst, n, [&](void *buf, size_t off, size_t len) { b.read_bytes_at(name, off, buf, len); });
+}
+
+static void upload_host(tcu_ctx *ctx, const void *src, void *dst, size_t n) {
+    staged_upload(ctx, dst, n, [&](void *buf, size_t off, size_t len) { std::memcpy(buf, static_cast<const uint8_t *>(src) + off, len); });
+}
+
+static size_t col_kv_floats(const tcu_model *m) {
+    const auto &rs = m->w->rows.shape;
+    return (size_t)m->features * m->digits * rs.col_blocks * 2 * rs.e * rs.inds;
+}
+
+struct NodeMeta {
+    std::vector<int32_t> meta;
+    std::vector<TreeNode> tree;
+};
+
+static NodeMeta node_meta(const Bundle &b, const std::string &p) {
+    NodeMeta nm{b.i32s(p + "meta"), {}};
+    if (nm.meta.size() != 7) fail(TCU_ERR_FORMAT, p + "meta is damaged");
+    if (nm.meta[4] < 0 || nm.meta[4] > 2) fail(TCU_ERR_FORMAT, "meta: unknown key/value format " + std::to_string(nm.meta[4]));
+    auto tree = b.i32s(p + "tree");
+    nm.tree = parse_tree(tree.data(), tree.size(), nm.meta[6]);
+    return nm;
+}
+
+MemberInfo member_info(const Bundle &b, const std::string &p) {
+    auto nm = node_meta(b, p);
+    return MemberInfo{std::max(1, (int)nm.meta[6]), std::max(1, (int)nm.meta[5])};
+}
+
+tcu_ctx *ctx_of(const tcu_weights *w) {
+    CU(cudaSetDevice(w->ctx->device));
+    return w->ctx;
+}
+
+bool has_col(const tcu_model *m) { return m->col_kv.p != nullptr; }
+
+tcu_ctx *ctx_of_weights(const tcu_weights *w) { return w->ctx; }
+
+size_t node_bytes(const tcu_weights *w, const Bundle &b, const std::string &p, int node, bool with_col) {
+    auto nm = node_meta(b, p);
+    if (node < 0 || node >= (int)nm.tree.size()) fail(TCU_ERR_ARG, "no such node");
+    const size_t col = with_col && w->rows.on && b.has(p + "col_kv") ? b.entry(p + "col_kv").len() : 0;
+    return model_bytes_of(w, nm.tree[node].rows, std::max(1, (int)nm.meta[3]), nm.meta[4], col);
+}
+
+tcu_model *load_node(tcu_weights *w, const Bundle &b, const std::string &p, int node, bool with_col) {
+    tcu_ctx *ctx = ctx_of(w);
+    auto nm = node_meta(b, p);
+    const auto &meta = nm.meta;
+    if (node < 0 || node >= (int)nm.tree.size()) fail(TCU_ERR_ARG, "model_from_bundle: no such node");
+    ModelPtr m(new tcu_model());
+    {
+        // creation touches the weights' reference count and the context's tables: under the lock; the uploads not
+        std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+        if (!w->ready) fail(TCU_ERR_STATE, "model_from_bundle: weights not ready");
+        model_init(m.get(), w, nm.tree[node].rows, meta[3], meta[4], nm.tree[node].k);
+        m->features = meta[1];
+        m->digits = std::max(1, (int)meta[5]), m->nodes = std::max(1, (int)meta[6]);
+    }
+    const int L = w->shape.layers, d = w->shape.d;
+    auto sc = b.f32s(p + "n" + std::to_string(node) + "_scale");
+    if (sc.size() != (size_t)L * d) fail(TCU_ERR_FORMAT, p + "n" + std::to_string(node) + "_scale: expected layers * d floats");
+    upload_host(ctx, sc.data(), m->scales.p, sizeof(float) * sc.size());
+    m->have_scales = true;
+    if (with_col && w->rows.on && b.has(p + "col_kv")) {
+        const std::string name = p + "col_kv";
+        const Entry &e = b.entry(name);
+        const size_t want = col_kv_floats(m.get());
+        if (e.len() != want || m->features < 1) fail(TCU_ERR_FORMAT, name + ": expected features * digits * column blocks * 2 * e * inducing points = " + std::to_string(want) + " floats");
+        m->col_kv.ensure(sizeof(float) * want);
+        if (e.dtype == "float32") {
+            upload_tensor(ctx, b, name, m->col_kv.p, sizeof(float) * want);
+        } else {
+            auto v = b.f32s(name);
+            upload_host(ctx, v.data(), m->col_kv.p, sizeof(float) * want);
+        }
+    }
+    for (int l = 0; l < L; l++) {
+        const std::string name = p + "n" + std::to_string(node) + "_kv" + std::to_string(l);
         const Entry &e = b.entry(name);
         if (e.nbytes != m->layer_bytes) fail(TCU_ERR_FORMAT, name + ": " + std::to_string(e.nbytes) + " bytes, expected " + std::to_string(m->layer_bytes));
-        auto bytes = b.bytes(name);
-        ok(tcu_model_put_layer(m, l, 0, bytes.data(), bytes.size()));
+        upload_tensor(ctx, b, name, m->layers.as<uint8_t>() + m->layer_stride * l, m->layer_bytes);
+        m->have_layer[l] = true;
     }
-    return guard.release();
+    return m.release();
 }
+
+}  // namespace tcu
+
+extern "C" {
 
 int tcu_model_from_bundle(tcu_weights *w, const char *path, const char *prefix, int node, tcu_model **out) {
     if (!w) return TCU_ERR_ARG;
@@ -1755,11 +1882,8 @@ int tcu_model_from_bundle(tcu_weights *w, const char *path, const char *prefix, 
 
 size_t tcu_model_bytes(const tcu_model *m) {
     if (!m) return 0;
-    // the tensor-core attention's pre-split copy of the keys and values is built by the first call: it is counted
-    // from the start, so that a budget charged at load time holds afterwards
-    const size_t tc = std::max(m->tctiles.bytes, tc_shape(m) ? tc_layer_bytes(m) * m->w->shape.layers : 0);
-    return m->layers.bytes + m->scales.bytes + m->items.bytes + m->tiles.bytes + m->col_kv.bytes + tc + m->rtiles.bytes +
-           m->rtmaps.bytes + m->rlayers.bytes + m->rsync.bytes;
+    // what the model will hold, its lazily built copies and tables included: a budget charged at load time holds
+    return model_bytes_of(m->w, m->rows, m->chunk, m->kv, m->col_kv.bytes / sizeof(float));
 }
 
 int tcu_model_set_columns(tcu_model *m, int features, int digits) {

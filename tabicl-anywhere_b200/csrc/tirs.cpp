@@ -87,12 +87,24 @@ std::unique_ptr<Bundle> Bundle::from_bytes(std::vector<uint8_t> bytes) {
     return b;
 }
 
+std::unique_ptr<Bundle> Bundle::from_reader(std::function<void(void *, uint64_t, uint64_t)> read, uint64_t size) {
+    std::unique_ptr<Bundle> b(new Bundle());
+    b->reader_ = std::move(read);
+    b->size_ = size;
+    b->parse();
+    return b;
+}
+
 Bundle::~Bundle() {
     if (file_) std::fclose(file_);
 }
 
 void Bundle::read_at(void *buf, uint64_t n, uint64_t offset) const {
     if (offset > size_ || n > size_ - offset) throw BundleError(TCU_ERR_FORMAT, "read past the end of the bundle");
+    if (reader_) {
+        reader_(buf, n, offset);
+        return;
+    }
     if (!file_) {
         std::memcpy(buf, mem_.data() + offset, n);
         return;

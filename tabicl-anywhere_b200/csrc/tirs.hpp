@@ -4,6 +4,7 @@
 #pragma once
 #include <cstdint>
 #include <cstdio>
+#include <functional>
 #include <map>
 #include <memory>
 #include <stdexcept>
@@ -35,6 +36,9 @@ class Bundle {
   public:
     static std::unique_ptr<Bundle> open(const std::string &path);
     static std::unique_ptr<Bundle> from_bytes(std::vector<uint8_t> bytes);
+    // A source read by the caller's positional reads (store.rs:45-50 ReadAt: a file, memory, object storage, a
+    // sealed bundle decrypted as it is read): read(buf, n, offset) fills buf or throws BundleError.
+    static std::unique_ptr<Bundle> from_reader(std::function<void(void *, uint64_t, uint64_t)> read, uint64_t size);
     ~Bundle();
     bool has(const std::string &name) const { return by_name_.count(name) != 0; }
     const Entry &entry(const std::string &name) const;
@@ -53,6 +57,7 @@ class Bundle {
     void read_at(void *buf, uint64_t n, uint64_t offset) const;
     FILE *file_ = nullptr;
     std::vector<uint8_t> mem_;
+    std::function<void(void *, uint64_t, uint64_t)> reader_;
     uint64_t size_ = 0;
     std::vector<Entry> entries_;
     std::map<std::string, size_t> by_name_;
