@@ -376,15 +376,27 @@ def multi_configs(pkg, synth, gpu, w, d, world, rank, stream, comm, a, bf16):
     sharded_pass()
     torch.cuda.synchronize()
     ms4 = max_over_ranks(ev_time(stream, sharded_pass, 2), world)
+    breakdown = None
+    if world > 1:
+        # one more pass with an event at each phase boundary (untimed): where the time goes, per rank, maximum taken
+        comm.breakdown(True)
+        sharded_pass()
+        breakdown = comm.breakdown(False)
+        bt = torch.tensor([breakdown[k] for k in comm.SHARD_PHASES], dtype=torch.float64, device="cuda")
+        torch.distributed.all_reduce(bt, op=torch.distributed.ReduceOp.MAX)
+        breakdown = {k: round(float(v), 4) for k, v in zip(comm.SHARD_PHASES, bt.tolist())}
     fl4 = stage_flops_per_row(N4, d, L, ff, hid, heads, dff, classes) * R4
     r4 = {"workload": "BASELINE config 4: 100,000-row i8 cache (1.25 GB), 4,096 test rows, training rows split over "
-                      "the devices, attention merged every layer (all-reduce max, rescale, all-reduce sum)",
+                      "the devices; every layer the partial attention states go to the rank that owns the row, which "
+                      "merges them and runs the rest of the layer for its slice of rows; queries gathered",
           "ms_per_pass": ms4, "rows_per_s": R4 / (ms4 / 1e3),
           "attention_tflops_per_gpu": 4.0 * N4 * d * L * R4 / world / (ms4 / 1e3) / 1e12,
           "roofline": {"bound": "tensor", "achieved": fl4 / world / (ms4 / 1e3) / 1e12, "peak": bf16,
                        "unit": "TFLOP/s", "frac": fl4 / world / (ms4 / 1e3) / 1e12 / bf16,
                        "what": "whole stage per GPU, algorithmic flops (dense layers counted once)"},
           "shard_rows": N4 // world}
+    if breakdown is not None:
+        r4["breakdown_ms_max_over_ranks"] = breakdown
     if ref is not None:
         r4["max_diff_vs_unsharded"] = float((o4[:ref.shape[0]] - ref).abs().max().item())
         r4["max_diff_vs_oracle"] = float(np.abs(o4[:16].cpu().numpy() - want4).max())

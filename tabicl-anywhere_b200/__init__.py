@@ -151,6 +151,7 @@ def lib():
         "tcu_tier_debug_pin": (_c_int, [_c_void, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _c_int, P(_c_void)]),
         "tcu_tier_debug_unpin": (None, [_c_void]),
         "tcu_stage_sharded_device": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_void, _c_void]),
+        "tcu_comm_breakdown": (_c_int, [_c_void, _c_int, P(ctypes.c_double)]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -749,6 +750,16 @@ class Comm:
 
     def wait(self, timeout_ms, stream=None):
         return self.gpu.check(lib().tcu_comm_wait(self._h, stream, int(timeout_ms)))
+
+    SHARD_PHASES = ("attention", "local_merge", "max_scale_reduce_scatter", "finish", "dense", "gather_queries",
+                    "decoder_outputs")
+
+    def breakdown(self, enable):
+        """Device ms per phase of the last sharded stage run while timing was on (waits for it), then timing on or
+        off for the calls that follow."""
+        ms = (ctypes.c_double * len(self.SHARD_PHASES))()
+        self.gpu.check(lib().tcu_comm_breakdown(self._h, int(enable), ms))
+        return dict(zip(self.SHARD_PHASES, [float(v) for v in ms]))
 
     def free(self):
         if self._h:

@@ -443,7 +443,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
             const int m = idx / HD, k = idx % HD, r = r0 + m;
             if (r >= a.R) break;  // rows grow with idx
             const float v = ostage[m * (HD + 1) + k] * oun;
-            if (whole) {
+            if (whole && a.state_ms) {
+                a.out[(size_t)r * a.ldo + h * HD + k] = ok ? v : 0.f;
+                if (k == 0) {
+                    float *ms = a.state_ms + ((size_t)r * H + h) * 2;
+                    ms[0] = ok ? rowx[m] : -FLT_MAX, ms[1] = ok ? rowx[BQ + m] : 0.f;
+                }
+            } else if (whole) {
                 a.out[(size_t)r * a.ldo + h * HD + k] = ok ? v * rowx[2 * BQ + m] : 0.f;
             } else {
                 a.part_acc[((size_t)split * a.R + r) * d + h * HD + k] = ok ? v : 0.f;
@@ -503,7 +509,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
                         }
                     }
                 }
-                winv[tid] = 1.0f / S;
+                winv[tid] = a.state_ms ? 1.0f : 1.0f / S;
+                if (a.state_ms) {
+                    float *st = a.state_ms + ((size_t)r * H + h) * 2;
+                    st[0] = S > 0.f ? M : -FLT_MAX, st[1] = S;
+                }
             }
             __syncthreads();
             const size_t pstride = (size_t)a.R * d;

@@ -205,6 +205,12 @@ struct NcclApi {
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
     ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*group_start)() = nullptr;
+    ncclResult_t (*group_end)() = nullptr;
+    ncclResult_t (*reduce_scatter)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     const char *(*error_string)(ncclResult_t) = nullptr;
     std::string why;
 };
@@ -223,7 +229,14 @@ static const NcclApi &nccl_api() {
         a.comm_abort = reinterpret_cast<decltype(a.comm_abort)>(dlsym(h, "ncclCommAbort"));
         a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
         a.error_string = reinterpret_cast<decltype(a.error_string)>(dlsym(h, "ncclGetErrorString"));
-        if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.comm_abort || !a.all_reduce || !a.error_string)
+        a.send = reinterpret_cast<decltype(a.send)>(dlsym(h, "ncclSend"));
+        a.recv = reinterpret_cast<decltype(a.recv)>(dlsym(h, "ncclRecv"));
+        a.group_start = reinterpret_cast<decltype(a.group_start)>(dlsym(h, "ncclGroupStart"));
+        a.group_end = reinterpret_cast<decltype(a.group_end)>(dlsym(h, "ncclGroupEnd"));
+        a.reduce_scatter = reinterpret_cast<decltype(a.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
+        a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
+        if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.comm_abort || !a.all_reduce || !a.error_string ||
+            !a.send || !a.recv || !a.group_start || !a.group_end || !a.reduce_scatter || !a.all_gather)
             a.why = "libnccl.so.2 lacks an entry point";
         return a;
     }();
@@ -235,6 +248,14 @@ struct tcu_comm {
     ncclComm_t comm = nullptr;
     int nranks = 1, rank = 0;
     bool aborted = false;
+    // optional timing of the sharded stage's phases (tcu_comm_breakdown): an event at the start of each phase,
+    // read after the call
+    bool prof = false;
+    std::vector<cudaEvent_t> events;
+    std::vector<int> marks;  // the phase each recorded event starts
+    // the sharded stage's collectives run on a stream of their own, ordered against the compute stream by events
+    cudaStream_t cstream = nullptr;
+    cudaEvent_t sync[10] = {};
 };
 
 // ---- handle lifetimes: a context lives while its weights do, weights while their models do --------------------
@@ -787,10 +808,13 @@ static void ensure_work(tcu_model *m, int R) {
 }
 
 // attention of R scaled queries q (device, [R][d]) against a layer given in stored form; out [R][d]
-// Returns the number of parts left in part_ms / part_acc when parts_only (the outputs are not finished then).
+// Returns the number of parts left in part_ms / part_acc when parts_only (the outputs are not finished then). With
+// state_ms (and parts_only), the tensor-core path leaves the merged state itself when it can (out the unnormalised
+// values, state_ms their (max, weight sum)) and returns 0; otherwise the parts are left as above.
 static int attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int rows, int chunk, int kv, const int2 *items,
                         int nitems, const int4 *tiles, int ntiles, const float *q, int R, float *out, cudaStream_t s,
-                        int eK = 0, int eV = 0, bool parts_only = false, const void *tc_tiles = nullptr) {
+                        int eK = 0, int eV = 0, bool parts_only = false, const void *tc_tiles = nullptr,
+                        float *state_ms = nullptr) {
     const auto &sh = m->w->shape;
     AttnArgs a;
     a.layer = layer, a.rows = rows, a.chunk = chunk, a.d = sh.d, a.heads = sh.heads;
@@ -841,7 +865,10 @@ static int attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int ro
         // merged by k_attend_merge, one block per (row, head), instead of by a few CTAs reading them all
         if (a.splits <= 8 && m->mcnt.bytes >= sizeof(int) * ((size_t)(R + 127) / 128) * sh.heads)
             a.merge_cnt = m->mcnt.as<int>();
+        const bool state = state_ms && (a.splits == 1 || a.merge_cnt);
+        if (state) a.parts_only = 0, a.state_ms = state_ms;
         ck(launch_attend_tc(kv, a, s, &ctx->launches), "attend (tensor cores)");
+        if (state) return 0;
     } else {
         ck(launch_attend_flash(kv, hd, a, s, &ctx->launches), "attend (flash)");
     }
@@ -1436,41 +1463,150 @@ static void nccl_check(ncclResult_t r, const char *what) {
 }
 
 // The stage with every layer's attention merged over the ranks of c (m holds this rank's rows; m->h in, m->out out).
+// predict.rs:398-409, 521-532 (training rows split over readers, partial states merged by nn.rs:261-286) with the
+// readers on separate devices. The rows are split into G groups (two when each rank's slice of a group keeps at least
+// 2048 rows, else one: the rest of a layer on fewer rows costs about as much, so splitting smaller calls loses more
+// than the overlap wins), each padded to N equal slices of Rs rows (padding rows start at zero); in group g rank j owns rows
+// g Rg + [j Rs, (j + 1) Rs), Rg = N Rs. Every layer, every rank attends each group's rows over its own chunks; the
+// maxima of the states are all-reduced (max), each rank scales its states to them, and a reduce-scatter (sum) hands
+// each rank the summed states of its own slice, which it divides and runs through the rest of the layer and the next
+// layer's query; an all-gather gives every rank all of the group's queries. Per layer and rank: R H floats all-reduced,
+// R (d + H) reduce-scattered, R d gathered. The compute runs on the caller's stream, the collectives (with the small
+// kernels between them) on the communicator's own stream, so that one group's collectives run while the other group
+// computes; with timing on (tcu_comm_breakdown) everything runs on the caller's stream, one phase after another.
 static void stage_sharded(tcu_ctx *ctx, tcu_model *m, tcu_comm *c, int R, int out_n, cudaStream_t s) {
     check_ready(m);
     const auto &sh = m->w->shape;
-    const int d = sh.d, H = sh.heads, L = sh.layers, dff = sh.dec_ff;
+    const int d = sh.d, H = sh.heads, L = sh.layers, dff = sh.dec_ff, N = c->nranks, me = c->rank;
     if (out_n < 1 || out_n > sh.outs) fail(TCU_ERR_ARG, "stage: out_n must be 1..decoder outputs");
     if (c->aborted) fail(TCU_ERR_STATE, "communicator was aborted");
+    const int G = R >= 4096 * N ? 2 : 1;
+    const int Rs = (R + G * N - 1) / (G * N), Rg = Rs * N, Rp = Rg * G;
     scan_model(ctx, m, ctx->stream);
-    ensure_work(m, R);
-    if (m->out.ensure(sizeof(float) * (size_t)R * out_n)) drop_graphs(m);
-    m->sh_m.ensure(sizeof(float) * (size_t)R * H);
-    m->sh_mall.ensure(sizeof(float) * (size_t)R * H);
-    m->sh_packed.ensure(sizeof(float) * (size_t)R * (d + H));
+    ensure_work(m, Rg);
+    ensure_work(m, Rp);
+    if (m->out.ensure(sizeof(float) * (size_t)Rp * out_n)) drop_graphs(m);
+    const size_t w = (size_t)d + H;
+    m->sh_m.ensure(sizeof(float) * (size_t)Rp * H * 2);     // per group: this rank's maxima, then the maxima over ranks
+    m->sh_mall.ensure(sizeof(float) * (size_t)Rp * H * 2);  // the merged (max, weight sum) of every row
+    m->sh_packed.ensure(sizeof(float) * ((size_t)Rp + (size_t)G * Rs) * w);
     const auto &api = nccl_api();
-    Launch ck{ctx, s};
     const float *scales = m->scales.as<float>();
-    float *h = m->h.as<float>(), *q = m->q.as<float>(), *att = m->att.as<float>();
-    for (int l = 0; l < L; l++) {
-        query_rows(ctx, m, l, scales + (size_t)l * d, h, R, q, s);
-        const int parts = attend_layer(ctx, m, layer_ptr(m, l), m->rows, m->chunk, m->kv, m->items.as<int2>(), m->nitems,
-                                       m->tiles.as<int4>(), m->ntiles, q, R, att, s, m->tc_eK[l], m->tc_eV[l], true,
-                                       tc_tiles_of(m, l));
-        AttnArgs a;
-        a.R = R, a.heads = H, a.d = d, a.part_ms = m->part_ms.as<float>(), a.part_acc = m->part_acc.as<float>();
-        ck(launch_merge_local(a, parts, m->sh_m.as<float>(), m->sh_packed.as<float>(), s, &ctx->launches), "merge (local)");
-        nccl_check(api.all_reduce(m->sh_m.p, m->sh_mall.p, (size_t)R * H, ncclFloat32, ncclMax, c->comm, s), "all-reduce (max)");
-        ck(launch_merge_rescale(m->sh_m.as<float>(), m->sh_mall.as<float>(), R, H, d, m->sh_packed.as<float>(), s,
-                                &ctx->launches), "merge (rescale)");
-        nccl_check(api.all_reduce(m->sh_packed.p, m->sh_packed.p, (size_t)R * (d + H), ncclFloat32, ncclSum, c->comm, s),
-                   "all-reduce (sum)");
-        ck(launch_merge_finish(m->sh_packed.as<float>(), R, H, d, att, d, s, &ctx->launches), "merge (finish)");
-        block_tail(ctx, m, l, h, att, R, s);
+    float *h = m->h.as<float>(), *q = m->q.as<float>(), *att = m->att.as<float>(), *om = m->out.as<float>();
+    const bool serial = c->prof;
+    cudaStream_t cs = serial ? s : c->cstream;
+    Launch ck{ctx, s}, cc{ctx, cs};
+    c->marks.clear();
+    auto mark = [&](int phase) {
+        if (!c->prof) return;
+        const size_t i = c->marks.size();
+        if (i == c->events.size()) {
+            cudaEvent_t e;
+            CU(cudaEventCreate(&e));
+            c->events.push_back(e);
+        }
+        CU(cudaEventRecord(c->events[i], s));
+        c->marks.push_back(phase);
+    };
+    // cross-stream order (nothing to do on one stream): event e marks what `from` has queued so far; `to` waits for it
+    auto signal = [&](cudaStream_t from, int e) {
+        if (!serial) CU(cudaEventRecord(c->sync[e], from));
+    };
+    auto wait = [&](cudaStream_t to, int e) {
+        if (!serial) CU(cudaStreamWaitEvent(to, c->sync[e], 0));
+    };
+    enum { EV_INPUT = 0, EV_QUERY = 1, EV_GATHERED = 3, EV_ATTENDED = 5, EV_MERGED = 7, EV_OUTPUT = 9 };
+    struct Group {
+        float *h, *q, *att, *hm, *qm, *am, *ms, *mloc, *mall, *packed, *mine;
+        int parts;
+    };
+    std::vector<Group> gs(G);
+    for (int g = 0; g < G; g++) {
+        Group &x = gs[g];
+        const size_t o = (size_t)g * Rg;
+        x.h = h + o * d, x.q = q + o * d, x.att = att + o * d;
+        x.hm = x.h + (size_t)me * Rs * d, x.qm = x.q + (size_t)me * Rs * d, x.am = x.att + (size_t)me * Rs * d;
+        x.ms = m->sh_mall.as<float>() + o * H * 2;
+        x.mloc = m->sh_m.as<float>() + o * H * 2, x.mall = x.mloc + (size_t)Rg * H;
+        x.packed = m->sh_packed.as<float>() + o * w;
+        x.mine = m->sh_packed.as<float>() + (size_t)Rp * w + (size_t)g * Rs * w;
     }
-    linear(ctx, m, h, d, R, d, m->w->lnw, m->w->lnb, m->w->dec0w, m->w->dec0b, dff, m->mid.as<float>(), dff, 1, 0, s, m->w->tdec0);
-    linear(ctx, m, m->mid.as<float>(), dff, R, dff, nullptr, nullptr, m->w->dec2w, m->w->dec2b, out_n, m->out.as<float>(),
-           out_n, 0, 0, s, m->w->tdec2);
+    // group g's queries from this rank's slice to every rank, once they are computed on s
+    auto gather = [&](int g) {
+        signal(s, EV_QUERY + g);
+        wait(cs, EV_QUERY + g);
+        mark(5);
+        nccl_check(api.all_gather(gs[g].qm, gs[g].q, (size_t)Rs * d, ncclFloat32, c->comm, cs), "all-gather (queries)");
+        signal(cs, EV_GATHERED + g);
+    };
+    for (int g = 0; g < G; g++) {
+        mark(4);
+        query_rows(ctx, m, 0, scales, gs[g].hm, Rs, gs[g].qm, s);
+        gather(g);
+    }
+    for (int l = 0; l < L; l++) {
+        // attention of each group (after its queries are gathered), its state then merged on the collective stream
+        for (int g = 0; g < G; g++) {
+            Group &x = gs[g];
+            wait(s, EV_GATHERED + g);
+            mark(0);
+            x.parts = attend_layer(ctx, m, layer_ptr(m, l), m->rows, m->chunk, m->kv, m->items.as<int2>(), m->nitems,
+                                   m->tiles.as<int4>(), m->ntiles, x.q, Rg, x.att, s, m->tc_eK[l], m->tc_eV[l], true,
+                                   tc_tiles_of(m, l), x.ms);
+            mark(1);
+            // the kernel left the merged state (parts 0), or one part is it, or several are merged into one first
+            const float *sms = x.parts == 0 ? x.ms : m->part_ms.as<float>(), *sacc = x.parts == 0 ? x.att : m->part_acc.as<float>();
+            if (x.parts > 1) {
+                AttnArgs a;
+                a.R = Rg, a.heads = H, a.d = d, a.part_ms = m->part_ms.as<float>(), a.part_acc = m->part_acc.as<float>();
+                ck(launch_merge_state(a, x.parts, x.ms, x.att, s, &ctx->launches), "merge (local)");
+                sms = x.ms, sacc = x.att;
+            } else if (x.parts == 1) {
+                // the parts are reused by the next group's attention: the state moves out of them first
+                CU(cudaMemcpyAsync(x.ms, sms, sizeof(float) * Rg * H * 2, cudaMemcpyDeviceToDevice, s));
+                CU(cudaMemcpyAsync(x.att, sacc, sizeof(float) * Rg * d, cudaMemcpyDeviceToDevice, s));
+                sms = x.ms, sacc = x.att;
+            }
+            signal(s, EV_ATTENDED + g);
+            wait(cs, EV_ATTENDED + g);
+            mark(2);
+            cc(launch_state_max(sms, Rg, H, x.mloc, cs, &ctx->launches), "merge (maxima)");
+            nccl_check(api.all_reduce(x.mloc, x.mall, (size_t)Rg * H, ncclFloat32, ncclMax, c->comm, cs), "all-reduce (max)");
+            cc(launch_state_pack(sms, sacc, x.mall, Rg, H, d, x.packed, cs, &ctx->launches), "merge (scale)");
+            nccl_check(api.reduce_scatter(x.packed, x.mine, (size_t)Rs * w, ncclFloat32, ncclSum, c->comm, cs), "reduce-scatter (states)");
+            mark(3);
+            cc(launch_state_finish(x.mine, Rs, H, d, x.am, d, cs, &ctx->launches), "merge (finish)");
+            signal(cs, EV_MERGED + g);
+        }
+        // the rest of the layer and the next query for this rank's slice of each group, its queries then gathered
+        for (int g = 0; g < G; g++) {
+            Group &x = gs[g];
+            wait(s, EV_MERGED + g);
+            mark(4);
+            block_tail(ctx, m, l, x.hm, x.am, Rs, s);
+            if (l + 1 < L) {
+                query_rows(ctx, m, l + 1, scales + (size_t)(l + 1) * d, x.hm, Rs, x.qm, s);
+                gather(g);
+            }
+        }
+    }
+    mark(6);
+    for (int g = 0; g < G; g++) {
+        Group &x = gs[g];
+        float *og = om + (size_t)g * Rg * out_n, *mo = og + (size_t)me * Rs * out_n;
+        linear(ctx, m, x.hm, d, Rs, d, m->w->lnw, m->w->lnb, m->w->dec0w, m->w->dec0b, dff, m->mid.as<float>(), dff, 1, 0, s, m->w->tdec0);
+        linear(ctx, m, m->mid.as<float>(), dff, Rs, dff, nullptr, nullptr, m->w->dec2w, m->w->dec2b, out_n, mo, out_n, 0, 0, s,
+               m->w->tdec2);
+    }
+    signal(s, EV_OUTPUT);
+    wait(cs, EV_OUTPUT);
+    for (int g = 0; g < G; g++) {
+        float *og = om + (size_t)g * Rg * out_n, *mo = og + (size_t)me * Rs * out_n;
+        nccl_check(api.all_gather(mo, og, (size_t)Rs * out_n, ncclFloat32, c->comm, cs), "all-gather (outputs)");
+    }
+    signal(cs, EV_INPUT);
+    wait(s, EV_INPUT);
+    mark(7);
 }
 
 // fit.rs:577-747 in-memory path on the device
@@ -2185,6 +2321,8 @@ int tcu_comm_init(tcu_ctx *ctx, const uint8_t id[TCU_COMM_ID_BYTES], int nranks,
         ncclUniqueId u;
         std::memcpy(&u, id, sizeof(u));
         nccl_check(api.comm_init_rank(&c->comm, nranks, u, rank), "comm_init");
+        CU(cudaStreamCreateWithFlags(&c->cstream, cudaStreamNonBlocking));
+        for (auto &e : c->sync) CU(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
         ctx->refs++;  // released by tcu_comm_free
         *out = c.release();
         return TCU_OK;
@@ -2198,6 +2336,10 @@ void tcu_comm_free(tcu_comm *c) {
         std::lock_guard<std::recursive_mutex> lock(ctx->mu);
         cudaSetDevice(ctx->device);
         if (c->comm) (c->aborted ? nccl_api().comm_abort : nccl_api().comm_destroy)(c->comm);
+        for (auto e : c->events) cudaEventDestroy(e);
+        for (auto e : c->sync)
+            if (e) cudaEventDestroy(e);
+        if (c->cstream) cudaStreamDestroy(c->cstream);
         delete c;
     }
     ctx_release(ctx);
@@ -2258,6 +2400,26 @@ int tcu_model_slice(const tcu_model *m, int first_chunk, int nchunks, tcu_model 
     });
 }
 
+int tcu_comm_breakdown(tcu_comm *c, int enable, double *ms) {
+    if (!c) return TCU_ERR_ARG;
+    return guarded(c->ctx, [&]() -> int {
+        if (ms) {
+            for (int i = 0; i < TCU_SHARD_PHASES; i++) ms[i] = 0.0;
+            const size_t n = c->marks.size();
+            if (n > 1) {
+                CU(cudaEventSynchronize(c->events[n - 1]));
+                for (size_t k = 0; k + 1 < n; k++) {
+                    float t = 0.f;
+                    CU(cudaEventElapsedTime(&t, c->events[k], c->events[k + 1]));
+                    if (c->marks[k] >= 0 && c->marks[k] < TCU_SHARD_PHASES) ms[c->marks[k]] += t;
+                }
+            }
+        }
+        c->prof = enable != 0;
+        return TCU_OK;
+    });
+}
+
 int tcu_stage_sharded_device(tcu_model *m, tcu_comm *c, const float *h, int rows, int out_n, float *out, void *stream) {
     if (!m || !c) return TCU_ERR_ARG;
     tcu_ctx *ctx = m->w->ctx;
@@ -2268,8 +2430,12 @@ int tcu_stage_sharded_device(tcu_model *m, tcu_comm *c, const float *h, int rows
         if (rows == 0) return TCU_OK;
         cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
         const size_t n = (size_t)rows * m->w->shape.d;
-        if (m->h.ensure(sizeof(float) * n)) drop_graphs(m);
+        // the rows padded to equal slices (in one or two groups, as stage_sharded splits them), the padding rows zero
+        const int G = rows >= 4096 * c->nranks ? 2 : 1;
+        const size_t np = (size_t)((rows + G * c->nranks - 1) / (G * c->nranks)) * G * c->nranks * m->w->shape.d;
+        if (m->h.ensure(sizeof(float) * np)) drop_graphs(m);
         CU(cudaMemcpyAsync(m->h.p, h, sizeof(float) * n, cudaMemcpyDeviceToDevice, s));
+        if (np > n) CU(cudaMemsetAsync(m->h.as<float>() + n, 0, sizeof(float) * (np - n), s));
         stage_sharded(ctx, m, c, rows, out_n, s);
         CU(cudaMemcpyAsync(out, m->out.p, sizeof(float) * (size_t)rows * out_n, cudaMemcpyDeviceToDevice, s));
         return TCU_OK;

@@ -695,10 +695,11 @@ __global__ void __launch_bounds__(256) k_attend_merge(const float *ms, const flo
     }
 }
 
-// Training rows split across devices: this device's parts of each (row, head) into one state, as the merge above
-// but without the division: packed[r][h hd + j] = sum_p w_p acc_p, packed[r][d + h] = sum_p w_p s_p, m[r][h] = M.
-__global__ void __launch_bounds__(256) k_merge_local(const float *ms, const float *acc, int P, int R, int H, int d,
-                                                     float *m_out, float *packed) {
+// Training rows split across devices: this device's parts of each (row, head) into one unnormalised state, as the
+// merge above but without the division, written as one part of the merge (ms_out [R][H][2] = max, weight sum;
+// acc_out [R][d] = weighted values), so that the states of all devices for a row are merged by k_attend_merge.
+__global__ void __launch_bounds__(256) k_merge_state(const float *ms, const float *acc, int P, int R, int H, int d,
+                                                     float *ms_out, float *acc_out) {
     extern __shared__ __align__(16) float wsm[];  // [P] part weights, then [8][hd] warp sums
     __shared__ float red[8];
     const int r = blockIdx.x / H, h = blockIdx.x % H, hd = d / H, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -734,29 +735,39 @@ __global__ void __launch_bounds__(256) k_merge_local(const float *ms, const floa
         wsum[warp * hd + j] = o;
     }
     __syncthreads();
-    float *dst = packed + (size_t)r * (d + H);
+    float *dst = acc_out + (size_t)r * d + h * hd;
     for (int j = tid; j < hd; j += blockDim.x) {
         float o = 0.f;
         for (int w = 0; w < 8; w++) o += wsum[w * hd + j];
-        dst[h * hd + j] = o;
+        dst[j] = o;
     }
     if (tid == 0) {
-        dst[d + h] = S;
-        m_out[(size_t)r * H + h] = S > 0.f ? M : -FLT_MAX;
+        float *q = ms_out + ((size_t)r * H + h) * 2;
+        q[0] = S > 0.f ? M : -FLT_MAX;
+        q[1] = S;
     }
 }
 
-// Scale this device's state to the maximum over devices (a device without keys for the row has weight 0).
-__global__ void k_merge_rescale(const float *m_local, const float *m_all, int R, int H, int d, float *packed) {
+// The sharded stage's merge across devices, around two collectives (an all-reduce of the maxima, a reduce-scatter of
+// the scaled states): one state per (row, head), ms [R][H][2] = (max, weight sum), acc [R][d] weighted values.
+// m_out[r][h]: the state's max (-FLT_MAX without weight).
+__global__ void k_state_max(const float *ms, int n, float *m_out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) m_out[i] = ms[2 * (size_t)i + 1] > 0.f ? ms[2 * (size_t)i] : -FLT_MAX;
+}
+
+// packed[r] = (acc[r] w_h, s_h w_h over h) with w_h = e^(m - M), M the maximum over devices (0 without weight).
+__global__ void k_state_pack(const float *ms, const float *acc, const float *m_all, int R, int H, int d, float *packed) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x, w = (size_t)d + H;
     if (i >= (size_t)R * w) return;
     const int r = (int)(i / w), c = (int)(i % w), h = c < d ? c / (d / H) : c - d;
-    const float ml = m_local[(size_t)r * H + h];
-    packed[i] *= ml > -FLT_MAX ? exp1(ml - m_all[(size_t)r * H + h]) : 0.f;
+    const float *st = ms + ((size_t)r * H + h) * 2;
+    const float f = st[1] > 0.f ? exp1(st[0] - m_all[(size_t)r * H + h]) : 0.f;
+    packed[i] = (c < d ? acc[(size_t)r * d + c] : st[1]) * f;
 }
 
-// nn.rs:280-286 finish: weighted values / weight sum.
-__global__ void k_merge_finish(const float *packed, int R, int H, int d, float *out, int ldo) {
+// nn.rs:280-286 finish of the summed states: weighted values / weight sum.
+__global__ void k_state_finish(const float *packed, int R, int H, int d, float *out, int ldo) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)R * d) return;
     const int r = (int)(i / d), c = (int)(i % d);
@@ -1134,27 +1145,39 @@ cudaError_t launch_attend_flash(int kv, int hd, const AttnArgs &a, cudaStream_t 
     return cudaSuccess;
 }
 
-cudaError_t launch_merge_local(const AttnArgs &a, int parts, float *m, float *packed, cudaStream_t s, uint64_t *launches) {
+cudaError_t launch_merge_state(const AttnArgs &a, int parts, float *ms_out, float *acc_out, cudaStream_t s,
+                               uint64_t *launches) {
+    if (a.R <= 0) return cudaSuccess;
     const size_t smem = sizeof(float) * ((size_t)((parts + 3) & ~3) + 8 * (size_t)(a.d / a.heads));
-    cudaError_t e = allow_smem(k_merge_local, smem);
+    cudaError_t e = allow_smem(k_merge_state, smem);
     if (e != cudaSuccess) return e;
-    k_merge_local<<<a.R * a.heads, 256, smem, s>>>(a.part_ms, a.part_acc, parts, a.R, a.heads, a.d, m, packed);
+    k_merge_state<<<a.R * a.heads, 256, smem, s>>>(a.part_ms, a.part_acc, parts, a.R, a.heads, a.d, ms_out, acc_out);
     TCU_LAUNCHED(launches);
     return cudaGetLastError();
 }
 
-cudaError_t launch_merge_rescale(const float *m_local, const float *m_all, int R, int H, int d, float *packed,
-                                 cudaStream_t s, uint64_t *launches) {
+cudaError_t launch_state_max(const float *ms, int R, int H, float *m_out, cudaStream_t s, uint64_t *launches) {
+    const int n = R * H;
+    if (n <= 0) return cudaSuccess;
+    k_state_max<<<(n + 255) / 256, 256, 0, s>>>(ms, n, m_out);
+    TCU_LAUNCHED(launches);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_state_pack(const float *ms, const float *acc, const float *m_all, int R, int H, int d, float *packed,
+                              cudaStream_t s, uint64_t *launches) {
     const size_t n = (size_t)R * (d + H);
-    k_merge_rescale<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(m_local, m_all, R, H, d, packed);
+    if (!n) return cudaSuccess;
+    k_state_pack<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ms, acc, m_all, R, H, d, packed);
     TCU_LAUNCHED(launches);
     return cudaGetLastError();
 }
 
-cudaError_t launch_merge_finish(const float *packed, int R, int H, int d, float *out, int ldo, cudaStream_t s,
+cudaError_t launch_state_finish(const float *packed, int R, int H, int d, float *out, int ldo, cudaStream_t s,
                                 uint64_t *launches) {
     const size_t n = (size_t)R * d;
-    k_merge_finish<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(packed, R, H, d, out, ldo);
+    if (!n) return cudaSuccess;
+    k_state_finish<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(packed, R, H, d, out, ldo);
     TCU_LAUNCHED(launches);
     return cudaGetLastError();
 }

@@ -59,6 +59,9 @@ struct AttnArgs {
     int tc_eK = 0, tc_eV = 0;      // tensor-core path: power-of-two scalings of the keys and values
     int *err = nullptr;            // report slot (host memory, mapped): set to 1 when the kernel gave up waiting
     int parts_only = 0;            // 1: always leave parts (no merge), even with a single split
+    // tensor-core path: when set, the result is the merged state left unnormalised: out [R][ldo] the weighted values,
+    // state_ms [R][heads][2] the (max, weight sum) they are relative to (one split, or splits merged in the kernel)
+    float *state_ms = nullptr;
     const void *tc_tiles = nullptr;  // tensor-core path: the layer's tiles pre-split by launch_tc_tiles
     int *merge_cnt = nullptr;  // tensor-core path: [R / 128][heads] arrival counters (zero between launches); when
                                // set, the last split of each (row block, head) merges the parts itself
@@ -153,14 +156,16 @@ cudaError_t launch_attend_decode(int kv, int hd, const AttnArgs &a, cudaStream_t
 // row-blocked attention for many rows; merges itself when splits == 1, else writes parts
 cudaError_t launch_attend_flash(int kv, int hd, const AttnArgs &a, cudaStream_t s, uint64_t *launches);
 cudaError_t launch_attend_merge(const AttnArgs &a, int parts, cudaStream_t s, uint64_t *launches);
-// Attention over training rows split across devices (nn.rs:261-286 merge, in three steps around two all-reduces):
-// this device's parts into one unnormalised state per (row, head): m [R][H] its max, packed [R][d + H] the weighted
-// values then the weight sums; after the maxima are reduced (max) over devices, scale to the common max; after the
-// states are summed over devices, divide.
-cudaError_t launch_merge_local(const AttnArgs &a, int parts, float *m, float *packed, cudaStream_t s, uint64_t *launches);
-cudaError_t launch_merge_rescale(const float *m_local, const float *m_all, int R, int H, int d, float *packed,
-                                 cudaStream_t s, uint64_t *launches);
-cudaError_t launch_merge_finish(const float *packed, int R, int H, int d, float *out, int ldo, cudaStream_t s,
+// Attention over training rows split across devices (nn.rs:261-286 merge): this device's parts of each (row, head)
+// into one unnormalised state laid out as a single part (ms_out [R][H][2] = max, weight sum; acc_out [R][d]); its
+// maxima m_out [R][H]; the state scaled to the maxima over devices m_all, packed [R][d + H] (values, then weight
+// sums) for a sum over devices; the summed states divided (out [R][d]).
+cudaError_t launch_merge_state(const AttnArgs &a, int parts, float *ms_out, float *acc_out, cudaStream_t s,
+                               uint64_t *launches);
+cudaError_t launch_state_max(const float *ms, int R, int H, float *m_out, cudaStream_t s, uint64_t *launches);
+cudaError_t launch_state_pack(const float *ms, const float *acc, const float *m_all, int R, int H, int d, float *packed,
+                              cudaStream_t s, uint64_t *launches);
+cudaError_t launch_state_finish(const float *packed, int R, int H, int d, float *out, int ldo, cudaStream_t s,
                                 uint64_t *launches);
 cudaError_t launch_pack(const float *kvT, int ld, int d, int rows, int chunk, int kv, uint8_t *out, cudaStream_t s,
                         uint64_t *launches);

@@ -3,8 +3,9 @@
     python tests/multi_rank.py MODE RANK WORLD PORT
 
 MODE
-  merge-cpu  gloo on CPU: the cross-device attention merge (max all-reduce, rescale, sum all-reduce, divide) on
-             shards of a random cache, in numpy, against attention over the whole cache (src/nn.rs:187-286).
+  merge-cpu  gloo on CPU: the cross-device merge of the sharded stage (maxima all-reduced, states scaled to them,
+             summed with each rank keeping its slice of rows, divided) on shards of a random cache, in numpy,
+             against attention over the whole cache (src/nn.rs:187-286).
   stage-gpu  one GPU per rank: the sharded stage through the C ABI against the oracle's stage over the whole
              cache, and the f64 all-reduce of ensemble members' class-logit sums.
 Prints one JSON line with the rank's result.
@@ -33,20 +34,25 @@ def shard_chunks(nchunks, world, rank):
 
 
 def merge_cpu(rank, world, port):
+    """The merge of the sharded stage: each rank's unnormalised state per (row, head) over its chunks; the maxima
+    all-reduced (max); each rank's states scaled to them; summed over ranks and each rank keeping its slice of rows
+    (a reduce-scatter: here an all-reduce of the sum, then the slice); divided (nn.rs:261-286). The rows are padded to
+    equal slices."""
     import torch
     dist = init(rank, world, port)
     rng = np.random.default_rng(7)
-    R, H, hd, n, chunk = 5, 4, 16, 333, 40
+    R, H, hd, n, chunk = 7, 4, 16, 333, 40
     d = H * hd
-    q = rng.normal(0, 1, (R, d))
+    Rs = -(-R // world)
+    q = np.zeros((Rs * world, d))
+    q[:R] = rng.normal(0, 1, (R, d))
     k = rng.normal(0, 1, (n, d))
     v = rng.normal(0, 1, (n, d))
     nchunks = (n + chunk - 1) // chunk
     c0, nc = shard_chunks(nchunks, world, rank)
     lo, hi = c0 * chunk, min(n, (c0 + nc) * chunk)
-    # this rank's unnormalised state per (row, head)
-    m_loc = np.full((R, H), -np.inf)
-    packed = np.zeros((R, d + H))
+    m_loc = np.zeros((len(q), H))
+    packed = np.zeros((len(q), d + H))
     for h in range(H):
         sl = slice(h * hd, (h + 1) * hd)
         sc = q[:, sl] @ k[lo:hi, sl].T
@@ -57,25 +63,26 @@ def merge_cpu(rank, world, port):
         packed[:, d + h] = p.sum(1)
     mt = torch.from_numpy(m_loc.copy())
     dist.all_reduce(mt, op=dist.ReduceOp.MAX)
-    m_all = mt.numpy()
-    w = np.exp(m_loc - m_all)
+    w = np.exp(m_loc - mt.numpy())
     for h in range(H):
         packed[:, h * hd:(h + 1) * hd] *= w[:, h:h + 1]
         packed[:, d + h] *= w[:, h]
     pt = torch.from_numpy(packed)
     dist.all_reduce(pt, op=dist.ReduceOp.SUM)
-    packed = pt.numpy()
-    att = np.concatenate([packed[:, h * hd:(h + 1) * hd] / packed[:, d + h:d + h + 1] for h in range(H)], 1)
-    want = np.zeros((R, d))
+    mine = pt.numpy()[rank * Rs:(rank + 1) * Rs]
+    att = np.concatenate([mine[:, h * hd:(h + 1) * hd] / mine[:, d + h:d + h + 1] for h in range(H)], 1)
+    want = np.zeros((len(q), d))
     for h in range(H):
         sl = slice(h * hd, (h + 1) * hd)
         sc = q[:, sl] @ k[:, sl].T
         p = np.exp(sc - sc.max(1, keepdims=True))
         want[:, sl] = (p / p.sum(1, keepdims=True)) @ v[:, sl]
-    rows = torch.tensor([hi - lo])
-    dist.all_reduce(rows)
+    real = max(0, min(Rs, R - rank * Rs))
+    counts = torch.tensor([hi - lo, real])
+    dist.all_reduce(counts)
     dist.destroy_process_group()
-    return {"rank": rank, "err": float(np.abs(att - want).max()), "rows_total": int(rows.item()), "rows": hi - lo}
+    return {"rank": rank, "err": float(np.abs(att - want[rank * Rs:(rank + 1) * Rs]).max()), "rows_total": int(counts[0]),
+            "rows": hi - lo, "test_rows_total": int(counts[1])}
 
 
 def stage_gpu(rank, world, port):
@@ -106,7 +113,7 @@ def stage_gpu(rank, world, port):
         full = tcu.VramModel.from_parts(w, [n, 7, 10, chunk, kv, 1, 1], n, 10, scales, caches)
         c0, nc = tcu.shard_chunks((n + chunk - 1) // chunk, world, rank)
         shard = full.slice(c0, nc)
-        for rows in (1, 5, 70):
+        for rows in (1, 5, 70, 301, 8200):
             h = synth.row_reps(rows, m.d, 40 + rows)
             hd_ = torch.from_numpy(h).cuda()
             o = torch.empty((rows, 10), device="cuda")

@@ -1,6 +1,7 @@
-"""Host logic of the multi-device paths on CPU (gloo, two ranks as separate processes): the cross-device attention
-merge (max all-reduce, rescale, sum all-reduce, divide) gives the attention over the whole cache, and the shards
-cover every training row once. The same protocol runs on GPUs in tests/test_gpu_multi.py."""
+"""Host logic of the multi-device paths on CPU (gloo, ranks as separate processes): the merge of the sharded stage
+(maxima all-reduced, states scaled to them and summed, each rank keeping its equal slice of the padded rows) gives the
+attention over the whole cache; the shards cover every training row once and the slices every test row once. The
+same protocol runs on GPUs in tests/test_gpu_multi.py."""
 import json
 import os
 import socket
@@ -36,11 +37,12 @@ def run_ranks(mode, world, timeout, env=None):
     return outs
 
 
-def test_merge_over_two_ranks_equals_whole_cache():
-    outs = run_ranks("merge-cpu", 2, timeout=120)
+@pytest.mark.parametrize("world", [2, 3])
+def test_merge_over_ranks_equals_whole_cache(world):
+    outs = run_ranks("merge-cpu", world, timeout=120)
     for o in outs:
         assert o["err"] < 1e-12, o
-        assert o["rows_total"] == 333
+        assert o["rows_total"] == 333 and o["test_rows_total"] == 7
     assert sum(o["rows"] for o in outs) == 333
 
 
