@@ -462,6 +462,49 @@ def multi_configs(pkg, synth, gpu, w, d, world, rank, stream, comm, a, bf16):
     return res
 
 
+def bundle_load(pkg, gpu, w, vm, a, classes, d):
+    """Loading a fitted problem (the card tier's uploads): config 2's fitted cache written as a bundle the way
+    fit_raw stores it (m0/meta, m0/tree, m0/n0_scale, m0/n0_kv{l}), read back through the pinned staging buffers by
+    tcu_model_from_bundle (blocking; the file already in the page cache, so this is the upload path, not the disk),
+    and by a tier whose first call declines while the load runs on a thread of its own."""
+    import tempfile
+    from tabicl_anywhere_b200 import tirs
+    L = 12
+    nbytes = pkg.record(a.kv, d, CHUNK) * (a.train_rows // CHUNK) + (pkg.record(a.kv, d, a.train_rows % CHUNK) if a.train_rows % CHUNK else 0)
+    t = {"m0/meta": np.array([a.train_rows, FEATURES, classes, CHUNK, a.kv, 1, 1], np.int32),
+         "m0/tree": np.array([1, a.train_rows, classes] + list(range(classes)), np.int32), "m0/n0_scale": vm.scales()}
+    for l in range(L):
+        t[f"m0/n0_kv{l}"] = vm.layer_bytes(l, nbytes)
+    fd, path = tempfile.mkstemp(suffix=".tirs")
+    os.close(fd)
+    try:
+        tirs.write(path, t)
+        stored = L * nbytes + t["m0/n0_scale"].nbytes
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            m = pkg.VramModel.from_bundle(w, path, "m0/", 0)
+            times.append(time.perf_counter() - t0)
+            resident = m.nbytes
+            m.free()
+        best = min(times)
+        tier = pkg.VramTier(gpu, 4 * resident, 4 * resident, background=True)
+        h = tier.handle("tenant", "model", path, w)
+        x = np.zeros((1, d), np.float32)
+        t0 = time.perf_counter()
+        declined = h.stage("m0/", 0, x, d, classes) is None
+        tier.wait()
+        tier_s = time.perf_counter() - t0
+        answered = h.stage("m0/", 0, x, d, classes) is not None
+        h.free(), tier.free()
+    finally:
+        os.unlink(path)
+    return {"what": "config 2's fitted cache from a bundle file to the device (12 layers, i16)", "stored_bytes": stored,
+            "resident_bytes": resident, "from_bundle_ms": best * 1e3, "upload_gbs": stored / best / 1e9,
+            "tier_first_call_declined": declined, "tier_background_load_ms": tier_s * 1e3,
+            "tier_answers_after_load": answered}
+
+
 def full_predict(pkg, synth, gpu, vm, cfg, wt, a, rank, world, stream, out, classes):
     """The whole prediction of config 2's member from normalised features (the AttendCached `rows` hook,
     predict.rs:638-652): the column stage over the 100 feature groups, the row stage over the 104 tokens, the
@@ -709,6 +752,7 @@ def main():
         sizes.append({"rows": rs, "p50_us": ts[len(ts) // 2], "rows_per_s": rs / (ts[len(ts) // 2] * 1e-6)})
 
     full = full_predict(pkg, synth, gpu, vm, cfg, wt, a, rank, world, stream, out, classes)
+    load = bundle_load(pkg, gpu, w, vm, a, classes, d) if rank == 0 else None
 
     hbm, bf16, kind = peaks()
     traffic = ncu_traffic(a)
@@ -747,6 +791,7 @@ def main():
                                       "p50_gbs": (L * layer_bytes + weight_bytes) / (pct(0.5) * 1e-6) / 1e9}},
         "latency_rows": sizes,
         "full_predict": full,
+        "bundle_load": load,
         "clocks": clocks.summary(),
     }
     if not a.no_multi:

@@ -339,6 +339,9 @@ TCU_API int tcu_comm_init(tcu_ctx *ctx, const uint8_t id[TCU_COMM_ID_BYTES], int
 TCU_API void tcu_comm_free(tcu_comm *c);
 /* Sum `count` doubles over all ranks in place (device buffer), e.g. per-rank class-logit sums of ensemble members
  * placed one per device. Queued on `stream` (NULL: the context's stream). */
+/* Abort the communicator now (ncclCommAbort): for a rank that learned on the host that a peer has left, so that
+ * nothing waits on it; every later collective on it fails with TCU_ERR_STATE. */
+TCU_API int tcu_comm_abort(tcu_comm *c);
 TCU_API int tcu_comm_allreduce_f64(tcu_comm *c, double *buf, size_t count, void *stream);
 /* Wait up to timeout_ms for `stream` (NULL: the context's stream); on timeout the communicator is aborted, so that
  * collectives still waiting for a lost rank end, and TCU_ERR_CUDA is returned. The communicator is unusable after. */

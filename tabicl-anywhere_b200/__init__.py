@@ -152,6 +152,7 @@ def lib():
         "tcu_tier_debug_unpin": (None, [_c_void]),
         "tcu_stage_sharded_device": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_void, _c_void]),
         "tcu_comm_breakdown": (_c_int, [_c_void, _c_int, P(ctypes.c_double)]),
+        "tcu_comm_abort": (_c_int, [_c_void]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -750,6 +751,10 @@ class Comm:
 
     def wait(self, timeout_ms, stream=None):
         return self.gpu.check(lib().tcu_comm_wait(self._h, stream, int(timeout_ms)))
+
+    def abort(self):
+        """Abort the communicator (a peer has left): nothing waits on it; later collectives fail."""
+        return self.gpu.check(lib().tcu_comm_abort(self._h))
 
     SHARD_PHASES = ("attention", "local_merge", "max_scale_reduce_scatter", "finish", "dense", "gather_queries",
                     "decoder_outputs")

@@ -2345,6 +2345,15 @@ void tcu_comm_free(tcu_comm *c) {
     ctx_release(ctx);
 }
 
+int tcu_comm_abort(tcu_comm *c) {
+    if (!c) return TCU_ERR_ARG;
+    return guarded(c->ctx, [&]() -> int {
+        if (c->comm) nccl_api().comm_abort(c->comm);
+        c->comm = nullptr, c->aborted = true;
+        return TCU_OK;
+    });
+}
+
 int tcu_comm_allreduce_f64(tcu_comm *c, double *buf, size_t count, void *stream) {
     if (!c) return TCU_ERR_ARG;
     return guarded(c->ctx, [&]() -> int {

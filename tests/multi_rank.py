@@ -135,7 +135,73 @@ def stage_gpu(rank, world, port):
     return out
 
 
+def leave_gpu(rank, world, port):
+    """A rank leaves between steps (nothing of it in flight): it says so in the rendezvous store and aborts its own
+    communicator; the others see it in the store before their next launch and abort theirs, so no collective is left
+    waiting on the missing rank."""
+    import time
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, HERE)
+    from conftest import load_package
+    tcu = load_package()
+    from tabicl_anywhere_b200 import synth
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=timedelta(seconds=60))
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    torch.cuda.set_device(rank)
+    gpu = tcu.Gpu(rank)
+    uid = torch.zeros(tcu.COMM_ID_BYTES, dtype=torch.uint8)
+    if rank == 0:
+        uid = torch.frombuffer(bytearray(tcu.comm_unique_id()), dtype=torch.uint8)
+    dist.broadcast(uid, 0)
+    comm = tcu.Comm(gpu, bytes(uid.numpy().tobytes()), world, rank)
+    cfg = synth.config("full", icl_num_blocks=2)
+    wt = synth.weights(cfg, seed=51, std=0.08)
+    w = tcu.GpuWeights.from_tensors(gpu, synth.icl_shape(cfg), {k: v for k, v in wt.items() if k.startswith("icl_")},
+                                    for_fit=True)
+    n, chunk, d = 600, 64, 512
+    h = torch.from_numpy(synth.row_reps(n, d, 52)).cuda()
+    y = torch.from_numpy(synth.labels(n, 10, 53)).cuda()
+    torch.cuda.synchronize()
+    full = tcu.fit_icl(w, h.data_ptr(), y.data_ptr(), n, chunk, 1)
+    c0, nc = tcu.shard_chunks((n + chunk - 1) // chunk, world, rank)
+    shard = full.slice(c0, nc)
+    x = torch.from_numpy(synth.row_reps(40, d, 54)).cuda()
+    o = torch.empty((40, 10), device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    steps = 0
+    out = {"rank": rank}
+    for step in range(3):
+        # before every launch: has a rank left?
+        if store.check(["left"]):
+            out["saw_leave_before_step"] = step
+            break
+        shard.stage_sharded_device(comm, x.data_ptr(), 40, 10, o.data_ptr(), stream)
+        comm.wait(20000, stream)
+        steps += 1
+        dist.barrier()
+        if step == 0 and rank == world - 1:
+            # this rank leaves here: none of its work is in flight
+            torch.cuda.synchronize()
+            comm.abort()
+            store.set("left", str(rank))
+            out["left_after_step"] = step
+            break
+        if step == 0:
+            t0 = time.time()
+            while not store.check(["left"]) and time.time() - t0 < 30:
+                time.sleep(0.05)
+    if "left_after_step" not in out:
+        comm.abort()
+    out["steps"] = steps
+    torch.cuda.synchronize()
+    shard.free(), full.free(), w.free()
+    comm.free()
+    gpu.close()
+    return out
+
+
 if __name__ == "__main__":
     mode, rank, world, port = sys.argv[1], int(sys.argv[2]), int(sys.argv[3]), int(sys.argv[4])
-    res = {"merge-cpu": merge_cpu, "stage-gpu": stage_gpu}[mode](rank, world, port)
+    res = {"merge-cpu": merge_cpu, "stage-gpu": stage_gpu, "leave-gpu": leave_gpu}[mode](rank, world, port)
     print(json.dumps(res), flush=True)
