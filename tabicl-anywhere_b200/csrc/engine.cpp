@@ -856,7 +856,9 @@ static int attend_layer(tcu_ctx *ctx, tcu_model *m, const uint8_t *layer, int ro
         return parts_only ? nitems : 0;
     }
     a.tiles = tiles, a.ntiles = ntiles;
-    a.tiles_per_split = (ntiles + plan.splits - 1) / plan.splits;
+    // a merged state is left by the kernel itself for up to eight splits: keep to eight when one is asked for
+    const int splits = state_ms && plan.path == Path::Tensor ? std::min(plan.splits, 8) : plan.splits;
+    a.tiles_per_split = (ntiles + splits - 1) / splits;
     a.splits = (ntiles + a.tiles_per_split - 1) / a.tiles_per_split;
     if (plan.path == Path::Tensor) {
         if (!tc_tiles) fail(TCU_ERR_STATE, "attend: tensor-core tiles were not built");
@@ -1290,7 +1292,8 @@ static void represent(tcu_ctx *ctx, tcu_model *m, float *tok, int R, float *rep,
     const size_t M = (size_t)R * T;
     m->cqkv.ensure(sizeof(float) * M * 3 * e), m->catt.ensure(sizeof(float) * M * e), m->cnew.ensure(sizeof(float) * M * e);
     m->cmid.ensure(sizeof(float) * M * ff);
-    if (!row_attend_smem(e, T, heads)) m->ckt.ensure(sizeof(float) * row_attend_workspace(R, T, e));
+    if (row_attend_needs_workspace(e, T, T, heads) || row_attend_needs_workspace(e, T, rs.cls, heads))
+        m->ckt.ensure(sizeof(float) * row_attend_workspace(R, T, e));
     ensure_linear(m, M, std::max(e, ff));
     if (m->crope_T != T) {
         // nn.rs:309-321: cos and sin of position times frequency, in f32

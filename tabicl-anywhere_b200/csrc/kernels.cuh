@@ -194,6 +194,8 @@ cudaError_t launch_col_attend(const float *Q, int R, int F, const float *kv, siz
 // tables cs, sn [T][head width / 2]; `work` (row_attend_workspace floats) when row_attend_smem is 0.
 size_t row_attend_smem(int e, int T, int heads);
 size_t row_attend_workspace(int R, int T, int e);
+// Whether a row attention of nq queries over T tokens needs that workspace.
+bool row_attend_needs_workspace(int e, int T, int nq, int heads);
 cudaError_t launch_row_attend(const float *QKV, int R, int T, int nq, int e, int heads, const float *cs, const float *sn,
                               float *work, float *att, cudaStream_t s, uint64_t *launches);
 // tok [R][cls + F][e]: the class tokens, then the cells.

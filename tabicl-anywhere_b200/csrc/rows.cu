@@ -81,6 +81,62 @@ __global__ void __launch_bounds__(256) k_col_attend(const float *Q, int R, int F
     }
 }
 
+// The same attention with one query per thread: block (group g, head h, run of blockDim rows); the head's keys and
+// values of group g in shared memory as [n][HD] rows, read by every lane at once (broadcast); the query, then the
+// weighted values, in registers. The scores are taken twice (their maximum first, as the CPU's two-pass softmax
+// needs; then again, identically, for the weights), so each score, weight and weighted sum is the one above; only
+// the weights' sum is added in key order by one thread instead of across a warp.
+template <int HD>
+__global__ void __launch_bounds__(256) k_col_attend_q(const float *Q, int R, int F, const float *kv, size_t gstride,
+                                                      int e, int n, float scale, float *att) {
+    extern __shared__ __align__(16) float sm[];
+    const int g = blockIdx.x, h = blockIdx.y;
+    const float *Kg = kv + (size_t)g * gstride, *Vg = Kg + (size_t)e * n;
+    float *Ks = sm, *Vs = sm + (size_t)n * HD;
+    for (int i = threadIdx.x; i < n * HD; i += blockDim.x) {
+        const int j = i / n, k = i - j * n;
+        Ks[k * HD + j] = Kg[(size_t)(h * HD + j) * n + k];
+        Vs[k * HD + j] = Vg[(size_t)(h * HD + j) * n + k];
+    }
+    __syncthreads();
+    const int r = blockIdx.z * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    const size_t cell = (size_t)r * F + g;
+    const float *qp = Q + cell * e + h * HD;
+    float q[HD], acc[HD];
+#pragma unroll
+    for (int j = 0; j < HD; j++) q[j] = qp[j] * scale, acc[j] = 0.f;
+    auto score = [&](int k) {
+        const float4 *kr = reinterpret_cast<const float4 *>(Ks + k * HD);
+        float s = 0.f;
+#pragma unroll
+        for (int j4 = 0; j4 < HD / 4; j4++) {
+            const float4 kk = kr[j4];
+            s = fmaf(q[4 * j4], kk.x, s), s = fmaf(q[4 * j4 + 1], kk.y, s);
+            s = fmaf(q[4 * j4 + 2], kk.z, s), s = fmaf(q[4 * j4 + 3], kk.w, s);
+        }
+        return s;
+    };
+    float mx = -FLT_MAX;
+    for (int k = 0; k < n; k++) mx = fmaxf(mx, score(k));
+    float sum = 0.f;
+    for (int k = 0; k < n; k++) {
+        const float p = exp1(score(k) - mx);
+        sum += p;
+        const float4 *vr = reinterpret_cast<const float4 *>(Vs + k * HD);
+#pragma unroll
+        for (int j4 = 0; j4 < HD / 4; j4++) {
+            const float4 vv = vr[j4];
+            acc[4 * j4] = fmaf(vv.x, p, acc[4 * j4]), acc[4 * j4 + 1] = fmaf(vv.y, p, acc[4 * j4 + 1]);
+            acc[4 * j4 + 2] = fmaf(vv.z, p, acc[4 * j4 + 2]), acc[4 * j4 + 3] = fmaf(vv.w, p, acc[4 * j4 + 3]);
+        }
+    }
+    const float inv = 1.0f / sum;
+    float *op = att + cell * e + h * HD;
+#pragma unroll
+    for (int j = 0; j < HD; j++) op[j] = acc[j] * inv;
+}
+
 // The rotary rotation (nn.rs:380-395) of element j of a head's key or query row x (head width hd), position t.
 __device__ __forceinline__ float rope(const float *x, int j, int half, const float *cs, const float *sn, int t) {
     if (j < half) return x[j] * cs[t * half + j] - x[j + half] * sn[t * half + j];
@@ -157,6 +213,61 @@ __global__ void __launch_bounds__(256) k_row_attend(const float *QKV, int R, int
     }
 }
 
+// k_row_attend with one query token per thread: block (row r, head h), the head's rotated keys and values of the row
+// in shared memory as [T][HD] rows, read by every lane at once; the query and the weighted values in registers.
+// Scores taken twice (maximum, then weights) as in k_col_attend_q: the same scores, weights and weighted sums as
+// k_row_attend, the weights' sum added in key order.
+template <int HD>
+__global__ void __launch_bounds__(512) k_row_attend_q(const float *QKV, int R, int T, int nq, int e, const float *cs,
+                                                       const float *sn, float *att) {
+    extern __shared__ __align__(16) float sm[];
+    const int r = blockIdx.x, h = blockIdx.y, half = HD / 2;
+    const float *base = QKV + (size_t)r * T * 3 * e;
+    float *Ks = sm, *Vs = sm + (size_t)T * HD;
+    for (int i = threadIdx.x; i < T * HD; i += blockDim.x) {
+        const int t = i / HD, j = i - t * HD;
+        Ks[i] = rope(base + (size_t)t * 3 * e + e + h * HD, j, half, cs, sn, t);
+        Vs[i] = base[(size_t)t * 3 * e + 2 * e + h * HD + j];
+    }
+    __syncthreads();
+    const int t = threadIdx.x;
+    if (t >= nq) return;
+    const float inv = 1.0f / sqrtf((float)HD);
+    const float *qr = base + (size_t)t * 3 * e + h * HD;
+    float q[HD], acc[HD];
+#pragma unroll
+    for (int j = 0; j < HD; j++) q[j] = rope(qr, j, half, cs, sn, t) * inv, acc[j] = 0.f;
+    auto score = [&](int k) {
+        const float4 *kr = reinterpret_cast<const float4 *>(Ks + k * HD);
+        float s = 0.f;
+#pragma unroll
+        for (int j4 = 0; j4 < HD / 4; j4++) {
+            const float4 kk = kr[j4];
+            s = fmaf(q[4 * j4], kk.x, s), s = fmaf(q[4 * j4 + 1], kk.y, s);
+            s = fmaf(q[4 * j4 + 2], kk.z, s), s = fmaf(q[4 * j4 + 3], kk.w, s);
+        }
+        return s;
+    };
+    float mx = -FLT_MAX;
+    for (int k = 0; k < T; k++) mx = fmaxf(mx, score(k));
+    float sum = 0.f;
+    for (int k = 0; k < T; k++) {
+        const float p = exp1(score(k) - mx);
+        sum += p;
+        const float4 *vr = reinterpret_cast<const float4 *>(Vs + k * HD);
+#pragma unroll
+        for (int j4 = 0; j4 < HD / 4; j4++) {
+            const float4 vv = vr[j4];
+            acc[4 * j4] = fmaf(vv.x, p, acc[4 * j4]), acc[4 * j4 + 1] = fmaf(vv.y, p, acc[4 * j4 + 1]);
+            acc[4 * j4 + 2] = fmaf(vv.z, p, acc[4 * j4 + 2]), acc[4 * j4 + 3] = fmaf(vv.w, p, acc[4 * j4 + 3]);
+        }
+    }
+    const float s = 1.0f / sum;
+    float *op = att + ((size_t)r * nq + t) * e + h * HD;
+#pragma unroll
+    for (int j = 0; j < HD; j++) op[j] = acc[j] * s;
+}
+
 // tok [R][T][e]: rows t < cls are the class tokens, rows cls + g the cells X [R * F][e] (T = cls + F).
 __global__ void k_tokens(const float *X, const float *cls_tokens, int R, int F, int cls, int e, float *tok) {
     const int T = cls + F;
@@ -214,8 +325,28 @@ cudaError_t launch_col_cells(const float *x, int R, int F, int group, const floa
 
 size_t col_attend_smem(int e, int n, int heads) { return sizeof(float) * ((size_t)2 * e * n + 8 * (size_t)(n + e / heads)); }
 
+template <int HD>
+static cudaError_t col_attend_q(const float *Q, int R, int F, const float *kv, size_t gstride, int e, int n, int heads,
+                                float scale, float *att, cudaStream_t s) {
+    const size_t smem = sizeof(float) * 2 * (size_t)n * HD;
+    cudaError_t err = allow_dynamic_smem((const void *)k_col_attend_q<HD>, smem);
+    if (err != cudaSuccess) return err;
+    dim3 grid(F, heads, (R + 255) / 256);
+    k_col_attend_q<HD><<<grid, 256, smem, s>>>(Q, R, F, kv, gstride, e, n, scale, att);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_col_attend(const float *Q, int R, int F, const float *kv, size_t gstride, int e, int n, int heads,
                               float scale, float *att, cudaStream_t s, uint64_t *launches) {
+    const int hd = e / heads;
+    if (sizeof(float) * 2 * (size_t)n * hd <= 200 * 1024 && (hd == 8 || hd == 16 || hd == 32 || hd == 64)) {
+        const cudaError_t err = hd == 8    ? col_attend_q<8>(Q, R, F, kv, gstride, e, n, heads, scale, att, s)
+                                : hd == 16 ? col_attend_q<16>(Q, R, F, kv, gstride, e, n, heads, scale, att, s)
+                                : hd == 32 ? col_attend_q<32>(Q, R, F, kv, gstride, e, n, heads, scale, att, s)
+                                           : col_attend_q<64>(Q, R, F, kv, gstride, e, n, heads, scale, att, s);
+        if (launches) ++*launches;
+        return err;
+    }
     const size_t smem = col_attend_smem(e, n, heads);
     cudaError_t err = allow_dynamic_smem((const void *)k_col_attend, smem);
     if (err != cudaSuccess) return err;
@@ -240,8 +371,37 @@ size_t row_attend_smem(int e, int T, int heads) {
 }
 size_t row_attend_workspace(int R, int T, int e) { return (size_t)R * T * e; }
 
+template <int HD>
+static cudaError_t row_attend_q(const float *QKV, int R, int T, int nq, int e, int heads, const float *cs,
+                                const float *sn, float *att, cudaStream_t s) {
+    const size_t smem = sizeof(float) * 2 * (size_t)T * HD;
+    cudaError_t err = allow_dynamic_smem((const void *)k_row_attend_q<HD>, smem);
+    if (err != cudaSuccess) return err;
+    k_row_attend_q<HD><<<dim3(R, heads), (nq + 31) / 32 * 32, smem, s>>>(QKV, R, T, nq, e, cs, sn, att);
+    return cudaGetLastError();
+}
+
+// Whether the one-query-per-thread row attention takes the shape (else k_row_attend).
+static bool row_attend_by_query(int e, int T, int nq, int heads) {
+    const int hd = e / heads;
+    return nq <= 512 && sizeof(float) * 2 * (size_t)T * hd <= 200 * 1024 && (hd == 8 || hd == 16 || hd == 32 || hd == 64);
+}
+
+bool row_attend_needs_workspace(int e, int T, int nq, int heads) {
+    return !row_attend_by_query(e, T, nq, heads) && !row_attend_smem(e, T, heads);
+}
+
 cudaError_t launch_row_attend(const float *QKV, int R, int T, int nq, int e, int heads, const float *cs, const float *sn,
                               float *work, float *att, cudaStream_t s, uint64_t *launches) {
+    if (row_attend_by_query(e, T, nq, heads)) {
+        const int hd = e / heads;
+        const cudaError_t err = hd == 8    ? row_attend_q<8>(QKV, R, T, nq, e, heads, cs, sn, att, s)
+                                : hd == 16 ? row_attend_q<16>(QKV, R, T, nq, e, heads, cs, sn, att, s)
+                                : hd == 32 ? row_attend_q<32>(QKV, R, T, nq, e, heads, cs, sn, att, s)
+                                           : row_attend_q<64>(QKV, R, T, nq, e, heads, cs, sn, att, s);
+        if (launches) ++*launches;
+        return err;
+    }
     const size_t smem = row_attend_smem(e, T, heads);
     cudaError_t err;
     if (smem) {
