@@ -98,11 +98,11 @@ struct tcu_ctx {
 };
 
 // Which wait each report slot stands for.
-enum { ERR_ATTEND_TC = 0, ERR_GEMM_TC = 1, ERR_QMLP_TC = 2, ERR_ROWS = 3, ERR_SLOTS = 8 };
-static const char *const err_slot_names[6] = {
+enum { ERR_ATTEND_TC = 0, ERR_GEMM_TC = 1, ERR_QMLP_TC = 2, ERR_ROWS = 3, ERR_PEER = 6, ERR_SLOTS = 8 };
+static const char *const err_slot_names[7] = {
     "tensor-core attention (matrix-unit or copy wait)", "tensor-core linear layer (matrix-unit or copy wait)",
     "tensor-core query MLP (matrix-unit wait)", "one-kernel stage (grid barrier)", "one-kernel stage (key tile copy)",
-    "one-kernel stage (left after another CTA gave up)"};
+    "one-kernel stage (left after another CTA gave up)", "cross-device exchange (a peer's data never arrived)"};
 
 // A weight matrix [N][K] split once for the tensor cores: f16 hi + lo (bit patterns) of W * 2^e(n) in 128 x 64
 // blocks (tc_block_off), and 2^-e(n). No blocks when K is not a multiple of 64.
@@ -256,6 +256,14 @@ struct tcu_comm {
     // the sharded stage's collectives run on a stream of their own, ordered against the compute stream by events
     cudaStream_t cstream = nullptr;
     cudaEvent_t sync[10] = {};
+    // exchanges by peer stores: this rank's exchange buffer (mapped by every peer through CUDA IPC) and the peers'
+    // buffers mapped here; per exchange kind an epoch that every rank advances in step
+    int p2p = -1;  // -1 not tried yet, 0 not available (every rank agreed), 1 set up
+    void *pbuf = nullptr;
+    size_t pbytes = 0;
+    std::vector<void *> ppeer;
+    unsigned *pdone = nullptr;
+    unsigned epoch_q = 0, epoch_s = 0;
 };
 
 // ---- handle lifetimes: a context lives while its weights do, weights while their models do --------------------
@@ -894,7 +902,7 @@ static void linear(tcu_ctx *ctx, tcu_model *m, const float *x, int ldx, int R, i
 static void check_device_error(tcu_ctx *ctx) {
     volatile int *slot = ctx->err_host;
     std::string which;
-    for (int i = 0; i < 6; i++) {
+    for (int i = 0; i < 7; i++) {
         if (slot[i]) {
             slot[i] = 0;
             which += (which.empty() ? "" : "; ") + std::string(err_slot_names[i]);
@@ -1466,6 +1474,183 @@ static void nccl_check(ncclResult_t r, const char *what) {
 }
 
 // The stage with every layer's attention merged over the ranks of c (m holds this rank's rows; m->h in, m->out out).
+static bool p2p_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("TCU_SHARD_P2P");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// This rank's exchange buffer of at least `bytes`, mapped by every peer, and theirs mapped here (all ranks call this
+// with the same size, in step). The buffer is made anew when it must grow; the handles are exchanged by an NCCL
+// all-gather and every rank agrees (all-reduce of the outcome) whether the mappings work everywhere: false, for good,
+// when they do not.
+static bool ensure_peer(tcu_comm *c, size_t bytes, cudaStream_t s) {
+    if (c->p2p == 0 || !p2p_enabled() || c->nranks > PUSH_MAX_RANKS) return false;
+    if (c->p2p == 1 && bytes <= c->pbytes) return true;
+    const auto &api = nccl_api();
+    const int N = c->nranks, me = c->rank;
+    CU(cudaStreamSynchronize(s));
+    DevBuf hd, okd;
+    okd.ensure(sizeof(int));
+    if (c->pbuf) {
+        // a buffer that must grow: every rank lets go of its mappings of the others' before any is freed
+        for (int j = 0; j < (int)c->ppeer.size(); j++)
+            if (j != me && c->ppeer[j]) cudaIpcCloseMemHandle(c->ppeer[j]);
+        nccl_check(api.all_reduce(okd.p, okd.p, 1, ncclInt32, ncclMin, c->comm, s), "all-reduce (exchange buffers)");
+        CU(cudaStreamSynchronize(s));
+        CU(cudaFree(c->pbuf));
+    }
+    c->ppeer.assign(N, nullptr);
+    c->pbuf = nullptr, c->pbytes = 0;
+    bytes = (bytes + 4095) / 4096 * 4096;
+    CU(cudaMalloc(&c->pbuf, bytes));
+    CU(cudaMemset(c->pbuf, 0, bytes));
+    if (!c->pdone) CU(cudaMalloc(&c->pdone, sizeof(unsigned) * PUSH_MAX_RANKS));
+    CU(cudaMemset(c->pdone, 0, sizeof(unsigned) * PUSH_MAX_RANKS));
+    cudaIpcMemHandle_t mine;
+    CU(cudaIpcGetMemHandle(&mine, c->pbuf));
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    hd.ensure(hb * N);
+    CU(cudaMemcpy(hd.as<uint8_t>() + hb * me, &mine, hb, cudaMemcpyHostToDevice));
+    nccl_check(api.all_gather(hd.as<uint8_t>() + hb * me, hd.p, hb, ncclUint8, c->comm, s), "all-gather (exchange handles)");
+    CU(cudaStreamSynchronize(s));
+    std::vector<cudaIpcMemHandle_t> hs(N);
+    CU(cudaMemcpy(hs.data(), hd.p, hb * N, cudaMemcpyDeviceToHost));
+    int ok = 1;
+    for (int j = 0; j < N; j++) {
+        if (j == me) {
+            c->ppeer[j] = c->pbuf;
+            continue;
+        }
+        if (cudaIpcOpenMemHandle(&c->ppeer[j], hs[j], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            c->ppeer[j] = nullptr, ok = 0;
+        }
+    }
+    CU(cudaMemcpy(okd.p, &ok, sizeof(int), cudaMemcpyHostToDevice));
+    nccl_check(api.all_reduce(okd.p, okd.p, 1, ncclInt32, ncclMin, c->comm, s), "all-reduce (exchange mappings)");
+    CU(cudaMemcpyAsync(&ok, okd.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CU(cudaStreamSynchronize(s));
+    c->epoch_q = c->epoch_s = 0;
+    if (!ok) {
+        for (int j = 0; j < N; j++)
+            if (j != me && c->ppeer[j]) cudaIpcCloseMemHandle(c->ppeer[j]);
+        c->ppeer.assign(N, nullptr);
+        CU(cudaFree(c->pbuf));
+        c->pbuf = nullptr, c->p2p = 0;
+        return false;
+    }
+    c->pbytes = bytes, c->p2p = 1;
+    return true;
+}
+
+// The sharded stage with its exchanges as peer stores (NVLink) instead of collectives. The rows are padded to N
+// equal slices of Rs rows, rank j owning rows [j Rs, (j + 1) Rs). Every layer: every rank attends all rows over its
+// own chunks (the kernel leaving the merged state of its splits, unnormalised); it stores the states of rank j's rows
+// into j's exchange buffer; each rank, once every rank's states have arrived, merges them in rank order
+// (k_attend_merge: nn.rs:261-286) and runs the rest of the layer and the next query for its slice, whose queries it
+// stores into every rank's query buffer. Per layer and rank: R (d + 2H) floats and R d floats leave, as many arrive.
+// Nothing overwrites data still being read: a rank's next stores into a peer need the peer's own next step first.
+// False (nothing queued) when peer mappings are not available; the caller then takes the collective path.
+static bool stage_sharded_p2p(tcu_ctx *ctx, tcu_model *m, tcu_comm *c, int R, int out_n, cudaStream_t s) {
+    const auto &sh = m->w->shape;
+    const int d = sh.d, H = sh.heads, L = sh.layers, dff = sh.dec_ff, N = c->nranks, me = c->rank;
+    const int Rs = (R + N - 1) / N, Rp = Rs * N, r0 = me * Rs;
+    auto a16 = [](size_t b) { return (b + 255) / 256 * 256; };
+    const size_t off_q = 256, off_ms = off_q + a16(sizeof(float) * (size_t)Rp * d);
+    const size_t off_acc = off_ms + a16(sizeof(float) * (size_t)N * Rs * H * 2);
+    const size_t bytes = off_acc + a16(sizeof(float) * (size_t)N * Rs * d);
+    if (!ensure_peer(c, bytes, s)) return false;
+    check_ready(m);
+    if (out_n < 1 || out_n > sh.outs) fail(TCU_ERR_ARG, "stage: out_n must be 1..decoder outputs");
+    scan_model(ctx, m, ctx->stream);
+    ensure_work(m, Rp);
+    if (m->out.ensure(sizeof(float) * (size_t)Rp * out_n)) drop_graphs(m);
+    m->sh_mall.ensure(sizeof(float) * (size_t)Rp * H * 2);
+    uint8_t *base = static_cast<uint8_t *>(c->pbuf);
+    float *qbuf = reinterpret_cast<float *>(base + off_q), *rms = reinterpret_cast<float *>(base + off_ms);
+    float *racc = reinterpret_cast<float *>(base + off_acc);
+    const unsigned *flags_q = reinterpret_cast<unsigned *>(base), *flags_s = flags_q + PUSH_MAX_RANKS;
+    const float *scales = m->scales.as<float>();
+    float *h = m->h.as<float>(), *att = m->att.as<float>(), *om = m->out.as<float>(), *ms1 = m->sh_mall.as<float>();
+    float *hm = h + (size_t)r0 * d, *am = att + (size_t)r0 * d, *qm = qbuf + (size_t)r0 * d;
+    Launch ck{ctx, s};
+    const long long wait_cycles = 4000000000ll;  // about two seconds at boost clock
+    int *err = ctx->err_mapped + ERR_PEER;
+    PushArgs pa;
+    for (int j = 0; j < N; j++) pa.peer[j] = static_cast<uint8_t *>(c->ppeer[j]);
+    pa.done = c->pdone, pa.ranks = N, pa.me = me;
+    const int bpd = std::max(1, std::min(32, ctx->sms / std::max(1, N)));  // blocks per destination
+    c->marks.clear();
+    auto mark = [&](int phase) {
+        if (!c->prof) return;
+        const size_t i = c->marks.size();
+        if (i == c->events.size()) {
+            cudaEvent_t e;
+            CU(cudaEventCreate(&e));
+            c->events.push_back(e);
+        }
+        CU(cudaEventRecord(c->events[i], s));
+        c->marks.push_back(phase);
+    };
+    // this rank's slice of the queries to every rank, then all of them here
+    auto push_q = [&]() {
+        mark(5);
+        PushArgs a = pa;
+        a.segments = 1, a.epoch = ++c->epoch_q, a.flag_off = 0;
+        a.src[0] = qm, a.src_step[0] = 0, a.count[0] = (size_t)Rs * d, a.dst_off[0] = off_q + sizeof(float) * (size_t)r0 * d;
+        ck(launch_push(a, bpd, s, &ctx->launches), "push (queries)");
+        ck(launch_wait_flags(flags_q, N, a.epoch, wait_cycles, err, s, &ctx->launches), "wait (queries)");
+    };
+    mark(4);
+    query_rows(ctx, m, 0, scales, hm, Rs, qm, s);
+    push_q();
+    for (int l = 0; l < L; l++) {
+        mark(0);
+        const int parts = attend_layer(ctx, m, layer_ptr(m, l), m->rows, m->chunk, m->kv, m->items.as<int2>(), m->nitems,
+                                       m->tiles.as<int4>(), m->ntiles, qbuf, Rp, att, s, m->tc_eK[l], m->tc_eV[l], true,
+                                       tc_tiles_of(m, l), ms1);
+        mark(1);
+        const float *sms = parts == 0 ? ms1 : m->part_ms.as<float>(), *sacc = parts == 0 ? att : m->part_acc.as<float>();
+        if (parts > 1) {
+            AttnArgs a;
+            a.R = Rp, a.heads = H, a.d = d, a.part_ms = m->part_ms.as<float>(), a.part_acc = m->part_acc.as<float>();
+            ck(launch_merge_state(a, parts, ms1, att, s, &ctx->launches), "merge (local)");
+            sms = ms1, sacc = att;
+        }
+        // the states of rank j's rows into rank j's buffer, block `me`; then every rank's here
+        mark(2);
+        PushArgs a = pa;
+        a.segments = 2, a.epoch = ++c->epoch_s, a.flag_off = sizeof(unsigned) * PUSH_MAX_RANKS;
+        a.src[0] = sms, a.src_step[0] = (size_t)Rs * H * 2, a.count[0] = (size_t)Rs * H * 2;
+        a.dst_off[0] = off_ms + sizeof(float) * (size_t)me * Rs * H * 2;
+        a.src[1] = sacc, a.src_step[1] = (size_t)Rs * d, a.count[1] = (size_t)Rs * d;
+        a.dst_off[1] = off_acc + sizeof(float) * (size_t)me * Rs * d;
+        ck(launch_push(a, bpd, s, &ctx->launches), "push (states)");
+        ck(launch_wait_flags(flags_s, N, a.epoch, wait_cycles, err, s, &ctx->launches), "wait (states)");
+        mark(3);
+        AttnArgs b;
+        b.R = Rs, b.heads = H, b.d = d, b.part_ms = rms, b.part_acc = racc, b.out = am, b.ldo = d;
+        ck(launch_attend_merge(b, N, s, &ctx->launches), "merge (ranks)");
+        mark(4);
+        block_tail(ctx, m, l, hm, am, Rs, s);
+        if (l + 1 < L) {
+            query_rows(ctx, m, l + 1, scales + (size_t)(l + 1) * d, hm, Rs, qm, s);
+            push_q();
+        }
+    }
+    mark(6);
+    linear(ctx, m, hm, d, Rs, d, m->w->lnw, m->w->lnb, m->w->dec0w, m->w->dec0b, dff, m->mid.as<float>(), dff, 1, 0, s, m->w->tdec0);
+    linear(ctx, m, m->mid.as<float>(), dff, Rs, dff, nullptr, nullptr, m->w->dec2w, m->w->dec2b, out_n,
+           om + (size_t)r0 * out_n, out_n, 0, 0, s, m->w->tdec2);
+    nccl_check(nccl_api().all_gather(om + (size_t)r0 * out_n, om, (size_t)Rs * out_n, ncclFloat32, c->comm, s),
+               "all-gather (outputs)");
+    mark(7);
+    return true;
+}
+
 // predict.rs:398-409, 521-532 (training rows split over readers, partial states merged by nn.rs:261-286) with the
 // readers on separate devices. The rows are split into G groups (two when each rank's slice of a group keeps at least
 // 2048 rows, else one: the rest of a layer on fewer rows costs about as much, so splitting smaller calls loses more
@@ -1478,6 +1663,8 @@ static void nccl_check(ncclResult_t r, const char *what) {
 // kernels between them) on the communicator's own stream, so that one group's collectives run while the other group
 // computes; with timing on (tcu_comm_breakdown) everything runs on the caller's stream, one phase after another.
 static void stage_sharded(tcu_ctx *ctx, tcu_model *m, tcu_comm *c, int R, int out_n, cudaStream_t s) {
+    if (c->aborted) fail(TCU_ERR_STATE, "communicator was aborted");
+    if (stage_sharded_p2p(ctx, m, c, R, out_n, s)) return;
     check_ready(m);
     const auto &sh = m->w->shape;
     const int d = sh.d, H = sh.heads, L = sh.layers, dff = sh.dec_ff, N = c->nranks, me = c->rank;
@@ -2342,6 +2529,10 @@ void tcu_comm_free(tcu_comm *c) {
         for (auto e : c->events) cudaEventDestroy(e);
         for (auto e : c->sync)
             if (e) cudaEventDestroy(e);
+        for (size_t j = 0; j < c->ppeer.size(); j++)
+            if ((int)j != c->rank && c->ppeer[j]) cudaIpcCloseMemHandle(c->ppeer[j]);
+        if (c->pbuf) cudaFree(c->pbuf);
+        if (c->pdone) cudaFree(c->pdone);
         if (c->cstream) cudaStreamDestroy(c->cstream);
         delete c;
     }

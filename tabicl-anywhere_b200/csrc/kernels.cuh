@@ -212,6 +212,24 @@ cudaError_t launch_divide(float *y, const float *x, size_t n, float a, cudaStrea
 // class scores out [R][classes]; nodes in walk order {k, leaf, score offset, map offset}; wbuf [n_nodes][R].
 cudaError_t launch_tree_combine(const float *logits, const int4 *nodes, const int *map, int n_nodes, int R, int classes,
                                 float *wbuf, float *out, cudaStream_t s, uint64_t *launches);
+// The sharded stage's exchanges by peer stores (peer.cu): for every destination rank j, segment s's count[s] floats
+// at src[s] + j * src_step[s] go to peer[j] + dst_off[s] (bytes); once all of j's blocks are done, this rank's flag
+// in j's buffer (at flag_off, one u32 per source rank) becomes `epoch`. done: ranks counters in this rank's memory,
+// zero between pushes.
+constexpr int PUSH_MAX_RANKS = 8;
+struct PushArgs {
+    uint8_t *peer[PUSH_MAX_RANKS] = {};
+    const float *src[2] = {};
+    size_t src_step[2] = {}, count[2] = {}, dst_off[2] = {};
+    size_t flag_off = 0;
+    unsigned *done = nullptr;
+    int segments = 0, ranks = 0, me = 0;
+    unsigned epoch = 0;
+};
+cudaError_t launch_push(const PushArgs &a, int blocks_per_dest, cudaStream_t s, uint64_t *launches);
+// Wait (one thread, bounded by max_cycles) until flags[0..n) have all reached epoch; on giving up, 1 into *err.
+cudaError_t launch_wait_flags(const unsigned *flags, int n, unsigned epoch, long long max_cycles, int *err,
+                              cudaStream_t s, uint64_t *launches);
 // Opt `kernel` in to `bytes` of dynamic shared memory on the current device (the attribute is per function and
 // device); remembered per (device, kernel), so repeated calls cost a map lookup.
 cudaError_t allow_dynamic_smem(const void *kernel, size_t bytes);

@@ -6,6 +6,8 @@ MODE
   merge-cpu  gloo on CPU: the cross-device merge of the sharded stage (maxima all-reduced, states scaled to them,
              summed with each rank keeping its slice of rows, divided) on shards of a random cache, in numpy,
              against attention over the whole cache (src/nn.rs:187-286).
+  push-cpu   gloo on CPU: the same merge by peer stores (every rank's states of a row to the rank owning the row,
+             merged there in rank order).
   stage-gpu  one GPU per rank: the sharded stage through the C ABI against the oracle's stage over the whole
              cache, and the f64 all-reduce of ensemble members' class-logit sums.
 Prints one JSON line with the rank's result.
@@ -83,6 +85,67 @@ def merge_cpu(rank, world, port):
     dist.destroy_process_group()
     return {"rank": rank, "err": float(np.abs(att - want[rank * Rs:(rank + 1) * Rs]).max()), "rows_total": int(counts[0]),
             "rows": hi - lo, "test_rows_total": int(counts[1])}
+
+
+def push_cpu(rank, world, port):
+    """The merge of the sharded stage by peer stores: each rank's unnormalised state per (row, head) over its chunks,
+    for the rows of rank j's slice, goes to rank j (here by send/receive), which merges every rank's states in rank
+    order (nn.rs:261-286: the largest maximum, each state scaled to it, the sums, the division). Rows padded to equal
+    slices."""
+    import torch
+    dist = init(rank, world, port)
+    rng = np.random.default_rng(9)
+    R, H, hd, n, chunk = 7, 2, 8, 200, 24
+    d = H * hd
+    Rs = -(-R // world)
+    q = np.zeros((Rs * world, d))
+    q[:R] = rng.normal(0, 1, (R, d))
+    k = rng.normal(0, 1, (n, d))
+    v = rng.normal(0, 1, (n, d))
+    c0, nc = shard_chunks((n + chunk - 1) // chunk, world, rank)
+    lo, hi = c0 * chunk, min(n, (c0 + nc) * chunk)
+    ms = np.zeros((len(q), H, 2))
+    acc = np.zeros((len(q), d))
+    for h in range(H):
+        sl = slice(h * hd, (h + 1) * hd)
+        sc = q[:, sl] @ k[lo:hi, sl].T
+        m = sc.max(1)
+        p = np.exp(sc - m[:, None])
+        ms[:, h, 0], ms[:, h, 1] = m, p.sum(1)
+        acc[:, sl] = p @ v[lo:hi, sl]
+    got_ms = np.zeros((world, Rs, H, 2))
+    got_acc = np.zeros((world, Rs, d))
+    reqs, bufs = [], []
+    for j in range(world):
+        part = slice(j * Rs, (j + 1) * Rs)
+        if j == rank:
+            got_ms[j], got_acc[j] = ms[part], acc[part]
+            continue
+        reqs.append(dist.isend(torch.from_numpy(np.ascontiguousarray(ms[part])), j, tag=0))
+        reqs.append(dist.isend(torch.from_numpy(np.ascontiguousarray(acc[part])), j, tag=1))
+        bm, ba = torch.zeros((Rs, H, 2), dtype=torch.float64), torch.zeros((Rs, d), dtype=torch.float64)
+        reqs.append(dist.irecv(bm, j, tag=0))
+        reqs.append(dist.irecv(ba, j, tag=1))
+        bufs.append((j, bm, ba))
+    for r in reqs:
+        r.wait()
+    for j, bm, ba in bufs:
+        got_ms[j], got_acc[j] = bm.numpy(), ba.numpy()
+    att = np.zeros((Rs, d))
+    for h in range(H):
+        sl = slice(h * hd, (h + 1) * hd)
+        M = got_ms[:, :, h, 0].max(0)
+        w = np.where(got_ms[:, :, h, 1] > 0, np.exp(got_ms[:, :, h, 0] - M), 0.0)
+        S = (got_ms[:, :, h, 1] * w).sum(0)
+        att[:, sl] = (got_acc[:, :, sl] * w[:, :, None]).sum(0) / S[:, None]
+    want = np.zeros((len(q), d))
+    for h in range(H):
+        sl = slice(h * hd, (h + 1) * hd)
+        sc = q[:, sl] @ k[:, sl].T
+        p = np.exp(sc - sc.max(1, keepdims=True))
+        want[:, sl] = (p / p.sum(1, keepdims=True)) @ v[:, sl]
+    dist.destroy_process_group()
+    return {"rank": rank, "err": float(np.abs(att - want[rank * Rs:(rank + 1) * Rs]).max())}
 
 
 def stage_gpu(rank, world, port):
@@ -203,5 +266,5 @@ def leave_gpu(rank, world, port):
 
 if __name__ == "__main__":
     mode, rank, world, port = sys.argv[1], int(sys.argv[2]), int(sys.argv[3]), int(sys.argv[4])
-    res = {"merge-cpu": merge_cpu, "stage-gpu": stage_gpu, "leave-gpu": leave_gpu}[mode](rank, world, port)
+    res = {"merge-cpu": merge_cpu, "push-cpu": push_cpu, "stage-gpu": stage_gpu, "leave-gpu": leave_gpu}[mode](rank, world, port)
     print(json.dumps(res), flush=True)

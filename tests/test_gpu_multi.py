@@ -14,11 +14,12 @@ pytestmark = pytest.mark.gpu
 STAGE = 5e-5
 
 
-def test_sharded_stage_on_two_gpus():
+@pytest.mark.parametrize("exchange", ["peer stores", "collectives"])
+def test_sharded_stage_on_two_gpus(exchange):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", TCU_SHARD_P2P="1" if exchange == "peer stores" else "0")
     outs = run_ranks("stage-gpu", 2, timeout=900, env=env)
     for o in outs:
         for k, err in o["stage"].items():

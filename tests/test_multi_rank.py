@@ -1,7 +1,8 @@
-"""Host logic of the multi-device paths on CPU (gloo, ranks as separate processes): the merge of the sharded stage
-(maxima all-reduced, states scaled to them and summed, each rank keeping its equal slice of the padded rows) gives the
-attention over the whole cache; the shards cover every training row once and the slices every test row once. The
-same protocol runs on GPUs in tests/test_gpu_multi.py."""
+"""Host logic of the multi-device paths on CPU (gloo, ranks as separate processes): both merges of the sharded stage
+(by collectives: maxima all-reduced, states scaled to them and summed, each rank keeping its equal slice of the
+padded rows; by peer stores: every rank's states of a row sent to the rank owning it and merged there in rank order)
+give the attention over the whole cache; the shards cover every training row once. The same protocols run on GPUs
+in tests/test_gpu_multi.py."""
 import json
 import os
 import socket
@@ -44,6 +45,13 @@ def test_merge_over_ranks_equals_whole_cache(world):
         assert o["err"] < 1e-12, o
         assert o["rows_total"] == 333 and o["test_rows_total"] == 7
     assert sum(o["rows"] for o in outs) == 333
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_merge_by_peer_stores_equals_whole_cache(world):
+    outs = run_ranks("push-cpu", world, timeout=120)
+    for o in outs:
+        assert o["err"] < 1e-12, o
 
 
 @pytest.mark.parametrize("n,world", [(1, 1), (7, 2), (40, 3), (39, 8), (3, 8)])
