@@ -353,17 +353,19 @@ TCU_API int tcu_model_slice(const tcu_model *m, int first_chunk, int nchunks, tc
 /* The stage of `rows` rows (h, out device buffers as in tcu_stage_device, the same rows on every rank) with `m`
  * holding this rank's shard of the training rows (predict.rs:398-409, 521-532 with the readers on separate devices).
  * The rows are padded to equal slices of ceil(rows / ranks), one per rank. Every layer, each rank attends all rows
- * over its shard; the partial states (max, weight sum, weighted values per row and head) are merged across ranks
- * (nn.rs:261-286) by an all-reduce of the maxima and a reduce-scatter of the states scaled to them, which leaves each
- * rank the merged states of its own slice; it runs the rest of the layer and the next layer's query for that slice
- * only, and an all-gather gives every rank all queries. Every rank ends with all rows' outputs. Queued on `stream`
- * (NULL: the context's stream). */
+ * over its shard; the partial states (max, weight sum, weighted values per row and head) of each slice go to the rank
+ * owning it, which merges them (nn.rs:261-286) and runs the rest of the layer and the next layer's query for its
+ * slice only; every rank then receives all queries. The exchanges are stores into the peers' memory over NVLink
+ * (CUDA IPC mappings set up at the first call, flags with bounded waits; a wait that gives up is reported as for the
+ * other kernels), or, where the mappings are not available on every rank (or with TCU_SHARD_P2P=0), NCCL: an
+ * all-reduce of the maxima, a reduce-scatter of the states scaled to them and an all-gather of the queries. Every rank
+ * ends with all rows' outputs. Queued on `stream` (NULL: the context's stream). */
 TCU_API int tcu_stage_sharded_device(tcu_model *m, tcu_comm *c, const float *h, int rows, int out_n, float *out,
                                      void *stream);
-/* Phases of tcu_stage_sharded_device timed by tcu_comm_breakdown: attention over the shard, merge of its splits and
- * the states' maxima, the all-reduce of the maxima with the scaling and the reduce-scatter of the states, the
- * division of the merged states, the rest of each layer and the next query, the gather of queries, the decoder and
- * the gather of outputs. */
+/* Phases of tcu_stage_sharded_device timed by tcu_comm_breakdown: attention over the shard; merge of its splits (and
+ * the states' maxima); the exchange of states (peer stores and the wait for every rank's, or the all-reduce of the
+ * maxima, the scaling and the reduce-scatter); the merge over ranks (or the division of the summed states); the rest
+ * of each layer and the next query; the exchange of queries; the decoder and the gather of outputs. */
 enum { TCU_SHARD_PHASES = 7 };
 /* ms (NULL: only switch): the device time of each phase in the last sharded call made while timing was on (summed
  * over layers; waits for that call); then timing on for the following calls when `enable` is nonzero. */

@@ -756,7 +756,7 @@ class Comm:
         """Abort the communicator (a peer has left): nothing waits on it; later collectives fail."""
         return self.gpu.check(lib().tcu_comm_abort(self._h))
 
-    SHARD_PHASES = ("attention", "local_merge", "max_scale_reduce_scatter", "finish", "dense", "gather_queries",
+    SHARD_PHASES = ("attention", "local_merge", "exchange_states", "merge_states", "dense", "exchange_queries",
                     "decoder_outputs")
 
     def breakdown(self, enable):
