@@ -55,10 +55,16 @@ class OrCBlock(ctypes.Structure):
                [("ff", ctypes.c_int)]
 
 
+class OrIsab1(ctypes.Structure):
+    _fields_ = [("b", OrCBlock)] + [(n, _fp) for n in ("sb0w", "sb0b", "sb2w", "sb2b", "q0w", "q0b", "q2w", "q2b")] + \
+               [("hid", ctypes.c_int), ("ind", _fp)]
+
+
 class OrRowsModel(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in ("e", "group", "inds", "cls", "col_heads", "row_heads", "ncol", "nrow")] + \
                [("in_w", _fp), ("in_b", _fp), ("col", _P(OrCBlock)), ("cls_tokens", _fp), ("row", _P(OrCBlock)),
-                ("rope_freqs", _fp), ("out_lnw", _fp), ("out_lnb", _fp)]
+                ("rope_freqs", _fp), ("out_lnw", _fp), ("out_lnb", _fp), ("col1", _P(OrIsab1)), ("col_y", _fp),
+                ("max_classes", ctypes.c_int)]
 
 
 def lib():
@@ -206,6 +212,33 @@ class RowsModel:
         m.cls_tokens, m.rope_freqs = k(g("row_interactor.cls_tokens")), k(g("row_interactor.tf_row.rope.freqs"))
         m.out_lnw = k(g("row_interactor.out_ln.weight"))
         m.out_lnb = k(g("row_interactor.out_ln.bias") if "row_interactor.out_ln.bias" in tensors else np.zeros(e, np.float32))
+        # fitting: each column block's first attention with its scalable softmax and inducing points, and the label's
+        # embedding table (model.rs:163-177: a class's row = weight column + bias; regression: [weight][bias])
+        p1 = "col_embedder.tf_col.blocks.0.multihead_attn1."
+        self.fit = p1 + "attn.in_proj_weight" in tensors and "col_embedder.y_encoder.weight" in tensors
+        if self.fit:
+            isabs = []
+            for i in range(ncol):
+                p = f"col_embedder.tf_col.blocks.{i}."
+                a = OrIsab1()
+                a.b = block(p + "multihead_attn1.")
+                ss = p + "multihead_attn1.attn.ssmax_layer."
+                a.sb0w, a.sb0b = k(g(ss + "base_mlp.0.weight")), k(g(ss + "base_mlp.0.bias"))
+                a.sb2w, a.sb2b = k(g(ss + "base_mlp.2.weight")), k(g(ss + "base_mlp.2.bias"))
+                a.q0w, a.q0b = k(g(ss + "query_mlp.0.weight")), k(g(ss + "query_mlp.0.bias"))
+                a.q2w, a.q2b = k(g(ss + "query_mlp.2.weight")), k(g(ss + "query_mlp.2.bias"))
+                a.hid = g(ss + "base_mlp.0.bias").size
+                a.ind = k(g(p + "ind_vectors"))
+                isabs.append(a)
+            self._isabs = (OrIsab1 * ncol)(*isabs)
+            m.col1 = ctypes.cast(self._isabs, _P(OrIsab1))
+            yw, yb = g("col_embedder.y_encoder.weight"), g("col_embedder.y_encoder.bias")
+            mc = cfg["max_classes"]
+            if mc > 0:
+                table = (yw.reshape(e, mc).T + yb[None, :]).astype(np.float32)
+            else:
+                table = np.concatenate([yw, yb]).astype(np.float32)
+            m.col_y, m.max_classes = k(table), mc
         self.m = m
         self.e, self.cls, self.inds, self.ncol, self.nrow = e, m.cls, m.inds, ncol, nrow
 
@@ -229,6 +262,23 @@ def embed(rm, x, col_kv, digits=1):
     tok = np.empty((n, rm.cls + feats, rm.e), np.float32)
     lib().or_embed(rm.ref, _p(x), n, feats, _p(ck), digits, _p(tok))
     return tok
+
+
+def fit_columns(rm, x, y, chunk, bases=(0,)):
+    """fit.rs:298-420: training rows x [n][features] (normalised) and targets y to the member's column cache
+    [features][digits][blocks][2][e][inds] and the training tokens [n][cls + features][e]; `bases` the plan's label
+    digits (one entry, unused, for a single digit)."""
+    assert rm.fit, "the weights have no column-stage fit tensors"
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, feats = x.shape
+    y = np.ascontiguousarray(y, dtype=np.float32)
+    digits = len(bases)
+    b = np.ascontiguousarray(bases, dtype=np.int32)
+    col_kv = np.zeros((feats, digits, rm.ncol, 2, rm.e, rm.inds), np.float32)
+    tok = np.zeros((n, rm.cls + feats, rm.e), np.float32)
+    lib().or_fit_columns(rm.ref, _p(x), _p(y), n, feats, chunk, digits, b.ctypes.data_as(_P(ctypes.c_int32)), _p(col_kv),
+                         _p(tok))
+    return col_kv, tok
 
 
 def represent(rm, tok):

@@ -831,6 +831,15 @@ typedef struct {
     int ff;
 } or_cblock;
 
+/* A column block's first attention (multihead_attn1: the inducing points over a column's training cells) with its
+ * scalable softmax (base_mlp for the length term, query_mlp per head) and the inducing points; fit only. */
+typedef struct {
+    or_cblock b;
+    const float *sb0w, *sb0b, *sb2w, *sb2b, *q0w, *q0b, *q2w, *q2b;
+    int hid;
+    const float *ind; /* [inds][e] */
+} or_isab1;
+
 typedef struct {
     int e, group, inds, cls, col_heads, row_heads, ncol, nrow;
     const float *in_w, *in_b;         /* col_embedder.in_linear: [e][group], [e] */
@@ -839,6 +848,9 @@ typedef struct {
     const or_cblock *row;             /* nrow */
     const float *rope_freqs;          /* [row head width / 2] */
     const float *out_lnw, *out_lnb;   /* row_interactor.out_ln: [e] */
+    const or_isab1 *col1;             /* fit: the column blocks' first attention, ncol (NULL for prediction) */
+    const float *col_y;               /* fit: the label's embedding table (model.rs:163-177) */
+    int max_classes;
 } or_rows_model;
 
 /* nn.rs:156-164 feed_forward: x += l2(gelu(l1(norm2 x))); t [e], h [ff] scratch */
@@ -1019,4 +1031,169 @@ EXPORT void or_represent(const or_rows_model *m, float *tok, int n, int tokens, 
     j.m = m, j.tok = tok, j.rep = rep, j.tokens = tokens, j.cosv = cosv, j.sinv = sinv;
     par_for(n, represent_one, &j);
     free(cosv), free(sinv);
+}
+
+
+/* ---- fit.rs:298-420: the column stage of fitting ------------------------------------------------------------- */
+
+/* nn.rs:97-107 query_scale for the column stage's first attention: the scalable softmax's length term for n rows,
+ * times 1/sqrt(head width) */
+static void query_scale_c(const or_isab1 *a, int e, int heads, int n, float *out) {
+    const float inv = 1.0f / sqrtf((float)(e / heads));
+    const float logn = logf((float)(n > 1 ? n : 1));
+    float *h = malloc(sizeof(float) * a->hid);
+    for (int i = 0; i < a->hid; i++) h[i] = a->sb0w[i] * logn + a->sb0b[i];
+    gelu_inplace(h, a->hid);
+    linear(a->sb2w, a->sb2b, h, a->hid, e, out);
+    for (int i = 0; i < e; i++) out[i] *= inv;
+    free(h);
+}
+
+/* nn.rs:130-152 query with the first attention's weights (its in_proj's query rows) */
+static void query_c(const or_isab1 *a, int e, int heads, const float *scale, const float *x, float *q) {
+    const int hd = e / heads;
+    float *t = malloc(sizeof(float) * e), *h = malloc(sizeof(float) * a->hid), *mm = malloc(sizeof(float) * hd);
+    layer_norm(x, a->b.n1w, a->b.n1b, e, t);
+    linear(a->b.inw, a->b.inb, t, e, e, q);
+    for (int hh = 0; hh < heads; hh++) {
+        float *qh = q + hh * hd;
+        linear(a->q0w, a->q0b, qh, hd, a->hid, h);
+        gelu_inplace(h, a->hid);
+        linear(a->q2w, a->q2b, h, a->hid, hd, mm);
+        for (int i = 0; i < hd; i++) qh[i] *= scale[hh * hd + i] * (1.0f + or_tanh1(mm[i]));
+    }
+    free(t), free(h), free(mm);
+}
+
+/* model.rs:186-200 add_y: the embedding of target y added to a cell (a class's row of the table; for a regression
+ * model, weight times y plus bias) */
+static void add_y_c(const float *table, int max_classes, int w, float y, float *cell) {
+    if (max_classes > 0) {
+        const float *row = table + (size_t)y * w;
+        for (int i = 0; i < w; i++) cell[i] += row[i];
+    } else {
+        for (int i = 0; i < w; i++) cell[i] += table[i] * y + table[w + i];
+    }
+}
+
+typedef struct {
+    const or_rows_model *m;
+    const float *x, *y, *ind_q; /* ind_q [ncol][inds][e] */
+    const int *bases;
+    int n, feats, chunk, digits;
+    float *col_kv, *tok;
+} fitcol_job;
+
+/* fit.rs:326-420 col_one: one feature group's training cells through the column blocks, its cache written */
+static void fitcol_one(void *ctx, int g) {
+    const fitcol_job *j = (const fitcol_job *)ctx;
+    const or_rows_model *m = j->m;
+    const int e = m->e, inds = m->inds, nb = m->ncol, n = j->n, heads = m->col_heads, hd = e / heads, D = j->digits;
+    const int chunk = j->chunk < n ? j->chunk : n, tokens = m->cls + j->feats;
+    int ffmax = 0;
+    for (int b = 0; b < nb; b++) {
+        ffmax = m->col[b].ff > ffmax ? m->col[b].ff : ffmax;
+        ffmax = m->col1[b].b.ff > ffmax ? m->col1[b].b.ff : ffmax;
+    }
+    float *src = malloc(sizeof(float) * (size_t)n * e), *plain = NULL, *sum = NULL;
+    if (D > 1) plain = malloc(sizeof(float) * (size_t)n * e), sum = calloc((size_t)n * e, sizeof(float));
+    float *kt = malloc(sizeof(float) * (size_t)e * chunk), *vt = malloc(sizeof(float) * (size_t)e * chunk);
+    float *kv = malloc(sizeof(float) * 2 * e), *t = malloc(sizeof(float) * e), *hidden = malloc(sizeof(float) * (size_t)inds * e);
+    float *q = malloc(sizeof(float) * e), *h = malloc(sizeof(float) * ffmax), *tmp = malloc(sizeof(float) * hd);
+    float *sc = malloc(sizeof(float) * (chunk > inds ? chunk : inds)), *scale2 = malloc(sizeof(float) * e);
+    soft *softs = malloc(sizeof(soft) * inds);
+    for (int i = 0; i < inds; i++) {
+        softs[i].heads = heads, softs[i].d = e;
+        softs[i].m = malloc(sizeof(float) * heads), softs[i].s = malloc(sizeof(float) * heads), softs[i].acc = malloc(sizeof(float) * e);
+    }
+    soft st;
+    st.heads = heads, st.d = e;
+    st.m = malloc(sizeof(float) * heads), st.s = malloc(sizeof(float) * heads), st.acc = malloc(sizeof(float) * e);
+    for (int i = 0; i < e; i++) scale2[i] = 1.0f / sqrtf((float)hd);
+    float vals[8];
+    for (int r = 0; r < n; r++) {
+        float *cell = src + (size_t)r * e;
+        group_values(j->x + (size_t)r * j->feats, j->feats, g, m->group, vals);
+        int missing = 1;
+        for (int i = 0; i < m->group; i++) missing &= vals[i] == -100.0f;
+        if (missing)
+            for (int i = 0; i < e; i++) cell[i] = -100.0f;
+        else
+            linear(m->in_w, m->in_b, vals, m->group, e, cell);
+    }
+    if (D > 1) memcpy(plain, src, sizeof(float) * (size_t)n * e);
+    const size_t per = (size_t)2 * e * inds;
+    for (int dg = 0; dg < D; dg++) {
+        if (dg > 0) memcpy(src, plain, sizeof(float) * (size_t)n * e);
+        int divisor = 1;
+        for (int b = dg + 1; b < D; b++) divisor *= j->bases[b];
+        for (int r = 0; r < n; r++) {
+            const float yv = D > 1 ? (float)(((int)j->y[r] / divisor) % j->bases[dg]) : j->y[r];
+            add_y_c(m->col_y, m->max_classes, e, yv, src + (size_t)r * e);
+        }
+        float *rec = j->col_kv + (size_t)g * D * nb * per + (size_t)dg * nb * per;
+        for (int bi = 0; bi < nb; bi++) {
+            const or_isab1 *a1 = &m->col1[bi];
+            /* the inducing points look at this column's training cells, a chunk of rows at a time */
+            for (int i = 0; i < inds; i++) soft_reset(&softs[i]);
+            for (int r0 = 0; r0 < n; r0 += chunk) {
+                const int rc = chunk < n - r0 ? chunk : n - r0;
+                for (int r = 0; r < rc; r++) {
+                    layer_norm(src + (size_t)(r0 + r) * e, a1->b.n1w, a1->b.n1b, e, t);
+                    linear(a1->b.inw + (size_t)e * e, a1->b.inb + e, t, e, 2 * e, kv);
+                    for (int c = 0; c < e; c++) kt[(size_t)c * rc + r] = kv[c], vt[(size_t)c * rc + r] = kv[e + c];
+                }
+                for (int i = 0; i < inds; i++)
+                    soft_update_f32(&softs[i], j->ind_q + ((size_t)bi * inds + i) * e, kt, vt, rc, sc, tmp);
+            }
+            for (int i = 0; i < inds; i++) {
+                soft_finish(&softs[i]);
+                float *hid = hidden + (size_t)i * e;
+                linear(a1->b.ow, a1->b.ob, softs[i].acc, e, e, hid);
+                for (int c = 0; c < e; c++) hid[c] += a1->ind[(size_t)i * e + c];
+                feed_forward_c(&a1->b, e, hid, t, h);
+            }
+            /* their keys and values for the second attention: what prediction reuses */
+            const or_cblock *a2 = &m->col[bi];
+            float *rk = rec + (size_t)bi * per, *rv = rk + (size_t)e * inds;
+            for (int i = 0; i < inds; i++) {
+                layer_norm(hidden + (size_t)i * e, a2->n1w, a2->n1b, e, t);
+                linear(a2->inw + (size_t)e * e, a2->inb + e, t, e, 2 * e, kv);
+                for (int c = 0; c < e; c++) rk[(size_t)c * inds + i] = kv[c], rv[(size_t)c * inds + i] = kv[e + c];
+            }
+            for (int r = 0; r < n; r++) cached_block(a2, e, heads, scale2, rk, rv, inds, src + (size_t)r * e, t, q, h, sc, tmp, &st);
+        }
+        if (D > 1)
+            for (size_t i = 0; i < (size_t)n * e; i++) sum[i] += src[i];
+    }
+    if (D > 1) {
+        const float inv = 1.0f / (float)D;
+        for (size_t i = 0; i < (size_t)n * e; i++) src[i] = sum[i] * inv;
+    }
+    for (int r = 0; r < n; r++) memcpy(j->tok + ((size_t)r * tokens + m->cls + g) * e, src + (size_t)r * e, sizeof(float) * e);
+    for (int i = 0; i < inds; i++) free(softs[i].m), free(softs[i].s), free(softs[i].acc);
+    free(softs), free(st.m), free(st.s), free(st.acc);
+    free(src), free(plain), free(sum), free(kt), free(vt), free(kv), free(t), free(hidden), free(q), free(h), free(tmp), free(sc), free(scale2);
+}
+
+/* fit.rs:298-420 for a member's training rows: x [n][feats] (normalised), y [n] (classes, or the standardised target),
+ * the rows `chunk` at a time through the inducing points' attention, `digits` label digits of mixed-radix `bases`.
+ * Writes col_kv [feats][digits][blocks][2][e][inds] and the training tokens [n][cls + feats][e] (the class tokens,
+ * then the cells after the column stage), the row stage's input. */
+EXPORT void or_fit_columns(const or_rows_model *m, const float *x, const float *y, int n, int feats, int chunk,
+                           int digits, const int *bases, float *col_kv, float *tok) {
+    const int e = m->e, inds = m->inds, nb = m->ncol;
+    float *ind_q = malloc(sizeof(float) * (size_t)nb * inds * e), *scale = malloc(sizeof(float) * e);
+    /* fit.rs:300-314: the inducing points' queries are the same for every column */
+    for (int bi = 0; bi < nb; bi++) {
+        query_scale_c(&m->col1[bi], e, m->col_heads, n, scale);
+        for (int i = 0; i < inds; i++)
+            query_c(&m->col1[bi], e, m->col_heads, scale, m->col1[bi].ind + (size_t)i * e, ind_q + ((size_t)bi * inds + i) * e);
+    }
+    for (int r = 0; r < n; r++) memcpy(tok + (size_t)r * (m->cls + feats) * e, m->cls_tokens, sizeof(float) * m->cls * e);
+    fitcol_job j;
+    j.m = m, j.x = x, j.y = y, j.ind_q = ind_q, j.bases = bases, j.n = n, j.feats = feats, j.chunk = chunk < 8 ? 8 : chunk;
+    j.digits = digits, j.col_kv = col_kv, j.tok = tok;
+    par_for(feats, fitcol_one, &j);
+    free(ind_q), free(scale);
 }

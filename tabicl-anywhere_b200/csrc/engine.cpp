@@ -126,6 +126,18 @@ struct CBlockPtrs {
     int ff;
 };
 
+// A column block's first attention for fitting (multihead_attn1): on the device its LayerNorm, key/value rows of
+// in_proj, out-projection and feed-forward (`b`, `b.inw` [2e][e]) and the inducing points; on the host what the
+// inducing points' queries need (the query rows of in_proj and the scalable softmax's MLPs).
+struct Isab1 {
+    CBlockPtrs b;
+    const float *ind = nullptr;      // [inds][e]
+    const float *kv2w = nullptr, *kv2b = nullptr;  // the second attention's key/value rows of in_proj [2e][e]
+    SplitW tkv2;
+    std::vector<float> n1w, n1b, wq, bq, q0w, q0b, q2w, q2b, sb0w, sb0b, sb2w, sb2b, ind_h;
+    int hid = 0;
+};
+
 // The column and row stages' weights (src/model.rs:199-245), when the bundle has them.
 struct RowsWeights {
     bool on = false;
@@ -133,6 +145,11 @@ struct RowsWeights {
     const float *in_w = nullptr, *in_b = nullptr, *cls_tokens = nullptr, *out_lnw = nullptr, *out_lnb = nullptr;
     std::vector<float> rope_freqs;  // host copy: the position tables are made per token count
     std::vector<CBlockPtrs> col, row;
+    // fitting (weights made for_fit with the column stage's first attention present)
+    bool fit = false;
+    std::vector<Isab1> col1;
+    const float *col_y = nullptr;  // the label's embedding table (model.rs:163-177)
+    int max_classes = 0;
     DevBuf dev, dev16;
 };
 
@@ -603,15 +620,16 @@ static int rows_ready(tcu_weights *w) {
         Packer::SplitIdx tin, to, t1, t2;
         int ff;
     };
-    auto block = [&](const std::string &p, bool q_only, int ff) {
+    // in_proj rows: the query's only (q_only 1), the keys' and values' only (2), or all three (0)
+    auto block = [&](const std::string &p, int q_only, int ff) {
         BIdx x;
-        const int nin = q_only ? e : 3 * e;
+        const int nin = q_only == 1 ? e : (q_only == 2 ? 2 * e : 3 * e), first = q_only == 2 ? e : 0;
         const auto &inw = need(w, p + "attn.in_proj_weight", (size_t)3 * e * e);
         const auto &inb = need(w, p + "attn.in_proj_bias", (size_t)3 * e);
         x.n1w = pk.add(need(w, p + "norm1.weight", e));
         x.n1b = pk.add(opt_zero(w, p + "norm1.bias", e));
-        x.inw = pk.add(std::vector<float>(inw.begin(), inw.begin() + (size_t)nin * e));
-        x.inb = pk.add(std::vector<float>(inb.begin(), inb.begin() + nin));
+        x.inw = pk.add(std::vector<float>(inw.begin() + (size_t)first * e, inw.begin() + (size_t)(first + nin) * e));
+        x.inb = pk.add(std::vector<float>(inb.begin() + first, inb.begin() + first + nin));
         x.ow = pk.add(need(w, p + "attn.out_proj.weight", (size_t)e * e));
         x.ob = pk.add(need(w, p + "attn.out_proj.bias", e));
         x.n2w = pk.add(need(w, p + "norm2.weight", e));
@@ -625,11 +643,58 @@ static int rows_ready(tcu_weights *w) {
         x.ff = ff;
         return x;
     };
-    std::vector<BIdx> cb, rb;
+    std::vector<BIdx> cb, rb, c1, c2kv;
     for (int i = 0; i < s.col_blocks; i++)
-        cb.push_back(block("col_embedder.tf_col.blocks." + std::to_string(i) + ".multihead_attn2.", true, s.col_ff));
+        cb.push_back(block("col_embedder.tf_col.blocks." + std::to_string(i) + ".multihead_attn2.", 1, s.col_ff));
     for (int i = 0; i < s.row_blocks; i++)
-        rb.push_back(block("row_interactor.tf_row.blocks." + std::to_string(i) + ".", false, s.row_ff));
+        rb.push_back(block("row_interactor.tf_row.blocks." + std::to_string(i) + ".", 0, s.row_ff));
+    // fitting: the first attention of each column block (its key/value rows on the device, its query on the host),
+    // the inducing points, the second attention's key/value rows, and the label's embedding table
+    rw.fit = w->for_fit && w->host.count("col_embedder.tf_col.blocks.0.multihead_attn1.attn.in_proj_weight") &&
+             w->host.count("col_embedder.y_encoder.weight");
+    std::vector<size_t> i_ind;
+    size_t i_coly = 0;
+    rw.col1.clear();
+    if (rw.fit) {
+        for (int i = 0; i < s.col_blocks; i++) {
+            const std::string p = "col_embedder.tf_col.blocks." + std::to_string(i) + ".";
+            c1.push_back(block(p + "multihead_attn1.", 2, s.col_ff));
+            c2kv.push_back(block(p + "multihead_attn2.", 2, s.col_ff));
+            const auto &ind = need(w, p + "ind_vectors", (size_t)s.inds * e);
+            i_ind.push_back(pk.add(ind));
+            Isab1 a;
+            const std::string q = p + "multihead_attn1.", ss = q + "attn.ssmax_layer.";
+            const auto &inw = need(w, q + "attn.in_proj_weight", (size_t)3 * e * e);
+            const auto &inb = need(w, q + "attn.in_proj_bias", (size_t)3 * e);
+            a.n1w = need(w, q + "norm1.weight", e), a.n1b = opt_zero(w, q + "norm1.bias", e);
+            a.wq.assign(inw.begin(), inw.begin() + (size_t)e * e), a.bq.assign(inb.begin(), inb.begin() + e);
+            a.sb0b = w->host.at(ss + "base_mlp.0.bias");
+            a.hid = (int)a.sb0b.size();
+            const int hd = e / s.col_heads;
+            a.sb0w = need(w, ss + "base_mlp.0.weight", a.hid), a.sb2w = need(w, ss + "base_mlp.2.weight", (size_t)e * a.hid);
+            a.sb2b = need(w, ss + "base_mlp.2.bias", e);
+            a.q0w = need(w, ss + "query_mlp.0.weight", (size_t)a.hid * hd), a.q0b = need(w, ss + "query_mlp.0.bias", a.hid);
+            a.q2w = need(w, ss + "query_mlp.2.weight", (size_t)hd * a.hid), a.q2b = need(w, ss + "query_mlp.2.bias", hd);
+            a.ind_h = ind;
+            rw.col1.push_back(std::move(a));
+        }
+        rw.max_classes = w->shape.max_classes;
+        const auto &yw = w->host.at("col_embedder.y_encoder.weight");
+        const auto &yb = need(w, "col_embedder.y_encoder.bias", e);
+        std::vector<float> table;
+        if (rw.max_classes > 0) {
+            // model.rs:163-177: a class's row is the one-hot layer's weight column plus its bias
+            const int mc = rw.max_classes;
+            if (yw.size() != (size_t)e * mc) fail(TCU_ERR_FORMAT, "weights: col_embedder.y_encoder.weight has the wrong length");
+            table.resize((size_t)mc * e);
+            for (int c = 0; c < mc; c++)
+                for (int o = 0; o < e; o++) table[(size_t)c * e + o] = yw[(size_t)o * mc + c] + yb[o];
+        } else {
+            table = yw;
+            table.insert(table.end(), yb.begin(), yb.end());
+        }
+        i_coly = pk.add(table);
+    }
     const size_t i_inw = pk.add(need(w, "col_embedder.in_linear.weight", (size_t)e * s.group));
     const size_t i_inb = pk.add(need(w, "col_embedder.in_linear.bias", e));
     const size_t i_cls = pk.add(need(w, "row_interactor.cls_tokens", (size_t)s.cls * e));
@@ -645,6 +710,12 @@ static int rows_ready(tcu_weights *w) {
     rw.col.clear(), rw.row.clear();
     for (const auto &x : cb) rw.col.push_back(ptrs(x));
     for (const auto &x : rb) rw.row.push_back(ptrs(x));
+    for (size_t i = 0; i < rw.col1.size(); i++) {
+        rw.col1[i].b = ptrs(c1[i]);
+        rw.col1[i].ind = pk.P(i_ind[i]);
+        rw.col1[i].kv2w = pk.P(c2kv[i].inw), rw.col1[i].kv2b = pk.P(c2kv[i].inb), rw.col1[i].tkv2 = pk.S(c2kv[i].tin);
+    }
+    if (rw.fit) rw.col_y = pk.P(i_coly);
     rw.in_w = pk.P(i_inw), rw.in_b = pk.P(i_inb), rw.cls_tokens = pk.P(i_cls), rw.out_lnw = pk.P(i_lnw), rw.out_lnb = pk.P(i_lnb);
     return TCU_OK;
 }

@@ -6,11 +6,12 @@ tabicl-anywhere repository is available; the outputs are committed and the GPU b
 * tiny-clf.tirs / tiny-reg.tirs: the reference's tiny random TabICL checkpoints (tests/data/tiny-{clf,reg}.ckpt,
   made by its tools/make_tiny.py) as weight bundles: every tensor of the state dict as float32 plus
   config.json, the layout its tools/export_weights.py writes.
-* tiny-raw-icl.tirs: the prediction side of the reference's golden dump tests/data/tiny-raw.tirs (PyTorch
-  TabICL's own numbers for the tiny classifier): training and test row representations, training labels, the
-  in-context keys/values of every layer ([heads][rows][head width]) and the logits; and for the column and row
-  stages the normalised test rows, the column stage's cached keys/values of every block ([columns][heads][inducing
-  points][head width], the class-token columns first) and the test rows' tokens after the column stage.
+* tiny-raw-icl.tirs: the reference's golden dump tests/data/tiny-raw.tirs (PyTorch TabICL's own numbers for the
+  tiny classifier) without its plain-attention logits: the normalised training and test rows and training labels,
+  training and test row representations, the in-context keys/values of every layer ([heads][rows][head width]) and
+  the logits; and for the column and row stages the column stage's cached keys/values of every block ([columns]
+  [heads][inducing points][head width], the class-token columns first) and the training and test rows' tokens after
+  the column stage.
 """
 import json
 import os
@@ -41,7 +42,7 @@ def main(ref):
     weights(os.path.join(data, "tiny-clf.ckpt"), os.path.join(HERE, "tiny-clf.tirs"))
     weights(os.path.join(data, "tiny-reg.ckpt"), os.path.join(HERE, "tiny-reg.tirs"))
     raw = tirs.Bundle(os.path.join(data, "tiny-raw.tirs"))
-    keep = ["train_rep", "y_train", "test_rep", "logits", "x_test", "test_emb"]
+    keep = ["train_rep", "y_train", "test_rep", "logits", "x_test", "test_emb", "x_train", "train_emb"]
     keep += [n for n in raw.names() if n.startswith(("icl_k", "icl_v", "col_k", "col_v"))]
     out = os.path.join(HERE, "tiny-raw-icl.tirs")
     tirs.write(out, {n: np.array(raw[n]) for n in keep})

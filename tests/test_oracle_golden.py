@@ -251,3 +251,18 @@ def test_digit_average_of_identical_caches_is_the_plain_stage(tiny):
     three = np.concatenate([ck, ck, ck], axis=1)
     got = oracle.embed(rm, t["x_test"], three, digits=3)
     assert np.abs(got - one).max() < 1e-5
+
+
+def test_column_fit_matches_reference(tiny):
+    """fit.rs:298-420 on the dump's normalised training rows and labels (FitOpts chunk 48, tests/reference.rs:42-72)
+    gives the dump's column-stage cache (tests/reference.rs:79-95), its training embeddings, and through the row
+    stage its training row representations."""
+    t = tiny
+    rm, fx = t["rm"], t["fx"]
+    x, y = np.array(fx["x_train"], np.float32), np.array(fx["y_train"], np.float32)
+    col_kv, tok = oracle.fit_columns(rm, x, y, 48)
+    assert np.abs(col_kv - t["col_kv"]).max() < TINY
+    emb = np.array(fx["train_emb"], np.float32)
+    assert np.abs(tok[:, rm.cls:] - emb[:, rm.cls:]).max() < TINY
+    rep = oracle.represent(rm, tok)
+    assert np.abs(rep - np.array(fx["train_rep"], np.float32)).max() < TINY
