@@ -269,7 +269,40 @@ TCU_API int tcu_regression_head_device(tcu_ctx *ctx, const float *qout, int rows
                                int na, double target_mean, double target_scale, double *mean, double *variance,
                                double *median, double *quantiles);
 
-/* ---- fitting's in-context stage on the device (src/fit.rs:577-747) ----------------------------------------- */
+/* ---- fitting on the device (src/fit.rs:285-747) ------------------------------------------------------------- */
+
+/* The accelerator hooks of fit::Attend (src/fit.rs:25-74), host buffers in and out. */
+/* fit::Attend::column_batch (src/fit.rs:54-56): feature groups tcu_fit_columns takes at once for `rows` training rows
+ * (0: not offered, as for weights without the column stage's fit tensors). */
+TCU_API int tcu_fit_column_batch(const tcu_weights *w, int rows);
+/* fit::Attend::columns (src/fit.rs:33-38, 57-59, called at 426-448): the column stage of `groups` feature groups for
+ * one label digit. cells [rows][groups][e] (through the input layer, the target's embedding added) is replaced by the
+ * cells after the stage; ind_q [column blocks][inds][e] holds each block's inducing-point queries, scaled; rec
+ * receives [groups][column blocks][2][e][inds]. */
+TCU_API int tcu_fit_columns(tcu_weights *w, float *cells, int rows, int groups, const float *ind_q, float *rec);
+/* fit::Attend::row_batch (src/fit.rs:60-62): rows tcu_fit_rows takes at once for tables of `features` features. */
+TCU_API int tcu_fit_row_batch(const tcu_weights *w, int features);
+/* fit::Attend::rows (src/fit.rs:39, 63-65, called at 493-518): the row stage of n rows, cells [n][features][e] to
+ * reps [n][d]. */
+TCU_API int tcu_fit_rows(tcu_weights *w, const float *cells, int n, int features, float *reps);
+/* Receives layer `layer`'s keys and values, [rows][d] each (host, valid during the call); nonzero stops the pass. */
+typedef int (*tcu_layer_sink)(void *user, int layer, const float *k, const float *v);
+/* fit::Attend::in_context (src/fit.rs:66-71, called at 622): the whole in-context stage of one problem. h
+ * [rows][d] (host): the row representations with the target's embedding added; scales [layers][d] (host): each
+ * layer's query scale. `sink` is called once per layer, in order. Weights made with for_fit. */
+TCU_API int tcu_fit_in_context(tcu_weights *w, const float *h, int rows, const float *scales, tcu_layer_sink sink,
+                               void *user);
+
+/* The column and row stages of fitting one member (src/fit.rs:298-540; fit_raw_async's column stage 300-481 and row
+ * stage 487-540). x: normalised training rows (device [rows][features]); y: their labels (device [rows]: class
+ * indices as floats, or standardised targets); `digits` label digits of mixed-radix `bases` (host [digits], each at
+ * least 2; unused for one digit: the label itself). Writes col_kv (device [features][digits][column blocks][2][e]
+ * [inds]: the member's `m{i}/col_kv`, src/fit.rs:230) and rep (device [rows][d]: the training rows' representations,
+ * which tcu_fit_icl_device takes per node of the class tree). `w` made with for_fit from a bundle that holds the
+ * column stage's first attention and label embedding; TCU_DECLINED otherwise. Working memory is taken and freed in
+ * the call; returns once the results are written. */
+TCU_API int tcu_fit_rows_device(tcu_weights *w, const float *x, const float *y, int rows, int features, int digits,
+                                const int32_t *bases, float *col_kv, float *rep, void *stream);
 
 /* Training rows h [rows][d] (device; consumed) with targets y [rows] (device; class index or standardised
  * value) to a resident cache: every layer's keys and values packed as `kv` in chunks of `chunk` rows

@@ -92,6 +92,9 @@ def lib():
             "or_regression_add": (None, [_fp, i, i, i, _P(d), i, d, d, _P(d), _P(d), _P(d), _P(d)]),
             "or_embed": (None, [_P(OrRowsModel), _fp, i, i, _fp, i, _fp]),
             "or_represent": (None, [_P(OrRowsModel), _fp, i, i, _fp]),
+            "or_fit_columns": (None, [_P(OrRowsModel), _fp, _fp, i, i, i, i, _P(ctypes.c_int32), _fp, _fp]),
+            "or_ind_queries": (None, [_P(OrRowsModel), i, _fp]),
+            "or_fit_cells": (None, [_P(OrRowsModel), _fp, _fp, i, i, _fp]),
             "or_threads": (i, []),
             "or_set_threads": (None, [i]),
         }
@@ -281,6 +284,26 @@ def fit_columns(rm, x, y, chunk, bases=(0,)):
     return col_kv, tok
 
 
+def ind_queries(rm, n):
+    """fit.rs:300-314: every column block's inducing-point queries (scaled) for n training rows, [blocks][inds][e]."""
+    assert rm.fit, "the weights have no column-stage fit tensors"
+    out = np.empty((rm.ncol, rm.inds, rm.e), np.float32)
+    lib().or_ind_queries(rm.ref, n, _p(out))
+    return out
+
+
+def fit_cells(rm, x, y):
+    """fit.rs:316-345 for one label digit: training cells [n][features][e] through the input layer, the label's
+    embedding added."""
+    assert rm.fit, "the weights have no column-stage fit tensors"
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.ascontiguousarray(y, dtype=np.float32)
+    n, feats = x.shape
+    out = np.empty((n, feats, rm.e), np.float32)
+    lib().or_fit_cells(rm.ref, _p(x), _p(y), n, feats, _p(out))
+    return out
+
+
 def represent(rm, tok):
     """predict.rs:356-372: tokens [n][tokens][e] to row representations [n][cls e]."""
     tok = np.array(tok, dtype=np.float32)  # a copy: consumed
@@ -353,6 +376,14 @@ def in_context(model, kv, layers, scales, rows, chunk, h, out_n, parts=1):
     out = np.empty((n, out_n), np.float32)
     lib().or_in_context(model.ref, kv, ptrs, _p(sc), rows, chunk, _p(h), n, out_n, parts, _p(out))
     return out
+
+
+def add_y(model, h, y):
+    """model.rs:185-200 add_y for the in-context stage: h [rows][d] plus the targets' embedding (a copy)."""
+    h = np.array(h, dtype=np.float32).reshape(-1, model.d)
+    y = np.ascontiguousarray(y, dtype=np.float32)
+    lib().or_add_y(model.ref, _p(y), h.shape[0], _p(h))
+    return h
 
 
 def icl_fit(model, h, y, chunk, kv):

@@ -1176,6 +1176,37 @@ static void fitcol_one(void *ctx, int g) {
     free(src), free(plain), free(sum), free(kt), free(vt), free(kv), free(t), free(hidden), free(q), free(h), free(tmp), free(sc), free(scale2);
 }
 
+/* fit.rs:300-314: every column block's inducing-point queries for n training rows, out [blocks][inds][e] */
+EXPORT void or_ind_queries(const or_rows_model *m, int n, float *out) {
+    const int e = m->e, inds = m->inds;
+    float *scale = malloc(sizeof(float) * e);
+    for (int bi = 0; bi < m->ncol; bi++) {
+        query_scale_c(&m->col1[bi], e, m->col_heads, n, scale);
+        for (int i = 0; i < inds; i++)
+            query_c(&m->col1[bi], e, m->col_heads, scale, m->col1[bi].ind + (size_t)i * e, out + ((size_t)bi * inds + i) * e);
+    }
+    free(scale);
+}
+
+/* fit.rs:333-345, 316-324 for one label digit: the training cells through the input layer with the label's embedding
+ * added, out [n][feats][e] (what the `columns` hook of fit::Attend is given) */
+EXPORT void or_fit_cells(const or_rows_model *m, const float *x, const float *y, int n, int feats, float *out) {
+    const int e = m->e;
+    float vals[8];
+    for (int r = 0; r < n; r++)
+        for (int g = 0; g < feats; g++) {
+            float *cell = out + ((size_t)r * feats + g) * e;
+            group_values(x + (size_t)r * feats, feats, g, m->group, vals);
+            int missing = 1;
+            for (int i = 0; i < m->group; i++) missing &= vals[i] == -100.0f;
+            if (missing)
+                for (int i = 0; i < e; i++) cell[i] = -100.0f;
+            else
+                linear(m->in_w, m->in_b, vals, m->group, e, cell);
+            add_y_c(m->col_y, m->max_classes, e, y[r], cell);
+        }
+}
+
 /* fit.rs:298-420 for a member's training rows: x [n][feats] (normalised), y [n] (classes, or the standardised target),
  * the rows `chunk` at a time through the inducing points' attention, `digits` label digits of mixed-radix `bases`.
  * Writes col_kv [feats][digits][blocks][2][e][inds] and the training tokens [n][cls + feats][e] (the class tokens,

@@ -59,6 +59,11 @@ class _Source(ctypes.Structure):
     _fields_ = [("user", ctypes.c_void_p), ("read_at", _READ_AT), ("size", ctypes.c_uint64)]
 
 
+# tcu_layer_sink: (user, layer, k [rows][d], v [rows][d]) -> 0 to go on
+_LayerSink = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float),
+                              ctypes.POINTER(ctypes.c_float))
+
+
 def lib():
     """The loaded C library (fails loudly if it is not built)."""
     global _lib
@@ -103,6 +108,13 @@ def lib():
         "tcu_regression_head_device": (_c_int, [_c_void, _c_void, _c_int, _c_int, _c_int, _c_void, _c_int,
                                                 ctypes.c_double, ctypes.c_double, _c_void, _c_void, _c_void, _c_void]),
         "tcu_fit_icl_device": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_int, P(_c_void)]),
+        "tcu_fit_rows_device": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_int, P(ctypes.c_int32), _c_void,
+                                         _c_void, _c_void]),
+        "tcu_fit_column_batch": (_c_int, [_c_void, _c_int]),
+        "tcu_fit_columns": (_c_int, [_c_void, _c_float_p, _c_int, _c_int, _c_float_p, _c_float_p]),
+        "tcu_fit_row_batch": (_c_int, [_c_void, _c_int]),
+        "tcu_fit_rows": (_c_int, [_c_void, _c_float_p, _c_int, _c_int, _c_float_p]),
+        "tcu_fit_in_context": (_c_int, [_c_void, _c_float_p, _c_int, _c_float_p, _LayerSink, _c_void]),
         "tcu_pack_device": (_c_int, [_c_void, _c_int, _c_int, _c_int, _c_void, _c_void]),
         "tcu_record": (_c_size, [_c_int, _c_int, _c_int]),
         "tcu_layer_rows_device": (_c_int, [_c_void, _c_int, _c_int, _c_void, _c_int, _c_int, _c_void, _c_void]),
@@ -559,6 +571,139 @@ def fit_member(weights, h, y, classes, features, col_kv, chunk=256, kv=KV_F32):
         for m in nodes:
             m.free()
         raise
+
+
+def layer_len(kv, d, rows, chunk):
+    """Bytes of one layer's stored keys and values (fit.rs:234 raw_entries): the full chunks, then the rest."""
+    chunk = max(int(chunk), 8)
+    return (rows // chunk) * record(kv, d, chunk) + (record(kv, d, rows % chunk) if rows % chunk else 0)
+
+
+def raw_entries(weights, prefix, rows, features, chunk, kv, plan):
+    """fit::raw_entries (src/fit.rs:224-241): the tensors a member's fit fills, as (name, dtype, dims)."""
+    s, rs = weights.shape, weights.rows_shape
+    chunk = max(int(chunk), 8)
+    v = [(prefix + "meta", "int32", [7]), (prefix + "tree", "int32", [len(plan.tree(rows))]),
+         (prefix + "col_kv", "float32", [features, len(plan.bases), rs["col_blocks"], 2, rs["e"], rs["inds"]])]
+    for i, nd in enumerate(plan.nodes):
+        nr = rows if nd.rows is None else len(nd.rows)
+        v.append((prefix + f"n{i}_scale", "float32", [s["layers"], s["d"]]))
+        for l in range(s["layers"]):
+            v.append((prefix + f"n{i}_kv{l}", "uint8", [layer_len(kv, s["d"], nr, chunk)]))
+    return v
+
+
+def fit_raw(weights, x, y, classes, chunk=256, kv=KV_F32, prefix=""):
+    """fit_raw_async (src/fit.rs:285-752) for one member, every stage on the device: normalised training rows x
+    [rows][features] and labels y (class indices as floats, or standardised targets; host) through the column stage
+    (fit.rs:298-481), the row stage (487-540) and, per node of fit::Plan's class tree (159-221), the in-context stage
+    (577-747). `classes` is what prediction returns (classes, or the model's quantile outputs).
+
+    Returns (member, entries): the fitted member resident on the device (VramMember), and the tensors raw_entries
+    names with their contents, in that order, ready for tirs.write (with the weights, or on their own)."""
+    import torch  # device buffers for the fit
+
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.ascontiguousarray(y, dtype=np.float32)
+    rows, features = x.shape
+    s, rs = weights.shape, weights.rows_shape
+    chunk = max(int(chunk), 8)
+    plan = Plan.new(s["max_classes"], y, classes)
+    D = len(plan.bases)
+    bases = np.ascontiguousarray(plan.bases, dtype=np.int32)
+    xd, yd = torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()
+    ck = torch.empty((features, D, rs["col_blocks"], 2, rs["e"], rs["inds"]), dtype=torch.float32, device="cuda")
+    rep = torch.empty((rows, s["d"]), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    weights.gpu.check(lib().tcu_fit_rows_device(weights._h, xd.data_ptr(), yd.data_ptr(), rows, features, D,
+                                                bases.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ck.data_ptr(),
+                                                rep.data_ptr(), None))
+    nodes = []
+    try:
+        for nd in plan.nodes:
+            if nd.rows is None:
+                hd = rep if len(plan.nodes) == 1 else rep.clone()
+            else:
+                hd = rep[torch.as_tensor(np.asarray(nd.rows, dtype=np.int64), device="cuda")].contiguous()
+            yn = torch.from_numpy(np.ascontiguousarray(nd.y, dtype=np.float32)).cuda()
+            torch.cuda.synchronize()
+            nodes.append(fit_icl(weights, hd.data_ptr(), yn.data_ptr(), hd.shape[0], chunk, kv))
+            torch.cuda.synchronize()
+        col_kv = ck.cpu().numpy()
+        weights.gpu.check(lib().tcu_model_set_columns(nodes[0]._h, features, D))
+        nodes[0].put_col_kv(col_kv)
+        tree = plan.tree(rows)
+        member = VramMember.from_nodes(nodes, tree, classes)
+    except Exception:
+        for m in nodes:
+            m.free()
+        raise
+    out = {prefix + "meta": np.array([rows, features, classes, chunk, kv, D, len(plan.nodes)], np.int32),
+           prefix + "tree": tree, prefix + "col_kv": col_kv}
+    for i, nd in enumerate(plan.nodes):
+        nr = rows if nd.rows is None else len(nd.rows)
+        out[prefix + f"n{i}_scale"] = nodes[i].scales()
+        for l in range(s["layers"]):
+            out[prefix + f"n{i}_kv{l}"] = nodes[i].layer_bytes(l, layer_len(kv, s["d"], nr, chunk))
+    return member, out
+
+
+class CudaFit:
+    """fit::Attend on the device (src/fit.rs:25-74; the reference's card implements it at src/gpu.rs:1471-1716): the
+    column stage, the row stage and the in-context stage of fitting, offered to a CPU fitting pass, host arrays in and
+    out. Weights made with for_fit."""
+
+    def __init__(self, weights):
+        self.weights = weights
+
+    def column_batch(self, rows):
+        """Feature groups `columns` takes at once (0: not offered)."""
+        return int(lib().tcu_fit_column_batch(self.weights._h, rows))
+
+    def columns(self, cells, ind_q):
+        """cells [rows][groups][e] (replaced in place by the cells after the stage; through the input layer, the
+        target's embedding added), ind_q [blocks][inds][e]: returns rec [groups][blocks][2][e][inds]."""
+        assert cells.dtype == np.float32 and cells.flags.c_contiguous
+        rows, groups, e = cells.shape
+        rs = self.weights.rows_shape
+        q = np.ascontiguousarray(ind_q, dtype=np.float32)
+        rec = np.empty((groups, rs["col_blocks"], 2, e, rs["inds"]), np.float32)
+        self.weights.gpu.check(lib().tcu_fit_columns(self.weights._h, _f32p(cells), rows, groups, _f32p(q), _f32p(rec)))
+        return rec
+
+    def row_batch(self, features):
+        return int(lib().tcu_fit_row_batch(self.weights._h, features))
+
+    def rows(self, cells):
+        """cells [n][features][e] to the rows' representations [n][d]."""
+        c = np.ascontiguousarray(cells, dtype=np.float32)
+        n, features, _ = c.shape
+        reps = np.empty((n, self.weights.shape["d"]), np.float32)
+        self.weights.gpu.check(lib().tcu_fit_rows(self.weights._h, _f32p(c), n, features, _f32p(reps)))
+        return reps
+
+    def in_context(self, h, scales, sink):
+        """h [rows][d] (target's embedding added), scales [layers][d]; sink(layer, k, v) gets each layer's keys and
+        values ([rows][d] arrays, copies) in order. Returns True (the stage was done)."""
+        h = np.ascontiguousarray(h, dtype=np.float32)
+        sc = np.ascontiguousarray(scales, dtype=np.float32)
+        rows, d = h.shape
+        failed = []
+
+        def cb(_user, layer, k, v):
+            try:
+                sink(layer, np.ctypeslib.as_array(k, (rows, d)).copy(), np.ctypeslib.as_array(v, (rows, d)).copy())
+                return 0
+            except Exception as e:  # carried back to the caller after the pass stops
+                failed.append(e)
+                return 1
+
+        fn = _LayerSink(cb)
+        r = lib().tcu_fit_in_context(self.weights._h, _f32p(h), rows, _f32p(sc), fn, None)
+        if failed:
+            raise failed[0]
+        self.weights.gpu.check(r)
+        return True
 
 
 def _b(text):

@@ -12,7 +12,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libtabicl_b200.so")
-SOURCES = ["kernels.cu", "attend_tc.cu", "gemm_tc.cu", "stage_rows.cu", "rows.cu", "qmlp_tc.cu", "tree.cu", "peer.cu", "engine.cpp", "tier.cpp", "tirs.cpp", "noalloc.cu"]
+SOURCES = ["kernels.cu", "attend_tc.cu", "gemm_tc.cu", "stage_rows.cu", "rows.cu", "qmlp_tc.cu", "tree.cu", "peer.cu", "fitcol.cu", "engine.cpp", "tier.cpp", "tirs.cpp", "noalloc.cu"]
 HEADERS = ["device.cuh", "kernels.cuh", "tirs.hpp", "tc.cuh", "stage_common.cuh", "engine.hpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [

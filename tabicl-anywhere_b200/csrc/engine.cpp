@@ -396,6 +396,42 @@ static float h_erf1(float x) {
 }
 static float h_gelu(float v) { return 0.5f * v * (1.0f + h_erf1(v * 0.70710678118654752440f)); }
 
+static float h_tanh1(float x) {  // kern.rs:292-297
+    const float e = h_exp1(2.0f * (x < -10.0f ? -10.0f : (x > 10.0f ? 10.0f : x)));
+    return (e - 1.0f) / (e + 1.0f);
+}
+
+// kern.rs:42-61 dot: four running sums of fused products, then the remainder
+static float h_dot(const float *a, const float *b, int n) {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int i = 0;
+    for (; i + 4 <= n; i += 4) {
+        s0 = std::fma(a[i], b[i], s0);
+        s1 = std::fma(a[i + 1], b[i + 1], s1);
+        s2 = std::fma(a[i + 2], b[i + 2], s2);
+        s3 = std::fma(a[i + 3], b[i + 3], s3);
+    }
+    float s = (s0 + s1) + (s2 + s3);
+    for (; i < n; i++) s += a[i] * b[i];
+    return s;
+}
+
+// kern.rs:154-159 linear, y = w x + b with w [out][in]
+static void h_linear(const float *w, const float *b, const float *x, int in, int out, float *y) {
+    for (int o = 0; o < out; o++) y[o] = h_dot(w + (size_t)o * in, x, in) + (b ? b[o] : 0.f);
+}
+
+// kern.rs:357-376 layer norm: eps 1e-5, biased variance
+static void h_layer_norm(const float *x, const float *w, const float *b, int n, float *y) {
+    float s = 0.f;
+    for (int i = 0; i < n; i++) s += x[i];
+    const float mean = s / (float)n;
+    float q = 0.f;
+    for (int i = 0; i < n; i++) q = std::fma(x[i] - mean, x[i] - mean, q);
+    const float inv = 1.0f / std::sqrt(q / (float)n + 1e-5f);
+    for (int i = 0; i < n; i++) y[i] = (x[i] - mean) * inv * w[i] + b[i];
+}
+
 static std::vector<float> query_scale(const tcu_weights *w, int l, int n) {
     const int d = w->shape.d, hd = d / w->shape.heads;
     const auto &b0w = w->sb0w[l], &b0b = w->sb0b[l], &b2w = w->sb2w[l], &b2b = w->sb2b[l];
@@ -1311,11 +1347,15 @@ static void stage_replay(tcu_ctx *ctx, tcu_model *m, int R, int out_n, cudaStrea
 
 // ---- the column and row stages (predict.rs:282-372) -------------------------------------------------------------
 
-static void check_rows_ready(const tcu_model *m) {
-    const RowsWeights &rw = m->w->rows;
+static void check_rows_weights(const tcu_weights *w) {
+    const RowsWeights &rw = w->rows;
     if (!rw.on) fail(TCU_DECLINED, "rows: the weights have no column and row stages");
+    if (rw.shape.cls * rw.shape.e != w->shape.d) fail(TCU_ERR_FORMAT, "rows: class tokens times width differ from the in-context width");
+}
+
+static void check_rows_ready(const tcu_model *m) {
+    check_rows_weights(m->w);
     if (!m->col_kv.p) fail(TCU_DECLINED, "rows: the cache has no column-stage keys and values (col_kv was never put)");
-    if (rw.shape.cls * rw.shape.e != m->w->shape.d) fail(TCU_ERR_FORMAT, "rows: class tokens times width differ from the in-context width");
 }
 
 // Grow the linear layers' scratch (row statistics, split rows) for M rows of width up to K; graphs that used the old
@@ -1324,6 +1364,22 @@ static void ensure_linear(tcu_model *m, size_t M, int K) {
     bool moved = m->stats.ensure(sizeof(float) * 4 * M);
     moved |= m->atiles.ensure(tc_split_bytes((int)M, K));
     if (moved) drop_graphs(m);
+}
+
+// nn.rs:289-302 cached_block for every cell of X [R * F][e] (in place): the second attention of a column block against
+// group g's inducing points (keys and values at kv + g * gstride), then the block's feed-forward. Q, A [R * F][e] and
+// H [R * F][ff] are scratch.
+static void cached_block(tcu_ctx *ctx, tcu_model *m, const CBlockPtrs &B, float *X, float *Q, float *A, float *H, int R,
+                         int F, const float *kv, size_t gstride, cudaStream_t s) {
+    const auto &rs = m->w->rows.shape;
+    const int e = rs.e, ff = B.ff, M = R * F;
+    const float scale = 1.0f / std::sqrt((float)(e / rs.col_heads));
+    linear(ctx, m, X, e, M, e, B.n1w, B.n1b, B.inw, B.inb, e, Q, e, 0, 0, s, B.tin);
+    Launch{ctx, s}(launch_col_attend(Q, R, F, kv, gstride, e, rs.inds, rs.col_heads, scale, A, s, &ctx->launches),
+                   "column attention");
+    linear(ctx, m, A, e, M, e, nullptr, nullptr, B.ow, B.ob, e, X, e, 0, 1, s, B.to);
+    linear(ctx, m, X, e, M, e, B.n2w, B.n2b, B.w1, B.b1, ff, H, ff, 1, 0, s, B.t1);
+    linear(ctx, m, H, ff, M, ff, nullptr, nullptr, B.w2, B.b2, e, X, e, 0, 1, s, B.t2);
 }
 
 // predict.rs:282-353 embed: normalised rows x (device [R][F]) to tokens tok (device [R][cls + F][e]). Every cell
@@ -1342,19 +1398,10 @@ static void embed(tcu_ctx *ctx, tcu_model *m, const float *x, int R, float *tok,
     float *X = m->cx.as<float>(), *Q = m->cq.as<float>(), *A = m->catt.as<float>(), *H = m->cmid.as<float>();
     Launch ck{ctx, s};
     ck(launch_col_cells(x, R, F, rs.group, rw.in_w, rw.in_b, e, D > 1 ? m->cx0.as<float>() : X, s, &ctx->launches), "cells");
-    const float scale = 1.0f / std::sqrt((float)(e / rs.col_heads));
     for (int dg = 0; dg < D; dg++) {
         if (D > 1) CU(cudaMemcpyAsync(X, m->cx0.p, sizeof(float) * M * e, cudaMemcpyDeviceToDevice, s));
-        for (int b = 0; b < nb; b++) {
-            const CBlockPtrs &B = rw.col[b];
-            linear(ctx, m, X, e, (int)M, e, B.n1w, B.n1b, B.inw, B.inb, e, Q, e, 0, 0, s, B.tin);
-            ck(launch_col_attend(Q, R, F, m->col_kv.as<float>() + (dg * nb + b) * per, gstride, e, inds, rs.col_heads, scale,
-                                 A, s, &ctx->launches),
-               "column attention");
-            linear(ctx, m, A, e, (int)M, e, nullptr, nullptr, B.ow, B.ob, e, X, e, 0, 1, s, B.to);
-            linear(ctx, m, X, e, (int)M, e, B.n2w, B.n2b, B.w1, B.b1, ff, H, ff, 1, 0, s, B.t1);
-            linear(ctx, m, H, ff, (int)M, ff, nullptr, nullptr, B.w2, B.b2, e, X, e, 0, 1, s, B.t2);
-        }
+        for (int b = 0; b < nb; b++)
+            cached_block(ctx, m, rw.col[b], X, Q, A, H, R, F, m->col_kv.as<float>() + (dg * nb + b) * per, gstride, s);
         if (D > 1) ck(launch_scale_add(m->csum.as<float>(), X, M * e, 1.0f, dg > 0, s, &ctx->launches), "digit sum");
     }
     if (D > 1) ck(launch_divide(X, m->csum.as<float>(), M * e, (float)D, s, &ctx->launches), "digit average");
@@ -1364,7 +1411,7 @@ static void embed(tcu_ctx *ctx, tcu_model *m, const float *x, int R, float *tok,
 // predict.rs:356-372 represent: tokens (device [R][T][e], consumed) to row representations rep (device [R][cls e]):
 // the row blocks (nn.rs:357-419; the last one only for the class tokens), then the class tokens' LayerNorm.
 static void represent(tcu_ctx *ctx, tcu_model *m, float *tok, int R, float *rep, cudaStream_t s) {
-    check_rows_ready(m);
+    check_rows_weights(m->w);
     const RowsWeights &rw = m->w->rows;
     const auto &rs = rw.shape;
     const int e = rs.e, T = rs.cls + m->features, heads = rs.row_heads, half = e / heads / 2, ff = rs.row_ff;
@@ -1418,6 +1465,149 @@ static void rows_stage(tcu_ctx *ctx, tcu_model *m, const float *x, int R, int ou
     embed(ctx, m, x, R, m->ctok.as<float>(), s);
     represent(ctx, m, m->ctok.as<float>(), R, m->h.as<float>(), s);
     stage_replay(ctx, m, R, out_n, s);
+}
+
+// ---- the column and row stages of fitting (fit.rs:298-540) ---------------------------------------------------------
+
+// fit.rs:300-314: the inducing points' queries of a column block's first attention for n training rows, [inds][e]:
+// nn.rs:130-152 query (LayerNorm, the query rows of in_proj, the per-head query MLP) times nn.rs:97-107 query_scale.
+static std::vector<float> ind_queries(const Isab1 &a, const tcu_rows_shape &rs, int n) {
+    const int e = rs.e, heads = rs.col_heads, hd = e / heads, hid = a.hid;
+    std::vector<float> scale(e), h(hid), t(e), mm(hd), out((size_t)rs.inds * e);
+    const float logn = std::log((float)(n > 1 ? n : 1)), inv = 1.0f / std::sqrt((float)hd);
+    for (int i = 0; i < hid; i++) h[i] = h_gelu(a.sb0w[i] * logn + a.sb0b[i]);
+    h_linear(a.sb2w.data(), a.sb2b.data(), h.data(), hid, e, scale.data());
+    for (int i = 0; i < e; i++) scale[i] *= inv;
+    for (int i = 0; i < rs.inds; i++) {
+        float *q = out.data() + (size_t)i * e;
+        h_layer_norm(a.ind_h.data() + (size_t)i * e, a.n1w.data(), a.n1b.data(), e, t.data());
+        h_linear(a.wq.data(), a.bq.data(), t.data(), e, e, q);
+        for (int hh = 0; hh < heads; hh++) {
+            float *qh = q + hh * hd;
+            h_linear(a.q0w.data(), a.q0b.data(), qh, hd, hid, h.data());
+            for (int j = 0; j < hid; j++) h[j] = h_gelu(h[j]);
+            h_linear(a.q2w.data(), a.q2b.data(), h.data(), hid, hd, mm.data());
+            for (int j = 0; j < hd; j++) qh[j] *= scale[hh * hd + j] * (1.0f + h_tanh1(mm[j]));
+        }
+    }
+    return out;
+}
+
+// fit.rs:326-420 col_one for F feature groups at once (the `columns` hook of fit::Attend, fit.rs:33-38): the training
+// cells X (device [n * F][e], cell (r, g) at row r * F + g, through the input layer with the label's embedding added;
+// replaced by the cells after the stage) through every column block. Per block: the cells' keys and values for the
+// first attention, the inducing points' attention over every group's cells (queries iq, device [blocks][inds][e],
+// scaled), its out-projection with the inducing points as residual and the feed-forward, the result's keys and values
+// for the second attention (block b's cache of group g at col_kv + g * gstride + off + b * 2 e inds), then every cell
+// through the second attention against them. The reference walks the cells `chunk` rows at a time only to bound its
+// memory; the attention here takes every row of a group at once, split for parallelism: the same up to rounding.
+static void column_blocks(tcu_ctx *ctx, tcu_model *m, float *X, int n, int F, const float *iq, float *col_kv,
+                          size_t gstride, size_t off, cudaStream_t s) {
+    const RowsWeights &rw = m->w->rows;
+    const auto &rs = rw.shape;
+    const int e = rs.e, nb = rs.col_blocks, inds = rs.inds, heads = rs.col_heads, hd = e / heads, ff = rs.col_ff;
+    const size_t M = (size_t)n * F, per = (size_t)2 * e * inds, I = (size_t)F * inds;
+    if (M > (size_t)INT32_MAX / 4 || I > (size_t)INT32_MAX / 4) fail(TCU_ERR_ARG, "fit: too many training cells for one call");
+    const int splits = ind_attend_splits(n, F, heads, inds);
+    m->cq.ensure(sizeof(float) * M * 2 * e), m->catt.ensure(sizeof(float) * M * e), m->cmid.ensure(sizeof(float) * M * ff);
+    ensure_linear(m, std::max(M, I), std::max(e, ff));
+    DevBuf pms, pacc, hid, hmid, kv2;
+    pms.ensure(sizeof(float) * 2 * (size_t)F * heads * splits * inds);
+    pacc.ensure(sizeof(float) * (size_t)F * heads * splits * inds * hd);
+    hid.ensure(sizeof(float) * I * e), hmid.ensure(sizeof(float) * I * std::max(e, ff));
+    kv2.ensure(sizeof(float) * I * 2 * e);
+    float *KV = m->cq.as<float>(), *A = m->catt.as<float>(), *H = m->cmid.as<float>();
+    float *hb = hid.as<float>(), *hm = hmid.as<float>();
+    Launch ck{ctx, s};
+    for (int b = 0; b < nb; b++) {
+        const Isab1 &a1 = rw.col1[b];
+        // the cells' keys and values for the first attention [M][2e]
+        linear(ctx, m, X, e, (int)M, e, a1.b.n1w, a1.b.n1b, a1.b.inw, a1.b.inb, 2 * e, KV, 2 * e, 0, 0, s, a1.b.tin);
+        // the attention [F * inds][e] goes into the feed-forward's buffer, which it leaves before the feed-forward
+        ck(launch_ind_attend(iq + (size_t)b * inds * e, KV, n, F, e, inds, heads, splits, pms.as<float>(), pacc.as<float>(),
+                             hm, s, &ctx->launches),
+           "inducing attention");
+        ck(launch_repeat(hb, a1.ind, (size_t)inds * e, F, s, &ctx->launches), "inducing residual");
+        linear(ctx, m, hm, e, (int)I, e, nullptr, nullptr, a1.b.ow, a1.b.ob, e, hb, e, 0, 1, s, a1.b.to);
+        linear(ctx, m, hb, e, (int)I, e, a1.b.n2w, a1.b.n2b, a1.b.w1, a1.b.b1, a1.b.ff, hm, a1.b.ff, 1, 0, s, a1.b.t1);
+        linear(ctx, m, hm, a1.b.ff, (int)I, a1.b.ff, nullptr, nullptr, a1.b.w2, a1.b.b2, e, hb, e, 0, 1, s, a1.b.t2);
+        // their keys and values for the second attention: the cache prediction reads (fit.rs:392-404)
+        const CBlockPtrs &B = rw.col[b];
+        linear(ctx, m, hb, e, (int)I, e, B.n1w, B.n1b, a1.kv2w, a1.kv2b, 2 * e, kv2.as<float>(), 2 * e, 0, 0, s, a1.tkv2);
+        ck(launch_col_kv_scatter(kv2.as<float>(), F, e, inds, gstride, off + b * per, col_kv, s, &ctx->launches),
+           "cache scatter");
+        cached_block(ctx, m, B, X, KV, A, H, n, F, col_kv + off + b * per, gstride, s);
+    }
+    // the locals above are freed on return: finish with them first
+    CU(cudaStreamSynchronize(s));
+}
+
+static void check_fit_weights(const tcu_weights *w) {
+    check_rows_weights(w);
+    if (!w->rows.fit) fail(TCU_DECLINED, "fit: the weights were not made for fitting, or have no column-stage fit tensors");
+}
+
+// fit.rs:300-314: every column block's inducing-point queries for n training rows, on the device [blocks][inds][e].
+static void put_ind_queries(const tcu_weights *w, int n, DevBuf &iq, cudaStream_t s) {
+    const RowsWeights &rw = w->rows;
+    const auto &rs = rw.shape;
+    const size_t one = (size_t)rs.inds * rs.e;
+    std::vector<float> q_all(one * rs.col_blocks);
+    for (int b = 0; b < rs.col_blocks; b++) {
+        auto q = ind_queries(rw.col1[b], rs, n);
+        std::copy(q.begin(), q.end(), q_all.begin() + b * one);
+    }
+    iq.ensure(sizeof(float) * q_all.size());
+    CU(cudaMemcpyAsync(iq.p, q_all.data(), sizeof(float) * q_all.size(), cudaMemcpyHostToDevice, s));
+    CU(cudaStreamSynchronize(s));
+}
+
+// fit.rs:298-481 on the device: normalised training rows x (device [n][F]) and labels y (device [n]) to the member's
+// column cache col_kv (device [F][D][blocks][2][e][inds]) and the training tokens tok (device [n][cls + F][e]): the
+// cells through the input layer, then per label digit (fit.rs:316-324: digit ((int)y / divisor) % base of the class
+// label) the label's embedding and the column blocks; with several digits the cells' average over them.
+static void fit_columns(tcu_ctx *ctx, tcu_model *m, const float *x, const float *y, int n, int F, int D,
+                        const int32_t *bases, float *col_kv, float *tok, cudaStream_t s) {
+    const tcu_weights *w = m->w;
+    check_fit_weights(w);
+    const RowsWeights &rw = w->rows;
+    const auto &rs = rw.shape;
+    const int e = rs.e, nb = rs.col_blocks, inds = rs.inds;
+    if (n < 1 || F < 1 || D < 1) fail(TCU_ERR_ARG, "fit: rows, features and digits must be positive");
+    for (int dg = 0; D > 1 && dg < D; dg++)
+        if (bases[dg] < 2) fail(TCU_ERR_ARG, "fit: every digit's base must be at least 2");
+    const size_t M = (size_t)n * F, per = (size_t)2 * e * inds, gstride = (size_t)D * nb * per;
+    m->cx.ensure(sizeof(float) * M * e);
+    if (D > 1) m->cx0.ensure(sizeof(float) * M * e), m->csum.ensure(sizeof(float) * M * e);
+    DevBuf iq;
+    put_ind_queries(w, n, iq, s);
+    float *X = m->cx.as<float>();
+    Launch ck{ctx, s};
+    ck(launch_col_cells(x, n, F, rs.group, rw.in_w, rw.in_b, e, D > 1 ? m->cx0.as<float>() : X, s, &ctx->launches), "cells");
+    for (int dg = 0; dg < D; dg++) {
+        if (D > 1) CU(cudaMemcpyAsync(X, m->cx0.p, sizeof(float) * M * e, cudaMemcpyDeviceToDevice, s));
+        int divisor = 1;
+        for (int b = dg + 1; b < D; b++) divisor *= bases[b];
+        ck(launch_col_add_y(X, y, n, F, e, rw.max_classes, rw.col_y, divisor, D > 1 ? bases[dg] : 0, s, &ctx->launches),
+           "cell labels");
+        column_blocks(ctx, m, X, n, F, iq.as<float>(), col_kv, gstride, (size_t)dg * nb * per, s);
+        if (D > 1) ck(launch_scale_add(m->csum.as<float>(), X, M * e, 1.0f, dg > 0, s, &ctx->launches), "digit sum");
+    }
+    if (D > 1) ck(launch_divide(X, m->csum.as<float>(), M * e, (float)D, s, &ctx->launches), "digit average");
+    ck(launch_tokens(X, rw.cls_tokens, n, F, rs.cls, e, tok, s, &ctx->launches), "tokens");
+}
+
+// fit.rs:487-540: the training tokens (device [n][cls + F][e], consumed) through the row stage to the training rows'
+// representations rep (device [n][d]), a block of rows at a time to bound the working memory.
+static void fit_rows(tcu_ctx *ctx, tcu_model *m, float *tok, int n, int F, float *rep, cudaStream_t s) {
+    const auto &rs = m->w->rows.shape;
+    const size_t T = (size_t)rs.cls + F;
+    const int block = (int)std::max<size_t>(256, std::min<size_t>(n, (size_t)(1u << 22) / T));
+    for (int r0 = 0; r0 < n; r0 += block) {
+        const int rb = std::min(block, n - r0);
+        represent(ctx, m, tok + (size_t)r0 * T * rs.e, rb, rep + (size_t)r0 * m->w->shape.d, s);
+    }
+    CU(cudaStreamSynchronize(s));
 }
 
 // ---- a member's problems and the class tree (predict.rs:638-699) -------------------------------------------------
@@ -1870,8 +2060,15 @@ static void stage_sharded(tcu_ctx *ctx, tcu_model *m, tcu_comm *c, int R, int ou
     mark(7);
 }
 
-// fit.rs:577-747 in-memory path on the device
-static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, int chunk, int kv) {
+// fit.rs:577-747 in-memory path on the device. With `scales_in` (host [layers][d]) those query scales are used instead
+// of the ones worked out for `rows`; without y, h already carries the target's embedding; with `sink`, every layer's
+// keys and values ([rows][d] each, host) are handed to it in layer order (the in_context hook of fit::Attend).
+struct LayerSink {
+    tcu_layer_sink fn = nullptr;
+    void *user = nullptr;
+};
+static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, int chunk, int kv,
+                          const float *scales_in = nullptr, LayerSink sink = LayerSink()) {
     tcu_ctx *ctx = w->ctx;
     if (!w->for_fit || !w->ready) fail(TCU_ERR_STATE, "fit: weights must be made with for_fit and be ready");
     if (chunk < 8) chunk = 8;  // fit.rs:226
@@ -1897,16 +2094,28 @@ static tcu_model *fit_icl(tcu_weights *w, float *h, const float *y, int rows, in
         items = fit_items.as<int2>(), nitems = (int)it.size();
     }
     Launch ck{ctx, s};
-    ck(launch_add_y(h, y, rows, d, sh.max_classes, w->icl_y, s, &ctx->launches), "add_y");
+    if (y) ck(launch_add_y(h, y, rows, d, sh.max_classes, w->icl_y, s, &ctx->launches), "add_y");
+    DevBuf kvr;
+    std::vector<float> hk, hv;
+    if (sink.fn) kvr.ensure(sizeof(float) * (size_t)rows * 2 * d), hk.resize((size_t)rows * d), hv.resize((size_t)rows * d);
     // the float view of a layer (for the training rows' own attention) has its own items/tiles: same chunking
     std::vector<float> scales((size_t)L * d);
     for (int l = 0; l < L; l++) {
         const LayerPtrs &p = w->layer[l];
-        auto sc = query_scale(w, l, rows);
+        auto sc = scales_in ? std::vector<float>(scales_in + (size_t)l * d, scales_in + (size_t)(l + 1) * d) : query_scale(w, l, rows);
         std::memcpy(scales.data() + (size_t)l * d, sc.data(), sizeof(float) * d);
         CU(cudaMemcpyAsync(m->scales.as<float>() + (size_t)l * d, sc.data(), sizeof(float) * d, cudaMemcpyHostToDevice, s));
         // keys and values, coordinate-major: kvT[j][r] = Wkv[j] . LN1(h_r) + bkv[j] (fit.rs:633-647)
         linear(ctx, m.get(), h, d, rows, d, p.n1w, p.n1b, p.wkv, p.bkv, 2 * d, kvT.as<float>(), rows, 0, 0, s, p.tkv, 1);
+        if (sink.fn) {
+            // the same keys and values row by row for the caller: [rows][2d], keys then values of each row
+            linear(ctx, m.get(), h, d, rows, d, p.n1w, p.n1b, p.wkv, p.bkv, 2 * d, kvr.as<float>(), 2 * d, 0, 0, s, p.tkv);
+            const size_t row = sizeof(float) * d;
+            CU(cudaMemcpy2DAsync(hk.data(), row, kvr.p, 2 * row, row, rows, cudaMemcpyDeviceToHost, s));
+            CU(cudaMemcpy2DAsync(hv.data(), row, kvr.as<float>() + d, 2 * row, row, rows, cudaMemcpyDeviceToHost, s));
+            CU(cudaStreamSynchronize(s));
+            if (sink.fn(sink.user, l, hk.data(), hv.data()) != 0) fail(TCU_ERR_ARG, "fit_in_context: the layer sink failed");
+        }
         ck(launch_pack(kvT.as<float>(), rows, d, rows, chunk, kv, m->layers.as<uint8_t>() + m->layer_stride * l, s, &ctx->launches), "pack");
         m->have_layer[l] = true;
         if (l + 1 == L) break;  // fit.rs:664-666
@@ -2515,6 +2724,120 @@ int tcu_fit_icl_device(tcu_weights *w, float *h, const float *y, int rows, int c
     return guarded(w->ctx, [&]() -> int {
         if (!h || !y || !out || rows < 1 || kv < 0 || kv > 2) fail(TCU_ERR_ARG, "fit_icl: bad argument");
         *out = fit_icl(w, h, y, rows, chunk, kv);
+        return TCU_OK;
+    });
+}
+
+int tcu_fit_rows_device(tcu_weights *w, const float *x, const float *y, int rows, int features, int digits,
+                        const int32_t *bases, float *col_kv, float *rep, void *stream) {
+    if (!w) return TCU_ERR_ARG;
+    tcu_ctx *ctx = w->ctx;
+    return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
+        if (!x || !y || !col_kv || !rep || rows < 1 || features < 1 || digits < 1 || (digits > 1 && !bases))
+            fail(TCU_ERR_ARG, "fit_rows: bad argument");
+        if (!w->ready) fail(TCU_ERR_STATE, "fit_rows: weights not ready");
+        const cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+        // working memory only (no cache): freed on return
+        std::unique_ptr<tcu_model> sc(new tcu_model());
+        sc->w = w, sc->features = features, sc->digits = digits;
+        const auto &rs = w->rows.shape;
+        DevBuf tok;
+        tok.ensure(sizeof(float) * (size_t)rows * (rs.cls + features) * rs.e);
+        fit_columns(ctx, sc.get(), x, y, rows, features, digits, bases, col_kv, tok.as<float>(), s);
+        fit_rows(ctx, sc.get(), tok.as<float>(), rows, features, rep, s);
+        check_device_error(ctx);
+        return TCU_OK;
+    });
+}
+
+// Working memory the fit's column and row stages may take per call (the hooks size their batches by it).
+static constexpr size_t FIT_WORK_BYTES = (size_t)16 << 30;
+
+int tcu_fit_column_batch(const tcu_weights *w, int rows) {
+    if (!w || rows < 1 || !w->ready || !w->rows.on || !w->rows.fit) return 0;
+    const auto &rs = w->rows.shape;
+    const size_t wide = std::max(rs.e, rs.col_ff);
+    // per cell: the cells, their keys and values, attention, hidden units, split rows (two f16 halves)
+    const size_t per_cell = sizeof(float) * (4 * (size_t)rs.e + rs.col_ff + wide);
+    return (int)std::max<size_t>(1, std::min<size_t>(1 << 20, FIT_WORK_BYTES / per_cell / (size_t)rows));
+}
+
+int tcu_fit_columns(tcu_weights *w, float *cells, int rows, int groups, const float *ind_q, float *rec) {
+    if (!w) return TCU_ERR_ARG;
+    tcu_ctx *ctx = w->ctx;
+    return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
+        if (!cells || !ind_q || !rec || rows < 1 || groups < 1) fail(TCU_ERR_ARG, "fit_columns: bad argument");
+        if (!w->ready) fail(TCU_ERR_STATE, "fit_columns: weights not ready");
+        check_fit_weights(w);
+        const auto &rs = w->rows.shape;
+        const cudaStream_t s = ctx->stream;
+        const size_t M = (size_t)rows * groups, per = (size_t)2 * rs.e * rs.inds, nq = (size_t)rs.col_blocks * rs.inds * rs.e;
+        std::unique_ptr<tcu_model> sc(new tcu_model());
+        sc->w = w, sc->features = groups;
+        DevBuf iq, out;
+        sc->cx.ensure(sizeof(float) * M * rs.e), iq.ensure(sizeof(float) * nq);
+        out.ensure(sizeof(float) * groups * rs.col_blocks * per);
+        CU(cudaMemcpyAsync(sc->cx.p, cells, sizeof(float) * M * rs.e, cudaMemcpyHostToDevice, s));
+        CU(cudaMemcpyAsync(iq.p, ind_q, sizeof(float) * nq, cudaMemcpyHostToDevice, s));
+        column_blocks(ctx, sc.get(), sc->cx.as<float>(), rows, groups, iq.as<float>(), out.as<float>(), rs.col_blocks * per, 0, s);
+        CU(cudaMemcpyAsync(cells, sc->cx.p, sizeof(float) * M * rs.e, cudaMemcpyDeviceToHost, s));
+        CU(cudaMemcpyAsync(rec, out.p, out.bytes, cudaMemcpyDeviceToHost, s));
+        CU(cudaStreamSynchronize(s));
+        check_device_error(ctx);
+        return TCU_OK;
+    });
+}
+
+int tcu_fit_row_batch(const tcu_weights *w, int features) {
+    if (!w || features < 1 || !w->ready || !w->rows.on) return 0;
+    const auto &rs = w->rows.shape;
+    const size_t T = (size_t)rs.cls + features, wide = std::max(rs.e, rs.row_ff);
+    // per row: its tokens, their projections, attention, new tokens, hidden units, split rows
+    const size_t per_row = sizeof(float) * T * (6 * (size_t)rs.e + rs.row_ff + wide);
+    return (int)std::max<size_t>(1, std::min<size_t>(1 << 16, FIT_WORK_BYTES / per_row));
+}
+
+int tcu_fit_rows(tcu_weights *w, const float *cells, int n, int features, float *reps) {
+    if (!w) return TCU_ERR_ARG;
+    tcu_ctx *ctx = w->ctx;
+    return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
+        if (!cells || !reps || n < 1 || features < 1) fail(TCU_ERR_ARG, "fit_rows: bad argument");
+        if (!w->ready) fail(TCU_ERR_STATE, "fit_rows: weights not ready");
+        check_rows_weights(w);
+        const auto &rs = w->rows.shape;
+        const cudaStream_t s = ctx->stream;
+        const size_t M = (size_t)n * features, d = w->shape.d;
+        std::unique_ptr<tcu_model> sc(new tcu_model());
+        sc->w = w, sc->features = features;
+        DevBuf x, tok, rep;
+        x.ensure(sizeof(float) * M * rs.e), tok.ensure(sizeof(float) * (size_t)n * (rs.cls + features) * rs.e);
+        rep.ensure(sizeof(float) * n * d);
+        CU(cudaMemcpyAsync(x.p, cells, sizeof(float) * M * rs.e, cudaMemcpyHostToDevice, s));
+        Launch{ctx, s}(launch_tokens(x.as<float>(), w->rows.cls_tokens, n, features, rs.cls, rs.e, tok.as<float>(), s,
+                                     &ctx->launches),
+                       "tokens");
+        fit_rows(ctx, sc.get(), tok.as<float>(), n, features, rep.as<float>(), s);
+        CU(cudaMemcpy(reps, rep.p, sizeof(float) * n * d, cudaMemcpyDeviceToHost));
+        check_device_error(ctx);
+        return TCU_OK;
+    });
+}
+
+int tcu_fit_in_context(tcu_weights *w, const float *h, int rows, const float *scales, tcu_layer_sink sink, void *user) {
+    if (!w) return TCU_ERR_ARG;
+    tcu_ctx *ctx = w->ctx;
+    return guarded(ctx, [&]() -> int {
+        check_device_error(ctx);
+        if (!h || !scales || !sink || rows < 1) fail(TCU_ERR_ARG, "fit_in_context: bad argument");
+        const size_t n = (size_t)rows * w->shape.d;
+        DevBuf hd;
+        hd.ensure(sizeof(float) * n);
+        CU(cudaMemcpy(hd.p, h, sizeof(float) * n, cudaMemcpyHostToDevice));
+        // the stored form is not asked for: the cache the pass keeps on the way is f32 in chunks of 256 rows
+        ModelPtr m(fit_icl(w, hd.as<float>(), nullptr, rows, 256, 0, scales, LayerSink{sink, user}));
         return TCU_OK;
     });
 }

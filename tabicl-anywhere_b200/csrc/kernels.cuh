@@ -208,6 +208,22 @@ cudaError_t launch_copy_rows(float *x, const float *y, int R, int nq, int T, int
 cudaError_t launch_scale_add(float *y, const float *x, size_t n, float a, int accumulate, cudaStream_t s,
                              uint64_t *launches);
 cudaError_t launch_divide(float *y, const float *x, size_t n, float a, cudaStream_t s, uint64_t *launches);
+// The column stage of fitting (fitcol.cu; src/fit.rs:298-420).
+// Training cells X [n * F][e] += the label's embedding (digit ((int)y / divisor) % base of a class label when base > 0).
+cudaError_t launch_col_add_y(float *X, const float *y, int n, int F, int e, int max_classes, const float *table,
+                             int divisor, int base, cudaStream_t s, uint64_t *launches);
+// How many splits of the training cells the inducing points' attention takes (the part buffers hold
+// F * heads * splits * inds states: 2 floats in part_ms, head width floats in part_acc).
+int ind_attend_splits(int n, int F, int heads, int inds);
+// The inducing points' scaled queries q [inds][e] against each group's training cells (keys and values the rows
+// r * F + g of kv [n * F][2e]): att [F * inds][e].
+cudaError_t launch_ind_attend(const float *q, const float *kv, int n, int F, int e, int inds, int heads, int splits,
+                              float *part_ms, float *part_acc, float *att, cudaStream_t s, uint64_t *launches);
+// dst [times][count] = src [count], repeated.
+cudaError_t launch_repeat(float *dst, const float *src, size_t count, int times, cudaStream_t s, uint64_t *launches);
+// kv2 [F * inds][2e] (keys, values) into col_kv: group g's [2][e][inds] at col_kv + g * gstride + off.
+cudaError_t launch_col_kv_scatter(const float *kv2, int F, int e, int inds, size_t gstride, size_t off, float *col_kv,
+                                  cudaStream_t s, uint64_t *launches);
 // The class tree (tree.cu; src/predict.rs:661-692): nodes' scores (node t's [R][k] at logits + nodes[t].z * R) to
 // class scores out [R][classes]; nodes in walk order {k, leaf, score offset, map offset}; wbuf [n_nodes][R].
 cudaError_t launch_tree_combine(const float *logits, const int4 *nodes, const int *map, int n_nodes, int R, int classes,
