@@ -1545,6 +1545,8 @@ static void column_blocks(tcu_ctx *ctx, tcu_model *m, float *X, int n, int F, co
 static void check_fit_weights(const tcu_weights *w) {
     check_rows_weights(w);
     if (!w->rows.fit) fail(TCU_DECLINED, "fit: the weights were not made for fitting, or have no column-stage fit tensors");
+    if (!ind_attend_takes(w->rows.shape.e, w->rows.shape.col_heads))
+        fail(TCU_DECLINED, "fit: the column stage's head width is not one of 4, 8, 16, 32, 64");
 }
 
 // fit.rs:300-314: every column block's inducing-point queries for n training rows, on the device [blocks][inds][e].

@@ -164,6 +164,11 @@ cudaError_t ind_attend(const float *q, const float *kv, int n, int F, int e, int
 
 }  // namespace
 
+bool ind_attend_takes(int e, int heads) {
+    const int hd = heads > 0 && e % heads == 0 ? e / heads : 0;
+    return hd == 4 || hd == 8 || hd == 16 || hd == 32 || hd == 64;
+}
+
 int ind_attend_splits(int n, int F, int heads, int inds) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
@@ -183,7 +188,8 @@ cudaError_t launch_ind_attend(const float *q, const float *kv, int n, int F, int
     const int hd = e / heads;
     if (n < 1 || F < 1 || inds < 1 || splits < 1 || e % heads || e % 4) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(kv) | reinterpret_cast<uintptr_t>(part_acc)) % 16) return cudaErrorInvalidValue;
-    cudaError_t err = hd == 8    ? ind_attend<8>(q, kv, n, F, e, inds, heads, splits, part_ms, part_acc, s)
+    cudaError_t err = hd == 4    ? ind_attend<4>(q, kv, n, F, e, inds, heads, splits, part_ms, part_acc, s)
+                      : hd == 8  ? ind_attend<8>(q, kv, n, F, e, inds, heads, splits, part_ms, part_acc, s)
                       : hd == 16 ? ind_attend<16>(q, kv, n, F, e, inds, heads, splits, part_ms, part_acc, s)
                       : hd == 32 ? ind_attend<32>(q, kv, n, F, e, inds, heads, splits, part_ms, part_acc, s)
                       : hd == 64 ? ind_attend<64>(q, kv, n, F, e, inds, heads, splits, part_ms, part_acc, s)

@@ -215,6 +215,8 @@ cudaError_t launch_col_add_y(float *X, const float *y, int n, int F, int e, int 
 // How many splits of the training cells the inducing points' attention takes (the part buffers hold
 // F * heads * splits * inds states: 2 floats in part_ms, head width floats in part_acc).
 int ind_attend_splits(int n, int F, int heads, int inds);
+// Whether the inducing points' attention takes this width and head count (head widths 4, 8, 16, 32, 64).
+bool ind_attend_takes(int e, int heads);
 // The inducing points' scaled queries q [inds][e] against each group's training cells (keys and values the rows
 // r * F + g of kv [n * F][2e]): att [F * inds][e].
 cudaError_t launch_ind_attend(const float *q, const float *kv, int n, int F, int e, int inds, int heads, int splits,
