@@ -9,6 +9,7 @@
 
 #include "device.cuh"
 #include "kernels.cuh"
+#include "pdl.cuh"
 #include "tc.cuh"
 
 namespace tcu {
@@ -200,6 +201,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
         mbar_init_fence();
         *abort_flag = 0;
     }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    pdl_trigger();  // every block holds its tensor memory
+    const uint32_t tmem = *tslot;
+    const uint32_t half_bytes = (uint32_t)(2 * TC_BLOCK * sizeof(__half));
+    auto load = [&](int i, bool values) {  // the load thread: keys or values of tile t0 + i into slot i % NS
+        const __half *src = tiles + ((size_t)(t0 + i) * H + h) * 4 * TC_BLOCK + (values ? 2 * TC_BLOCK : 0);
+        __half *dst = (values ? Vring : Kring) + (size_t)(i % NS) * 2 * TC_BLOCK;
+        uint64_t *m = values ? &mV[i % NS] : &mK[i % NS];
+        expect_tx(m, half_bytes);
+        bulk_g2s(dst, src, half_bytes, m);
+    };
+    // the first tiles before the kernel before has finished: the split keys and values are written only by kernels
+    // launched the ordinary way (at load, or per layer of a fit), which every later kernel starts after
+    if (warp == 9 && lane == 0) {
+        for (int i = 0; i < min(nt, NS); i++) load(i, false), load(i, true);
+    }
+    pdl_wait();  // the queries come from the kernel before
     // each compute thread: half of its row's query (head columns 64 * part + [0, 64)) and its largest magnitude
     float qv[64];
     if (tid < 2 * BQ) {
@@ -222,18 +242,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_attend_tc(AttnArgs a) {
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
-    const uint32_t tmem = *tslot;
-    const uint32_t half_bytes = (uint32_t)(2 * TC_BLOCK * sizeof(__half));
-    auto load = [&](int i, bool values) {  // the load thread: keys or values of tile t0 + i into slot i % NS
-        const __half *src = tiles + ((size_t)(t0 + i) * H + h) * 4 * TC_BLOCK + (values ? 2 * TC_BLOCK : 0);
-        __half *dst = (values ? Vring : Kring) + (size_t)(i % NS) * 2 * TC_BLOCK;
-        uint64_t *m = values ? &mV[i % NS] : &mK[i % NS];
-        expect_tx(m, half_bytes);
-        bulk_g2s(dst, src, half_bytes, m);
-    };
-    if (warp == 9 && lane == 0) {
-        for (int i = 0; i < min(nt, NS); i++) load(i, false), load(i, true);
-    }
     // the row's query scale (its largest |q| maps below 2^14); Q split into TMEM
     float rs = 1.f;
     if (tid < 2 * BQ) {
@@ -603,13 +611,13 @@ cudaError_t launch_attend_tc(int kv, const AttnArgs &a, cudaStream_t s, uint64_t
     cudaError_t e = cudaSuccess;
     if (kv == 0) {
         e = allow_dynamic_smem((const void *)k_attend_tc<0>, smem);
-        if (e == cudaSuccess) k_attend_tc<0><<<grid, TC_THREADS, smem, s>>>(a);
+        if (e == cudaSuccess) e = launch_pdl(k_attend_tc<0>, grid, dim3(TC_THREADS), smem, s, a);
     } else if (kv == 1) {
         e = allow_dynamic_smem((const void *)k_attend_tc<1>, smem);
-        if (e == cudaSuccess) k_attend_tc<1><<<grid, TC_THREADS, smem, s>>>(a);
+        if (e == cudaSuccess) e = launch_pdl(k_attend_tc<1>, grid, dim3(TC_THREADS), smem, s, a);
     } else {
         e = allow_dynamic_smem((const void *)k_attend_tc<2>, smem);
-        if (e == cudaSuccess) k_attend_tc<2><<<grid, TC_THREADS, smem, s>>>(a);
+        if (e == cudaSuccess) e = launch_pdl(k_attend_tc<2>, grid, dim3(TC_THREADS), smem, s, a);
     }
     if (e != cudaSuccess) return e;
     e = cudaGetLastError();

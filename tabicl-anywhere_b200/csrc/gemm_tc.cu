@@ -18,6 +18,7 @@
 
 #include "device.cuh"
 #include "kernels.cuh"
+#include "pdl.cuh"
 #include "tc.cuh"
 
 namespace tcu {
@@ -52,6 +53,8 @@ __global__ void __launch_bounds__(256) k_split_rows(const float *x, int ldx, int
                                                     const float *lnb, float4 *stats, __half *tiles) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = blockIdx.x * 8 + warp;
     const bool real = row < M;
+    pdl_trigger();
+    pdl_wait();
     const float *p = x + (size_t)(real ? row : 0) * ldx;
     float v[NJ][8];
 #pragma unroll
@@ -167,10 +170,10 @@ __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4
         mbar_init_fence();
         *abort_flag = 0;
     }
-    if (tid < GBM) un_row[tid] = m0 + tid < a.M ? stats[m0 + tid].w : 0.f;
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
+    pdl_trigger();  // every block holds its tensor memory
     const uint32_t tmem = *tslot;
     const uint8_t *A = reinterpret_cast<const uint8_t *>(a.tc_atiles) + (size_t)mt * nk * G::A_BYTES;
     // weights are stored in 128-row blocks; a 64-wide tile is the first or second half of each hi and lo block
@@ -189,22 +192,32 @@ __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4
     for (int e = 0; e < HALF; e++) sum[e] = 0.f;
     const int col0 = ((warp >> 2) & 1) * HALF;
     if (warp == 9) {
-        // the load thread: chunk c into slot c % S once the MMAs of chunk c - S have read it
+        // the load thread: chunk c into slot c % S once the MMAs of chunk c - S have read it. The weights of the first
+        // S chunks are asked for before the kernel before has finished (no kernel writes them); the rows after.
         if (lane == 0) {
-            int issued = 0;
-            for (int c = 0; c < nk; c++) {
+            auto load_w = [&](int c) {
                 const int s = c % S;
-                if (c >= S && !wait(&mEmpty[s], (uint32_t)((c / S) - 1) & 1u)) break;
                 uint8_t *dst = smraw + (size_t)s * G::SLOT;
                 const uint8_t *wsrc = Wt + (size_t)c * 2 * GBLOCK * 2;
                 g_expect(&mFull[s], G::SLOT);
-                g_bulk(dst, A + (size_t)c * G::A_BYTES, G::A_BYTES, &mFull[s]);
                 if (BN == GBM) {
                     g_bulk(dst + G::A_BYTES, wsrc, G::W_BYTES, &mFull[s]);
                 } else {
                     g_bulk(dst + G::A_BYTES, wsrc, G::W_BYTES / 2, &mFull[s]);
                     g_bulk(dst + G::A_BYTES + G::W_BYTES / 2, wsrc + GBLOCK * 2, G::W_BYTES / 2, &mFull[s]);
                 }
+            };
+            const int pre = min(nk, S);
+            for (int c = 0; c < pre; c++) load_w(c);
+            pdl_wait();
+            for (int c = 0; c < pre; c++)
+                g_bulk(smraw + (size_t)(c % S) * G::SLOT, A + (size_t)c * G::A_BYTES, G::A_BYTES, &mFull[c % S]);
+            int issued = pre;
+            for (int c = pre; c < nk; c++) {
+                const int s = c % S;
+                if (!wait(&mEmpty[s], (uint32_t)((c / S) - 1) & 1u)) break;
+                load_w(c);
+                g_bulk(smraw + (size_t)s * G::SLOT, A + (size_t)c * G::A_BYTES, G::A_BYTES, &mFull[s]);
                 issued = c + 1;
             }
             // the last loads land before the block lets go of shared memory
@@ -212,7 +225,8 @@ __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4
                 mbar_wait(&mFull[c % S], (uint32_t)(c / S) & 1u, GEMM_WAIT_CYCLES);
         }
     } else if (warp == 8) {
-        // the MMA thread
+        // the MMA thread (its bounded waits start once the kernel before has finished)
+        pdl_wait();
         if (lane == 0) {
             const uint32_t id = idesc_f16(GBM, BN, 0, 0);
             // K-major, no swizzle: core matrices 128 B apart along K (LBO), 8-row groups 1024 B apart (SBO)
@@ -240,6 +254,7 @@ __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4
         }
     } else {
         // eight warps: lane (row) (warp % 4) * 32 + lane, columns col0 + [0, BN / 2) of every chunk's accumulator
+        pdl_wait();
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         for (int c = 0; c < nk; c++) {
             const int b = c % GBUFS;
@@ -262,6 +277,8 @@ __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4
             if (!okc) break;
         }
     }
+    pdl_wait();  // the rows' scalings and the residual come from earlier kernels
+    if (tid < GBM) un_row[tid] = m0 + tid < a.M ? stats[m0 + tid].w : 0.f;
     fence_before_sync();
     __syncthreads();
     const bool ok = !*abort_flag;
@@ -357,22 +374,23 @@ static cudaError_t launch_bn(const LinArgs &a, float4 *stats, cudaStream_t s) {
     cudaError_t e = allow_dynamic_smem((const void *)k_gemm_tc<BN>, GemmShape<BN>::SMEM);
     if (e != cudaSuccess) return e;
     dim3 grid((a.N + BN - 1) / BN, (a.M + GBM - 1) / GBM);
-    k_gemm_tc<BN><<<grid, GTHREADS, GemmShape<BN>::SMEM, s>>>(a, stats);
-    return cudaGetLastError();
+    return launch_pdl(k_gemm_tc<BN>, grid, dim3(GTHREADS), GemmShape<BN>::SMEM, s, a, (const float4 *)stats);
 }
 
 cudaError_t launch_gemm_tc(const LinArgs &a, float4 *stats, cudaStream_t s, uint64_t *launches) {
     if (!a.tc_wtiles || !a.tc_atiles || a.K % GBK || a.K > 2048) return cudaErrorInvalidValue;
     const int sblocks = (a.M + GBM - 1) / GBM * (GBM / 8);
     __half *at = reinterpret_cast<__half *>(a.tc_atiles);
+    cudaError_t e0;
     if (a.K <= 256)
-        k_split_rows<1><<<sblocks, 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
+        e0 = launch_pdl(k_split_rows<1>, dim3(sblocks), dim3(256), 0, s, a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
     else if (a.K <= 512)
-        k_split_rows<2><<<sblocks, 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
+        e0 = launch_pdl(k_split_rows<2>, dim3(sblocks), dim3(256), 0, s, a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
     else if (a.K <= 1024)
-        k_split_rows<4><<<sblocks, 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
+        e0 = launch_pdl(k_split_rows<4>, dim3(sblocks), dim3(256), 0, s, a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
     else
-        k_split_rows<8><<<sblocks, 256, 0, s>>>(a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
+        e0 = launch_pdl(k_split_rows<8>, dim3(sblocks), dim3(256), 0, s, a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
+    if (e0 != cudaSuccess) return e0;
     if (launches) ++*launches;
     const cudaError_t e = gemm_bn(a.M, a.N) == 64 ? launch_bn<64>(a, stats, s) : launch_bn<128>(a, stats, s);
     if (launches) ++*launches;

@@ -3,6 +3,7 @@
 // attention over the stored key/value chunks with the integer dequantisation fused into the loads, the
 // log-sum-exp merge, fitting's chunk packer, and the classification / regression heads.
 #include "kernels.cuh"
+#include "pdl.cuh"
 #include "device.cuh"
 
 #include <cfloat>
@@ -217,6 +218,8 @@ __global__ void __launch_bounds__(256, 2) k_gemm(LinArgs a) {
 __global__ void __launch_bounds__(256) k_ssmax(float *q, int R, int d, int heads, int hid, const float *q0w,
                                                const float *q0b, const float *q2w, const float *q2b,
                                                const float *scale, int rows_per_block) {
+    pdl_trigger();
+    pdl_wait();  // the inputs come from the kernel before
     extern __shared__ float sm[];
     const int hd = d / heads, h = blockIdx.y, r0 = blockIdx.x * rows_per_block;
     const int RB = rows_per_block;
@@ -255,6 +258,8 @@ __global__ void __launch_bounds__(256) k_ssmax(float *q, int R, int d, int heads
 __global__ void __launch_bounds__(256) k_ssmax_rows(float *q, int d, int heads, int hid, const float *q0w,
                                                     const float *q0b, const float *q2w, const float *q2b,
                                                     const float *scale) {
+    pdl_trigger();
+    pdl_wait();  // the inputs come from the kernel before
     extern __shared__ float sm[];
     const int hd = d / heads, r = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float *qs = sm, *hs = sm + hd;
@@ -320,6 +325,8 @@ __global__ void __launch_bounds__(256) k_ssmax_rows(float *q, int d, int heads, 
 
 // q_h *= scale_h * (1 + tanh(m)) for every (row, coordinate), m the query MLP's output (nn.rs:148).
 __global__ void k_ssmax_apply(float *q, const float *m, const float *scale, int R, int d) {
+    pdl_trigger();
+    pdl_wait();  // the inputs come from the kernel before
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)R * d) return;
     q[i] = q[i] * (scale[i % d] * (1.0f + tanh1(m[i])));
@@ -357,6 +364,8 @@ __device__ __forceinline__ uint4 gather_vec(const uint8_t *row, int k, int len) 
 // weighted values) for the merge.
 template <int KV, int HD, int RSB>
 __global__ void __launch_bounds__(128) k_attend_decode(AttnArgs a) {
+    pdl_trigger();
+    pdl_wait();  // the inputs come from the kernel before
     // 8-byte vectors for 8-bit values keep a lane at 8 keys, as 16-byte vectors do for 16-bit ones
     constexpr int W = KvFmt<KV>::W, VB = KV == 2 ? 8 : 16, EPV = VB / W, KS = 8 * EPV, DG = 16;
     constexpr int DPT = HD >= DG ? HD / DG : 1;
@@ -483,6 +492,8 @@ __global__ void __launch_bounds__(128) k_attend_decode(AttnArgs a) {
 // the reference's rescaling rule (nn.rs:207-215).
 template <int KV, int HD>
 __global__ void __launch_bounds__(256, 2) k_attend_flash(AttnArgs a) {
+    pdl_trigger();
+    pdl_wait();  // the inputs come from the kernel before
     constexpr int W = KvFmt<KV>::W, EPV = KvFmt<KV>::EPV, BQ = FLASH_ROWS, KT = FLASH_KEYS;
     constexpr int OD = HD >= 16 ? HD / 16 : 1;
     constexpr int VPR = KT / EPV;
@@ -637,6 +648,8 @@ __global__ void __launch_bounds__(256, 2) k_attend_flash(AttnArgs a) {
 // with 16-byte loads along the head's values, and the warps' sums meet in shared memory.
 __global__ void __launch_bounds__(256) k_attend_merge(const float *ms, const float *acc, int P, int R, int H, int d,
                                                       float *out, int ldo) {
+    pdl_trigger();
+    pdl_wait();  // the inputs come from the kernel before
     extern __shared__ __align__(16) float wsm[];  // [P] part weights, then [8][hd] warp sums
     __shared__ float red[8];
     const int r = blockIdx.x / H, h = blockIdx.x % H, hd = d / H, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1054,7 +1067,8 @@ cudaError_t launch_ssmax(float *q, int R, int d, int heads, int hid, const float
     const int hd = d / heads;
     // one block per (row, head) for few rows, and up to 128 rows at the shape whose weights it loads all at once
     if (R <= 16 || (R <= 128 && hd == 128 && hid == 64)) {
-        k_ssmax_rows<<<dim3(R, heads), 256, sizeof(float) * (hd + hid), s>>>(q, d, heads, hid, q0w, q0b, q2w, q2b, scale);
+        const cudaError_t e = launch_pdl(k_ssmax_rows, dim3(R, heads), dim3(256), sizeof(float) * (hd + hid), s, q, d, heads, hid, q0w, q0b, q2w, q2b, scale);
+        if (e != cudaSuccess) return e;
         TCU_LAUNCHED(launches);
         return cudaGetLastError();
     }
@@ -1063,7 +1077,8 @@ cudaError_t launch_ssmax(float *q, int R, int d, int heads, int hid, const float
     cudaError_t e = allow_smem(k_ssmax, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((R + rb - 1) / rb, heads);
-    k_ssmax<<<grid, 256, smem, s>>>(q, R, d, heads, hid, q0w, q0b, q2w, q2b, scale, rb);
+    e = launch_pdl(k_ssmax, grid, dim3(256), smem, s, q, R, d, heads, hid, q0w, q0b, q2w, q2b, scale, rb);
+    if (e != cudaSuccess) return e;
     TCU_LAUNCHED(launches);
     return cudaGetLastError();
 }
@@ -1071,7 +1086,8 @@ cudaError_t launch_ssmax(float *q, int R, int d, int heads, int hid, const float
 cudaError_t launch_ssmax_apply(float *q, const float *m, const float *scale, int R, int d, cudaStream_t s,
                                uint64_t *launches) {
     const size_t n = (size_t)R * d;
-    k_ssmax_apply<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(q, m, scale, R, d);
+    const cudaError_t e = launch_pdl(k_ssmax_apply, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, q, m, scale, R, d);
+    if (e != cudaSuccess) return e;
     TCU_LAUNCHED(launches);
     return cudaGetLastError();
 }
@@ -1079,11 +1095,12 @@ cudaError_t launch_ssmax_apply(float *q, const float *m, const float *scale, int
 template <int KV, int HD>
 static cudaError_t decode_hd(const AttnArgs &a, cudaStream_t s) {
     dim3 grid(a.nitems, a.heads);
+    cudaError_t e;
     if (a.R == 1)
-        k_attend_decode<KV, HD, 1><<<grid, 128, 0, s>>>(a);
+        e = launch_pdl(k_attend_decode<KV, HD, 1>, grid, dim3(128), 0, s, a);
     else
-        k_attend_decode<KV, HD, 8><<<grid, 128, 0, s>>>(a);
-    return cudaGetLastError();
+        e = launch_pdl(k_attend_decode<KV, HD, 8>, grid, dim3(128), 0, s, a);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <int KV>
@@ -1102,7 +1119,8 @@ cudaError_t launch_attend_merge(const AttnArgs &a, int parts, cudaStream_t s, ui
     const size_t smem = sizeof(float) * ((size_t)((parts + 3) & ~3) + 8 * (size_t)(a.d / a.heads));
     cudaError_t e = allow_smem(k_attend_merge, smem);
     if (e != cudaSuccess) return e;
-    k_attend_merge<<<a.R * a.heads, 256, smem, s>>>(a.part_ms, a.part_acc, parts, a.R, a.heads, a.d, a.out, a.ldo);
+    e = launch_pdl(k_attend_merge, dim3(a.R * a.heads), dim3(256), smem, s, (const float *)a.part_ms, (const float *)a.part_acc, parts, a.R, a.heads, a.d, a.out, a.ldo);
+    if (e != cudaSuccess) return e;
     TCU_LAUNCHED(launches);
     return cudaGetLastError();
 }
@@ -1121,7 +1139,8 @@ static cudaError_t flash_hd(const AttnArgs &a, cudaStream_t s) {
     cudaError_t e = allow_smem(k_attend_flash<KV, HD>, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((a.R + FLASH_ROWS - 1) / FLASH_ROWS, a.heads, a.splits);
-    k_attend_flash<KV, HD><<<grid, 256, smem, s>>>(a);
+    e = launch_pdl(k_attend_flash<KV, HD>, grid, dim3(256), smem, s, a);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -11,6 +11,7 @@
 
 #include "device.cuh"
 #include "kernels.cuh"
+#include "pdl.cuh"
 #include "tc.cuh"
 
 namespace tcu {
@@ -94,6 +95,9 @@ __global__ void __launch_bounds__(QM_THREADS, 1) k_qmlp_tc(QmlpArgs a) {
     for (int i = threadIdx.x; i < QM_HID; i += QM_THREADS) c_w0u[i] = a.w0_unscale[i], c_b0[i] = a.b0[i];
     for (int i = threadIdx.x; i < QM_HD; i += QM_THREADS) c_w2u[i] = a.w2_unscale[i], c_b2[i] = a.b2[i];
     for (int i = threadIdx.x; i < a.heads * QM_HD; i += QM_THREADS) c_scl[i] = a.scale[i];
+    __syncthreads();
+    pdl_trigger();  // every block holds its tensor memory
+    pdl_wait();     // the queries come from the kernel before
     // 1. the pairs: thread (row m, quarter c) holds head columns 32c..32c+31 of pair p0 + m
     const int m = tid & (QM_ROWS - 1), c = tid >> 7, p = p0 + m;
     const bool real = p < a.pairs;
@@ -253,7 +257,8 @@ cudaError_t launch_qmlp_tc(const QmlpArgs &a, cudaStream_t s, uint64_t *launches
     if (smem > 227 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = allow_dynamic_smem((const void *)k_qmlp_tc, smem);
     if (e != cudaSuccess) return e;
-    k_qmlp_tc<<<(a.pairs + QM_ROWS - 1) / QM_ROWS, QM_THREADS, smem, s>>>(a);
+    e = launch_pdl(k_qmlp_tc, dim3((a.pairs + QM_ROWS - 1) / QM_ROWS), dim3(QM_THREADS), smem, s, a);
+    if (e != cudaSuccess) return e;
     if (launches) ++*launches;
     return cudaGetLastError();
 }
