@@ -43,6 +43,9 @@ def args():
     p.add_argument("--latency-reps", type=int, default=100)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-multi", action="store_true", help="skip the config 3 (members) and 4 (sharded) passes")
+    p.add_argument("--trace-one-row", action="store_true",
+                   help="after the timed runs, one traced one-row call (run with TCU_GRAPHS=0): the one-kernel stage's "
+                        "work and grid-barrier wait per phase, in one_row_phases_us")
     p.add_argument("--profile-call", choices=["stage", "rows"], default=None,
                    help="after the timed runs, one more call (the in-context stage of --rows rows, or the whole "
                         "prediction from features) between cudaProfilerStart and Stop, for ncu --profile-from-start off")
@@ -593,6 +596,40 @@ def full_predict(pkg, synth, gpu, vm, cfg, wt, a, rank, world, stream, out, clas
     return res
 
 
+def one_row_phases(vm, h1, classes, o1, sp, layers):
+    """The one-row one-kernel stage's timeline: thread 0 of every CTA records the global timer on entering and leaving
+    each grid-barrier wait (TCU_ROWS_TRACE; eager calls only, TCU_GRAPHS=0). Per phase of a layer (A the query
+    projection, B the query MLP and attention, C the merge, D the out-projection, E and F the feed-forward layers):
+    the work before its barrier and the wait in it, the mean over CTAs and layers 1 on (layer 0 starts from the
+    prefetched state), and the slowest CTA's work, microseconds."""
+    import tempfile
+    import torch
+    if os.environ.get("TCU_GRAPHS") != "0":
+        return {"skipped": "run with TCU_GRAPHS=0: captured calls are not traced"}
+    path = os.path.join(tempfile.gettempdir(), f"tcu_rows_trace_{os.getpid()}.bin")
+    os.environ["TCU_ROWS_TRACE"] = path
+    try:
+        vm.stage_device(h1.data_ptr(), 1, classes, o1.data_ptr(), sp)
+        torch.cuda.synchronize()
+    finally:
+        del os.environ["TCU_ROWS_TRACE"]
+    raw = open(path, "rb").read()
+    os.remove(path)
+    G, K = (int(v) for v in np.frombuffer(raw[:8], np.int32))
+    t = np.frombuffer(raw[8:], np.uint64).reshape(G, K).astype(np.int64)
+    nm = int((t[0] > 0).sum())
+    t = t[:, :nm] - t[:, :nm].min()
+    ent, ext = t[:, 0::2], t[:, 1::2]
+    prev = np.concatenate([np.zeros((G, 1), np.int64), ext[:, :-1]], axis=1)
+    work, wait = (ent - prev) / 1e3, (ext - ent) / 1e3
+    out = {"ctas": G, "barriers": int(ent.shape[1]), "span_us": float(ext.max() / 1e3)}
+    for i, name in enumerate("ABCDEF"):
+        cols = [6 * l + i for l in range(1, layers) if 6 * l + i < ent.shape[1]]
+        out[name] = {"work_mean": float(work[:, cols].mean()), "work_slowest": float(work[:, cols].max(axis=0).mean()),
+                     "wait_mean": float(wait[:, cols].mean())}
+    return out
+
+
 def fit_baseline(pkg, synth, w, d, a):
     """fit_raw_async (fit.rs:285-752) of config 2's table (10,000 normalised rows x 100 features, 10 classes) with
     every stage on the device: the column stage, the row stage, the in-context stage, and the fitted member's entries
@@ -785,6 +822,8 @@ def main():
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
 
+    phases = one_row_phases(vm, h1, classes, o1, sp, shape["layers"]) if a.trace_one_row else None
+
     hbm, bf16, kind = peaks()
     traffic = ncu_traffic(a)
     layer_bytes = pkg.record(a.kv, d, CHUNK) * (a.train_rows // CHUNK) + (pkg.record(a.kv, d, a.train_rows % CHUNK) if a.train_rows % CHUNK else 0)
@@ -825,6 +864,8 @@ def main():
         "bundle_load": load,
         "clocks": clocks.summary(),
     }
+    if phases is not None:
+        line["latency_1row"]["one_row_phases_us"] = phases
     if not a.no_multi:
         comm = None
         if world > 1:

@@ -1279,8 +1279,30 @@ static void stage_rows(tcu_ctx *ctx, tcu_model *m, const tcu_model::RowsPlan &p,
         ev_end = ctx->prof_events[ctx->prof_used + 1];
         ctx->prof_used += 2;
     }
+    // diagnostics: TCU_ROWS_TRACE=<file> writes each CTA's barrier entry and exit times of this launch there
+    const char *trace_path = getenv("TCU_ROWS_TRACE");
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    CU(cudaStreamIsCapturing(s, &capturing));
+    if (capturing != cudaStreamCaptureStatusNone) trace_path = nullptr;  // eager calls only (TCU_GRAPHS=0)
+    DevBuf trace;
+    if (trace_path) {
+        trace.ensure(sizeof(unsigned long long) * (size_t)p.grid * ROWS_TRACE_MARKS);
+        CU(cudaMemsetAsync(trace.p, 0, trace.bytes, s));
+        a.trace = trace.as<unsigned long long>();
+    }
     Launch{ctx, s}(launch_stage_rows(m->kv, hd, a, p.grid, p.smem, s, &ctx->launches), "stage (one kernel)");
     if (ev_end) CU(cudaEventRecord(ev_end, s));
+    if (trace_path) {
+        std::vector<unsigned long long> t(trace.bytes / sizeof(unsigned long long));
+        CU(cudaMemcpyAsync(t.data(), trace.p, trace.bytes, cudaMemcpyDeviceToHost, s));
+        CU(cudaStreamSynchronize(s));
+        if (FILE *f = std::fopen(trace_path, "wb")) {
+            const int32_t head[2] = {p.grid, ROWS_TRACE_MARKS};
+            std::fwrite(head, sizeof(head), 1, f);
+            std::fwrite(t.data(), sizeof(unsigned long long), t.size(), f);
+            std::fclose(f);
+        }
+    }
 }
 
 // The stage on the model's own buffers (m->h in, m->out out), replayed from a CUDA graph captured on the context

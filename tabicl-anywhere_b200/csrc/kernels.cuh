@@ -101,7 +101,11 @@ struct RowsArgs {
                                         // gave up, every CTA then leaves at its next barrier
     int *err_report = nullptr;          // report slots (host memory, mapped): [0] a grid barrier gave up, [1] a
                                         // tile's copy did not arrive, [2] the CTA left because another gave up
+    // diagnostics (null: off): [grid][ROWS_TRACE_MARKS] global-timer nanoseconds, thread 0 of each CTA recording
+    // its entry into and exit from every grid barrier wait, in order
+    unsigned long long *trace = nullptr;
 };
+constexpr int ROWS_TRACE_MARKS = 512;
 
 // Keys per tile of the one-kernel stage for a stored format (f32 32, i16 64, i8 64).
 int rows_tile_keys(int kv);

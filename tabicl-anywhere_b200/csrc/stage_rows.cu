@@ -133,7 +133,20 @@ struct Stage {
     // Slot s + b of the ring (b < slots).
     __device__ __forceinline__ int slot_add(int s, int b) const { return s + b >= a.slots ? s + b - a.slots : s + b; }
     __device__ __forceinline__ void arrive() { grid_arrive(a, target); }
-    __device__ __forceinline__ bool wait() { return grid_wait(a, target, flag_s); }
+    __device__ __forceinline__ bool wait() {
+        mark();
+        const bool r = grid_wait(a, target, flag_s);
+        mark();
+        return r;
+    }
+    int nmark = 0;
+    __device__ __forceinline__ void mark() {
+        if (a.trace && threadIdx.x == 0 && nmark < ROWS_TRACE_MARKS) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            a.trace[(size_t)blockIdx.x * ROWS_TRACE_MARKS + nmark++] = t;
+        }
+    }
     // Start the copies of the next tiles of the sequence, up to `limit`, into the slots that are free.
     __device__ void issue_upto(int limit) {
         limit = min(limit, min(total, consumed + a.slots));
