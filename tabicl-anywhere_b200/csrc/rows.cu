@@ -81,18 +81,66 @@ __global__ void __launch_bounds__(256) k_col_attend(const float *Q, int R, int F
     }
 }
 
+// Keys per chunk: as many independent chains as the query and the weighted values leave registers for.
+__host__ __device__ constexpr int attend_chunk(int hd) { return hd <= 16 ? 16 : hd == 32 ? 8 : 4; }
+
+// nn.rs:187-228, 280-286 for one query (scaled, in registers) against n keys and values held in shared memory as
+// [n][HD] rows, read by every lane at once: the online softmax over chunks of KC keys, the running maximum replaced
+// (and the sums rescaled) only when a chunk's maximum exceeds it, as Soft::update does. A chunk's KC scores are
+// independent chains, each added in coordinate order. acc (HD) receives the weighted values; returns the weights' sum.
+template <int HD, int KC>
+__device__ __forceinline__ float attend_query(const float *q, const float *Ks, const float *Vs, int n, float *acc) {
+    float m = -FLT_MAX, sum = 0.f;
+    for (int k0 = 0; k0 < n; k0 += KC) {
+        float sc[KC];
+#pragma unroll
+        for (int c = 0; c < KC; c++) sc[c] = 0.f;
+#pragma unroll
+        for (int j4 = 0; j4 < HD / 4; j4++) {
+#pragma unroll
+            for (int c = 0; c < KC; c++) {
+                const float4 kk = reinterpret_cast<const float4 *>(Ks + min(k0 + c, n - 1) * HD)[j4];
+                sc[c] = fmaf(q[4 * j4], kk.x, sc[c]), sc[c] = fmaf(q[4 * j4 + 1], kk.y, sc[c]);
+                sc[c] = fmaf(q[4 * j4 + 2], kk.z, sc[c]), sc[c] = fmaf(q[4 * j4 + 3], kk.w, sc[c]);
+            }
+        }
+        float cm = -FLT_MAX;
+#pragma unroll
+        for (int c = 0; c < KC; c++)
+            if (k0 + c < n) cm = fmaxf(cm, sc[c]);
+        if (cm > m) {
+            const float corr = exp1(m - cm);
+            m = cm, sum *= corr;
+#pragma unroll
+            for (int j = 0; j < HD; j++) acc[j] *= corr;
+        }
+#pragma unroll
+        for (int c = 0; c < KC; c++) {
+            const float p = k0 + c < n ? exp1(sc[c] - m) : 0.f;
+            sum += p;
+            const float4 *vr = reinterpret_cast<const float4 *>(Vs + min(k0 + c, n - 1) * HD);
+#pragma unroll
+            for (int j4 = 0; j4 < HD / 4; j4++) {
+                const float4 vv = vr[j4];
+                acc[4 * j4] = fmaf(vv.x, p, acc[4 * j4]), acc[4 * j4 + 1] = fmaf(vv.y, p, acc[4 * j4 + 1]);
+                acc[4 * j4 + 2] = fmaf(vv.z, p, acc[4 * j4 + 2]), acc[4 * j4 + 3] = fmaf(vv.w, p, acc[4 * j4 + 3]);
+            }
+        }
+    }
+    return sum;
+}
+
 // The same attention with one query per thread: block (group g, head h, run of blockDim rows); the head's keys and
 // values of group g in shared memory as [n][HD] rows, read by every lane at once (broadcast); the query, then the
-// weighted values, in registers. The scores are taken twice (their maximum first, as the CPU's two-pass softmax
-// needs; then again, identically, for the weights), so each score, weight and weighted sum is the one above; only
-// the weights' sum is added in key order by one thread instead of across a warp.
+// weighted values, in registers (attend_query).
 template <int HD>
-__global__ void __launch_bounds__(256) k_col_attend_q(const float *Q, int R, int F, const float *kv, size_t gstride,
+__global__ void __launch_bounds__(256, HD <= 32 ? 2 : 1) k_col_attend_q(const float *Q, int R, int F, const float *kv, size_t gstride,
                                                       int e, int n, float scale, float *att) {
     extern __shared__ __align__(16) float sm[];
     const int g = blockIdx.x, h = blockIdx.y;
     const float *Kg = kv + (size_t)g * gstride, *Vg = Kg + (size_t)e * n;
     float *Ks = sm, *Vs = sm + (size_t)n * HD;
+#pragma unroll 8
     for (int i = threadIdx.x; i < n * HD; i += blockDim.x) {
         const int j = i / n, k = i - j * n;
         Ks[k * HD + j] = Kg[(size_t)(h * HD + j) * n + k];
@@ -106,32 +154,7 @@ __global__ void __launch_bounds__(256) k_col_attend_q(const float *Q, int R, int
     float q[HD], acc[HD];
 #pragma unroll
     for (int j = 0; j < HD; j++) q[j] = qp[j] * scale, acc[j] = 0.f;
-    auto score = [&](int k) {
-        const float4 *kr = reinterpret_cast<const float4 *>(Ks + k * HD);
-        float s = 0.f;
-#pragma unroll
-        for (int j4 = 0; j4 < HD / 4; j4++) {
-            const float4 kk = kr[j4];
-            s = fmaf(q[4 * j4], kk.x, s), s = fmaf(q[4 * j4 + 1], kk.y, s);
-            s = fmaf(q[4 * j4 + 2], kk.z, s), s = fmaf(q[4 * j4 + 3], kk.w, s);
-        }
-        return s;
-    };
-    float mx = -FLT_MAX;
-    for (int k = 0; k < n; k++) mx = fmaxf(mx, score(k));
-    float sum = 0.f;
-    for (int k = 0; k < n; k++) {
-        const float p = exp1(score(k) - mx);
-        sum += p;
-        const float4 *vr = reinterpret_cast<const float4 *>(Vs + k * HD);
-#pragma unroll
-        for (int j4 = 0; j4 < HD / 4; j4++) {
-            const float4 vv = vr[j4];
-            acc[4 * j4] = fmaf(vv.x, p, acc[4 * j4]), acc[4 * j4 + 1] = fmaf(vv.y, p, acc[4 * j4 + 1]);
-            acc[4 * j4 + 2] = fmaf(vv.z, p, acc[4 * j4 + 2]), acc[4 * j4 + 3] = fmaf(vv.w, p, acc[4 * j4 + 3]);
-        }
-    }
-    const float inv = 1.0f / sum;
+    const float inv = 1.0f / attend_query<HD, attend_chunk(HD)>(q, Ks, Vs, n, acc);
     float *op = att + cell * e + h * HD;
 #pragma unroll
     for (int j = 0; j < HD; j++) op[j] = acc[j] * inv;
@@ -214,9 +237,8 @@ __global__ void __launch_bounds__(256) k_row_attend(const float *QKV, int R, int
 }
 
 // k_row_attend with one query token per thread: block (row r, head h), the head's rotated keys and values of the row
-// in shared memory as [T][HD] rows, read by every lane at once; the query and the weighted values in registers.
-// Scores taken twice (maximum, then weights) as in k_col_attend_q: the same scores, weights and weighted sums as
-// k_row_attend, the weights' sum added in key order.
+// in shared memory as [T][HD] rows, read by every lane at once; the query and the weighted values in registers
+// (attend_query).
 template <int HD>
 __global__ void __launch_bounds__(512) k_row_attend_q(const float *QKV, int R, int T, int nq, int e, const float *cs,
                                                        const float *sn, float *att) {
@@ -224,6 +246,7 @@ __global__ void __launch_bounds__(512) k_row_attend_q(const float *QKV, int R, i
     const int r = blockIdx.x, h = blockIdx.y, half = HD / 2;
     const float *base = QKV + (size_t)r * T * 3 * e;
     float *Ks = sm, *Vs = sm + (size_t)T * HD;
+#pragma unroll 8
     for (int i = threadIdx.x; i < T * HD; i += blockDim.x) {
         const int t = i / HD, j = i - t * HD;
         Ks[i] = rope(base + (size_t)t * 3 * e + e + h * HD, j, half, cs, sn, t);
@@ -237,32 +260,7 @@ __global__ void __launch_bounds__(512) k_row_attend_q(const float *QKV, int R, i
     float q[HD], acc[HD];
 #pragma unroll
     for (int j = 0; j < HD; j++) q[j] = rope(qr, j, half, cs, sn, t) * inv, acc[j] = 0.f;
-    auto score = [&](int k) {
-        const float4 *kr = reinterpret_cast<const float4 *>(Ks + k * HD);
-        float s = 0.f;
-#pragma unroll
-        for (int j4 = 0; j4 < HD / 4; j4++) {
-            const float4 kk = kr[j4];
-            s = fmaf(q[4 * j4], kk.x, s), s = fmaf(q[4 * j4 + 1], kk.y, s);
-            s = fmaf(q[4 * j4 + 2], kk.z, s), s = fmaf(q[4 * j4 + 3], kk.w, s);
-        }
-        return s;
-    };
-    float mx = -FLT_MAX;
-    for (int k = 0; k < T; k++) mx = fmaxf(mx, score(k));
-    float sum = 0.f;
-    for (int k = 0; k < T; k++) {
-        const float p = exp1(score(k) - mx);
-        sum += p;
-        const float4 *vr = reinterpret_cast<const float4 *>(Vs + k * HD);
-#pragma unroll
-        for (int j4 = 0; j4 < HD / 4; j4++) {
-            const float4 vv = vr[j4];
-            acc[4 * j4] = fmaf(vv.x, p, acc[4 * j4]), acc[4 * j4 + 1] = fmaf(vv.y, p, acc[4 * j4 + 1]);
-            acc[4 * j4 + 2] = fmaf(vv.z, p, acc[4 * j4 + 2]), acc[4 * j4 + 3] = fmaf(vv.w, p, acc[4 * j4 + 3]);
-        }
-    }
-    const float s = 1.0f / sum;
+    const float s = 1.0f / attend_query<HD, attend_chunk(HD)>(q, Ks, Vs, T, acc);
     float *op = att + ((size_t)r * nq + t) * e + h * HD;
 #pragma unroll
     for (int j = 0; j < HD; j++) op[j] = acc[j] * s;

@@ -151,3 +151,4 @@ def test_rows_declines_without_column_stages(gpu, tiny):
     vm2 = tcu.VramModel.from_parts(w2, [t["n"], feats, 3, 48, 0, 1, 1], t["n"], 3, t["scales"], layers)
     assert vm2.rows(t["x_test"], 3) is None  # no col_kv
     vm.free(), vm2.free(), w.free(), w2.free()
+
