@@ -81,61 +81,86 @@ __global__ void __launch_bounds__(256) k_col_attend(const float *Q, int R, int F
     }
 }
 
-// Keys per chunk: as many independent chains as the query and the weighted values leave registers for.
-__host__ __device__ constexpr int attend_chunk(int hd) { return hd <= 16 ? 16 : hd == 32 ? 8 : 4; }
+// Queries per thread (each key and value row read from shared memory serves all of them) and keys per chunk (as
+// many independent chains as the queries and the weighted values leave registers for), by head width.
+__host__ __device__ constexpr int attend_nq(int hd) { return hd <= 32 ? 2 : 1; }
+__host__ __device__ constexpr int attend_chunk(int hd, int nq) {
+    return nq == 2 ? (hd <= 8 ? 16 : hd == 16 ? 8 : 4) : (hd <= 16 ? 16 : hd == 32 ? 8 : 4);
+}
 
-// nn.rs:187-228, 280-286 for one query (scaled, in registers) against n keys and values held in shared memory as
-// [n][HD] rows, read by every lane at once: the online softmax over chunks of KC keys, the running maximum replaced
-// (and the sums rescaled) only when a chunk's maximum exceeds it, as Soft::update does. A chunk's KC scores are
-// independent chains, each added in coordinate order. acc (HD) receives the weighted values; returns the weights' sum.
-template <int HD, int KC>
-__device__ __forceinline__ float attend_query(const float *q, const float *Ks, const float *Vs, int n, float *acc) {
-    float m = -FLT_MAX, sum = 0.f;
-    for (int k0 = 0; k0 < n; k0 += KC) {
-        float sc[KC];
+// nn.rs:187-228, 280-286 for NQ queries (scaled, in registers) against n keys and values held in shared memory as
+// [n][HD] rows, read by every lane at once: the online softmax over chunks of KC keys, each query's running maximum
+// replaced (and its sums rescaled) only when a chunk's maximum exceeds it, as Soft::update does. A chunk's scores are
+// independent chains, each added in coordinate order. acc[i] (HD) receives query i's weighted values, sum[i] its
+// weights' sum.
+template <int HD, int KC, int NQ>
+__device__ __forceinline__ void attend_queries(const float (&q)[NQ][HD], const float *Ks, const float *Vs, int n,
+                                               float (&acc)[NQ][HD], float (&sum)[NQ]) {
+    float m[NQ];
 #pragma unroll
-        for (int c = 0; c < KC; c++) sc[c] = 0.f;
+    for (int i = 0; i < NQ; i++) m[i] = -FLT_MAX, sum[i] = 0.f;
+    for (int k0 = 0; k0 < n; k0 += KC) {
+        float sc[NQ][KC];
+#pragma unroll
+        for (int i = 0; i < NQ; i++)
+#pragma unroll
+            for (int c = 0; c < KC; c++) sc[i][c] = 0.f;
 #pragma unroll
         for (int j4 = 0; j4 < HD / 4; j4++) {
 #pragma unroll
             for (int c = 0; c < KC; c++) {
                 const float4 kk = reinterpret_cast<const float4 *>(Ks + min(k0 + c, n - 1) * HD)[j4];
-                sc[c] = fmaf(q[4 * j4], kk.x, sc[c]), sc[c] = fmaf(q[4 * j4 + 1], kk.y, sc[c]);
-                sc[c] = fmaf(q[4 * j4 + 2], kk.z, sc[c]), sc[c] = fmaf(q[4 * j4 + 3], kk.w, sc[c]);
+#pragma unroll
+                for (int i = 0; i < NQ; i++) {
+                    sc[i][c] = fmaf(q[i][4 * j4], kk.x, sc[i][c]), sc[i][c] = fmaf(q[i][4 * j4 + 1], kk.y, sc[i][c]);
+                    sc[i][c] = fmaf(q[i][4 * j4 + 2], kk.z, sc[i][c]), sc[i][c] = fmaf(q[i][4 * j4 + 3], kk.w, sc[i][c]);
+                }
             }
         }
-        float cm = -FLT_MAX;
+        float p[NQ][KC];
 #pragma unroll
-        for (int c = 0; c < KC; c++)
-            if (k0 + c < n) cm = fmaxf(cm, sc[c]);
-        if (cm > m) {
-            const float corr = exp1(m - cm);
-            m = cm, sum *= corr;
+        for (int i = 0; i < NQ; i++) {
+            float cm = -FLT_MAX;
 #pragma unroll
-            for (int j = 0; j < HD; j++) acc[j] *= corr;
+            for (int c = 0; c < KC; c++)
+                if (k0 + c < n) cm = fmaxf(cm, sc[i][c]);
+            if (cm > m[i]) {
+                const float corr = exp1(m[i] - cm);
+                m[i] = cm, sum[i] *= corr;
+#pragma unroll
+                for (int j = 0; j < HD; j++) acc[i][j] *= corr;
+            }
+#pragma unroll
+            for (int c = 0; c < KC; c++) {
+                p[i][c] = k0 + c < n ? exp1(sc[i][c] - m[i]) : 0.f;
+                sum[i] += p[i][c];
+            }
         }
 #pragma unroll
         for (int c = 0; c < KC; c++) {
-            const float p = k0 + c < n ? exp1(sc[c] - m) : 0.f;
-            sum += p;
             const float4 *vr = reinterpret_cast<const float4 *>(Vs + min(k0 + c, n - 1) * HD);
 #pragma unroll
             for (int j4 = 0; j4 < HD / 4; j4++) {
                 const float4 vv = vr[j4];
-                acc[4 * j4] = fmaf(vv.x, p, acc[4 * j4]), acc[4 * j4 + 1] = fmaf(vv.y, p, acc[4 * j4 + 1]);
-                acc[4 * j4 + 2] = fmaf(vv.z, p, acc[4 * j4 + 2]), acc[4 * j4 + 3] = fmaf(vv.w, p, acc[4 * j4 + 3]);
+#pragma unroll
+                for (int i = 0; i < NQ; i++) {
+                    acc[i][4 * j4] = fmaf(vv.x, p[i][c], acc[i][4 * j4]);
+                    acc[i][4 * j4 + 1] = fmaf(vv.y, p[i][c], acc[i][4 * j4 + 1]);
+                    acc[i][4 * j4 + 2] = fmaf(vv.z, p[i][c], acc[i][4 * j4 + 2]);
+                    acc[i][4 * j4 + 3] = fmaf(vv.w, p[i][c], acc[i][4 * j4 + 3]);
+                }
             }
         }
     }
-    return sum;
 }
 
-// The same attention with one query per thread: block (group g, head h, run of blockDim rows); the head's keys and
-// values of group g in shared memory as [n][HD] rows, read by every lane at once (broadcast); the query, then the
-// weighted values, in registers (attend_query).
+// The same attention with one query per thread, or two: block (group g, head h, run of NQ * blockDim rows); the
+// head's keys and values of group g in shared memory as [n][HD] rows, read by every lane at once (broadcast); the
+// queries, then the weighted values, in registers (attend_queries). Thread t takes rows t and t + blockDim of the run.
 template <int HD>
-__global__ void __launch_bounds__(256, HD <= 32 ? 2 : 1) k_col_attend_q(const float *Q, int R, int F, const float *kv, size_t gstride,
+__global__ void __launch_bounds__(128) k_col_attend_q(const float *Q, int R, int F, const float *kv, size_t gstride,
                                                       int e, int n, float scale, float *att) {
+    constexpr int NQ = attend_nq(HD);
     extern __shared__ __align__(16) float sm[];
     const int g = blockIdx.x, h = blockIdx.y;
     const float *Kg = kv + (size_t)g * gstride, *Vg = Kg + (size_t)e * n;
@@ -147,17 +172,26 @@ __global__ void __launch_bounds__(256, HD <= 32 ? 2 : 1) k_col_attend_q(const fl
         Vs[k * HD + j] = Vg[(size_t)(h * HD + j) * n + k];
     }
     __syncthreads();
-    const int r = blockIdx.z * blockDim.x + threadIdx.x;
-    if (r >= R) return;
-    const size_t cell = (size_t)r * F + g;
-    const float *qp = Q + cell * e + h * HD;
-    float q[HD], acc[HD];
+    const int r0 = blockIdx.z * NQ * blockDim.x + threadIdx.x;
+    if (r0 >= R) return;
+    float q[NQ][HD], acc[NQ][HD], sum[NQ];
+    int rr[NQ];
 #pragma unroll
-    for (int j = 0; j < HD; j++) q[j] = qp[j] * scale, acc[j] = 0.f;
-    const float inv = 1.0f / attend_query<HD, attend_chunk(HD)>(q, Ks, Vs, n, acc);
-    float *op = att + cell * e + h * HD;
+    for (int i = 0; i < NQ; i++) {
+        rr[i] = r0 + i * blockDim.x;
+        const float *qp = Q + ((size_t)min(rr[i], R - 1) * F + g) * e + h * HD;  // a row past R repeats the last one
 #pragma unroll
-    for (int j = 0; j < HD; j++) op[j] = acc[j] * inv;
+        for (int j = 0; j < HD; j++) q[i][j] = qp[j] * scale, acc[i][j] = 0.f;
+    }
+    attend_queries<HD, attend_chunk(HD, NQ), NQ>(q, Ks, Vs, n, acc, sum);
+#pragma unroll
+    for (int i = 0; i < NQ; i++) {
+        if (rr[i] >= R) break;
+        const float inv = 1.0f / sum[i];
+        float *op = att + ((size_t)rr[i] * F + g) * e + h * HD;
+#pragma unroll
+        for (int j = 0; j < HD; j++) op[j] = acc[i][j] * inv;
+    }
 }
 
 // The rotary rotation (nn.rs:380-395) of element j of a head's key or query row x (head width hd), position t.
@@ -238,10 +272,11 @@ __global__ void __launch_bounds__(256) k_row_attend(const float *QKV, int R, int
 
 // k_row_attend with one query token per thread: block (row r, head h), the head's rotated keys and values of the row
 // in shared memory as [T][HD] rows, read by every lane at once; the query and the weighted values in registers
-// (attend_query).
+// (attend_queries).
 template <int HD>
 __global__ void __launch_bounds__(512) k_row_attend_q(const float *QKV, int R, int T, int nq, int e, const float *cs,
                                                        const float *sn, float *att) {
+    constexpr int NQ = 1;  // two tokens a thread measured slower: the row's blocks are bound by loading its keys
     extern __shared__ __align__(16) float sm[];
     const int r = blockIdx.x, h = blockIdx.y, half = HD / 2;
     const float *base = QKV + (size_t)r * T * 3 * e;
@@ -253,17 +288,27 @@ __global__ void __launch_bounds__(512) k_row_attend_q(const float *QKV, int R, i
         Vs[i] = base[(size_t)t * 3 * e + 2 * e + h * HD + j];
     }
     __syncthreads();
-    const int t = threadIdx.x;
-    if (t >= nq) return;
+    if ((int)threadIdx.x >= nq) return;
     const float inv = 1.0f / sqrtf((float)HD);
-    const float *qr = base + (size_t)t * 3 * e + h * HD;
-    float q[HD], acc[HD];
+    float q[NQ][HD], acc[NQ][HD], sum[NQ];
+    int tt[NQ];
 #pragma unroll
-    for (int j = 0; j < HD; j++) q[j] = rope(qr, j, half, cs, sn, t) * inv, acc[j] = 0.f;
-    const float s = 1.0f / attend_query<HD, attend_chunk(HD)>(q, Ks, Vs, T, acc);
-    float *op = att + ((size_t)r * nq + t) * e + h * HD;
+    for (int i = 0; i < NQ; i++) {
+        tt[i] = threadIdx.x + i * blockDim.x;
+        const int t = min(tt[i], nq - 1);  // a token past nq repeats the last one
+        const float *qr = base + (size_t)t * 3 * e + h * HD;
 #pragma unroll
-    for (int j = 0; j < HD; j++) op[j] = acc[j] * s;
+        for (int j = 0; j < HD; j++) q[i][j] = rope(qr, j, half, cs, sn, t) * inv, acc[i][j] = 0.f;
+    }
+    attend_queries<HD, attend_chunk(HD, NQ), NQ>(q, Ks, Vs, T, acc, sum);
+#pragma unroll
+    for (int i = 0; i < NQ; i++) {
+        if (tt[i] >= nq) break;
+        const float s = 1.0f / sum[i];
+        float *op = att + ((size_t)r * nq + tt[i]) * e + h * HD;
+#pragma unroll
+        for (int j = 0; j < HD; j++) op[j] = acc[i][j] * s;
+    }
 }
 
 // tok [R][T][e]: rows t < cls are the class tokens, rows cls + g the cells X [R * F][e] (T = cls + F).
@@ -329,8 +374,9 @@ static cudaError_t col_attend_q(const float *Q, int R, int F, const float *kv, s
     const size_t smem = sizeof(float) * 2 * (size_t)n * HD;
     cudaError_t err = allow_dynamic_smem((const void *)k_col_attend_q<HD>, smem);
     if (err != cudaSuccess) return err;
-    dim3 grid(F, heads, (R + 255) / 256);
-    k_col_attend_q<HD><<<grid, 256, smem, s>>>(Q, R, F, kv, gstride, e, n, scale, att);
+    constexpr int NQ = attend_nq(HD), TH = 128;
+    dim3 grid(F, heads, (R + NQ * TH - 1) / (NQ * TH));
+    k_col_attend_q<HD><<<grid, TH, smem, s>>>(Q, R, F, kv, gstride, e, n, scale, att);
     return cudaGetLastError();
 }
 
