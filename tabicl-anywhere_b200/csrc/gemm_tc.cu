@@ -47,11 +47,28 @@ size_t tc_split_bytes(int rows, int K) { return (size_t)((rows + GBM - 1) / GBM)
 // power-of-two scale that keeps the row's largest transformed magnitude below 2^14 (stats[m] = {mean, rstd, scale,
 // 1 / scale}), and the row, transformed and scaled, split into f16 hi + lo in its 128 x 64 blocks:
 // tiles[(m / 128) * (K / 64) + k / 64] = [hi block][lo block], element (m % 128, k % 64) at blk_off. Rows from M up
-// to the next multiple of 128 are written as zeros. NJ = K / 256 rounded up (K up to 2048).
-template <int NJ>
+// to the next multiple of 128 are written as zeros. NJ = K / 256 rounded up (K up to 2048). With RPW = 2 (K up to 128)
+// each half-warp takes a row of its own: the lanes a whole warp would leave idle (they hold zeros there), so every sum
+// and maximum is the same, added in the same order.
+template <int LW>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+    for (int o = LW / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+template <int LW>
+__device__ __forceinline__ float group_max(float v) {
+#pragma unroll
+    for (int o = LW / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+template <int NJ, int RPW = 1>
 __global__ void __launch_bounds__(256) k_split_rows(const float *x, int ldx, int M, int K, const float *lnw,
                                                     const float *lnb, float4 *stats, __half *tiles) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, row = blockIdx.x * 8 + warp;
+    constexpr int LW = 32 / RPW;  // lanes per row
+    const int warp = threadIdx.x >> 5, lane = (threadIdx.x & 31) % LW;
+    const int row = (blockIdx.x * 8 + warp) * RPW + (int)(threadIdx.x & 31) / LW;
     const bool real = row < M;
     pdl_trigger();
     pdl_wait();
@@ -76,7 +93,7 @@ __global__ void __launch_bounds__(256) k_split_rows(const float *x, int ldx, int
         for (int j = 0; j < NJ; j++)
 #pragma unroll
             for (int e = 0; e < 8; e++) s += v[j][e];
-        mean = warp_sum(s) / (float)K;
+        mean = group_sum<LW>(s) / (float)K;
         float q = 0.f;
 #pragma unroll
         for (int j = 0; j < NJ; j++) {
@@ -88,7 +105,7 @@ __global__ void __launch_bounds__(256) k_split_rows(const float *x, int ldx, int
                 }
             }
         }
-        inv = 1.0f / sqrtf(warp_sum(q) / (float)K + 1e-5f);
+        inv = 1.0f / sqrtf(group_sum<LW>(q) / (float)K + 1e-5f);
 #pragma unroll
         for (int j = 0; j < NJ; j++) {
             const int k = 256 * j + 8 * lane;
@@ -107,7 +124,7 @@ __global__ void __launch_bounds__(256) k_split_rows(const float *x, int ldx, int
     for (int j = 0; j < NJ; j++)
 #pragma unroll
         for (int e = 0; e < 8; e++) mx = fmaxf(mx, fabsf(v[j][e]));
-    mx = warp_max(mx);
+    mx = group_max<LW>(mx);
     int ex = 0;
     if (mx > 0.f) {
         ex = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xff) - 126);  // mx < 2^(14 - ex)
@@ -382,7 +399,9 @@ cudaError_t launch_gemm_tc(const LinArgs &a, float4 *stats, cudaStream_t s, uint
     const int sblocks = (a.M + GBM - 1) / GBM * (GBM / 8);
     __half *at = reinterpret_cast<__half *>(a.tc_atiles);
     cudaError_t e0;
-    if (a.K <= 256)
+    if (a.K <= 128)
+        e0 = launch_pdl(k_split_rows<1, 2>, dim3(sblocks / 2), dim3(256), 0, s, a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
+    else if (a.K <= 256)
         e0 = launch_pdl(k_split_rows<1>, dim3(sblocks), dim3(256), 0, s, a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
     else if (a.K <= 512)
         e0 = launch_pdl(k_split_rows<2>, dim3(sblocks), dim3(256), 0, s, a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
