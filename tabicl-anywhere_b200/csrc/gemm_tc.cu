@@ -28,9 +28,10 @@ using namespace tc;
 constexpr long long GEMM_WAIT_CYCLES = 2000000000ll;
 constexpr int GBM = 128, GBK = 64, GTHREADS = 320, GBUFS = 4;
 constexpr size_t GBLOCK = (size_t)GBM * GBK;  // halves in one operand block (hi or lo)
-template <int BN>
+// STAGES: slots of the copy ring (0: the default for the tile width)
+template <int BN, int SLOTS = 0>
 struct GemmShape {
-    static constexpr int STAGES = BN == 128 ? 3 : 4;
+    static constexpr int STAGES = SLOTS ? SLOTS : (BN == 128 ? 3 : 4);
     static constexpr uint32_t A_BYTES = 2 * GBLOCK * sizeof(__half);            // hi + lo of 128 rows
     static constexpr uint32_t W_BYTES = 2 * (uint32_t)BN * GBK * sizeof(__half);  // hi + lo of BN rows
     static constexpr uint32_t SLOT = A_BYTES + W_BYTES;
@@ -161,9 +162,9 @@ __device__ __forceinline__ void g_expect(uint64_t *mbar, uint32_t bytes) {
                  : "memory");
 }
 
-template <int BN>
+template <int BN, int SLOTS = 0>
 __global__ void __launch_bounds__(GTHREADS, 1) k_gemm_tc(LinArgs a, const float4 *stats) {
-    using G = GemmShape<BN>;
+    using G = GemmShape<BN, SLOTS>;
     constexpr int S = G::STAGES, HALF = BN / 2;
     extern __shared__ __align__(1024) uint8_t smraw[];
     // ring of S slots: [A hi][A lo][W hi][W lo]
@@ -386,12 +387,13 @@ static int gemm_bn(int M, int N) {
     return (long)((M + GBM - 1) / GBM) * ((N + 127) / 128) * 2 <= sms ? 64 : 128;
 }
 
-template <int BN>
+template <int BN, int SLOTS = 0>
 static cudaError_t launch_bn(const LinArgs &a, float4 *stats, cudaStream_t s) {
-    cudaError_t e = allow_dynamic_smem((const void *)k_gemm_tc<BN>, GemmShape<BN>::SMEM);
+    using G = GemmShape<BN, SLOTS>;
+    cudaError_t e = allow_dynamic_smem((const void *)k_gemm_tc<BN, SLOTS>, G::SMEM);
     if (e != cudaSuccess) return e;
     dim3 grid((a.N + BN - 1) / BN, (a.M + GBM - 1) / GBM);
-    return launch_pdl(k_gemm_tc<BN>, grid, dim3(GTHREADS), GemmShape<BN>::SMEM, s, a, (const float4 *)stats);
+    return launch_pdl(k_gemm_tc<BN, SLOTS>, grid, dim3(GTHREADS), G::SMEM, s, a, (const float4 *)stats);
 }
 
 cudaError_t launch_gemm_tc(const LinArgs &a, float4 *stats, cudaStream_t s, uint64_t *launches) {
@@ -411,6 +413,17 @@ cudaError_t launch_gemm_tc(const LinArgs &a, float4 *stats, cudaStream_t s, uint
         e0 = launch_pdl(k_split_rows<8>, dim3(sblocks), dim3(256), 0, s, a.x, a.ldx, a.M, a.K, a.lnw, a.lnb, stats, at);
     if (e0 != cudaSuccess) return e0;
     if (launches) ++*launches;
+    // many tiles of at most four K chunks (the column and row stages): 64-wide tiles with a two-slot ring, so that two
+    // CTAs share an SM and one's set-up and epilogue overlap the other's copies and MMAs (TCU_GEMM_PAIR=0: never)
+    static const bool pair = [] {
+        const char *v = getenv("TCU_GEMM_PAIR");
+        return !(v && v[0] == '0');
+    }();
+    if (pair && a.K <= 256 && (long)((a.M + GBM - 1) / GBM) * ((a.N + 63) / 64) >= 4L * 148) {
+        const cudaError_t e = launch_bn<64, 2>(a, stats, s);
+        if (launches) ++*launches;
+        return e;
+    }
     const cudaError_t e = gemm_bn(a.M, a.N) == 64 ? launch_bn<64>(a, stats, s) : launch_bn<128>(a, stats, s);
     if (launches) ++*launches;
     return e;
