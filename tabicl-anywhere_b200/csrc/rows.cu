@@ -92,10 +92,10 @@ __host__ __device__ constexpr int attend_chunk(int hd, int nq) {
 // [n][HD] rows, read by every lane at once: the online softmax over chunks of KC keys, each query's running maximum
 // replaced (and its sums rescaled) only when a chunk's maximum exceeds it, as Soft::update does. A chunk's scores are
 // independent chains, each added in coordinate order. acc[i] (HD) receives query i's weighted values, sum[i] its
-// weights' sum.
+// weights' sum. Key (and value) rows are ld floats apart.
 template <int HD, int KC, int NQ>
 __device__ __forceinline__ void attend_queries(const float (&q)[NQ][HD], const float *Ks, const float *Vs, int n,
-                                               float (&acc)[NQ][HD], float (&sum)[NQ]) {
+                                               float (&acc)[NQ][HD], float (&sum)[NQ], int ld = HD) {
     float m[NQ];
 #pragma unroll
     for (int i = 0; i < NQ; i++) m[i] = -FLT_MAX, sum[i] = 0.f;
@@ -109,7 +109,7 @@ __device__ __forceinline__ void attend_queries(const float (&q)[NQ][HD], const f
         for (int j4 = 0; j4 < HD / 4; j4++) {
 #pragma unroll
             for (int c = 0; c < KC; c++) {
-                const float4 kk = reinterpret_cast<const float4 *>(Ks + min(k0 + c, n - 1) * HD)[j4];
+                const float4 kk = reinterpret_cast<const float4 *>(Ks + (size_t)min(k0 + c, n - 1) * ld)[j4];
 #pragma unroll
                 for (int i = 0; i < NQ; i++) {
                     sc[i][c] = fmaf(q[i][4 * j4], kk.x, sc[i][c]), sc[i][c] = fmaf(q[i][4 * j4 + 1], kk.y, sc[i][c]);
@@ -138,7 +138,7 @@ __device__ __forceinline__ void attend_queries(const float (&q)[NQ][HD], const f
         }
 #pragma unroll
         for (int c = 0; c < KC; c++) {
-            const float4 *vr = reinterpret_cast<const float4 *>(Vs + min(k0 + c, n - 1) * HD);
+            const float4 *vr = reinterpret_cast<const float4 *>(Vs + (size_t)min(k0 + c, n - 1) * ld);
 #pragma unroll
             for (int j4 = 0; j4 < HD / 4; j4++) {
                 const float4 vv = vr[j4];
@@ -164,12 +164,15 @@ __global__ void __launch_bounds__(128) k_col_attend_q(const float *Q, int R, int
     extern __shared__ __align__(16) float sm[];
     const int g = blockIdx.x, h = blockIdx.y;
     const float *Kg = kv + (size_t)g * gstride, *Vg = Kg + (size_t)e * n;
-    float *Ks = sm, *Vs = sm + (size_t)n * HD;
+    // rows padded to HD + 4 floats: the turn-round's stores (consecutive keys, one coordinate) fall in eight banks
+    // instead of one, and every row still starts on 16 bytes
+    constexpr int LD = HD + 4;
+    float *Ks = sm, *Vs = sm + (size_t)n * LD;
 #pragma unroll 8
     for (int i = threadIdx.x; i < n * HD; i += blockDim.x) {
         const int j = i / n, k = i - j * n;
-        Ks[k * HD + j] = Kg[(size_t)(h * HD + j) * n + k];
-        Vs[k * HD + j] = Vg[(size_t)(h * HD + j) * n + k];
+        Ks[k * LD + j] = Kg[(size_t)(h * HD + j) * n + k];
+        Vs[k * LD + j] = Vg[(size_t)(h * HD + j) * n + k];
     }
     __syncthreads();
     const int r0 = blockIdx.z * NQ * blockDim.x + threadIdx.x;
@@ -183,7 +186,7 @@ __global__ void __launch_bounds__(128) k_col_attend_q(const float *Q, int R, int
 #pragma unroll
         for (int j = 0; j < HD; j++) q[i][j] = qp[j] * scale, acc[i][j] = 0.f;
     }
-    attend_queries<HD, attend_chunk(HD, NQ), NQ>(q, Ks, Vs, n, acc, sum);
+    attend_queries<HD, attend_chunk(HD, NQ), NQ>(q, Ks, Vs, n, acc, sum, LD);
 #pragma unroll
     for (int i = 0; i < NQ; i++) {
         if (rr[i] >= R) break;
@@ -371,7 +374,7 @@ size_t col_attend_smem(int e, int n, int heads) { return sizeof(float) * ((size_
 template <int HD>
 static cudaError_t col_attend_q(const float *Q, int R, int F, const float *kv, size_t gstride, int e, int n, int heads,
                                 float scale, float *att, cudaStream_t s) {
-    const size_t smem = sizeof(float) * 2 * (size_t)n * HD;
+    const size_t smem = sizeof(float) * 2 * (size_t)n * (HD + 4);
     cudaError_t err = allow_dynamic_smem((const void *)k_col_attend_q<HD>, smem);
     if (err != cudaSuccess) return err;
     constexpr int NQ = attend_nq(HD), TH = 128;
@@ -383,7 +386,7 @@ static cudaError_t col_attend_q(const float *Q, int R, int F, const float *kv, s
 cudaError_t launch_col_attend(const float *Q, int R, int F, const float *kv, size_t gstride, int e, int n, int heads,
                               float scale, float *att, cudaStream_t s, uint64_t *launches) {
     const int hd = e / heads;
-    if (sizeof(float) * 2 * (size_t)n * hd <= 200 * 1024 && (hd == 8 || hd == 16 || hd == 32 || hd == 64)) {
+    if (sizeof(float) * 2 * (size_t)n * (hd + 4) <= 200 * 1024 && (hd == 8 || hd == 16 || hd == 32 || hd == 64)) {
         const cudaError_t err = hd == 8    ? col_attend_q<8>(Q, R, F, kv, gstride, e, n, heads, scale, att, s)
                                 : hd == 16 ? col_attend_q<16>(Q, R, F, kv, gstride, e, n, heads, scale, att, s)
                                 : hd == 32 ? col_attend_q<32>(Q, R, F, kv, gstride, e, n, heads, scale, att, s)
