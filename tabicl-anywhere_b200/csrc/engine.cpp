@@ -1438,7 +1438,8 @@ static void represent(tcu_ctx *ctx, tcu_model *m, float *tok, int R, float *rep,
     const auto &rs = rw.shape;
     const int e = rs.e, T = rs.cls + m->features, heads = rs.row_heads, half = e / heads / 2, ff = rs.row_ff;
     const size_t M = (size_t)R * T;
-    m->cqkv.ensure(sizeof(float) * M * 3 * e), m->catt.ensure(sizeof(float) * M * e), m->cnew.ensure(sizeof(float) * M * e);
+    m->cqkv.ensure(sizeof(float) * M * 3 * e), m->catt.ensure(sizeof(float) * M * e);
+    m->cnew.ensure(sizeof(float) * (size_t)R * rs.cls * e);  // the last block's class tokens
     m->cmid.ensure(sizeof(float) * M * ff);
     if (row_attend_needs_workspace(e, T, T, heads) || row_attend_needs_workspace(e, T, rs.cls, heads))
         m->ckt.ensure(sizeof(float) * row_attend_workspace(R, T, e));
@@ -1464,11 +1465,18 @@ static void represent(tcu_ctx *ctx, tcu_model *m, float *tok, int R, float *rep,
         const int nq = last ? rs.cls : T, MQ = R * nq;
         linear(ctx, m, cur, e, (int)M, e, B.n1w, B.n1b, B.inw, B.inb, 3 * e, QKV, 3 * e, 0, 0, s, B.tin);
         ck(launch_row_attend(QKV, R, T, nq, e, heads, cs, sn, m->ckt.as<float>(), A, s, &ctx->launches), "row attention");
+        if (!last) {
+            // every token is a query: the out-projection adds onto the tokens themselves (the residual, the same sum
+            // as adding the tokens onto it), and the feed-forward updates them in place for the next block
+            linear(ctx, m, A, e, MQ, e, nullptr, nullptr, B.ow, B.ob, e, cur, e, 0, 1, s, B.to);
+            linear(ctx, m, cur, e, MQ, e, B.n2w, B.n2b, B.w1, B.b1, ff, H, ff, 1, 0, s, B.t1);
+            linear(ctx, m, H, ff, MQ, ff, nullptr, nullptr, B.w2, B.b2, e, cur, e, 0, 1, s, B.t2);
+            continue;
+        }
         linear(ctx, m, A, e, MQ, e, nullptr, nullptr, B.ow, B.ob, e, nxt, e, 0, 0, s, B.to);
         ck(launch_add_rows(nxt, cur, R, nq, T, e, s, &ctx->launches), "row residual");
         linear(ctx, m, nxt, e, MQ, e, B.n2w, B.n2b, B.w1, B.b1, ff, H, ff, 1, 0, s, B.t1);
         linear(ctx, m, H, ff, MQ, ff, nullptr, nullptr, B.w2, B.b2, e, nxt, e, 0, 1, s, B.t2);
-        if (!last) std::swap(cur, nxt);  // every token was a query: the new tokens are the next block's input
     }
     // the last block left the class tokens [R][cls][e] in nxt: their LayerNorm, laid end to end, is the representation
     ck(launch_ln_apply(nxt, R * rs.cls, e, rw.out_lnw, rw.out_lnb, rep, s, &ctx->launches), "row LayerNorm");
