@@ -14,7 +14,7 @@ namespace {
 
 // predict.rs:300-315 and nn.rs:422-429: cell (r, g) = in_linear of the features g+1, g+2, g+4, ... (circular), or
 // -100 everywhere when all of them are missing (-100); X [R * F][e]. Products and sums unfused, as the CPU's short dot.
-__global__ void k_col_cells(const float *x, int R, int F, int group, const float *in_w, const float *in_b, int e, float *X) {
+__global__ void k_col_cells1(const float *x, int R, int F, int group, const float *in_w, const float *in_b, int e, float *X) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)R * F * e) return;
     const int k = (int)(i % e);
@@ -29,6 +29,31 @@ __global__ void k_col_cells(const float *x, int R, int F, int group, const float
         s = __fadd_rn(s, __fmul_rn(in_w[k * group + j], v));
     }
     X[i] = missing ? -100.0f : __fadd_rn(s, in_b[k]);
+}
+
+// The same, four consecutive outputs of a cell per thread (e a multiple of 4, X 16-byte aligned): the cell's feature
+// values are read once for them.
+__global__ void k_col_cells(const float *x, int R, int F, int group, const float *in_w, const float *in_b, int e, float *X) {
+    const size_t i4 = (size_t)blockIdx.x * blockDim.x + threadIdx.x, e4 = e / 4;
+    if (i4 >= (size_t)R * F * e4) return;
+    const int k0 = (int)(i4 % e4) * 4;
+    const size_t cell = i4 / e4;
+    const int g = (int)(cell % F), r = (int)(cell / F);
+    const float *row = x + (size_t)r * F;
+    bool missing = true;
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < group; j++) {
+        const float v = row[(g + (1 << j)) % F];
+        missing &= v == -100.0f;
+#pragma unroll
+        for (int c = 0; c < 4; c++) s[c] = __fadd_rn(s[c], __fmul_rn(in_w[(k0 + c) * group + j], v));
+    }
+    float4 o;
+    o.x = missing ? -100.0f : __fadd_rn(s[0], in_b[k0]);
+    o.y = missing ? -100.0f : __fadd_rn(s[1], in_b[k0 + 1]);
+    o.z = missing ? -100.0f : __fadd_rn(s[2], in_b[k0 + 2]);
+    o.w = missing ? -100.0f : __fadd_rn(s[3], in_b[k0 + 3]);
+    reinterpret_cast<float4 *>(X)[i4] = o;
 }
 
 // nn.rs:187-228, 280-286 for one query against n fixed keys: the column stage's attention of cell (r, g) against the
@@ -315,7 +340,7 @@ __global__ void __launch_bounds__(512) k_row_attend_q(const float *QKV, int R, i
 }
 
 // tok [R][T][e]: rows t < cls are the class tokens, rows cls + g the cells X [R * F][e] (T = cls + F).
-__global__ void k_tokens(const float *X, const float *cls_tokens, int R, int F, int cls, int e, float *tok) {
+__global__ void k_tokens1(const float *X, const float *cls_tokens, int R, int F, int cls, int e, float *tok) {
     const int T = cls + F;
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)R * T * e) return;
@@ -323,6 +348,19 @@ __global__ void k_tokens(const float *X, const float *cls_tokens, int R, int F, 
     const size_t rt = i / e;
     const int t = (int)(rt % T), r = (int)(rt / T);
     tok[i] = t < cls ? cls_tokens[t * e + k] : X[((size_t)r * F + (t - cls)) * e + k];
+}
+
+// The same, four values a thread (e a multiple of 4, the buffers 16-byte aligned).
+__global__ void k_tokens(const float *X, const float *cls_tokens, int R, int F, int cls, int e, float *tok) {
+    const int T = cls + F, e4 = e / 4;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)R * T * e4) return;
+    const int k = (int)(i % e4);
+    const size_t rt = i / e4;
+    const int t = (int)(rt % T), r = (int)(rt / T);
+    reinterpret_cast<float4 *>(tok)[i] =
+        t < cls ? reinterpret_cast<const float4 *>(cls_tokens)[t * e4 + k]
+                : reinterpret_cast<const float4 *>(X)[((size_t)r * F + (t - cls)) * e4 + k];
 }
 
 // y[r][t] (nq rows of each of R) += x[r][t] (T rows of each): the residual of the row stage's query tokens.
@@ -364,7 +402,10 @@ inline unsigned blocks_for(size_t n) { return (unsigned)((n + 255) / 256); }
 
 cudaError_t launch_col_cells(const float *x, int R, int F, int group, const float *in_w, const float *in_b, int e,
                              float *X, cudaStream_t s, uint64_t *launches) {
-    k_col_cells<<<blocks_for((size_t)R * F * e), 256, 0, s>>>(x, R, F, group, in_w, in_b, e, X);
+    if (e % 4 || reinterpret_cast<uintptr_t>(X) % 16)
+        k_col_cells1<<<blocks_for((size_t)R * F * e), 256, 0, s>>>(x, R, F, group, in_w, in_b, e, X);
+    else
+        k_col_cells<<<blocks_for((size_t)R * F * e / 4), 256, 0, s>>>(x, R, F, group, in_w, in_b, e, X);
     if (launches) ++*launches;
     return cudaGetLastError();
 }
@@ -470,7 +511,10 @@ cudaError_t launch_row_attend(const float *QKV, int R, int T, int nq, int e, int
 
 cudaError_t launch_tokens(const float *X, const float *cls_tokens, int R, int F, int cls, int e, float *tok, cudaStream_t s,
                           uint64_t *launches) {
-    k_tokens<<<blocks_for((size_t)R * (cls + F) * e), 256, 0, s>>>(X, cls_tokens, R, F, cls, e, tok);
+    if (e % 4 || (reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(cls_tokens) | reinterpret_cast<uintptr_t>(tok)) % 16)
+        k_tokens1<<<blocks_for((size_t)R * (cls + F) * e), 256, 0, s>>>(X, cls_tokens, R, F, cls, e, tok);
+    else
+        k_tokens<<<blocks_for((size_t)R * (cls + F) * e / 4), 256, 0, s>>>(X, cls_tokens, R, F, cls, e, tok);
     if (launches) ++*launches;
     return cudaGetLastError();
 }
