@@ -1,5 +1,7 @@
 """The class tree on the host: fit::Plan (src/fit.rs:151-221) and its stored form, and the oracle's restatement of
-the tree step of prediction (src/predict.rs:664-692), each against answers worked out by hand."""
+the tree step of prediction (src/predict.rs:664-692), each against answers worked out by hand; and the names and sizes
+of the tensors a fit fills (fit::raw_entries, src/fit.rs:224-241)."""
+import pytest
 import numpy as np
 
 from conftest import tcu
@@ -96,3 +98,32 @@ def test_tree_scores_map_a_permuted_leaf():
     got = oracle.tree_scores([s], [1, 4, 3, 2, 0, 1], 1, 3)
     ident = oracle.tree_scores([s], [1, 4, 3, 0, 1, 2], 1, 3)
     assert np.array_equal(got[:, [2, 0, 1]], ident)
+
+
+class _Shapes:
+    """What raw_entries reads from the device weights: the in-context and the column stages' sizes."""
+    shape = {"layers": 12, "d": 512}
+    rows_shape = {"col_blocks": 3, "e": 128, "inds": 128}
+
+
+@pytest.mark.parametrize("classes,kv", [(10, 1), (37, 2), (3, 0)])
+def test_raw_entries_names_and_sizes(classes, kv):
+    """fit::raw_entries (src/fit.rs:224-241): meta [7], the tree, col_kv [features][digits][blocks][2][e][inds], then
+    per node its query scales [layers][d] and every layer's stored bytes, full chunks then the rest (chunk at least 8)."""
+    rows, features, chunk = 1000, 7, 300
+    y = np.arange(rows) % classes
+    plan = tcu.Plan.new(10, y, classes)
+    ent = tcu.raw_entries(_Shapes(), "m3/", rows, features, chunk, kv, plan)
+    names = [n for n, _, _ in ent]
+    assert names[:3] == ["m3/meta", "m3/tree", "m3/col_kv"]
+    assert ent[0][1:] == ("int32", [7]) and ent[1][1:] == ("int32", [len(plan.tree(rows))])
+    assert ent[2][2] == [features, len(plan.bases), 3, 2, 128, 128]
+    at = 3
+    for i, nd in enumerate(plan.nodes):
+        nr = rows if nd.rows is None else len(nd.rows)
+        assert ent[at] == (f"m3/n{i}_scale", "float32", [12, 512])
+        want = (nr // chunk) * oracle.record(kv, 512, chunk) + (oracle.record(kv, 512, nr % chunk) if nr % chunk else 0)
+        for l in range(12):
+            assert ent[at + 1 + l] == (f"m3/n{i}_kv{l}", "uint8", [want])
+        at += 13
+    assert at == len(ent)
